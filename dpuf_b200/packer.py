@@ -1,0 +1,121 @@
+"""Mode-12 ("Hadamard-4bit packed") weight encoder: Python front of libdpuf_pack.so.
+
+Produces the exact bytes of the reference packer's `encode_tensor_qr_hadamard4_packed`
+(dpuf_format.py:1563) for 2-D weights whose column count is a multiple of 64.
+
+The per-tensor column signs follow `_make_had_sign_bits` (dpuf_format.py:1424-1430):
+numpy's default_rng seeded with crc32(seed_name) ^ 0x9E3779B9 draws one bit per column,
+packed little-endian.  Projections that share an input share a seed name
+(`_hadamard_seed_name`, pack_dpuf.py:206-216): q/k/v use "blk.{l}.qkv_in", gate/up use
+"blk.{l}.mlp_in", everything else its own tensor name.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import zlib
+
+import numpy as np
+
+from . import _native
+
+MODE_QR_HAD4_PACKED = 12
+TILE_ROWS = 16
+ECC_GROUP = 64
+FINDER_BYTES = 64
+
+
+def _lib():
+    lib = _native.load_pack()
+    if not getattr(lib, "_dpuf_typed", False):
+        lib.dpuf_pack_mode12_size.restype = ctypes.c_int64
+        lib.dpuf_pack_mode12_size.argtypes = [ctypes.c_int32] * 4
+        lib.dpuf_pack_mode12.restype = ctypes.c_int32
+        lib.dpuf_pack_mode12.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32]
+        lib.dpuf_gen_normal_bf16.restype = None
+        lib.dpuf_gen_normal_bf16.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_float,
+                                             ctypes.c_void_p, ctypes.c_int32]
+        lib.dpuf_pack_crc32.restype = ctypes.c_uint32
+        lib.dpuf_pack_crc32.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
+        lib._dpuf_typed = True
+    return lib
+
+
+def default_threads() -> int:
+    return max(1, min(64, os.cpu_count() or 1))
+
+
+def hadamard_seed_name(tensor_name: str) -> str:
+    """Seed name shared by co-input projections (pack_dpuf.py:206-216)."""
+    if tensor_name.startswith("blk."):
+        parts = tensor_name.split(".", 2)
+        if len(parts) == 3:
+            l_idx, suffix = parts[1], parts[2]
+            if suffix in ("attn_q.weight", "attn_k.weight", "attn_v.weight"):
+                return f"blk.{l_idx}.qkv_in"
+            if suffix in ("ffn_gate.weight", "ffn_up.weight"):
+                return f"blk.{l_idx}.mlp_in"
+    return tensor_name
+
+
+def sign_bits_for(cols: int, seed_name: str) -> np.ndarray:
+    """Column sign bits, cols/8 bytes (dpuf_format.py:1424-1430)."""
+    seed = zlib.crc32(seed_name.encode("utf-8")) ^ 0x9E3779B9
+    rng = np.random.default_rng(seed)
+    flags = rng.integers(0, 2, size=cols, dtype=np.uint8)
+    return np.packbits(flags, bitorder="little")
+
+
+def fp32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bits (dpuf_format.py:74-79)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + (((u >> 16) & 1) + np.uint32(0x7FFF))) >> 16).astype(np.uint16)
+
+
+def encode_mode12(w_bf16: np.ndarray, seed_name: str, n_threads: int | None = None) -> np.ndarray:
+    """Encodes a [rows, cols] bf16 (uint16 bits) matrix; returns the blob as a uint8 array."""
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    if w.ndim != 2 or w.shape[1] % 64 != 0 or min(w.shape) < 64:
+        raise ValueError(f"mode 12 needs a 2-D matrix with cols % 64 == 0, got {w.shape}")
+    rows, cols = w.shape
+    lib = _lib()
+    size = lib.dpuf_pack_mode12_size(rows, cols, TILE_ROWS, ECC_GROUP)
+    if size <= 0:
+        raise ValueError("bad shape for mode 12")
+    out = np.empty(size, dtype=np.uint8)
+    sb = sign_bits_for(cols, seed_name)
+    rc = lib.dpuf_pack_mode12(w.ctypes.data, rows, cols, sb.ctypes.data, TILE_ROWS, ECC_GROUP,
+                              out.ctypes.data, n_threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"dpuf_pack_mode12 failed ({rc})")
+    return out
+
+
+def gen_normal_bf16(seed: int, stream: int, shape, sigma: float = 0.02, n_threads: int | None = None) -> np.ndarray:
+    """Seeded N(0, sigma) weights rounded to bf16 (counter-based; independent of threads)."""
+    n = int(np.prod(shape))
+    out = np.empty(n, dtype=np.uint16)
+    _lib().dpuf_gen_normal_bf16(seed & (2**64 - 1), stream & (2**64 - 1), n, sigma, out.ctypes.data,
+                                n_threads or default_threads())
+    return out.reshape(shape)
+
+
+class BlobView:
+    """Parsed view of a mode-12 blob: finder header fields and the arrays the engine binds
+    (the same fields `bind_qr_weight` fills, dpuf-cli.c:1646-1756)."""
+
+    def __init__(self, blob: np.ndarray):
+        b = np.ascontiguousarray(blob, dtype=np.uint8)
+        if bytes(b[1:5]) != b"QRDP":
+            raise ValueError("not a QR-tiled blob (finder magic mismatch)")
+        self.blob = b
+        hdr = b[:64]
+        self.mode = int(hdr[0])
+        self.tile_rows = int(hdr[5])
+        self.ecc_group = int(hdr[6:8].view(np.uint16)[0])
+        self.rows, self.cols, self.n_tiles, self.n_ecc = (int(v) for v in hdr[8:24].view(np.uint32))
+        self.aux_off, self.tiles_base_off, self.ecc_base_off = (int(v) for v in hdr[24:48].view(np.uint64))
+        self.tile_offsets = b[64:64 + (self.n_tiles + 1) * 8].view(np.uint64)
+        self.tiles = b[self.tiles_base_off:self.ecc_base_off]
+        self.sign_bits = b[self.aux_off:self.aux_off + self.cols // 8]

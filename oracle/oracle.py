@@ -1,0 +1,217 @@
+"""Checkers for the CUDA engine.  TEST INFRASTRUCTURE ONLY: imported by tests/,
+__graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference legs, never by the
+product package.
+
+Two CPU engines with the reference's C ABI are driven here:
+  * OracleEngine - the scalar C restatement oracle/dpuf_oracle.c (liboracle.so, built by
+    `build()` below from this directory);
+  * RefEngine    - the reference's own AVX2/OpenMP engine compiled from its unmodified
+    sources by oracle/build_ref.sh into oracle/_ref/libdpuf_avx2.so.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libdpuf_avx2.so"
+REF_SRC_DEFAULT = pathlib.Path("/root/reference")
+
+
+def build(force: bool = False) -> pathlib.Path:
+    src = HERE / "dpuf_oracle.c"
+    hdr = HERE.parent / "include" / "dpuf_kernels.h"
+    if force or not ORACLE_LIB.exists() or max(src.stat().st_mtime, hdr.stat().st_mtime) > ORACLE_LIB.stat().st_mtime:
+        subprocess.run(["gcc", "-O2", "-std=gnu11", "-fPIC", "-shared", "-fopenmp", "-ffp-contract=off",
+                        "-fno-fast-math", str(src), "-o", str(ORACLE_LIB), "-lm"], check=True)
+    return ORACLE_LIB
+
+
+def build_ref(ref_dir: pathlib.Path = REF_SRC_DEFAULT) -> pathlib.Path | None:
+    """Builds oracle/_ref/libdpuf_avx2.so when the reference sources are present."""
+    if not (ref_dir / "dpuf_engine.c").exists():
+        return REF_LIB if REF_LIB.exists() else None
+    subprocess.run(["bash", str(HERE / "build_ref.sh"), str(ref_dir)], check=True, capture_output=True)
+    return REF_LIB
+
+
+_F = ctypes.POINTER(ctypes.c_float)
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(_F)
+
+
+class _EngineBase:
+    lib: ctypes.CDLL
+
+    def argmax(self, logits: np.ndarray) -> int:
+        """First index of the maximum (greedy sample_token, dpuf-cli.c:1997-2005)."""
+        return int(np.argmax(logits))  # numpy returns the first maximal index
+
+
+class OracleEngine(_EngineBase):
+    _lib = None
+
+    @classmethod
+    def lib_(cls) -> ctypes.CDLL:
+        if cls._lib is None:
+            if not ORACLE_LIB.exists():
+                raise RuntimeError("oracle/liboracle.so is not built")
+            lib = ctypes.CDLL(str(ORACLE_LIB))
+            lib.orc_engine_create.restype = ctypes.c_void_p
+            lib.orc_engine_create.argtypes = [ctypes.c_void_p] * 5
+            lib.orc_engine_destroy.argtypes = [ctypes.c_void_p]
+            lib.orc_engine_reset_cache.argtypes = [ctypes.c_void_p]
+            lib.orc_engine_forward.restype = ctypes.c_int32
+            lib.orc_engine_forward.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32,
+                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+            lib.orc_matmul_mode12_f32.argtypes = [ctypes.c_int32] * 4 + [ctypes.c_void_p] * 5
+            lib.orc_embed_mode12_f32.argtypes = [ctypes.c_int32, ctypes.c_int32] + [ctypes.c_void_p] * 5
+            lib.orc_prep_mode12.argtypes = [ctypes.c_int32] + [ctypes.c_void_p] * 5
+            lib.orc_swiglu_is_vector.restype = ctypes.c_int32
+            lib.orc_swiglu_is_vector.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, model):
+        self.lib = self.lib_()
+        self.model = model
+        self.h = self.lib.orc_engine_create(*model.create_args())
+        if not self.h:
+            raise RuntimeError("orc_engine_create failed")
+        self.vocab = model.shape.vocab
+
+    def close(self):
+        if self.h:
+            self.lib.orc_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        self.lib.orc_engine_reset_cache(self.h)
+
+    def forward(self, ids, pos0: int, only_last: int = 1, zone: bool = False):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        M = len(ids)
+        out = np.empty((1 if only_last == 1 else M, self.vocab), dtype=np.float32)
+        zone_out = np.zeros(4, dtype=np.int32)
+        rc = self.lib.orc_engine_forward(self.h, M, ids.ctypes.data, pos0, only_last,
+                                         out.ctypes.data if only_last != 2 else None, zone_out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"orc_engine_forward -> {rc}")
+        return (out, zone_out) if zone else out
+
+
+class RefEngine(_EngineBase):
+    """The reference engine (dpuf_engine.c) through its own C ABI (dpuf_kernels.h:316-360)."""
+    _lib = None
+
+    @classmethod
+    def available(cls) -> bool:
+        return REF_LIB.exists()
+
+    @classmethod
+    def lib_(cls) -> ctypes.CDLL:
+        if cls._lib is None:
+            if not REF_LIB.exists():
+                raise RuntimeError("oracle/_ref/libdpuf_avx2.so is not built (needs the reference sources)")
+            lib = ctypes.CDLL(str(REF_LIB))
+            lib.dpuf_engine_create.restype = ctypes.c_void_p
+            lib.dpuf_engine_create.argtypes = [ctypes.c_void_p] * 5
+            lib.dpuf_engine_destroy.argtypes = [ctypes.c_void_p]
+            lib.dpuf_engine_reset_cache.argtypes = [ctypes.c_void_p]
+            lib.dpuf_engine_forward_batch.restype = ctypes.c_int32
+            lib.dpuf_engine_forward_batch.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+            lib.dpuf_matmul_qr_hadamard4_packed_f32.argtypes = [ctypes.c_int32] * 4 + [ctypes.c_void_p] * 5
+            lib.dpuf_embed_qr_hadamard4_packed_f32.argtypes = [ctypes.c_int32, ctypes.c_int32] + [ctypes.c_void_p] * 5
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, model, n_threads: int = 8):
+        self.lib = self.lib_()
+        self.model = model
+        model.cfg.n_threads = n_threads
+        self.h = self.lib.dpuf_engine_create(*model.create_args())
+        model.cfg.n_threads = 8
+        if not self.h:
+            raise RuntimeError("reference dpuf_engine_create failed")
+        self.vocab = model.shape.vocab
+
+    def close(self):
+        if self.h:
+            self.lib.dpuf_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        self.lib.dpuf_engine_reset_cache(self.h)
+
+    def forward(self, ids, pos0: int, only_last: int = 1):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        M = len(ids)
+        out = np.empty((1 if only_last == 1 else M, self.vocab), dtype=np.float32)
+        rc = self.lib.dpuf_engine_forward_batch(self.h, M, ids.ctypes.data, pos0, only_last,
+                                                out.ctypes.data if only_last != 2 else None)
+        if rc != 0:
+            raise RuntimeError(f"reference forward -> {rc}")
+        return out
+
+
+def oracle_matmul(M, blob, x):
+    """Standalone mode-12 matmul through the C restatement: out[M][rows]."""
+    lib = OracleEngine.lib_()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty((M, blob.rows), dtype=np.float32)
+    lib.orc_matmul_mode12_f32(M, blob.rows, blob.cols, blob.n_tiles, x.ctypes.data, blob.tiles.ctypes.data,
+                              blob.tile_offsets.ctypes.data, blob.sign_bits.ctypes.data, out.ctypes.data)
+    return out
+
+
+def ref_matmul(M, blob, x):
+    lib = RefEngine.lib_()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty((M, blob.rows), dtype=np.float32)
+    lib.dpuf_matmul_qr_hadamard4_packed_f32(M, blob.rows, blob.cols, blob.n_tiles, x.ctypes.data,
+                                            blob.tiles.ctypes.data, blob.tile_offsets.ctypes.data,
+                                            blob.sign_bits.ctypes.data, out.ctypes.data)
+    return out
+
+
+def greedy_run(engine, prompt, n_decode: int):
+    """pp(prompt) + n_decode greedy steps at batch 1 (run_turn_ex, dpuf-cli.c:2344-2420).
+    Returns (generated ids, list of per-step logits [prefill last + each decode step])."""
+    engine.reset()
+    logits = [engine.forward(prompt, 0, 1)[0].copy()]
+    ids = []
+    pos = len(prompt)
+    for _ in range(n_decode):
+        nxt = int(np.argmax(logits[-1]))
+        ids.append(nxt)
+        logits.append(engine.forward(np.array([nxt], np.int32), pos, 1)[0].copy())
+        pos += 1
+    return ids, logits
+
+
+def cpu_model_string() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
