@@ -28,11 +28,11 @@ CUDA_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CUDA_SOURCES = [
     "engine.cu",
+    "expf_table.cu",
     "kernels_mode12.cu",
     "kernels_layer.cu",
     "kernels_attn.cu",
     "kernels_lmhead.cu",
-    "kernels_gemm_tc.cu",
     "ops_abi.cu",
 ]
 
@@ -60,13 +60,13 @@ def build_pack(force: bool = False) -> pathlib.Path:
 
 def build_cuda(force: bool = False, extra: list[str] | None = None) -> pathlib.Path:
     srcs = [CSRC / s for s in CUDA_SOURCES]
-    deps = srcs + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    deps = srcs + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     if force or extra or _stale(CUDA_LIB, deps):
         objdir = PKG_DIR / "_build"
         objdir.mkdir(exist_ok=True)
         objs = []
         common = [NVCC, *CUDA_ARCH, "-O3", "-lineinfo", "-std=c++17", "--fmad=false",
-                  "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", str(INCLUDE), "-I", str(CSRC),
+                  "-Xcompiler", "-fPIC,-fvisibility=hidden,-ffp-contract=off", "-I", str(INCLUDE), "-I", str(CSRC),
                   "-Xptxas", "-warn-spills", *(extra or [])]
         for s in srcs:
             o = objdir / (s.stem + ".o")

@@ -1,0 +1,794 @@
+// engine.cu - the persistent DPUF engine on one B200, behind the reference's C ABI
+// (dpuf_kernels.h:316-360; semantics of dpuf_engine.c:1182-2170).
+//
+// Device memory layout (all resident for the engine's lifetime):
+//   weight arena   every mode-12 matrix in container layout (tiles, tile offsets rebased to
+//                  the tile span, sign bits), norm gains, RoPE tables - uploaded once at create
+//   KV slots       up to 8 caches [L][n_kv][max_seq][hd] fp32, allocated on first use
+//   prefixes       up to 8 frozen prefixes [L][n_kv][len][hd]
+//   activations    h, hn, q, k, v, att, gate, up [256][dim] fp32; three prep slots (int8
+//                  codes, block scales, block sums); logits [256][vocab]
+// A forward step is one stream of kernels (see enqueue_step) captured once per shape and
+// environment knobs into a CUDA graph; token ids and the start position are copied from
+// pinned staging by the graph itself, so one graph serves every position.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <set>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "dpuf_cuda.h"
+#include "dpuf_kernels.h"
+#include "engine_internal.h"
+#include "kernels.cuh"
+
+namespace dpuf {
+
+namespace {
+thread_local std::string g_err;
+}
+void set_error(const std::string& msg) { g_err = msg; }
+
+cudaError_t configure_mode12_kernels();
+cudaError_t configure_layer_kernels();
+cudaError_t configure_attn_kernels();
+cudaError_t configure_kernels() {
+  cudaError_t e;
+  if ((e = configure_mode12_kernels()) != cudaSuccess) return e;
+  if ((e = configure_layer_kernels()) != cudaSuccess) return e;
+  return configure_attn_kernels();
+}
+
+namespace {
+
+constexpr int kMaxSlots = 8;
+constexpr int kMaxPrefixes = 8;
+
+#define CK(expr)                                                                                  \
+  do {                                                                                            \
+    cudaError_t _e = (expr);                                                                      \
+    if (_e != cudaSuccess) {                                                                      \
+      set_error(std::string(#expr) + ": " + cudaGetErrorString(_e) + " (" __FILE__ ":" +         \
+                std::to_string(__LINE__) + ")");                                                  \
+      return _e;                                                                                  \
+    }                                                                                             \
+  } while (0)
+
+struct LayerDev {
+  W12 q, k, v, o, gate, up, down;
+  const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+};
+
+struct Slot {
+  float* k = nullptr;
+  float* v = nullptr;
+};
+struct Prefix {
+  float* k = nullptr;
+  float* v = nullptr;
+  int len = 0, cap = 0;
+  bool valid = false;
+};
+
+struct StepKey {
+  int M, only_last, keep, za;
+  uint32_t margin_bits;
+  int slot;
+  bool operator<(const StepKey& o) const {
+    return std::tie(M, only_last, keep, za, margin_bits, slot) <
+           std::tie(o.M, o.only_last, o.keep, o.za, o.margin_bits, o.slot);
+  }
+};
+
+// Pinned staging shared by the host and the captured graphs.
+struct Staging {
+  int32_t ids[kMaxBatch];
+  int32_t pos0;
+  int32_t pad[3];
+};
+
+struct Engine {
+  DpufModelConfig cfg;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool use_pdl = true, use_graphs = true;
+  int H, I, L, nq, nkv, hd, qd, kvd, V, S, act_ld;
+  float deadzone = 0.005f;
+  int nt_ref = 8;
+
+  unsigned char* arena = nullptr;
+  std::vector<LayerDev> layers;
+  W12 tok, lm;
+  const float* out_norm = nullptr;
+  float *cos_tab = nullptr, *sin_tab = nullptr;
+
+  Slot slots[kMaxSlots];
+  int active = 0;
+  Prefix prefixes[kMaxPrefixes];
+
+  float *h = nullptr, *hn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *gate = nullptr,
+        *up = nullptr, *logits = nullptr;
+  Act prep[3];
+  int8_t* prep_q8 = nullptr;
+  float* prep_xs = nullptr;
+  int32_t* prep_xm = nullptr;
+  int32_t* d_ids = nullptr;
+  int32_t* d_pos0 = nullptr;
+  int* d_flag = nullptr;
+  float* d_b12 = nullptr;
+  int32_t* d_argmax = nullptr;
+  Staging* stage = nullptr;  // pinned
+  float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
+  uint32_t* d_exp_keys = nullptr;
+  uint32_t* d_exp_vals = nullptr;
+  ExpfTable et{};
+
+  std::map<StepKey, cudaGraphExec_t> graphs;
+  // last step
+  int last_rows = 0, last_zone_used = 0;
+};
+
+// ------------------------------------------------------------------ helpers
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Bytes of tile data of a matrix: from its first tile to the end of its last tile (computed
+// from the last tile's row count, since the tile offset array has n_tiles entries in the ABI).
+size_t tile_span(const DpufWeightDesc& w, uint64_t* base_off) {
+  uint64_t lo = w.tile_offsets[0], hi = 0;
+  const int n_blk = w.cols / 32;
+  for (int t = 0; t < w.n_tiles; t++) {
+    const uint8_t* tp = w.tensor_base + w.tile_offsets[t];
+    const int n_r = tp[4] | (tp[5] << 8);
+    const uint64_t end = w.tile_offsets[t] + 16 + (uint64_t)((n_r + 7) / 8) * n_blk * 144;
+    lo = std::min<uint64_t>(lo, w.tile_offsets[t]);
+    hi = std::max<uint64_t>(hi, end);
+  }
+  *base_off = lo;
+  return (size_t)(hi - lo);
+}
+
+bool desc_ok(const DpufWeightDesc& w, int rows, int cols) {
+  if (w.mode != DPUF_MODE_QR_HAD4_PACKED || !w.tensor_base || !w.tile_offsets || !w.sign_bits) return false;
+  if (w.rows != rows || w.cols != cols || (cols % 64) != 0) return false;
+  if (w.n_tiles != (rows + kTileRows - 1) / kTileRows) return false;
+  return true;
+}
+
+// Arena builder: first pass sizes, second pass uploads.  Matrices shared by pointer (tied
+// embeddings) are uploaded once.
+struct ArenaPlan {
+  size_t bytes = 0;
+  std::map<const uint8_t*, size_t> tile_at, toff_at, sign_at;
+  std::map<std::string, size_t> sign_by_content;  // equal sign tables share one device copy
+  std::map<const float*, size_t> f32_at;
+};
+
+void plan_w(ArenaPlan& P, const DpufWeightDesc& w) {
+  if (P.tile_at.count(w.tensor_base)) return;
+  uint64_t base;
+  const size_t span = tile_span(w, &base);
+  P.tile_at[w.tensor_base] = P.bytes;
+  P.bytes = align256(P.bytes + span);
+  P.toff_at[w.tensor_base] = P.bytes;
+  P.bytes = align256(P.bytes + (size_t)w.n_tiles * 8);
+  const std::string key((const char*)w.sign_bits, (size_t)w.cols / 8);
+  auto it = P.sign_by_content.find(key);
+  if (it == P.sign_by_content.end()) {
+    it = P.sign_by_content.emplace(key, P.bytes).first;
+    P.bytes = align256(P.bytes + (size_t)w.cols / 8);
+  }
+  P.sign_at[w.tensor_base] = it->second;
+}
+
+void plan_f(ArenaPlan& P, const float* f, int n) {
+  if (!f || P.f32_at.count(f)) return;
+  P.f32_at[f] = P.bytes;
+  P.bytes = align256(P.bytes + (size_t)n * 4);
+}
+
+cudaError_t upload_w(Engine* e, const ArenaPlan& P, const DpufWeightDesc& w, W12* out, std::set<size_t>& done) {
+  const size_t t_at = P.tile_at.at(w.tensor_base);
+  out->tiles = e->arena + t_at;
+  out->toff = (const uint64_t*)(e->arena + P.toff_at.at(w.tensor_base));
+  out->signs = e->arena + P.sign_at.at(w.tensor_base);
+  out->rows = w.rows;
+  out->cols = w.cols;
+  out->n_tiles = w.n_tiles;
+  if (!done.insert(t_at).second) return cudaSuccess;
+  uint64_t base;
+  const size_t span = tile_span(w, &base);
+  CK(cudaMemcpy(e->arena + t_at, w.tensor_base + base, span, cudaMemcpyHostToDevice));
+  std::vector<uint64_t> toff(w.n_tiles);
+  for (int t = 0; t < w.n_tiles; t++) toff[t] = w.tile_offsets[t] - base;
+  CK(cudaMemcpy((void*)out->toff, toff.data(), toff.size() * 8, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy((void*)out->signs, w.sign_bits, (size_t)w.cols / 8, cudaMemcpyHostToDevice));
+  return cudaSuccess;
+}
+
+const float* upload_f(Engine* e, const ArenaPlan& P, const float* f, int n) {
+  if (!f) return nullptr;
+  const size_t at = P.f32_at.at(f);
+  if (cudaMemcpy(e->arena + at, f, (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+  return (const float*)(e->arena + at);
+}
+
+// RoPE tables exactly as precompute_rope (dpuf_engine.c:183-223), computed on the host with
+// the same libm calls.
+void rope_tables(const DpufModelConfig& c, std::vector<float>& cs, std::vector<float>& sn) {
+  const int hd = c.head_dim, half = hd / 2;
+  std::vector<float> inv(half);
+  for (int j = 0; j < half; j++) {
+    float freq = 1.0f / powf(c.rope_theta, (float)(2 * j) / (float)hd);
+    if (c.use_llama3_rope) {
+      const float factor = c.rope_factor, low_f = c.rope_low_freq, high_f = c.rope_high_freq;
+      const float orig = (float)c.rope_orig_max_pos;
+      const float wavelen = (2.0f * (float)3.14159265358979323846) / freq;
+      const float low_w = orig / low_f, high_w = orig / high_f;
+      if (wavelen > low_w) {
+        freq /= factor;
+      } else if (wavelen >= high_w) {
+        const float smooth = (orig / wavelen - low_f) / (high_f - low_f);
+        freq = (1.0f - smooth) * (freq / factor) + smooth * freq;
+      }
+    }
+    inv[j] = freq;
+  }
+  cs.resize((size_t)c.max_seq_len * half);
+  sn.resize(cs.size());
+  for (int p = 0; p < c.max_seq_len; p++) {
+    const float pf = (float)p;
+    for (int j = 0; j < half; j++) {
+      const float ang = pf * inv[j];
+      cs[(size_t)p * half + j] = cosf(ang);
+      sn[(size_t)p * half + j] = sinf(ang);
+    }
+  }
+}
+
+cudaError_t slot_alloc(Engine* e, int s) {
+  if (e->slots[s].k) return cudaSuccess;
+  const size_t n = (size_t)e->L * e->S * e->kvd;
+  CK(cudaMalloc(&e->slots[s].k, n * 4));
+  CK(cudaMalloc(&e->slots[s].v, n * 4));
+  CK(cudaMemset(e->slots[s].k, 0, n * 4));
+  CK(cudaMemset(e->slots[s].v, 0, n * 4));
+  return cudaSuccess;
+}
+
+void destroy_engine(Engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& s : e->slots) { cudaFree(s.k); cudaFree(s.v); }
+  for (auto& p : e->prefixes) { cudaFree(p.k); cudaFree(p.v); }
+  cudaFree(e->arena);
+  cudaFree(e->cos_tab); cudaFree(e->sin_tab);
+  cudaFree(e->h); cudaFree(e->hn); cudaFree(e->q); cudaFree(e->k); cudaFree(e->v); cudaFree(e->att);
+  cudaFree(e->gate); cudaFree(e->up); cudaFree(e->logits);
+  cudaFree(e->prep_q8); cudaFree(e->prep_xs); cudaFree(e->prep_xm);
+  cudaFree(e->d_ids); cudaFree(e->d_pos0); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
+  cudaFree(e->d_exp_keys); cudaFree(e->d_exp_vals);
+  cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+// ------------------------------------------------------------------ the forward step
+struct StepParams {
+  int M, only_last, keep, za;
+  float margin;
+};
+
+LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
+  LinJobs J = {};
+  J.n = 1;
+  J.j[0] = {w, a, out, ldo, t0, t1};
+  J.tile_prefix[0] = 0;
+  J.tile_prefix[1] = t1 - t0;
+  return J;
+}
+
+cudaError_t run_linear(const Launch& Lc, const LinJobs& J, int M, const int* skip) {
+  if (J.tile_prefix[J.n] == 0) return cudaSuccess;
+  return M == 1 ? launch_gemv(Lc, J, skip) : launch_gemm_exact(Lc, J, M);
+}
+
+// Prep targets for weights sharing one input: identical sign tables share a prep slot
+// (weights_share_prep, dpuf_engine.c:887-897).  slot_of[i] receives the slot used by w[i].
+int prep_targets(Engine* e, const W12* const* ws, int n, PrepTarget* t, int* slot_of) {
+  int nt = 0;
+  for (int i = 0; i < n; i++) {
+    int found = -1;
+    for (int j = 0; j < nt; j++)
+      if (t[j].signs == ws[i]->signs) found = j;  // same device copy <=> same sign table
+    if (found < 0) {
+      t[nt].signs = ws[i]->signs;
+      t[nt].act = e->prep[nt];
+      found = nt++;
+    }
+    slot_of[i] = found;
+  }
+  return nt;
+}
+
+cudaError_t enqueue_step(Engine* e, const StepParams& P) {
+  const Launch Lc{e->stream, e->use_pdl};
+  const int M = P.M, H = e->H;
+  CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
+  CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
+  const Slot& sl = e->slots[e->active];
+  for (int l = 0; l < e->L; l++) {
+    const LayerDev& lw = e->layers[l];
+    KvCache kv{sl.k + (size_t)l * e->nkv * e->S * e->hd, sl.v + (size_t)l * e->nkv * e->S * e->hd, e->S};
+    // 1-2. [h += hn] RMSNorm + prep of q/k/v inputs
+    {
+      const W12* ws[3] = {&lw.q, &lw.k, &lw.v};
+      PrepTarget t[3];
+      int so[3];
+      const int n = prep_targets(e, ws, 3, t, so);
+      CK(launch_norm_prep(Lc, e->h, l > 0 ? e->hn : nullptr, lw.attn_norm, e->cfg.rms_eps, M, H, t, n, nullptr));
+      LinJobs J = {};
+      float* outs[3] = {e->q, e->k, e->v};
+      const int ldo[3] = {e->qd, e->kvd, e->kvd};
+      J.n = 3;
+      J.tile_prefix[0] = 0;
+      for (int i = 0; i < 3; i++) {
+        J.j[i] = {*ws[i], e->prep[so[i]], outs[i], ldo[i], 0, ws[i]->n_tiles};
+        J.tile_prefix[i + 1] = J.tile_prefix[i] + ws[i]->n_tiles;
+      }
+      CK(run_linear(Lc, J, M, nullptr));
+    }
+    // 3-4. QK norm, RoPE, KV store; attention
+    CK(launch_qk_post(Lc, e->q, e->k, e->v, M, e->nq, e->nkv, e->hd, e->cfg.has_qk_norm ? lw.q_norm : nullptr,
+                      e->cfg.has_qk_norm ? lw.k_norm : nullptr, e->cfg.rms_eps, e->cos_tab, e->sin_tab, e->d_pos0,
+                      kv));
+    CK(launch_attention(Lc, e->q, M, e->nq, e->nkv, e->hd, e->d_pos0, kv, e->att, e->et));
+    // 5. o_proj
+    CK(launch_prep(Lc, e->att, e->qd, M, e->qd, lw.o.signs, e->prep[0]));
+    CK(run_linear(Lc, one_job(lw.o, e->prep[0], e->hn, H, 0, lw.o.n_tiles), M, nullptr));
+    // 6-8. h += o; RMSNorm; gate/up
+    {
+      const W12* ws[2] = {&lw.gate, &lw.up};
+      PrepTarget t[2];
+      int so[2];
+      const int n = prep_targets(e, ws, 2, t, so);
+      CK(launch_norm_prep(Lc, e->h, e->hn, lw.ffn_norm, e->cfg.rms_eps, M, H, t, n, nullptr));
+      LinJobs J = {};
+      J.n = 2;
+      J.tile_prefix[0] = 0;
+      J.j[0] = {lw.gate, e->prep[so[0]], e->gate, e->I, 0, lw.gate.n_tiles};
+      J.tile_prefix[1] = lw.gate.n_tiles;
+      J.j[1] = {lw.up, e->prep[so[1]], e->up, e->I, 0, lw.up.n_tiles};
+      J.tile_prefix[2] = lw.gate.n_tiles + lw.up.n_tiles;
+      CK(run_linear(Lc, J, M, nullptr));
+    }
+    // 9-11. SwiGLU + prep, down (optionally pruned to the first `keep` tiles)
+    CK(launch_swiglu_prep(Lc, e->gate, e->up, M, e->I, e->deadzone, e->nt_ref, lw.down.signs, e->prep[0], e->et));
+    const int keep = (P.keep > 0 && P.keep < lw.down.n_tiles) ? P.keep : lw.down.n_tiles;
+    CK(run_linear(Lc, one_job(lw.down, e->prep[0], e->hn, H, 0, keep), M, nullptr));
+    if (keep < lw.down.n_tiles) CK(launch_zero_rows(Lc, e->hn, M, H, keep * kTileRows));
+  }
+  if (P.only_last == 2) return cudaSuccess;
+  const int lm_start = P.only_last ? M - 1 : 0, lm_M = M - lm_start;
+  {
+    const W12* ws[1] = {&e->lm};
+    PrepTarget t[1];
+    int so[1];
+    prep_targets(e, ws, 1, t, so);
+    CK(launch_norm_prep(Lc, e->h + (size_t)lm_start * H, e->L > 0 ? e->hn + (size_t)lm_start * H : nullptr,
+                        e->out_norm, e->cfg.rms_eps, lm_M, H, t, 1, nullptr));
+  }
+  if (P.za > 0) {
+    const int n_za = std::min(P.za * kTileRows, e->V);
+    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, P.za), 1, nullptr));
+    CK(launch_zone_test(Lc, e->logits, n_za, P.margin, e->d_flag, e->d_b12));
+    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, P.za, e->lm.n_tiles), 1, e->d_flag));
+    CK(launch_zone_mask(Lc, e->logits, P.za * kTileRows, e->V, e->d_flag));
+  } else {
+    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, e->lm.n_tiles), lm_M, nullptr));
+  }
+  return cudaSuccess;
+}
+
+cudaError_t run_step(Engine* e, const StepParams& P) {
+  if (!e->use_graphs) return enqueue_step(e, P);
+  uint32_t mb;
+  memcpy(&mb, &P.margin, 4);
+  const StepKey key{P.M, P.only_last, P.keep, P.za, mb, e->active};
+  auto it = e->graphs.find(key);
+  if (it == e->graphs.end()) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t err = enqueue_step(e, P);
+    cudaError_t err2 = cudaStreamEndCapture(e->stream, &g);
+    if (err != cudaSuccess) return err;
+    CK(err2);
+    cudaGraphExec_t ge;
+    err = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    CK(err);
+    it = e->graphs.emplace(key, ge).first;
+  }
+  CK(cudaGraphLaunch(it->second, e->stream));
+  return cudaSuccess;
+}
+
+void drop_graphs(Engine* e) {
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  e->graphs.clear();
+}
+
+int env_int(const char* name, int def) {
+  const char* s = getenv(name);
+  return s ? atoi(s) : def;
+}
+
+// Validation and environment knobs of dpuf_engine_forward_batch_ex (dpuf_engine.c:1639-1641,
+// 2022-2027, 2091-2118), then one step.
+int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, const float* embeds,
+                       const int32_t* pt, const int32_t* ph, const int32_t* pw, const float* const* ds,
+                       int32_t only_last, float* logits_out, bool want_logits) {
+  if (!e || (!ids && !embeds) || (want_logits && !logits_out && only_last != 2)) return -1;
+  if (n <= 0 || n > kMaxBatch) return -2;
+  if (pos0 < 0 || pos0 + n > e->S) return -3;
+  if (embeds || ds) {
+    set_error("embeds_in / deepstack_in are not supported by this engine");
+    return -5;
+  }
+  if (e->cfg.has_mrope && (pt || ph || pw)) {
+    set_error("M-RoPE positions are not supported by this engine");
+    return -5;
+  }
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= e->tok.rows) {
+      set_error("token id out of range");
+      return -1;
+    }
+  if (cudaSetDevice(e->device) != cudaSuccess) return -4;
+  StepParams P{};
+  P.M = n;
+  P.only_last = only_last == 0 ? 0 : (only_last == 2 ? 2 : 1);
+  P.keep = 0;
+  if (const char* kt = getenv(n > 1 ? "DPUF_PREFILL_KEEP_TILES" : "DPUF_GEN_KEEP_TILES")) {
+    const int v = atoi(kt);
+    P.keep = (v > 0) ? v : 0;
+  }
+  const int lm_M = P.only_last == 1 ? 1 : n;
+  P.za = 0;
+  P.margin = 0.0f;
+  const char* env_t = getenv("DPUF_EARLY_TILES");
+  if (env_t && P.only_last != 2 && lm_M == 1 && e->lm.n_tiles > 2048) {
+    int za = atoi(env_t);
+    za = std::max(za, 256);
+    za = std::min(za, e->lm.n_tiles);
+    P.za = za;
+    const char* env_m = getenv("DPUF_EARLY_MARGIN");
+    P.margin = env_m ? (float)atof(env_m) : 1.25f;
+  }
+  memcpy(e->stage->ids, ids, (size_t)n * 4);
+  e->stage->pos0 = pos0;
+  cudaError_t err = run_step(e, P);
+  if (err != cudaSuccess) return -4;
+  e->last_zone_used = P.za > 0;
+  e->last_rows = P.only_last == 2 ? 0 : lm_M;
+  if (P.only_last != 2 && want_logits) {
+    const size_t bytes = (size_t)lm_M * e->V * 4;
+    if (lm_M == 1) {
+      if (cudaMemcpyAsync(e->h_logits, e->logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess) return -4;
+      if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+      memcpy(logits_out, e->h_logits, bytes);
+    } else {
+      if (cudaMemcpyAsync(logits_out, e->logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess) return -4;
+      if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+    }
+  } else {
+    if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+  }
+  cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) {
+    set_error(cudaGetErrorString(le));
+    return -4;
+  }
+  return 0;
+}
+
+Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers, const DpufWeightDesc* tok,
+                      const DpufWeightDesc* lm, const float* out_norm) {
+  if (!cfg || !layers || !tok || !lm || !out_norm) return nullptr;
+  const DpufModelConfig& c = *cfg;
+  if (c.hidden_size <= 0 || c.num_layers < 0 || c.num_q_heads <= 0 || c.num_kv_heads <= 0 ||
+      c.num_q_heads % c.num_kv_heads != 0 || c.head_dim <= 0 || c.head_dim % 32 != 0 || c.head_dim > 256 ||
+      c.max_seq_len <= 0 || c.kv_type != DPUF_KV_F32 || c.hidden_size % 64 != 0 || c.intermediate_size % 64 != 0 ||
+      (c.num_q_heads * c.head_dim) % 64 != 0) {
+    set_error("unsupported model configuration");
+    return nullptr;
+  }
+  const int H = c.hidden_size, I = c.intermediate_size, qd = c.num_q_heads * c.head_dim,
+            kvd = c.num_kv_heads * c.head_dim;
+  for (int l = 0; l < c.num_layers; l++) {
+    const DpufLayerWeights& w = layers[l];
+    if (!desc_ok(w.w_q, qd, H) || !desc_ok(w.w_k, kvd, H) || !desc_ok(w.w_v, kvd, H) || !desc_ok(w.w_o, H, qd) ||
+        !desc_ok(w.w_gate, I, H) || !desc_ok(w.w_up, I, H) || !desc_ok(w.w_down, H, I) || !w.attn_norm ||
+        !w.ffn_norm) {
+      set_error("layer " + std::to_string(l) + ": weights must be mode 12 with matching shapes");
+      return nullptr;
+    }
+  }
+  if (!desc_ok(*tok, tok->rows, H) || !desc_ok(*lm, c.vocab_size, H)) {
+    set_error("embedding / LM head must be mode 12 with cols == hidden_size");
+    return nullptr;
+  }
+  Engine* e = new Engine();
+  e->cfg = c;
+  if (cudaGetDevice(&e->device) != cudaSuccess) { delete e; return nullptr; }
+  if (const char* d = getenv("DPUF_CUDA_DEVICE")) {
+    e->device = atoi(d);
+    if (cudaSetDevice(e->device) != cudaSuccess) { delete e; return nullptr; }
+  }
+  e->H = H; e->I = I; e->L = c.num_layers; e->nq = c.num_q_heads; e->nkv = c.num_kv_heads; e->hd = c.head_dim;
+  e->qd = qd; e->kvd = kvd; e->V = c.vocab_size; e->S = c.max_seq_len;
+  e->act_ld = std::max(std::max(H, I), qd);
+  const char* dz = getenv("DPUF_SWIGLU_DEADZONE");
+  e->deadzone = dz ? (float)atof(dz) : 0.005f;
+  e->nt_ref = c.n_threads <= 0 ? 8 : std::min(c.n_threads, 32);
+  e->use_pdl = env_int("DPUF_CUDA_PDL", 1) != 0;
+  e->use_graphs = env_int("DPUF_CUDA_GRAPHS", 1) != 0;
+
+  auto fail = [&](const char* what) -> Engine* {
+    if (g_err.empty()) set_error(what);
+    destroy_engine(e);
+    return nullptr;
+  };
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+  if (cudaError_t ce = configure_kernels()) {
+    set_error(std::string("kernel attributes: ") + cudaGetErrorString(ce));
+    return fail("kernel attributes");
+  }
+
+  // ---- weights
+  ArenaPlan P;
+  for (int l = 0; l < c.num_layers; l++) {
+    const DpufLayerWeights& w = layers[l];
+    for (const DpufWeightDesc* d : {&w.w_q, &w.w_k, &w.w_v, &w.w_o, &w.w_gate, &w.w_up, &w.w_down}) plan_w(P, *d);
+    plan_f(P, w.attn_norm, H);
+    plan_f(P, w.ffn_norm, H);
+    plan_f(P, w.attn_q_norm, c.head_dim);
+    plan_f(P, w.attn_k_norm, c.head_dim);
+  }
+  plan_w(P, *tok);
+  plan_w(P, *lm);
+  plan_f(P, out_norm, H);
+  if (cudaMalloc(&e->arena, P.bytes) != cudaSuccess) return fail("weight arena allocation");
+  std::set<size_t> done;
+  e->layers.resize(c.num_layers);
+  for (int l = 0; l < c.num_layers; l++) {
+    const DpufLayerWeights& w = layers[l];
+    LayerDev& d = e->layers[l];
+    if (upload_w(e, P, w.w_q, &d.q, done) || upload_w(e, P, w.w_k, &d.k, done) || upload_w(e, P, w.w_v, &d.v, done) ||
+        upload_w(e, P, w.w_o, &d.o, done) || upload_w(e, P, w.w_gate, &d.gate, done) ||
+        upload_w(e, P, w.w_up, &d.up, done) || upload_w(e, P, w.w_down, &d.down, done))
+      return fail("weight upload");
+    d.attn_norm = upload_f(e, P, w.attn_norm, H);
+    d.ffn_norm = upload_f(e, P, w.ffn_norm, H);
+    d.q_norm = upload_f(e, P, w.attn_q_norm, c.head_dim);
+    d.k_norm = upload_f(e, P, w.attn_k_norm, c.head_dim);
+    if (!d.attn_norm || !d.ffn_norm) return fail("norm upload");
+  }
+  if (upload_w(e, P, *tok, &e->tok, done) || upload_w(e, P, *lm, &e->lm, done)) return fail("embedding upload");
+  e->out_norm = upload_f(e, P, out_norm, H);
+  if (!e->out_norm) return fail("norm upload");
+
+  // ---- RoPE tables
+  {
+    std::vector<float> cs, sn;
+    rope_tables(c, cs, sn);
+    if (cudaMalloc(&e->cos_tab, cs.size() * 4) || cudaMalloc(&e->sin_tab, sn.size() * 4) ||
+        cudaMemcpy(e->cos_tab, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) ||
+        cudaMemcpy(e->sin_tab, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice))
+      return fail("rope tables");
+  }
+  // ---- expf exception table
+  {
+    const auto& keys = expf_exception_keys();
+    const auto& vals = expf_exception_vals();
+    if (cudaMalloc(&e->d_exp_keys, keys.size() * 4 + 4) || cudaMalloc(&e->d_exp_vals, vals.size() * 4 + 4) ||
+        cudaMemcpy(e->d_exp_keys, keys.data(), keys.size() * 4, cudaMemcpyHostToDevice) ||
+        cudaMemcpy(e->d_exp_vals, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice))
+      return fail("expf table");
+    e->et = ExpfTable{e->d_exp_keys, e->d_exp_vals, (int)keys.size()};
+  }
+  // ---- activations
+  const size_t B = kMaxBatch;
+  const int ld = e->act_ld;
+  if (cudaMalloc(&e->h, B * H * 4) || cudaMalloc(&e->hn, B * H * 4) || cudaMalloc(&e->q, B * qd * 4) ||
+      cudaMalloc(&e->k, B * kvd * 4) || cudaMalloc(&e->v, B * kvd * 4) ||
+      cudaMalloc(&e->att, B * std::max(qd, H) * 4) || cudaMalloc(&e->gate, B * I * 4) ||
+      cudaMalloc(&e->up, B * I * 4) || cudaMalloc(&e->logits, B * (size_t)e->V * 4) ||
+      cudaMalloc(&e->prep_q8, 3 * B * ld) || cudaMalloc(&e->prep_xs, 3 * B * (ld / 32) * 4) ||
+      cudaMalloc(&e->prep_xm, 3 * B * (ld / 32) * 4) || cudaMalloc(&e->d_ids, sizeof(Staging)) ||
+      cudaMalloc(&e->d_flag, 16) || cudaMalloc(&e->d_b12, 16) || cudaMalloc(&e->d_argmax, B * 4) ||
+      cudaMallocHost(&e->stage, sizeof(Staging)) || cudaMallocHost(&e->h_logits, (size_t)e->V * 4))
+    return fail("activation buffers");
+  e->d_pos0 = e->d_ids + kMaxBatch;
+  for (int i = 0; i < 3; i++)
+    e->prep[i] = Act{e->prep_q8 + i * B * ld, e->prep_xs + i * B * (ld / 32), e->prep_xm + i * B * (ld / 32), ld};
+  cudaMemset(e->d_flag, 0, 16);
+  if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
+  return e;
+}
+
+}  // namespace
+}  // namespace dpuf
+
+using dpuf::Engine;
+
+// ==================================================================== C ABI
+extern "C" {
+
+DPUF_EXPORT const char* dpuf_cuda_last_error(void) { return dpuf::g_err.c_str(); }
+
+DPUF_EXPORT void* dpuf_engine_create(const DpufModelConfig* cfg, const DpufLayerWeights* layers,
+                                     const DpufWeightDesc* w_tok_embd, const DpufWeightDesc* w_lm_head,
+                                     const float* output_norm) {
+  dpuf::g_err.clear();
+  return dpuf::create_engine(cfg, layers, w_tok_embd, w_lm_head, output_norm);
+}
+
+DPUF_EXPORT void dpuf_engine_destroy(void* handle) { dpuf::destroy_engine((Engine*)handle); }
+
+DPUF_EXPORT int32_t dpuf_engine_set_slot(void* handle, int32_t slot_id) {
+  Engine* e = (Engine*)handle;
+  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots) return -1;
+  cudaSetDevice(e->device);
+  if (dpuf::slot_alloc(e, slot_id) != cudaSuccess) return -2;
+  e->active = slot_id;
+  return 0;
+}
+
+DPUF_EXPORT int32_t dpuf_engine_get_slot(void* handle) { return handle ? ((Engine*)handle)->active : 0; }
+
+DPUF_EXPORT int32_t dpuf_engine_num_slots(void* handle) { return handle ? dpuf::kMaxSlots : 1; }
+
+DPUF_EXPORT void dpuf_engine_reset_slot(void* handle, int32_t slot_id) {
+  Engine* e = (Engine*)handle;
+  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots || !e->slots[slot_id].k) return;
+  cudaSetDevice(e->device);
+  const size_t n = (size_t)e->L * e->S * e->kvd * 4;
+  cudaMemsetAsync(e->slots[slot_id].k, 0, n, e->stream);
+  cudaMemsetAsync(e->slots[slot_id].v, 0, n, e->stream);
+  cudaStreamSynchronize(e->stream);
+}
+
+DPUF_EXPORT void dpuf_engine_reset_cache(void* handle) {
+  Engine* e = (Engine*)handle;
+  if (e) dpuf_engine_reset_slot(handle, e->active);
+}
+
+DPUF_EXPORT size_t dpuf_engine_slot_memory(void* handle) {
+  Engine* e = (Engine*)handle;
+  return e ? 2 * (size_t)e->L * e->S * e->kvd * sizeof(float) : 0;
+}
+
+// Freeze / apply copy [L][n_kv][len][hd] between the active slot and a prefix store with one
+// strided device copy (dpuf_engine.c:1509-1594).
+DPUF_EXPORT int32_t dpuf_engine_freeze_prefix(void* handle, int32_t pfx_id, int32_t prefix_len) {
+  Engine* e = (Engine*)handle;
+  if (!e || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes || prefix_len <= 0 || prefix_len > e->S) return 0;
+  cudaSetDevice(e->device);
+  dpuf::Prefix& p = e->prefixes[pfx_id];
+  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd;
+  if (p.cap < prefix_len || !p.k) {
+    cudaFree(p.k);
+    cudaFree(p.v);
+    p = dpuf::Prefix();
+    if (cudaMalloc(&p.k, rows * prefix_len * hd * 4) != cudaSuccess) { p.k = nullptr; return 0; }
+    if (cudaMalloc(&p.v, rows * prefix_len * hd * 4) != cudaSuccess) { cudaFree(p.k); p.k = nullptr; p.v = nullptr; return 0; }
+    p.cap = prefix_len;
+  }
+  const dpuf::Slot& s = e->slots[e->active];
+  if (!s.k) return 0;
+  const size_t w = (size_t)prefix_len * hd * 4;
+  if (cudaMemcpy2DAsync(p.k, w, s.k, (size_t)e->S * hd * 4, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(p.v, w, s.v, (size_t)e->S * hd * 4, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaStreamSynchronize(e->stream))
+    return 0;
+  p.len = prefix_len;
+  p.valid = true;
+  return 1;
+}
+
+DPUF_EXPORT int32_t dpuf_engine_apply_prefix(void* handle, int32_t slot_id, int32_t pfx_id) {
+  Engine* e = (Engine*)handle;
+  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes) return 0;
+  dpuf::Prefix& p = e->prefixes[pfx_id];
+  if (!p.valid || p.len <= 0) return 0;
+  cudaSetDevice(e->device);
+  if (dpuf::slot_alloc(e, slot_id) != cudaSuccess) return 0;
+  const dpuf::Slot& s = e->slots[slot_id];
+  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd, w = (size_t)p.len * hd * 4;
+  if (cudaMemcpy2DAsync(s.k, (size_t)e->S * hd * 4, p.k, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(s.v, (size_t)e->S * hd * 4, p.v, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaStreamSynchronize(e->stream))
+    return 0;
+  return p.len;
+}
+
+DPUF_EXPORT int32_t dpuf_engine_get_prefix_len(void* handle, int32_t pfx_id) {
+  Engine* e = (Engine*)handle;
+  if (!e || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes) return 0;
+  return e->prefixes[pfx_id].valid ? e->prefixes[pfx_id].len : 0;
+}
+
+DPUF_EXPORT int32_t dpuf_engine_forward_batch_ex(void* handle, int32_t n_tokens, const int32_t* token_ids,
+                                                 int32_t pos0, const float* embeds_in, const int32_t* pos_t,
+                                                 const int32_t* pos_h, const int32_t* pos_w,
+                                                 const float* const* deepstack_in, int32_t only_last_logits,
+                                                 float* logits_out) {
+  return dpuf::forward_common((Engine*)handle, n_tokens, token_ids, pos0, embeds_in, pos_t, pos_h, pos_w,
+                              deepstack_in, only_last_logits, logits_out, true);
+}
+
+DPUF_EXPORT int32_t dpuf_engine_forward_batch(void* handle, int32_t n_tokens, const int32_t* token_ids, int32_t pos0,
+                                              int32_t only_last_logits, float* logits_out) {
+  return dpuf::forward_common((Engine*)handle, n_tokens, token_ids, pos0, nullptr, nullptr, nullptr, nullptr,
+                              nullptr, only_last_logits, logits_out, true);
+}
+
+DPUF_EXPORT int32_t dpuf_engine_forward_token(void* handle, int32_t token_id, int32_t pos, float* logits_out) {
+  const int32_t id = token_id;
+  return dpuf_engine_forward_batch(handle, 1, &id, pos, 1, logits_out);
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, const int32_t* token_ids, int32_t pos0,
+                                             int32_t* next_id) {
+  Engine* e = (Engine*)handle;
+  if (!e || !next_id) return -1;
+  const int32_t rc = dpuf::forward_common(e, n_tokens, token_ids, pos0, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                          1, nullptr, false);
+  if (rc != 0) return rc;
+  const dpuf::Launch Lc{e->stream, false};
+  if (dpuf::launch_argmax(Lc, e->logits, 1, e->V, e->V, e->d_argmax) != cudaSuccess ||
+      cudaMemcpyAsync(next_id, e->d_argmax, 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
+      cudaStreamSynchronize(e->stream) != cudaSuccess)
+    return -4;
+  return 0;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out) {
+  Engine* e = (Engine*)handle;
+  if (!e || !out || row < 0 || row >= e->last_rows) return -1;
+  cudaSetDevice(e->device);
+  if (cudaMemcpy(out, e->logits + (size_t)row * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
+  return 0;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t value) {
+  Engine* e = (Engine*)handle;
+  if (!e || !name) return -1;
+  if (!strcmp(name, "pdl")) { e->use_pdl = value != 0; dpuf::drop_graphs(e); return 0; }
+  if (!strcmp(name, "graphs")) { e->use_graphs = value != 0; dpuf::drop_graphs(e); return 0; }
+  return -1;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2) {
+  Engine* e = (Engine*)handle;
+  if (!e) return -1;
+  int flag = 0;
+  float b[2] = {0, 0};
+  cudaSetDevice(e->device);
+  if (cudaMemcpy(&flag, e->d_flag, 4, cudaMemcpyDeviceToHost) || cudaMemcpy(b, e->d_b12, 8, cudaMemcpyDeviceToHost))
+    return -4;
+  if (used) *used = e->last_zone_used;
+  if (exited) *exited = e->last_zone_used ? flag : 0;
+  if (b1) *b1 = b[0];
+  if (b2) *b2 = b[1];
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,251 @@
+// kernels_layer.cu - per-layer pointwise and row-reduction kernels with the reference's
+// exact fp32 operation order: residual add + RMSNorm + mode-12 prep, QK RMSNorm + NeoX RoPE
+// + KV-cache store, SwiGLU with dead-zone + prep of the down-projection input.
+#include "kernels.cuh"
+
+namespace dpuf {
+
+namespace {
+
+template <typename K, typename... Args>
+cudaError_t launch_k(const Launch& L, K kernel, dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = L.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+struct PrepTargets {
+  PrepTarget t[3];
+  int n;
+};
+
+// ------------------------------------------------------------------ residual + RMSNorm + prep
+// add_and_rms_norm_f32 (dpuf_engine.c:244-272): s = h + res (stored back to h); "AVX lane" j
+// accumulates fma(s_i, s_i, .) over i = j, j+8, ... in order; ss = split tree; the n % 8 tail
+// is added sequentially; inv = 1 / sqrt(ss / n + eps); out_i = (s_i * inv) * w_i.
+// One CTA per token.  Eight threads run the eight sequential chains.
+__global__ void __launch_bounds__(1024) norm_prep_kernel(float* __restrict__ h, const float* __restrict__ res,
+                                                         const float* __restrict__ w, float eps, int H, PrepTargets T,
+                                                         float* __restrict__ norm_out) {
+  extern __shared__ __align__(16) float S[];  // [H]
+  __shared__ float lanes[8];
+  __shared__ float inv_s;
+  cudaGridDependencySynchronize();
+  const int m = blockIdx.x;
+  float* hr = h + (size_t)m * H;
+  const float* rr = res ? res + (size_t)m * H : nullptr;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float s = hr[i];
+    if (rr) {
+      s = __fadd_rn(s, rr[i]);
+      hr[i] = s;
+    }
+    S[i] = s;
+  }
+  __syncthreads();
+  const int H8 = H & ~7;
+  if (threadIdx.x < 8) {
+    float acc = 0.0f;
+    int i = threadIdx.x;
+    for (; i + 56 < H8; i += 64) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = S[i + 8 * u];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = __fmaf_rn(v[u], v[u], acc);
+    }
+    for (; i < H8; i += 8) acc = __fmaf_rn(S[i], S[i], acc);
+    lanes[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ss = tree8_split_arr(lanes);
+    for (int i = H8; i < H; i++) ss = __fadd_rn(ss, __fmul_rn(S[i], S[i]));
+    inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float o = __fmul_rn(__fmul_rn(S[i], inv), w[i]);
+    S[i] = o;
+    if (norm_out) norm_out[(size_t)m * H + i] = o;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int k = 0; k < T.n; k++) {
+    const Act& a = T.t[k].act;
+    for (int c = warp; c < H / 64; c += nw) {
+      const int c0 = c * 64;
+      prep_chunk_warp(S[c0 + lane], S[c0 + 32 + lane], T.t[k].signs, c0, lane, a.q8 + (size_t)m * a.ld,
+                      a.xs + (size_t)m * (a.ld >> 5), a.xm + (size_t)m * (a.ld >> 5));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ QK-norm + RoPE + KV store
+// Per (token, head) (dpuf_engine.c:1788-1822 / 1840-1879): RMSNorm over head_dim with the
+// head's norm gain (same lane/tree order as above), NeoX rotation with host cos/sin tables
+// (apply_rope_neox_f32, dpuf_engine.c:274-295: x1*c - x2*s and x2*c + x1*s as fused
+// multiply-subtract/add of the rounded cross product), then K and V rows are written to the
+// cache at position pos0 + m.  One warp per head vector.
+__global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_q,
+                               int n_kv, int hd, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+                               float eps, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
+                               const int* __restrict__ pos0_dev, KvCache kv) {
+  extern __shared__ __align__(16) float sv[];  // [warps][hd]
+  cudaGridDependencySynchronize();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = blockIdx.x;
+  const int hidx = blockIdx.y * (blockDim.x >> 5) + warp;
+  if (hidx >= n_q + n_kv) return;
+  const int pos = *pos0_dev + m;
+  const bool is_k = hidx < n_kv;
+  const int head = is_k ? hidx : hidx - n_kv;
+  float* vec = is_k ? k + ((size_t)m * n_kv + head) * hd : q + ((size_t)m * n_q + head) * hd;
+  const float* nw = is_k ? k_norm : q_norm;
+  float* s = sv + warp * hd;
+  for (int i = lane; i < hd; i += 32) s[i] = vec[i];
+  __syncwarp();
+  if (nw) {
+    const int hd8 = hd & ~7;
+    float acc = 0.0f;
+    if (lane < 8)
+      for (int i = lane; i < hd8; i += 8) acc = __fmaf_rn(s[i], s[i], acc);
+    float ss = tree8_split(acc);  // lanes 0..7 hold the tree result
+    ss = __shfl_sync(kFull, ss, 0);
+    for (int i = hd8; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(s[i], s[i]));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) s[i] = __fmul_rn(__fmul_rn(s[i], inv), nw[i]);
+    __syncwarp();
+  }
+  const int half = hd >> 1, half8 = half & ~7;
+  const float* cp = cos_tab + (size_t)pos * half;
+  const float* sp = sin_tab + (size_t)pos * half;
+  for (int j = lane; j < half; j += 32) {
+    const float x1 = s[j], x2 = s[j + half], c = cp[j], sn = sp[j];
+    float o1, o2;
+    if (j < half8) {
+      o1 = __fmaf_rn(x1, c, -__fmul_rn(x2, sn));
+      o2 = __fmaf_rn(x2, c, __fmul_rn(x1, sn));
+    } else {
+      o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+      o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+    }
+    vec[j] = o1;
+    vec[j + half] = o2;
+    if (is_k) {
+      float* kc = kv.k + ((size_t)head * kv.max_seq + pos) * hd;
+      kc[j] = o1;
+      kc[j + half] = o2;
+    }
+  }
+  if (is_k) {
+    const float* vr = v + ((size_t)m * n_kv + head) * hd;
+    float* vc = kv.v + ((size_t)head * kv.max_seq + pos) * hd;
+    for (int i = lane; i < hd; i += 32) vc[i] = vr[i];
+  }
+}
+
+// ------------------------------------------------------------------ SwiGLU + prep for w_down
+// swiglu_range_avx2 (dpuf_engine.c:967-997): the 8-wide formula
+//   silu = g / (1 + exp_poly(clamp(0 - g, -40, 40))),  r = silu * u,  |r| < dz -> 0
+// for elements in the vector part of a thread's range, and the scalar formula (libm expf)
+// for the range's tail.  Ranges follow the reference's split of the flat [M*I] array over
+// its nt threads (dpuf_engine.c:2007-2011), or whole 6-token slabs when the reference takes
+// its slab-fused path (M >= 2 and ceil(M/6) >= nt, dpuf_engine.c:1983-2005).
+DPUF_DEV bool swiglu_vector_elem(long long idx, long long total, int nt, bool slab) {
+  if (slab) return true;
+  long long tid = (idx * nt) / total;
+  while (tid > 0 && (total * tid) / nt > idx) tid--;
+  while (tid + 1 < nt && (total * (tid + 1)) / nt <= idx) tid++;
+  const long long s0 = (total * tid) / nt, s1 = (total * (tid + 1)) / nt;
+  return (idx - s0) < ((s1 - s0) & ~7LL);
+}
+
+DPUF_DEV float swiglu_one(float g, float u, float dz, bool vec, const ExpfTable& et) {
+  float r;
+  if (vec) {
+    const float ng = max_ps(-40.0f, min_ps(__fsub_rn(0.0f, g), 40.0f));
+    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, exp_poly(ng)));
+    r = __fmul_rn(silu, u);
+    if (dz > 0.0f && !(fabsf(r) >= dz)) r = 0.0f;
+  } else {
+    const float silu = (g >= 40.0f) ? g : ((g <= -40.0f) ? 0.0f : __fdiv_rn(g, __fadd_rn(1.0f, glibc_expf(-g, et))));
+    r = __fmul_rn(silu, u);
+    if (dz > 0.0f && fabsf(r) < dz) r = 0.0f;
+  }
+  return r;
+}
+
+__global__ void swiglu_prep_kernel(const float* __restrict__ gate, const float* __restrict__ up, int M, int I,
+                                   float dz, int nt, const uint8_t* __restrict__ signs, Act out, ExpfTable et) {
+  cudaGridDependencySynchronize();
+  const int lane = threadIdx.x & 31;
+  const int chunk = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int m = blockIdx.y;
+  if (chunk * 64 >= I) return;
+  const int c0 = chunk * 64;
+  const long long total = (long long)M * I;
+  const bool slab = (M >= 2) && ((M + 5) / 6 >= nt);
+  const long long ia = (long long)m * I + c0 + lane, ib = ia + 32;
+  const float a = swiglu_one(gate[ia], up[ia], dz, swiglu_vector_elem(ia, total, nt, slab), et);
+  const float b = swiglu_one(gate[ib], up[ib], dz, swiglu_vector_elem(ib, total, nt, slab), et);
+  prep_chunk_warp(a, b, signs, c0, lane, out.q8 + (size_t)m * out.ld, out.xs + (size_t)m * (out.ld >> 5),
+                  out.xm + (size_t)m * (out.ld >> 5));
+}
+
+__global__ void zero_rows_kernel(float* __restrict__ out, int H, int r0) {
+  cudaGridDependencySynchronize();
+  const int m = blockIdx.y;
+  for (int i = r0 + blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) out[(size_t)m * H + i] = 0.0f;
+}
+
+}  // namespace
+
+cudaError_t configure_layer_kernels() {
+  return set_max_dyn_smem(norm_prep_kernel);
+}
+
+cudaError_t launch_norm_prep(const Launch& L, float* h, const float* res, const float* w, float eps, int M, int H,
+                             const PrepTarget* targets, int n_targets, float* norm_out) {
+  PrepTargets T = {};
+  T.n = n_targets;
+  for (int i = 0; i < n_targets && i < 3; i++) T.t[i] = targets[i];
+  const int threads = H >= 4096 ? 1024 : (H >= 1024 ? 512 : 256);
+  const size_t smem = (size_t)H * sizeof(float);
+  if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
+  return launch_k(L, norm_prep_kernel, dim3(M), dim3(threads), smem, h, res, w, eps, H, T, norm_out);
+}
+
+cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
+                           const float* q_norm, const float* k_norm, float eps, const float* cos_tab,
+                           const float* sin_tab, const int* pos0_dev, KvCache kv) {
+  const int wpb = 4;
+  const int heads = n_q + n_kv;
+  return launch_k(L, qk_post_kernel, dim3(M, (heads + wpb - 1) / wpb), dim3(wpb * 32), (size_t)wpb * hd * 4, q, k, v,
+                  n_q, n_kv, hd, q_norm, k_norm, eps, cos_tab, sin_tab, pos0_dev, kv);
+}
+
+cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* up, int M, int I, float deadzone,
+                               int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et) {
+  const int chunks = I / 64, wpb = 8;
+  return launch_k(L, swiglu_prep_kernel, dim3((chunks + wpb - 1) / wpb, M), dim3(wpb * 32), 0, gate, up, M, I,
+                  deadzone, nt_ref, signs, out, et);
+}
+
+cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0) {
+  if (r0 >= H) return cudaSuccess;
+  const int n = H - r0;
+  return launch_k(L, zero_rows_kernel, dim3((n + 255) / 256, M), dim3(256), 0, out, H, r0);
+}
+
+}  // namespace dpuf

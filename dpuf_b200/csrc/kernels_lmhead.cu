@@ -1,0 +1,121 @@
+// kernels_lmhead.cu - Zone-A early-exit test and masking, greedy argmax.
+//
+// Zone A (dpuf_engine.c:2091-2139): after the LM-head rows of tiles [0, Z) are computed,
+// the reference scans logits[0, min(16Z, V)) sequentially keeping the top two values with
+// strict '>' (a repeated maximum counts for the second place) and exits when
+// margin > 0 && b1 - b2 >= margin; on exit logits[16Z, V) = -1e9, otherwise the remaining
+// tiles are computed.  The sequential top-2 equals a tree merge of partial (b1, b2) pairs
+// (b1 = max, b2 = max(min(b1a, b1b), b2a, b2b)), which is what the kernel reduces.
+#include "kernels.cuh"
+
+namespace dpuf {
+
+namespace {
+
+template <typename K, typename... Args>
+cudaError_t launch_k(const Launch& L, K kernel, dim3 grid, dim3 block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = L.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+DPUF_DEV void top2_push(float v, float& b1, float& b2) {
+  if (v > b1) { b2 = b1; b1 = v; }
+  else if (v > b2) { b2 = v; }
+}
+DPUF_DEV void top2_merge(float& b1, float& b2, float o1, float o2) {
+  const float lo = fminf(b1, o1);
+  b1 = fmaxf(b1, o1);
+  b2 = fmaxf(fmaxf(b2, o2), lo);
+}
+
+__global__ void __launch_bounds__(1024) zone_test_kernel(const float* __restrict__ logits, int n, float margin,
+                                                         int* __restrict__ flag, float* __restrict__ b12) {
+  __shared__ float s1[32], s2[32];
+  cudaGridDependencySynchronize();
+  float b1 = -1e30f, b2 = -1e30f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) top2_push(logits[i], b1, b2);
+  for (int m = 16; m; m >>= 1) {
+    const float o1 = __shfl_xor_sync(kFull, b1, m), o2 = __shfl_xor_sync(kFull, b2, m);
+    top2_merge(b1, b2, o1, o2);
+  }
+  if ((threadIdx.x & 31) == 0) { s1[threadIdx.x >> 5] = b1; s2[threadIdx.x >> 5] = b2; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    b1 = threadIdx.x < nw ? s1[threadIdx.x] : -1e30f;
+    b2 = threadIdx.x < nw ? s2[threadIdx.x] : -1e30f;
+    for (int m = 16; m; m >>= 1) {
+      const float o1 = __shfl_xor_sync(kFull, b1, m), o2 = __shfl_xor_sync(kFull, b2, m);
+      top2_merge(b1, b2, o1, o2);
+    }
+    if (threadIdx.x == 0) {
+      *flag = (margin > 0.0f && __fsub_rn(b1, b2) >= margin) ? 1 : 0;
+      if (b12) { b12[0] = b1; b12[1] = b2; }
+    }
+  }
+}
+
+__global__ void zone_mask_kernel(float* __restrict__ logits, int from, int V, const int* __restrict__ flag) {
+  cudaGridDependencySynchronize();
+  if (!*flag) return;
+  for (int i = from + blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) logits[i] = -1e9f;
+}
+
+// First index of the maximum (strict '>' scan, dpuf-cli.c:1997-2005): ties keep the lower index.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int ld,
+                                                      int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  cudaGridDependencySynchronize();
+  const float* row = logits + (size_t)blockIdx.x * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = row[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+  for (int m = 16; m; m >>= 1) {
+    const float ov = __shfl_xor_sync(kFull, bv, m);
+    const int oi = __shfl_xor_sync(kFull, bi, m);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    bv = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+    for (int m = 16; m; m >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, bv, m);
+      const int oi = __shfl_xor_sync(kFull, bi, m);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = (bi == 0x7fffffff) ? 0 : bi;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_zone_test(const Launch& L, const float* logits, int n, float margin, int* flag, float* b12) {
+  return launch_k(L, zone_test_kernel, dim3(1), dim3(1024), 0, logits, n, margin, flag, b12);
+}
+
+cudaError_t launch_zone_mask(const Launch& L, float* logits, int from, int V, const int* flag) {
+  if (from >= V) return cudaSuccess;
+  return launch_k(L, zone_mask_kernel, dim3(min(148, (V - from + 255) / 256)), dim3(256), 0, logits, from, V, flag);
+}
+
+cudaError_t launch_argmax(const Launch& L, const float* logits, int M, int V, int ld, int32_t* out) {
+  return launch_k(L, argmax_kernel, dim3(M), dim3(1024), 0, logits, V, ld, out);
+}
+
+}  // namespace dpuf

@@ -1,0 +1,190 @@
+// ops_abi.cu - standalone mode-12 ops behind the reference's exported signatures
+// (dpuf_kernels.h:267-277; dpuf_avx2.c:2678-2783) and device-resident weight handles.
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+
+#include "dpuf_cuda.h"
+#include "dpuf_kernels.h"
+#include "engine_internal.h"
+#include "kernels.cuh"
+
+namespace dpuf {
+namespace {
+
+struct W12Handle {
+  int device = 0;
+  W12 w{};
+  unsigned char* mem = nullptr;
+  int8_t* q8 = nullptr;
+  float* xs = nullptr;
+  int32_t* xm = nullptr;
+};
+
+constexpr int kOpChunk = kMaxBatch;  // tokens per launch of the standalone matmul
+
+bool fail(const char* where, cudaError_t e) {
+  set_error(std::string(where) + ": " + cudaGetErrorString(e));
+  return false;
+}
+
+// Uploads tiles [0, n_tiles) of a mode-12 matrix; the span end comes from the last tile's row
+// count because the ABI does not pass tile_offsets[n_tiles].
+bool upload(W12Handle* h, int rows, int cols, int n_tiles, const uint8_t* base, const uint64_t* toff,
+            const uint8_t* signs) {
+  if (cols <= 0 || cols % 64 != 0 || n_tiles <= 0 || !base || !toff) {
+    set_error("bad mode-12 descriptor");
+    return false;
+  }
+  uint64_t lo = toff[0], hi = 0;
+  const int n_blk = cols / 32;
+  for (int t = 0; t < n_tiles; t++) {
+    const uint8_t* tp = base + toff[t];
+    const int n_r = tp[4] | (tp[5] << 8);
+    lo = std::min<uint64_t>(lo, toff[t]);
+    hi = std::max<uint64_t>(hi, toff[t] + 16 + (uint64_t)((n_r + 7) / 8) * n_blk * 144);
+  }
+  const size_t span = (size_t)(hi - lo);
+  const size_t off_toff = (span + 255) & ~(size_t)255;
+  const size_t off_sign = (off_toff + (size_t)n_tiles * 8 + 255) & ~(size_t)255;
+  const size_t total = off_sign + (size_t)cols / 8;
+  cudaError_t e;
+  if ((e = cudaGetDevice(&h->device)) != cudaSuccess) return fail("cudaGetDevice", e);
+  if ((e = configure_kernels()) != cudaSuccess) return fail("kernel attributes", e);
+  if ((e = cudaMalloc(&h->mem, total)) != cudaSuccess) return fail("cudaMalloc", e);
+  if ((e = cudaMemcpy(h->mem, base + lo, span, cudaMemcpyHostToDevice)) != cudaSuccess) return fail("upload", e);
+  std::string toffs((size_t)n_tiles * 8, '\0');
+  uint64_t* tp = (uint64_t*)&toffs[0];
+  for (int t = 0; t < n_tiles; t++) tp[t] = toff[t] - lo;
+  if ((e = cudaMemcpy(h->mem + off_toff, tp, (size_t)n_tiles * 8, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return fail("upload", e);
+  if (signs && (e = cudaMemcpy(h->mem + off_sign, signs, (size_t)cols / 8, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return fail("upload", e);
+  h->w = W12{h->mem, (const uint64_t*)(h->mem + off_toff), signs ? h->mem + off_sign : nullptr, rows, cols, n_tiles};
+  return true;
+}
+
+bool alloc_act(W12Handle* h) {
+  const size_t cols = h->w.cols;
+  cudaError_t e;
+  if ((e = cudaMalloc(&h->q8, kOpChunk * cols)) != cudaSuccess) return fail("cudaMalloc", e);
+  if ((e = cudaMalloc(&h->xs, kOpChunk * (cols / 32) * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+  if ((e = cudaMalloc(&h->xm, kOpChunk * (cols / 32) * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+  return true;
+}
+
+void free_handle(W12Handle* h) {
+  if (!h) return;
+  cudaFree(h->mem);
+  cudaFree(h->q8);
+  cudaFree(h->xs);
+  cudaFree(h->xm);
+  delete h;
+}
+
+// y = W x for M tokens, device pointers, in chunks of kOpChunk tokens.
+int32_t matmul_dev(W12Handle* h, int M, const float* x, float* y, cudaStream_t s) {
+  const Launch L{s, false};
+  const Act a{h->q8, h->xs, h->xm, h->w.cols};
+  for (int m0 = 0; m0 < M; m0 += kOpChunk) {
+    const int mc = std::min(kOpChunk, M - m0);
+    cudaError_t e = launch_prep(L, x + (size_t)m0 * h->w.cols, h->w.cols, mc, h->w.cols, h->w.signs, a);
+    if (e != cudaSuccess) return fail("prep", e), -4;
+    LinJobs J = {};
+    J.n = 1;
+    J.j[0] = {h->w, a, y + (size_t)m0 * h->w.rows, h->w.rows, 0, h->w.n_tiles};
+    J.tile_prefix[1] = h->w.n_tiles;
+    e = mc == 1 ? launch_gemv(L, J, nullptr) : launch_gemm_exact(L, J, mc);
+    if (e != cudaSuccess) return fail("matmul", e), -4;
+  }
+  return 0;
+}
+
+}  // namespace
+}  // namespace dpuf
+
+using dpuf::W12Handle;
+
+extern "C" {
+
+DPUF_EXPORT void* dpuf_cuda_w12_upload(const DpufWeightDesc* w) {
+  if (!w || w->mode != DPUF_MODE_QR_HAD4_PACKED) {
+    dpuf::set_error("dpuf_cuda_w12_upload: mode-12 descriptor required");
+    return nullptr;
+  }
+  W12Handle* h = new W12Handle();
+  if (!dpuf::upload(h, w->rows, w->cols, w->n_tiles, w->tensor_base, w->tile_offsets, w->sign_bits) ||
+      !dpuf::alloc_act(h)) {
+    dpuf::free_handle(h);
+    return nullptr;
+  }
+  return h;
+}
+
+DPUF_EXPORT void dpuf_cuda_w12_free(void* wh) { dpuf::free_handle((W12Handle*)wh); }
+
+DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev, float* y_dev, void* stream) {
+  W12Handle* h = (W12Handle*)wh;
+  if (!h || M <= 0 || !x_dev || !y_dev) return -1;
+  return dpuf::matmul_dev(h, M, x_dev, y_dev, (cudaStream_t)stream);
+}
+
+// Reference signature (dpuf_avx2.c:2678): host in, host out, synchronous.
+DPUF_EXPORT void dpuf_matmul_qr_hadamard4_packed_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                                     const float* x_in, const uint8_t* tensor_base,
+                                                     const uint64_t* tile_offsets, const uint8_t* sign_bits,
+                                                     float* out) {
+  dpuf::set_error("");
+  if (M <= 0 || !x_in || !out) return;
+  W12Handle* h = new W12Handle();
+  float *dx = nullptr, *dy = nullptr;
+  if (dpuf::upload(h, rows, cols, n_tiles, tensor_base, tile_offsets, sign_bits) && dpuf::alloc_act(h) &&
+      cudaMalloc(&dx, (size_t)M * cols * 4) == cudaSuccess && cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
+      cudaMemcpy(dx, x_in, (size_t)M * cols * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+      dpuf::matmul_dev(h, M, dx, dy, nullptr) == 0) {
+    cudaError_t e = cudaMemcpy(out, dy, (size_t)M * rows * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) dpuf::set_error(cudaGetErrorString(e));
+  }
+  cudaFree(dx);
+  cudaFree(dy);
+  dpuf::free_handle(h);
+}
+
+// Reference signature (dpuf_avx2.c:2738): rows are looked up by id; only the tiles up to the
+// largest id are uploaded.
+DPUF_EXPORT void dpuf_embed_qr_hadamard4_packed_f32(int32_t n_tokens, int32_t cols, const int32_t* token_ids,
+                                                    const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                                                    const uint8_t* sign_bits, float* out) {
+  dpuf::set_error("");
+  if (n_tokens <= 0 || !token_ids || !out) return;
+  int32_t max_id = 0;
+  for (int i = 0; i < n_tokens; i++) {
+    if (token_ids[i] < 0) {
+      dpuf::set_error("negative token id");
+      return;
+    }
+    max_id = std::max(max_id, token_ids[i]);
+  }
+  const int n_tiles = max_id / dpuf::kTileRows + 1;
+  W12Handle* h = new W12Handle();
+  int32_t* dids = nullptr;
+  float* dy = nullptr;
+  if (dpuf::upload(h, n_tiles * dpuf::kTileRows, cols, n_tiles, tensor_base, tile_offsets, sign_bits) &&
+      cudaMalloc(&dids, (size_t)n_tokens * 4) == cudaSuccess &&
+      cudaMalloc(&dy, (size_t)n_tokens * cols * 4) == cudaSuccess &&
+      cudaMemcpy(dids, token_ids, (size_t)n_tokens * 4, cudaMemcpyHostToDevice) == cudaSuccess) {
+    const dpuf::Launch L{nullptr, false};
+    for (int m0 = 0; m0 < n_tokens; m0 += 65535) {
+      const int mc = std::min(65535, n_tokens - m0);
+      if (dpuf::launch_embed(L, h->w, dids + m0, mc, dy + (size_t)m0 * cols) != cudaSuccess) break;
+    }
+    cudaError_t e = cudaMemcpy(out, dy, (size_t)n_tokens * cols * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) dpuf::set_error(cudaGetErrorString(e));
+  }
+  cudaFree(dids);
+  cudaFree(dy);
+  dpuf::free_handle(h);
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+/*
+ * dpuf_cuda.h - entry points of libdpuf_cuda.so beyond the reference's C ABI.
+ *
+ * These have no counterpart in the reference (which is CPU-only); they expose what a GPU
+ * host needs on top of dpuf_kernels.h: greedy decoding without shipping logits to the host,
+ * device-resident weights for the standalone op, per-engine options and error text.
+ */
+#ifndef DPUF_CUDA_H
+#define DPUF_CUDA_H
+
+#include "dpuf_kernels.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Text of the last error seen by this thread's most recent failing call ("" if none). */
+DPUF_EXPORT const char* dpuf_cuda_last_error(void);
+
+/* Same step as dpuf_engine_forward_batch(..., only_last_logits = 1, ...) but the logits stay
+ * on the device; *next_id receives the greedy token (first index of the maximum, as the
+ * reference CLI's sample_token at temperature 0, dpuf-cli.c:1997-2005).  Returns the
+ * forward_batch codes. */
+DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, const int32_t* token_ids,
+                                             int32_t pos0, int32_t* next_id);
+
+/* Copies the last forward's logits row `row` (0-based among the rows produced) to host. */
+DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out);
+
+/* Engine options (call before the first forward):
+ *   "pdl" (0/1)    programmatic dependent launch between kernels (default 1)
+ *   "graphs" (0/1) capture each step shape in a CUDA graph (default 1) */
+DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t value);
+
+/* Zone-A decision of the last forward: {used, exited} and the top-2 values. */
+DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2);
+
+/* ---- device-resident standalone op (for measuring the kernel with weights in HBM) ---- */
+/* Uploads one mode-12 matrix; returns an opaque handle or NULL. */
+DPUF_EXPORT void* dpuf_cuda_w12_upload(const DpufWeightDesc* w);
+DPUF_EXPORT void dpuf_cuda_w12_free(void* wh);
+/* y[M][rows] = W x[M][cols]; x and y are DEVICE pointers; runs on `stream` (cudaStream_t,
+ * NULL = default stream) without synchronising.  Scratch for the quantised activation is
+ * owned by the weight handle.  Returns 0 or a negative error. */
+DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev, float* y_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DPUF_CUDA_H */

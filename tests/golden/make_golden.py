@@ -1,0 +1,111 @@
+"""Generates the golden fixtures in this directory from the REFERENCE itself.
+
+Run in a container that has the reference sources (default /root/reference):
+    python tests/golden/make_golden.py [REF_DIR]
+It builds oracle/_ref/libdpuf_avx2.so from the unmodified reference sources
+(oracle/build_ref.sh), imports the reference packer module, and records:
+  * pack.json     sha256 of the reference packer's blob for each PACK_CASES input;
+  * matmul.npz    outputs of the reference's exported dpuf_matmul_qr_hadamard4_packed_f32 and
+                  dpuf_embed_qr_hadamard4_packed_f32;
+  * engine.json / engine_logits.npz
+                  greedy ids and logit digests (full logits for small vocabularies) of the
+                  reference engine (8 threads) for every ENGINE_SCENARIOS entry.
+The engine models are packed with this repository's packer, whose bytes are checked against
+the reference packer by pack.json.
+"""
+from __future__ import annotations
+
+import json
+import os
+import pathlib
+import sys
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(HERE))
+
+from dpuf_b200 import _native, model as mdl, packer  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+import scenarios as sc  # noqa: E402
+
+
+def main() -> None:
+    ref_dir = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    _native.build_pack()
+    orc.build_ref(ref_dir)
+    sys.path.insert(0, str(ref_dir))
+    import dpuf_format as ref_format  # the reference packer module
+
+    # ---- packer
+    pack = {}
+    blobs = []
+    for i, (rows, cols, name, seed) in enumerate(sc.PACK_CASES):
+        w = packer.gen_normal_bf16(seed, i, (rows, cols), 0.02)
+        w[0, :32] = 0
+        w[min(1, rows - 1), 5] = packer.fp32_to_bf16(np.array([3.0], np.float32))[0]
+        ref_blob = ref_format.encode_tensor_qr_hadamard4_packed(w, tensor_name=name)
+        pack[f"case{i}"] = {"rows": rows, "cols": cols, "name": name, "seed": seed, "sha256": sc.blob_digest(ref_blob)}
+        blobs.append(packer.BlobView(np.frombuffer(ref_blob, dtype=np.uint8).copy()))
+    (HERE / "pack.json").write_text(json.dumps(pack, indent=1))
+
+    # ---- standalone ops
+    arrays = {}
+    for ci, M, kind in sc.MATMUL_CASES:
+        bv = blobs[ci]
+        x = sc.matmul_input(ci, M, kind, bv.cols)
+        arrays[f"matmul_{ci}_{M}_{kind}"] = orc.ref_matmul(M, bv, x)
+    lib = orc.RefEngine.lib_()
+    for ci in (3, 4):
+        bv = blobs[ci]
+        ids = np.random.default_rng(ci).integers(0, bv.rows, size=9).astype(np.int32)
+        out = np.empty((len(ids), bv.cols), np.float32)
+        lib.dpuf_embed_qr_hadamard4_packed_f32(len(ids), bv.cols, ids.ctypes.data, bv.tiles.ctypes.data,
+                                               bv.tile_offsets.ctypes.data, bv.sign_bits.ctypes.data, out.ctypes.data)
+        arrays[f"embed_{ci}_ids"] = ids
+        arrays[f"embed_{ci}"] = out
+    np.savez_compressed(HERE / "matmul.npz", **arrays)
+
+    # ---- engine scenarios
+    eng_out = {}
+    eng_logits = {}
+    for s in sc.ENGINE_SCENARIOS:
+        saved = {k: os.environ.get(k) for k, _ in s.env}
+        os.environ.update(dict(s.env))
+        try:
+            m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter)
+            ref = orc.RefEngine(m, n_threads=8)
+            prompt = mdl.prompt_ids(s.prompt_len, m.shape.vocab, s.seed)
+            rec = {"prompt": prompt.tolist()}
+            if s.all_logits:
+                ref.reset()
+                allp = ref.forward(prompt, 0, 0)
+                rec["prefill_all_digest"] = sc.logits_digest(allp)
+            ids, logits = orc.greedy_run(ref, prompt, s.n_decode)
+            rec["ids"] = ids
+            rec["digests"] = [sc.logits_digest(l) for l in logits]
+            rec["head"] = [l[:4].tolist() for l in logits]
+            rms = float(np.sqrt(np.mean(np.stack(logits) ** 2)))
+            rec["logit_rms"] = rms
+            if dict(s.env).get("DPUF_EARLY_TILES"):
+                za = max(256, int(dict(s.env)["DPUF_EARLY_TILES"]))
+                rec["zone_exit"] = [bool(np.all(l[16 * za:] == np.float32(-1e9))) for l in logits]
+            if s.full_logits:
+                eng_logits[s.name] = np.stack(logits)
+            eng_out[s.name] = rec
+            ref.close()
+            print(s.name, "ids", ids[:8], "rms", rms, flush=True)
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+    (HERE / "engine.json").write_text(json.dumps(eng_out, indent=1))
+    np.savez_compressed(HERE / "engine_logits.npz", **eng_logits)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,74 @@
+"""Parity scenarios shared by the golden-fixture generator and the tests.
+
+Each engine scenario is: a synthetic model shape and seed, environment knobs, a prompt and a
+number of greedy decode steps (the reference CLI's run_turn_ex, dpuf-cli.c:2344-2420).
+Golden outputs were produced by the reference engine built from its own sources
+(oracle/build_ref.sh) and the reference packer; see make_golden.py.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+
+import numpy as np
+
+
+@dataclasses.dataclass(frozen=True)
+class EngineScenario:
+    name: str
+    shape: str
+    prompt_len: int
+    n_decode: int
+    env: tuple = ()
+    norm_jitter: float = 0.0
+    seed: int = 0
+    all_logits: bool = False  # also record the prefill with only_last_logits = 0
+    full_logits: bool = False  # store the full logit vectors (small vocab only)
+
+
+ENGINE_SCENARIOS = [
+    EngineScenario("tiny_gqa", "tiny", 20, 12, norm_jitter=0.1, all_logits=True, full_logits=True),
+    EngineScenario("tiny_mha_slab", "tiny-mha", 50, 8, env=(("DPUF_SWIGLU_DEADZONE", "0.02"),), norm_jitter=0.1),
+    EngineScenario("tiny_keep_tiles", "tiny", 61, 9,
+                   env=(("DPUF_PREFILL_KEEP_TILES", "12"), ("DPUF_GEN_KEEP_TILES", "14")), norm_jitter=0.1),
+    EngineScenario("tiny_zone_a", "tiny-zone", 20, 16,
+                   env=(("DPUF_EARLY_TILES", "300"), ("DPUF_EARLY_MARGIN", "0.05")), norm_jitter=0.1),
+    EngineScenario("tiny_long", "tiny", 200, 60, seed=3),
+    EngineScenario("qwen3_0_6b_pp32_tg32", "qwen3-0.6b", 32, 32),
+]
+
+# Packer cases: (rows, cols, tensor name used for the column signs, generator seed).
+PACK_CASES = [
+    (64, 64, "t0", 1),
+    (72, 128, "blk.0.qkv_in", 2),
+    (100, 256, "x", 3),
+    (256, 1024, "blk.3.ffn_down.weight", 4),
+    (1000, 512, "output.weight", 5),
+    (4104, 192, "odd", 6),
+]
+
+# Standalone matmul cases: (pack case index, M, input kind).
+MATMUL_CASES = [
+    (3, 1, "normal"),
+    (3, 7, "normal"),
+    (4, 1, "sparse"),   # zero blocks exercise the xs == 0 skip
+    (4, 50, "normal"),  # M >= 24: the reference's multi-slab path
+    (5, 3, "normal"),   # ragged last tile (4104 rows)
+]
+
+
+def matmul_input(case_idx: int, M: int, kind: str, cols: int) -> np.ndarray:
+    rng = np.random.default_rng(1000 + 17 * case_idx + M)
+    x = rng.standard_normal((M, cols)).astype(np.float32)
+    if kind == "sparse":
+        x[:, : cols // 2] = 0.0
+        x[:, cols // 2: cols // 2 + 32] *= np.float32(1e-6)
+    return x
+
+
+def logits_digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a, dtype=np.float32).tobytes()).hexdigest()[:32]
+
+
+def blob_digest(b) -> str:
+    return hashlib.sha256(bytes(b)).hexdigest()

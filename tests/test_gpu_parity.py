@@ -1,0 +1,135 @@
+"""GPU parity: the CUDA engine and ops, called through the C ABI, against the reference's
+golden outputs and the CPU oracle.  Integer/byte work and every fp32 result are compared bit
+for bit (the reference's operation order is reproduced), so the tolerance is zero."""
+import numpy as np
+import pytest
+
+import scenarios as sc
+from _util import EnvScope, bitexact, golden_arrays, golden_engine, pack_case_blob, run_scenario
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def eng_mod():
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from dpuf_b200 import _native, engine
+
+    _native.build_cuda()
+    engine.cuda_lib()
+    return engine
+
+
+@pytest.mark.parametrize("ci,M,kind", sc.MATMUL_CASES)
+def test_matmul_matches_reference(eng_mod, ci, M, kind):
+    bv = pack_case_blob(ci)
+    x = sc.matmul_input(ci, M, kind, bv.cols)
+    got = eng_mod.matmul(M, bv, x)
+    assert bitexact(got, golden_arrays("matmul.npz")[f"matmul_{ci}_{M}_{kind}"])
+
+
+@pytest.mark.parametrize("ci", [3, 4])
+def test_embed_matches_reference(eng_mod, ci):
+    g = golden_arrays("matmul.npz")
+    bv = pack_case_blob(ci)
+    assert bitexact(eng_mod.embed(bv, g[f"embed_{ci}_ids"]), g[f"embed_{ci}"])
+
+
+@pytest.mark.parametrize("M", [1, 2, 5, 16, 17, 33, 256])
+def test_matmul_token_counts_match_oracle(eng_mod, M):
+    from oracle import oracle as orc
+
+    bv = pack_case_blob(3)
+    x = np.random.default_rng(M).standard_normal((M, bv.cols)).astype(np.float32)
+    x[:, 64:96] = 0.0
+    assert bitexact(eng_mod.matmul(M, bv, x), orc.oracle_matmul(M, bv, x))
+
+
+@pytest.mark.parametrize("scn", sc.ENGINE_SCENARIOS, ids=lambda s: s.name)
+def test_engine_matches_reference(eng_mod, scn):
+    g = golden_engine()[scn.name]
+    rec, logits, _ = run_scenario(eng_mod.CudaTransformerEngine, scn)
+    assert rec["ids"] == g["ids"]
+    assert rec["digests"] == g["digests"]
+    if scn.all_logits:
+        assert rec["prefill_all_digest"] == g["prefill_all_digest"]
+    if scn.full_logits:
+        assert bitexact(np.stack(logits), golden_arrays("engine_logits.npz")[scn.name])
+    if "zone_exit" in g:
+        za = max(256, int(dict(scn.env)["DPUF_EARLY_TILES"]))
+        assert [bool(np.all(l[16 * za:] == np.float32(-1e9))) for l in logits] == g["zone_exit"]
+
+
+def test_engine_without_graphs_or_pdl_matches(eng_mod):
+    scn = sc.ENGINE_SCENARIOS[0]
+    g = golden_engine()[scn.name]
+    for opts in ({"graphs": 0}, {"pdl": 0}):
+        rec, _, _ = run_scenario(lambda m: eng_mod.CudaTransformerEngine(m, opts), scn)
+        assert rec["digests"] == g["digests"], opts
+
+
+def test_greedy_api_matches_logits(eng_mod):
+    from dpuf_b200 import model as mdl
+
+    m = mdl.SyntheticModel(mdl.TINY, seed=5, norm_jitter=0.1)
+    e = eng_mod.CudaTransformerEngine(m)
+    prompt = mdl.prompt_ids(9, m.shape.vocab, 5)
+    e.reset_cache()
+    lg = e.forward_batch(prompt, 0)[0]
+    e.reset_cache()
+    assert e.forward_greedy(prompt, 0) == int(np.argmax(lg))
+    e.close()
+
+
+def test_slots_and_prefixes_match_oracle(eng_mod):
+    """Prefix freeze/apply and slot switching (dpuf_engine.c:1404-1600) give the same logits as
+    recomputing the prefix."""
+    from dpuf_b200 import model as mdl
+    from oracle import oracle as orc
+
+    m = mdl.SyntheticModel(mdl.TINY, seed=2, norm_jitter=0.1)
+    e = eng_mod.CudaTransformerEngine(m)
+    o = orc.OracleEngine(m)
+    prefix = mdl.prompt_ids(12, m.shape.vocab, 2)
+    tail = mdl.prompt_ids(5, m.shape.vocab, 9)
+    e.reset_cache()
+    e.forward_batch(prefix, 0)
+    assert e.freeze_prefix(1, len(prefix)) == 1
+    assert e.get_prefix_len(1) == len(prefix)
+    assert e.set_slot(3) == 0 and e.get_slot() == 3
+    assert e.apply_prefix(3, 1) == len(prefix)
+    got = e.forward_batch(tail, len(prefix))[0]
+    o.reset()
+    o.forward(prefix, 0)
+    want = o.forward(tail, len(prefix))[0]
+    assert bitexact(got, want)
+    # slot 0 still holds the prefix only; a fresh slot 5 starts empty
+    assert e.set_slot(5) == 0
+    e.reset_cache()
+    got5 = e.forward_batch(tail, 0)[0]
+    o.reset()
+    assert bitexact(got5, o.forward(tail, 0)[0])
+    assert e.num_slots() == 8 and e.slot_memory() > 0
+    assert e.set_slot(8) == -1
+    e.close()
+    o.close()
+
+
+def test_forward_error_codes(eng_mod):
+    from dpuf_b200 import model as mdl
+
+    m = mdl.SyntheticModel(mdl.TINY, seed=0)
+    e = eng_mod.CudaTransformerEngine(m)
+    lib = e.lib
+    ids = np.zeros(300, np.int32)
+    out = np.zeros(m.shape.vocab, np.float32)
+    assert lib.dpuf_engine_forward_batch(e._handle, 0, ids.ctypes.data, 0, 1, out.ctypes.data) == -2
+    assert lib.dpuf_engine_forward_batch(e._handle, 257, ids.ctypes.data, 0, 1, out.ctypes.data) == -2
+    assert lib.dpuf_engine_forward_batch(e._handle, 4, ids.ctypes.data, m.shape.max_seq - 3, 1,
+                                         out.ctypes.data) == -3
+    assert lib.dpuf_engine_forward_batch(e._handle, 4, None, 0, 1, out.ctypes.data) == -1
+    assert lib.dpuf_engine_forward_batch(e._handle, 4, ids.ctypes.data, 0, 1, None) == -1
+    assert lib.dpuf_engine_forward_batch(e._handle, 4, ids.ctypes.data, 0, 2, None) == 0
+    e.close()
