@@ -1,0 +1,397 @@
+"""Benchmark of DPUF's per-token LM loop on B200: Qwen3-8B-shaped random-init mode-12 model,
+prompt of 32 ids (pp32) then batch-1 greedy decode (tg).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dpuf|reference]
+
+A step is one greedy decode token at batch 1 (the reference CLI's decode loop, dpuf-cli.c:2398-2420).
+  value   decode tok/s, device time (CUDA events on the engine stream) of K back-to-back steps
+          with the token fed back on the device; weights (4.26 GB) exceed L2, so every step
+          streams them from HBM
+  e2e     the same steps through the reference's C ABI (dpuf_engine_forward_token): token id
+          host->device, logits[vocab] device->host, greedy argmax on the host
+  roofline  the dominant kernel (the mode-12 decode GEMV, gate/up shape 2x12288x4096) timed alone
+          with CUDA events over 8 weight copies (> L2), bytes = tile bytes per launch
+  cpu_baseline  the reference's own AVX2/OpenMP engine (built from its sources) on this host's
+          cores, same model and prompt, a bounded number of decode steps
+Multi-GPU (torchrun, --gpus N): data parallel, one independent sequence per GPU (weak scaling);
+the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def gemv_roofline(hbm_peak: float, peak_kind: str):
+    """Kernel-only timing of the mode-12 decode GEMV on the gate/up shape."""
+    import torch
+
+    from dpuf_b200 import engine, model as mdl, packer
+
+    lib = engine.cuda_lib()
+    w = packer.gen_normal_bf16(11, 22, (24576, 4096), 0.02)
+    bv = packer.BlobView(packer.encode_mode12(w, "blk.0.mlp_in"))
+    d = mdl.DpufWeightDesc(12, bv.rows, bv.cols, bv.n_tiles, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data, None,
+                           bv.sign_bits.ctypes.data)
+    n_copies = 6  # 6 x 56.7 MB > 126 MB L2
+    hs = [lib.dpuf_cuda_w12_upload(ctypes.byref(d)) for _ in range(n_copies)]
+    if not all(hs):
+        raise RuntimeError(engine.last_error())
+    x = torch.randn(1, 4096, device="cuda")
+    y = torch.empty(1, 24576, device="cuda")
+    arr = (ctypes.c_void_p * n_copies)(*hs)
+    ms = ctypes.c_float()
+    st = torch.cuda.current_stream().cuda_stream
+    rc = lib.dpuf_cuda_matmul_dev_timed(arr, n_copies, 1, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                                        60, ctypes.c_void_p(st), ctypes.byref(ms))
+    for h in hs:
+        lib.dpuf_cuda_w12_free(h)
+    if rc != 0:
+        raise RuntimeError(engine.last_error())
+    bytes_per_launch = int(bv.tiles.nbytes)
+    achieved = bytes_per_launch / (ms.value * 1e-3) / 1e9
+    traffic = None
+    prof = REPO / "profiles" / "gemv_m1_gate_up_24576x4096.md"
+    if prof.exists():
+        for line in prof.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    traffic = int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    pass
+    return {"kernel": "gemv_kernel (mode-12 M=1, 24576x4096)", "bound": "hbm", "achieved": round(achieved, 1),
+            "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "traffic": traffic, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms.value * 1e3, 2)}
+
+
+def cpu_baseline(m, prompt, n_steps: int, threads: int):
+    from oracle import oracle as orc
+
+    if not orc.RefEngine.available():
+        return None
+    ref = orc.RefEngine(m, n_threads=threads)
+    ref.reset()
+    lg = ref.forward(prompt, 0, 1)[0]
+    nxt = int(np.argmax(lg))
+    pos = len(prompt)
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        lg = ref.forward(np.array([nxt], np.int32), pos, 1)[0]
+        nxt = int(np.argmax(lg))
+        pos += 1
+    dt = time.perf_counter() - t0
+    ref.close()
+    return {"value": round(n_steps / dt, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{n_steps} greedy decode steps after pp32 on the same 8B-shaped model, "
+                      f"reference AVX2/OpenMP engine, {orc.cpu_model_string()}"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU engine on this host, same workload and metric."""
+    from dpuf_b200 import model as mdl
+    from oracle import oracle as orc
+
+    if rank != 0:
+        return
+    cfg = {"workload": "qwen3-8b-shape random-init mode-12, pp32 then batch-1 greedy decode", "prompt": 32,
+           "batch": 1, "kv": "fp32"}
+    if not orc.RefEngine.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdpuf_avx2.so not built "
+                                                              "(needs the reference sources at build time)"}))
+        return
+    threads = min(32, orc.host_threads())
+    m = mdl.SyntheticModel(mdl.QWEN3_8B, seed=0)
+    prompt = mdl.prompt_ids(32, m.shape.vocab, 0)
+    ref = orc.RefEngine(m, n_threads=threads)
+    ref.reset()
+    t0 = time.perf_counter()
+    lg = ref.forward(prompt, 0, 1)[0]
+    pp_s = time.perf_counter() - t0
+    nxt = int(np.argmax(lg))
+    pos = 32
+    for _ in range(args.warmup):
+        nxt = int(np.argmax(ref.forward(np.array([nxt], np.int32), pos, 1)[0]))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        nxt = int(np.argmax(ref.forward(np.array([nxt], np.int32), pos, 1)[0]))
+        pos += 1
+    dt = time.perf_counter() - t0
+    ref.close()
+    v = args.steps / dt
+    print(json.dumps({
+        "impl": "reference", "metric": "decode_tok_per_s", "value": round(v, 3), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->f32",
+        "data": "synthetic random-init weights ~N(0,0.02), seed-0 prompt", "config": cfg,
+        "prefill": {"tok_per_s": round(32 / pp_s, 3)},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} decode steps after pp32, {orc.cpu_model_string()}"},
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_dpuf(args, world, rank, local):
+    import torch
+
+    from dpuf_b200 import engine, model as mdl
+
+    torch.cuda.set_device(local)
+    hbm_peak, peak_kind = peaks()
+    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    t_build = time.perf_counter()
+    m = mdl.SyntheticModel(shape, seed=0)
+    t_build = time.perf_counter() - t_build
+    eng = engine.CudaTransformerEngine(m)
+    lib = eng.lib
+    # each rank decodes its own sequence (data parallel); rank 0 uses the seed-0 prompt
+    prompt = mdl.prompt_ids(32, shape.vocab, rank)
+    n_total = args.warmup + args.steps
+    if 32 + 2 * n_total + 8 > shape.max_seq:
+        raise SystemExit("steps + warmup exceed the 2304-position context")
+
+    # ---- pp32 (prefill) through the C ABI
+    eng.reset_cache()
+    eng.forward_batch(prompt, 0)
+    eng.reset_cache()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    lg = eng.forward_batch(prompt, 0)[0]
+    pp_s = time.perf_counter() - t0
+    first = int(np.argmax(lg))
+
+    # ---- device-timed decode (value)
+    ids = np.zeros(n_total, np.int32)
+    ms = ctypes.c_float()
+    rc = lib.dpuf_cuda_decode_greedy(eng._handle, first, 32, args.warmup, ids.ctypes.data, ctypes.byref(ms))
+    if rc != 0:
+        raise RuntimeError(engine.last_error())
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("decode")
+        rc = lib.dpuf_cuda_decode_greedy(eng._handle, int(ids[args.warmup - 1]) if args.warmup else first,
+                                         32 + args.warmup, args.steps, ids[args.warmup:].ctypes.data,
+                                         ctypes.byref(ms))
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    if rc != 0:
+        raise RuntimeError(engine.last_error())
+    barrier(world)
+    dev_ms = allreduce_max(float(ms.value), world)
+    value = world * args.steps / (dev_ms * 1e-3)
+
+    if args.no_extras:
+        eng.close()
+        if rank == 0:
+            print(json.dumps({"metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s",
+                              "model": shape.name, "ms_per_step": round(dev_ms / args.steps, 4)}), flush=True)
+        return
+    # ---- e2e through the drop-in C ABI with host buffers
+    eng.reset_cache()
+    lg = eng.forward_batch(prompt, 0)[0]
+    nxt = int(np.argmax(lg))
+    pos = 32
+    for _ in range(args.warmup):
+        lg = eng.forward_token(nxt, pos)
+        nxt = int(np.argmax(lg))
+        pos += 1
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lg = eng.forward_token(nxt, pos)
+        nxt = int(np.argmax(lg))
+        pos += 1
+    e2e_s = allreduce_max(time.perf_counter() - t0, world)
+    e2e = world * args.steps / e2e_s
+
+    roof = None
+    cpu = None
+    if rank == 0:
+        roof = gemv_roofline(hbm_peak, peak_kind)
+        from oracle import oracle as orc
+
+        cpu = cpu_baseline(m, prompt, n_steps=24, threads=min(32, orc.host_threads()))
+    eng.close()
+    if rank != 0:
+        return
+    wbytes = shape.weight_bytes_per_token()
+    step_s = dev_ms * 1e-3 / args.steps
+    clocks = clk.summary()
+    line = {
+        "metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->f32",
+        "data": "synthetic random-init weights ~N(0,0.02) (bf16-rounded, mode-12 packed), seed-0 prompt",
+        "config": {"workload": f"{shape.name}-shape random-init mode-12, pp32 then batch-1 greedy decode",
+                   "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab, "prompt": 32,
+                   "batch_per_gpu": 1,
+                   "kv": "fp32", "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "weights 4.26 GB > 126 MB L2: every step streams them from HBM"},
+        "step_roofline": {"bytes_per_step": wbytes, "achieved_gbs": round(wbytes / step_s / 1e9, 1),
+                          "frac": round(wbytes / step_s / 1e9 / hbm_peak, 4), "peak": hbm_peak,
+                          "peak_kind": peak_kind},
+        "roofline": roof,
+        "prefill": {"tok_per_s": round(32 / pp_s, 1), "what": "pp32 through dpuf_engine_forward_batch"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 1040,
+                "d2h_bytes_per_step": shape.vocab * 4,
+                "what": "dpuf_engine_forward_token per step: staging H2D, logits D2H, host argmax"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": None,
+        "model_build_s": round(t_build, 1),
+    }
+    launches = os.environ.get("DPUF_BENCH_LAUNCHES_PER_STEP")
+    line["gpu_launches"] = int(launches) * args.steps if launches else steps_launch_count(shape) * args.steps
+    print(json.dumps(line), flush=True)
+
+
+def steps_launch_count(shape) -> int:
+    """Kernels of one decode step: embed; per layer norm, qkv gemv, qk_post, attention, prep,
+    o gemv, norm, gate/up gemv, swiglu_prep, down gemv; final norm, lm gemv, greedy advance."""
+    return 1 + 10 * shape.layers + 3
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="dpuf", choices=["dpuf", "reference"])
+    ap.add_argument("--model", default="8b", choices=["8b", "0.6b"],
+                    help="8b = the benchmark workload; 0.6b = a small case for profiling")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_dpuf(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

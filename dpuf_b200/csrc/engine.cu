@@ -78,10 +78,10 @@ struct Prefix {
 struct StepKey {
   int M, only_last, keep, za;
   uint32_t margin_bits;
-  int slot;
+  int slot, greedy_loop;
   bool operator<(const StepKey& o) const {
-    return std::tie(M, only_last, keep, za, margin_bits, slot) <
-           std::tie(o.M, o.only_last, o.keep, o.za, o.margin_bits, o.slot);
+    return std::tie(M, only_last, keep, za, margin_bits, slot, greedy_loop) <
+           std::tie(o.M, o.only_last, o.keep, o.za, o.margin_bits, o.slot, o.greedy_loop);
   }
 };
 
@@ -122,6 +122,8 @@ struct Engine {
   int* d_flag = nullptr;
   float* d_b12 = nullptr;
   int32_t* d_argmax = nullptr;
+  int32_t* d_hist = nullptr;   // greedy-loop token history [max_seq] and step counter
+  int32_t* d_hist_step = nullptr;
   Staging* stage = nullptr;  // pinned
   float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
   uint32_t* d_exp_keys = nullptr;
@@ -272,7 +274,7 @@ void destroy_engine(Engine* e) {
   cudaFree(e->h); cudaFree(e->hn); cudaFree(e->q); cudaFree(e->k); cudaFree(e->v); cudaFree(e->att);
   cudaFree(e->gate); cudaFree(e->up); cudaFree(e->logits);
   cudaFree(e->prep_q8); cudaFree(e->prep_xs); cudaFree(e->prep_xm);
-  cudaFree(e->d_ids); cudaFree(e->d_pos0); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
+  cudaFree(e->d_ids); cudaFree(e->d_hist); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
   cudaFree(e->d_exp_keys); cudaFree(e->d_exp_vals);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -283,6 +285,7 @@ void destroy_engine(Engine* e) {
 struct StepParams {
   int M, only_last, keep, za;
   float margin;
+  bool greedy_loop;  // ids/pos live on the device and advance by greedy feedback
 };
 
 LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
@@ -320,7 +323,8 @@ int prep_targets(Engine* e, const W12* const* ws, int n, PrepTarget* t, int* slo
 cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   const Launch Lc{e->stream, e->use_pdl};
   const int M = P.M, H = e->H;
-  CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
+  if (!P.greedy_loop)
+    CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
   CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
   const Slot& sl = e->slots[e->active];
   for (int l = 0; l < e->L; l++) {
@@ -393,6 +397,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   } else {
     CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, e->lm.n_tiles), lm_M, nullptr));
   }
+  if (P.greedy_loop) CK(launch_greedy_advance(Lc, e->logits, e->V, e->d_ids, e->d_pos0, e->d_hist, e->d_hist_step));
   return cudaSuccess;
 }
 
@@ -400,7 +405,7 @@ cudaError_t run_step(Engine* e, const StepParams& P) {
   if (!e->use_graphs) return enqueue_step(e, P);
   uint32_t mb;
   memcpy(&mb, &P.margin, 4);
-  const StepKey key{P.M, P.only_last, P.keep, P.za, mb, e->active};
+  const StepKey key{P.M, P.only_last, P.keep, P.za, mb, e->active, P.greedy_loop ? 1 : 0};
   auto it = e->graphs.find(key);
   if (it == e->graphs.end()) {
     cudaGraph_t g;
@@ -422,6 +427,32 @@ cudaError_t run_step(Engine* e, const StepParams& P) {
 void drop_graphs(Engine* e) {
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   e->graphs.clear();
+}
+
+// Environment knobs read per call, as the reference does (dpuf_engine.c:2022-2027, 2091-2118).
+StepParams step_params(const Engine* e, int n, int only_last) {
+  StepParams P{};
+  P.M = n;
+  P.only_last = only_last == 0 ? 0 : (only_last == 2 ? 2 : 1);
+  P.keep = 0;
+  if (const char* kt = getenv(n > 1 ? "DPUF_PREFILL_KEEP_TILES" : "DPUF_GEN_KEEP_TILES")) {
+    const int v = atoi(kt);
+    P.keep = (v > 0) ? v : 0;
+  }
+  const int lm_M = P.only_last == 1 ? 1 : n;
+  P.za = 0;
+  P.margin = 0.0f;
+  P.greedy_loop = false;
+  const char* env_t = getenv("DPUF_EARLY_TILES");
+  if (env_t && P.only_last != 2 && lm_M == 1 && e->lm.n_tiles > 2048) {
+    int za = atoi(env_t);
+    za = std::max(za, 256);
+    za = std::min(za, e->lm.n_tiles);
+    P.za = za;
+    const char* env_m = getenv("DPUF_EARLY_MARGIN");
+    P.margin = env_m ? (float)atof(env_m) : 1.25f;
+  }
+  return P;
 }
 
 int env_int(const char* name, int def) {
@@ -451,26 +482,8 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
       return -1;
     }
   if (cudaSetDevice(e->device) != cudaSuccess) return -4;
-  StepParams P{};
-  P.M = n;
-  P.only_last = only_last == 0 ? 0 : (only_last == 2 ? 2 : 1);
-  P.keep = 0;
-  if (const char* kt = getenv(n > 1 ? "DPUF_PREFILL_KEEP_TILES" : "DPUF_GEN_KEEP_TILES")) {
-    const int v = atoi(kt);
-    P.keep = (v > 0) ? v : 0;
-  }
+  const StepParams P = step_params(e, n, only_last);
   const int lm_M = P.only_last == 1 ? 1 : n;
-  P.za = 0;
-  P.margin = 0.0f;
-  const char* env_t = getenv("DPUF_EARLY_TILES");
-  if (env_t && P.only_last != 2 && lm_M == 1 && e->lm.n_tiles > 2048) {
-    int za = atoi(env_t);
-    za = std::max(za, 256);
-    za = std::min(za, e->lm.n_tiles);
-    P.za = za;
-    const char* env_m = getenv("DPUF_EARLY_MARGIN");
-    P.margin = env_m ? (float)atof(env_m) : 1.25f;
-  }
   memcpy(e->stage->ids, ids, (size_t)n * 4);
   e->stage->pos0 = pos0;
   cudaError_t err = run_step(e, P);
@@ -613,9 +626,11 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
       cudaMalloc(&e->prep_q8, 3 * B * ld) || cudaMalloc(&e->prep_xs, 3 * B * (ld / 32) * 4) ||
       cudaMalloc(&e->prep_xm, 3 * B * (ld / 32) * 4) || cudaMalloc(&e->d_ids, sizeof(Staging)) ||
       cudaMalloc(&e->d_flag, 16) || cudaMalloc(&e->d_b12, 16) || cudaMalloc(&e->d_argmax, B * 4) ||
+      cudaMalloc(&e->d_hist, (size_t)(e->S + 4) * 4) ||
       cudaMallocHost(&e->stage, sizeof(Staging)) || cudaMallocHost(&e->h_logits, (size_t)e->V * 4))
     return fail("activation buffers");
   e->d_pos0 = e->d_ids + kMaxBatch;
+  e->d_hist_step = e->d_hist + e->S;
   for (int i = 0; i < 3; i++)
     e->prep[i] = Act{e->prep_q8 + i * B * ld, e->prep_xs + i * B * (ld / 32), e->prep_xm + i * B * (ld / 32), ld};
   cudaMemset(e->d_flag, 0, 16);
@@ -758,6 +773,43 @@ DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, con
       cudaStreamSynchronize(e->stream) != cudaSuccess)
     return -4;
   return 0;
+}
+
+// n_steps greedy decode steps at batch 1 with the token fed back on the device.  The step
+// kernels are the same as dpuf_engine_forward_token's; only the id hand-off differs.
+DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int32_t pos0, int32_t n_steps,
+                                            int32_t* ids_out, float* device_ms) {
+  Engine* e = (Engine*)handle;
+  if (!e || !ids_out) return -1;
+  if (n_steps <= 0) return -2;
+  if (pos0 < 0 || pos0 + n_steps > e->S) return -3;
+  if (first_id < 0 || first_id >= e->tok.rows) return -1;
+  if (cudaSetDevice(e->device) != cudaSuccess) return -4;
+  dpuf::StepParams P = dpuf::step_params(e, 1, 1);
+  P.greedy_loop = true;
+  e->stage->ids[0] = first_id;
+  e->stage->pos0 = pos0;
+  const int32_t zero = 0;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  if (cudaMemcpyAsync(e->d_ids, e->stage, sizeof(dpuf::Staging), cudaMemcpyHostToDevice, e->stream) ||
+      cudaMemcpyAsync(e->d_hist_step, &zero, 4, cudaMemcpyHostToDevice, e->stream) ||
+      cudaStreamSynchronize(e->stream) || cudaEventCreate(&ev0) || cudaEventCreate(&ev1))
+    return -4;
+  cudaEventRecord(ev0, e->stream);
+  for (int i = 0; i < n_steps; i++)
+    if (dpuf::run_step(e, P) != cudaSuccess) { cudaEventDestroy(ev0); cudaEventDestroy(ev1); return -4; }
+  cudaEventRecord(ev1, e->stream);
+  int32_t rc = 0;
+  if (cudaMemcpyAsync(ids_out, e->d_hist, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->stream) ||
+      cudaStreamSynchronize(e->stream))
+    rc = -4;
+  float ms = 0.0f;
+  if (rc == 0 && cudaEventElapsedTime(&ms, ev0, ev1) != cudaSuccess) rc = -4;
+  if (device_ms) *device_ms = ms;
+  cudaEventDestroy(ev0);
+  cudaEventDestroy(ev1);
+  e->last_rows = 1;
+  return rc;
 }
 
 DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out) {

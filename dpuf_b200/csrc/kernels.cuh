@@ -74,6 +74,9 @@ cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0);
 cudaError_t launch_zone_test(const Launch& L, const float* logits, int n, float margin, int* flag, float* b12);
 // If *flag: logits[from, V) = -1e9.
 cudaError_t launch_zone_mask(const Launch& L, float* logits, int from, int V, const int* flag);
+// Greedy feedback between back-to-back decode steps (see kernels_lmhead.cu).
+cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, int32_t* ids, int32_t* pos0,
+                                  int32_t* hist, int32_t* step);
 // First index of the maximum of each of M rows.
 cudaError_t launch_argmax(const Launch& L, const float* logits, int M, int V, int ld, int32_t* out);
 

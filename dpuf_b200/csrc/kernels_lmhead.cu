@@ -103,7 +103,53 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
+// Device-side greedy feedback for back-to-back decode steps: the first maximal index of the
+// logits becomes the next step's token id; the position advances by one and the id is appended
+// to the history.
+__global__ void __launch_bounds__(1024) greedy_advance_kernel(const float* __restrict__ logits, int V,
+                                                              int32_t* __restrict__ ids, int32_t* __restrict__ pos0,
+                                                              int32_t* __restrict__ hist, int32_t* __restrict__ step) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  cudaGridDependencySynchronize();
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = logits[i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+  for (int m = 16; m; m >>= 1) {
+    const float ov = __shfl_xor_sync(kFull, bv, m);
+    const int oi = __shfl_xor_sync(kFull, bi, m);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    bv = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
+    for (int m = 16; m; m >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, bv, m);
+      const int oi = __shfl_xor_sync(kFull, bi, m);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (threadIdx.x == 0) {
+      const int id = (bi == 0x7fffffff) ? 0 : bi;
+      ids[0] = id;
+      hist[*step] = id;
+      *step += 1;
+      *pos0 += 1;
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, int32_t* ids, int32_t* pos0,
+                                  int32_t* hist, int32_t* step) {
+  return launch_k(L, greedy_advance_kernel, dim3(1), dim3(1024), 0, logits, V, ids, pos0, hist, step);
+}
 
 cudaError_t launch_zone_test(const Launch& L, const float* logits, int n, float margin, int* flag, float* b12) {
   return launch_k(L, zone_test_kernel, dim3(1), dim3(1024), 0, logits, n, margin, flag, b12);

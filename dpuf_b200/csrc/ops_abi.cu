@@ -130,6 +130,45 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev
   return dpuf::matmul_dev(h, M, x_dev, y_dev, (cudaStream_t)stream);
 }
 
+// Kernel-only timing: preps x once per handle, then launches only the matmul kernel `iters`
+// times, rotating over the handles (so the weights streamed exceed L2), bracketed by CUDA
+// events on `stream`.  *ms_out = average milliseconds per launch.
+DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, int32_t M, const float* x_dev,
+                                               float* y_dev, int32_t iters, void* stream, float* ms_out) {
+  if (!whs || n_handles <= 0 || M <= 0 || M > dpuf::kOpChunk || iters <= 0 || !ms_out) return -1;
+  cudaStream_t s = (cudaStream_t)stream;
+  const dpuf::Launch L{s, false};
+  for (int i = 0; i < n_handles; i++) {
+    W12Handle* h = (W12Handle*)whs[i];
+    const dpuf::Act a{h->q8, h->xs, h->xm, h->w.cols};
+    if (dpuf::launch_prep(L, x_dev, h->w.cols, M, h->w.cols, h->w.signs, a) != cudaSuccess) return -4;
+  }
+  auto launch = [&](int i) {
+    W12Handle* h = (W12Handle*)whs[i % n_handles];
+    const dpuf::Act a{h->q8, h->xs, h->xm, h->w.cols};
+    dpuf::LinJobs J = {};
+    J.n = 1;
+    J.j[0] = {h->w, a, y_dev, h->w.rows, 0, h->w.n_tiles};
+    J.tile_prefix[1] = h->w.n_tiles;
+    return M == 1 ? dpuf::launch_gemv(L, J, nullptr) : dpuf::launch_gemm_exact(L, J, M);
+  };
+  for (int i = 0; i < 2 * n_handles; i++)
+    if (launch(i) != cudaSuccess) return -4;
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) || cudaEventCreate(&e1)) return -4;
+  cudaEventRecord(e0, s);
+  for (int i = 0; i < iters; i++)
+    if (launch(i) != cudaSuccess) return -4;
+  cudaEventRecord(e1, s);
+  float ms = 0;
+  const bool ok = cudaEventSynchronize(e1) == cudaSuccess && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (!ok) return -4;
+  *ms_out = ms / iters;
+  return 0;
+}
+
 // Reference signature (dpuf_avx2.c:2678): host in, host out, synchronous.
 DPUF_EXPORT void dpuf_matmul_qr_hadamard4_packed_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
                                                      const float* x_in, const uint8_t* tensor_base,

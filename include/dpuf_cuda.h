@@ -24,6 +24,13 @@ DPUF_EXPORT const char* dpuf_cuda_last_error(void);
 DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, const int32_t* token_ids,
                                              int32_t pos0, int32_t* next_id);
 
+/* n_steps greedy decode steps at batch 1 starting from token first_id at position pos0, with
+ * each step's token chosen and fed back on the device (same kernels as forward_token; the
+ * logits never leave the device).  ids_out[n_steps] receives the generated ids; *device_ms
+ * (optional) the CUDA-event time of the steps on the engine's stream. */
+DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int32_t pos0, int32_t n_steps,
+                                            int32_t* ids_out, float* device_ms);
+
 /* Copies the last forward's logits row `row` (0-based among the rows produced) to host. */
 DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out);
 
@@ -43,6 +50,14 @@ DPUF_EXPORT void dpuf_cuda_w12_free(void* wh);
  * NULL = default stream) without synchronising.  Scratch for the quantised activation is
  * owned by the weight handle.  Returns 0 or a negative error. */
 DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev, float* y_dev, void* stream);
+
+/* Kernel-only timing of the matmul (activation prep excluded): `iters` launches rotating over
+ * n_handles uploaded weights, CUDA events on `stream`; *ms_out = mean ms per launch. */
+DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, int32_t M, const float* x_dev,
+                                               float* y_dev, int32_t iters, void* stream, float* ms_out);
+
+/* Builds or loads the glibc expf exception table; returns its entry count (host only). */
+DPUF_EXPORT int64_t dpuf_cuda_prepare_expf_table(void);
 
 #ifdef __cplusplus
 }
