@@ -34,6 +34,7 @@ CUDA_SOURCES = [
     "kernels_attn.cu",
     "kernels_lmhead.cu",
     "ops_abi.cu",
+    "noalloc.cu",
 ]
 
 

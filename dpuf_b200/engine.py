@@ -63,6 +63,8 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_embed_qr_hadamard4_packed_f32.restype = None
     lib.dpuf_embed_qr_hadamard4_packed_f32.argtypes = [_I32, _I32] + [_VP] * 5
     lib.dpuf_cuda_prepare_expf_table.restype = ctypes.c_int64
+    lib.dpuf_cuda_matmul_noalloc.restype = _I32
+    lib.dpuf_cuda_matmul_noalloc.argtypes = [_I32] * 4 + [_VP] * 6
     lib._dpuf_typed = True
     return lib
 

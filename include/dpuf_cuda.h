@@ -56,6 +56,23 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev
 DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, int32_t M, const float* x_dev,
                                                float* y_dev, int32_t iters, void* stream, float* ms_out);
 
+/* The standalone matmul for callers that cannot allocate device memory: hosts that reserve
+ * the GPU's memory for their own pool at start-up (a further cudaMalloc fails or escapes their
+ * accounting) and latency-critical loops that cannot afford cudaMalloc/cudaFree's implicit
+ * device synchronisation.  No counterpart in the reference (its matmul is CPU-only).
+ * Everything is a DEVICE pointer the caller owns: x[M][cols] in, y[M][rows] out, the weight as
+ * its container tiles, tile offsets relative to tiles_dev (the reference's tile_offsets) and
+ * sign bits.  Allocates nothing: the quantised activation lives in a fixed device array of
+ * 2^20 values (1.25 MiB, held by every GPU that loads the library until exit).
+ * Returns 0; -1 bad arguments; -2 M * cols > 2^20 (rejected, see dpuf_cuda_last_error);
+ * -4 CUDA error.  Enqueues on `stream` without synchronising.  The first call on a device sets
+ * the device up (resolves the array's address); make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised. */
+DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                             const float* x_dev, const uint8_t* tiles_dev,
+                                             const uint64_t* tile_offsets_dev, const uint8_t* sign_bits_dev,
+                                             float* y_dev, void* stream);
+
 /* Builds or loads the glibc expf exception table; returns its entry count (host only). */
 DPUF_EXPORT int64_t dpuf_cuda_prepare_expf_table(void);
 
