@@ -375,12 +375,20 @@ def main():
     ap.add_argument("--impl", default="dpuf", choices=["dpuf", "reference"])
     ap.add_argument("--model", default="8b", choices=["8b", "0.6b"],
                     help="8b = the benchmark workload; 0.6b = a small case for profiling")
+    ap.add_argument("--gemv-only", action="store_true",
+                    help="only the kernel-only GEMV roofline measurement (for profiling the GEMV)")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args.gpus)
+    if args.gemv_only:
+        import torch
+
+        torch.cuda.set_device(local)
+        print(json.dumps(gemv_roofline(*peaks())), flush=True)
+        return
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

@@ -30,6 +30,7 @@ CUDA_SOURCES = [
     "engine.cu",
     "expf_table.cu",
     "kernels_mode12.cu",
+    "kernels_gemv.cu",
     "kernels_layer.cu",
     "kernels_attn.cu",
     "kernels_lmhead.cu",

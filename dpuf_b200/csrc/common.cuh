@@ -45,12 +45,16 @@ struct Act {
 };
 
 // glibc expf reproduction: dpuf_exp_d rounded to float, corrected by an exception table of
-// the inputs where glibc's expf differs (sorted input bit patterns -> glibc output bits).
+// the inputs where glibc's expf differs, held as an open-addressing hash: slot i holds
+// (input bits, glibc output bits), empty slots hold kExpfEmpty; a key's probe sequence starts
+// at expf_hash(key) & mask and is at most max_probe slots long.
+constexpr uint32_t kExpfEmpty = 0xFFFFFFFFu;  // a NaN pattern: never an exception key
 struct ExpfTable {
-  const uint32_t* keys;
-  const uint32_t* vals;
-  int n;
+  const uint2* slots;
+  uint32_t mask;
+  int max_probe;
 };
+DPUF_HD uint32_t expf_hash(uint32_t key) { return (key * 2654435761u) ^ (key >> 15); }
 
 // Raises a kernel's dynamic shared-memory limit to the device's opt-in maximum minus the
 // kernel's static shared memory.
@@ -154,13 +158,13 @@ DPUF_HD double dpuf_exp_d(double x) {
 }
 
 DPUF_DEV float glibc_expf(float x, const ExpfTable& t) {
-  uint32_t key = __float_as_uint(x);
-  int lo = 0, hi = t.n - 1;
-  while (lo <= hi) {
-    int mid = (lo + hi) >> 1;
-    uint32_t k = t.keys[mid];
-    if (k == key) return __uint_as_float(t.vals[mid]);
-    if (k < key) lo = mid + 1; else hi = mid - 1;
+  const uint32_t key = __float_as_uint(x);
+  uint32_t i = expf_hash(key) & t.mask;
+  for (int p = 0; p < t.max_probe; p++) {
+    const uint2 e = t.slots[i];
+    if (e.x == key) return __uint_as_float(e.y);
+    if (e.x == kExpfEmpty) break;
+    i = (i + 1) & t.mask;
   }
   return __double2float_rn(dpuf_exp_d((double)x));
 }

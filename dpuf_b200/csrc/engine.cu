@@ -126,8 +126,10 @@ struct Engine {
   int32_t* d_hist_step = nullptr;
   Staging* stage = nullptr;  // pinned
   float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
-  uint32_t* d_exp_keys = nullptr;
-  uint32_t* d_exp_vals = nullptr;
+  uint2* d_exp_slots = nullptr;
+  unsigned* d_counter = nullptr;  // last-block counters of the multi-CTA argmax
+  float2* d_part = nullptr;       // per-CTA argmax partials
+  GemvSplit split{};              // GEMV scratch for 16-row units shared by CTAs
   ExpfTable et{};
 
   std::map<StepKey, cudaGraphExec_t> graphs;
@@ -158,6 +160,8 @@ bool desc_ok(const DpufWeightDesc& w, int rows, int cols) {
   if (w.mode != DPUF_MODE_QR_HAD4_PACKED || !w.tensor_base || !w.tile_offsets || !w.sign_bits) return false;
   if (w.rows != rows || w.cols != cols || (cols % 64) != 0) return false;
   if (w.n_tiles != (rows + kTileRows - 1) / kTileRows) return false;
+  for (int t = 0; t < w.n_tiles; t++)  // the GEMV streams tiles with 16-byte async copies
+    if (w.tile_offsets[t] % 16 != 0) return false;
   return true;
 }
 
@@ -275,7 +279,8 @@ void destroy_engine(Engine* e) {
   cudaFree(e->gate); cudaFree(e->up); cudaFree(e->logits);
   cudaFree(e->prep_q8); cudaFree(e->prep_xs); cudaFree(e->prep_xm);
   cudaFree(e->d_ids); cudaFree(e->d_hist); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
-  cudaFree(e->d_exp_keys); cudaFree(e->d_exp_vals);
+  cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part);
+  cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -297,9 +302,9 @@ LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1)
   return J;
 }
 
-cudaError_t run_linear(const Launch& Lc, const LinJobs& J, int M, const int* skip) {
+cudaError_t run_linear(const Engine* e, const Launch& Lc, const LinJobs& J, int M, const int* skip) {
   if (J.tile_prefix[J.n] == 0) return cudaSuccess;
-  return M == 1 ? launch_gemv(Lc, J, skip) : launch_gemm_exact(Lc, J, M);
+  return M == 1 ? launch_gemv(Lc, J, skip, &e->split) : launch_gemm_exact(Lc, J, M);
 }
 
 // Prep targets for weights sharing one input: identical sign tables share a prep slot
@@ -346,7 +351,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
         J.j[i] = {*ws[i], e->prep[so[i]], outs[i], ldo[i], 0, ws[i]->n_tiles};
         J.tile_prefix[i + 1] = J.tile_prefix[i] + ws[i]->n_tiles;
       }
-      CK(run_linear(Lc, J, M, nullptr));
+      CK(run_linear(e, Lc, J, M, nullptr));
     }
     // 3-4. QK norm, RoPE, KV store; attention
     CK(launch_qk_post(Lc, e->q, e->k, e->v, M, e->nq, e->nkv, e->hd, e->cfg.has_qk_norm ? lw.q_norm : nullptr,
@@ -355,7 +360,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
     CK(launch_attention(Lc, e->q, M, e->nq, e->nkv, e->hd, e->d_pos0, kv, e->att, e->et));
     // 5. o_proj
     CK(launch_prep(Lc, e->att, e->qd, M, e->qd, lw.o.signs, e->prep[0]));
-    CK(run_linear(Lc, one_job(lw.o, e->prep[0], e->hn, H, 0, lw.o.n_tiles), M, nullptr));
+    CK(run_linear(e, Lc, one_job(lw.o, e->prep[0], e->hn, H, 0, lw.o.n_tiles), M, nullptr));
     // 6-8. h += o; RMSNorm; gate/up
     {
       const W12* ws[2] = {&lw.gate, &lw.up};
@@ -370,12 +375,12 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
       J.tile_prefix[1] = lw.gate.n_tiles;
       J.j[1] = {lw.up, e->prep[so[1]], e->up, e->I, 0, lw.up.n_tiles};
       J.tile_prefix[2] = lw.gate.n_tiles + lw.up.n_tiles;
-      CK(run_linear(Lc, J, M, nullptr));
+      CK(run_linear(e, Lc, J, M, nullptr));
     }
     // 9-11. SwiGLU + prep, down (optionally pruned to the first `keep` tiles)
     CK(launch_swiglu_prep(Lc, e->gate, e->up, M, e->I, e->deadzone, e->nt_ref, lw.down.signs, e->prep[0], e->et));
     const int keep = (P.keep > 0 && P.keep < lw.down.n_tiles) ? P.keep : lw.down.n_tiles;
-    CK(run_linear(Lc, one_job(lw.down, e->prep[0], e->hn, H, 0, keep), M, nullptr));
+    CK(run_linear(e, Lc, one_job(lw.down, e->prep[0], e->hn, H, 0, keep), M, nullptr));
     if (keep < lw.down.n_tiles) CK(launch_zero_rows(Lc, e->hn, M, H, keep * kTileRows));
   }
   if (P.only_last == 2) return cudaSuccess;
@@ -390,14 +395,16 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   }
   if (P.za > 0) {
     const int n_za = std::min(P.za * kTileRows, e->V);
-    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, P.za), 1, nullptr));
+    CK(run_linear(e, Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, P.za), 1, nullptr));
     CK(launch_zone_test(Lc, e->logits, n_za, P.margin, e->d_flag, e->d_b12));
-    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, P.za, e->lm.n_tiles), 1, e->d_flag));
+    CK(run_linear(e, Lc, one_job(e->lm, e->prep[0], e->logits, e->V, P.za, e->lm.n_tiles), 1, e->d_flag));
     CK(launch_zone_mask(Lc, e->logits, P.za * kTileRows, e->V, e->d_flag));
   } else {
-    CK(run_linear(Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, e->lm.n_tiles), lm_M, nullptr));
+    CK(run_linear(e, Lc, one_job(e->lm, e->prep[0], e->logits, e->V, 0, e->lm.n_tiles), lm_M, nullptr));
   }
-  if (P.greedy_loop) CK(launch_greedy_advance(Lc, e->logits, e->V, e->d_ids, e->d_pos0, e->d_hist, e->d_hist_step));
+  if (P.greedy_loop)
+    CK(launch_greedy_advance(Lc, e->logits, e->V, e->d_part, e->d_counter, e->d_ids, e->d_pos0, e->d_hist,
+                             e->d_hist_step));
   return cudaSuccess;
 }
 
@@ -608,13 +615,14 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   }
   // ---- expf exception table
   {
-    const auto& keys = expf_exception_keys();
-    const auto& vals = expf_exception_vals();
-    if (cudaMalloc(&e->d_exp_keys, keys.size() * 4 + 4) || cudaMalloc(&e->d_exp_vals, vals.size() * 4 + 4) ||
-        cudaMemcpy(e->d_exp_keys, keys.data(), keys.size() * 4, cudaMemcpyHostToDevice) ||
-        cudaMemcpy(e->d_exp_vals, vals.data(), vals.size() * 4, cudaMemcpyHostToDevice))
+    std::vector<uint2> slots;
+    uint32_t mask = 0;
+    int max_probe = 0;
+    expf_exception_hash(slots, &mask, &max_probe);
+    if (cudaMalloc(&e->d_exp_slots, slots.size() * sizeof(uint2)) ||
+        cudaMemcpy(e->d_exp_slots, slots.data(), slots.size() * sizeof(uint2), cudaMemcpyHostToDevice))
       return fail("expf table");
-    e->et = ExpfTable{e->d_exp_keys, e->d_exp_vals, (int)keys.size()};
+    e->et = ExpfTable{e->d_exp_slots, mask, max_probe};
   }
   // ---- activations
   const size_t B = kMaxBatch;
@@ -626,14 +634,21 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
       cudaMalloc(&e->prep_q8, 3 * B * ld) || cudaMalloc(&e->prep_xs, 3 * B * (ld / 32) * 4) ||
       cudaMalloc(&e->prep_xm, 3 * B * (ld / 32) * 4) || cudaMalloc(&e->d_ids, sizeof(Staging)) ||
       cudaMalloc(&e->d_flag, 16) || cudaMalloc(&e->d_b12, 16) || cudaMalloc(&e->d_argmax, B * 4) ||
-      cudaMalloc(&e->d_hist, (size_t)(e->S + 4) * 4) ||
+      cudaMalloc(&e->d_hist, (size_t)(e->S + 4) * 4) || cudaMalloc(&e->d_counter, 64) ||
+      cudaMalloc(&e->d_part, kArgmaxBlocks * sizeof(float2)) ||
       cudaMallocHost(&e->stage, sizeof(Staging)) || cudaMallocHost(&e->h_logits, (size_t)e->V * 4))
     return fail("activation buffers");
+  if (cudaMalloc(&e->split.pairs, gemv_split_pairs_bytes(ld)) ||
+      cudaMalloc(&e->split.acc, (size_t)kGemvMaxCtas * kTileRows * sizeof(float)) ||
+      cudaMalloc(&e->split.count, (size_t)kGemvMaxCtas * sizeof(unsigned)) ||
+      cudaMemset(e->split.count, 0, (size_t)kGemvMaxCtas * sizeof(unsigned)))
+    return fail("GEMV scratch");
   e->d_pos0 = e->d_ids + kMaxBatch;
   e->d_hist_step = e->d_hist + e->S;
   for (int i = 0; i < 3; i++)
     e->prep[i] = Act{e->prep_q8 + i * B * ld, e->prep_xs + i * B * (ld / 32), e->prep_xm + i * B * (ld / 32), ld};
   cudaMemset(e->d_flag, 0, 16);
+  cudaMemset(e->d_counter, 0, 64);
   if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
   return e;
 }
@@ -768,7 +783,7 @@ DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, con
                                           1, nullptr, false);
   if (rc != 0) return rc;
   const dpuf::Launch Lc{e->stream, false};
-  if (dpuf::launch_argmax(Lc, e->logits, 1, e->V, e->V, e->d_argmax) != cudaSuccess ||
+  if (dpuf::launch_argmax(Lc, e->logits, e->V, e->d_part, e->d_counter + 1, e->d_argmax) != cudaSuccess ||
       cudaMemcpyAsync(next_id, e->d_argmax, 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
       cudaStreamSynchronize(e->stream) != cudaSuccess)
     return -4;

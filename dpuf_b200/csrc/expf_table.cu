@@ -160,6 +160,27 @@ const std::vector<uint32_t>& expf_exception_vals() {
   return g_vals;
 }
 
+void expf_exception_hash(std::vector<uint2>& slots, uint32_t* mask, int* max_probe) {
+  const auto& keys = expf_exception_keys();
+  const auto& vals = expf_exception_vals();
+  size_t cap = 1024;
+  while (cap < keys.size() * 3) cap <<= 1;  // load factor <= 1/3
+  slots.assign(cap, make_uint2(kExpfEmpty, 0u));
+  *mask = (uint32_t)(cap - 1);
+  int longest = 1;
+  for (size_t k = 0; k < keys.size(); k++) {
+    uint32_t i = expf_hash(keys[k]) & *mask;
+    int probe = 1;
+    while (slots[i].x != kExpfEmpty) {
+      i = (i + 1) & *mask;
+      probe++;
+    }
+    slots[i] = make_uint2(keys[k], vals[k]);
+    longest = std::max(longest, probe);
+  }
+  *max_probe = longest;
+}
+
 }  // namespace dpuf
 
 // Builds (or validates) the cached table; returns the number of exceptions.  Called by the

@@ -37,8 +37,19 @@ cudaError_t configure_kernels();
 // ---- kernels_mode12.cu
 cudaError_t launch_prep(const Launch& L, const float* x, int ldx, int M, int cols, const uint8_t* signs, Act out);
 cudaError_t launch_embed(const Launch& L, const W12& w, const int32_t* ids, int M, float* out);
-// M == 1: HBM-streaming GEMV.  skip_flag: when non-null and nonzero at run time, CTAs exit.
-cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag);
+// M == 1: HBM-streaming GEMV over a persistent grid (kernels_gemv.cu).  All jobs of one launch
+// share K.  skip_flag: when non-null and nonzero at run time, CTAs exit.  split: scratch that
+// lets a 16-row unit be shared by two or more CTAs (pairs: gemv_split_pairs_bytes(cols) bytes,
+// acc: kGemvMaxCtas*16 floats, count: kGemvMaxCtas zero-initialised words, left at zero); with
+// split == nullptr every CTA takes whole units.  One launch at a time may use a scratch.
+struct GemvSplit {
+  float2* pairs;
+  float* acc;
+  unsigned* count;
+};
+constexpr int kGemvMaxCtas = 512;
+size_t gemv_split_pairs_bytes(int max_cols);
+cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split);
 // M > 1: exact integer-dot GEMM on CUDA cores (reference order per (token,row)).
 cudaError_t launch_gemm_exact(const Launch& L, const LinJobs& jobs, int M);
 
@@ -74,10 +85,13 @@ cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0);
 cudaError_t launch_zone_test(const Launch& L, const float* logits, int n, float margin, int* flag, float* b12);
 // If *flag: logits[from, V) = -1e9.
 cudaError_t launch_zone_mask(const Launch& L, float* logits, int from, int V, const int* flag);
-// Greedy feedback between back-to-back decode steps (see kernels_lmhead.cu).
-cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, int32_t* ids, int32_t* pos0,
-                                  int32_t* hist, int32_t* step);
-// First index of the maximum of each of M rows.
-cudaError_t launch_argmax(const Launch& L, const float* logits, int M, int V, int ld, int32_t* out);
+// Greedy argmax over V logits on kArgmaxBlocks CTAs (part: kArgmaxBlocks partials; counter: one
+// zero-initialised word, left at zero).  launch_argmax writes the index to *out;
+// launch_greedy_advance feeds it back as the next decode step's token (ids[0], *pos0 += 1,
+// hist[(*step)++]).
+constexpr int kArgmaxBlocks = 148;
+cudaError_t launch_argmax(const Launch& L, const float* logits, int V, float2* part, unsigned* counter, int32_t* out);
+cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, float2* part, unsigned* counter,
+                                  int32_t* ids, int32_t* pos0, int32_t* hist, int32_t* step);
 
 }  // namespace dpuf

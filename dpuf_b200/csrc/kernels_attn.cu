@@ -123,24 +123,27 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
     for (int k = tid; k < kv8; k += blockDim.x) sc[h * kv.max_seq + k] = exp_poly(__fsub_rn(sc[h * kv.max_seq + k], mx));
   }
   __syncthreads();
-  // ---- lane sums (8 sequential chains per head), split tree, sequential tail
+  // ---- lane sums (8 sequential chains per head); the <= 7 tail exponentials (glibc expf) are
+  // independent, so eight more threads per head evaluate them meanwhile
   if (tid < 8 * nh) {
     const int h = tid >> 3, l = tid & 7;
     const float* s = sc + h * kv.max_seq;
     float acc = 0.0f;
     for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, s[k]);
     lane_sum[h][l] = acc;
+  } else if (tid >= 64 && tid < 64 + 8 * nh) {
+    const int h = (tid - 64) >> 3, k = kv8 + ((tid - 64) & 7);
+    if (k < kv_len) {
+      float* s = sc + h * kv.max_seq;
+      s[k] = glibc_expf(__fsub_rn(s[k], max_s[h]), et);
+    }
   }
   __syncthreads();
+  // split tree of the lane sums, then the tail added in order
   if (tid < nh) {
-    float* s = sc + tid * kv.max_seq;
-    const float mx = max_s[tid];
+    const float* s = sc + tid * kv.max_seq;
     float sp = tree8_split_arr(lane_sum[tid]);
-    for (int k = kv8; k < kv_len; k++) {
-      const float e = glibc_expf(__fsub_rn(s[k], mx), et);
-      s[k] = e;
-      sp = __fadd_rn(sp, e);
-    }
+    for (int k = kv8; k < kv_len; k++) sp = __fadd_rn(sp, s[k]);
     inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(sp, 1e-12f));
   }
   __syncthreads();

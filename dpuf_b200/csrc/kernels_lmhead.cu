@@ -70,23 +70,21 @@ __global__ void zone_mask_kernel(float* __restrict__ logits, int from, int V, co
   for (int i = from + blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) logits[i] = -1e9f;
 }
 
-// First index of the maximum (strict '>' scan, dpuf-cli.c:1997-2005): ties keep the lower index.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int ld,
-                                                      int32_t* __restrict__ out) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  cudaGridDependencySynchronize();
-  const float* row = logits + (size_t)blockIdx.x * ld;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = row[i];
-    if (v > bv) { bv = v; bi = i; }
-  }
+// First index of the maximum (strict '>' scan, dpuf-cli.c:1997-2005), over kArgmaxBlocks CTAs:
+// CTA c reduces the slice [c*V/n, (c+1)*V/n) to (value, index) with ties keeping the lower
+// index, writes it to part[c], and the last CTA to finish (counted by an atomic, no waiting)
+// reduces the partials in slice order - the same first-maximal index as a sequential scan.
+// With `greedy`, the winner becomes the next decode step's token: ids[0] = winner, the
+// position advances and the id is appended to the history (back-to-back decode steps).
+DPUF_DEV void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+}
+
+DPUF_DEV void block_argmax(float& bv, int& bi, float* sv, int* si) {
   for (int m = 16; m; m >>= 1) {
     const float ov = __shfl_xor_sync(kFull, bv, m);
     const int oi = __shfl_xor_sync(kFull, bi, m);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    better(bv, bi, ov, oi);
   }
   if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
   __syncthreads();
@@ -97,58 +95,61 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     for (int m = 16; m; m >>= 1) {
       const float ov = __shfl_xor_sync(kFull, bv, m);
       const int oi = __shfl_xor_sync(kFull, bi, m);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      better(bv, bi, ov, oi);
     }
-    if (threadIdx.x == 0) out[blockIdx.x] = (bi == 0x7fffffff) ? 0 : bi;
   }
 }
 
-// Device-side greedy feedback for back-to-back decode steps: the first maximal index of the
-// logits becomes the next step's token id; the position advances by one and the id is appended
-// to the history.
-__global__ void __launch_bounds__(1024) greedy_advance_kernel(const float* __restrict__ logits, int V,
-                                                              int32_t* __restrict__ ids, int32_t* __restrict__ pos0,
-                                                              int32_t* __restrict__ hist, int32_t* __restrict__ step) {
+__global__ void __launch_bounds__(256) argmax_blocks_kernel(const float* __restrict__ logits, int V, float2* part,
+                                                            unsigned* counter, int32_t* out, bool greedy,
+                                                            int32_t* ids, int32_t* pos0, int32_t* hist,
+                                                            int32_t* step) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  __shared__ bool last;
   cudaGridDependencySynchronize();
+  const int c = blockIdx.x, nb = gridDim.x;
+  const int i0 = (int)((long long)V * c / nb), i1 = (int)((long long)V * (c + 1) / nb);
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = logits[i];
-    if (v > bv) { bv = v; bi = i; }
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) better(bv, bi, logits[i], i);
+  block_argmax(bv, bi, sv, si);
+  if (threadIdx.x == 0) {
+    part[c] = make_float2(bv, __int_as_float(bi));
+    __threadfence();
+    last = atomicAdd(counter, 1u) == (unsigned)(nb - 1);
   }
-  for (int m = 16; m; m >>= 1) {
-    const float ov = __shfl_xor_sync(kFull, bv, m);
-    const int oi = __shfl_xor_sync(kFull, bi, m);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-  }
-  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const int nw = blockDim.x >> 5;
-    bv = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
-    bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffff;
-    for (int m = 16; m; m >>= 1) {
-      const float ov = __shfl_xor_sync(kFull, bv, m);
-      const int oi = __shfl_xor_sync(kFull, bi, m);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (threadIdx.x == 0) {
-      const int id = (bi == 0x7fffffff) ? 0 : bi;
+  if (!last) return;
+  __threadfence();
+  bv = -INFINITY;
+  bi = 0x7fffffff;
+  for (int k = threadIdx.x; k < nb; k += blockDim.x) {
+    const float2 p = __ldcg(part + k);
+    better(bv, bi, p.x, __float_as_int(p.y));
+  }
+  __syncthreads();
+  block_argmax(bv, bi, sv, si);
+  if (threadIdx.x == 0) {
+    const int id = (bi == 0x7fffffff) ? 0 : bi;
+    *counter = 0u;
+    if (greedy) {
       ids[0] = id;
       hist[*step] = id;
       *step += 1;
       *pos0 += 1;
+    } else {
+      *out = id;
     }
   }
 }
 
 }  // namespace
 
-cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, int32_t* ids, int32_t* pos0,
-                                  int32_t* hist, int32_t* step) {
-  return launch_k(L, greedy_advance_kernel, dim3(1), dim3(1024), 0, logits, V, ids, pos0, hist, step);
+cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, float2* part, unsigned* counter,
+                                  int32_t* ids, int32_t* pos0, int32_t* hist, int32_t* step) {
+  return launch_k(L, argmax_blocks_kernel, dim3(kArgmaxBlocks), dim3(256), 0, logits, V, part, counter,
+                  (int32_t*)nullptr, true, ids, pos0, hist, step);
 }
 
 cudaError_t launch_zone_test(const Launch& L, const float* logits, int n, float margin, int* flag, float* b12) {
@@ -160,8 +161,9 @@ cudaError_t launch_zone_mask(const Launch& L, float* logits, int from, int V, co
   return launch_k(L, zone_mask_kernel, dim3(min(148, (V - from + 255) / 256)), dim3(256), 0, logits, from, V, flag);
 }
 
-cudaError_t launch_argmax(const Launch& L, const float* logits, int M, int V, int ld, int32_t* out) {
-  return launch_k(L, argmax_kernel, dim3(M), dim3(1024), 0, logits, V, ld, out);
+cudaError_t launch_argmax(const Launch& L, const float* logits, int V, float2* part, unsigned* counter, int32_t* out) {
+  return launch_k(L, argmax_blocks_kernel, dim3(kArgmaxBlocks), dim3(256), 0, logits, V, part, counter, out, false,
+                  (int32_t*)nullptr, (int32_t*)nullptr, (int32_t*)nullptr, (int32_t*)nullptr);
 }
 
 }  // namespace dpuf

@@ -1,5 +1,5 @@
 // kernels_mode12.cu - mode-12 ("Hadamard-4bit packed") activation prep, embedding lookup,
-// decode GEMV and exact prefill GEMM on CUDA cores.
+// and exact prefill GEMM on CUDA cores (the decode GEMV is in kernels_gemv.cu).
 //
 // Arithmetic per (token, row), identical to dpuf_matmul_qr_hadamard4_packed_tile_range
 // (dpuf_avx2.c:2585-2676):
@@ -71,64 +71,6 @@ __global__ void embed_kernel(W12 w, const int32_t* __restrict__ ids, float* __re
   float* o = out + (size_t)m * cols;
   o[c0 + lane] = w.signs ? apply_sign(v[0], w.signs, c0 + lane) : v[0];
   o[c0 + 32 + lane] = w.signs ? apply_sign(v[1], w.signs, c0 + 32 + lane) : v[1];
-}
-
-// ------------------------------------------------------------------ decode GEMV (M == 1)
-// One CTA per 16-row tile.  Phase 1: 256 threads compute the exact block dots of the tile
-// (thread = row-in-group ri, group rg, block phase bs) into shared memory.  Phase 2: one
-// thread per row runs the in-order fp32 chain over the blocks.
-constexpr int kGemvThreads = 256;
-
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(LinJobs J, const int* skip_flag) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  int t;
-  const int j = find_job(J, blockIdx.x, t);
-  const LinJob& job = J.j[j];
-  const int cols = job.w.cols, n_blk = cols >> 5;
-  const uint8_t* tp = tile_ptr(job.w, t);
-  cudaGridDependencySynchronize();
-  if (skip_flag && *skip_flag) return;
-  const int ldd = n_blk + 1;                            // padded: conflict-free stores
-  int* D = (int*)smem;                                  // [16][n_blk + 1]
-  int8_t* xq = (int8_t*)(D + ((16 * ldd + 3) & ~3));    // [cols]
-  float* xs = (float*)(xq + cols);                      // [n_blk]
-  int* xm = (int*)(xs + n_blk);                         // [n_blk]
-  for (int i = threadIdx.x; i < cols / 16; i += blockDim.x)
-    ((int4*)xq)[i] = ((const int4*)job.act.q8)[i];
-  for (int i = threadIdx.x; i < n_blk; i += blockDim.x) {
-    xs[i] = job.act.xs[i];
-    xm[i] = job.act.xm[i];
-  }
-  __syncthreads();
-  const int n_r = tile_nrows(tp);
-  const int n_8g = (n_r + 7) >> 3;
-  {
-    const int ri = threadIdx.x & 7, rg = (threadIdx.x >> 3) & 1, bs = threadIdx.x >> 4;
-    if (rg < n_8g) {
-      const uint8_t* qg = tp + 16 + (size_t)rg * n_blk * 144 + (size_t)n_blk * 16 + ri * 4;
-      for (int b = bs; b < n_blk; b += 16) {
-        const uint8_t* qb = qg + (size_t)b * 128;
-        const int* xw = (const int*)(xq + b * 32);
-        int d = -xm[b];
-#pragma unroll
-        for (int c = 0; c < 4; c++) d = dot_nibbles(*(const uint32_t*)(qb + c * 32), xw[2 * c], xw[2 * c + 1], d);
-        D[(rg * 8 + ri) * ldd + b] = d;
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x < n_r) {
-    const int row = threadIdx.x, rg = row >> 3, ri = row & 7;
-    const uint8_t* sc = tp + 16 + (size_t)rg * n_blk * 144 + ri * 2;
-    float acc = 0.0f;
-    for (int b = 0; b < n_blk; b++) {
-      const float bs = xs[b];
-      if (bs <= 0.0f) continue;
-      const float s = __fmul_rn(f16bits_to_f32(*(const uint16_t*)(sc + (size_t)b * 16)), bs);
-      acc = __fmaf_rn((float)D[row * ldd + b], s, acc);
-    }
-    job.out[(size_t)t * kTileRows + row] = acc;
-  }
 }
 
 // ------------------------------------------------------------------ exact prefill GEMM (M > 1)
@@ -218,9 +160,8 @@ cudaError_t launch_k(const Launch& L, K kernel, dim3 grid, dim3 block, size_t sm
 
 }  // namespace
 
-cudaError_t configure_mode12_kernels() {
-  return set_max_dyn_smem(gemv_kernel);
-}
+cudaError_t configure_gemv_kernels();
+cudaError_t configure_mode12_kernels() { return configure_gemv_kernels(); }
 
 cudaError_t launch_prep(const Launch& L, const float* x, int ldx, int M, int cols, const uint8_t* signs, Act out) {
   const int chunks = cols / 64, wpb = 8;
@@ -230,15 +171,6 @@ cudaError_t launch_prep(const Launch& L, const float* x, int ldx, int M, int col
 cudaError_t launch_embed(const Launch& L, const W12& w, const int32_t* ids, int M, float* out) {
   const int chunks = w.cols / 64, wpb = 8;
   return launch_k(L, embed_kernel, dim3((chunks + wpb - 1) / wpb, M), dim3(wpb * 32), 0, w, ids, out);
-}
-
-cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag) {
-  int max_cols = 0;
-  for (int i = 0; i < jobs.n; i++) max_cols = max(max_cols, jobs.j[i].w.cols);
-  const int n_blk = max_cols / 32;
-  const size_t smem = (size_t)((16 * (n_blk + 1) + 3) & ~3) * 4 + max_cols + (size_t)n_blk * 8;
-  if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
-  return launch_k(L, gemv_kernel, dim3(jobs.tile_prefix[jobs.n]), dim3(kGemvThreads), smem, jobs, skip_flag);
 }
 
 cudaError_t launch_gemm_exact(const Launch& L, const LinJobs& jobs, int M) {

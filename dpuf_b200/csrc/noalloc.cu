@@ -73,6 +73,10 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t co
     dpuf::set_error("dpuf_cuda_matmul_noalloc: null device pointer");
     return -1;
   }
+  if (((uintptr_t)tiles_dev & 15) != 0) {
+    dpuf::set_error("dpuf_cuda_matmul_noalloc: tiles_dev must be 16-byte aligned");
+    return -1;
+  }
   if (rows <= 0 || cols <= 0 || cols % 64 != 0 || n_tiles != (rows + dpuf::kTileRows - 1) / dpuf::kTileRows) {
     dpuf::set_error("dpuf_cuda_matmul_noalloc: need rows > 0, cols % 64 == 0, n_tiles == ceil(rows / 16)");
     return -1;
@@ -102,7 +106,7 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t co
     J.n = 1;
     J.j[0] = {w, a, y_dev, rows, 0, n_tiles};
     J.tile_prefix[1] = n_tiles;
-    e = M == 1 ? dpuf::launch_gemv(L, J, nullptr) : dpuf::launch_gemm_exact(L, J, M);
+    e = M == 1 ? dpuf::launch_gemv(L, J, nullptr, nullptr) : dpuf::launch_gemm_exact(L, J, M);
   }
   if (e != cudaSuccess) {
     dpuf::set_error(std::string("dpuf_cuda_matmul_noalloc: launch: ") + cudaGetErrorString(e));

@@ -20,6 +20,7 @@ struct W12Handle {
   int8_t* q8 = nullptr;
   float* xs = nullptr;
   int32_t* xm = nullptr;
+  GemvSplit split{};  // GEMV scratch (units shared by CTAs)
 };
 
 constexpr int kOpChunk = kMaxBatch;  // tokens per launch of the standalone matmul
@@ -40,6 +41,10 @@ bool upload(W12Handle* h, int rows, int cols, int n_tiles, const uint8_t* base, 
   uint64_t lo = toff[0], hi = 0;
   const int n_blk = cols / 32;
   for (int t = 0; t < n_tiles; t++) {
+    if (toff[t] % 16 != 0) {
+      set_error("tile offsets must be multiples of 16 bytes");
+      return false;
+    }
     const uint8_t* tp = base + toff[t];
     const int n_r = tp[4] | (tp[5] << 8);
     lo = std::min<uint64_t>(lo, toff[t]);
@@ -71,6 +76,11 @@ bool alloc_act(W12Handle* h) {
   if ((e = cudaMalloc(&h->q8, kOpChunk * cols)) != cudaSuccess) return fail("cudaMalloc", e);
   if ((e = cudaMalloc(&h->xs, kOpChunk * (cols / 32) * 4)) != cudaSuccess) return fail("cudaMalloc", e);
   if ((e = cudaMalloc(&h->xm, kOpChunk * (cols / 32) * 4)) != cudaSuccess) return fail("cudaMalloc", e);
+  if ((e = cudaMalloc(&h->split.pairs, gemv_split_pairs_bytes((int)cols))) != cudaSuccess ||
+      (e = cudaMalloc(&h->split.acc, (size_t)kGemvMaxCtas * kTileRows * sizeof(float))) != cudaSuccess ||
+      (e = cudaMalloc(&h->split.count, (size_t)kGemvMaxCtas * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMemset(h->split.count, 0, (size_t)kGemvMaxCtas * sizeof(unsigned))) != cudaSuccess)
+    return fail("cudaMalloc", e);
   return true;
 }
 
@@ -80,6 +90,9 @@ void free_handle(W12Handle* h) {
   cudaFree(h->q8);
   cudaFree(h->xs);
   cudaFree(h->xm);
+  cudaFree(h->split.pairs);
+  cudaFree(h->split.acc);
+  cudaFree(h->split.count);
   delete h;
 }
 
@@ -95,7 +108,7 @@ int32_t matmul_dev(W12Handle* h, int M, const float* x, float* y, cudaStream_t s
     J.n = 1;
     J.j[0] = {h->w, a, y + (size_t)m0 * h->w.rows, h->w.rows, 0, h->w.n_tiles};
     J.tile_prefix[1] = h->w.n_tiles;
-    e = mc == 1 ? launch_gemv(L, J, nullptr) : launch_gemm_exact(L, J, mc);
+    e = mc == 1 ? launch_gemv(L, J, nullptr, &h->split) : launch_gemm_exact(L, J, mc);
     if (e != cudaSuccess) return fail("matmul", e), -4;
   }
   return 0;
@@ -150,7 +163,7 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, in
     J.n = 1;
     J.j[0] = {h->w, a, y_dev, h->w.rows, 0, h->w.n_tiles};
     J.tile_prefix[1] = h->w.n_tiles;
-    return M == 1 ? dpuf::launch_gemv(L, J, nullptr) : dpuf::launch_gemm_exact(L, J, M);
+    return M == 1 ? dpuf::launch_gemv(L, J, nullptr, &h->split) : dpuf::launch_gemm_exact(L, J, M);
   };
   for (int i = 0; i < 2 * n_handles; i++)
     if (launch(i) != cudaSuccess) return -4;

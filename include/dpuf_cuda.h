@@ -62,7 +62,8 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, in
  * device synchronisation.  No counterpart in the reference (its matmul is CPU-only).
  * Everything is a DEVICE pointer the caller owns: x[M][cols] in, y[M][rows] out, the weight as
  * its container tiles, tile offsets relative to tiles_dev (the reference's tile_offsets) and
- * sign bits.  Allocates nothing: the quantised activation lives in a fixed device array of
+ * sign bits (tiles_dev 16-byte aligned, tile offsets multiples of 16 as every packed container
+ * has them).  Allocates nothing: the quantised activation lives in a fixed device array of
  * 2^20 values (1.25 MiB, held by every GPU that loads the library until exit).
  * Returns 0; -1 bad arguments; -2 M * cols > 2^20 (rejected, see dpuf_cuda_last_error);
  * -4 CUDA error.  Enqueues on `stream` without synchronising.  The first call on a device sets
