@@ -47,7 +47,7 @@ struct GemvSplit {
   float* acc;
   unsigned* count;
 };
-constexpr int kGemvMaxCtas = 512;
+constexpr int kGemvMaxCtas = 600;
 size_t gemv_split_pairs_bytes(int max_cols);
 cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split);
 // M > 1: exact integer-dot GEMM on CUDA cores (reference order per (token,row)).

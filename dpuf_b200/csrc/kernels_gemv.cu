@@ -6,30 +6,30 @@
 //
 // Work list.  The weight is a list of units (16-row container tiles, possibly from up to three
 // matrices with the same K); each unit is n_st stages of KB = 32 blocks (1024 columns).  The
-// units are dealt to a persistent grid (up to three CTAs per SM) in contiguous ranges; the
+// units are dealt to a persistent grid (up to four CTAs per SM) in contiguous ranges; the
 // grid is the smallest one that reaches the minimal number of units per CTA, so the ranges
 // are as even as whole units allow.  Only a GEMV with fewer units than SMs splits units.
 // Streaming.  A CTA copies its items into an NS-stage shared-memory ring with 16-byte cp.async
-// (thread t copies piece t of each 8-row group), continuously across unit boundaries; the first
+// (thread t copies pieces t and t + 160 of each 8-row group), continuously across unit boundaries; the first
 // NS-1 stages are requested before griddepcontrol.wait, so with programmatic dependent launch
 // the stream starts while the previous kernel is still finishing.
-// Compute, as a three-step pipeline over the stages of a CTA (one __syncthreads per stage):
-//   MMA warps (4)   stage i: the integer block dots with warp-level int8 MMA (m16n8k32, exact
-//                   int32).  A = the activation block (all 16 A rows equal), B = 8 weight rows'
-//                   nibbles (0..15) of one block; lane (g, t) supplies weight row g, chunk t:
-//                   its low nibbles as k = 4t..4t+3 and its high nibbles as k = 16+4t..16+4t+3,
-//                   with A permuted the same way, so B needs one load and two masks.  The dots
-//                   sum(u * q) of rows 2t, 2t+1 go to a shared array D.
-//   pair warps (4)  stage i-1: p = float(dot - xm), s = ws * xs (both 0 for a skipped block,
-//                   which leaves the chain unchanged bit for bit) into a pair array.
-//   chain warp (1)  stage i-2: lane = row, acc = fma(p, s, acc) over the blocks in order.
+// Compute, as a two-step pipeline over the stages of a CTA (one __syncthreads per stage):
+//   MMA warps (4)  stage i, 8 blocks each: the integer block dots with warp-level int8 MMA
+//                  (m16n8k32, exact int32).  A = the activation block (all 16 A rows equal),
+//                  B = 8 weight rows' nibbles (0..15) of one block; lane (g, t) supplies weight
+//                  row g, chunk t: its low nibbles as k = 4t..4t+3 and its high nibbles as
+//                  k = 16+4t..16+4t+3, with A permuted the same way, so B needs one load and two
+//                  masks.  Lane (g, t) keeps rows 2t, 2t+1 of the warp's g-th block and writes
+//                  the pairs p = float(dot - xm), s = ws * xs (both 0 for a skipped block, which
+//                  leaves the chain unchanged bit for bit).
+//   chain warp (1) stage i-1: lane = row, acc = fma(p, s, acc) over the blocks in order.
 // Units split between CTAs.  The in-order chain is kept exact: the part holding stage 0 (head)
 // stores its accumulator after its last stage, every later part stores its pairs, and the last
 // part to finish (an atomic arrival count; nobody waits) continues the chain from the head's
 // accumulator through the stored pairs in block order and writes the rows.  Without scratch
 // (split == nullptr) units are never split.
-// Bank layout.  Within a stage the nibbles of group g start at g * (KB*128 + 32) bytes and the
-// odd-block lanes take the four chunks in rotated order, so the 32 lanes of a load hit 32 banks.
+// Bank layout.  Within a stage the nibbles of group g start at g * (KB*128 + 32) bytes; the B
+// load of one MMA (lane (g, t) reads word 8t + g of a block) covers 32 consecutive words.
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -40,22 +40,21 @@ namespace {
 
 constexpr int kKB = 32;  // blocks (of 32 columns) per stage
 constexpr int kMmaWarps = 4;
-constexpr int kPairWarps = 4;
-constexpr int kChainWarp = kMmaWarps + kPairWarps;
-constexpr int kThreads = (kChainWarp + 1) * 32;  // 288
+constexpr int kChainWarp = kMmaWarps;
+constexpr int kThreads = (kChainWarp + 1) * 32;  // 160
 constexpr int kRT = 16;                         // rows per unit (one container tile)
 constexpr int kNG = 2;                          // 8-row groups per unit
 constexpr int kQG = kKB * 128 + 32;             // nibble bytes per group per stage (+ bank pad)
 constexpr int kSG = kKB * 16 + 32;              // scale bytes per group per stage (+ bank pad)
 constexpr int kStage = kNG * (kQG + kSG);       // 9344
-constexpr int kNS = 5;                          // ring depth (three CTAs per SM)
-constexpr int kPF = kNS - 2;                     // stages in flight ahead of the MMA warps
-constexpr int kPsBytes = 2 * kKB * kRT * 8;     // double-buffered (p, s) pairs
-constexpr int kDBytes = 2 * kKB * kRT * 4;      // double-buffered integer dots D[block][row]
+constexpr int kNS = 4;                          // ring depth (four CTAs per SM)
+constexpr int kPF = kNS - 1;                     // stages in flight ahead of the MMA warps
+constexpr int kPsStride = 24;                   // pairs per block row (16 used; conflict-free stores)
+constexpr int kPsBytes = 2 * kKB * kPsStride * 8;  // double-buffered (p, s) pairs
 constexpr int kMaxUnitsPerCta = 96;
 constexpr int kCopyThreads = kKB * 8 + kKB;     // 288: nibble pieces then scale pieces of a group
 static_assert(kStage % 128 == 0, "stage alignment");
-static_assert(kThreads == kCopyThreads, "every thread copies one piece per group");
+static_assert(2 * kThreads >= kCopyThreads, "every thread copies at most two pieces per group");
 
 DPUF_DEV void cp_async16(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -99,14 +98,13 @@ DPUF_DEV int owner_of(const GemvArgs& A, long long i) {
   return c;
 }
 
-__global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, const int* skip_flag) {
+__global__ void __launch_bounds__(kThreads, 4) gemv_stream_kernel(GemvArgs A, const int* skip_flag) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ const uint8_t* unit_base[kMaxUnitsPerCta];  // tile start of each unit of this CTA
   __shared__ int unit_rows[kMaxUnitsPerCta];
   unsigned char* ring = smem;
   float2* ps = (float2*)(smem + kNS * kStage);
-  int* dd = (int*)(smem + kNS * kStage + kPsBytes);
-  int8_t* xq_all = (int8_t*)(smem + kNS * kStage + kPsBytes + kDBytes);
+  int8_t* xq_all = (int8_t*)(smem + kNS * kStage + kPsBytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
@@ -139,25 +137,23 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, co
   }
   __syncthreads();
 
-  // copy assignment: thread tid < 256 moves nibble piece tid (block tid/8) of both groups,
-  // threads 256..287 move scale piece tid-256 (the 8 scales of one block) of both groups
-  const bool copier = tid < kCopyThreads;
-  const bool q_piece = tid < kKB * 8;
-  const int piece = q_piece ? tid : tid - kKB * 8;
-  const int piece_block = q_piece ? (piece >> 3) : piece;
-  const int src_off = q_piece ? n_blk * 16 + piece * 16 : piece * 16;
-  const int dst_off = q_piece ? piece * 16 : kNG * kQG + piece * 16;
-  const int dst_gstride = q_piece ? kQG : kSG;
-  const int stage_stride = q_piece ? kKB * 128 : kKB * 16;
+  // copy assignment: per group and item there are 288 16-byte pieces, 256 of nibbles (piece p
+  // holds block p/8) and 32 of scales (one block each); thread t moves pieces t and t + 160
   int ik = 0, is = s_first, islot = 0;  // issue cursor: unit, stage, ring slot
+  auto copy_piece = [&](int pc, const uint8_t* tb, unsigned char* stage) {
+    const bool q = pc < kKB * 8;
+    const int pi = q ? pc : pc - kKB * 8;
+    if (is * kKB + (q ? (pi >> 3) : pi) >= n_blk) return;  // partial last stage
+    const int src = q ? n_blk * 16 + is * (kKB * 128) + pi * 16 : is * (kKB * 16) + pi * 16;
+    unsigned char* dst = stage + (q ? pi * 16 : kNG * kQG + pi * 16);
+    cp_async16(dst, tb + src);
+    if (unit_rows[ik] > 8) cp_async16(dst + (q ? kQG : kSG), tb + n_blk * 144 + src);
+  };
   auto issue_next = [&]() {
-    if (copier && is * kKB + piece_block < n_blk) {  // (partial last stage)
-      const uint8_t* tb = unit_base[ik] + 16;
-      unsigned char* dst = ring + islot * kStage + dst_off;
-      const int off = src_off + is * stage_stride;
-      cp_async16(dst, tb + off);
-      if (unit_rows[ik] > 8) cp_async16(dst + dst_gstride, tb + n_blk * 144 + off);
-    }
+    const uint8_t* tb = unit_base[ik] + 16;
+    unsigned char* stage = ring + islot * kStage;
+    copy_piece(tid, tb, stage);
+    if (tid + kThreads < kCopyThreads) copy_piece(tid + kThreads, tb, stage);
     if (++is == n_st) { is = 0; ik++; }
     if (++islot == kNS) islot = 0;
   };
@@ -198,8 +194,7 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, co
 
   // per-role cursors over this CTA's items: unit k, stage s, ring slot
   int mk = 0, ms = s_first, mslot = 0;  // MMA warps: item ii
-  int pk = 0, pss = s_first, pslot = 0; // pair warps: item ii - 1
-  int ck = 0, cs = s_first;             // chain warp: item ii - 2
+  int ck = 0, cs = s_first;             // chain warp: item ii - 1
   bool c_head = true, c_split = false;
   int c_slot = 0;
   float acc = 0.0f;
@@ -212,94 +207,89 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, co
   };
   if (warp == kChainWarp) chain_unit_begin();
 
-  for (int ii = 0; ii <= n_items + 1; ii++) {
+  for (int ii = 0; ii <= n_items; ii++) {
     cp_async_wait<kPF - 1>();
     __syncthreads();  // item ii landed; every role finished iteration ii-1
-    if (ii + kPF < n_items) issue_next();  // refills the slot of item ii-2 (no longer read)
+    if (ii + kPF < n_items) issue_next();  // refills the slot of item ii-1 (no longer read)
     cp_async_commit();
     if (warp < kMmaWarps) {
-      // ---- integer dots of item ii: blocks 8w..8w+7, both 8-row groups
+      // ---- item ii, blocks 8w..8w+7: integer dots by MMA for both 8-row groups; lane (g, t)
+      // keeps block 8w+g, rows 2t and 2t+1 of each group, and turns them into (p, s) pairs
       if (ii < n_items) {
         const int b0 = ms * kKB, kb = min(kKB, n_blk - b0);
         const int8_t* xq = xq_all + unit_xoff[mk];
+        const float* xs = (const float*)(xq + cols);
+        const int* xm = (const int*)(xs + n_blk);
         const unsigned char* st = ring + mslot * kStage;
-        int* dout = dd + (ii & 1) * kKB * kRT;
-        const int gq = lane >> 2, t = lane & 3;
+        const int g = lane >> 2, t = lane & 3;
+        constexpr int per = kKB / kMmaWarps;  // 8 blocks per warp
+        int keep[kNG][2];
 #pragma unroll 4
-        for (int q = 0; q < kKB / kMmaWarps; q++) {
-          const int bb = warp * (kKB / kMmaWarps) + q;
-          if (bb < kb) {
-            const int2 xw = *(const int2*)(xq + (b0 + bb) * 32 + t * 8);  // x words 2t, 2t+1
+        for (int j = 0; j < per; j++) {
+          const int bb = warp * per + j;
+          if (bb >= kb) break;  // partial last stage (warp-uniform): no activation bytes there
+          const int2 xw = *(const int2*)(xq + (b0 + bb) * 32 + t * 8);  // x words 2t, 2t+1
 #pragma unroll
-            for (int grp = 0; grp < kNG; grp++) {
-              const uint32_t w = *(const uint32_t*)(st + grp * kQG + bb * 128 + t * 32 + gq * 4);
-              int d0, d1, d2, d3;
-              mma_s8_16832(d0, d1, d2, d3, xw.x, xw.x, xw.y, xw.y, (int)(w & 0x0F0F0F0Fu),
-                           (int)((w >> 4) & 0x0F0F0F0Fu));
-              if (gq == 0) *(int2*)(dout + bb * kRT + grp * 8 + 2 * t) = make_int2(d0, d1);
+          for (int grp = 0; grp < kNG; grp++) {
+            const uint32_t w = *(const uint32_t*)(st + grp * kQG + bb * 128 + t * 32 + g * 4);
+            int d0, d1, d2, d3;
+            mma_s8_16832(d0, d1, d2, d3, xw.x, xw.x, xw.y, xw.y, (int)(w & 0x0F0F0F0Fu),
+                         (int)((w >> 4) & 0x0F0F0F0Fu));
+            if (g == j) {
+              keep[grp][0] = d0;
+              keep[grp][1] = d1;
             }
+          }
+        }
+        const int bb = warp * per + g;
+        if (bb < kb) {
+          const int b = b0 + bb;
+          const float bsc = xs[b];
+          const int xmb = xm[b];
+          float2* out = ps + (ii & 1) * kKB * kPsStride + bb * kPsStride + 2 * t;
+#pragma unroll
+          for (int grp = 0; grp < kNG; grp++) {
+            float4 pr = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (bsc > 0.0f) {
+              const uint32_t ws2 = *(const uint32_t*)(st + kNG * kQG + grp * kSG + bb * 16 + t * 4);
+              pr.x = (float)(keep[grp][0] - xmb);
+              pr.y = __fmul_rn(f16bits_to_f32((uint16_t)(ws2 & 0xFFFFu)), bsc);
+              pr.z = (float)(keep[grp][1] - xmb);
+              pr.w = __fmul_rn(f16bits_to_f32((uint16_t)(ws2 >> 16)), bsc);
+            }
+            *(float4*)(out + grp * 8) = pr;
           }
         }
         if (++ms == n_st) { ms = 0; mk++; }
         if (++mslot == kNS) mslot = 0;
       }
-    } else if (warp < kChainWarp) {
-      // ---- pairs of item ii-1: lane = (row, block parity), blocks 8pw + sub + 2i
-      if (ii >= 1 && ii <= n_items) {
-        const int b0 = pss * kKB, kb = min(kKB, n_blk - b0);
-        const int8_t* xq = xq_all + unit_xoff[pk];
-        const float* xs = (const float*)(xq + cols);
-        const int* xm = (const int*)(xs + n_blk);
-        const unsigned char* st = ring + pslot * kStage;
-        const int* din = dd + ((ii - 1) & 1) * kKB * kRT;
-        float2* pout = ps + ((ii - 1) & 1) * kKB * kRT;
-        const int r = lane & 15, sub = lane >> 4, pw = warp - kMmaWarps;
-        constexpr int per = kKB / kPairWarps;
-#pragma unroll
-        for (int i = 0; i < per / 2; i++) {
-          const int bb = pw * per + sub + 2 * i;
-          if (bb < kb) {
-            const int b = b0 + bb;
-            const float bsc = xs[b];
-            float p = 0.0f, sc = 0.0f;
-            if (bsc > 0.0f) {
-              p = (float)(din[bb * kRT + r] - xm[b]);
-              sc = __fmul_rn(
-                  f16bits_to_f32(*(const uint16_t*)(st + kNG * kQG + (r >> 3) * kSG + bb * 16 + (r & 7) * 2)), bsc);
-            }
-            pout[bb * kRT + r] = make_float2(p, sc);
-          }
-        }
-        if (++pss == n_st) { pss = 0; pk++; }
-        if (++pslot == kNS) pslot = 0;
-      }
-    } else if (ii >= 2) {
-      // ---- chain warp: item ii-2 (unit ck, stage cs)
+    } else if (ii >= 1) {
+      // ---- chain warp: item ii-1 (unit ck, stage cs)
       const int kb = min(kKB, n_blk - cs * kKB);
-      const float2* in_ps = ps + ((ii - 2) & 1) * kKB * kRT;
+      const float2* in_ps = ps + ((ii - 1) & 1) * kKB * kPsStride;
       if (c_head) {
         if (lane < kRT) {
           int b = 0;
           for (; b + 3 < kb; b += 4) {
-            const float2 a0 = in_ps[(b + 0) * kRT + lane], a1 = in_ps[(b + 1) * kRT + lane];
-            const float2 a2 = in_ps[(b + 2) * kRT + lane], a3 = in_ps[(b + 3) * kRT + lane];
+            const float2 a0 = in_ps[(b + 0) * kPsStride + lane], a1 = in_ps[(b + 1) * kPsStride + lane];
+            const float2 a2 = in_ps[(b + 2) * kPsStride + lane], a3 = in_ps[(b + 3) * kPsStride + lane];
             acc = __fmaf_rn(a0.x, a0.y, acc);
             acc = __fmaf_rn(a1.x, a1.y, acc);
             acc = __fmaf_rn(a2.x, a2.y, acc);
             acc = __fmaf_rn(a3.x, a3.y, acc);
           }
           for (; b < kb; b++) {
-            const float2 a = in_ps[b * kRT + lane];
+            const float2 a = in_ps[b * kPsStride + lane];
             acc = __fmaf_rn(a.x, a.y, acc);
           }
         }
       } else {
         // later part of a split unit: hand the pairs over
         float2* dst = A.split.pairs + ((size_t)c_slot * n_blk + cs * kKB) * kRT;
-        for (int e = lane; e < kb * kRT; e += 32) dst[e] = in_ps[e];
+        for (int e = lane; e < kb * kRT; e += 32) dst[e] = in_ps[(e >> 4) * kPsStride + (e & 15)];
       }
       const bool unit_end = cs + 1 == n_st;
-      if (unit_end || ii == n_items + 1) {  // this CTA's part of the unit is done
+      if (unit_end || ii == n_items) {  // this CTA's part of the unit is done
         const int n_r = unit_rows[ck];
         float* out = unit_out[ck];
         if (!c_split) {
@@ -321,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, co
             // loaded with every request of a refill in flight before the in-order chain reads them
             float a = lane < kRT ? __ldcg(A.split.acc + c_slot * kRT + lane) : 0.0f;
             const float2* pr = A.split.pairs + (size_t)c_slot * n_blk * kRT;
-            float2* stage_buf = ps + ((ii - 2) & 1) * kKB * kRT;
+            float2* stage_buf = ps + ((ii - 1) & 1) * kKB * kPsStride;
             constexpr int kFB = kKB / 2;  // blocks per refill
             for (int b0 = head_end * kKB; b0 < n_blk; b0 += kFB) {
               const int nb = min(kFB, n_blk - b0);
@@ -348,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 3) gemv_stream_kernel(GemvArgs A, co
       if (unit_end) {
         cs = 0;
         ck++;
-        if (ii <= n_items) chain_unit_begin();
+        if (ii < n_items) chain_unit_begin();
       } else {
         cs++;
       }
@@ -416,7 +406,7 @@ cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_fl
   A.split = can_split ? *split : GemvSplit{nullptr, nullptr, nullptr};
   // Whole units: the smallest grid (up to three CTAs per SM) reaching the minimal number of
   // units per CTA.  Units are split between CTAs only when there are fewer units than SMs.
-  const int max_ctas = std::min(3 * sms, kGemvMaxCtas);
+  const int max_ctas = std::min(4 * sms, kGemvMaxCtas);
   long long grid;
   if (can_split && A.n_units < sms && A.n_st > 1) {
     grid = std::min<long long>(A.items, 2LL * sms);
@@ -427,7 +417,7 @@ cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_fl
     grid = (A.n_units + per - 1) / per;
   }
   if ((A.n_units + grid - 1) / grid + 2 > kMaxUnitsPerCta) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)kNS * kStage + kPsBytes + kDBytes + (size_t)A.n_x * (A.cols + A.n_blk * 8);
+  const size_t smem = (size_t)kNS * kStage + kPsBytes + (size_t)A.n_x * (A.cols + A.n_blk * 8);
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
   return launch_k(L, gemv_stream_kernel, dim3((unsigned)grid), dim3(kThreads), smem, A, skip_flag);
 }
