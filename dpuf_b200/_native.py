@@ -34,6 +34,7 @@ CUDA_SOURCES = [
     "kernels_layer.cu",
     "kernels_attn.cu",
     "kernels_lmhead.cu",
+    "kernels_decode.cu",
     "ops_abi.cu",
     "noalloc.cu",
 ]

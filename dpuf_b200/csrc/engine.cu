@@ -41,6 +41,7 @@ cudaError_t configure_kernels() {
   cudaError_t e;
   if ((e = configure_mode12_kernels()) != cudaSuccess) return e;
   if ((e = configure_layer_kernels()) != cudaSuccess) return e;
+  if ((e = configure_decode_kernel()) != cudaSuccess) return e;
   return configure_attn_kernels();
 }
 
@@ -135,6 +136,15 @@ struct Engine {
   std::map<StepKey, cudaGraphExec_t> graphs;
   // last step
   int last_rows = 0, last_zone_used = 0;
+
+  // persistent batch-1 decode (kernels_decode.cu)
+  bool dec_ok = false, use_persistent = true;
+  std::string dec_why;     // why the persistent kernel is not used
+  DecodeArgs dec{};        // everything but the per-call fields
+  DecLayer* d_dec_layers = nullptr;
+  float *dec_o = nullptr, *dec_s = nullptr, *dec_d = nullptr;
+  float2* dec_part = nullptr;
+  unsigned* dec_bar = nullptr;  // [0] grid barrier counter, [1] error word
 };
 
 // ------------------------------------------------------------------ helpers
@@ -281,6 +291,8 @@ void destroy_engine(Engine* e) {
   cudaFree(e->d_ids); cudaFree(e->d_hist); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
   cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part);
   cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
+  cudaFree(e->d_dec_layers); cudaFree(e->dec_o); cudaFree(e->dec_s); cudaFree(e->dec_d);
+  cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -436,6 +448,141 @@ void drop_graphs(Engine* e) {
   e->graphs.clear();
 }
 
+int env_int(const char* name, int def) {
+  const char* s = getenv(name);
+  return s ? atoi(s) : def;
+}
+
+// ------------------------------------------------------------------ persistent decode
+// Tile stride of a matrix whose tiles are equally spaced (what the reference's packer writes);
+// false otherwise.  *first = byte offset of tile 0 from the start of the uploaded span.
+bool uniform_tiles(const DpufWeightDesc& w, long long* stride, long long* first) {
+  uint64_t base;
+  tile_span(w, &base);
+  *first = (long long)(w.tile_offsets[0] - base);
+  *stride = w.n_tiles > 1 ? (long long)(w.tile_offsets[1] - w.tile_offsets[0]) : 0;
+  if (w.n_tiles > 1 && *stride <= 0) return false;
+  for (int t = 0; t < w.n_tiles; t++)
+    if ((long long)(w.tile_offsets[t] - w.tile_offsets[0]) != (long long)t * *stride) return false;
+  return true;
+}
+
+// Decides whether batch-1 steps run as the persistent kernel and prepares its arguments.
+// Falls back (dec_ok = false, reason in dec_why) when a matrix's tiles are not equally
+// spaced, when co-inputs use different sign tables, or when the device cannot hold one CTA
+// per SM with a ring of at least four stages.
+void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* tok, const DpufWeightDesc* lm) {
+  auto no = [&](const std::string& why) { e->dec_ok = false; e->dec_why = why; };
+  int coop = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device) != cudaSuccess || !coop)
+    return no("device without cooperative launch");
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device) != cudaSuccess || sms <= 0)
+    return no("SM count");
+  std::vector<DecLayer> tab(e->L);
+  for (int l = 0; l < e->L; l++) {
+    const DpufLayerWeights& w = lw[l];
+    const LayerDev& d = e->layers[l];
+    const DpufWeightDesc* ws[7] = {&w.w_q, &w.w_k, &w.w_v, &w.w_o, &w.w_gate, &w.w_up, &w.w_down};
+    const W12* dw[7] = {&d.q, &d.k, &d.v, &d.o, &d.gate, &d.up, &d.down};
+    for (int i = 0; i < 7; i++) {
+      long long first;
+      if (!uniform_tiles(*ws[i], &tab[l].stride[i], &first)) return no("tiles not equally spaced");
+      tab[l].tiles[i] = dw[i]->tiles + first;
+    }
+    if (d.q.signs != d.k.signs || d.q.signs != d.v.signs || d.gate.signs != d.up.signs)
+      return no("co-inputs with different sign tables");
+    tab[l].signs[0] = d.q.signs;
+    tab[l].signs[1] = d.o.signs;
+    tab[l].signs[2] = d.gate.signs;
+    tab[l].signs[3] = d.down.signs;
+    tab[l].attn_norm = d.attn_norm;
+    tab[l].ffn_norm = d.ffn_norm;
+    tab[l].q_norm = e->cfg.has_qk_norm ? d.q_norm : nullptr;
+    tab[l].k_norm = e->cfg.has_qk_norm ? d.k_norm : nullptr;
+  }
+  DecodeArgs& A = e->dec;
+  A = DecodeArgs{};
+  long long first;
+  if (!uniform_tiles(*lm, &A.lm_stride, &first)) return no("tiles not equally spaced");
+  A.lm_tiles = e->lm.tiles + first;
+  if (!uniform_tiles(*tok, &A.tok_stride, &first)) return no("tiles not equally spaced");
+  A.tok_tiles = e->tok.tiles + first;
+  A.lm_signs = e->lm.signs;
+  A.tok_signs = e->tok.signs;
+  A.L = e->L; A.H = e->H; A.I = e->I; A.nq = e->nq; A.nkv = e->nkv; A.hd = e->hd; A.qd = e->qd; A.kvd = e->kvd;
+  A.V = e->V; A.S = e->S; A.kmax = std::max(std::max(e->H, e->I), e->qd); A.tok_rows = e->tok.rows;
+  A.out_norm = e->out_norm;
+  A.eps = e->cfg.rms_eps;
+  A.deadzone = e->deadzone;
+  A.nt_ref = e->nt_ref;
+  A.cos_tab = e->cos_tab;
+  A.sin_tab = e->sin_tab;
+  A.et = e->et;
+  A.q = e->q; A.k = e->k; A.v = e->v; A.att = e->att; A.logits = e->logits; A.hist = e->d_hist;
+  A.grid = sms;
+  A.stage_cap = decode_stage_cap(A);
+  size_t limit = 0;
+  if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");
+  A.n_ring = decode_ring_slots(A, limit);
+  if (A.n_ring < 4) return no("shared memory: ring shorter than four stages");
+  int per_sm = 0;
+  if (decode_blocks_per_sm(A, &per_sm) != cudaSuccess || per_sm < 1) return no("occupancy");
+  if (cudaMalloc(&e->d_dec_layers, std::max<size_t>(1, tab.size()) * sizeof(DecLayer)) ||
+      (!tab.empty() &&
+       cudaMemcpy(e->d_dec_layers, tab.data(), tab.size() * sizeof(DecLayer), cudaMemcpyHostToDevice)) ||
+      cudaMalloc(&e->dec_o, (size_t)e->H * 4) || cudaMalloc(&e->dec_s, (size_t)e->I * 4) ||
+      cudaMalloc(&e->dec_d, (size_t)e->H * 4) || cudaMalloc(&e->dec_part, (size_t)sms * sizeof(float2)) ||
+      cudaMalloc(&e->dec_bar, 16))
+    return no("allocation");
+  A.layers = e->d_dec_layers;
+  A.o_out = e->dec_o;
+  A.s_out = e->dec_s;
+  A.d_out = e->dec_d;
+  A.part = e->dec_part;
+  A.bar = e->dec_bar;
+  A.err = (int*)(e->dec_bar + 1);
+  if (env_int("DPUF_CUDA_TRACE_DECODE", 0)) {
+    A.trace_per_cta = decode_trace_events(e->L);
+    if (cudaMalloc(&A.trace, (size_t)sms * A.trace_per_cta * 8) ||
+        cudaMemset(A.trace, 0, (size_t)sms * A.trace_per_cta * 8))
+      return no("allocation");
+  }
+  e->dec_ok = true;
+  e->dec_why.clear();
+}
+
+bool persistent_step(const Engine* e, const StepParams& P) {
+  return P.M == 1 && P.za == 0 && e->dec_ok && e->use_persistent;
+}
+
+// Launches the persistent kernel for n_steps batch-1 steps from (first_id, pos0) and queues the
+// read of its error word into the pinned staging (checked by the caller after synchronising).
+cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool write_logits, int keep) {
+  DecodeArgs A = e->dec;
+  A.first_id = first_id;
+  A.pos0 = pos0;
+  A.n_steps = n_steps;
+  A.write_logits = write_logits ? 1 : 0;
+  const int down_tiles = e->L > 0 ? e->layers[0].down.n_tiles : 0;
+  A.keep_down = (keep > 0 && keep < down_tiles) ? keep : down_tiles;
+  A.kv_k = e->slots[e->active].k;
+  A.kv_v = e->slots[e->active].v;
+  e->stage->pad[0] = 0;
+  CK(cudaMemsetAsync(e->dec_bar, 0, 16, e->stream));
+  CK(launch_decode(e->stream, A));
+  CK(cudaMemcpyAsync(&e->stage->pad[0], A.err, 4, cudaMemcpyDeviceToHost, e->stream));
+  return cudaSuccess;
+}
+
+// After the stream is synchronised: the persistent kernel's error word.
+int32_t decode_status(Engine* e) {
+  const int code = e->stage->pad[0];
+  if (code == 0) return 0;
+  set_error(code == 1 ? "persistent decode: a pipeline wait timed out"
+                      : "persistent decode: a grid barrier wait timed out");
+  return -6;
+}
+
 // Environment knobs read per call, as the reference does (dpuf_engine.c:2022-2027, 2091-2118).
 StepParams step_params(const Engine* e, int n, int only_last) {
   StepParams P{};
@@ -462,10 +609,6 @@ StepParams step_params(const Engine* e, int n, int only_last) {
   return P;
 }
 
-int env_int(const char* name, int def) {
-  const char* s = getenv(name);
-  return s ? atoi(s) : def;
-}
 
 // Validation and environment knobs of dpuf_engine_forward_batch_ex (dpuf_engine.c:1639-1641,
 // 2022-2027, 2091-2118), then one step.
@@ -493,7 +636,8 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   const int lm_M = P.only_last == 1 ? 1 : n;
   memcpy(e->stage->ids, ids, (size_t)n * 4);
   e->stage->pos0 = pos0;
-  cudaError_t err = run_step(e, P);
+  const bool persistent = persistent_step(e, P);
+  cudaError_t err = persistent ? run_decode(e, ids[0], pos0, 1, P.only_last != 2, P.keep) : run_step(e, P);
   if (err != cudaSuccess) return -4;
   e->last_zone_used = P.za > 0;
   e->last_rows = P.only_last == 2 ? 0 : lm_M;
@@ -515,7 +659,7 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
     set_error(cudaGetErrorString(le));
     return -4;
   }
-  return 0;
+  return persistent ? decode_status(e) : 0;
 }
 
 Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers, const DpufWeightDesc* tok,
@@ -650,6 +794,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   cudaMemset(e->d_flag, 0, 16);
   cudaMemset(e->d_counter, 0, 64);
   if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
+  e->use_persistent = env_int("DPUF_CUDA_PERSISTENT", 1) != 0;
+  plan_decode(e, layers, tok, lm);
   return e;
 }
 
@@ -810,9 +956,18 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
       cudaMemcpyAsync(e->d_hist_step, &zero, 4, cudaMemcpyHostToDevice, e->stream) ||
       cudaStreamSynchronize(e->stream) || cudaEventCreate(&ev0) || cudaEventCreate(&ev1))
     return -4;
+  const bool persistent = dpuf::persistent_step(e, P);
   cudaEventRecord(ev0, e->stream);
-  for (int i = 0; i < n_steps; i++)
-    if (dpuf::run_step(e, P) != cudaSuccess) { cudaEventDestroy(ev0); cudaEventDestroy(ev1); return -4; }
+  if (persistent) {
+    if (dpuf::run_decode(e, first_id, pos0, n_steps, true, P.keep) != cudaSuccess) {
+      cudaEventDestroy(ev0);
+      cudaEventDestroy(ev1);
+      return -4;
+    }
+  } else {
+    for (int i = 0; i < n_steps; i++)
+      if (dpuf::run_step(e, P) != cudaSuccess) { cudaEventDestroy(ev0); cudaEventDestroy(ev1); return -4; }
+  }
   cudaEventRecord(ev1, e->stream);
   int32_t rc = 0;
   if (cudaMemcpyAsync(ids_out, e->d_hist, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->stream) ||
@@ -820,10 +975,12 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
     rc = -4;
   float ms = 0.0f;
   if (rc == 0 && cudaEventElapsedTime(&ms, ev0, ev1) != cudaSuccess) rc = -4;
+  if (rc == 0 && persistent) rc = dpuf::decode_status(e);
   if (device_ms) *device_ms = ms;
   cudaEventDestroy(ev0);
   cudaEventDestroy(ev1);
   e->last_rows = 1;
+  e->last_zone_used = 0;
   return rc;
 }
 
@@ -840,7 +997,28 @@ DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t
   if (!e || !name) return -1;
   if (!strcmp(name, "pdl")) { e->use_pdl = value != 0; dpuf::drop_graphs(e); return 0; }
   if (!strcmp(name, "graphs")) { e->use_graphs = value != 0; dpuf::drop_graphs(e); return 0; }
+  if (!strcmp(name, "persistent")) { e->use_persistent = value != 0; return 0; }
   return -1;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_t* per_cta, uint64_t* out,
+                                           int64_t max_values) {
+  Engine* e = (Engine*)handle;
+  if (!e || !e->dec.trace) return -1;
+  if (n_ctas) *n_ctas = e->dec.grid;
+  if (per_cta) *per_cta = e->dec.trace_per_cta;
+  const int64_t n = (int64_t)e->dec.grid * e->dec.trace_per_cta;
+  if (!out) return 0;
+  if (max_values < n) return -2;
+  cudaSetDevice(e->device);
+  return cudaMemcpy(out, e->dec.trace, (size_t)n * 8, cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -4;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why) {
+  Engine* e = (Engine*)handle;
+  if (!e) return -1;
+  if (why) *why = e->dec_ok ? "" : e->dec_why.c_str();
+  return e->dec_ok && e->use_persistent ? 1 : 0;
 }
 
 DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2) {

@@ -94,4 +94,56 @@ cudaError_t launch_argmax(const Launch& L, const float* logits, int V, float2* p
 cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, float2* part, unsigned* counter,
                                   int32_t* ids, int32_t* pos0, int32_t* hist, int32_t* step);
 
+// ---- kernels_decode.cu: batch-1 decode as one persistent cooperative kernel
+// Device pointers of one layer (weights in container layout with a uniform tile stride).
+struct DecLayer {
+  const uint8_t* tiles[7];   // tile 0 of q, k, v, o, gate, up, down
+  long long stride[7];       // bytes from one tile to the next
+  const uint8_t* signs[4];   // sign tables of the inputs of q/k/v, o, gate/up, down
+  const float* attn_norm;
+  const float* ffn_norm;
+  const float* q_norm;       // null without QK-norm
+  const float* k_norm;
+};
+static_assert(sizeof(DecLayer) % 16 == 0, "layer table rows are copied as int4");
+
+struct DecodeArgs {
+  const DecLayer* layers;  // [L], device
+  int L, H, I, nq, nkv, hd, qd, kvd, V, S, kmax, tok_rows;
+  const uint8_t* lm_tiles;
+  long long lm_stride;
+  const uint8_t* lm_signs;
+  const uint8_t* tok_tiles;
+  long long tok_stride;
+  const uint8_t* tok_signs;
+  const float* out_norm;
+  float eps, deadzone;
+  int nt_ref;     // the reference's thread count (SwiGLU vector/tail split)
+  int keep_down;  // down-projection tiles computed (rows beyond are zero)
+  const float* cos_tab;
+  const float* sin_tab;
+  float* kv_k;    // active slot, [L][n_kv][S][hd]
+  float* kv_v;
+  ExpfTable et;
+  float *q, *k, *v, *att, *o_out, *s_out, *d_out, *logits;
+  float2* part;   // [grid] argmax partials
+  unsigned* bar;  // grid barrier counter, zero at launch
+  int* err;       // 0 at launch; 1 = mbarrier wait timed out, 2 = grid barrier timed out
+  int32_t* hist;  // [n_steps] greedy ids
+  int first_id, pos0, n_steps, write_logits;
+  int grid, n_ring;
+  int stage_cap;      // columns per staged piece (decode_stage_cap)
+  unsigned long long* trace;  // optional per-CTA phase timestamps of the last step (null: off)
+  int trace_per_cta;
+};
+int decode_stage_cap(const DecodeArgs& A);
+int decode_trace_events(int L);
+size_t decode_smem_bytes(const DecodeArgs& A);
+int decode_ring_slots(const DecodeArgs& A, size_t smem_limit);
+cudaError_t configure_decode_kernel();
+cudaError_t decode_max_dyn_smem(size_t* bytes);
+cudaError_t decode_blocks_per_sm(const DecodeArgs& A, int* blocks);
+cudaError_t launch_decode(cudaStream_t stream, const DecodeArgs& A);
+
 }  // namespace dpuf
+

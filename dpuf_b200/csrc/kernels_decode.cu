@@ -1,0 +1,788 @@
+// kernels_decode.cu - batch-1 decode as one persistent cooperative kernel.
+//
+// One CTA per SM runs every step of a greedy decode (or one forward_token step): embedding,
+// all layers, final norm, LM head and argmax, with grid-wide barriers only where the
+// reference's step has a data dependency across rows (after each projection and after
+// attention).  The per-element arithmetic is the same as the per-step kernels' (layer_dev.cuh,
+// and the GEMV's exact block chain), so logits and ids are bit-identical to the reference's.
+//
+// Weight stream.  The weights never depend on activations, so a producer warp per CTA walks
+// the CTA's share of every projection of every layer and step in order, moving each stage
+// (the two 8-row groups' scales and nibbles of 32 blocks of one 16-row tile: 9216 bytes)
+// into a shared-memory ring with cp.async.bulk (TMA, no multicast) completed on an mbarrier.
+// It runs ahead across phase and grid barriers, bounded only by the ring, so HBM keeps
+// streaming while the consumers normalise, attend or wait at a barrier.
+//
+// Consumers (warps 0..8).  Per stage, eight MMA warps compute the exact integer block dots
+// with one m16n8k32 int8 MMA per 32-column block for all 16 rows (A = the tile's nibbles, rows
+// 0..7 from group 0 and 8..15 from group 1, low nibbles as k = 4t..4t+3 and high nibbles as
+// k = 16+4t..16+4t+3; B = the activation block with the same permutation in every column),
+// turn them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand
+// them to the chain warp through a 4-deep pair ring; the chain warp runs acc = fma(p, s, acc)
+// per row over the blocks in order (dpuf_avx2.c:2601-2640) and writes each 16-row unit's
+// outputs (with SwiGLU for gate/up pairs, and the running argmax for the LM head).
+// Between projections the consumers do the row-wide steps redundantly in every CTA (the
+// residual stream h lives in each CTA's shared memory): residual add, RMSNorm, activation
+// prep; attention runs on one CTA per (KV head, query-head pair).
+//
+// Work split.  Each projection's 16-row units are dealt in contiguous ranges, and the CTA that
+// receives the remainder units rotates from one projection to the next, so every CTA streams
+// about the same bytes per layer and the ring absorbs the one-unit imbalance of a projection.
+//
+// Every wait is bounded: an mbarrier or grid-barrier wait gives up after kWaitNs, sets the
+// error word and the CTA's abort flag.  After that every wait returns at once, but the
+// consumers keep their control flow (every loop runs its full trip count and reaches every
+// named barrier, with all addresses depending on shapes only), so no warp is left waiting at
+// a barrier; the producer stops issuing and waits, bounded, for the copies it issued.
+#include <algorithm>
+
+#include "kernels.cuh"
+#include "layer_dev.cuh"
+
+namespace dpuf {
+
+namespace {
+
+constexpr int kMmaWarps = 8;
+constexpr int kChainWarp = 8;
+constexpr int kProdWarp = 9;
+constexpr int kThreads = 320;
+constexpr int kConsumers = 288;     // warps 0..8
+constexpr int kSlotBytes = 9344;    // one stage: nibbles g0 | g1 (+32 pad) | scales g0 | g1
+constexpr int kNib1 = 4128, kSc0 = 8256, kSc1 = 8800;
+constexpr int kMaxRing = 24;
+constexpr int kNPs = 4;             // pair buffers between MMA warps and the chain warp
+constexpr int kPsRow = 20;          // float2 per block row (16 used): conflict-free stores
+constexpr int kPsBuf = 32 * kPsRow;
+constexpr int kBarConsumers = 1, kBarAttn = 2;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
+
+// ------------------------------------------------------------------ PTX helpers
+DPUF_DEV unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+DPUF_DEV void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+DPUF_DEV void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+DPUF_DEV void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+DPUF_DEV bool mbar_try(uint64_t* b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+DPUF_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+DPUF_DEV unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+DPUF_DEV unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+DPUF_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+DPUF_DEV void mma_s8_16832(int& d0, int& d1, int& d2, int& d3, int a0, int a1, int a2, int a3, int b0, int b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Shared state of a CTA that is not in the dynamic buffer.
+struct DecShared {
+  uint64_t full[kMaxRing], empty[kMaxRing], psf[kNPs], pse[kNPs];
+  AttnShared attn;
+  float lanes[8];
+  float inv;
+  int next_id;
+  volatile int abort;
+};
+
+// Bounded mbarrier wait by one thread: false (and the CTA abort flag and the error word set)
+// once kWaitNs pass, or when the CTA or another CTA has aborted.  The fast path is one
+// try_wait; the CTA flag is polled every 16 tries, the timer and the global error word every
+// 256.
+DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, int* err) {
+  if (mbar_try(b, parity)) return true;
+  unsigned long long t0 = 0;
+  for (int it = 1;; it++) {
+    if (mbar_try(b, parity)) return true;
+    if ((it & 15) == 0 && S.abort) return false;
+    if ((it & 255) == 0) {
+      if (*(volatile int*)err) {
+        S.abort = 1;
+        return false;
+      }
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitNs) {
+        S.abort = 1;
+        atomicCAS(err, 0, 1);
+        return false;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ work plan
+struct Unit {
+  const uint8_t* tile;
+  int n_r;     // rows in the tile
+  int row;     // first row of the tile in its matrix
+  float* out;  // output of row `row` (chain epilogue)
+};
+
+DPUF_DEV int kind_cols(const DecodeArgs& A, int kind) {
+  return kind == kO ? A.qd : (kind == kDown ? A.I : A.H);
+}
+DPUF_DEV int kind_units(const DecodeArgs& A, int kind) {
+  const int tq = (A.qd + 15) >> 4, tkv = (A.kvd + 15) >> 4, th = (A.H + 15) >> 4, ti = (A.I + 15) >> 4;
+  switch (kind) {
+    case kQKV: return tq + 2 * tkv;
+    case kO: return th;
+    case kGU: return ti;
+    case kDown: return A.keep_down;
+    default: return (A.V + 15) >> 4;
+  }
+}
+DPUF_DEV int kind_subs(int kind) { return kind == kGU ? 2 : 1; }
+
+DPUF_DEV Unit make_unit(const uint8_t* tiles, long long stride, int rows, int t, float* out) {
+  Unit u;
+  u.tile = tiles + (size_t)t * stride;
+  u.row = t * kTileRows;
+  u.n_r = min(kTileRows, rows - u.row);
+  u.out = out ? out + u.row : nullptr;
+  return u;
+}
+
+DPUF_DEV Unit unit_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, int sub) {
+  switch (kind) {
+    case kQKV: {
+      const int tq = (A.qd + 15) >> 4, tkv = (A.kvd + 15) >> 4;
+      if (u < tq) return make_unit(Ly.tiles[0], Ly.stride[0], A.qd, u, A.q);
+      if (u < tq + tkv) return make_unit(Ly.tiles[1], Ly.stride[1], A.kvd, u - tq, A.k);
+      return make_unit(Ly.tiles[2], Ly.stride[2], A.kvd, u - tq - tkv, A.v);
+    }
+    case kO: return make_unit(Ly.tiles[3], Ly.stride[3], A.H, u, A.o_out);
+    case kGU: return sub == 0 ? make_unit(Ly.tiles[4], Ly.stride[4], A.I, u, nullptr)
+                              : make_unit(Ly.tiles[5], Ly.stride[5], A.I, u, A.s_out);
+    case kDown: return make_unit(Ly.tiles[6], Ly.stride[6], A.H, u, A.d_out);
+    default: return make_unit(A.lm_tiles, A.lm_stride, A.V, u, A.logits);
+  }
+}
+
+// Contiguous unit range of CTA c in a projection of U units; the remainder units go to the
+// `U % G` CTAs starting at `rot`, which then advances by U % G.
+DPUF_DEV void take_range(int U, int& rot, int& u0, int& n) {
+  const int G = gridDim.x, c = blockIdx.x;
+  const int v = (c - rot + G) % G;
+  const int base = U / G, ext = U % G;
+  n = base + (v < ext ? 1 : 0);
+  u0 = v * base + min(v, ext);
+  rot = (rot + ext) % G;
+}
+
+// ------------------------------------------------------------------ producer
+struct Producer {
+  int slot = 0;
+  unsigned phase = 0;     // parity of the slot's current use
+  long long issued = 0;
+};
+
+DPUF_DEV bool produce_unit(const Unit& un, int n_blk, int n_st, unsigned char* ring, int n_ring, Producer& P,
+                           DecShared& S, int* err) {
+  const int groups = un.n_r > 8 ? 2 : 1;
+  for (int s = 0; s < n_st; s++) {
+    if (!wait_bar(&S.empty[P.slot], P.phase ^ 1u, S, err)) return false;
+    const int kb = min(32, n_blk - s * 32);
+    unsigned char* dst = ring + (size_t)P.slot * kSlotBytes;
+    mbar_expect_tx(&S.full[P.slot], (unsigned)(groups * kb * 144));
+    for (int g = 0; g < groups; g++) {
+      const uint8_t* gp = un.tile + 16 + (size_t)g * n_blk * 144;
+      bulk_g2s(dst + (g ? kNib1 : 0), gp + (size_t)n_blk * 16 + (size_t)s * 4096, (unsigned)kb * 128, &S.full[P.slot]);
+      bulk_g2s(dst + (g ? kSc1 : kSc0), gp + (size_t)s * 512, (unsigned)kb * 16, &S.full[P.slot]);
+    }
+    P.issued++;
+    if (++P.slot == n_ring) {
+      P.slot = 0;
+      P.phase ^= 1u;
+    }
+  }
+  return true;
+}
+
+DPUF_DEV bool produce_phase(const DecodeArgs& A, const DecLayer* layers, int l, int kind, int& rot,
+                            unsigned char* ring, int n_ring, Producer& P, DecShared& S) {
+  int u0, n;
+  take_range(kind_units(A, kind), rot, u0, n);
+  const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
+  const DecLayer& Ly = layers[kind == kLM ? 0 : l];
+  for (int u = u0; u < u0 + n; u++)
+    for (int sub = 0; sub < kind_subs(kind); sub++)
+      if (!produce_unit(unit_of(A, Ly, kind, u, sub), n_blk, n_st, ring, n_ring, P, S, A.err)) return false;
+  return true;
+}
+
+// ------------------------------------------------------------------ consumers
+struct Consumer {
+  int slot = 0;
+  unsigned phase = 0;  // ring parity
+  int pb = 0;
+  unsigned pphase = 0; // pair-buffer parity
+  int rot = 0;
+};
+
+DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
+
+// MMA warp w: blocks 4w..4w+3 of the stage; lane (g, t) keeps block 4w+t, rows g and g+8.
+DPUF_DEV void mma_stage(const unsigned char* st, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
+                        int warp, int lane, float2* buf) {
+  const int g = lane >> 2, t = lane & 3;
+  int k0 = 0, k8 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int bb = warp * 4 + j;
+    if (bb < kb) {  // warp-uniform
+      const int2 xw = *(const int2*)(xq + (b0 + bb) * 32 + t * 8);
+      const uint32_t w0 = *(const uint32_t*)(st + bb * 128 + t * 32 + g * 4);
+      const uint32_t w1 = *(const uint32_t*)(st + kNib1 + bb * 128 + t * 32 + g * 4);
+      int d0, d1, d2, d3;
+      mma_s8_16832(d0, d1, d2, d3, (int)(w0 & 0x0F0F0F0Fu), (int)(w1 & 0x0F0F0F0Fu), (int)((w0 >> 4) & 0x0F0F0F0Fu),
+                   (int)((w1 >> 4) & 0x0F0F0F0Fu), xw.x, xw.y);
+      if (t == j) {
+        k0 = d0;
+        k8 = d2;
+      }
+    }
+  }
+  const int bb = warp * 4 + t;
+  if (bb < kb) {
+    const int b = b0 + bb;
+    const float bsc = xs[b];
+    const int xmb = xm[b];
+    float2 r0 = make_float2(0.0f, 0.0f), r8 = r0;
+    if (bsc > 0.0f) {
+      const float ws0 = f16bits_to_f32(*(const uint16_t*)(st + kSc0 + bb * 16 + g * 2));
+      const float ws8 = f16bits_to_f32(*(const uint16_t*)(st + kSc1 + bb * 16 + g * 2));
+      r0 = make_float2((float)(k0 - xmb), __fmul_rn(ws0, bsc));
+      r8 = make_float2((float)(k8 - xmb), __fmul_rn(ws8, bsc));
+    }
+    float2* o = buf + bb * kPsRow;
+    o[g] = r0;
+    o[g + 8] = r8;
+  }
+}
+
+DPUF_DEV void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// One projection on the consumer side.
+DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, Consumer& C, unsigned char* ring,
+                            int n_ring, const int8_t* xq, const float* xs, const int* xm, float2* ps, DecShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u0, n;
+  take_range(kind_units(A, kind), C.rot, u0, n);
+  const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
+  const int subs = kind_subs(kind);
+  float bv = -INFINITY, gate_v = 0.0f;
+  int bi = 0x7fffffff;
+  for (int u = u0; u < u0 + n; u++)
+    for (int sub = 0; sub < subs; sub++) {
+      const Unit un = unit_of(A, Ly, kind, u, sub);
+      float acc = 0.0f;
+      for (int s = 0; s < n_st; s++) {
+        const int kb = min(32, n_blk - s * 32);
+        float2* buf = ps + C.pb * kPsBuf;
+        if (warp < kMmaWarps) {
+          bool ok = true;
+          if (lane == 0)
+            ok = wait_bar(&S.full[C.slot], C.phase, S, A.err) && wait_bar(&S.pse[C.pb], C.pphase ^ 1u, S, A.err);
+          if (__shfl_sync(kFull, (int)ok, 0))
+            mma_stage(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, warp, lane, buf);
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&S.psf[C.pb]);
+            mbar_arrive(&S.empty[C.slot]);
+          }
+        } else {
+          bool ok = true;
+          if (lane == 0) ok = wait_bar(&S.psf[C.pb], C.pphase, S, A.err);
+          ok = __shfl_sync(kFull, (int)ok, 0);
+          if (ok && lane < kTileRows) {
+            int b = 0;
+            for (; b + 7 < kb; b += 8) {
+              float2 v[8];
+#pragma unroll
+              for (int q = 0; q < 8; q++) v[q] = buf[(b + q) * kPsRow + lane];
+#pragma unroll
+              for (int q = 0; q < 8; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
+            }
+            for (; b < kb; b++) {
+              const float2 v = buf[b * kPsRow + lane];
+              acc = __fmaf_rn(v.x, v.y, acc);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.pse[C.pb]);
+        }
+        if (++C.slot == n_ring) {
+          C.slot = 0;
+          C.phase ^= 1u;
+        }
+        if (++C.pb == kNPs) {
+          C.pb = 0;
+          C.pphase ^= 1u;
+        }
+      }
+      // ---- epilogue of the unit (chain warp, lane = row)
+      if (warp == kChainWarp && lane < un.n_r) {
+        const int row = un.row + lane;
+        if (kind == kGU) {
+          if (sub == 0) {
+            gate_v = acc;
+          } else {
+            un.out[lane] = swiglu_one(gate_v, acc, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et);
+          }
+        } else if (kind == kLM) {
+          if (A.write_logits) un.out[lane] = acc;
+          better(bv, bi, acc, row);
+        } else {
+          un.out[lane] = acc;
+        }
+      }
+    }
+  if (kind == kLM && warp == kChainWarp) {
+    for (int m = 16; m; m >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, bv, m);
+      const int oi = __shfl_xor_sync(kFull, bi, m);
+      better(bv, bi, ov, oi);
+    }
+    if (lane == 0) A.part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+  }
+}
+
+// Grid-wide barrier of the consumer threads (the producer never joins): arrive on a global
+// counter and wait, bounded, until every CTA has arrived `target / gridDim.x` times.
+DPUF_DEV void grid_sync(const DecodeArgs& A, unsigned& target, DecShared& S) {
+  cbar();
+  target += gridDim.x;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(A.bar, 1u);
+    unsigned long long t0 = 0;
+    for (int it = 0; !S.abort; it++) {
+      if ((int)(ld_acquire(A.bar) - target) >= 0) break;
+      if (*(volatile int*)A.err) {
+        S.abort = 1;
+        break;
+      }
+      if ((it & 15) == 15) {
+        const unsigned long long now = globaltimer();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitNs) {
+          atomicCAS(A.err, 0, 2);
+          S.abort = 1;
+          break;
+        }
+      }
+      __nanosleep(20);
+    }
+  }
+  cbar();
+}
+
+// Async copies by the consumer threads into shared memory: 16-byte pieces through L2 (data
+// other CTAs wrote; bytes % 16 == 0) and 8-byte pieces of read-only tables (bytes % 8 == 0).
+DPUF_DEV void stage16(void* dst, const void* src, int bytes) {
+  for (int i = threadIdx.x * 16; i < bytes; i += kConsumers * 16)
+    cp_async16_cg((unsigned char*)dst + i, (const unsigned char*)src + i);
+}
+DPUF_DEV void stage8(void* dst, const void* src, int bytes) {
+  for (int i = threadIdx.x * 8; i < bytes; i += kConsumers * 8)
+    cp_async8_ca((unsigned char*)dst + i, (const unsigned char*)src + i);
+}
+
+// h[i] += res[i] for i < n_valid, h[i] += 0 beyond (rows pruned from the down projection);
+// res is staged into shared memory first (one round trip).
+DPUF_DEV void add_residual(float* h, const float* res, int H, int n_valid, float* stage) {
+  stage16(stage, res, min(H, n_valid) * 4);
+  cp_async_commit_wait_all();
+  cbar();
+  for (int i = threadIdx.x; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? stage[i] : 0.0f);
+}
+
+// RMSNorm of h with gain w, then the activation prep of the result (signs) into x.  The gains
+// and sign bytes are copied into shared memory while threads 0..7 run the sum-of-squares
+// chains.
+DPUF_DEV void norm_prep(const float* h, const float* w, int H, float eps, const uint8_t* signs, int8_t* xq, float* xs,
+                        int* xm, float* stage, DecShared& S) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* sg = (uint8_t*)(stage + H);
+  stage16(stage, w, H * 4);
+  if (signs) stage8(sg, signs, H / 8);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (tid < 8) S.lanes[tid] = sumsq_lane(h, H & ~7, tid);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  cbar();
+  if (tid == 0) S.inv = rms_inv(S.lanes, h, H, eps);
+  cbar();
+  const float inv = S.inv;
+  const int nch = H / 64;
+  for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
+    const int c = cb + (lane >> 3);
+    const bool active = c < nch;
+    const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
+    float v[8];
+    const float4 h0 = *(const float4*)(h + col), h1 = *(const float4*)(h + col + 4);
+    const float4 w0 = *(const float4*)(stage + col), w1 = *(const float4*)(stage + col + 4);
+    v[0] = __fmul_rn(__fmul_rn(h0.x, inv), w0.x);
+    v[1] = __fmul_rn(__fmul_rn(h0.y, inv), w0.y);
+    v[2] = __fmul_rn(__fmul_rn(h0.z, inv), w0.z);
+    v[3] = __fmul_rn(__fmul_rn(h0.w, inv), w0.w);
+    v[4] = __fmul_rn(__fmul_rn(h1.x, inv), w1.x);
+    v[5] = __fmul_rn(__fmul_rn(h1.y, inv), w1.y);
+    v[6] = __fmul_rn(__fmul_rn(h1.z, inv), w1.z);
+    v[7] = __fmul_rn(__fmul_rn(h1.w, inv), w1.w);
+    prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, active ? c * 64 : 0, lane, xq, xs, xm);
+  }
+}
+
+// Activation prep of a vector written by other CTAs: pieces of `cap` columns (a multiple of
+// 128) are staged into shared memory with their sign bytes, then prepped from there.
+DPUF_DEV void prep_global(const float* src, int K, const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage,
+                          int cap) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* sg = (uint8_t*)(stage + cap);
+  for (int p0 = 0; p0 < K; p0 += cap) {
+    const int n = min(cap, K - p0);
+    stage16(stage, src + p0, n * 4);
+    if (signs) stage8(sg, signs + p0 / 8, n / 8);
+    cp_async_commit_wait_all();
+    cbar();
+    const int nch = n / 64;
+    for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
+      const int c = cb + (lane >> 3);
+      const bool active = c < nch;
+      const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
+      const float4 a0 = *(const float4*)(stage + col), a1 = *(const float4*)(stage + col + 4);
+      float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, p0 + (active ? c * 64 : 0), lane, xq, xs, xm);
+    }
+    cbar();
+  }
+}
+
+struct AttnSync {
+  DPUF_DEV void operator()() const { named_sync(kBarAttn, kAttnThreads); }
+};
+
+// Attention items (KV head, query-head pair) of this CTA: QK-norm + RoPE of the pair's query
+// heads and of the KV head's key, K/V rows stored at `pos` (both pairs of a KV head store the
+// same bits), then attn_pair_body.  Threads 0..255 only.
+DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, int pos, float* scratch,
+                              DecShared& S) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int groups = A.nq / A.nkv, n_pairs = (groups + 1) / 2, hd = A.hd;
+  float* qs = scratch;                       // [2][hd]
+  float* sc = qs + 2 * hd;                   // [2][S]
+  float* kt = sc + 2 * (size_t)A.S;          // [kAttnKeyTile][hd + 8]
+  const float* cp = A.cos_tab + (size_t)pos * (hd >> 1);
+  const float* sp = A.sin_tab + (size_t)pos * (hd >> 1);
+  for (int it = blockIdx.x; it < A.nkv * n_pairs; it += gridDim.x) {
+    const int kvh = it / n_pairs, pr = it % n_pairs;
+    const int g0 = pr * 2, nh = (g0 + 1 < groups) ? 2 : 1, qh0 = kvh * groups + g0;
+    float* kc = A.kv_k + ((size_t)l * A.nkv + kvh) * A.S * hd;
+    float* vc = A.kv_v + ((size_t)l * A.nkv + kvh) * A.S * hd;
+    named_sync(kBarAttn, kAttnThreads);  // scratch free (previous item done)
+    if (warp == 0) {
+      float* kb = kt;
+      for (int i = lane; i < hd; i += 32) kb[i] = __ldcg(A.k + (size_t)kvh * hd + i);
+      __syncwarp();
+      qk_norm_rope_warp(kb, Ly.k_norm, A.eps, hd, cp, sp, lane);
+      for (int i = lane; i < hd; i += 32) kc[(size_t)pos * hd + i] = kb[i];
+    } else if (warp == 1) {
+      for (int i = lane; i < hd; i += 32) vc[(size_t)pos * hd + i] = __ldcg(A.v + (size_t)kvh * hd + i);
+    } else if (warp < 2 + nh) {
+      float* qv = qs + (warp - 2) * hd;
+      for (int i = lane; i < hd; i += 32) qv[i] = __ldcg(A.q + (size_t)(qh0 + warp - 2) * hd + i);
+      __syncwarp();
+      qk_norm_rope_warp(qv, Ly.q_norm, A.eps, hd, cp, sp, lane);
+    }
+    attn_pair_body(qs, nh, hd, pos + 1, kc, vc, A.S, sc, kt, &S.attn, A.att + (size_t)qh0 * hd, A.et, tid,
+                   AttnSync{});
+  }
+}
+
+// Optional trace of the last step: per CTA, the time (globaltimer, ns) at which each phase of
+// the consumer side ended (14 per layer, then 6 per step) and at which the producer began each
+// projection (4 per layer + the LM head).
+enum {
+  kEvNorm1, kEvQKV, kEvB1, kEvAttn, kEvB2, kEvPrepO, kEvO, kEvB3, kEvNorm2, kEvGU, kEvB4, kEvPrepD, kEvDown, kEvB5,
+  kEvPerLayer
+};
+enum { kEvStart, kEvEmbed, kEvNormF, kEvLM, kEvBLM, kEvArg, kEvPerStep };
+DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
+  if (A.trace && step == A.n_steps - 1) A.trace[(size_t)blockIdx.x * A.trace_per_cta + ev] = globaltimer();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ DecShared S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_ring = A.n_ring;
+  unsigned char* ring = smem;
+  DecLayer* layers = (DecLayer*)(smem + (size_t)n_ring * kSlotBytes);
+  float* h = (float*)(layers + max(A.L, 1));
+  unsigned char* uni = (unsigned char*)(h + A.H);
+  int8_t* xq = (int8_t*)uni;
+  float* xs = (float*)(uni + A.kmax);
+  int* xm = (int*)(xs + A.kmax / 32);
+  float2* ps = (float2*)(xm + A.kmax / 32);
+  float* stage = (float*)(xm + A.kmax / 32);  // staging area (overlaps the pair buffers)
+  float* attn_scratch = (float*)uni;
+
+  if (tid == 0) {
+    for (int i = 0; i < n_ring; i++) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.empty[i], kMmaWarps);
+    }
+    for (int i = 0; i < kNPs; i++) {
+      mbar_init(&S.psf[i], kMmaWarps);
+      mbar_init(&S.pse[i], 1);
+    }
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  {
+    const int4* src = (const int4*)A.layers;
+    int4* dst = (int4*)layers;
+    for (int i = tid; i < A.L * (int)(sizeof(DecLayer) / 16); i += kThreads) dst[i] = src[i];
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- producer warp
+  if (warp == kProdWarp) {
+    if (lane != 0) return;
+    Producer P;
+    int rot = 0;
+    bool ok = true;
+    const int ev0 = kEvPerLayer * A.L + kEvPerStep;
+    for (int step = 0; ok && step < A.n_steps; step++) {
+      for (int l = 0; ok && l < A.L; l++)
+        for (int kind = kQKV; ok && kind <= kDown; kind++) {
+          trace_at(A, step, ev0 + 4 * l + kind);
+          ok = produce_phase(A, layers, l, kind, rot, ring, n_ring, P, S);
+        }
+      trace_at(A, step, ev0 + 4 * A.L);
+      if (ok) ok = produce_phase(A, layers, 0, kLM, rot, ring, n_ring, P, S);
+    }
+    if (!ok) {
+      // copies still in flight must land before the CTA exits: wait (bounded) for the last
+      // use of every slot
+      const unsigned long long t0 = globaltimer();
+      for (int sl = 0; sl < n_ring; sl++) {
+        const long long uses = P.issued / n_ring + (sl < P.issued % n_ring ? 1 : 0);
+        if (uses == 0) continue;
+        const unsigned par = (unsigned)((uses - 1) & 1);
+        while (!mbar_try(&S.full[sl], par) && globaltimer() - t0 < kWaitNs) {
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumer warps
+  Consumer C;
+  unsigned target = 0;
+  const int H = A.H;
+  const int n_chunks = A.H / 64;
+  for (int step = 0; step < A.n_steps; step++) {
+    const int pos = A.pos0 + step;
+    const int id = step == 0 ? A.first_id : S.next_id;
+    const int sb = kEvPerLayer * A.L;
+    if (tid == 0) trace_at(A, step, sb + kEvStart);
+    // embedding row -> h: the row's 8-row group of its tile and the sign table are staged in
+    // shared memory, then every warp expands its chunks from there
+    {
+      const int n_blk = H >> 5, lr = id % kTileRows;
+      const uint8_t* grp = A.tok_tiles + (size_t)(id / kTileRows) * A.tok_stride + 16 + (size_t)(lr >> 3) * n_blk * 144;
+      uint8_t* sgrp = (uint8_t*)stage;
+      uint8_t* sg = sgrp + n_blk * 144;
+      stage16(sgrp, grp, n_blk * 144);
+      if (A.tok_signs) stage8(sg, A.tok_signs, H / 8);
+      cp_async_commit_wait_all();
+      cbar();
+      for (int c = warp; c < n_chunks; c += kConsumers / 32) {
+        float a, b;
+        embed_chunk_warp(sgrp - 16, n_blk, lr & 7, A.tok_signs ? sg : nullptr, c * 64, lane, a, b);
+        h[c * 64 + lane] = a;
+        h[c * 64 + 32 + lane] = b;
+      }
+    }
+    cbar();
+    if (tid == 0) trace_at(A, step, sb + kEvEmbed);
+    for (int l = 0; l < A.L; l++) {
+      const DecLayer& Ly = layers[l];
+      const int lb = kEvPerLayer * l;
+      if (l > 0) {
+        add_residual(h, A.d_out, H, A.keep_down * kTileRows, stage);
+        cbar();
+      }
+      norm_prep(h, Ly.attn_norm, H, A.eps, Ly.signs[0], xq, xs, xm, stage, S);
+      cbar();
+      if (tid == 0) trace_at(A, step, lb + kEvNorm1);
+      consume_phase(A, Ly, kQKV, C, ring, n_ring, xq, xs, xm, ps, S);
+      if (tid == 0) trace_at(A, step, lb + kEvQKV);
+      grid_sync(A, target, S);
+      if (tid == 0) trace_at(A, step, lb + kEvB1);
+      if (tid < kAttnThreads) attention_items(A, Ly, l, pos, attn_scratch, S);
+      if (tid == 0) trace_at(A, step, lb + kEvAttn);
+      grid_sync(A, target, S);
+      if (tid == 0) trace_at(A, step, lb + kEvB2);
+      prep_global(A.att, A.qd, Ly.signs[1], xq, xs, xm, stage, A.stage_cap);
+      cbar();
+      if (tid == 0) trace_at(A, step, lb + kEvPrepO);
+      consume_phase(A, Ly, kO, C, ring, n_ring, xq, xs, xm, ps, S);
+      if (tid == 0) trace_at(A, step, lb + kEvO);
+      grid_sync(A, target, S);
+      if (tid == 0) trace_at(A, step, lb + kEvB3);
+      add_residual(h, A.o_out, H, H, stage);
+      cbar();
+      norm_prep(h, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
+      cbar();
+      if (tid == 0) trace_at(A, step, lb + kEvNorm2);
+      consume_phase(A, Ly, kGU, C, ring, n_ring, xq, xs, xm, ps, S);
+      if (tid == 0) trace_at(A, step, lb + kEvGU);
+      grid_sync(A, target, S);
+      if (tid == 0) trace_at(A, step, lb + kEvB4);
+      prep_global(A.s_out, A.I, Ly.signs[3], xq, xs, xm, stage, A.stage_cap);
+      cbar();
+      if (tid == 0) trace_at(A, step, lb + kEvPrepD);
+      consume_phase(A, Ly, kDown, C, ring, n_ring, xq, xs, xm, ps, S);
+      if (tid == 0) trace_at(A, step, lb + kEvDown);
+      grid_sync(A, target, S);
+      if (tid == 0) trace_at(A, step, lb + kEvB5);
+    }
+    if (A.L > 0) {
+      add_residual(h, A.d_out, H, A.keep_down * kTileRows, stage);
+      cbar();
+    }
+    norm_prep(h, A.out_norm, H, A.eps, A.lm_signs, xq, xs, xm, stage, S);
+    cbar();
+    if (tid == 0) trace_at(A, step, sb + kEvNormF);
+    consume_phase(A, layers[0], kLM, C, ring, n_ring, xq, xs, xm, ps, S);
+    if (tid == 0) trace_at(A, step, sb + kEvLM);
+    grid_sync(A, target, S);
+    if (tid == 0) trace_at(A, step, sb + kEvBLM);
+    if (warp == 0) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int c = lane; c < (int)gridDim.x; c += 32) {
+        const float2 p = __ldcg(A.part + c);
+        better(bv, bi, p.x, __float_as_int(p.y));
+      }
+      for (int m = 16; m; m >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, m);
+        const int oi = __shfl_xor_sync(kFull, bi, m);
+        better(bv, bi, ov, oi);
+      }
+      if (lane == 0) {
+        // the winner is a row of the head; anything else (all logits NaN, or an aborted run)
+        // feeds row 0 so that the embedding lookup stays in bounds
+        const int id_next = (bi >= 0 && bi < A.V && bi < A.tok_rows) ? bi : 0;
+        S.next_id = id_next;
+        if (blockIdx.x == 0) A.hist[step] = id_next;
+      }
+    }
+    if (tid == 0) trace_at(A, step, sb + kEvArg);
+    // without layers the next LM phase would rewrite the partials other CTAs may still read
+    if (A.L == 0) grid_sync(A, target, S);
+    cbar();
+  }
+}
+
+}  // namespace
+
+// Shared memory of one CTA: ring | layer table | h | a union of {activation x + pair buffers
+// or staging area} and the attention scratch.  The staging area (after x) holds an embedding
+// group with its sign table (4.625 H bytes), norm gains with signs (4.125 H) or a piece of a
+// vector being prepped.
+size_t decode_x_bytes(const DecodeArgs& A) { return (size_t)A.kmax + (size_t)(A.kmax / 32) * 8; }
+size_t decode_uni_bytes(const DecodeArgs& A) {
+  const size_t xb = decode_x_bytes(A);
+  const size_t uni_x = xb + (size_t)kNPs * kPsBuf * sizeof(float2);
+  const size_t uni_stage = xb + (size_t)A.H * 4 + (size_t)A.H / 2 + (size_t)A.H / 8 + 64;
+  const size_t uni_attn = attn_scratch_floats(A.hd, A.S) * sizeof(float);
+  return std::max(std::max(uni_x, uni_stage), uni_attn);
+}
+int decode_stage_cap(const DecodeArgs& A) {
+  const size_t bytes = decode_uni_bytes(A) - decode_x_bytes(A);
+  return (int)(bytes * 8 / 33 / 128 * 128);  // 4 + 1/8 bytes per column
+}
+size_t decode_smem_bytes(const DecodeArgs& A) {
+  return (size_t)A.n_ring * kSlotBytes + (size_t)std::max(A.L, 1) * sizeof(DecLayer) + (size_t)A.H * 4 +
+         decode_uni_bytes(A);
+}
+
+int decode_ring_slots(const DecodeArgs& A, size_t smem_limit) {
+  DecodeArgs B = A;
+  B.n_ring = 0;
+  const size_t fixed = decode_smem_bytes(B);
+  if (fixed >= smem_limit) return 0;
+  return (int)std::min<size_t>(kMaxRing, (smem_limit - fixed) / kSlotBytes);
+}
+
+int decode_trace_events(int L) { return kEvPerLayer * L + kEvPerStep + 4 * L + 1; }
+
+cudaError_t configure_decode_kernel() { return set_max_dyn_smem(decode_kernel); }
+
+cudaError_t decode_max_dyn_smem(size_t* bytes) {
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, (const void*)decode_kernel);
+  if (e == cudaSuccess) *bytes = (size_t)a.maxDynamicSharedSizeBytes;
+  return e;
+}
+
+cudaError_t decode_blocks_per_sm(const DecodeArgs& A, int* blocks) {
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, decode_kernel, kThreads, decode_smem_bytes(A));
+}
+
+cudaError_t launch_decode(cudaStream_t stream, const DecodeArgs& A) {
+  if (A.n_ring < 2 || A.n_ring > kMaxRing) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)A.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = decode_smem_bytes(A);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_kernel, A);
+}
+
+}  // namespace dpuf

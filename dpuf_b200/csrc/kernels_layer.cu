@@ -2,6 +2,7 @@
 // exact fp32 operation order: residual add + RMSNorm + mode-12 prep, QK RMSNorm + NeoX RoPE
 // + KV-cache store, SwiGLU with dead-zone + prep of the down-projection input.
 #include "kernels.cuh"
+#include "layer_dev.cuh"
 
 namespace dpuf {
 
@@ -51,26 +52,9 @@ __global__ void __launch_bounds__(1024) norm_prep_kernel(float* __restrict__ h, 
     S[i] = s;
   }
   __syncthreads();
-  const int H8 = H & ~7;
-  if (threadIdx.x < 8) {
-    float acc = 0.0f;
-    int i = threadIdx.x;
-    for (; i + 56 < H8; i += 64) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) v[u] = S[i + 8 * u];
-#pragma unroll
-      for (int u = 0; u < 8; u++) acc = __fmaf_rn(v[u], v[u], acc);
-    }
-    for (; i < H8; i += 8) acc = __fmaf_rn(S[i], S[i], acc);
-    lanes[threadIdx.x] = acc;
-  }
+  if (threadIdx.x < 8) lanes[threadIdx.x] = sumsq_lane(S, H & ~7, threadIdx.x);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float ss = tree8_split_arr(lanes);
-    for (int i = H8; i < H; i++) ss = __fadd_rn(ss, __fmul_rn(S[i], S[i]));
-    inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
-  }
+  if (threadIdx.x == 0) inv_s = rms_inv(lanes, S, H, eps);
   __syncthreads();
   const float inv = inv_s;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -114,39 +98,10 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   float* s = sv + warp * hd;
   for (int i = lane; i < hd; i += 32) s[i] = vec[i];
   __syncwarp();
-  if (nw) {
-    const int hd8 = hd & ~7;
-    float acc = 0.0f;
-    if (lane < 8)
-      for (int i = lane; i < hd8; i += 8) acc = __fmaf_rn(s[i], s[i], acc);
-    float ss = tree8_split(acc);  // lanes 0..7 hold the tree result
-    ss = __shfl_sync(kFull, ss, 0);
-    for (int i = hd8; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(s[i], s[i]));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
-    __syncwarp();
-    for (int i = lane; i < hd; i += 32) s[i] = __fmul_rn(__fmul_rn(s[i], inv), nw[i]);
-    __syncwarp();
-  }
-  const int half = hd >> 1, half8 = half & ~7;
-  const float* cp = cos_tab + (size_t)pos * half;
-  const float* sp = sin_tab + (size_t)pos * half;
-  for (int j = lane; j < half; j += 32) {
-    const float x1 = s[j], x2 = s[j + half], c = cp[j], sn = sp[j];
-    float o1, o2;
-    if (j < half8) {
-      o1 = __fmaf_rn(x1, c, -__fmul_rn(x2, sn));
-      o2 = __fmaf_rn(x2, c, __fmul_rn(x1, sn));
-    } else {
-      o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
-      o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
-    }
-    vec[j] = o1;
-    vec[j + half] = o2;
-    if (is_k) {
-      float* kc = kv.k + ((size_t)head * kv.max_seq + pos) * hd;
-      kc[j] = o1;
-      kc[j + half] = o2;
-    }
+  qk_norm_rope_warp(s, nw, eps, hd, cos_tab + (size_t)pos * (hd >> 1), sin_tab + (size_t)pos * (hd >> 1), lane);
+  for (int i = lane; i < hd; i += 32) {
+    vec[i] = s[i];
+    if (is_k) kv.k[((size_t)head * kv.max_seq + pos) * hd + i] = s[i];
   }
   if (is_k) {
     const float* vr = v + ((size_t)m * n_kv + head) * hd;
@@ -156,36 +111,7 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
 }
 
 // ------------------------------------------------------------------ SwiGLU + prep for w_down
-// swiglu_range_avx2 (dpuf_engine.c:967-997): the 8-wide formula
-//   silu = g / (1 + exp_poly(clamp(0 - g, -40, 40))),  r = silu * u,  |r| < dz -> 0
-// for elements in the vector part of a thread's range, and the scalar formula (libm expf)
-// for the range's tail.  Ranges follow the reference's split of the flat [M*I] array over
-// its nt threads (dpuf_engine.c:2007-2011), or whole 6-token slabs when the reference takes
-// its slab-fused path (M >= 2 and ceil(M/6) >= nt, dpuf_engine.c:1983-2005).
-DPUF_DEV bool swiglu_vector_elem(long long idx, long long total, int nt, bool slab) {
-  if (slab) return true;
-  long long tid = (idx * nt) / total;
-  while (tid > 0 && (total * tid) / nt > idx) tid--;
-  while (tid + 1 < nt && (total * (tid + 1)) / nt <= idx) tid++;
-  const long long s0 = (total * tid) / nt, s1 = (total * (tid + 1)) / nt;
-  return (idx - s0) < ((s1 - s0) & ~7LL);
-}
-
-DPUF_DEV float swiglu_one(float g, float u, float dz, bool vec, const ExpfTable& et) {
-  float r;
-  if (vec) {
-    const float ng = max_ps(-40.0f, min_ps(__fsub_rn(0.0f, g), 40.0f));
-    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, exp_poly(ng)));
-    r = __fmul_rn(silu, u);
-    if (dz > 0.0f && !(fabsf(r) >= dz)) r = 0.0f;
-  } else {
-    const float silu = (g >= 40.0f) ? g : ((g <= -40.0f) ? 0.0f : __fdiv_rn(g, __fadd_rn(1.0f, glibc_expf(-g, et))));
-    r = __fmul_rn(silu, u);
-    if (dz > 0.0f && fabsf(r) < dz) r = 0.0f;
-  }
-  return r;
-}
-
+// swiglu_one per element (layer_dev.cuh), then the prep of each 64-column chunk.
 __global__ void swiglu_prep_kernel(const float* __restrict__ gate, const float* __restrict__ up, int M, int I,
                                    float dz, int nt, const uint8_t* __restrict__ signs, Act out, ExpfTable et) {
   cudaGridDependencySynchronize();

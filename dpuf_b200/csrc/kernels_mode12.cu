@@ -7,6 +7,7 @@
 //   acc   = fmaf((float)dot_b, ws_b * xs_b, acc)   for blocks b ascending, xs_b <= 0 skipped
 // The integer dot uses dp4a on nibbles widened to bytes (u < 16 fits a signed byte).
 #include "kernels.cuh"
+#include "layer_dev.cuh"
 
 namespace dpuf {
 
@@ -53,24 +54,12 @@ __global__ void embed_kernel(W12 w, const int32_t* __restrict__ ids, float* __re
   const int cols = w.cols, n_blk = cols >> 5;
   if (chunk * 64 >= cols) return;
   const int r = ids[m];
-  const int t = r / kTileRows, lr = r % kTileRows, rg = lr >> 3, ri = lr & 7;
-  const uint8_t* grp = tile_ptr(w, t) + 16 + (size_t)rg * n_blk * 144;
-  const uint8_t* qg = grp + (size_t)n_blk * 16;
-  float v[2];
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    const int b = chunk * 2 + h;
-    const float ws = f16bits_to_f32(*(const uint16_t*)(grp + (size_t)b * 16 + ri * 2));
-    const int c = lane >> 3, k = lane & 3, hi = (lane >> 2) & 1;
-    const uint8_t byte = qg[(size_t)b * 128 + c * 32 + ri * 4 + k];
-    const int u = hi ? (byte >> 4) : (byte & 15);
-    v[h] = __fmul_rn((float)(u - 8), ws);
-  }
-  fwht64_warp(v[0], v[1], lane);
   const int c0 = chunk * 64;
+  float oa, ob;
+  embed_chunk_warp(tile_ptr(w, r / kTileRows), n_blk, r % kTileRows, w.signs, c0, lane, oa, ob);
   float* o = out + (size_t)m * cols;
-  o[c0 + lane] = w.signs ? apply_sign(v[0], w.signs, c0 + lane) : v[0];
-  o[c0 + 32 + lane] = w.signs ? apply_sign(v[1], w.signs, c0 + 32 + lane) : v[1];
+  o[c0 + lane] = oa;
+  o[c0 + 32 + lane] = ob;
 }
 
 // ------------------------------------------------------------------ exact prefill GEMM (M > 1)

@@ -1,0 +1,428 @@
+// layer_dev.cuh - per-layer device math shared by the per-step kernels and the persistent
+// decode kernel, so both paths produce the same bits.  Every function restates one piece of
+// the reference's fp32 operation order (dpuf_engine.c, cited per function).
+#pragma once
+#include "common.cuh"
+
+namespace dpuf {
+
+// ------------------------------------------------------------------ RMSNorm
+// add_and_rms_norm_f32 / rms_norm_f32 (dpuf_engine.c:225-272): "AVX lane" j accumulates
+// fma(s_i, s_i, .) over i = j, j+8, ... < (n & ~7) in order.
+DPUF_DEV float sumsq_lane(const float* S, int n8, int j) {
+  float acc = 0.0f;
+  int i = j;
+  for (; i + 56 < n8; i += 64) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = S[i + 8 * u];
+#pragma unroll
+    for (int u = 0; u < 8; u++) acc = __fmaf_rn(v[u], v[u], acc);
+  }
+  for (; i < n8; i += 8) acc = __fmaf_rn(S[i], S[i], acc);
+  return acc;
+}
+
+// inv = 1 / sqrt(ss / n + eps) with ss = split tree of the eight lane sums, then the n % 8
+// tail added in order.
+DPUF_DEV float rms_inv(const float* lanes, const float* S, int n, float eps) {
+  float ss = tree8_split_arr(lanes);
+  for (int i = n & ~7; i < n; i++) ss = __fadd_rn(ss, __fmul_rn(S[i], S[i]));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// ------------------------------------------------------------------ QK-norm + NeoX RoPE
+// One warp, one head vector s[hd] in shared memory, in place (dpuf_engine.c:1788-1822):
+// RMSNorm over hd with gain nw (when nw != null), then apply_rope_neox_f32
+// (dpuf_engine.c:274-295): for j < half & ~7, x1*c - x2*s and x2*c + x1*s as fused
+// multiply-subtract/add of the rounded cross product; the tail j uses separate products.
+DPUF_DEV void qk_norm_rope_warp(float* s, const float* nw, float eps, int hd, const float* cp, const float* sp,
+                                int lane) {
+  if (nw) {
+    const int hd8 = hd & ~7;
+    float acc = 0.0f;
+    if (lane < 8)
+      for (int i = lane; i < hd8; i += 8) acc = __fmaf_rn(s[i], s[i], acc);
+    float ss = tree8_split(acc);  // lanes 0..7 hold the tree result
+    ss = __shfl_sync(kFull, ss, 0);
+    for (int i = hd8; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(s[i], s[i]));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    __syncwarp();
+    for (int i = lane; i < hd; i += 32) s[i] = __fmul_rn(__fmul_rn(s[i], inv), nw[i]);
+    __syncwarp();
+  }
+  const int half = hd >> 1, half8 = half & ~7;
+  for (int j = lane; j < half; j += 32) {
+    const float x1 = s[j], x2 = s[j + half], c = cp[j], sn = sp[j];
+    float o1, o2;
+    if (j < half8) {
+      o1 = __fmaf_rn(x1, c, -__fmul_rn(x2, sn));
+      o2 = __fmaf_rn(x2, c, __fmul_rn(x1, sn));
+    } else {
+      o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+      o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+    }
+    s[j] = o1;
+    s[j + half] = o2;
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------ SwiGLU with dead zone
+// swiglu_range_avx2 (dpuf_engine.c:967-997): the 8-wide formula
+//   silu = g / (1 + exp_poly(clamp(0 - g, -40, 40))),  r = silu * u,  |r| < dz -> 0
+// for elements in the vector part of a thread's range, and the scalar formula (libm expf)
+// for the range's tail.  Ranges follow the reference's split of the flat [M*I] array over
+// its nt threads (dpuf_engine.c:2007-2011), or whole 6-token slabs when the reference takes
+// its slab-fused path (M >= 2 and ceil(M/6) >= nt, dpuf_engine.c:1983-2005).
+DPUF_DEV bool swiglu_vector_elem(long long idx, long long total, int nt, bool slab) {
+  if (slab) return true;
+  long long tid = (idx * nt) / total;
+  while (tid > 0 && (total * tid) / nt > idx) tid--;
+  while (tid + 1 < nt && (total * (tid + 1)) / nt <= idx) tid++;
+  const long long s0 = (total * tid) / nt, s1 = (total * (tid + 1)) / nt;
+  return (idx - s0) < ((s1 - s0) & ~7LL);
+}
+
+DPUF_DEV float swiglu_one(float g, float u, float dz, bool vec, const ExpfTable& et) {
+  float r;
+  if (vec) {
+    const float ng = max_ps(-40.0f, min_ps(__fsub_rn(0.0f, g), 40.0f));
+    const float silu = __fdiv_rn(g, __fadd_rn(1.0f, exp_poly(ng)));
+    r = __fmul_rn(silu, u);
+    if (dz > 0.0f && !(fabsf(r) >= dz)) r = 0.0f;
+  } else {
+    const float silu = (g >= 40.0f) ? g : ((g <= -40.0f) ? 0.0f : __fdiv_rn(g, __fadd_rn(1.0f, glibc_expf(-g, et))));
+    r = __fmul_rn(silu, u);
+    if (dz > 0.0f && fabsf(r) < dz) r = 0.0f;
+  }
+  return r;
+}
+
+// ------------------------------------------------------------------ embedding row chunk
+// One warp: columns [c0, c0+64) of row r of a mode-12 matrix as the embedding lookup computes
+// them (dpuf_embed_qr_hadamard4_packed_f32, dpuf_avx2.c:2738-2783): (u - 8) * ws, FWHT-64,
+// then the column sign.  tp = the row's tile, lr = the row within the tile.  embed_load
+// fetches what lane `lane` needs (so a warp can have several chunks' loads in flight),
+// embed_finish computes the lane's two values (columns c0+lane and c0+32+lane).
+struct EmbedRaw {
+  uint16_t ws[2];
+  uint8_t q[2];
+  uint8_t sa, sb;  // sign bytes of the lane's two columns
+};
+DPUF_DEV EmbedRaw embed_load(const uint8_t* tp, int n_blk, int lr, const uint8_t* signs, int c0, int lane) {
+  const int rg = lr >> 3, ri = lr & 7;
+  const uint8_t* grp = tp + 16 + (size_t)rg * n_blk * 144;
+  const uint8_t* qg = grp + (size_t)n_blk * 16;
+  EmbedRaw r;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int b = (c0 >> 5) + h;
+    r.ws[h] = *(const uint16_t*)(grp + (size_t)b * 16 + ri * 2);
+    r.q[h] = qg[(size_t)b * 128 + (lane >> 3) * 32 + ri * 4 + (lane & 3)];
+  }
+  r.sa = signs ? signs[(c0 + lane) >> 3] : 0;
+  r.sb = signs ? signs[(c0 + 32 + lane) >> 3] : 0;
+  return r;
+}
+DPUF_DEV void embed_finish(const EmbedRaw& r, int c0, int lane, float& oa, float& ob) {
+  float v[2];
+  const int hi = (lane >> 2) & 1;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int u = hi ? (r.q[h] >> 4) : (r.q[h] & 15);
+    v[h] = __fmul_rn((float)(u - 8), f16bits_to_f32(r.ws[h]));
+  }
+  fwht64_warp(v[0], v[1], lane);
+  oa = ((r.sa >> ((c0 + lane) & 7)) & 1) ? -v[0] : v[0];
+  ob = ((r.sb >> ((c0 + 32 + lane) & 7)) & 1) ? -v[1] : v[1];
+}
+DPUF_DEV void embed_chunk_warp(const uint8_t* tp, int n_blk, int lr, const uint8_t* signs, int c0, int lane,
+                               float& oa, float& ob) {
+  embed_finish(embed_load(tp, n_blk, lr, signs, c0, lane), c0, lane, oa, ob);
+}
+
+// Prep of one 64-chunk whose sign bytes were loaded ahead (sa, sb: the bytes holding the
+// lane's columns c0+lane and c0+32+lane); same arithmetic as prep_chunk_warp.
+DPUF_DEV void prep_chunk_warp_sb(float a, float b, uint8_t sa, uint8_t sb, int c0, int lane, int8_t* q8, float* xs,
+                                 int32_t* xm) {
+  if ((sa >> ((c0 + lane) & 7)) & 1) a = -a;
+  if ((sb >> ((c0 + 32 + lane) & 7)) & 1) b = -b;
+  fwht64_warp(a, b, lane);
+  const int blk = c0 >> 5;
+  quant32_warp(a, lane, q8 + c0, xs + blk, xm + blk);
+  quant32_warp(b, lane, q8 + c0 + 32, xs + blk + 1, xm + blk + 1);
+}
+
+// ------------------------------------------------------------------ prep, 8 lanes per chunk
+// The activation prep of one 64-column chunk (dpuf_prep_had4_packed_slab, dpuf_avx2.c:2364-2449)
+// by a group of eight lanes, lane q of the group holding columns c0+8q .. c0+8q+7 in v[] (so a
+// warp preps four chunks at once):
+//   sign flip (bit r of sign byte sbyte negates v[r]),
+//   FWHT-64 with ascending strides (fwht64_block_f32, dpuf_avx2.c:724-772): strides 1, 2, 4
+//   inside the lane, 8, 16, 32 across lanes q^1, q^2, q^4; each butterfly gives (a+b, a-b) for
+//   the pair (lower, upper), then x0.125 - the same operations on the same operands as the
+//   one-chunk-per-warp form, so the same bits;
+//   per 32-block (lanes 0-3 and 4-7 of the group): amax, xs = amax/127,
+//   q = clamp(rint(v * (127/amax)), -127, 127), xm = 8 * sum(q); amax <= 1e-4 gives zeros.
+// Every lane of the warp must call this (shuffles span the warp); `active` masks groups
+// without a chunk (they compute on zeros and store nothing).
+DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, int lane, int8_t* q8, float* xs,
+                            int32_t* xm) {
+  const int q = lane & 7;
+#pragma unroll
+  for (int r = 0; r < 8; r++)
+    if ((sbyte >> r) & 1) v[r] = -v[r];
+#pragma unroll
+  for (int h = 1; h < 8; h <<= 1) {
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+      if (!(r & h)) {
+        const float a = v[r], b = v[r + h];
+        v[r] = __fadd_rn(a, b);
+        v[r + h] = __fsub_rn(a, b);
+      }
+  }
+#pragma unroll
+  for (int m = 1; m < 8; m <<= 1) {
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+      const float p = __shfl_xor_sync(kFull, v[r], m);
+      v[r] = (q & m) ? __fsub_rn(p, v[r]) : __fadd_rn(v[r], p);
+    }
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    v[r] = __fmul_rn(v[r], 0.125f);
+    amax = fmaxf(amax, fabsf(v[r]));
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+  int qs[8];
+  float xsv = 0.0f;
+  int sum = 0;
+  if (amax > 1e-4f) {
+    xsv = __fdiv_rn(amax, 127.0f);
+    const float inv = (amax > 1e-12f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+      qs[r] = max(-127, min(127, __float2int_rn(__fmul_rn(v[r], inv))));
+      sum += qs[r];
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < 8; r++) qs[r] = 0;
+  }
+  sum += __shfl_xor_sync(kFull, sum, 1);
+  sum += __shfl_xor_sync(kFull, sum, 2);
+  if (active) {
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      lo |= (uint32_t)(qs[r] & 0xFF) << (8 * r);
+      hi |= (uint32_t)(qs[r + 4] & 0xFF) << (8 * r);
+    }
+    *(uint2*)(q8 + c0 + 8 * q) = make_uint2(lo, hi);
+    if ((q & 3) == 0) {
+      const int blk = (c0 >> 5) + (q >> 2);
+      xs[blk] = xsv;
+      xm[blk] = sum * 8;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ attention, one head pair
+// gqa_attn_head_pair_f32 (dpuf_engine.c:341-577) for one (token, KV head, pair of Q heads),
+// run by kAttnThreads threads (tid 0..255) that call sync() as a barrier among themselves:
+//   scores  keys t < kv_len & ~3: eight lanes accumulate fma(q_i, k_i) over i = l, l+8, ...;
+//           "pairs" tree (hsum4_256_ps); keys in the kv_len % 4 tail: "split" tree
+//           (eng_hsum256_ps) - for a lone head the tail uses dot_f32_avx2's two accumulators
+//           over 16-wide steps, summed lane-wise before the split tree; then * 1/sqrt(hd).
+//   softmax e_k = exp_poly(s_k - max) for k < kv_len & ~7, lane sums over k = j mod 8 in
+//           order, split tree, then the tail adds glibc expf(s_k - max) sequentially;
+//           p_k = e_k * (1 / (sum + 1e-12)).
+//   PV      per output dim: fma(p_k, v_kd, acc) over k ascending (pair path); the lone-head
+//           path takes keys two at a time, k+1 first (dpuf_engine.c:541-548).
+// qs [2][hd] holds the (normed, rotated) query heads; kc/vc are this KV head's cache rows
+// [max_seq][hd] (read through L2: other CTAs may have written them); sc [2][max_seq] and
+// kt [kAttnKeyTile][hd+8] are scratch; out receives nh * hd values.
+constexpr int kAttnThreads = 256;
+constexpr int kAttnKeyTile = 32;  // keys staged per pass (8 threads per key)
+
+struct AttnShared {
+  float red[2][kAttnThreads / 32];
+  float lane_sum[2][8];
+  float inv_s[2], max_s[2];
+};
+
+DPUF_HD size_t attn_scratch_floats(int hd, int max_seq) {
+  return (size_t)2 * hd + 2 * (size_t)max_seq + (size_t)kAttnKeyTile * (hd + 8);
+}
+
+// ------------------------------------------------------------------ async copies to shared
+DPUF_DEV void cp_async16_cg(void* dst, const void* src) {  // L2 only: data other CTAs wrote
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+DPUF_DEV void cp_async8_ca(void* dst, const void* src) {  // read-only tables
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+DPUF_DEV void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Copies rows [0, nk) of a row-major [.][hd] array (read through L2; hd % 4 == 0, 16-byte
+// aligned rows) into dst with a padded row stride of hd + 8, as 16-byte async copies; each
+// thread waits for its own copies, the caller then synchronises the threads.
+DPUF_DEV void stage_rows(float* dst, const float* src, int nk, int hd, int tid) {
+  const int per_row = hd >> 2, n = nk * per_row;
+  for (int i = tid; i < n; i += kAttnThreads) {
+    const int r = i / per_row, c = (i - r * per_row) * 4;
+    cp_async16_cg(dst + r * (hd + 8) + c, src + (size_t)r * hd + c);
+  }
+  cp_async_commit_wait_all();
+}
+
+template <typename Sync>
+DPUF_DEV void attn_pair_body(const float* qs, int nh, int hd, int kv_len, const float* kc, const float* vc,
+                             int max_seq, float* sc, float* kt, AttnShared* sh, float* out, const ExpfTable& et,
+                             int tid, Sync sync) {
+  const int lane = tid & 31;
+  const int kvs = hd + 8;  // padded smem row of a staged key
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
+  float lmax[2] = {-1e30f, -1e30f};
+  // ---- scores
+  for (int t0 = 0; t0 < kv_len; t0 += kAttnKeyTile) {
+    const int nk = min(kAttnKeyTile, kv_len - t0);
+    sync();
+    stage_rows(kt, kc + (size_t)t0 * hd, nk, hd, tid);
+    sync();
+    const int key = tid >> 3, l = tid & 7;
+    const int t = t0 + key;
+    const bool valid = key < nk;
+    const float* kp = kt + key * kvs;
+    for (int h = 0; h < nh; h++) {
+      const float* qv = qs + h * hd;
+      // Shuffle trees run on all lanes (keys of one warp may sit on both sides of kv4).
+      float acc = 0.0f;
+      if (valid)
+        for (int i = l; i < hd; i += 8) acc = __fmaf_rn(qv[i], kp[i], acc);
+      const float t_pairs = tree8_pairs(acc);
+      float t_split;
+      if (nh == 2) {
+        t_split = tree8_split(acc);
+      } else {
+        // lone head, tail key: dot_f32_avx2 (dpuf_engine.c:325-339)
+        float a0 = 0.0f, a1 = 0.0f;
+        if (valid) {
+          int i = 0;
+          for (; i + 15 < hd; i += 16) {
+            a0 = __fmaf_rn(qv[i + l], kp[i + l], a0);
+            a1 = __fmaf_rn(qv[i + 8 + l], kp[i + 8 + l], a1);
+          }
+          for (; i + 7 < hd; i += 8) a0 = __fmaf_rn(qv[i + l], kp[i + l], a0);
+        }
+        t_split = tree8_split(__fadd_rn(a0, a1));
+      }
+      float s = __fmul_rn((t < kv4) ? t_pairs : t_split, scale);
+      if (valid && l == 0) {
+        sc[h * max_seq + t] = s;
+        lmax[h] = max_ps(lmax[h], s);
+      }
+    }
+  }
+  // ---- max
+  for (int h = 0; h < nh; h++) {
+    float v = warp_max(lmax[h]);
+    if (lane == 0) sh->red[h][tid >> 5] = v;
+  }
+  sync();
+  if (tid < nh) {
+    float v = -1e30f;
+    for (int w = 0; w < kAttnThreads / 32; w++) v = max_ps(v, sh->red[tid][w]);
+    sh->max_s[tid] = v;
+  }
+  sync();
+  // ---- exp over the 8-aligned part
+  for (int h = 0; h < nh; h++) {
+    const float mx = sh->max_s[h];
+    for (int k = tid; k < kv8; k += kAttnThreads) sc[h * max_seq + k] = exp_poly(__fsub_rn(sc[h * max_seq + k], mx));
+  }
+  sync();
+  // ---- lane sums (8 sequential chains per head); the <= 7 tail exponentials (glibc expf) are
+  // independent, so eight more threads per head evaluate them meanwhile
+  if (tid < 8 * nh) {
+    const int h = tid >> 3, l = tid & 7;
+    const float* s = sc + h * max_seq;
+    float acc = 0.0f;
+    for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, s[k]);
+    sh->lane_sum[h][l] = acc;
+  } else if (tid >= 64 && tid < 64 + 8 * nh) {
+    const int h = (tid - 64) >> 3, k = kv8 + ((tid - 64) & 7);
+    if (k < kv_len) {
+      float* s = sc + h * max_seq;
+      s[k] = glibc_expf(__fsub_rn(s[k], sh->max_s[h]), et);
+    }
+  }
+  sync();
+  // split tree of the lane sums, then the tail added in order
+  if (tid < nh) {
+    const float* s = sc + tid * max_seq;
+    float sp = tree8_split_arr(sh->lane_sum[tid]);
+    for (int k = kv8; k < kv_len; k++) sp = __fadd_rn(sp, s[k]);
+    sh->inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(sp, 1e-12f));
+  }
+  sync();
+  for (int h = 0; h < nh; h++) {
+    const float inv = sh->inv_s[h];
+    for (int k = tid; k < kv_len; k += kAttnThreads) sc[h * max_seq + k] = __fmul_rn(sc[h * max_seq + k], inv);
+  }
+  sync();
+  // ---- PV: value rows staged a tile at a time (kt is free again); thread o owns outputs
+  // o and o + kAttnThreads, each a sequential chain over the keys in the reference's order
+  float acc[2] = {0.0f, 0.0f};
+  const int hd8 = hd & ~7;
+  for (int t0 = 0; t0 < kv_len; t0 += kAttnKeyTile) {
+    const int nk = min(kAttnKeyTile, kv_len - t0);
+    sync();
+    stage_rows(kt, vc + (size_t)t0 * hd, nk, hd, tid);
+    sync();
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int o = tid + j * kAttnThreads;
+      if (o >= nh * hd) break;
+      const int h = o / hd, d = o % hd;
+      const float* p = sc + h * max_seq + t0;
+      const float* vt = kt + d;
+      float a = acc[j];
+      if (nh == 2) {
+        for (int k = 0; k < nk; k++) a = __fmaf_rn(p[k], vt[k * kvs], a);
+      } else if ((hd & 63) == 0) {
+        // keys two at a time, k+1 first (tiles hold an even number of keys but the last)
+        int k = 0;
+        for (; k + 1 < nk; k += 2) {
+          const float t1 = __fmaf_rn(p[k + 1], vt[(k + 1) * kvs], a);
+          a = __fmaf_rn(p[k], vt[k * kvs], t1);
+        }
+        if (k < nk) a = __fmaf_rn(p[k], vt[k * kvs], a);
+      } else {
+        for (int k = 0; k < nk; k++) {
+          const float pv = p[k], vv = vt[k * kvs];
+          a = (d < hd8) ? __fmaf_rn(pv, vv, a) : __fadd_rn(a, __fmul_rn(pv, vv));
+        }
+      }
+      acc[j] = a;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int o = tid + j * kAttnThreads;
+    if (o < nh * hd) out[o] = acc[j];
+  }
+}
+
+}  // namespace dpuf

@@ -50,6 +50,10 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_cuda_read_logits.argtypes = [_VP, _I32, _VP]
     lib.dpuf_cuda_set_option.restype = _I32
     lib.dpuf_cuda_set_option.argtypes = [_VP, ctypes.c_char_p, ctypes.c_int64]
+    lib.dpuf_cuda_decode_greedy.restype = _I32
+    lib.dpuf_cuda_decode_greedy.argtypes = [_VP, _I32, _I32, _I32, _VP, _VP]
+    lib.dpuf_cuda_persistent_decode.restype = _I32
+    lib.dpuf_cuda_persistent_decode.argtypes = [_VP, _VP]
     lib.dpuf_cuda_zone_info.restype = _I32
     lib.dpuf_cuda_zone_info.argtypes = [_VP, _VP, _VP, _VP, _VP]
     lib.dpuf_cuda_last_error.restype = ctypes.c_char_p
@@ -128,6 +132,22 @@ class CudaTransformerEngine:
         if rc != 0:
             raise RuntimeError(f"dpuf_cuda_forward_greedy failed with rc={rc}: {last_error()}")
         return int(nxt[0])
+
+    def decode_greedy(self, first_id: int, pos0: int, n_steps: int) -> tuple[list[int], float]:
+        """n_steps greedy steps with the token fed back on the device; (ids, device ms)."""
+        ids = np.zeros(n_steps, np.int32)
+        ms = ctypes.c_float()
+        rc = self.lib.dpuf_cuda_decode_greedy(self._handle, int(first_id), int(pos0), int(n_steps), ids.ctypes.data,
+                                              ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"dpuf_cuda_decode_greedy failed with rc={rc}: {last_error()}")
+        return [int(i) for i in ids], float(ms.value)
+
+    def persistent_decode(self) -> tuple[bool, str]:
+        """Whether batch-1 steps run as the persistent kernel, and why not."""
+        why = ctypes.c_char_p()
+        on = self.lib.dpuf_cuda_persistent_decode(self._handle, ctypes.byref(why))
+        return on == 1, (why.value or b"").decode()
 
     def zone_info(self):
         used, exited = np.zeros(1, np.int32), np.zeros(1, np.int32)

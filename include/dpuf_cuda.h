@@ -35,9 +35,28 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
 DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out);
 
 /* Engine options (call before the first forward):
- *   "pdl" (0/1)    programmatic dependent launch between kernels (default 1)
- *   "graphs" (0/1) capture each step shape in a CUDA graph (default 1) */
+ *   "pdl" (0/1)        programmatic dependent launch between kernels (default 1)
+ *   "graphs" (0/1)     capture each step shape in a CUDA graph (default 1)
+ *   "persistent" (0/1) run batch-1 steps (forward_token, forward_batch with one token,
+ *                      decode_greedy) as one persistent cooperative kernel when the engine
+ *                      supports it (default 1; env DPUF_CUDA_PERSISTENT=0 turns it off) */
 DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t value);
+
+/* 1 if batch-1 steps run as the persistent kernel, 0 if they run as per-step kernels, -1 for a
+ * null handle.  *why (optional) receives the reason the persistent kernel cannot be used ("" if
+ * it can; Zone-A steps always use the per-step kernels).  A persistent step that hits a device
+ * wait limit returns -6 with the reason in dpuf_cuda_last_error(). */
+DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why);
+
+/* Phase trace of the persistent kernel's last step, recorded when the engine was created with
+ * env DPUF_CUDA_TRACE_DECODE=1 (otherwise returns -1).  Per CTA, per_cta globaltimer stamps
+ * (ns): for each layer the end of norm1, q/k/v, barrier, attention, barrier, o prep, o,
+ * barrier, norm2, gate/up, barrier, down prep, down, barrier (14); then step start, embedding,
+ * final norm, LM head, barrier, argmax (6); then the producer's start of each projection
+ * (4 per layer, then the LM head).  *n_ctas and *per_cta receive the shape; out (optional)
+ * receives n_ctas * per_cta values when max_values is large enough (else -2). */
+DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_t* per_cta, uint64_t* out,
+                                           int64_t max_values);
 
 /* Zone-A decision of the last forward: {used, exited} and the top-2 values. */
 DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2);

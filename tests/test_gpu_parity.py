@@ -65,7 +65,7 @@ def test_engine_matches_reference(eng_mod, scn):
 def test_engine_without_graphs_or_pdl_matches(eng_mod):
     scn = sc.ENGINE_SCENARIOS[0]
     g = golden_engine()[scn.name]
-    for opts in ({"graphs": 0}, {"pdl": 0}):
+    for opts in ({"graphs": 0}, {"pdl": 0}, {"persistent": 0}):
         rec, _, _ = run_scenario(lambda m: eng_mod.CudaTransformerEngine(m, opts), scn)
         assert rec["digests"] == g["digests"], opts
 
@@ -149,3 +149,45 @@ def test_gemv_decode_shapes_match_oracle(eng_mod, rows, cols):
     want = orc.oracle_matmul(1, bv, x)
     for _ in range(2):  # the split arrival counters must be left at zero for the next call
         assert bitexact(eng_mod.matmul(1, bv, x), want)
+
+
+@pytest.mark.parametrize("shape", ["TINY", "TINY_MHA"])
+def test_persistent_decode_matches_step_kernels(eng_mod, shape):
+    """Greedy decode as one persistent kernel gives the ids and last logits of the per-step
+    kernels, which match the reference (the engine goldens above)."""
+    from dpuf_b200 import model as mdl
+
+    m = mdl.SyntheticModel(getattr(mdl, shape), seed=3, norm_jitter=0.1)
+    prompt = mdl.prompt_ids(11, m.shape.vocab, 3)
+    runs = []
+    for persistent in (1, 0):
+        e = eng_mod.CudaTransformerEngine(m, {"persistent": persistent})
+        on, why = e.persistent_decode()
+        assert on == bool(persistent), why
+        e.reset_cache()
+        first = int(np.argmax(e.forward_batch(prompt, 0)[0]))
+        ids, _ = e.decode_greedy(first, len(prompt), 24)
+        logits = np.empty(m.shape.vocab, np.float32)
+        assert e.lib.dpuf_cuda_read_logits(e._handle, 0, logits.ctypes.data) == 0
+        runs.append((ids, logits))
+        e.close()
+    assert runs[0][0] == runs[1][0]
+    assert bitexact(runs[0][1], runs[1][1])
+
+
+def test_persistent_decode_with_pruned_down(eng_mod):
+    """DPUF_GEN_KEEP_TILES: rows beyond the kept down-projection tiles add zero to the residual."""
+    from dpuf_b200 import model as mdl
+
+    m = mdl.SyntheticModel(mdl.TINY, seed=4, norm_jitter=0.1)
+    prompt = mdl.prompt_ids(7, m.shape.vocab, 4)
+    outs = []
+    with EnvScope([("DPUF_GEN_KEEP_TILES", "12")]):
+        for persistent in (1, 0):
+            e = eng_mod.CudaTransformerEngine(m, {"persistent": persistent})
+            e.reset_cache()
+            e.forward_batch(prompt, 0)
+            outs.append([e.forward_token(t, len(prompt) + i) for i, t in enumerate((5, 17, 300))])
+            e.close()
+    for a, b in zip(*outs):
+        assert bitexact(a, b)
