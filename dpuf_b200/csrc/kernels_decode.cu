@@ -7,20 +7,19 @@
 // and the GEMV's exact block chain), so logits and ids are bit-identical to the reference's.
 //
 // Weight stream.  The weights never depend on activations, so a producer warp per CTA walks
-// the CTA's share of every projection of every layer and step in order, moving each stage
-// (the two 8-row groups' scales and nibbles of 32 blocks of one 16-row tile: 9216 bytes)
-// into a shared-memory ring with cp.async.bulk (TMA, no multicast) completed on an mbarrier.
-// It runs ahead across phase and grid barriers, bounded only by the ring, so HBM keeps
-// streaming while the consumers normalise, attend or wait at a barrier.
+// the CTA's share of every projection of every layer and step in order, moving stage s (32
+// blocks: the two 8-row groups' scales and nibbles, 4608 bytes per group) of two 16-row units
+// at a time into a shared-memory ring slot with cp.async.bulk (TMA, no multicast) completed
+// on an mbarrier.  It runs ahead across phase and grid barriers, bounded only by the ring,
+// so HBM keeps streaming while the consumers normalise, attend or wait at a barrier.
 //
-// Consumers (warps 0..8).  Per stage, eight MMA warps compute the exact integer block dots
-// with one m16n8k32 int8 MMA per 32-column block for all 16 rows (A = the tile's nibbles, rows
-// 0..7 from group 0 and 8..15 from group 1, low nibbles as k = 4t..4t+3 and high nibbles as
-// k = 16+4t..16+4t+3; B = the activation block with the same permutation in every column),
-// turn them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand
-// them to the chain warp through a 4-deep pair ring; the chain warp runs acc = fma(p, s, acc)
-// per row over the blocks in order (dpuf_avx2.c:2601-2640) and writes each 16-row unit's
-// outputs (with SwiGLU for gate/up pairs, and the running argmax for the LM head).
+// Consumers (warps 0..8).  Per slot, eight dot warps compute the exact integer block dots
+// sum_k u_k q_k with dp4a (lane = unit and row, four blocks each, independent chains), turn
+// them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand them to
+// the chain warp through a 3-deep pair ring; the chain warp runs acc = fma(p, s, acc) per row
+// over the blocks in order (dpuf_avx2.c:2601-2640), lanes 0..15 for unit A and 16..31 for
+// unit B, and writes the units' outputs (SwiGLU for a gate/up pair - gate tile in A, up tile
+// in B - and the running argmax for the LM head).
 // Between projections the consumers do the row-wide steps redundantly in every CTA (the
 // residual stream h lives in each CTA's shared memory): residual add, RMSNorm, activation
 // prep; attention runs on one CTA per (KV head, query-head pair).
@@ -43,17 +42,20 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kMmaWarps = 8;
+constexpr int kMmaWarps = 8;   // dot warps
 constexpr int kChainWarp = 8;
 constexpr int kProdWarp = 9;
 constexpr int kThreads = 320;
 constexpr int kConsumers = 288;     // warps 0..8
-constexpr int kSlotBytes = 9344;    // one stage: nibbles g0 | g1 (+32 pad) | scales g0 | g1
+// A ring slot holds stage s (32 blocks) of two 16-row units A and B; per unit: nibbles of
+// group 0 | group 1 (+32 pad) | scales of group 0 | group 1, and unit B starts 64 bytes past
+// a unit's size so that A's and B's lanes read different banks.
 constexpr int kNib1 = 4128, kSc0 = 8256, kSc1 = 8800;
+constexpr int kHalf = 9408;
+constexpr int kSlotBytes = 2 * kHalf;
 constexpr int kMaxRing = 24;
-constexpr int kNPs = 4;             // pair buffers between MMA warps and the chain warp
-constexpr int kPsRow = 20;          // float2 per block row (16 used): conflict-free stores
-constexpr int kPsBuf = 32 * kPsRow;
+constexpr int kNPs = 3;             // pair buffers between the dot warps and the chain warp
+constexpr int kPsBuf = 2 * 32 * 16; // float2 per pair buffer: [unit][block][row]
 constexpr int kBarConsumers = 1, kBarAttn = 2;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
@@ -78,10 +80,29 @@ DPUF_DEV bool mbar_try(uint64_t* b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-DPUF_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+// try_wait that lets the hardware park the thread until the phase completes or `ns` pass, so
+// a waiting thread takes no issue slots from the warps doing the work.
+DPUF_DEV bool mbar_try_for(uint64_t* b, unsigned parity, unsigned ns) {
+  unsigned ok;
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Weight bytes are read once per step, so their L2 lines are marked evict-first: the stream
+// then does not push the KV cache, the activations and the barrier words out of L2.
+DPUF_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+DPUF_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 DPUF_DEV unsigned long long globaltimer() {
@@ -96,14 +117,6 @@ DPUF_DEV unsigned ld_acquire(const unsigned* p) {
 }
 DPUF_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-DPUF_DEV void mma_s8_16832(int& d0, int& d1, int& d2, int& d3, int a0, int a1, int a2, int a3, int b0, int b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};\n"
-      : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-
 // Shared state of a CTA that is not in the dynamic buffer.
 struct DecShared {
   uint64_t full[kMaxRing], empty[kMaxRing], psf[kNPs], pse[kNPs];
@@ -115,28 +128,22 @@ struct DecShared {
 };
 
 // Bounded mbarrier wait by one thread: false (and the CTA abort flag and the error word set)
-// once kWaitNs pass, or when the CTA or another CTA has aborted.  The fast path is one
-// try_wait; the CTA flag is polled every 16 tries, the timer and the global error word every
-// 256.
+// once kWaitNs pass, or when the CTA or another CTA has aborted.  Each try parks the thread
+// for up to 20 us unless the phase completes first.
 DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, int* err) {
   if (mbar_try(b, parity)) return true;
-  unsigned long long t0 = 0;
-  for (int it = 1;; it++) {
-    if (mbar_try(b, parity)) return true;
-    if ((it & 15) == 0 && S.abort) return false;
-    if ((it & 255) == 0) {
-      if (*(volatile int*)err) {
-        S.abort = 1;
-        return false;
-      }
-      const unsigned long long now = globaltimer();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitNs) {
-        S.abort = 1;
-        atomicCAS(err, 0, 1);
-        return false;
-      }
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_for(b, parity, 20000u)) return true;
+    if (S.abort) return false;
+    if (*(volatile int*)err) {
+      S.abort = 1;
+      return false;
+    }
+    if (globaltimer() - t0 > kWaitNs) {
+      S.abort = 1;
+      atomicCAS(err, 0, 1);
+      return false;
     }
   }
 }
@@ -162,7 +169,6 @@ DPUF_DEV int kind_units(const DecodeArgs& A, int kind) {
     default: return (A.V + 15) >> 4;
   }
 }
-DPUF_DEV int kind_subs(int kind) { return kind == kGU ? 2 : 1; }
 
 DPUF_DEV Unit make_unit(const uint8_t* tiles, long long stride, int rows, int t, float* out) {
   Unit u;
@@ -205,21 +211,32 @@ struct Producer {
   int slot = 0;
   unsigned phase = 0;     // parity of the slot's current use
   long long issued = 0;
+  uint64_t policy = 0;    // L2 policy of the weight copies
 };
 
-DPUF_DEV bool produce_unit(const Unit& un, int n_blk, int n_st, unsigned char* ring, int n_ring, Producer& P,
-                           DecShared& S, int* err) {
+// Copies of stage s of unit un into the half-slot dst; returns the bytes.
+DPUF_DEV unsigned copy_stage(const Unit& un, int n_blk, int s, unsigned char* dst, uint64_t* bar, uint64_t pol) {
   const int groups = un.n_r > 8 ? 2 : 1;
+  const int kb = min(32, n_blk - s * 32);
+  for (int g = 0; g < groups; g++) {
+    const uint8_t* gp = un.tile + 16 + (size_t)g * n_blk * 144;
+    bulk_g2s(dst + (g ? kNib1 : 0), gp + (size_t)n_blk * 16 + (size_t)s * 4096, (unsigned)kb * 128, bar, pol);
+    bulk_g2s(dst + (g ? kSc1 : kSc0), gp + (size_t)s * 512, (unsigned)kb * 16, bar, pol);
+  }
+  return (unsigned)(groups * kb * 144);
+}
+
+DPUF_DEV bool produce_pair(const Unit& ua, const Unit& ub, bool has_b, int n_blk, int n_st, unsigned char* ring,
+                           int n_ring, Producer& P, DecShared& S, int* err) {
   for (int s = 0; s < n_st; s++) {
     if (!wait_bar(&S.empty[P.slot], P.phase ^ 1u, S, err)) return false;
     const int kb = min(32, n_blk - s * 32);
+    const unsigned bytes = (unsigned)(((ua.n_r > 8 ? 2 : 1) + (has_b ? (ub.n_r > 8 ? 2 : 1) : 0)) * kb * 144);
+    uint64_t* bar = &S.full[P.slot];
     unsigned char* dst = ring + (size_t)P.slot * kSlotBytes;
-    mbar_expect_tx(&S.full[P.slot], (unsigned)(groups * kb * 144));
-    for (int g = 0; g < groups; g++) {
-      const uint8_t* gp = un.tile + 16 + (size_t)g * n_blk * 144;
-      bulk_g2s(dst + (g ? kNib1 : 0), gp + (size_t)n_blk * 16 + (size_t)s * 4096, (unsigned)kb * 128, &S.full[P.slot]);
-      bulk_g2s(dst + (g ? kSc1 : kSc0), gp + (size_t)s * 512, (unsigned)kb * 16, &S.full[P.slot]);
-    }
+    mbar_expect_tx(bar, bytes);
+    copy_stage(ua, n_blk, s, dst, bar, P.policy);
+    if (has_b) copy_stage(ub, n_blk, s, dst + kHalf, bar, P.policy);
     P.issued++;
     if (++P.slot == n_ring) {
       P.slot = 0;
@@ -229,15 +246,35 @@ DPUF_DEV bool produce_unit(const Unit& un, int n_blk, int n_st, unsigned char* r
   return true;
 }
 
+// Units of a projection are consumed in pairs: for gate/up, (gate tile u, up tile u); for the
+// others, consecutive units of the CTA's range (the last one alone when the count is odd).
+DPUF_DEV void pair_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, int u_end, Unit& ua, Unit& ub,
+                      bool& has_b, int& step) {
+  if (kind == kGU) {
+    ua = unit_of(A, Ly, kind, u, 0);
+    ub = unit_of(A, Ly, kind, u, 1);
+    has_b = true;
+    step = 1;
+  } else {
+    ua = unit_of(A, Ly, kind, u, 0);
+    has_b = u + 1 < u_end;
+    ub = has_b ? unit_of(A, Ly, kind, u + 1, 0) : ua;
+    step = 2;
+  }
+}
+
 DPUF_DEV bool produce_phase(const DecodeArgs& A, const DecLayer* layers, int l, int kind, int& rot,
                             unsigned char* ring, int n_ring, Producer& P, DecShared& S) {
   int u0, n;
   take_range(kind_units(A, kind), rot, u0, n);
   const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
   const DecLayer& Ly = layers[kind == kLM ? 0 : l];
-  for (int u = u0; u < u0 + n; u++)
-    for (int sub = 0; sub < kind_subs(kind); sub++)
-      if (!produce_unit(unit_of(A, Ly, kind, u, sub), n_blk, n_st, ring, n_ring, P, S, A.err)) return false;
+  for (int u = u0, step = 1; u < u0 + n; u += step) {
+    Unit ua, ub;
+    bool has_b;
+    pair_of(A, Ly, kind, u, u0 + n, ua, ub, has_b, step);
+    if (!produce_pair(ua, ub, has_b, n_blk, n_st, ring, n_ring, P, S, A.err)) return false;
+  }
   return true;
 }
 
@@ -252,42 +289,39 @@ struct Consumer {
 
 DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
 
-// MMA warp w: blocks 4w..4w+3 of the stage; lane (g, t) keeps block 4w+t, rows g and g+8.
-DPUF_DEV void mma_stage(const unsigned char* st, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
-                        int warp, int lane, float2* buf) {
-  const int g = lane >> 2, t = lane & 3;
-  int k0 = 0, k8 = 0;
+// Dot warp w: blocks 4w..4w+3 of both units of the slot; lane = (unit lane/16, row lane%16)
+// computes dot = sum_k u_k q_k with dp4a on the row's nibbles (low nibbles against x bytes
+// 8c..8c+3, high against 8c+4..8c+7) and stores p = float(dot - xm), s = ws * xs (0, 0 for
+// a skipped block) at buf[unit][block][row].
+DPUF_DEV void dot_stage(const unsigned char* st, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
+                        bool has_b, int warp, int lane, float2* buf) {
+  const int unit = lane >> 4, r = lane & 15, g = r >> 3, ri = r & 7;
+  if (unit == 1 && !has_b) return;
+  const unsigned char* ut = st + unit * kHalf;
+  const unsigned char* wb = ut + (g ? kNib1 : 0) + ri * 4;
+  const unsigned char* sb = ut + (g ? kSc1 : kSc0) + ri * 2;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     const int bb = warp * 4 + j;
-    if (bb < kb) {  // warp-uniform
-      const int2 xw = *(const int2*)(xq + (b0 + bb) * 32 + t * 8);
-      const uint32_t w0 = *(const uint32_t*)(st + bb * 128 + t * 32 + g * 4);
-      const uint32_t w1 = *(const uint32_t*)(st + kNib1 + bb * 128 + t * 32 + g * 4);
-      int d0, d1, d2, d3;
-      mma_s8_16832(d0, d1, d2, d3, (int)(w0 & 0x0F0F0F0Fu), (int)(w1 & 0x0F0F0F0Fu), (int)((w0 >> 4) & 0x0F0F0F0Fu),
-                   (int)((w1 >> 4) & 0x0F0F0F0Fu), xw.x, xw.y);
-      if (t == j) {
-        k0 = d0;
-        k8 = d2;
-      }
+    if (bb < kb) {
+      const int4 xa = *(const int4*)(xq + (b0 + bb) * 32), xc = *(const int4*)(xq + (b0 + bb) * 32 + 16);
+      const uint32_t w0 = *(const uint32_t*)(wb + bb * 128), w1 = *(const uint32_t*)(wb + bb * 128 + 32);
+      const uint32_t w2 = *(const uint32_t*)(wb + bb * 128 + 64), w3 = *(const uint32_t*)(wb + bb * 128 + 96);
+      int dot = __dp4a((int)(w0 & 0x0F0F0F0Fu), xa.x, 0);
+      dot = __dp4a((int)((w0 >> 4) & 0x0F0F0F0Fu), xa.y, dot);
+      dot = __dp4a((int)(w1 & 0x0F0F0F0Fu), xa.z, dot);
+      dot = __dp4a((int)((w1 >> 4) & 0x0F0F0F0Fu), xa.w, dot);
+      dot = __dp4a((int)(w2 & 0x0F0F0F0Fu), xc.x, dot);
+      dot = __dp4a((int)((w2 >> 4) & 0x0F0F0F0Fu), xc.y, dot);
+      dot = __dp4a((int)(w3 & 0x0F0F0F0Fu), xc.z, dot);
+      dot = __dp4a((int)((w3 >> 4) & 0x0F0F0F0Fu), xc.w, dot);
+      const int b = b0 + bb;
+      const float bsc = xs[b];
+      float2 pr = make_float2(0.0f, 0.0f);
+      if (bsc > 0.0f)
+        pr = make_float2((float)(dot - xm[b]), __fmul_rn(f16bits_to_f32(*(const uint16_t*)(sb + bb * 16)), bsc));
+      buf[(unit * 32 + bb) * 16 + r] = pr;
     }
-  }
-  const int bb = warp * 4 + t;
-  if (bb < kb) {
-    const int b = b0 + bb;
-    const float bsc = xs[b];
-    const int xmb = xm[b];
-    float2 r0 = make_float2(0.0f, 0.0f), r8 = r0;
-    if (bsc > 0.0f) {
-      const float ws0 = f16bits_to_f32(*(const uint16_t*)(st + kSc0 + bb * 16 + g * 2));
-      const float ws8 = f16bits_to_f32(*(const uint16_t*)(st + kSc1 + bb * 16 + g * 2));
-      r0 = make_float2((float)(k0 - xmb), __fmul_rn(ws0, bsc));
-      r8 = make_float2((float)(k8 - xmb), __fmul_rn(ws8, bsc));
-    }
-    float2* o = buf + bb * kPsRow;
-    o[g] = r0;
-    o[g + 8] = r8;
   }
 }
 
@@ -302,77 +336,83 @@ DPUF_DEV void better(float& bv, int& bi, float v, int i) {
 DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, Consumer& C, unsigned char* ring,
                             int n_ring, const int8_t* xq, const float* xs, const int* xm, float2* ps, DecShared& S) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, r = lane & 15;
   int u0, n;
   take_range(kind_units(A, kind), C.rot, u0, n);
   const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
-  const int subs = kind_subs(kind);
-  float bv = -INFINITY, gate_v = 0.0f;
+  float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int u = u0; u < u0 + n; u++)
-    for (int sub = 0; sub < subs; sub++) {
-      const Unit un = unit_of(A, Ly, kind, u, sub);
-      float acc = 0.0f;
-      for (int s = 0; s < n_st; s++) {
-        const int kb = min(32, n_blk - s * 32);
-        float2* buf = ps + C.pb * kPsBuf;
-        if (warp < kMmaWarps) {
-          bool ok = true;
-          if (lane == 0)
-            ok = wait_bar(&S.full[C.slot], C.phase, S, A.err) && wait_bar(&S.pse[C.pb], C.pphase ^ 1u, S, A.err);
-          if (__shfl_sync(kFull, (int)ok, 0))
-            mma_stage(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, warp, lane, buf);
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&S.psf[C.pb]);
-            mbar_arrive(&S.empty[C.slot]);
-          }
-        } else {
-          bool ok = true;
-          if (lane == 0) ok = wait_bar(&S.psf[C.pb], C.pphase, S, A.err);
-          ok = __shfl_sync(kFull, (int)ok, 0);
-          if (ok && lane < kTileRows) {
-            int b = 0;
-            for (; b + 7 < kb; b += 8) {
-              float2 v[8];
+  for (int u = u0, step = 1; u < u0 + n; u += step) {
+    Unit ua, ub;
+    bool has_b;
+    pair_of(A, Ly, kind, u, u0 + n, ua, ub, has_b, step);
+    float acc = 0.0f;
+    for (int s = 0; s < n_st; s++) {
+      const int kb = min(32, n_blk - s * 32);
+      float2* buf = ps + C.pb * kPsBuf;
+      if (warp < kMmaWarps) {
+        bool ok = true;
+        if (lane == 0)
+          ok = wait_bar(&S.full[C.slot], C.phase, S, A.err) && wait_bar(&S.pse[C.pb], C.pphase ^ 1u, S, A.err);
+        if (__shfl_sync(kFull, (int)ok, 0))
+          dot_stage(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&S.psf[C.pb]);
+          mbar_arrive(&S.empty[C.slot]);
+        }
+      } else {
+        bool ok = true;
+        if (lane == 0) ok = wait_bar(&S.psf[C.pb], C.pphase, S, A.err);
+        ok = __shfl_sync(kFull, (int)ok, 0);
+        if (ok && (half == 0 || has_b)) {
+          const float2* col = buf + half * 32 * 16 + r;
+          int b = 0;
+          for (; b + 7 < kb; b += 8) {
+            float2 v[8];
 #pragma unroll
-              for (int q = 0; q < 8; q++) v[q] = buf[(b + q) * kPsRow + lane];
+            for (int q = 0; q < 8; q++) v[q] = col[(b + q) * 16];
 #pragma unroll
-              for (int q = 0; q < 8; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
-            }
-            for (; b < kb; b++) {
-              const float2 v = buf[b * kPsRow + lane];
-              acc = __fmaf_rn(v.x, v.y, acc);
-            }
+            for (int q = 0; q < 8; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&S.pse[C.pb]);
+          for (; b < kb; b++) {
+            const float2 v = col[b * 16];
+            acc = __fmaf_rn(v.x, v.y, acc);
+          }
         }
-        if (++C.slot == n_ring) {
-          C.slot = 0;
-          C.phase ^= 1u;
-        }
-        if (++C.pb == kNPs) {
-          C.pb = 0;
-          C.pphase ^= 1u;
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.pse[C.pb]);
       }
-      // ---- epilogue of the unit (chain warp, lane = row)
-      if (warp == kChainWarp && lane < un.n_r) {
-        const int row = un.row + lane;
-        if (kind == kGU) {
-          if (sub == 0) {
-            gate_v = acc;
+      if (++C.slot == n_ring) {
+        C.slot = 0;
+        C.phase ^= 1u;
+      }
+      if (++C.pb == kNPs) {
+        C.pb = 0;
+        C.pphase ^= 1u;
+      }
+    }
+    // ---- epilogue of the pair (chain warp: lanes 0..15 unit A's rows, 16..31 unit B's)
+    if (warp == kChainWarp) {
+      if (kind == kGU) {
+        const float up = __shfl_down_sync(kFull, acc, 16);
+        if (half == 0 && r < ua.n_r) {
+          const int row = ua.row + r;
+          A.s_out[row] = swiglu_one(acc, up, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et);
+        }
+      } else if (half == 0 || has_b) {
+        const Unit& un = half ? ub : ua;
+        if (r < un.n_r) {
+          if (kind == kLM) {
+            if (A.write_logits) un.out[r] = acc;
+            better(bv, bi, acc, un.row + r);
           } else {
-            un.out[lane] = swiglu_one(gate_v, acc, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et);
+            un.out[r] = acc;
           }
-        } else if (kind == kLM) {
-          if (A.write_logits) un.out[lane] = acc;
-          better(bv, bi, acc, row);
-        } else {
-          un.out[lane] = acc;
         }
       }
     }
+  }
   if (kind == kLM && warp == kChainWarp) {
     for (int m = 16; m; m >>= 1) {
       const float ov = __shfl_xor_sync(kFull, bv, m);
@@ -587,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
   if (warp == kProdWarp) {
     if (lane != 0) return;
     Producer P;
+    P.policy = l2_evict_first_policy();
     int rot = 0;
     bool ok = true;
     const int ev0 = kEvPerLayer * A.L + kEvPerStep;
