@@ -145,6 +145,8 @@ struct Engine {
   float *dec_o = nullptr, *dec_s = nullptr, *dec_d = nullptr;
   float2* dec_part = nullptr;
   unsigned* dec_bar = nullptr;  // [0] grid barrier counter, [1] error word
+  unsigned char* dec_prep = nullptr;  // prepped o-projection input (fused prep)
+  size_t dec_bar_bytes = 0;
 };
 
 // ------------------------------------------------------------------ helpers
@@ -292,7 +294,7 @@ void destroy_engine(Engine* e) {
   cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part);
   cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
   cudaFree(e->d_dec_layers); cudaFree(e->dec_o); cudaFree(e->dec_s); cudaFree(e->dec_d);
-  cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace);
+  cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace); cudaFree(e->dec_prep);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -531,9 +533,19 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
       (!tab.empty() &&
        cudaMemcpy(e->d_dec_layers, tab.data(), tab.size() * sizeof(DecLayer), cudaMemcpyHostToDevice)) ||
       cudaMalloc(&e->dec_o, (size_t)e->H * 4) || cudaMalloc(&e->dec_s, (size_t)e->I * 4) ||
-      cudaMalloc(&e->dec_d, (size_t)e->H * 4) || cudaMalloc(&e->dec_part, (size_t)sms * sizeof(float2)) ||
-      cudaMalloc(&e->dec_bar, 16))
+      cudaMalloc(&e->dec_d, (size_t)e->H * 4) || cudaMalloc(&e->dec_part, (size_t)sms * sizeof(float2)))
     return no("allocation");
+  // barrier counter and error word, zeroed before every launch
+  e->dec_bar_bytes = 16;
+  if (cudaMalloc(&e->dec_bar, e->dec_bar_bytes)) return no("allocation");
+  A.fuse_o = (e->hd % 64 == 0 && e->qd % 128 == 0 && A.kmax % 128 == 0) ? 1 : 0;
+  {
+    const size_t qo = align256((size_t)e->qd), so = align256((size_t)e->qd / 8);
+    if (cudaMalloc(&e->dec_prep, qo + 2 * so)) return no("allocation");
+    A.xo_q8 = (int8_t*)e->dec_prep;
+    A.xo_xs = (float*)(e->dec_prep + qo);
+    A.xo_xm = (int32_t*)(e->dec_prep + qo + so);
+  }
   A.layers = e->d_dec_layers;
   A.o_out = e->dec_o;
   A.s_out = e->dec_s;
@@ -568,7 +580,7 @@ cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool writ
   A.kv_k = e->slots[e->active].k;
   A.kv_v = e->slots[e->active].v;
   e->stage->pad[0] = 0;
-  CK(cudaMemsetAsync(e->dec_bar, 0, 16, e->stream));
+  CK(cudaMemsetAsync(e->dec_bar, 0, e->dec_bar_bytes, e->stream));
   CK(launch_decode(e->stream, A));
   CK(cudaMemcpyAsync(&e->stage->pad[0], A.err, 4, cudaMemcpyDeviceToHost, e->stream));
   return cudaSuccess;

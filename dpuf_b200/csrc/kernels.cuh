@@ -133,6 +133,10 @@ struct DecodeArgs {
   int first_id, pos0, n_steps, write_logits;
   int grid, n_ring;
   int stage_cap;      // columns per staged piece (decode_stage_cap)
+  // Fused o-projection prep: the attention items prep their output columns (needs
+  // head_dim % 64 == 0 and q_dim % 128 == 0); every CTA then copies the prepped vector.
+  int fuse_o;
+  int8_t* xo_q8;   float* xo_xs;  int32_t* xo_xm;   // [q_dim], [q_dim/32] x2
   unsigned long long* trace;  // optional per-CTA phase timestamps of the last step (null: off)
   int trace_per_cta;
 };

@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
   const int kv_len = *pos0_dev + m + 1;
   float* qs = sm;                   // [2][hd]
   float* sc = qs + 2 * hd;          // [2][max_seq]
-  float* kt = sc + 2 * kv.max_seq;  // [kAttnKeyTile][hd + 8]
+  float* kt = sc + attn_sc_floats(kv.max_seq);  // [kAttnKeyTile][hd + 8]
   for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) qs[i] = q[((size_t)m * n_q + qh0) * hd + i];
   attn_pair_body(qs, nh, hd, kv_len, kv.k + (size_t)kvh * kv.max_seq * hd, kv.v + (size_t)kvh * kv.max_seq * hd,
                  kv.max_seq, sc, kt, &sh, out + ((size_t)m * n_q + qh0) * hd, et, (int)threadIdx.x, CtaSync{});

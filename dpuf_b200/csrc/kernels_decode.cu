@@ -292,7 +292,29 @@ DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
 // Dot warp w: blocks 4w..4w+3 of both units of the slot; lane = (unit lane/16, row lane%16)
 // computes dot = sum_k u_k q_k with dp4a on the row's nibbles (low nibbles against x bytes
 // 8c..8c+3, high against 8c+4..8c+7) and stores p = float(dot - xm), s = ws * xs (0, 0 for
-// a skipped block) at buf[unit][block][row].
+// a skipped block) at buf[unit][block][row].  kAll: all four blocks exist (a full stage), so
+// the four independent computations are scheduled together without guards.
+DPUF_DEV float2 dot_pair(const unsigned char* wb, const unsigned char* sb, const int8_t* xq, const float* xs,
+                         const int* xm, int b0, int bb) {
+  const int4 xa = *(const int4*)(xq + (b0 + bb) * 32), xc = *(const int4*)(xq + (b0 + bb) * 32 + 16);
+  const uint32_t w0 = *(const uint32_t*)(wb + bb * 128), w1 = *(const uint32_t*)(wb + bb * 128 + 32);
+  const uint32_t w2 = *(const uint32_t*)(wb + bb * 128 + 64), w3 = *(const uint32_t*)(wb + bb * 128 + 96);
+  int d0 = __dp4a((int)(w0 & 0x0F0F0F0Fu), xa.x, 0);
+  int d1 = __dp4a((int)((w0 >> 4) & 0x0F0F0F0Fu), xa.y, 0);
+  d0 = __dp4a((int)(w1 & 0x0F0F0F0Fu), xa.z, d0);
+  d1 = __dp4a((int)((w1 >> 4) & 0x0F0F0F0Fu), xa.w, d1);
+  d0 = __dp4a((int)(w2 & 0x0F0F0F0Fu), xc.x, d0);
+  d1 = __dp4a((int)((w2 >> 4) & 0x0F0F0F0Fu), xc.y, d1);
+  d0 = __dp4a((int)(w3 & 0x0F0F0F0Fu), xc.z, d0);
+  d1 = __dp4a((int)((w3 >> 4) & 0x0F0F0F0Fu), xc.w, d1);
+  const int b = b0 + bb;
+  const float bsc = xs[b];
+  const float ws = f16bits_to_f32(*(const uint16_t*)(sb + bb * 16));
+  const float2 pr = make_float2((float)(d0 + d1 - xm[b]), __fmul_rn(ws, bsc));
+  return bsc > 0.0f ? pr : make_float2(0.0f, 0.0f);
+}
+
+template <bool kAll>
 DPUF_DEV void dot_stage(const unsigned char* st, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
                         bool has_b, int warp, int lane, float2* buf) {
   const int unit = lane >> 4, r = lane & 15, g = r >> 3, ri = r & 7;
@@ -300,28 +322,16 @@ DPUF_DEV void dot_stage(const unsigned char* st, const int8_t* xq, const float* 
   const unsigned char* ut = st + unit * kHalf;
   const unsigned char* wb = ut + (g ? kNib1 : 0) + ri * 4;
   const unsigned char* sb = ut + (g ? kSc1 : kSc0) + ri * 2;
+  float2* o = buf + (unit * 32 + warp * 4) * 16 + r;
+  if (kAll) {
+    float2 pr[4];
 #pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const int bb = warp * 4 + j;
-    if (bb < kb) {
-      const int4 xa = *(const int4*)(xq + (b0 + bb) * 32), xc = *(const int4*)(xq + (b0 + bb) * 32 + 16);
-      const uint32_t w0 = *(const uint32_t*)(wb + bb * 128), w1 = *(const uint32_t*)(wb + bb * 128 + 32);
-      const uint32_t w2 = *(const uint32_t*)(wb + bb * 128 + 64), w3 = *(const uint32_t*)(wb + bb * 128 + 96);
-      int dot = __dp4a((int)(w0 & 0x0F0F0F0Fu), xa.x, 0);
-      dot = __dp4a((int)((w0 >> 4) & 0x0F0F0F0Fu), xa.y, dot);
-      dot = __dp4a((int)(w1 & 0x0F0F0F0Fu), xa.z, dot);
-      dot = __dp4a((int)((w1 >> 4) & 0x0F0F0F0Fu), xa.w, dot);
-      dot = __dp4a((int)(w2 & 0x0F0F0F0Fu), xc.x, dot);
-      dot = __dp4a((int)((w2 >> 4) & 0x0F0F0F0Fu), xc.y, dot);
-      dot = __dp4a((int)(w3 & 0x0F0F0F0Fu), xc.z, dot);
-      dot = __dp4a((int)((w3 >> 4) & 0x0F0F0F0Fu), xc.w, dot);
-      const int b = b0 + bb;
-      const float bsc = xs[b];
-      float2 pr = make_float2(0.0f, 0.0f);
-      if (bsc > 0.0f)
-        pr = make_float2((float)(dot - xm[b]), __fmul_rn(f16bits_to_f32(*(const uint16_t*)(sb + bb * 16)), bsc));
-      buf[(unit * 32 + bb) * 16 + r] = pr;
-    }
+    for (int j = 0; j < 4; j++) pr[j] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
+#pragma unroll
+    for (int j = 0; j < 4; j++) o[j * 16] = pr[j];
+  } else {
+    for (int j = 0; j < 4; j++)
+      if (warp * 4 + j < kb) o[j * 16] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
   }
 }
 
@@ -354,8 +364,12 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
         bool ok = true;
         if (lane == 0)
           ok = wait_bar(&S.full[C.slot], C.phase, S, A.err) && wait_bar(&S.pse[C.pb], C.pphase ^ 1u, S, A.err);
-        if (__shfl_sync(kFull, (int)ok, 0))
-          dot_stage(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
+        if (__shfl_sync(kFull, (int)ok, 0)) {
+          if (kb == 32)
+            dot_stage<true>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
+          else
+            dot_stage<false>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
+        }
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&S.psf[C.pb]);
@@ -367,17 +381,18 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
         ok = __shfl_sync(kFull, (int)ok, 0);
         if (ok && (half == 0 || has_b)) {
           const float2* col = buf + half * 32 * 16 + r;
-          int b = 0;
-          for (; b + 7 < kb; b += 8) {
-            float2 v[8];
+          if (kb == 32) {
+            // all 32 pairs are loaded before the chain starts
+            float2 v[32];
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = col[(b + q) * 16];
+            for (int q = 0; q < 32; q++) v[q] = col[q * 16];
 #pragma unroll
-            for (int q = 0; q < 8; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
-          }
-          for (; b < kb; b++) {
-            const float2 v = col[b * 16];
-            acc = __fmaf_rn(v.x, v.y, acc);
+            for (int q = 0; q < 32; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
+          } else {
+            for (int b = 0; b < kb; b++) {
+              const float2 v = col[b * 16];
+              acc = __fmaf_rn(v.x, v.y, acc);
+            }
           }
         }
         __syncwarp();
@@ -424,13 +439,13 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
 }
 
 // Grid-wide barrier of the consumer threads (the producer never joins): arrive on a global
-// counter and wait, bounded, until every CTA has arrived `target / gridDim.x` times.
+// counter (release) and wait, bounded, until every CTA has arrived `target / gridDim.x` times
+// (acquire).
 DPUF_DEV void grid_sync(const DecodeArgs& A, unsigned& target, DecShared& S) {
   cbar();
   target += gridDim.x;
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(A.bar, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.bar) : "memory");
     unsigned long long t0 = 0;
     for (int it = 0; !S.abort; it++) {
       if ((int)(ld_acquire(A.bar) - target) >= 0) break;
@@ -465,27 +480,28 @@ DPUF_DEV void stage8(void* dst, const void* src, int bytes) {
     cp_async8_ca((unsigned char*)dst + i, (const unsigned char*)src + i);
 }
 
-// h[i] += res[i] for i < n_valid, h[i] += 0 beyond (rows pruned from the down projection);
-// res is staged into shared memory first (one round trip).
-DPUF_DEV void add_residual(float* h, const float* res, int H, int n_valid, float* stage) {
-  stage16(stage, res, min(H, n_valid) * 4);
+// Residual add, RMSNorm and activation prep of the result (add_and_rms_norm_f32 /
+// rms_norm_f32, dpuf_engine.c:225-272, then the prep).  res (optional, written by other CTAs;
+// rows >= n_valid add 0, as the pruned down projection's zero rows do), the gains and the
+// sign bytes are staged in one async round; all threads add the residual, then threads 0..7
+// run the eight "AVX lane" chains
+// over h after the residual add, 32 elements at a time.
+DPUF_DEV void norm_prep(float* h, const float* res, int n_valid, const float* w, int H, float eps,
+                        const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* sr = stage;          // [H] residual
+  float* sw = stage + H;      // [H] gains
+  uint8_t* sg = (uint8_t*)(stage + 2 * H);
+  if (res) stage16(sr, res, min(H, n_valid) * 4);
+  stage16(sw, w, H * 4);
+  if (signs) stage8(sg, signs, H / 8);
   cp_async_commit_wait_all();
   cbar();
-  for (int i = threadIdx.x; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? stage[i] : 0.0f);
-}
-
-// RMSNorm of h with gain w, then the activation prep of the result (signs) into x.  The gains
-// and sign bytes are copied into shared memory while threads 0..7 run the sum-of-squares
-// chains.
-DPUF_DEV void norm_prep(const float* h, const float* w, int H, float eps, const uint8_t* signs, int8_t* xq, float* xs,
-                        int* xm, float* stage, DecShared& S) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* sg = (uint8_t*)(stage + H);
-  stage16(stage, w, H * 4);
-  if (signs) stage8(sg, signs, H / 8);
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  if (tid < 8) S.lanes[tid] = sumsq_lane(h, H & ~7, tid);
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (res) {
+    for (int i = tid; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? sr[i] : 0.0f);
+    cbar();
+  }
+  if (tid < 8) S.lanes[tid] = sumsq_lane32(h, H & ~7, tid);
   cbar();
   if (tid == 0) S.inv = rms_inv(S.lanes, h, H, eps);
   cbar();
@@ -497,7 +513,7 @@ DPUF_DEV void norm_prep(const float* h, const float* w, int H, float eps, const 
     const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
     float v[8];
     const float4 h0 = *(const float4*)(h + col), h1 = *(const float4*)(h + col + 4);
-    const float4 w0 = *(const float4*)(stage + col), w1 = *(const float4*)(stage + col + 4);
+    const float4 w0 = *(const float4*)(sw + col), w1 = *(const float4*)(sw + col + 4);
     v[0] = __fmul_rn(__fmul_rn(h0.x, inv), w0.x);
     v[1] = __fmul_rn(__fmul_rn(h0.y, inv), w0.y);
     v[2] = __fmul_rn(__fmul_rn(h0.z, inv), w0.z);
@@ -508,6 +524,16 @@ DPUF_DEV void norm_prep(const float* h, const float* w, int H, float eps, const 
     v[7] = __fmul_rn(__fmul_rn(h1.w, inv), w1.w);
     prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, active ? c * 64 : 0, lane, xq, xs, xm);
   }
+}
+
+// Copies a prepped activation (codes, block scales, block sums of K columns; K % 128 == 0)
+// written by other CTAs into x.
+DPUF_DEV void load_prepped(const int8_t* q8, const float* bxs, const int32_t* bxm, int K, int8_t* xq, float* xs,
+                           int* xm) {
+  stage16(xq, q8, K);
+  stage16(xs, bxs, K / 8);
+  stage16(xm, bxm, K / 8);
+  cp_async_commit_wait_all();
 }
 
 // Activation prep of a vector written by other CTAs: pieces of `cap` columns (a multiple of
@@ -539,40 +565,69 @@ struct AttnSync {
   DPUF_DEV void operator()() const { named_sync(kBarAttn, kAttnThreads); }
 };
 
-// Attention items (KV head, query-head pair) of this CTA: QK-norm + RoPE of the pair's query
-// heads and of the KV head's key, K/V rows stored at `pos` (both pairs of a KV head store the
-// same bits), then attn_pair_body.  Threads 0..255 only.
+// Attention items (KV head, query-head pair) of this CTA: the pair's query heads, the KV
+// head's key and value, the QK-norm gains and the RoPE row are staged in one async round;
+// QK-norm + RoPE of the queries and the key, K/V rows stored at `pos` (both pairs of a KV head
+// store the same bits), then attn_pair_body.  With fuse_o the item also preps its output
+// columns (whole 64-column chunks) for the o projection.  Threads 0..255 only.
 DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, int pos, float* scratch,
                               DecShared& S) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int groups = A.nq / A.nkv, n_pairs = (groups + 1) / 2, hd = A.hd;
   float* qs = scratch;                       // [2][hd]
   float* sc = qs + 2 * hd;                   // [2][S]
-  float* kt = sc + 2 * (size_t)A.S;          // [kAttnKeyTile][hd + 8]
-  const float* cp = A.cos_tab + (size_t)pos * (hd >> 1);
-  const float* sp = A.sin_tab + (size_t)pos * (hd >> 1);
+  float* kt = sc + attn_sc_floats(A.S);      // [kAttnKeyTile][hd + 8]; inputs staged here first
+  float *kin = kt, *vin = kt + hd, *qn = kt + 2 * hd, *kn = kt + 3 * hd, *cs = kt + 4 * hd, *sn = cs + hd / 2;
   for (int it = blockIdx.x; it < A.nkv * n_pairs; it += gridDim.x) {
     const int kvh = it / n_pairs, pr = it % n_pairs;
     const int g0 = pr * 2, nh = (g0 + 1 < groups) ? 2 : 1, qh0 = kvh * groups + g0;
     float* kc = A.kv_k + ((size_t)l * A.nkv + kvh) * A.S * hd;
     float* vc = A.kv_v + ((size_t)l * A.nkv + kvh) * A.S * hd;
     named_sync(kBarAttn, kAttnThreads);  // scratch free (previous item done)
+    {
+      const int q4 = hd / 4;  // 16-byte pieces per vector
+      for (int i = tid; i < q4 * (nh + 2); i += kAttnThreads) {
+        const int v = i / q4, o = (i % q4) * 4;
+        const float* src = v < nh ? A.q + (size_t)(qh0 + v) * hd : (v == nh ? A.k : A.v) + (size_t)kvh * hd;
+        float* dst = v < nh ? qs + v * hd : (v == nh ? kin : vin);
+        cp_async16_cg(dst + o, src + o);
+      }
+      for (int i = tid; i < q4; i += kAttnThreads) {
+        if (Ly.q_norm) cp_async16_cg(qn + i * 4, Ly.q_norm + i * 4);
+        if (Ly.k_norm) cp_async16_cg(kn + i * 4, Ly.k_norm + i * 4);
+        if (i < q4 / 2) {
+          cp_async16_cg(cs + i * 4, A.cos_tab + (size_t)pos * (hd >> 1) + i * 4);
+          cp_async16_cg(sn + i * 4, A.sin_tab + (size_t)pos * (hd >> 1) + i * 4);
+        }
+      }
+      cp_async_commit_wait_all();
+    }
+    named_sync(kBarAttn, kAttnThreads);
     if (warp == 0) {
-      float* kb = kt;
-      for (int i = lane; i < hd; i += 32) kb[i] = __ldcg(A.k + (size_t)kvh * hd + i);
-      __syncwarp();
-      qk_norm_rope_warp(kb, Ly.k_norm, A.eps, hd, cp, sp, lane);
-      for (int i = lane; i < hd; i += 32) kc[(size_t)pos * hd + i] = kb[i];
+      qk_norm_rope_warp(kin, Ly.k_norm ? kn : nullptr, A.eps, hd, cs, sn, lane);
+      for (int i = lane; i < hd; i += 32) kc[(size_t)pos * hd + i] = kin[i];
     } else if (warp == 1) {
-      for (int i = lane; i < hd; i += 32) vc[(size_t)pos * hd + i] = __ldcg(A.v + (size_t)kvh * hd + i);
+      for (int i = lane; i < hd; i += 32) vc[(size_t)pos * hd + i] = vin[i];
     } else if (warp < 2 + nh) {
-      float* qv = qs + (warp - 2) * hd;
-      for (int i = lane; i < hd; i += 32) qv[i] = __ldcg(A.q + (size_t)(qh0 + warp - 2) * hd + i);
-      __syncwarp();
-      qk_norm_rope_warp(qv, Ly.q_norm, A.eps, hd, cp, sp, lane);
+      qk_norm_rope_warp(qs + (warp - 2) * hd, Ly.q_norm ? qn : nullptr, A.eps, hd, cs, sn, lane);
     }
     attn_pair_body(qs, nh, hd, pos + 1, kc, vc, A.S, sc, kt, &S.attn, A.att + (size_t)qh0 * hd, A.et, tid,
-                   AttnSync{});
+                   AttnSync{}, A.fuse_o != 0);
+    if (A.fuse_o) {
+      named_sync(kBarAttn, kAttnThreads);
+      const int n_ch = nh * hd / 64;
+      if (warp * 4 < n_ch) {
+        const int c = warp * 4 + (lane >> 3);
+        const bool active = c < n_ch;
+        const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = qs[col + k];
+        const int gcol = qh0 * hd + col;  // column of the o-projection input
+        prep_chunk_g8(v, Ly.signs[1] ? Ly.signs[1][gcol >> 3] : 0, active, qh0 * hd + (active ? c * 64 : 0), lane,
+                      A.xo_q8, A.xo_xs, A.xo_xm);
+      }
+    }
   }
 }
 
@@ -688,11 +743,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
     for (int l = 0; l < A.L; l++) {
       const DecLayer& Ly = layers[l];
       const int lb = kEvPerLayer * l;
-      if (l > 0) {
-        add_residual(h, A.d_out, H, A.keep_down * kTileRows, stage);
-        cbar();
-      }
-      norm_prep(h, Ly.attn_norm, H, A.eps, Ly.signs[0], xq, xs, xm, stage, S);
+      norm_prep(h, l > 0 ? A.d_out : nullptr, A.keep_down * kTileRows, Ly.attn_norm, H, A.eps, Ly.signs[0], xq, xs,
+                xm, stage, S);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvNorm1);
       consume_phase(A, Ly, kQKV, C, ring, n_ring, xq, xs, xm, ps, S);
@@ -703,16 +755,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
       if (tid == 0) trace_at(A, step, lb + kEvAttn);
       grid_sync(A, target, S);
       if (tid == 0) trace_at(A, step, lb + kEvB2);
-      prep_global(A.att, A.qd, Ly.signs[1], xq, xs, xm, stage, A.stage_cap);
+      if (A.fuse_o)
+        load_prepped(A.xo_q8, A.xo_xs, A.xo_xm, A.qd, xq, xs, xm);
+      else
+        prep_global(A.att, A.qd, Ly.signs[1], xq, xs, xm, stage, A.stage_cap);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvPrepO);
       consume_phase(A, Ly, kO, C, ring, n_ring, xq, xs, xm, ps, S);
       if (tid == 0) trace_at(A, step, lb + kEvO);
       grid_sync(A, target, S);
       if (tid == 0) trace_at(A, step, lb + kEvB3);
-      add_residual(h, A.o_out, H, H, stage);
-      cbar();
-      norm_prep(h, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
+      norm_prep(h, A.o_out, H, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvNorm2);
       consume_phase(A, Ly, kGU, C, ring, n_ring, xq, xs, xm, ps, S);
@@ -727,11 +780,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
       grid_sync(A, target, S);
       if (tid == 0) trace_at(A, step, lb + kEvB5);
     }
-    if (A.L > 0) {
-      add_residual(h, A.d_out, H, A.keep_down * kTileRows, stage);
-      cbar();
-    }
-    norm_prep(h, A.out_norm, H, A.eps, A.lm_signs, xq, xs, xm, stage, S);
+    norm_prep(h, A.L > 0 ? A.d_out : nullptr, A.keep_down * kTileRows, A.out_norm, H, A.eps, A.lm_signs, xq, xs, xm,
+              stage, S);
     cbar();
     if (tid == 0) trace_at(A, step, sb + kEvNormF);
     consume_phase(A, layers[0], kLM, C, ring, n_ring, xq, xs, xm, ps, S);
@@ -769,13 +819,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
 
 // Shared memory of one CTA: ring | layer table | h | a union of {activation x + pair buffers
 // or staging area} and the attention scratch.  The staging area (after x) holds an embedding
-// group with its sign table (4.625 H bytes), norm gains with signs (4.125 H) or a piece of a
-// vector being prepped.
+// group with its sign table (4.625 H bytes), a residual with the norm gains and signs
+// (8.125 H) or a piece of a vector being prepped.
 size_t decode_x_bytes(const DecodeArgs& A) { return (size_t)A.kmax + (size_t)(A.kmax / 32) * 8; }
 size_t decode_uni_bytes(const DecodeArgs& A) {
   const size_t xb = decode_x_bytes(A);
   const size_t uni_x = xb + (size_t)kNPs * kPsBuf * sizeof(float2);
-  const size_t uni_stage = xb + (size_t)A.H * 4 + (size_t)A.H / 2 + (size_t)A.H / 8 + 64;
+  // residual + gains + signs of a norm, or a whole vector of kmax columns with its signs
+  const size_t uni_stage = xb + std::max((size_t)A.H * 8 + (size_t)A.H / 8, (size_t)A.kmax * 4 + (size_t)A.kmax / 8) + 128;
   const size_t uni_attn = attn_scratch_floats(A.hd, A.S) * sizeof(float);
   return std::max(std::max(uni_x, uni_stage), uni_attn);
 }

@@ -23,6 +23,21 @@ DPUF_DEV float sumsq_lane(const float* S, int n8, int j) {
   return acc;
 }
 
+// The same chain with 32 loads in flight per step (identical operation order).
+DPUF_DEV float sumsq_lane32(const float* S, int n8, int j) {
+  float acc = 0.0f;
+  int i = j;
+  for (; i + 248 < n8; i += 256) {
+    float v[32];
+#pragma unroll
+    for (int u = 0; u < 32; u++) v[u] = S[i + 8 * u];
+#pragma unroll
+    for (int u = 0; u < 32; u++) acc = __fmaf_rn(v[u], v[u], acc);
+  }
+  for (; i < n8; i += 8) acc = __fmaf_rn(S[i], S[i], acc);
+  return acc;
+}
+
 // inv = 1 / sqrt(ss / n + eps) with ss = split tree of the eight lane sums, then the n % 8
 // tail added in order.
 DPUF_DEV float rms_inv(const float* lanes, const float* S, int n, float eps) {
@@ -256,8 +271,11 @@ struct AttnShared {
   float inv_s[2], max_s[2];
 };
 
+// Scratch layout: qs [2][hd] | sc [2][max_seq] padded to a multiple of 4 | kt [kAttnKeyTile][hd+8]
+// (the key tile starts 16-byte aligned for the async copies).
+DPUF_HD size_t attn_sc_floats(int max_seq) { return 2 * (((size_t)max_seq + 3) & ~(size_t)3); }
 DPUF_HD size_t attn_scratch_floats(int hd, int max_seq) {
-  return (size_t)2 * hd + 2 * (size_t)max_seq + (size_t)kAttnKeyTile * (hd + 8);
+  return (size_t)2 * hd + attn_sc_floats(max_seq) + (size_t)kAttnKeyTile * (hd + 8);
 }
 
 // ------------------------------------------------------------------ async copies to shared
@@ -287,9 +305,9 @@ DPUF_DEV void stage_rows(float* dst, const float* src, int nk, int hd, int tid) 
 }
 
 template <typename Sync>
-DPUF_DEV void attn_pair_body(const float* qs, int nh, int hd, int kv_len, const float* kc, const float* vc,
+DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float* kc, const float* vc,
                              int max_seq, float* sc, float* kt, AttnShared* sh, float* out, const ExpfTable& et,
-                             int tid, Sync sync) {
+                             int tid, Sync sync, bool out_to_qs = false) {
   const int lane = tid & 31;
   const int kvs = hd + 8;  // padded smem row of a staged key
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
@@ -418,10 +436,14 @@ DPUF_DEV void attn_pair_body(const float* qs, int nh, int hd, int kv_len, const 
       acc[j] = a;
     }
   }
+  // (with out_to_qs the outputs also replace the queries, which are no longer read)
 #pragma unroll
   for (int j = 0; j < 2; j++) {
     const int o = tid + j * kAttnThreads;
-    if (o < nh * hd) out[o] = acc[j];
+    if (o < nh * hd) {
+      out[o] = acc[j];
+      if (out_to_qs) qs[o] = acc[j];
+    }
   }
 }
 
