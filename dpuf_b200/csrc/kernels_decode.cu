@@ -13,10 +13,11 @@
 // on an mbarrier.  It runs ahead across phase and grid barriers, bounded only by the ring,
 // so HBM keeps streaming while the consumers normalise, attend or wait at a barrier.
 //
-// Consumers (warps 0..8).  Per slot, eight dot warps compute the exact integer block dots
+// Consumers (warps 0..16).  Per slot, one of two teams of eight dot warps (teams take
+// alternate slots) computes the exact integer block dots
 // sum_k u_k q_k with dp4a (lane = unit and row, four blocks each, independent chains), turn
 // them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand them to
-// the chain warp through a 3-deep pair ring; the chain warp runs acc = fma(p, s, acc) per row
+// the chain warp through a 4-deep ring of pair buffers (named-barrier hand-off); the chain warp runs acc = fma(p, s, acc) per row
 // over the blocks in order (dpuf_avx2.c:2601-2640), lanes 0..15 for unit A and 16..31 for
 // unit B, and writes the units' outputs (SwiGLU for a gate/up pair - gate tile in A, up tile
 // in B - and the running argmax for the LM head).
@@ -42,11 +43,13 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kMmaWarps = 8;   // dot warps
-constexpr int kChainWarp = 8;
-constexpr int kProdWarp = 9;
-constexpr int kThreads = 320;
-constexpr int kConsumers = 288;     // warps 0..8
+constexpr int kTeamWarps = 8;                   // dot warps per team (one slot per team at a time)
+constexpr int kTeams = 1;                       // teams take alternate slots
+constexpr int kMmaWarps = kTeamWarps * kTeams;  // dot warps
+constexpr int kChainWarp = kMmaWarps;
+constexpr int kProdWarp = kMmaWarps + 1;
+constexpr int kThreads = (kMmaWarps + 2) * 32;  // 576
+constexpr int kConsumers = (kMmaWarps + 1) * 32;
 // A ring slot holds stage s (32 blocks) of two 16-row units A and B; per unit: nibbles of
 // group 0 | group 1 (+32 pad) | scales of group 0 | group 1, and unit B starts 64 bytes past
 // a unit's size so that A's and B's lanes read different banks.
@@ -54,8 +57,13 @@ constexpr int kNib1 = 4128, kSc0 = 8256, kSc1 = 8800;
 constexpr int kHalf = 9408;
 constexpr int kSlotBytes = 2 * kHalf;
 constexpr int kMaxRing = 24;
-constexpr int kNPs = 3;             // pair buffers between the dot warps and the chain warp
-constexpr int kPsBuf = 2 * 32 * 16; // float2 per pair buffer: [unit][block][row]
+constexpr int kNPs = 4;             // pair buffers between the dot warps and the chain warp
+constexpr int kPsRow = 34;          // float2 per row of a pair buffer: 32 blocks + pad (banks)
+constexpr int kPsBuf = 2 * 16 * kPsRow;  // float2 per pair buffer: [unit][row][block]
+// Named barriers: 1 consumers, 2 attention, then per pair buffer "filled" and "emptied".
+constexpr int kBarFilled = 3, kBarEmptied = kBarFilled + kNPs;
+static_assert(kBarEmptied + kNPs <= 16, "named barrier ids");
+constexpr int kHandoff = (kTeamWarps + 1) * 32;  // threads of a pair-buffer hand-off
 constexpr int kBarConsumers = 1, kBarAttn = 2;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
@@ -116,10 +124,11 @@ DPUF_DEV unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 DPUF_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+DPUF_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 // Shared state of a CTA that is not in the dynamic buffer.
 struct DecShared {
-  uint64_t full[kMaxRing], empty[kMaxRing], psf[kNPs], pse[kNPs];
+  uint64_t full[kMaxRing], empty[kMaxRing];
   AttnShared attn;
   float lanes[8];
   float inv;
@@ -283,8 +292,8 @@ struct Consumer {
   int slot = 0;
   unsigned phase = 0;  // ring parity
   int pb = 0;
-  unsigned pphase = 0; // pair-buffer parity
   int rot = 0;
+  unsigned item = 0;   // slots consumed so far (team of a slot = item % kTeams)
 };
 
 DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
@@ -292,7 +301,7 @@ DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
 // Dot warp w: blocks 4w..4w+3 of both units of the slot; lane = (unit lane/16, row lane%16)
 // computes dot = sum_k u_k q_k with dp4a on the row's nibbles (low nibbles against x bytes
 // 8c..8c+3, high against 8c+4..8c+7) and stores p = float(dot - xm), s = ws * xs (0, 0 for
-// a skipped block) at buf[unit][block][row].  kAll: all four blocks exist (a full stage), so
+// a skipped block) at buf[unit][row][block].  kAll: all four blocks exist (a full stage), so
 // the four independent computations are scheduled together without guards.
 DPUF_DEV float2 dot_pair(const unsigned char* wb, const unsigned char* sb, const int8_t* xq, const float* xs,
                          const int* xm, int b0, int bb) {
@@ -322,16 +331,16 @@ DPUF_DEV void dot_stage(const unsigned char* st, const int8_t* xq, const float* 
   const unsigned char* ut = st + unit * kHalf;
   const unsigned char* wb = ut + (g ? kNib1 : 0) + ri * 4;
   const unsigned char* sb = ut + (g ? kSc1 : kSc0) + ri * 2;
-  float2* o = buf + (unit * 32 + warp * 4) * 16 + r;
+  float2* o = buf + (unit * 16 + r) * kPsRow + warp * 4;
   if (kAll) {
     float2 pr[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) pr[j] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
-#pragma unroll
-    for (int j = 0; j < 4; j++) o[j * 16] = pr[j];
+    *(float4*)o = make_float4(pr[0].x, pr[0].y, pr[1].x, pr[1].y);
+    *(float4*)(o + 2) = make_float4(pr[2].x, pr[2].y, pr[3].x, pr[3].y);
   } else {
     for (int j = 0; j < 4; j++)
-      if (warp * 4 + j < kb) o[j * 16] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
+      if (warp * 4 + j < kb) o[j] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
   }
 }
 
@@ -361,51 +370,50 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
       const int kb = min(32, n_blk - s * 32);
       float2* buf = ps + C.pb * kPsBuf;
       if (warp < kMmaWarps) {
-        bool ok = true;
-        if (lane == 0)
-          ok = wait_bar(&S.full[C.slot], C.phase, S, A.err) && wait_bar(&S.pse[C.pb], C.pphase ^ 1u, S, A.err);
-        if (__shfl_sync(kFull, (int)ok, 0)) {
-          if (kb == 32)
-            dot_stage<true>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
-          else
-            dot_stage<false>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, warp, lane, buf);
-        }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&S.psf[C.pb]);
-          mbar_arrive(&S.empty[C.slot]);
+        if ((int)(C.item % kTeams) == warp / kTeamWarps) {
+          const int wt = warp % kTeamWarps;
+          bool ok = true;
+          if (lane == 0) ok = wait_bar(&S.full[C.slot], C.phase, S, A.err);
+          named_sync(kBarEmptied + C.pb, kHandoff);  // the chain is done with this pair buffer
+          if (__shfl_sync(kFull, (int)ok, 0)) {
+            if (kb == 32)
+              dot_stage<true>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, wt, lane, buf);
+            else
+              dot_stage<false>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, wt, lane, buf);
+          }
+          __syncwarp();
+          named_arrive(kBarFilled + C.pb, kHandoff);
+          if (lane == 0) mbar_arrive(&S.empty[C.slot]);
         }
       } else {
-        bool ok = true;
-        if (lane == 0) ok = wait_bar(&S.psf[C.pb], C.pphase, S, A.err);
-        ok = __shfl_sync(kFull, (int)ok, 0);
-        if (ok && (half == 0 || has_b)) {
-          const float2* col = buf + half * 32 * 16 + r;
+        named_sync(kBarFilled + C.pb, kHandoff);  // the dot warps filled this pair buffer
+        if (!S.abort && (half == 0 || has_b)) {
+          const float2* row = buf + (half * 16 + r) * kPsRow;
           if (kb == 32) {
-            // all 32 pairs are loaded before the chain starts
-            float2 v[32];
+            // all 32 pairs are loaded (two per 16-byte load) before the chain starts
+            float4 v[16];
 #pragma unroll
-            for (int q = 0; q < 32; q++) v[q] = col[q * 16];
+            for (int q = 0; q < 16; q++) v[q] = *(const float4*)(row + 2 * q);
 #pragma unroll
-            for (int q = 0; q < 32; q++) acc = __fmaf_rn(v[q].x, v[q].y, acc);
+            for (int q = 0; q < 16; q++) {
+              acc = __fmaf_rn(v[q].x, v[q].y, acc);
+              acc = __fmaf_rn(v[q].z, v[q].w, acc);
+            }
           } else {
             for (int b = 0; b < kb; b++) {
-              const float2 v = col[b * 16];
+              const float2 v = row[b];
               acc = __fmaf_rn(v.x, v.y, acc);
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.pse[C.pb]);
+        named_arrive(kBarEmptied + C.pb, kHandoff);
       }
+      C.item++;
       if (++C.slot == n_ring) {
         C.slot = 0;
         C.phase ^= 1u;
       }
-      if (++C.pb == kNPs) {
-        C.pb = 0;
-        C.pphase ^= 1u;
-      }
+      if (++C.pb == kNPs) C.pb = 0;
     }
     // ---- epilogue of the pair (chain warp: lanes 0..15 unit A's rows, 16..31 unit B's)
     if (warp == kChainWarp) {
@@ -644,6 +652,7 @@ DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
+  static_assert(kAttnThreads <= kTeamWarps * 32, "attention runs on the first team");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ DecShared S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -662,11 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
   if (tid == 0) {
     for (int i = 0; i < n_ring; i++) {
       mbar_init(&S.full[i], 1);
-      mbar_init(&S.empty[i], kMmaWarps);
-    }
-    for (int i = 0; i < kNPs; i++) {
-      mbar_init(&S.psf[i], kMmaWarps);
-      mbar_init(&S.pse[i], 1);
+      mbar_init(&S.empty[i], kTeamWarps);
     }
     S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -711,6 +716,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
   }
 
   // ---------------------------------------------------------------- consumer warps
+  // Pair-buffer hand-off on named barriers: the dot warps bar.sync "emptied" before filling a
+  // buffer and bar.arrive "filled"; the chain warp bar.syncs "filled" and bar.arrives
+  // "emptied".  The chain's first arrivals here free every buffer; the dot warps' syncs at the
+  // end take its last ones, so every barrier generation completes.
+  if (warp == kChainWarp)
+    for (int i = 0; i < kNPs; i++) named_arrive(kBarEmptied + i, kHandoff);
   Consumer C;
   unsigned target = 0;
   const int H = A.H;
@@ -813,6 +824,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
     if (A.L == 0) grid_sync(A, target, S);
     cbar();
   }
+  if (warp < kMmaWarps)
+    for (int i = 0; i < kNPs; i++) named_sync(kBarEmptied + i, kHandoff);
 }
 
 }  // namespace
