@@ -179,6 +179,32 @@ def gemv_roofline(hbm_peak: float, peak_kind: str):
             "traffic": traffic, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms.value * 1e3, 2)}
 
 
+def profile_value(name: str, key: str):
+    """A number recorded in a committed ncu summary under profiles/ (`key: value` line), or None."""
+    prof = REPO / "profiles" / name
+    if not prof.exists():
+        return None
+    for line in prof.read_text().splitlines():
+        if line.startswith(key + ":"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def decode_roofline(wbytes: int, step_s: float, hbm_peak: float, peak_kind: str):
+    """Roofline of the persistent decode kernel: one launch runs all timed steps, each step
+    streams the layer + LM-head weights once (the algorithmic bytes)."""
+    ratio = profile_value("decode_kernel_qwen3-0.6b_step.md", "traffic_per_algorithmic_byte")
+    achieved = wbytes / step_s / 1e9
+    return {"kernel": "decode_kernel (persistent, one step)", "bound": "hbm", "achieved": round(achieved, 1),
+            "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "traffic": int(wbytes * ratio) if ratio else None, "algorithmic_bytes_per_step": wbytes,
+            "us_per_step": round(step_s * 1e6, 2),
+            "traffic_note": "dram bytes per algorithmic byte from the 0.6B-shape ncu capture, times the 8B step bytes"}
+
+
 def cpu_baseline(m, prompt, n_steps: int, threads: int):
     from oracle import oracle as orc
 
@@ -297,10 +323,12 @@ def run_dpuf(args, world, rank, local):
     value = world * args.steps / (dev_ms * 1e-3)
 
     if args.no_extras:
+        persistent = eng.persistent_decode()[0]
         eng.close()
         if rank == 0:
             print(json.dumps({"metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s",
-                              "model": shape.name, "ms_per_step": round(dev_ms / args.steps, 4)}), flush=True)
+                              "model": shape.name, "ms_per_step": round(dev_ms / args.steps, 4),
+                              "persistent": persistent}), flush=True)
         return
     # ---- e2e through the drop-in C ABI with host buffers
     eng.reset_cache()
@@ -321,17 +349,22 @@ def run_dpuf(args, world, rank, local):
     e2e = world * args.steps / e2e_s
 
     roof = None
+    gemv = None
     cpu = None
+    persistent, why = eng.persistent_decode()
+    wbytes = shape.weight_bytes_per_token()
+    step_s = dev_ms * 1e-3 / args.steps
     if rank == 0:
-        roof = gemv_roofline(hbm_peak, peak_kind)
+        roof = decode_roofline(wbytes, step_s, hbm_peak, peak_kind) if persistent else None
+        gemv = gemv_roofline(hbm_peak, peak_kind)
+        if roof is None:
+            roof = gemv
         from oracle import oracle as orc
 
         cpu = cpu_baseline(m, prompt, n_steps=24, threads=min(32, orc.host_threads()))
     eng.close()
     if rank != 0:
         return
-    wbytes = shape.weight_bytes_per_token()
-    step_s = dev_ms * 1e-3 / args.steps
     clocks = clk.summary()
     line = {
         "metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
@@ -347,23 +380,26 @@ def run_dpuf(args, world, rank, local):
                           "frac": round(wbytes / step_s / 1e9 / hbm_peak, 4), "peak": hbm_peak,
                           "peak_kind": peak_kind},
         "roofline": roof,
+        "gemv_kernel": gemv if roof is not gemv else None,
+        "decode_path": "persistent cooperative kernel" if persistent else f"per-step kernels ({why})",
         "prefill": {"tok_per_s": round(32 / pp_s, 1), "what": "pp32 through dpuf_engine_forward_batch"},
-        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 1040,
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 if persistent else 1040,
                 "d2h_bytes_per_step": shape.vocab * 4,
-                "what": "dpuf_engine_forward_token per step: staging H2D, logits D2H, host argmax"},
+                "what": "dpuf_engine_forward_token per step: token id in, logits D2H, host argmax"},
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": None,
         "model_build_s": round(t_build, 1),
     }
-    launches = os.environ.get("DPUF_BENCH_LAUNCHES_PER_STEP")
-    line["gpu_launches"] = int(launches) * args.steps if launches else steps_launch_count(shape) * args.steps
+    # the timed decode_greedy call is one launch of the persistent kernel (all steps), or the
+    # per-step kernels of every step
+    line["gpu_launches"] = 1 if persistent else steps_launch_count(shape) * args.steps
     print(json.dumps(line), flush=True)
 
 
 def steps_launch_count(shape) -> int:
-    """Kernels of one decode step: embed; per layer norm, qkv gemv, qk_post, attention, prep,
-    o gemv, norm, gate/up gemv, swiglu_prep, down gemv; final norm, lm gemv, greedy advance."""
+    """Kernels of one per-step decode step: embed; per layer norm, qkv gemv, qk_post, attention,
+    prep, o gemv, norm, gate/up gemv, swiglu_prep, down gemv; final norm, lm gemv, greedy advance."""
     return 1 + 10 * shape.layers + 3
 
 
