@@ -179,6 +179,74 @@ def gemv_roofline(hbm_peak: float, peak_kind: str):
             "traffic": traffic, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms.value * 1e3, 2)}
 
 
+def run_op_configs(hbm_peak: float, peak_kind: str):
+    """Config 2 (isolated op): gate-shaped 12288x4096 and down-shaped 4096x12288 mode-12
+    matrices at M = 1 (GB/s of tile bytes) and M = 32 (dense-4-bit-equivalent TOP/s, 2*M*N*K),
+    kernel-only timing over copies that together exceed L2."""
+    import torch
+
+    from dpuf_b200 import engine, packer
+
+    lib = engine.cuda_lib()
+    for rows, cols, name in ((12288, 4096, "blk.0.mlp_in"), (4096, 12288, "blk.0.ffn_down.weight")):
+        w = packer.gen_normal_bf16(31, rows, (rows, cols), 0.02)
+        bv = packer.BlobView(packer.encode_mode12(w, name))
+        n_copies = 8  # 8 x 28.4 MB > 126 MB L2
+        hs = [engine.upload(bv) for _ in range(n_copies)]
+        arr = (ctypes.c_void_p * n_copies)(*hs)
+        x = torch.randn(32, cols, device="cuda")
+        if "down" in name:
+            x[x.abs() < 0.3] = 0.0
+        y = torch.empty(32, rows, device="cuda")
+        for M in (1, 32):
+            ms = ctypes.c_float()
+            rc = lib.dpuf_cuda_matmul_dev_timed(arr, n_copies, M, ctypes.c_void_p(x.data_ptr()),
+                                                ctypes.c_void_p(y.data_ptr()), 40,
+                                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                                ctypes.byref(ms))
+            if rc != 0:
+                raise RuntimeError(engine.last_error())
+            s = ms.value * 1e-3
+            line = {"config": "op", "shape": f"{rows}x{cols}", "seed_name": name, "M": M,
+                    "us_per_call": round(s * 1e6, 2), "tile_bytes": int(bv.tiles.nbytes)}
+            if M == 1:
+                gbs = bv.tiles.nbytes / s / 1e9
+                line.update({"GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4), "peak_kind": peak_kind})
+            else:
+                line.update({"TOP/s_4bit_equiv": round(2 * M * rows * cols / s / 1e12, 2),
+                             "GB/s": round(bv.tiles.nbytes / s / 1e9, 1),
+                             "kernel": "gemm_exact_kernel (dp4a on CUDA cores)"})
+            print(json.dumps(line), flush=True)
+        for h in hs:
+            engine.w12_free(h)
+
+
+def run_zone_config(hbm_peak: float, peak_kind: str, n_vec: int = 4096, za: int = 1000, margin: float = 0.8):
+    """Config 4 (Zone-A stress): the 151936x4096 head packed as output.weight, n_vec hidden
+    vectors N(0,1), half of them planted with beta * (dequantised head row i), i < 16Z."""
+    from dpuf_b200 import engine, packer
+
+    rows, cols = 151936, 4096
+    w = packer.gen_normal_bf16(41, 9, (rows, cols), 0.02)
+    bv = packer.BlobView(packer.encode_mode12(w, "output.weight"))
+    rng = np.random.default_rng(0)
+    planted = rng.integers(0, 16 * za, size=n_vec // 2).astype(np.int32)
+    x = rng.standard_normal((n_vec, cols)).astype(np.float32)
+    x[: n_vec // 2] += np.float32(5.0) * engine.embed(bv, planted)
+    engine.zone_head(bv, x[:64], za, margin)  # warm-up
+    ids, exits, ms = engine.zone_head(bv, x, za, margin)
+    s = ms * 1e-3
+    n_exit = int(exits.sum())
+    zone_bytes = bv.tiles.nbytes * min(16 * za, rows) / rows
+    bytes_total = n_exit * zone_bytes + (n_vec - n_exit) * bv.tiles.nbytes
+    print(json.dumps({"config": "zone_a", "head": f"{rows}x{cols}", "zone_tiles": za, "margin": margin,
+                      "vectors": n_vec, "vectors_per_s": round(n_vec / s, 1), "exit_fraction": round(n_exit / n_vec, 4),
+                      "planted_exit_fraction": round(float(exits[: n_vec // 2].mean()), 4),
+                      "planted_id_hits": round(float((ids[: n_vec // 2] == planted).mean()), 4),
+                      "GB/s": round(bytes_total / s / 1e9, 1), "frac_hbm": round(bytes_total / s / 1e9 / hbm_peak, 4),
+                      "peak_kind": peak_kind, "us_per_vector": round(s / n_vec * 1e6, 2)}), flush=True)
+
+
 def profile_value(name: str, key: str):
     """A number recorded in a committed ncu summary under profiles/ (`key: value` line), or None."""
     prof = REPO / "profiles" / name
@@ -413,17 +481,24 @@ def main():
                     help="8b = the benchmark workload; 0.6b = a small case for profiling")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the kernel-only GEMV roofline measurement (for profiling the GEMV)")
+    ap.add_argument("--op", action="store_true", help="config 2: isolated mode-12 matmuls at M = 1 and 32")
+    ap.add_argument("--zone", action="store_true", help="config 4: Zone-A LM head stress")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args.gpus)
-    if args.gemv_only:
+    if args.gemv_only or args.op or args.zone:
         import torch
 
         torch.cuda.set_device(local)
-        print(json.dumps(gemv_roofline(*peaks())), flush=True)
+        if args.gemv_only:
+            print(json.dumps(gemv_roofline(*peaks())), flush=True)
+        if args.op:
+            run_op_configs(*peaks())
+        if args.zone:
+            run_zone_config(*peaks())
         return
     try:
         if args.impl == "reference":

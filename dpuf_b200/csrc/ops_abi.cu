@@ -182,6 +182,66 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, in
   return 0;
 }
 
+// LM head with the Zone-A early exit on n_vec hidden vectors (already RMS-normalised), one at
+// a time as batch-1 decode steps, with the engine's step kernels (dpuf_engine.c:2091-2139):
+// prep, rows of tiles [0, Z), top-2 test over logits [0, min(16Z, V)), the remaining tiles
+// unless the test exits, logits [16Z, V) := -1e9 on exit, first-index argmax.  Z is clamped to
+// [256, n_tiles] as the engine does; margin <= 0 never exits.
+DPUF_EXPORT int32_t dpuf_cuda_zone_head(void* wh, int32_t n_vec, const float* x_dev, int32_t zone_tiles,
+                                        float margin, int32_t* ids_out, int32_t* exits_out, float* ms_out) {
+  W12Handle* h = (W12Handle*)wh;
+  if (!h || n_vec <= 0 || !x_dev || !ids_out || !exits_out) return -1;
+  const int V = h->w.rows, cols = h->w.cols, nt = h->w.n_tiles;
+  const int za = std::min(std::max(zone_tiles, 256), nt);
+  float *logits = nullptr, *b12 = nullptr;
+  int* flag = nullptr;
+  float2* part = nullptr;
+  unsigned* counter = nullptr;
+  int32_t *ids_d = nullptr, *exits_d = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int32_t rc = 0;
+  auto ck = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && rc == 0) {
+      dpuf::set_error(std::string(what) + ": " + cudaGetErrorString(e));
+      rc = -4;
+    }
+    return rc == 0;
+  };
+  if (ck(cudaMalloc(&logits, (size_t)V * 4), "cudaMalloc") && ck(cudaMalloc(&b12, 16), "cudaMalloc") &&
+      ck(cudaMalloc(&flag, 16), "cudaMalloc") && ck(cudaMalloc(&part, dpuf::kArgmaxBlocks * sizeof(float2)), "cudaMalloc") &&
+      ck(cudaMalloc(&counter, 64), "cudaMalloc") && ck(cudaMemset(counter, 0, 64), "cudaMemset") &&
+      ck(cudaMalloc(&ids_d, (size_t)n_vec * 4), "cudaMalloc") && ck(cudaMalloc(&exits_d, (size_t)n_vec * 4), "cudaMalloc") &&
+      ck(cudaEventCreate(&e0), "event") && ck(cudaEventCreate(&e1), "event")) {
+    const dpuf::Launch L{nullptr, false};
+    const dpuf::Act a{h->q8, h->xs, h->xm, cols};
+    ck(cudaEventRecord(e0, nullptr), "event");
+    for (int i = 0; i < n_vec && rc == 0; i++) {
+      dpuf::LinJobs J0 = {}, J1 = {};
+      J0.n = J1.n = 1;
+      J0.j[0] = {h->w, a, logits, V, 0, za};
+      J0.tile_prefix[1] = za;
+      J1.j[0] = {h->w, a, logits, V, za, nt};
+      J1.tile_prefix[1] = nt - za;
+      ck(dpuf::launch_prep(L, x_dev + (size_t)i * cols, cols, 1, cols, h->w.signs, a), "prep") &&
+          ck(dpuf::launch_gemv(L, J0, nullptr, &h->split), "zone gemv") &&
+          ck(dpuf::launch_zone_test(L, logits, std::min(za * dpuf::kTileRows, V), margin, flag, b12), "zone test") &&
+          ck(za < nt ? dpuf::launch_gemv(L, J1, flag, &h->split) : cudaSuccess, "rest gemv") &&
+          ck(dpuf::launch_zone_mask(L, logits, za * dpuf::kTileRows, V, flag), "zone mask") &&
+          ck(dpuf::launch_argmax(L, logits, V, part, counter, ids_d + i), "argmax") &&
+          ck(cudaMemcpyAsync(exits_d + i, flag, 4, cudaMemcpyDeviceToDevice, nullptr), "copy");
+    }
+    ck(cudaEventRecord(e1, nullptr), "event");
+    float ms = 0.0f;
+    if (ck(cudaEventSynchronize(e1), "sync") && ck(cudaEventElapsedTime(&ms, e0, e1), "event") && ms_out) *ms_out = ms;
+    ck(cudaMemcpy(ids_out, ids_d, (size_t)n_vec * 4, cudaMemcpyDeviceToHost), "copy");
+    ck(cudaMemcpy(exits_out, exits_d, (size_t)n_vec * 4, cudaMemcpyDeviceToHost), "copy");
+  }
+  cudaFree(logits); cudaFree(b12); cudaFree(flag); cudaFree(part); cudaFree(counter); cudaFree(ids_d); cudaFree(exits_d);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  return rc;
+}
+
 // Reference signature (dpuf_avx2.c:2678): host in, host out, synchronous.
 DPUF_EXPORT void dpuf_matmul_qr_hadamard4_packed_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
                                                      const float* x_in, const uint8_t* tensor_base,

@@ -50,6 +50,10 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_cuda_read_logits.argtypes = [_VP, _I32, _VP]
     lib.dpuf_cuda_set_option.restype = _I32
     lib.dpuf_cuda_set_option.argtypes = [_VP, ctypes.c_char_p, ctypes.c_int64]
+    lib.dpuf_cuda_zone_head.restype = _I32
+    lib.dpuf_cuda_zone_head.argtypes = [_VP, _I32, _VP, _I32, ctypes.c_float, _VP, _VP, _VP]
+    lib.dpuf_cuda_matmul_dev_timed.restype = _I32
+    lib.dpuf_cuda_matmul_dev_timed.argtypes = [_VP, _I32, _I32, _VP, _VP, _I32, _VP, _VP]
     lib.dpuf_cuda_decode_greedy.restype = _I32
     lib.dpuf_cuda_decode_greedy.argtypes = [_VP, _I32, _I32, _I32, _VP, _VP]
     lib.dpuf_cuda_persistent_decode.restype = _I32
@@ -206,6 +210,45 @@ def matmul(M: int, blob, x: np.ndarray) -> np.ndarray:
     if err:
         raise RuntimeError(err)
     return out
+
+
+def upload(blob):
+    """Device-resident copy of a mode-12 matrix (dpuf_cuda_w12_upload); free with w12_free."""
+    from . import model as mdl
+
+    lib = cuda_lib()
+    d = mdl.DpufWeightDesc(12, blob.rows, blob.cols, blob.n_tiles, blob.tiles.ctypes.data,
+                           blob.tile_offsets.ctypes.data, None, blob.sign_bits.ctypes.data)
+    h = lib.dpuf_cuda_w12_upload(ctypes.byref(d))
+    if not h:
+        raise RuntimeError(f"dpuf_cuda_w12_upload failed: {last_error()}")
+    return h
+
+
+def w12_free(h) -> None:
+    cuda_lib().dpuf_cuda_w12_free(h)
+
+
+def zone_head(blob, x: np.ndarray, zone_tiles: int, margin: float):
+    """LM head with the Zone-A early exit on hidden vectors x[n][cols] (already normalised):
+    (ids, exits, device ms) from dpuf_cuda_zone_head."""
+    import torch
+
+    lib = cuda_lib()
+    h = upload(blob)
+    try:
+        xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+        n = x.shape[0]
+        ids = np.zeros(n, np.int32)
+        exits = np.zeros(n, np.int32)
+        ms = ctypes.c_float()
+        rc = lib.dpuf_cuda_zone_head(h, n, ctypes.c_void_p(xd.data_ptr()), int(zone_tiles), float(margin),
+                                     ids.ctypes.data, exits.ctypes.data, ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"dpuf_cuda_zone_head failed with rc={rc}: {last_error()}")
+        return ids, exits, float(ms.value)
+    finally:
+        w12_free(h)
 
 
 def embed(blob, ids: np.ndarray) -> np.ndarray:

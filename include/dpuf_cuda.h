@@ -70,6 +70,16 @@ DPUF_EXPORT void dpuf_cuda_w12_free(void* wh);
  * owned by the weight handle.  Returns 0 or a negative error. */
 DPUF_EXPORT int32_t dpuf_cuda_matmul_dev(void* wh, int32_t M, const float* x_dev, float* y_dev, void* stream);
 
+/* LM head with the Zone-A early exit (the engine's step, dpuf_engine.c:2091-2139) on n_vec
+ * hidden vectors x_dev[n_vec][cols] (DEVICE, already RMS-normalised), each as one batch-1
+ * step: rows of tiles [0, Z) (Z = zone_tiles clamped to [256, n_tiles]), exit when margin > 0
+ * and the top two logits of [0, min(16Z, V)) differ by >= margin, else the remaining tiles;
+ * on exit logits [16Z, V) = -1e9.  ids_out[n_vec] (host) = first-index argmax,
+ * exits_out[n_vec] (host) = 1 where the step exited; *ms_out (optional) = device time of all
+ * steps.  Returns 0 or a negative error. */
+DPUF_EXPORT int32_t dpuf_cuda_zone_head(void* wh, int32_t n_vec, const float* x_dev, int32_t zone_tiles,
+                                        float margin, int32_t* ids_out, int32_t* exits_out, float* ms_out);
+
 /* Kernel-only timing of the matmul (activation prep excluded): `iters` launches rotating over
  * n_handles uploaded weights, CUDA events on `stream`; *ms_out = mean ms per launch. */
 DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, int32_t M, const float* x_dev,

@@ -215,3 +215,23 @@ def cpu_model_string() -> str:
 
 def host_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def zone_a(logits: np.ndarray, za_tiles: int, margin: float):
+    """Zone-A exit test and masking on one row of fp32 logits, as dpuf_engine.c:2101-2135:
+    sequential top-2 with strict '>' over logits[0, min(16Z, V)) from -1e30, exit iff
+    margin > 0 and (b1 - b2) >= margin in fp32; on exit logits[16Z, V) = -1e9.  Z is the
+    already-clamped tile count.  Returns (exit, logits after masking, b1, b2)."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    n = min(za_tiles * 16, lg.size)
+    b1 = b2 = np.float32(-1e30)
+    for v in lg[:n].tolist():
+        v = np.float32(v)
+        if v > b1:
+            b2, b1 = b1, v
+        elif v > b2:
+            b2 = v
+    exit_ = bool(margin > 0.0 and np.float32(b1 - b2) >= np.float32(margin))
+    if exit_:
+        lg[za_tiles * 16:] = np.float32(-1e9)
+    return exit_, lg, float(b1), float(b2)

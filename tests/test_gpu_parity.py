@@ -191,3 +191,45 @@ def test_persistent_decode_with_pruned_down(eng_mod):
             e.close()
     for a, b in zip(*outs):
         assert bitexact(a, b)
+
+
+def test_zone_head_matches_oracle(eng_mod):
+    """Zone-A LM head (config 4 semantics) on planted and flat hidden vectors: exit decisions and
+    greedy ids equal the oracle's (mode-12 matmul + the reference's sequential top-2 test)."""
+    from dpuf_b200 import packer
+    from oracle import oracle as orc
+
+    rows, cols, za, margin = 40960, 512, 1000, 0.8
+    w = packer.gen_normal_bf16(21, 7, (rows, cols), 0.02)
+    bv = packer.BlobView(packer.encode_mode12(w, "output.weight"))
+    rng = np.random.default_rng(4)
+    planted = rng.integers(0, 16 * za, size=4).astype(np.int32)
+    x = rng.standard_normal((8, cols)).astype(np.float32)
+    x[:4] += np.float32(20.0) * eng_mod.embed(bv, planted)
+    ids, exits, _ = eng_mod.zone_head(bv, x, za, margin)
+    want_ids, want_exits = [], []
+    for i in range(x.shape[0]):
+        lg = orc.oracle_matmul(1, bv, x[i:i + 1])[0]
+        ex, masked, _, _ = orc.zone_a(lg, za, margin)
+        want_exits.append(int(ex))
+        want_ids.append(int(np.argmax(masked)))
+    assert exits.tolist() == want_exits
+    assert ids.tolist() == want_ids
+    assert 0 < sum(want_exits) < len(want_exits)  # both paths exercised
+    assert ids[:4].tolist() == planted.tolist()
+
+
+@pytest.mark.parametrize("rows,cols,name", [(12288, 4096, "blk.0.mlp_in"), (4096, 12288, "blk.0.ffn_down.weight")])
+@pytest.mark.parametrize("M", [1, 32])
+def test_config2_ops_match_oracle(eng_mod, rows, cols, name, M):
+    """The isolated-op configuration: gate-shaped and down-shaped matrices at M = 1 and 32; the
+    down-shaped input is dead-zoned like a SwiGLU output."""
+    from dpuf_b200 import packer
+    from oracle import oracle as orc
+
+    w = packer.gen_normal_bf16(31, rows, (rows, cols), 0.02)
+    bv = packer.BlobView(packer.encode_mode12(w, name))
+    x = np.random.default_rng(M).standard_normal((M, cols)).astype(np.float32)
+    if "down" in name:
+        x[np.abs(x) < 0.3] = 0.0
+    assert bitexact(eng_mod.matmul(M, bv, x), orc.oracle_matmul(M, bv, x))

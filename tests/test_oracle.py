@@ -62,3 +62,20 @@ def test_oracle_qwen3_0_6b_matches_reference():
     rec, _, _ = run_scenario(orc.OracleEngine, scn)
     assert rec["ids"] == g["ids"]
     assert rec["digests"] == g["digests"]
+
+
+def test_zone_a_restatement():
+    """Sequential top-2 of dpuf_engine.c:2101-2135: a repeated maximum is also the second place,
+    margin <= 0 never exits, exit masks everything past the zone."""
+    from oracle import oracle as orc
+
+    lg = np.zeros(64, np.float32)
+    lg[3] = 5.0
+    lg[40] = 9.0  # outside a 2-tile zone (32 rows)
+    ex, masked, b1, b2 = orc.zone_a(lg, 2, 1.0)
+    assert ex and (b1, b2) == (5.0, 0.0)
+    assert np.all(masked[32:] == np.float32(-1e9)) and masked[3] == 5.0
+    lg[7] = 5.0
+    assert not orc.zone_a(lg, 2, 1.0)[0]
+    lg[7] = 0.0
+    assert not orc.zone_a(lg, 2, 0.0)[0]
