@@ -42,6 +42,7 @@ cudaError_t configure_kernels() {
   if ((e = configure_mode12_kernels()) != cudaSuccess) return e;
   if ((e = configure_layer_kernels()) != cudaSuccess) return e;
   if ((e = configure_decode_kernel()) != cudaSuccess) return e;
+  if ((e = configure_gemm_tc_kernels()) != cudaSuccess) return e;
   return configure_attn_kernels();
 }
 
@@ -136,6 +137,9 @@ struct Engine {
   std::map<StepKey, cudaGraphExec_t> graphs;
   // last step
   int last_rows = 0, last_zone_used = 0;
+
+  bool use_tc_gemm = true;  // M > 1 projections on the tensor cores (else the dp4a GEMM)
+  int* d_tc_err = nullptr;  // error word of the tensor-core GEMM
 
   // persistent batch-1 decode (kernels_decode.cu)
   bool dec_ok = false, use_persistent = true;
@@ -291,7 +295,7 @@ void destroy_engine(Engine* e) {
   cudaFree(e->gate); cudaFree(e->up); cudaFree(e->logits);
   cudaFree(e->prep_q8); cudaFree(e->prep_xs); cudaFree(e->prep_xm);
   cudaFree(e->d_ids); cudaFree(e->d_hist); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
-  cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part);
+  cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part); cudaFree(e->d_tc_err);
   cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
   cudaFree(e->d_dec_layers); cudaFree(e->dec_o); cudaFree(e->dec_s); cudaFree(e->dec_d);
   cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace); cudaFree(e->dec_prep);
@@ -318,7 +322,8 @@ LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1)
 
 cudaError_t run_linear(const Engine* e, const Launch& Lc, const LinJobs& J, int M, const int* skip) {
   if (J.tile_prefix[J.n] == 0) return cudaSuccess;
-  return M == 1 ? launch_gemv(Lc, J, skip, &e->split) : launch_gemm_exact(Lc, J, M);
+  if (M == 1) return launch_gemv(Lc, J, skip, &e->split);
+  return e->use_tc_gemm ? launch_gemm_tc(Lc, J, M, e->d_tc_err) : launch_gemm_exact(Lc, J, M);
 }
 
 // Prep targets for weights sharing one input: identical sign tables share a prep slot
@@ -671,6 +676,14 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
     set_error(cudaGetErrorString(le));
     return -4;
   }
+  if (!persistent && n > 1 && e->use_tc_gemm) {
+    int tc_err = 0;
+    if (cudaMemcpy(&tc_err, e->d_tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
+    if (tc_err) {
+      set_error("tensor-core GEMM: an MMA wait timed out");
+      return -6;
+    }
+  }
   return persistent ? decode_status(e) : 0;
 }
 
@@ -799,6 +812,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
       cudaMalloc(&e->split.count, (size_t)kGemvMaxCtas * sizeof(unsigned)) ||
       cudaMemset(e->split.count, 0, (size_t)kGemvMaxCtas * sizeof(unsigned)))
     return fail("GEMV scratch");
+  if (cudaMalloc(&e->d_tc_err, 16) || cudaMemset(e->d_tc_err, 0, 16)) return fail("GEMM error word");
+  e->use_tc_gemm = env_int("DPUF_CUDA_TC_GEMM", 1) != 0;
   e->d_pos0 = e->d_ids + kMaxBatch;
   e->d_hist_step = e->d_hist + e->S;
   for (int i = 0; i < 3; i++)
@@ -1010,6 +1025,7 @@ DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t
   if (!strcmp(name, "pdl")) { e->use_pdl = value != 0; dpuf::drop_graphs(e); return 0; }
   if (!strcmp(name, "graphs")) { e->use_graphs = value != 0; dpuf::drop_graphs(e); return 0; }
   if (!strcmp(name, "persistent")) { e->use_persistent = value != 0; return 0; }
+  if (!strcmp(name, "tc_gemm")) { e->use_tc_gemm = value != 0; dpuf::drop_graphs(e); return 0; }
   return -1;
 }
 

@@ -52,6 +52,10 @@ size_t gemv_split_pairs_bytes(int max_cols);
 cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split);
 // M > 1: exact integer-dot GEMM on CUDA cores (reference order per (token,row)).
 cudaError_t launch_gemm_exact(const Launch& L, const LinJobs& jobs, int M);
+// M > 1 on the tensor cores (kernels_gemm_tc.cu): per-block int8 MMA into TMEM, then the same
+// fp32 chain; *err (device) becomes nonzero if an MMA wait gives up.
+cudaError_t configure_gemm_tc_kernels();
+cudaError_t launch_gemm_tc(const Launch& L, const LinJobs& jobs, int M, int* err);
 
 // ---- kernels_layer.cu
 struct PrepTarget {

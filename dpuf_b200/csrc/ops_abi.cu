@@ -1,5 +1,6 @@
 // ops_abi.cu - standalone mode-12 ops behind the reference's exported signatures
 // (dpuf_kernels.h:267-277; dpuf_avx2.c:2678-2783) and device-resident weight handles.
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -21,6 +22,7 @@ struct W12Handle {
   float* xs = nullptr;
   int32_t* xm = nullptr;
   GemvSplit split{};  // GEMV scratch (units shared by CTAs)
+  int* tc_err = nullptr;  // error word of the tensor-core GEMM
 };
 
 constexpr int kOpChunk = kMaxBatch;  // tokens per launch of the standalone matmul
@@ -79,9 +81,16 @@ bool alloc_act(W12Handle* h) {
   if ((e = cudaMalloc(&h->split.pairs, gemv_split_pairs_bytes((int)cols))) != cudaSuccess ||
       (e = cudaMalloc(&h->split.acc, (size_t)kGemvMaxCtas * kTileRows * sizeof(float))) != cudaSuccess ||
       (e = cudaMalloc(&h->split.count, (size_t)kGemvMaxCtas * sizeof(unsigned))) != cudaSuccess ||
-      (e = cudaMemset(h->split.count, 0, (size_t)kGemvMaxCtas * sizeof(unsigned))) != cudaSuccess)
+      (e = cudaMemset(h->split.count, 0, (size_t)kGemvMaxCtas * sizeof(unsigned))) != cudaSuccess ||
+      (e = cudaMalloc(&h->tc_err, 16)) != cudaSuccess || (e = cudaMemset(h->tc_err, 0, 16)) != cudaSuccess)
     return fail("cudaMalloc", e);
   return true;
+}
+
+// M > 1 on the tensor cores unless env DPUF_CUDA_TC_GEMM=0 (the exact dp4a GEMM).
+bool tc_gemm_enabled() {
+  const char* v = getenv("DPUF_CUDA_TC_GEMM");
+  return !v || atoi(v) != 0;
 }
 
 void free_handle(W12Handle* h) {
@@ -93,6 +102,7 @@ void free_handle(W12Handle* h) {
   cudaFree(h->split.pairs);
   cudaFree(h->split.acc);
   cudaFree(h->split.count);
+  cudaFree(h->tc_err);
   delete h;
 }
 
@@ -108,8 +118,20 @@ int32_t matmul_dev(W12Handle* h, int M, const float* x, float* y, cudaStream_t s
     J.n = 1;
     J.j[0] = {h->w, a, y + (size_t)m0 * h->w.rows, h->w.rows, 0, h->w.n_tiles};
     J.tile_prefix[1] = h->w.n_tiles;
-    e = mc == 1 ? launch_gemv(L, J, nullptr, &h->split) : launch_gemm_exact(L, J, mc);
+    e = mc == 1 ? launch_gemv(L, J, nullptr, &h->split)
+                : (tc_gemm_enabled() ? launch_gemm_tc(L, J, mc, h->tc_err) : launch_gemm_exact(L, J, mc));
     if (e != cudaSuccess) return fail("matmul", e), -4;
+  }
+  return 0;
+}
+
+// Error word of the tensor-core GEMM after the stream has been synchronised.
+int32_t matmul_status(W12Handle* h) {
+  int v = 0;
+  if (cudaMemcpy(&v, h->tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
+  if (v) {
+    set_error("tensor-core GEMM: an MMA wait timed out");
+    return -6;
   }
   return 0;
 }
@@ -163,7 +185,9 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, in
     J.n = 1;
     J.j[0] = {h->w, a, y_dev, h->w.rows, 0, h->w.n_tiles};
     J.tile_prefix[1] = h->w.n_tiles;
-    return M == 1 ? dpuf::launch_gemv(L, J, nullptr, &h->split) : dpuf::launch_gemm_exact(L, J, M);
+    return M == 1 ? dpuf::launch_gemv(L, J, nullptr, &h->split)
+                  : (dpuf::tc_gemm_enabled() ? dpuf::launch_gemm_tc(L, J, M, h->tc_err)
+                                             : dpuf::launch_gemm_exact(L, J, M));
   };
   for (int i = 0; i < 2 * n_handles; i++)
     if (launch(i) != cudaSuccess) return -4;
@@ -257,6 +281,7 @@ DPUF_EXPORT void dpuf_matmul_qr_hadamard4_packed_f32(int32_t M, int32_t rows, in
       dpuf::matmul_dev(h, M, dx, dy, nullptr) == 0) {
     cudaError_t e = cudaMemcpy(out, dy, (size_t)M * rows * 4, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) dpuf::set_error(cudaGetErrorString(e));
+    else if (M > 1) dpuf::matmul_status(h);
   }
   cudaFree(dx);
   cudaFree(dy);
