@@ -215,7 +215,7 @@ def run_op_configs(hbm_peak: float, peak_kind: str):
             else:
                 line.update({"TOP/s_4bit_equiv": round(2 * M * rows * cols / s / 1e12, 2),
                              "GB/s": round(bv.tiles.nbytes / s / 1e9, 1),
-                             "kernel": "gemm_exact_kernel (dp4a on CUDA cores)"})
+                             "kernel": "gemm_tc_kernel (tcgen05 kind::i8, TMEM)" if os.environ.get("DPUF_CUDA_TC_GEMM", "1") != "0" else "gemm_exact_kernel (dp4a)"})
             print(json.dumps(line), flush=True)
         for h in hs:
             engine.w12_free(h)

@@ -9,18 +9,22 @@
 // MMA per 32-column block so that every block's dot lands in its own TMEM columns; the fp32
 // chain then runs on CUDA cores in the reference's order.
 //
-// CTA = 128 weight rows (8 container tiles of one job) x N tokens (8, 16 or 32).  Per stage of
-// kStageBlocks blocks all 256 threads
-//   1. unpack the tiles' nibbles to u8 in shared memory, K-major without swizzle (core
-//      matrices of 8 rows x 16 bytes; the two 16-byte K halves LBO = 128 bytes apart, 8-row
-//      groups SBO = 256 bytes apart) - A; copy the tokens' int8 codes the same way - B; the
-//      rows' fp16 block scales and the tokens' block scales and sums;
+// CTA = 128 weight rows (8 container tiles of one job) x N tokens (8, 16 or 32).  The raw
+// bytes of each stage (kStageBlocks blocks: nibbles and fp16 scales of 16 (tile, group)
+// pairs) arrive by TMA bulk copies into a double buffer requested one stage ahead.  Per stage
+// all 256 threads
+//   1. unpack the nibbles to u8 in shared memory, K-major without swizzle (core matrices of
+//      8 rows x 16 bytes; the two 16-byte K halves LBO = 128 bytes apart, 8-row groups
+//      SBO = 256 bytes apart) - A; copy the tokens' int8 codes the same way with cp.async - B;
+//      and the tokens' block scales and sums;
 //   2. thread 0 issues one tcgen05.mma per block (M=128, N, K=32) into TMEM columns
-//      [j*N, j*N+N) and commits them to an mbarrier;
+//      [j*N, j*N+N) of the stage's half of TMEM and commits them to an mbarrier;
 //   3. after the (bounded) wait, warp w reads TMEM lanes 32*(w%4).. (its rows), columns of its
 //      half of the tokens (tcgen05.ld 32x32b) and runs the chains of its (row, token) pairs.
-// Outputs are written after the last stage.  TMEM (256 columns) is allocated by warp 0 and
-// freed before exit, also when a wait gives up (it then sets the error word).
+// Steps 1 of stage s+1 run while the MMAs of stage s execute (A, B, scales and TMEM are double
+// buffered; raw weights are requested two stages ahead).  Outputs are written after the last
+// stage.  TMEM (2 x 8 x N columns) is allocated by warp 0 and freed before exit, also when a
+// wait gives up (it then sets the error word).
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -29,10 +33,10 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kTcThreads = 256;
+constexpr int kTcThreads = 288;   // warps 0..7 prepare stages and run the chains; warp 8 issues the MMAs
+constexpr int kWork = 256;
 constexpr int kTcRows = 128;
 constexpr int kStageBlocks = 8;
-constexpr int kTmemCols = 256;  // kStageBlocks * 32 tokens at most
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 DPUF_DEV unsigned su32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -93,12 +97,61 @@ struct TcArgs {
   int* err;         // set to 1 when an MMA wait gives up
 };
 
+DPUF_DEV bool wait_parity(uint64_t* bar, unsigned par, volatile int* abort_flag, int* err) {
+  const unsigned long long t0 = gtimer();
+  for (;;) {
+    unsigned ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(su32(bar)), "r"(par), "r"(20000u)
+        : "memory");
+    if (ok) return true;
+    if (*abort_flag || gtimer() - t0 > kTcWaitNs) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, 1);
+      return false;
+    }
+  }
+}
+
+DPUF_DEV void cp16_zfill(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+DPUF_DEV void cp4_zfill(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+
+// Raw stage bytes of one (tile, group): nibbles of kStageBlocks blocks, then their scales.
+constexpr int kRawTG = kStageBlocks * 128 + kStageBlocks * 16;
+constexpr int kRawBytes = (kTcRows / 8) * kRawTG;  // 16 (tile, group) pairs
+
+template <int N>
+struct TcLayout {  // shared memory of one CTA
+  static constexpr int kA = kStageBlocks * kTcRows * 32;  // one A buffer
+  static constexpr int kB = kStageBlocks * N * 32;        // one B buffer
+  static constexpr int kW = kTcRows * kStageBlocks * 2;   // row scales of a stage
+  static constexpr int kX = kStageBlocks * N * 4;         // xs or xm of a stage
+  static constexpr int raw = 0;                            // [2][kRawBytes]
+  static constexpr int a = raw + 2 * kRawBytes;           // [2][kA]
+  static constexpr int b = a + 2 * kA;                     // [2][kB]
+  static constexpr int w = b + 2 * kB;                     // [2][kW]
+  static constexpr int xs = w + 2 * kW;                    // [2][kX]
+  static constexpr int xm = xs + 2 * kX;                   // [2][kX]
+  static constexpr int bytes = xm + 2 * kX;
+  static constexpr int tmem_cols = 2 * kStageBlocks * N < 32 ? 32 : 2 * kStageBlocks * N;  // D double buffer
+};
+
 template <int N>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
+  using Lay = TcLayout<N>;
   extern __shared__ __align__(128) unsigned char sm[];
-  __shared__ __align__(8) uint64_t mma_bar;
+  __shared__ __align__(8) uint64_t mma_bar[2], raw_bar[2];
+  __shared__ const uint8_t* grp_base[kTcRows / 8];  // group data of each (tile, group), or null
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_sh;
+  __shared__ volatile int abort_sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // ---- this CTA's rows and tokens
@@ -109,22 +162,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   const int n_tiles_here = min(kTcRows / kTileRows, job.t_end - t_first);
   const int tok0 = blockIdx.y * N;
   const int cols = job.w.cols, n_blk = cols >> 5;
-
-  // ---- shared memory: A | B | ws | xs | xm per stage
-  unsigned char* sA = sm;                                        // [kStageBlocks][128 x 32 B]
-  unsigned char* sB = sA + kStageBlocks * kTcRows * 32;          // [kStageBlocks][N x 32 B]
-  uint16_t* sW = (uint16_t*)(sB + kStageBlocks * N * 32);        // [128][kStageBlocks]
-  float* sXs = (float*)(sW + kTcRows * kStageBlocks);            // [N][kStageBlocks]
-  int* sXm = (int*)(sXs + N * kStageBlocks);                     // [N][kStageBlocks]
+  const int n_stages = (n_blk + kStageBlocks - 1) / kStageBlocks;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_sh)),
-                 "r"(kTmemCols)
+                 "r"(Lay::tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  if (tid < kTcRows / 8) {  // (tile, group) bases; null where the group has no rows
+    const int t = tid >> 1, g = tid & 1;
+    const uint8_t* p = nullptr;
+    if (t < n_tiles_here) {
+      const int tt = t_first + t;
+      if (g * 8 < min(kTileRows, job.w.rows - tt * kTileRows))
+        p = job.w.tiles + job.w.toff[tt] + 16 + (size_t)g * n_blk * 144;
+    }
+    grp_base[tid] = p;
+  }
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&mma_bar)) : "memory");
+    for (int i = 0; i < 2; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&mma_bar[i])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&raw_bar[i])) : "memory");
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_sh = 0;
   }
@@ -132,9 +192,99 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base_sh;
-  cudaGridDependencySynchronize();
+
+  // warp 0 requests stage s's raw bytes into raw buffer s & 1 (one bulk copy per lane)
+  auto request_raw = [&](int s) {
+    const int buf = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
+    unsigned bytes = 0;
+    for (int tg = 0; tg < kTcRows / 8; tg++)
+      if (grp_base[tg]) bytes += (unsigned)kb * 144;
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&raw_bar[buf])), "r"(bytes)
+                   : "memory");
+    __syncwarp();
+    const int tg = lane >> 1, part = lane & 1;
+    const uint8_t* gb = grp_base[tg];
+    if (gb) {
+      unsigned char* dst = sm + Lay::raw + buf * kRawBytes + tg * kRawTG + (part ? kStageBlocks * 128 : 0);
+      const uint8_t* src = part ? gb + (size_t)b0 * 16 : gb + (size_t)n_blk * 16 + (size_t)b0 * 128;
+      const unsigned n = (unsigned)kb * (part ? 16 : 128);
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+          "l"(src), "r"(n), "r"(su32(&raw_bar[buf]))
+          : "memory");
+    }
+  };
 
   const Act& act = job.act;
+  const int xld = act.ld >> 5;
+  // all threads: the tokens' codes, block scales and block sums of stage s into buffer s & 1
+  // (async; waited by prepare)
+  auto request_act = [&](int s) {
+    if (tid >= kWork) return;
+    const int p = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
+    unsigned char* sB = sm + Lay::b + p * Lay::kB;
+    float* sXs = (float*)(sm + Lay::xs + p * Lay::kX);
+    int* sXm = (int*)(sm + Lay::xm + p * Lay::kX);
+    for (int i = tid; i < N * kStageBlocks * 2; i += kWork) {
+      const int h = i & 1, n = (i >> 1) % N, j = (i >> 1) / N;
+      const bool ok = j < kb && tok0 + n < P.M;
+      const int8_t* src = ok ? act.q8 + (size_t)(tok0 + n) * act.ld + (size_t)(b0 + j) * 32 + h * 16 : act.q8;
+      cp16_zfill(sB + j * (N * 32) + (n >> 3) * 256 + h * 128 + (n & 7) * 16, src, ok);
+    }
+    for (int i = tid; i < N * kStageBlocks; i += kWork) {
+      const int j = i / N, n = i % N;
+      const bool ok = j < kb && tok0 + n < P.M;
+      const size_t o = ok ? (size_t)(tok0 + n) * xld + b0 + j : 0;
+      cp4_zfill(sXs + i, act.xs + o, ok);
+      cp4_zfill(sXm + i, act.xm + o, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  // all threads: stage s's A (unpacked from its raw buffer) and row scales into buffer s & 1,
+  // then wait for its activation copies; the raw buffer is free again after the next barrier
+  auto prepare = [&](int s) {
+    if (tid >= kWork) return;
+    const int p = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
+    if (lane == 0) wait_parity(&raw_bar[p], (unsigned)((s >> 1) & 1), &abort_sh, P.err);
+    __syncwarp();
+    const unsigned char* rb = sm + Lay::raw + p * kRawBytes;
+    unsigned char* sA = sm + Lay::a + p * Lay::kA;
+    // one thread: rows 4q..4q+3 of a (tile, group), one block, one chunk (a 16-byte raw load)
+    for (int i = tid; i < (kTcRows / 4) * kStageBlocks * 4; i += kWork) {
+      const int c = i & 3, q = (i >> 2) & (kTcRows / 4 - 1), j = i >> 7;  // 32 row quads per block
+      const int tg = q >> 1, ri0 = (q & 1) * 4;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (j < kb && grp_base[tg]) w = *(const uint4*)(rb + tg * kRawTG + j * 128 + c * 32 + ri0 * 4);
+      unsigned char* dst = sA + j * (kTcRows * 32) + tg * 256 + (c >> 1) * 128 + ri0 * 16 + (c & 1) * 8;
+      *(uint2*)(dst + 0) = make_uint2(w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu);  // columns 8c..8c+7
+      *(uint2*)(dst + 16) = make_uint2(w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
+      *(uint2*)(dst + 32) = make_uint2(w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu);
+      *(uint2*)(dst + 48) = make_uint2(w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+    }
+    uint16_t* sW = (uint16_t*)(sm + Lay::w + p * Lay::kW);
+    for (int i = tid; i < kTcRows * kStageBlocks; i += kWork) {  // [row][block]
+      const int r = i >> 3, j = i & 7;
+      sW[i] = (j < kb && grp_base[r >> 3]) ? *(const uint16_t*)(rb + (r >> 3) * kRawTG + kStageBlocks * 128 + j * 16 +
+                                                                 (r & 7) * 2)
+                                           : (uint16_t)0;
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+  };
+
+  if (warp == 0) {  // weights do not depend on the previous kernel
+    request_raw(0);
+    if (n_stages > 1) request_raw(1);
+  }
+  cudaGridDependencySynchronize();
+  request_act(0);
+  if (n_stages > 1) request_act(1);
+  prepare(0);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0 && n_stages > 2) request_raw(2);  // raw buffer 0 is free again
+
   const int row = 32 * (warp & 3) + lane;  // TMEM lane = weight row of this thread's chains
   const int half = warp >> 2;              // which half of the N tokens
   constexpr int NH = N / 2;
@@ -143,121 +293,71 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   for (int i = 0; i < NH; i++) acc[i] = 0.0f;
   const uint32_t idesc = idesc_i8(N);
 
-  const int n_stages = (n_blk + kStageBlocks - 1) / kStageBlocks;
   for (int s = 0; s < n_stages; s++) {
-    const int b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
-    // ---- 1. A: unpack nibble words (row, block, chunk) to 8 bytes each
-    for (int i = tid; i < kTcRows * kStageBlocks * 4; i += kTcThreads) {
-      const int c = i & 3, r = (i >> 2) & (kTcRows - 1), j = i >> 9;  // 4 chunks x 128 rows per block
-      const int t = r >> 4, g = (r >> 3) & 1, ri = r & 7;
-      uint2 v = make_uint2(0u, 0u);
-      if (j < kb && t < n_tiles_here) {
-        const int tt = t_first + t;
-        const int n_r = min(kTileRows, job.w.rows - tt * kTileRows);
-        if (g * 8 + ri < n_r) {
-          const uint8_t* tp = job.w.tiles + job.w.toff[tt] + 16 + (size_t)g * n_blk * 144;
-          const uint32_t w = *(const uint32_t*)(tp + (size_t)n_blk * 16 + (size_t)(b0 + j) * 128 + c * 32 + ri * 4);
-          v = make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);  // columns 8c..8c+3, 8c+4..8c+7
-        }
-      }
-      *(uint2*)(sA + j * (kTcRows * 32) + (r >> 3) * 256 + (c >> 1) * 128 + (r & 7) * 16 + (c & 1) * 8) = v;
-    }
-    // ---- B: the tokens' codes, 16 bytes at a time
-    for (int i = tid; i < N * kStageBlocks * 2; i += kTcThreads) {
-      const int h = i & 1, n = (i >> 1) % N, j = (i >> 1) / N;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (j < kb && tok0 + n < P.M)
-        v = *(const uint4*)(act.q8 + (size_t)(tok0 + n) * act.ld + (size_t)(b0 + j) * 32 + h * 16);
-      *(uint4*)(sB + j * (N * 32) + (n >> 3) * 256 + h * 128 + (n & 7) * 16) = v;
-    }
-    // ---- row scales, token scales and sums
-    for (int i = tid; i < kTcRows * kStageBlocks; i += kTcThreads) {
-      const int r = i / kStageBlocks, j = i % kStageBlocks;
-      const int t = r >> 4, g = (r >> 3) & 1, ri = r & 7;
-      uint16_t w = 0;
-      if (j < kb && t < n_tiles_here) {
-        const int tt = t_first + t;
-        const int n_r = min(kTileRows, job.w.rows - tt * kTileRows);
-        if (g * 8 + ri < n_r)
-          w = *(const uint16_t*)(job.w.tiles + job.w.toff[tt] + 16 + (size_t)g * n_blk * 144 + (size_t)(b0 + j) * 16 +
-                                 ri * 2);
-      }
-      sW[r * kStageBlocks + j] = w;
-    }
-    for (int i = tid; i < N * kStageBlocks; i += kTcThreads) {
-      const int n = i / kStageBlocks, j = i % kStageBlocks;
-      float xs = 0.0f;
-      int xm = 0;
-      if (j < kb && tok0 + n < P.M) {
-        xs = act.xs[(size_t)(tok0 + n) * (act.ld >> 5) + b0 + j];
-        xm = act.xm[(size_t)(tok0 + n) * (act.ld >> 5) + b0 + j];
-      }
-      sXs[i] = xs;
-      sXm[i] = xm;
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
-    __syncthreads();
-
-    // ---- 2. one MMA per block, committed to the mbarrier
-    if (tid == 0) {
+    const int p = s & 1, kb = min(kStageBlocks, n_blk - s * kStageBlocks);
+    // ---- MMAs of stage s (buffers p) into TMEM columns p*8N + j*N
+    if (tid == kWork) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const unsigned char* sA = sm + Lay::a + p * Lay::kA;
+      const unsigned char* sB = sm + Lay::b + p * Lay::kB;
+      const uint64_t da0 = smem_desc(sA, 128, 256), db0 = smem_desc(sB, 128, 256);
       for (int j = 0; j < kb; j++) {
-        const uint64_t da = smem_desc(sA + j * (kTcRows * 32), 128, 256);
-        const uint64_t db = smem_desc(sB + j * (N * 32), 128, 256);
+        // the start-address field (bits 0..13, 16-byte units) advances by one block's bytes
+        const uint64_t da = da0 + (uint64_t)(j * (kTcRows * 32 / 16));
+        const uint64_t db = db0 + (uint64_t)(j * (N * 32 / 16));
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem + j * N),
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+                tmem + p * (kStageBlocks * N) + j * N),
             "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
             : "memory");
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(&mma_bar))
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       su32(&mma_bar[p]))
                    : "memory");
     }
-    // ---- 3. wait for the MMAs (bounded), then the chains
-    if (lane == 0) {
-      const unsigned par = (unsigned)(s & 1);
-      const unsigned long long t0 = gtimer();
-      for (;;) {
-        unsigned ok;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(su32(&mma_bar)), "r"(par), "r"(20000u)
-            : "memory");
-        if (ok) break;
-        if (abort_sh || gtimer() - t0 > kTcWaitNs) {
-          abort_sh = 1;
-          atomicCAS(P.err, 0, 1);
-          break;
-        }
-      }
-    }
-    __syncwarp();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (!abort_sh) {
-      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-      for (int j = 0; j < kb; j++) {
-        uint32_t d[NH];
-        tmem_ld<N>(tmem + lane_base + j * N + half * NH, d);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const float ws = f16bits_to_f32(sW[row * kStageBlocks + j]);
+    // ---- meanwhile: stage s+1 into buffers p^1
+    if (s + 1 < n_stages) prepare(s + 1);
+    // ---- chains of stage s (warps 0..7): all of the stage's TMEM columns are loaded before one
+    // wait, then the chains run
+    if (tid < kWork) {
+      if (lane == 0) wait_parity(&mma_bar[p], (unsigned)((s >> 1) & 1), &abort_sh, P.err);
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!abort_sh) {
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const uint16_t* wsp = (const uint16_t*)(sm + Lay::w + p * Lay::kW) + row * kStageBlocks;
+        const float* sXs = (const float*)(sm + Lay::xs + p * Lay::kX) + half * NH;
+        const int* sXm = (const int*)(sm + Lay::xm + p * Lay::kX) + half * NH;
+        uint32_t d[kStageBlocks][NH];
 #pragma unroll
-        for (int i = 0; i < NH; i++) {
-          const int n = half * NH + i;
-          const float xs = sXs[n * kStageBlocks + j];
-          const float p = (float)((int)d[i] - sXm[n * kStageBlocks + j]);
-          const float sc = __fmul_rn(ws, xs);
-          acc[i] = xs > 0.0f ? __fmaf_rn(p, sc, acc[i]) : acc[i];
+        for (int j = 0; j < kStageBlocks; j++)
+          if (j < kb) tmem_ld<N>(tmem + lane_base + p * (kStageBlocks * N) + j * N + half * NH, d[j]);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < kStageBlocks; j++) {
+          if (j < kb) {
+            const float ws = f16bits_to_f32(wsp[j]);
+            const float* xs = sXs + j * N;
+            const int* xm = sXm + j * N;
+#pragma unroll
+            for (int i = 0; i < NH; i++) {
+              const float pv = (float)((int)d[j][i] - xm[i]);
+              acc[i] = xs[i] > 0.0f ? __fmaf_rn(pv, __fmul_rn(ws, xs[i]), acc[i]) : acc[i];
+            }
+          }
         }
       }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();  // A, B and the TMEM columns are reused by the next stage
+    __syncthreads();  // buffers p and TMEM columns p are free; raw buffer (s+1)&1 is free
+    if (warp == 0 && s + 3 < n_stages) request_raw(s + 3);
+    if (s + 2 < n_stages) request_act(s + 2);
   }
 
   // ---- outputs
   const int t = row >> 4;
-  if (t < n_tiles_here) {
+  if (tid < kWork && t < n_tiles_here) {
     const int r_global = (t_first + t) * kTileRows + (row & 15);
     if (r_global < job.w.rows)
 #pragma unroll
@@ -267,16 +367,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
       }
   }
   cudaTriggerProgrammaticLaunchCompletion();
+  // after an abort, raw copies still in flight must land before the CTA exits
+  if (abort_sh && warp == 0 && lane == 0) {
+    const unsigned long long t0 = gtimer();
+    for (int q = n_stages - 2; q < n_stages; q++) {
+      if (q < 0) continue;
+      unsigned ok = 0;
+      while (!ok && gtimer() - t0 < kTcWaitNs)
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(su32(&raw_bar[q & 1])), "r"((unsigned)((q >> 1) & 1))
+            : "memory");
+    }
+  }
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Lay::tmem_cols)
+                 : "memory");
 }
 
 template <int N>
 size_t tc_smem_bytes() {
-  return (size_t)kStageBlocks * kTcRows * 32 + (size_t)kStageBlocks * N * 32 + (size_t)kTcRows * kStageBlocks * 2 +
-         (size_t)N * kStageBlocks * 8;
+  return (size_t)TcLayout<N>::bytes;
 }
 
 template <typename K, typename... Args>
@@ -294,9 +408,9 @@ cudaError_t launch_k(const Launch& L, K kernel, dim3 grid, dim3 block, size_t sm
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-// At least 96 KB of shared memory per CTA, so that at most two CTAs (2 x 256 TMEM columns)
-// share an SM and an allocation never waits on a third.
-constexpr size_t kTcMinSmem = 96 * 1024;
+// Shared memory per CTA at least 116 KB, so that one CTA holds an SM (its TMEM allocation is
+// up to 512 columns, the whole TMEM) and an allocation never waits on another CTA.
+constexpr size_t kTcMinSmem = 116 * 1024;
 
 }  // namespace
 
