@@ -114,20 +114,29 @@ def dist_setup(n_gpus: int):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
 
-def allreduce_max(x: float, world: int) -> float:
+def allreduce_max(x: float, world: int, device: str = "cuda") -> float:
+    """Max of x over the ranks of the default process group (device "cpu" for gloo)."""
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def dp_value(local_ms: float, steps: int, world: int, device: str = "cuda"):
+    """Data-parallel decode throughput: every rank decodes its own sequence for `steps` steps;
+    the job's time is the slowest rank's, the job's tokens are world * steps.  Returns
+    (tok/s of the whole job, the max time in ms)."""
+    dev_ms = allreduce_max(float(local_ms), world, device)
+    return world * steps / (dev_ms * 1e-3), dev_ms
 
 
 def barrier(world: int):
@@ -387,8 +396,7 @@ def run_dpuf(args, world, rank, local):
     if rc != 0:
         raise RuntimeError(engine.last_error())
     barrier(world)
-    dev_ms = allreduce_max(float(ms.value), world)
-    value = world * args.steps / (dev_ms * 1e-3)
+    value, dev_ms = dp_value(float(ms.value), args.steps, world)
 
     if args.no_extras:
         persistent = eng.persistent_decode()[0]
