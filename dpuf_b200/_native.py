@@ -38,6 +38,7 @@ CUDA_SOURCES = [
     "kernels_decode.cu",
     "ops_abi.cu",
     "noalloc.cu",
+    "sampling.cu",
 ]
 
 

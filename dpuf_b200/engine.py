@@ -73,6 +73,10 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_cuda_prepare_expf_table.restype = ctypes.c_int64
     lib.dpuf_cuda_matmul_noalloc.restype = _I32
     lib.dpuf_cuda_matmul_noalloc.argtypes = [_I32] * 4 + [_VP] * 6
+    lib.dpuf_cuda_sample_seed.restype = ctypes.c_uint64
+    lib.dpuf_cuda_sample_seed.argtypes = []
+    lib.dpuf_cuda_sample_token.restype = _I32
+    lib.dpuf_cuda_sample_token.argtypes = [_VP, _I32, ctypes.c_float, _VP]
     lib._dpuf_typed = True
     return lib
 
@@ -249,6 +253,28 @@ def zone_head(blob, x: np.ndarray, zone_tiles: int, margin: float):
         return ids, exits, float(ms.value)
     finally:
         w12_free(h)
+
+
+class Sampler:
+    """Token sampler of the engine's callers: the reference CLI's sample_token
+    (dpuf-cli.c:1997-2027) with its xorshift64* generator (dpuf-cli.c:1987-1995), whose state
+    this object carries (the reference keeps one process-global state, starting at
+    dpuf_cuda_sample_seed()).  temp <= 0 is greedy (first index of the maximum)."""
+
+    def __init__(self, state: int | None = None):
+        lib = cuda_lib()
+        self._state = ctypes.c_uint64(lib.dpuf_cuda_sample_seed() if state is None else state)
+
+    @property
+    def state(self) -> int:
+        return int(self._state.value)
+
+    def __call__(self, logits: np.ndarray, temp: float) -> int:
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        r = cuda_lib().dpuf_cuda_sample_token(lg.ctypes.data, lg.size, float(temp), ctypes.byref(self._state))
+        if r < 0:
+            raise ValueError("dpuf_cuda_sample_token: empty logits")
+        return int(r)
 
 
 def embed(blob, ids: np.ndarray) -> np.ndarray:

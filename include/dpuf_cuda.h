@@ -106,6 +106,16 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t co
 /* Builds or loads the glibc expf exception table; returns its entry count (host only). */
 DPUF_EXPORT int64_t dpuf_cuda_prepare_expf_table(void);
 
+/* ---- token sampling of the engine's callers (host code) ---- */
+/* Replaces the reference CLI's sample_token (dpuf-cli.c:1997-2027) with its generator
+ * rand_f32 (dpuf-cli.c:1987-1995), whose state is a process global there and the caller's
+ * `*rng` here (start it at dpuf_cuda_sample_seed(), the reference's initial state).
+ * temp <= 0: first index of the maximum (rng untouched); temp > 0: fp32 glibc expf
+ * probabilities of (l - max) * (1 / temp), one generator step, sequential double CDF.  Returns the
+ * id, or -1 for NULL logits, V <= 0, or NULL rng with temp > 0. */
+DPUF_EXPORT uint64_t dpuf_cuda_sample_seed(void);
+DPUF_EXPORT int32_t dpuf_cuda_sample_token(const float* logits, int32_t V, float temp, uint64_t* rng);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,3 +77,8 @@ gcc -shared -fopenmp -o "$OUT/libdpuf_avx2.so" \
     "$OUT/dpuf_avx2.o" "$OUT/dpuf_engine.o" "$OUT/dpuf_vision.o" -lm
 rm -f "$OUT"/*.o
 echo "build_ref: built $OUT/libdpuf_avx2.so"
+
+# The CLI's token sampler (file-static in dpuf-cli.c), exported by oracle/ref_sample_harness.c.
+gcc "${CFLAGS[@]}" -shared "$HERE/ref_sample_harness.c" -o "$OUT/libdpuf_ref_sample.so" \
+    -L"$OUT" -ldpuf_avx2 -Wl,-rpath,'$ORIGIN' -lm
+echo "build_ref: built $OUT/libdpuf_ref_sample.so"

@@ -11,6 +11,7 @@ Two CPU engines with the reference's C ABI are driven here:
 from __future__ import annotations
 
 import ctypes
+import ctypes.util
 import os
 import pathlib
 import subprocess
@@ -235,3 +236,60 @@ def zone_a(logits: np.ndarray, za_tiles: int, margin: float):
     if exit_:
         lg[za_tiles * 16:] = np.float32(-1e9)
     return exit_, lg, float(b1), float(b2)
+
+
+REF_SAMPLE_LIB = HERE / "_ref" / "libdpuf_ref_sample.so"
+SAMPLE_SEED = 88172645463325252  # initial g_rng, dpuf-cli.c:1987
+_LIBM = None
+
+
+def _expf(x: np.float32) -> np.float32:
+    """The host's glibc expf (the reference calls libm's expf, dpuf-cli.c:2015)."""
+    global _LIBM
+    if _LIBM is None:
+        _LIBM = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+        _LIBM.expf.restype = ctypes.c_float
+        _LIBM.expf.argtypes = [ctypes.c_float]
+    return np.float32(_LIBM.expf(float(x)))
+
+
+def rand_f32(state: int) -> tuple[float, int]:
+    """rand_f32 (dpuf-cli.c:1988-1995): one xorshift64 step of the state, then the top 24 bits
+    of state * 2685821657736338717 (mod 2^64) / 2^24.  Returns (value, new state)."""
+    m = (1 << 64) - 1
+    x = state
+    x ^= x >> 12
+    x = (x ^ (x << 25)) & m
+    x ^= x >> 27
+    return float(np.float32(((x * 2685821657736338717) & m) >> 40) / np.float32(16777216.0)), x
+
+
+def sample_token(logits: np.ndarray, temp: float, state: int) -> tuple[int, int]:
+    """sample_token (dpuf-cli.c:1997-2027).  temp <= 0: first index of the maximum.  Else
+    p_i = expf((l_i - max) * (1/temp)) in fp32, S their sequential double sum, r = u * S for
+    one generator step u, and the first i whose sequential double prefix sum reaches r (V-1 if
+    none).  np.cumsum is a sequential left-to-right accumulation.  Returns (id, new state)."""
+    lg = np.asarray(logits, dtype=np.float32)
+    t = np.float32(temp)
+    if t <= 0:
+        return int(np.argmax(lg)), state
+    mx = lg.max()
+    inv_t = np.float32(1.0) / t
+    z = (lg - mx) * inv_t  # fp32, elementwise
+    p = np.fromiter((_expf(v) for v in z.tolist()), dtype=np.float32, count=lg.size)
+    cdf = np.cumsum(p.astype(np.float64))
+    u, state = rand_f32(state)
+    r = u * float(cdf[-1])
+    hit = np.flatnonzero(cdf >= r)
+    return (int(hit[0]) if hit.size else lg.size - 1), state
+
+
+def ref_sample_token(logits: np.ndarray, temp: float, state: int) -> tuple[int, int]:
+    """The reference CLI's own sample_token (oracle/_ref/libdpuf_ref_sample.so)."""
+    lib = ctypes.CDLL(str(REF_SAMPLE_LIB))
+    lib.ref_sample_token.restype = ctypes.c_int32
+    lib.ref_sample_token.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p]
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    st = ctypes.c_uint64(state)
+    r = lib.ref_sample_token(lg.ctypes.data, lg.size, float(temp), ctypes.byref(st))
+    return int(r), int(st.value)
