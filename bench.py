@@ -14,7 +14,9 @@ A step is one greedy decode token at batch 1 (the reference CLI's decode loop, d
   cpu_baseline  the reference's own AVX2/OpenMP engine (built from its sources) on this host's
           cores, same model and prompt, a bounded number of decode steps
 Multi-GPU (torchrun, --gpus N): data parallel, one independent sequence per GPU (weak scaling);
-the time is the max over ranks.
+the time is the max over ranks.  With --tp the N ranks decode ONE sequence with tensor
+parallelism (every projection and the LM head split over all GPUs' CTAs, outputs exchanged
+through peer memory inside the persistent kernel; strong scaling).
 """
 from __future__ import annotations
 
@@ -362,8 +364,12 @@ def run_dpuf(args, world, rank, local):
     t_build = time.perf_counter() - t_build
     eng = engine.CudaTransformerEngine(m)
     lib = eng.lib
-    # each rank decodes its own sequence (data parallel); rank 0 uses the seed-0 prompt
-    prompt = mdl.prompt_ids(32, shape.vocab, rank)
+    tp = args.tp and world > 1
+    if tp:
+        eng.tp_attach(rank, world, engine.torch_all_gather())
+    # data parallel: each rank decodes its own sequence (rank 0 uses the seed-0 prompt); tensor
+    # parallel: all ranks decode the seed-0 sequence together
+    prompt = mdl.prompt_ids(32, shape.vocab, 0 if tp else rank)
     n_total = args.warmup + args.steps
     if 32 + 2 * n_total + 8 > shape.max_seq:
         raise SystemExit("steps + warmup exceed the 2304-position context")
@@ -397,6 +403,8 @@ def run_dpuf(args, world, rank, local):
         raise RuntimeError(engine.last_error())
     barrier(world)
     value, dev_ms = dp_value(float(ms.value), args.steps, world)
+    if tp:  # one sequence: the job's tokens are the steps
+        value /= world
 
     if args.no_extras:
         persistent = eng.persistent_decode()[0]
@@ -422,13 +430,15 @@ def run_dpuf(args, world, rank, local):
         nxt = int(np.argmax(lg))
         pos += 1
     e2e_s = allreduce_max(time.perf_counter() - t0, world)
-    e2e = world * args.steps / e2e_s
+    e2e = (1 if tp else world) * args.steps / e2e_s
 
     roof = None
     gemv = None
     cpu = None
     persistent, why = eng.persistent_decode()
     wbytes = shape.weight_bytes_per_token()
+    if tp:  # each GPU streams its share of the weights
+        wbytes //= world
     step_s = dev_ms * 1e-3 / args.steps
     if rank == 0:
         roof = decode_roofline(wbytes, step_s, hbm_peak, peak_kind) if persistent else None
@@ -445,12 +455,13 @@ def run_dpuf(args, world, rank, local):
     line = {
         "metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->f32",
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "int8xint4->f32",
         "data": "synthetic random-init weights ~N(0,0.02) (bf16-rounded, mode-12 packed), seed-0 prompt",
         "config": {"workload": f"{shape.name}-shape random-init mode-12, pp32 then batch-1 greedy decode",
                    "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab, "prompt": 32,
                    "batch_per_gpu": 1,
-                   "kv": "fp32", "parallelism": f"dp{world}" if world > 1 else "single",
+                   "kv": "fp32", "parallelism": (f"tp{world}" if tp else f"dp{world}") if world > 1 else "single",
                    "l2": "weights 4.26 GB > 126 MB L2: every step streams them from HBM"},
         "step_roofline": {"bytes_per_step": wbytes, "achieved_gbs": round(wbytes / step_s / 1e9, 1),
                           "frac": round(wbytes / step_s / 1e9 / hbm_peak, 4), "peak": hbm_peak,
@@ -491,6 +502,8 @@ def main():
                     help="only the kernel-only GEMV roofline measurement (for profiling the GEMV)")
     ap.add_argument("--op", action="store_true", help="config 2: isolated mode-12 matmuls at M = 1 and 32")
     ap.add_argument("--zone", action="store_true", help="config 4: Zone-A LM head stress")
+    ap.add_argument("--tp", action="store_true",
+                    help="with --gpus N > 1: tensor parallelism over the N GPUs (one sequence) instead of data parallel")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
     args = ap.parse_args()

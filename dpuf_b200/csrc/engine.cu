@@ -146,11 +146,24 @@ struct Engine {
   std::string dec_why;     // why the persistent kernel is not used
   DecodeArgs dec{};        // everything but the per-call fields
   DecLayer* d_dec_layers = nullptr;
-  float *dec_o = nullptr, *dec_s = nullptr, *dec_d = nullptr;
-  float2* dec_part = nullptr;
+  // tagged exchange vectors of the persistent kernel (q, k, v, o, gate/up, down; partials)
+  uint64_t *dec_q = nullptr, *dec_k = nullptr, *dec_v = nullptr, *dec_o = nullptr, *dec_s = nullptr,
+           *dec_d = nullptr, *dec_part = nullptr, *dec_dprep = nullptr;
+  unsigned dec_gen = 1;  // exchange generation of the next persistent launch's first phase
+  unsigned dec_dgen = 0; // down-input preps completed by earlier persistent launches
+  unsigned* dec_ctr = nullptr;  // completion counters [2]
   unsigned* dec_bar = nullptr;  // [0] grid barrier counter, [1] error word
   unsigned char* dec_prep = nullptr;  // prepped o-projection input (fused prep)
+  unsigned char* dec_dprep_plain = nullptr;  // prepped down-projection input (one GPU)
   size_t dec_bar_bytes = 0;
+  float* last_logits = nullptr;  // where the last step's logits are (per-step or persistent)
+
+  // tensor parallelism of the persistent decode (dpuf_cuda_tp_handle / dpuf_cuda_tp_attach)
+  int tp_rank = 0, tp_world = 1;     // world > 1 once attached
+  int tp_pending = 0;                // world announced by dpuf_cuda_tp_handle
+  unsigned char* tp_buf = nullptr;   // this rank's exchange buffer (exported by IPC handle)
+  size_t tp_bytes = 0;
+  void* tp_peer[kMaxTp] = {};        // other ranks' exchange buffers, opened
 };
 
 // ------------------------------------------------------------------ helpers
@@ -298,7 +311,12 @@ void destroy_engine(Engine* e) {
   cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part); cudaFree(e->d_tc_err);
   cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
   cudaFree(e->d_dec_layers); cudaFree(e->dec_o); cudaFree(e->dec_s); cudaFree(e->dec_d);
+  cudaFree(e->dec_q); cudaFree(e->dec_k); cudaFree(e->dec_v); cudaFree(e->dec_dprep); cudaFree(e->dec_ctr);
   cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace); cudaFree(e->dec_prep);
+  cudaFree(e->dec_dprep_plain);
+  for (void* p : e->tp_peer)
+    if (p) cudaIpcCloseMemHandle(p);
+  cudaFree(e->tp_buf);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -525,8 +543,10 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   A.cos_tab = e->cos_tab;
   A.sin_tab = e->sin_tab;
   A.et = e->et;
-  A.q = e->q; A.k = e->k; A.v = e->v; A.att = e->att; A.logits = e->logits; A.hist = e->d_hist;
+  A.att = e->att; A.logits = e->logits; A.hist = e->d_hist;
   A.grid = sms;
+  A.tp_rank = 0;
+  A.tp_world = 1;
   A.stage_cap = decode_stage_cap(A);
   size_t limit = 0;
   if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");
@@ -537,12 +557,28 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   if (cudaMalloc(&e->d_dec_layers, std::max<size_t>(1, tab.size()) * sizeof(DecLayer)) ||
       (!tab.empty() &&
        cudaMemcpy(e->d_dec_layers, tab.data(), tab.size() * sizeof(DecLayer), cudaMemcpyHostToDevice)) ||
-      cudaMalloc(&e->dec_o, (size_t)e->H * 4) || cudaMalloc(&e->dec_s, (size_t)e->I * 4) ||
-      cudaMalloc(&e->dec_d, (size_t)e->H * 4) || cudaMalloc(&e->dec_part, (size_t)sms * sizeof(float2)))
+      cudaMalloc(&e->dec_q, (size_t)e->qd * 8) || cudaMalloc(&e->dec_k, (size_t)e->kvd * 8) ||
+      cudaMalloc(&e->dec_v, (size_t)e->kvd * 8) || cudaMalloc(&e->dec_o, (size_t)e->H * 8) ||
+      cudaMalloc(&e->dec_s, (size_t)e->I * 8) || cudaMalloc(&e->dec_d, (size_t)e->H * 8) ||
+      cudaMalloc(&e->dec_part, (size_t)2 * sms * 16) ||
+      cudaMalloc(&e->dec_dprep, ((size_t)e->I / 4 + (size_t)e->I / 16) * 8) ||
+      cudaMalloc(&e->dec_ctr, 256))
     return no("allocation");
+  // tags start at 0; the first launch's generation is 1
+  if (cudaMemset(e->dec_q, 0, (size_t)e->qd * 8) || cudaMemset(e->dec_k, 0, (size_t)e->kvd * 8) ||
+      cudaMemset(e->dec_v, 0, (size_t)e->kvd * 8) || cudaMemset(e->dec_o, 0, (size_t)e->H * 8) ||
+      cudaMemset(e->dec_s, 0, (size_t)e->I * 8) || cudaMemset(e->dec_d, 0, (size_t)e->H * 8) ||
+      cudaMemset(e->dec_part, 0, (size_t)2 * sms * 16) ||
+      cudaMemset(e->dec_dprep, 0, ((size_t)e->I / 4 + (size_t)e->I / 16) * 8) ||
+      cudaMemset(e->dec_ctr, 0, 256))
+    return no("allocation");
+  e->dec_gen = 1;
+  e->dec_dgen = 0;
   // barrier counter and error word, zeroed before every launch
   e->dec_bar_bytes = 16;
   if (cudaMalloc(&e->dec_bar, e->dec_bar_bytes)) return no("allocation");
+  // the down projection's input is prepped in 64-column chunks and copied in 128-column pieces
+  if (e->I % 128) return no("intermediate size not a multiple of 128");
   A.fuse_o = (e->hd % 64 == 0 && e->qd % 128 == 0 && A.kmax % 128 == 0) ? 1 : 0;
   {
     const size_t qo = align256((size_t)e->qd), so = align256((size_t)e->qd / 8);
@@ -550,12 +586,22 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
     A.xo_q8 = (int8_t*)e->dec_prep;
     A.xo_xs = (float*)(e->dec_prep + qo);
     A.xo_xm = (int32_t*)(e->dec_prep + qo + so);
+    const size_t dq = align256((size_t)e->I), ds = align256((size_t)e->I / 8);
+    if (cudaMalloc(&e->dec_dprep_plain, dq + 2 * ds)) return no("allocation");
+    A.xd_q8 = (int8_t*)e->dec_dprep_plain;
+    A.xd_xs = (float*)(e->dec_dprep_plain + dq);
+    A.xd_xm = (int32_t*)(e->dec_dprep_plain + dq + ds);
   }
   A.layers = e->d_dec_layers;
+  A.q = e->dec_q;
+  A.k = e->dec_k;
+  A.v = e->dec_v;
   A.o_out = e->dec_o;
   A.s_out = e->dec_s;
   A.d_out = e->dec_d;
   A.part = e->dec_part;
+  A.dprep = e->dec_dprep;
+  A.ctr = e->dec_ctr;
   A.bar = e->dec_bar;
   A.err = (int*)(e->dec_bar + 1);
   if (env_int("DPUF_CUDA_TRACE_DECODE", 0)) {
@@ -584,9 +630,15 @@ cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool writ
   A.keep_down = (keep > 0 && keep < down_tiles) ? keep : down_tiles;
   A.kv_k = e->slots[e->active].k;
   A.kv_v = e->slots[e->active].v;
+  A.gen0 = e->dec_gen;
+  A.dgen0 = e->dec_dgen;
   e->stage->pad[0] = 0;
+  // the barrier counter and this GPU's error word (under tensor parallelism the error word is
+  // in the exchange buffer and stays set once a rank has failed)
   CK(cudaMemsetAsync(e->dec_bar, 0, e->dec_bar_bytes, e->stream));
   CK(launch_decode(e->stream, A));
+  e->dec_gen += (unsigned)n_steps * (unsigned)decode_phases(e->L);
+  e->dec_dgen += (unsigned)n_steps * (unsigned)e->L;
   CK(cudaMemcpyAsync(&e->stage->pad[0], A.err, 4, cudaMemcpyDeviceToHost, e->stream));
   return cudaSuccess;
 }
@@ -658,10 +710,12 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   if (err != cudaSuccess) return -4;
   e->last_zone_used = P.za > 0;
   e->last_rows = P.only_last == 2 ? 0 : lm_M;
+  e->last_logits = persistent ? e->dec.logits : e->logits;
   if (P.only_last != 2 && want_logits) {
     const size_t bytes = (size_t)lm_M * e->V * 4;
     if (lm_M == 1) {
-      if (cudaMemcpyAsync(e->h_logits, e->logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess) return -4;
+      if (cudaMemcpyAsync(e->h_logits, e->last_logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        return -4;
       if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
       memcpy(logits_out, e->h_logits, bytes);
     } else {
@@ -827,6 +881,49 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
 }
 
 }  // namespace
+// ------------------------------------------------------------------ tensor parallelism
+// Exchange buffer of one rank: the persistent kernel's tagged vectors, the logits and the
+// error word, which every rank stores into every rank's copy (zeroed: all tags 0).
+struct TpLayout {
+  size_t err, ctr, q, k, v, o, s, d, dprep, logits, part, total;
+};
+TpLayout tp_layout(const Engine* e, int world) {
+  TpLayout t{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  t.err = take(4);
+  t.ctr = take(8);
+  t.q = take((size_t)e->qd * 8);
+  t.k = take((size_t)e->kvd * 8);
+  t.v = take((size_t)e->kvd * 8);
+  t.o = take((size_t)e->H * 8);
+  t.s = take((size_t)e->I * 8);
+  t.d = take((size_t)e->H * 8);
+  t.dprep = take(((size_t)e->I / 4 + (size_t)e->I / 16) * 8);
+  t.logits = take((size_t)e->V * 4);
+  t.part = take((size_t)2 * world * e->dec.grid * 16);
+  t.total = off;
+  return t;
+}
+
+// What one rank publishes (DPUF_CUDA_TP_BLOB_BYTES): its IPC handle and what the other ranks
+// check before mapping it - same rank order, world, grid and model shape, and a GPU of its own
+// (ranks whose kernels wait on each other must never share a GPU: nothing guarantees that two
+// launches on one GPU run at the same time).
+struct TpBlob {
+  char magic[8];
+  int32_t rank, world, grid, L, H, I, V, qd, kvd, S;
+  uint64_t bytes;
+  char pci[32];  // PCI bus id of the rank's GPU
+  cudaIpcMemHandle_t handle;
+};
+static_assert(sizeof(TpBlob) <= DPUF_CUDA_TP_BLOB_BYTES, "tensor-parallel blob size");
+constexpr char kTpMagic[8] = {'D', 'P', 'U', 'F', 'T', 'P', '1', 0};
+
 }  // namespace dpuf
 
 using dpuf::Engine;
@@ -1008,6 +1105,7 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
   cudaEventDestroy(ev1);
   e->last_rows = 1;
   e->last_zone_used = 0;
+  e->last_logits = persistent ? e->dec.logits : e->logits;
   return rc;
 }
 
@@ -1015,7 +1113,8 @@ DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out)
   Engine* e = (Engine*)handle;
   if (!e || !out || row < 0 || row >= e->last_rows) return -1;
   cudaSetDevice(e->device);
-  if (cudaMemcpy(out, e->logits + (size_t)row * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
+  const float* src = e->last_logits ? e->last_logits : e->logits;
+  if (cudaMemcpy(out, src + (size_t)row * e->V, (size_t)e->V * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
   return 0;
 }
 
@@ -1047,6 +1146,112 @@ DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why) 
   if (!e) return -1;
   if (why) *why = e->dec_ok ? "" : e->dec_why.c_str();
   return e->dec_ok && e->use_persistent ? 1 : 0;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_tp_handle(void* handle, int32_t rank, int32_t world, uint8_t* blob_out) {
+  Engine* e = (Engine*)handle;
+  if (!e || !blob_out || world < 2 || world > dpuf::kMaxTp || rank < 0 || rank >= world) return -1;
+  if (e->tp_world > 1 || e->tp_buf) {
+    dpuf::set_error("tensor parallelism is already set up on this engine");
+    return -1;
+  }
+  if (!e->dec_ok) {
+    dpuf::set_error("tensor parallelism needs the persistent decode kernel: " + e->dec_why);
+    return -5;
+  }
+  // every rank must own units of the q/k/v, o and gate/up projections (see take_range)
+  if ((e->qd + 2 * e->kvd) / 16 < world || e->H / 16 < world || e->I / 16 < world) {
+    dpuf::set_error("tensor parallelism: the model has fewer 16-row tiles per projection than ranks");
+    return -1;
+  }
+  if (cudaSetDevice(e->device) != cudaSuccess) return -4;
+  const dpuf::TpLayout t = dpuf::tp_layout(e, world);
+  dpuf::TpBlob b{};
+  if (cudaDeviceGetPCIBusId(b.pci, (int)sizeof(b.pci) - 1, e->device) != cudaSuccess) return -4;
+  if (cudaMalloc(&e->tp_buf, t.total) != cudaSuccess || cudaMemset(e->tp_buf, 0, t.total) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&b.handle, e->tp_buf) != cudaSuccess) {
+    cudaFree(e->tp_buf);
+    e->tp_buf = nullptr;
+    dpuf::set_error("tensor parallelism: exchange buffer allocation or export failed");
+    return -4;
+  }
+  e->tp_bytes = t.total;
+  e->tp_rank = rank;
+  e->tp_pending = world;
+  memcpy(b.magic, dpuf::kTpMagic, 8);
+  b.rank = rank; b.world = world; b.grid = e->dec.grid; b.L = e->L; b.H = e->H; b.I = e->I; b.V = e->V;
+  b.qd = e->qd; b.kvd = e->kvd; b.S = e->S; b.bytes = t.total;
+  memset(blob_out, 0, DPUF_CUDA_TP_BLOB_BYTES);
+  memcpy(blob_out, &b, sizeof(b));
+  return 0;
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_tp_attach(void* handle, const uint8_t* blobs) {
+  Engine* e = (Engine*)handle;
+  if (!e || !blobs) return -1;
+  if (!e->tp_buf || e->tp_world > 1) {
+    dpuf::set_error("tensor parallelism: call dpuf_cuda_tp_handle once before dpuf_cuda_tp_attach");
+    return -1;
+  }
+  const int world = e->tp_pending;
+  for (int r = 0; r < world; r++) {
+    dpuf::TpBlob b;
+    memcpy(&b, blobs + (size_t)r * DPUF_CUDA_TP_BLOB_BYTES, sizeof(b));
+    if (memcmp(b.magic, dpuf::kTpMagic, 8) || b.rank != r || b.world != world || b.grid != e->dec.grid ||
+        b.L != e->L || b.H != e->H || b.I != e->I || b.V != e->V || b.qd != e->qd || b.kvd != e->kvd ||
+        b.S != e->S || b.bytes != e->tp_bytes) {
+      dpuf::set_error("tensor parallelism: rank " + std::to_string(r) +
+                      " published a different model, grid or rank order");
+      return -1;
+    }
+    for (int r2 = 0; r2 < r; r2++) {
+      dpuf::TpBlob b2;
+      memcpy(&b2, blobs + (size_t)r2 * DPUF_CUDA_TP_BLOB_BYTES, sizeof(b2));
+      if (!strncmp(b.pci, b2.pci, sizeof(b.pci))) {
+        dpuf::set_error("tensor parallelism: ranks " + std::to_string(r2) + " and " + std::to_string(r) +
+                        " are on the same GPU; every rank needs its own");
+        return -1;
+      }
+    }
+  }
+  if (cudaSetDevice(e->device) != cudaSuccess) return -4;
+  void* peer[dpuf::kMaxTp] = {};
+  for (int r = 0; r < world; r++) {
+    if (r == e->tp_rank) continue;
+    dpuf::TpBlob b;
+    memcpy(&b, blobs + (size_t)r * DPUF_CUDA_TP_BLOB_BYTES, sizeof(b));
+    if (cudaIpcOpenMemHandle(&peer[r], b.handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      for (void* p : peer)
+        if (p) cudaIpcCloseMemHandle(p);
+      cudaGetLastError();
+      dpuf::set_error("tensor parallelism: cannot map rank " + std::to_string(r) + "'s exchange buffer");
+      return -4;
+    }
+  }
+  const dpuf::TpLayout t = dpuf::tp_layout(e, world);
+  dpuf::DecodeArgs& A = e->dec;
+  unsigned char* base = e->tp_buf;
+  for (int r = 0; r < world; r++) {
+    e->tp_peer[r] = peer[r];
+    A.tp_delta[r] = r == e->tp_rank ? 0 : (long long)((unsigned char*)peer[r] - base);
+  }
+  A.tp_rank = e->tp_rank;
+  A.tp_world = world;
+  A.err = (int*)(base + t.err);
+  A.ctr = (unsigned*)(base + t.ctr);
+  A.q = (uint64_t*)(base + t.q);
+  A.k = (uint64_t*)(base + t.k);
+  A.v = (uint64_t*)(base + t.v);
+  A.o_out = (uint64_t*)(base + t.o);
+  A.s_out = (uint64_t*)(base + t.s);
+  A.d_out = (uint64_t*)(base + t.d);
+  A.dprep = (uint64_t*)(base + t.dprep);
+  A.logits = (float*)(base + t.logits);
+  A.part = (uint64_t*)(base + t.part);
+  e->tp_world = world;
+  e->dec_gen = 1;  // every rank starts at the same generation over zeroed buffers and counters
+  e->dec_dgen = 0;
+  return 0;
 }
 
 DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2) {

@@ -48,6 +48,7 @@ struct GemvSplit {
   unsigned* count;
 };
 constexpr int kGemvMaxCtas = 600;
+constexpr int kMaxTp = 8;  // tensor-parallel ranks of the persistent decode kernel
 size_t gemv_split_pairs_bytes(int max_cols);
 cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split);
 // M > 1: exact integer-dot GEMM on CUDA cores (reference order per (token,row)).
@@ -129,21 +130,48 @@ struct DecodeArgs {
   float* kv_k;    // active slot, [L][n_kv][S][hd]
   float* kv_v;
   ExpfTable et;
-  float *q, *k, *v, *att, *o_out, *s_out, *d_out, *logits;
-  float2* part;   // [grid] argmax partials
-  unsigned* bar;  // grid barrier counter, zero at launch
-  int* err;       // 0 at launch; 1 = mbarrier wait timed out, 2 = grid barrier timed out
+  // Vectors other CTAs (and ranks) produce are exchanged as tagged words: value bits in the low
+  // half, the producing phase's generation in the high half (one 64-bit store, so a reader sees
+  // the value and its tag together).  Readers wait on the tags of the elements they need, so
+  // no grid barrier is needed after a projection.
+  uint64_t *q, *k, *v, *o_out, *s_out, *d_out;  // [qd], [kvd] x2, [H], [I], [H]
+  uint64_t* part;  // argmax partials [2 (LM generation parity)][ctas of all ranks][value, index]
+  // the down projection's prepped input, produced by one CTA per 64-column chunk: [I/4] words
+  // of four int8 codes, then [I/32] block scales, then [I/32] block sums
+  uint64_t* dprep;
+  // one GPU: the same prepped input as plain codes, block scales and block sums, read after a
+  // grid barrier
+  int8_t* xd_q8;   float* xd_xs;  int32_t* xd_xm;   // [I], [I/32] x2
+  float* att;      // attention output (this CTA set only; read after a local grid barrier)
+  float* logits;   // [V] plain values, read by the host after the launch
+  unsigned gen0;   // generation of this launch's first phase (4 per layer + 1 per step)
+  unsigned dgen0;  // down-input preps (one per layer) completed before this launch
+  // Completion counters (never reset; wrap-safe): [0] += 1 per CTA of every rank and phase once
+  // its chain warp has stored the phase's outputs (so generation g is complete at (ctas of all
+  // ranks) * g), [1] the same per down-input prep.  Relaxed adds: a reader that finds a stale
+  // tag waits for the count, then re-copies what is still stale.
+  unsigned* ctr;
+  unsigned* bar;  // grid barrier counter (the barrier after attention), zero at launch
+  int* err;       // 0 at launch; 1 = mbarrier wait, 2 = grid barrier, 3 = exchange wait timed out
   int32_t* hist;  // [n_steps] greedy ids
   int first_id, pos0, n_steps, write_logits;
   int grid, n_ring;
-  int stage_cap;      // columns per staged piece (decode_stage_cap)
+  int stage_cap;      // columns per staged piece of a vector being prepped (decode_stage_cap)
   // Fused o-projection prep: the attention items prep their output columns (needs
   // head_dim % 64 == 0 and q_dim % 128 == 0); every CTA then copies the prepped vector.
   int fuse_o;
   int8_t* xo_q8;   float* xo_xs;  int32_t* xo_xm;   // [q_dim], [q_dim/32] x2
   unsigned long long* trace;  // optional per-CTA phase timestamps of the last step (null: off)
   int trace_per_cta;
+  // Tensor parallelism over tp_world processes (one GPU each; 1 = off).  Every projection's
+  // units are dealt over all ranks' CTAs (virtual CTA tp_rank * gridDim.x + blockIdx.x); the
+  // tagged vectors, the logits and the error word live in an exchange buffer that every rank
+  // maps, and producers store to every rank's copy (peer address = local + tp_delta[r]).
+  int tp_rank, tp_world;
+  long long tp_delta[kMaxTp];
 };
+// Exchange generations of one decode step (q/k/v, o, gate/up, down per layer; the LM head).
+DPUF_HD int decode_phases(int L) { return 4 * L + 1; }
 int decode_stage_cap(const DecodeArgs& A);
 int decode_trace_events(int L);
 size_t decode_smem_bytes(const DecodeArgs& A);

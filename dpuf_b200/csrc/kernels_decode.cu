@@ -9,7 +9,7 @@
 // Weight stream.  The weights never depend on activations, so a producer warp per CTA walks
 // the CTA's share of every projection of every layer and step in order, moving stage s (32
 // blocks: the two 8-row groups' scales and nibbles, 4608 bytes per group) of two 16-row units
-// at a time into a shared-memory ring slot with cp.async.bulk (TMA, no multicast) completed
+// at a time into a shared-memory ring slot with cp.async.bulk (TMA, this CTA's own copy) completed
 // on an mbarrier.  It runs ahead across phase and grid barriers, bounded only by the ring,
 // so HBM keeps streaming while the consumers normalise, attend or wait at a barrier.
 //
@@ -65,7 +65,8 @@ constexpr int kBarFilled = 3, kBarEmptied = kBarFilled + kNPs;
 static_assert(kBarEmptied + kNPs <= 16, "named barrier ids");
 constexpr int kHandoff = (kTeamWarps + 1) * 32;  // threads of a pair-buffer hand-off
 constexpr int kBarConsumers = 1, kBarAttn = 2;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kWaitNs = 2000000000ull;    // 2 s
+constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s: other ranks' hosts may launch later
 enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -132,14 +133,71 @@ struct DecShared {
   AttnShared attn;
   float lanes[8];
   float inv;
+  float arg_v[kConsumers / 32];  // per-warp argmax of the LM partials
+  int arg_i[kConsumers / 32];
   int next_id;
   volatile int abort;
 };
 
+// ------------------------------------------------------------------ exchange of vectors
+// A value other CTAs read is one 64-bit word: the value's bits, and the generation of the
+// phase that produced it in the high half.  It is stored to this rank's buffer and to every
+// other rank's copy (stores to the peer's memory over NVLink); a reader waits until the word
+// carries the generation it expects.  Every phase reads the whole output of the phase before,
+// so no producer can overwrite a word (with a later generation) that a reader still needs.
+DPUF_DEV uint64_t tagged(float v, unsigned gen) { return ((uint64_t)gen << 32) | __float_as_uint(v); }
+DPUF_DEV void st_tagged_sys(uint64_t* p, uint64_t w) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+DPUF_DEV void st_tagged_gpu(uint64_t* p, uint64_t w) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// (one GPU: device scope; several ranks: system scope, every rank's copy)
+DPUF_DEV void put_tagged(const DecodeArgs& A, uint64_t* p, uint64_t w) {
+  if (A.tp_world == 1) {
+    st_tagged_gpu(p, w);
+    return;
+  }
+  st_tagged_sys(p, w);
+  for (int r = 0; r < A.tp_world; r++)
+    if (r != A.tp_rank) st_tagged_sys((uint64_t*)((char*)p + A.tp_delta[r]), w);
+}
+DPUF_DEV void put_float(const DecodeArgs& A, float* p, float v) {
+  *p = v;
+  for (int r = 0; r < A.tp_world; r++)
+    if (r != A.tp_rank) *(float*)((char*)p + A.tp_delta[r]) = v;
+}
+// Adds 1 to completion counter i of this rank and of every other rank (relaxed: no fence; the
+// tags, not the count, say whether a value has arrived).
+DPUF_DEV void count_done(const DecodeArgs& A, int i) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(A.ctr + i) : "memory");
+  for (int r = 0; r < A.tp_world; r++)
+    if (r != A.tp_rank)
+      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"((char*)(A.ctr + i) + A.tp_delta[r]) : "memory");
+}
+DPUF_DEV ulonglong2 ld_tagged2(const uint64_t* p, bool sys) {
+  ulonglong2 v;
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+DPUF_DEV unsigned tag_of(uint64_t w) { return (unsigned)(w >> 32); }
+DPUF_DEV float value_of(uint64_t w) { return __uint_as_float((unsigned)w); }
+// Records a failure in the error word of this rank and of every other rank, whose waits then
+// stop at once instead of running into their own limits.
+DPUF_DEV void raise_err(const DecodeArgs& A, int code) {
+  atomicCAS(A.err, 0, code);
+  for (int r = 0; r < A.tp_world; r++)
+    if (r != A.tp_rank) atomicCAS((int*)((char*)A.err + A.tp_delta[r]), 0, code);
+}
+
 // Bounded mbarrier wait by one thread: false (and the CTA abort flag and the error word set)
 // once kWaitNs pass, or when the CTA or another CTA has aborted.  Each try parks the thread
 // for up to 20 us unless the phase completes first.
-DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, int* err) {
+DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, const DecodeArgs& A) {
+  int* err = A.err;
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (;;) {
@@ -151,8 +209,36 @@ DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, int* err) {
     }
     if (globaltimer() - t0 > kWaitNs) {
       S.abort = 1;
-      atomicCAS(err, 0, 1);
+      raise_err(A, 1);
       return false;
+    }
+  }
+}
+
+// Bounded wait of one thread for a pair of tagged words to carry generation `gen`: re-reads
+// until they do; gives up (returning what it read) once the CTA or another CTA or rank has
+// aborted, or the wait limit has passed (error word 3).  Under tensor parallelism the limit
+// allows for other ranks' hosts launching later.
+DPUF_DEV ulonglong2 wait_tagged2(const uint64_t* p, unsigned gen, const DecodeArgs& A, DecShared& S) {
+  unsigned long long t0 = 0;
+  const unsigned long long limit = A.tp_world > 1 ? kTpWaitNs : kWaitNs;
+  for (int it = 0;; it++) {
+    const ulonglong2 w = ld_tagged2(p, A.tp_world > 1);
+    if ((tag_of(w.x) == gen && tag_of(w.y) == gen) || S.abort) return w;
+    if (it >= 4) __nanosleep(64);  // polls of many threads share L2 with the weight stream
+    if ((it & 31) == 31) {
+      if (*(volatile int*)A.err) {
+        S.abort = 1;
+        return w;
+      }
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit) {
+        raise_err(A, 3);
+        S.abort = 1;
+        return w;
+      }
     }
   }
 }
@@ -160,9 +246,10 @@ DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, int* err) {
 // ------------------------------------------------------------------ work plan
 struct Unit {
   const uint8_t* tile;
-  int n_r;     // rows in the tile
-  int row;     // first row of the tile in its matrix
-  float* out;  // output of row `row` (chain epilogue)
+  int n_r;         // rows in the tile
+  int row;         // first row of the tile in its matrix
+  uint64_t* tout;  // tagged output of row `row` (chain epilogue), or null
+  float* out;      // plain output of row `row` (the LM head's logits), or null
 };
 
 DPUF_DEV int kind_cols(const DecodeArgs& A, int kind) {
@@ -179,11 +266,13 @@ DPUF_DEV int kind_units(const DecodeArgs& A, int kind) {
   }
 }
 
-DPUF_DEV Unit make_unit(const uint8_t* tiles, long long stride, int rows, int t, float* out) {
+DPUF_DEV Unit make_unit(const uint8_t* tiles, long long stride, int rows, int t, uint64_t* tout,
+                       float* out = nullptr) {
   Unit u;
   u.tile = tiles + (size_t)t * stride;
   u.row = t * kTileRows;
   u.n_r = min(kTileRows, rows - u.row);
+  u.tout = tout ? tout + u.row : nullptr;
   u.out = out ? out + u.row : nullptr;
   return u;
 }
@@ -200,14 +289,18 @@ DPUF_DEV Unit unit_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, 
     case kGU: return sub == 0 ? make_unit(Ly.tiles[4], Ly.stride[4], A.I, u, nullptr)
                               : make_unit(Ly.tiles[5], Ly.stride[5], A.I, u, A.s_out);
     case kDown: return make_unit(Ly.tiles[6], Ly.stride[6], A.H, u, A.d_out);
-    default: return make_unit(A.lm_tiles, A.lm_stride, A.V, u, A.logits);
+    default: return make_unit(A.lm_tiles, A.lm_stride, A.V, u, nullptr, A.logits);
   }
 }
 
 // Contiguous unit range of CTA c in a projection of U units; the remainder units go to the
-// `U % G` CTAs starting at `rot`, which then advances by U % G.
-DPUF_DEV void take_range(int U, int& rot, int& u0, int& n) {
-  const int G = gridDim.x, c = blockIdx.x;
+// `U % G` CTAs starting at `rot`, which then advances by U % G.  With tensor parallelism the
+// G CTAs are all ranks' CTAs, interleaved (c = blockIdx.x * ranks + rank), so that every rank
+// gets units of every projection with at least `ranks` units: each rank then takes part in
+// every phase, which is what keeps a fast rank from overwriting an exchanged vector (with a
+// later generation) before a slow rank has read it.
+DPUF_DEV void take_range(const DecodeArgs& A, int U, int& rot, int& u0, int& n) {
+  const int G = gridDim.x * A.tp_world, c = blockIdx.x * A.tp_world + A.tp_rank;
   const int v = (c - rot + G) % G;
   const int base = U / G, ext = U % G;
   n = base + (v < ext ? 1 : 0);
@@ -236,9 +329,9 @@ DPUF_DEV unsigned copy_stage(const Unit& un, int n_blk, int s, unsigned char* ds
 }
 
 DPUF_DEV bool produce_pair(const Unit& ua, const Unit& ub, bool has_b, int n_blk, int n_st, unsigned char* ring,
-                           int n_ring, Producer& P, DecShared& S, int* err) {
+                           int n_ring, Producer& P, DecShared& S, const DecodeArgs& A) {
   for (int s = 0; s < n_st; s++) {
-    if (!wait_bar(&S.empty[P.slot], P.phase ^ 1u, S, err)) return false;
+    if (!wait_bar(&S.empty[P.slot], P.phase ^ 1u, S, A)) return false;
     const int kb = min(32, n_blk - s * 32);
     const unsigned bytes = (unsigned)(((ua.n_r > 8 ? 2 : 1) + (has_b ? (ub.n_r > 8 ? 2 : 1) : 0)) * kb * 144);
     uint64_t* bar = &S.full[P.slot];
@@ -275,14 +368,14 @@ DPUF_DEV void pair_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, 
 DPUF_DEV bool produce_phase(const DecodeArgs& A, const DecLayer* layers, int l, int kind, int& rot,
                             unsigned char* ring, int n_ring, Producer& P, DecShared& S) {
   int u0, n;
-  take_range(kind_units(A, kind), rot, u0, n);
+  take_range(A, kind_units(A, kind), rot, u0, n);
   const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
   const DecLayer& Ly = layers[kind == kLM ? 0 : l];
   for (int u = u0, step = 1; u < u0 + n; u += step) {
     Unit ua, ub;
     bool has_b;
     pair_of(A, Ly, kind, u, u0 + n, ua, ub, has_b, step);
-    if (!produce_pair(ua, ub, has_b, n_blk, n_st, ring, n_ring, P, S, A.err)) return false;
+    if (!produce_pair(ua, ub, has_b, n_blk, n_st, ring, n_ring, P, S, A)) return false;
   }
   return true;
 }
@@ -297,6 +390,16 @@ struct Consumer {
 };
 
 DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
+// Barrier of the consumer threads that also returns whether any of them passed true.
+DPUF_DEV bool cbar_or(bool v) {
+  unsigned r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.u32 q, %1, 0; bar.red.or.pred p, %2, %3, q; selp.u32 %0, 1, 0, p; }"
+      : "=r"(r)
+      : "r"((unsigned)v), "r"(kBarConsumers), "r"(kConsumers)
+      : "memory");
+  return r != 0;
+}
 
 // Dot warp w: blocks 4w..4w+3 of both units of the slot; lane = (unit lane/16, row lane%16)
 // computes dot = sum_k u_k q_k with dp4a on the row's nibbles (low nibbles against x bytes
@@ -352,12 +455,13 @@ DPUF_DEV void better(float& bv, int& bi, float v, int i) {
 }
 
 // One projection on the consumer side.
-DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, Consumer& C, unsigned char* ring,
-                            int n_ring, const int8_t* xq, const float* xs, const int* xm, float2* ps, DecShared& S) {
+DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, unsigned gen, Consumer& C,
+                            unsigned char* ring, int n_ring, const int8_t* xq, const float* xs, const int* xm,
+                            float2* ps, DecShared& S) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = lane >> 4, r = lane & 15;
   int u0, n;
-  take_range(kind_units(A, kind), C.rot, u0, n);
+  take_range(A, kind_units(A, kind), C.rot, u0, n);
   const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
@@ -373,7 +477,7 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
         if ((int)(C.item % kTeams) == warp / kTeamWarps) {
           const int wt = warp % kTeamWarps;
           bool ok = true;
-          if (lane == 0) ok = wait_bar(&S.full[C.slot], C.phase, S, A.err);
+          if (lane == 0) ok = wait_bar(&S.full[C.slot], C.phase, S, A);
           named_sync(kBarEmptied + C.pb, kHandoff);  // the chain is done with this pair buffer
           if (__shfl_sync(kFull, (int)ok, 0)) {
             if (kb == 32)
@@ -421,16 +525,18 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
         const float up = __shfl_down_sync(kFull, acc, 16);
         if (half == 0 && r < ua.n_r) {
           const int row = ua.row + r;
-          A.s_out[row] = swiglu_one(acc, up, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et);
+          put_tagged(A, A.s_out + row,
+                     tagged(swiglu_one(acc, up, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et),
+                            gen));
         }
       } else if (half == 0 || has_b) {
         const Unit& un = half ? ub : ua;
         if (r < un.n_r) {
           if (kind == kLM) {
-            if (A.write_logits) un.out[r] = acc;
+            if (A.write_logits) put_float(A, un.out + r, acc);
             better(bv, bi, acc, un.row + r);
           } else {
-            un.out[r] = acc;
+            put_tagged(A, un.tout + r, tagged(acc, gen));
           }
         }
       }
@@ -442,37 +548,55 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, C
       const int oi = __shfl_xor_sync(kFull, bi, m);
       better(bv, bi, ov, oi);
     }
-    if (lane == 0) A.part[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+    // other ranks' hosts read this CTA's logits once they have seen its partial
+    if (A.tp_world > 1 && A.write_logits) __threadfence_system();
+    if (lane == 0) {
+      const int g_all = gridDim.x * A.tp_world;
+      uint64_t* pw = A.part + ((size_t)(gen & 1) * g_all + A.tp_rank * gridDim.x + blockIdx.x) * 2;
+      put_tagged(A, pw, tagged(bv, gen));
+      put_tagged(A, pw + 1, ((uint64_t)gen << 32) | (unsigned)bi);
+    }
+  }
+  if (warp == kChainWarp) {
+    __syncwarp();
+    if (lane == 0) count_done(A, 0);
   }
 }
 
-// Grid-wide barrier of the consumer threads (the producer never joins): arrive on a global
-// counter (release) and wait, bounded, until every CTA has arrived `target / gridDim.x` times
-// (acquire).
+// Bounded poll by one thread until a counter has reached `target` (wrap-safe), the CTA or
+// another CTA (or rank) has aborted, or the wait limit has passed (error word 2).
+DPUF_DEV void wait_count(const DecodeArgs& A, const unsigned* ctr, unsigned target, DecShared& S) {
+  unsigned long long t0 = 0;
+  const unsigned long long limit = A.tp_world > 1 ? kTpWaitNs : kWaitNs;
+  for (int it = 0; !S.abort; it++) {
+    if ((int)(ld_acquire(ctr) - target) >= 0) break;
+    if (*(volatile int*)A.err) {
+      S.abort = 1;
+      break;
+    }
+    if ((it & 15) == 15) {
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > limit) {
+        raise_err(A, 2);
+        S.abort = 1;
+        break;
+      }
+    }
+    __nanosleep(20);
+  }
+}
+
+// Grid-wide barrier of the consumer threads of this GPU (the producer never joins): arrive on
+// a global counter (release) and wait, bounded, until every CTA has arrived `target /
+// gridDim.x` times (acquire).
 DPUF_DEV void grid_sync(const DecodeArgs& A, unsigned& target, DecShared& S) {
   cbar();
   target += gridDim.x;
   if (threadIdx.x == 0) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.bar) : "memory");
-    unsigned long long t0 = 0;
-    for (int it = 0; !S.abort; it++) {
-      if ((int)(ld_acquire(A.bar) - target) >= 0) break;
-      if (*(volatile int*)A.err) {
-        S.abort = 1;
-        break;
-      }
-      if ((it & 15) == 15) {
-        const unsigned long long now = globaltimer();
-        if (t0 == 0) {
-          t0 = now;
-        } else if (now - t0 > kWaitNs) {
-          atomicCAS(A.err, 0, 2);
-          S.abort = 1;
-          break;
-        }
-      }
-      __nanosleep(20);
-    }
+    wait_count(A, A.bar, target, S);
   }
   cbar();
 }
@@ -488,25 +612,65 @@ DPUF_DEV void stage8(void* dst, const void* src, int bytes) {
     cp_async8_ca((unsigned char*)dst + i, (const unsigned char*)src + i);
 }
 
+// Stages words [0, n) (n even) of a tagged vector that other CTAs (or ranks) produce in
+// generation `gen`, together with whatever async copies the caller has issued (all consumer
+// threads call this).  Each thread copies its 16-byte pieces and waits; if any thread finds a
+// piece that predates `gen`, thread 0 alone waits (bounded) until completion counter ctr_i
+// reaches `target`, then every thread re-copies its stale pieces, and repeats (waiting on its
+// first stale piece itself) until no thread has one.  On return every staged word carries
+// `gen` (or the CTA has aborted) and the consumer threads have passed a CTA barrier.
+DPUF_DEV void stage_tagged(uint64_t* dst, const uint64_t* src, int n, unsigned gen, int ctr_i, unsigned target,
+                           const DecodeArgs& A, DecShared& S) {
+  for (int i = threadIdx.x * 2; i < n; i += kConsumers * 2) cp_async16_cg(dst + i, src + i);
+  cp_async_commit_wait_all();
+  auto first_stale = [&]() {
+    for (int i = threadIdx.x * 2; i < n; i += kConsumers * 2) {
+      const ulonglong2 w = *(const ulonglong2*)(dst + i);
+      if (tag_of(w.x) != gen || tag_of(w.y) != gen) return i;
+    }
+    return -1;
+  };
+  int first = first_stale();
+  if (!cbar_or(first >= 0)) return;
+  if (threadIdx.x == 0) wait_count(A, A.ctr + ctr_i, target, S);
+  cbar();
+  for (int round = 0;; round++) {
+    if (first >= 0 && !S.abort) {
+      if (round > 0) *(ulonglong2*)(dst + first) = wait_tagged2(src + first, gen, A, S);
+      for (int i = first; i < n; i += kConsumers * 2) {
+        const ulonglong2 w = *(const ulonglong2*)(dst + i);
+        if (tag_of(w.x) != gen || tag_of(w.y) != gen) cp_async16_cg(dst + i, src + i);
+      }
+      cp_async_commit_wait_all();
+      first = first_stale();
+    }
+    if (!cbar_or(first >= 0 && !S.abort)) return;
+  }
+}
+
 // Residual add, RMSNorm and activation prep of the result (add_and_rms_norm_f32 /
-// rms_norm_f32, dpuf_engine.c:225-272, then the prep).  res (optional, written by other CTAs;
-// rows >= n_valid add 0, as the pruned down projection's zero rows do), the gains and the
-// sign bytes are staged in one async round; all threads add the residual, then threads 0..7
-// run the eight "AVX lane" chains
-// over h after the residual add, 32 elements at a time.
-DPUF_DEV void norm_prep(float* h, const float* res, int n_valid, const float* w, int H, float eps,
-                        const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S) {
+// rms_norm_f32, dpuf_engine.c:225-272, then the prep).  The residual (optional; tagged words of
+// generation `gen` from other CTAs; rows >= n_valid add 0, as the pruned down projection's
+// zero rows do), the gains and the sign bytes are staged in one async round (plus re-copies
+// of residual words staged before they were produced); all threads add the residual, then
+// threads 0..7 run the eight "AVX lane" chains over h after the residual add, 32 elements at
+// a time.
+DPUF_DEV void norm_prep(const DecodeArgs& A, float* h, const uint64_t* res, unsigned gen, int n_valid, const float* w,
+                        int H, float eps, const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage,
+                        DecShared& S) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* sr = stage;          // [H] residual
-  float* sw = stage + H;      // [H] gains
-  uint8_t* sg = (uint8_t*)(stage + 2 * H);
-  if (res) stage16(sr, res, min(H, n_valid) * 4);
+  uint64_t* sr = (uint64_t*)stage;  // [H] tagged residual
+  float* sw = stage + 2 * H;         // [H] gains
+  uint8_t* sg = (uint8_t*)(stage + 3 * H);
   stage16(sw, w, H * 4);
   if (signs) stage8(sg, signs, H / 8);
-  cp_async_commit_wait_all();
+  if (res)
+    stage_tagged(sr, res, min(H, n_valid), gen, 0, gen * (unsigned)(gridDim.x * A.tp_world), A, S);
+  else
+    cp_async_commit_wait_all();
   cbar();
   if (res) {
-    for (int i = tid; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? sr[i] : 0.0f);
+    for (int i = tid; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? value_of(sr[i]) : 0.0f);
     cbar();
   }
   if (tid < 8) S.lanes[tid] = sumsq_lane32(h, H & ~7, tid);
@@ -534,6 +698,79 @@ DPUF_DEV void norm_prep(float* h, const float* res, int n_valid, const float* w,
   }
 }
 
+// Distributed prep of the gate/up output (tagged words of generation `gen`) for the down
+// projection: 64-column chunk ch is prepped by one CTA of all ranks (virtual CTA ch mod the
+// CTA count; eight lanes per chunk, so a warp preps four).  One GPU: the CTA stores the codes,
+// block scales and block sums as plain values, read by every CTA after a grid barrier.
+// Several ranks: it publishes them to every rank as tagged words of the same generation (four
+// codes per word) and counts its prep on completion counter 1.
+DPUF_DEV void prep_slices(const DecodeArgs& A, const uint8_t* signs, unsigned gen, DecShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x * A.tp_world, vc = blockIdx.x * A.tp_world + A.tp_rank;
+  const int nch = A.I / 64;
+  uint64_t* dq = A.dprep;
+  uint64_t* ds = dq + A.I / 4;
+  uint64_t* dm = ds + A.I / 32;
+  for (int k0 = warp * 4; vc + k0 * G < nch; k0 += kConsumers / 8) {
+    const int ch = vc + (k0 + (lane >> 3)) * G;
+    const bool active = ch < nch;
+    const int col = (active ? ch : 0) * 64 + (lane & 7) * 8;
+    const uint8_t sbyte = (active && signs) ? __ldg(signs + (col >> 3)) : 0;  // issued before the waits
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      ulonglong2 w = make_ulonglong2(0, 0);
+      if (active) {
+        w = ld_tagged2(A.s_out + col + j, A.tp_world > 1);
+        if (tag_of(w.x) != gen || tag_of(w.y) != gen) w = wait_tagged2(A.s_out + col + j, gen, A, S);
+      }
+      v[j] = value_of(w.x);
+      v[j + 1] = value_of(w.y);
+    }
+    const PrepOut o = prep_chunk_g8_core(v, sbyte, lane);
+    if (active && A.tp_world == 1) {
+      *(uint2*)(A.xd_q8 + col) = make_uint2(o.lo, o.hi);
+      if ((lane & 3) == 0) {
+        A.xd_xs[col >> 5] = o.xs;
+        A.xd_xm[col >> 5] = o.xm;
+      }
+    } else if (active) {
+      const uint64_t tg = (uint64_t)gen << 32;
+      put_tagged(A, dq + col / 4, tg | o.lo);
+      put_tagged(A, dq + col / 4 + 1, tg | o.hi);
+      if ((lane & 3) == 0) {
+        put_tagged(A, ds + (col >> 5), tagged(o.xs, gen));
+        put_tagged(A, dm + (col >> 5), tg | (unsigned)o.xm);
+      }
+    }
+  }
+  if (A.tp_world > 1) {
+    cbar();
+    if (threadIdx.x == 0) count_done(A, 1);
+  }
+}
+
+// The down projection's prepped input (prep_slices, generation `gen`, the `dgen`-th prep) into
+// x: the tagged words are staged, then unpacked to codes, block scales and block sums.
+// K % 64 == 0.
+DPUF_DEV void load_prepped_tagged(const DecodeArgs& A, int K, unsigned gen, unsigned dgen, int8_t* xq, float* xs,
+                                  int* xm, float* stage, DecShared& S) {
+  uint64_t* st = (uint64_t*)stage;
+  const int nq = K / 4, nb = K / 32;
+  // the chunks are published by all CTAs at about the same time, shortly after this CTA's own:
+  // wait for the count first, so that the one staging round finds them
+  const unsigned target = dgen * (unsigned)(gridDim.x * A.tp_world);
+  if (threadIdx.x == 0) wait_count(A, A.ctr + 1, target, S);
+  cbar();
+  stage_tagged(st, A.dprep, nq + 2 * nb, gen, 1, target, A, S);
+  cbar();
+  for (int i = threadIdx.x; i < nq; i += kConsumers) *(uint32_t*)(xq + 4 * i) = (uint32_t)st[i];
+  for (int b = threadIdx.x; b < nb; b += kConsumers) {
+    xs[b] = value_of(st[nq + b]);
+    xm[b] = (int)(unsigned)st[nq + nb + b];
+  }
+}
+
 // Copies a prepped activation (codes, block scales, block sums of K columns; K % 128 == 0)
 // written by other CTAs into x.
 DPUF_DEV void load_prepped(const int8_t* q8, const float* bxs, const int32_t* bxm, int K, int8_t* xq, float* xs,
@@ -544,8 +781,9 @@ DPUF_DEV void load_prepped(const int8_t* q8, const float* bxs, const int32_t* bx
   cp_async_commit_wait_all();
 }
 
-// Activation prep of a vector written by other CTAs: pieces of `cap` columns (a multiple of
-// 128) are staged into shared memory with their sign bytes, then prepped from there.
+// Activation prep of a vector written by other CTAs before a grid barrier: pieces of `cap`
+// columns (a multiple of 128) are staged into shared memory with their sign bytes, then
+// prepped from there.
 DPUF_DEV void prep_global(const float* src, int K, const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage,
                           int cap) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -578,7 +816,7 @@ struct AttnSync {
 // QK-norm + RoPE of the queries and the key, K/V rows stored at `pos` (both pairs of a KV head
 // store the same bits), then attn_pair_body.  With fuse_o the item also preps its output
 // columns (whole 64-column chunks) for the o projection.  Threads 0..255 only.
-DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, int pos, float* scratch,
+DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, int pos, unsigned gen, float* scratch,
                               DecShared& S) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int groups = A.nq / A.nkv, n_pairs = (groups + 1) / 2, hd = A.hd;
@@ -594,12 +832,8 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
     named_sync(kBarAttn, kAttnThreads);  // scratch free (previous item done)
     {
       const int q4 = hd / 4;  // 16-byte pieces per vector
-      for (int i = tid; i < q4 * (nh + 2); i += kAttnThreads) {
-        const int v = i / q4, o = (i % q4) * 4;
-        const float* src = v < nh ? A.q + (size_t)(qh0 + v) * hd : (v == nh ? A.k : A.v) + (size_t)kvh * hd;
-        float* dst = v < nh ? qs + v * hd : (v == nh ? kin : vin);
-        cp_async16_cg(dst + o, src + o);
-      }
+      // gains and the RoPE row asynchronously while the pair's query heads, the key and the
+      // value (tagged words of the q/k/v phase) are read, one pair of elements per thread
       for (int i = tid; i < q4; i += kAttnThreads) {
         if (Ly.q_norm) cp_async16_cg(qn + i * 4, Ly.q_norm + i * 4);
         if (Ly.k_norm) cp_async16_cg(kn + i * 4, Ly.k_norm + i * 4);
@@ -607,6 +841,14 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
           cp_async16_cg(cs + i * 4, A.cos_tab + (size_t)pos * (hd >> 1) + i * 4);
           cp_async16_cg(sn + i * 4, A.sin_tab + (size_t)pos * (hd >> 1) + i * 4);
         }
+      }
+      for (int i = tid * 2; i < (nh + 2) * hd; i += kAttnThreads * 2) {
+        const int v = i / hd, o = i % hd;
+        const uint64_t* src = (v < nh ? A.q + (size_t)(qh0 + v) * hd : (v == nh ? A.k : A.v) + (size_t)kvh * hd) + o;
+        float* dst = (v < nh ? qs + v * hd : (v == nh ? kin : vin)) + o;
+        ulonglong2 w = ld_tagged2(src, A.tp_world > 1);
+        if (tag_of(w.x) != gen || tag_of(w.y) != gen) w = wait_tagged2(src, gen, A, S);
+        *(float2*)dst = make_float2(value_of(w.x), value_of(w.y));
       }
       cp_async_commit_wait_all();
     }
@@ -751,18 +993,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
     }
     cbar();
     if (tid == 0) trace_at(A, step, sb + kEvEmbed);
+    // exchange generations: 4 per layer (q/k/v, o, gate/up, down) and the LM head's
+    const unsigned g_step = A.gen0 + (unsigned)step * (unsigned)decode_phases(A.L);
     for (int l = 0; l < A.L; l++) {
       const DecLayer& Ly = layers[l];
       const int lb = kEvPerLayer * l;
-      norm_prep(h, l > 0 ? A.d_out : nullptr, A.keep_down * kTileRows, Ly.attn_norm, H, A.eps, Ly.signs[0], xq, xs,
-                xm, stage, S);
+      const unsigned g = g_step + 4u * l;
+      // the previous layer's down output (generation g - 1) is the residual
+      norm_prep(A, h, l > 0 ? A.d_out : nullptr, g - 1, A.keep_down * kTileRows, Ly.attn_norm, H, A.eps, Ly.signs[0],
+                xq, xs, xm, stage, S);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvNorm1);
-      consume_phase(A, Ly, kQKV, C, ring, n_ring, xq, xs, xm, ps, S);
+      consume_phase(A, Ly, kQKV, g + kQKV, C, ring, n_ring, xq, xs, xm, ps, S);
       if (tid == 0) trace_at(A, step, lb + kEvQKV);
-      grid_sync(A, target, S);
+      cbar();  // the attention scratch overlaps the pair buffers
       if (tid == 0) trace_at(A, step, lb + kEvB1);
-      if (tid < kAttnThreads) attention_items(A, Ly, l, pos, attn_scratch, S);
+      if (tid < kAttnThreads) attention_items(A, Ly, l, pos, g + kQKV, attn_scratch, S);
       if (tid == 0) trace_at(A, step, lb + kEvAttn);
       grid_sync(A, target, S);
       if (tid == 0) trace_at(A, step, lb + kEvB2);
@@ -772,46 +1018,68 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
         prep_global(A.att, A.qd, Ly.signs[1], xq, xs, xm, stage, A.stage_cap);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvPrepO);
-      consume_phase(A, Ly, kO, C, ring, n_ring, xq, xs, xm, ps, S);
+      consume_phase(A, Ly, kO, g + kO, C, ring, n_ring, xq, xs, xm, ps, S);
       if (tid == 0) trace_at(A, step, lb + kEvO);
-      grid_sync(A, target, S);
+      cbar();
       if (tid == 0) trace_at(A, step, lb + kEvB3);
-      norm_prep(h, A.o_out, H, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
+      norm_prep(A, h, A.o_out, g + kO, H, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvNorm2);
-      consume_phase(A, Ly, kGU, C, ring, n_ring, xq, xs, xm, ps, S);
+      consume_phase(A, Ly, kGU, g + kGU, C, ring, n_ring, xq, xs, xm, ps, S);
       if (tid == 0) trace_at(A, step, lb + kEvGU);
-      grid_sync(A, target, S);
+      cbar();
       if (tid == 0) trace_at(A, step, lb + kEvB4);
-      prep_global(A.s_out, A.I, Ly.signs[3], xq, xs, xm, stage, A.stage_cap);
+      prep_slices(A, Ly.signs[3], g + kGU, S);
+      if (A.tp_world == 1) {
+        grid_sync(A, target, S);
+        load_prepped(A.xd_q8, A.xd_xs, A.xd_xm, A.I, xq, xs, xm);
+      } else {
+        load_prepped_tagged(A, A.I, g + kGU, A.dgen0 + (unsigned)(step * A.L + l + 1), xq, xs, xm, stage, S);
+      }
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvPrepD);
-      consume_phase(A, Ly, kDown, C, ring, n_ring, xq, xs, xm, ps, S);
+      consume_phase(A, Ly, kDown, g + kDown, C, ring, n_ring, xq, xs, xm, ps, S);
       if (tid == 0) trace_at(A, step, lb + kEvDown);
-      grid_sync(A, target, S);
+      cbar();
       if (tid == 0) trace_at(A, step, lb + kEvB5);
     }
-    norm_prep(h, A.L > 0 ? A.d_out : nullptr, A.keep_down * kTileRows, A.out_norm, H, A.eps, A.lm_signs, xq, xs, xm,
-              stage, S);
+    const unsigned g_lm = g_step + 4u * A.L;
+    norm_prep(A, h, A.L > 0 ? A.d_out : nullptr, g_lm - 1, A.keep_down * kTileRows, A.out_norm, H, A.eps, A.lm_signs,
+              xq, xs, xm, stage, S);
     cbar();
     if (tid == 0) trace_at(A, step, sb + kEvNormF);
-    consume_phase(A, layers[0], kLM, C, ring, n_ring, xq, xs, xm, ps, S);
+    consume_phase(A, layers[0], kLM, g_lm, C, ring, n_ring, xq, xs, xm, ps, S);
     if (tid == 0) trace_at(A, step, sb + kEvLM);
-    grid_sync(A, target, S);
+    cbar();
     if (tid == 0) trace_at(A, step, sb + kEvBLM);
-    if (warp == 0) {
+    {
+      // every CTA's partial (of every rank), tagged with the LM generation, read by all
+      // consumer threads; the two partial buffers alternate with the generation's parity, so
+      // a CTA already at the next step's LM head never overwrites a partial another CTA has
+      // yet to read
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int c = lane; c < (int)gridDim.x; c += 32) {
-        const float2 p = __ldcg(A.part + c);
-        better(bv, bi, p.x, __float_as_int(p.y));
+      const int g_all = gridDim.x * A.tp_world;
+      const uint64_t* part = A.part + (size_t)(g_lm & 1) * g_all * 2;
+      for (int c = tid; c < g_all; c += kConsumers) {
+        ulonglong2 w = ld_tagged2(part + 2 * c, A.tp_world > 1);
+        if (tag_of(w.x) != g_lm || tag_of(w.y) != g_lm) w = wait_tagged2(part + 2 * c, g_lm, A, S);
+        better(bv, bi, value_of(w.x), (int)(unsigned)w.y);
       }
+      // the logits other ranks stored before their partials are visible to this rank's host
+      if (A.tp_world > 1 && A.write_logits) __threadfence_system();
       for (int m = 16; m; m >>= 1) {
         const float ov = __shfl_xor_sync(kFull, bv, m);
         const int oi = __shfl_xor_sync(kFull, bi, m);
         better(bv, bi, ov, oi);
       }
       if (lane == 0) {
+        S.arg_v[warp] = bv;
+        S.arg_i[warp] = bi;
+      }
+      cbar();
+      if (tid == 0) {
+        for (int w = 1; w < kConsumers / 32; w++) better(bv, bi, S.arg_v[w], S.arg_i[w]);
         // the winner is a row of the head; anything else (all logits NaN, or an aborted run)
         // feeds row 0 so that the embedding lookup stays in bounds
         const int id_next = (bi >= 0 && bi < A.V && bi < A.tok_rows) ? bi : 0;
@@ -820,8 +1088,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
       }
     }
     if (tid == 0) trace_at(A, step, sb + kEvArg);
-    // without layers the next LM phase would rewrite the partials other CTAs may still read
-    if (A.L == 0) grid_sync(A, target, S);
     cbar();
   }
   if (warp < kMmaWarps)
@@ -832,14 +1098,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
 
 // Shared memory of one CTA: ring | layer table | h | a union of {activation x + pair buffers
 // or staging area} and the attention scratch.  The staging area (after x) holds an embedding
-// group with its sign table (4.625 H bytes), a residual with the norm gains and signs
-// (8.125 H) or a piece of a vector being prepped.
+// group with its sign table (4.625 H bytes), a tagged residual with the norm gains and signs
+// (12.125 H), the down projection's tagged prepped input (2.5 I) or a piece of a vector being
+// prepped (4.125 bytes per column).
 size_t decode_x_bytes(const DecodeArgs& A) { return (size_t)A.kmax + (size_t)(A.kmax / 32) * 8; }
 size_t decode_uni_bytes(const DecodeArgs& A) {
   const size_t xb = decode_x_bytes(A);
   const size_t uni_x = xb + (size_t)kNPs * kPsBuf * sizeof(float2);
-  // residual + gains + signs of a norm, or a whole vector of kmax columns with its signs
-  const size_t uni_stage = xb + std::max((size_t)A.H * 8 + (size_t)A.H / 8, (size_t)A.kmax * 4 + (size_t)A.kmax / 8) + 128;
+  // tagged residual + gains + signs of a norm, or a whole plain vector of kmax columns with
+  // its signs
+  const size_t uni_stage =
+      xb + std::max((size_t)A.H * 12 + (size_t)A.H / 8, (size_t)A.kmax * 4 + (size_t)A.kmax / 8) + 128;
   const size_t uni_attn = attn_scratch_floats(A.hd, A.S) * sizeof(float);
   return std::max(std::max(uni_x, uni_stage), uni_attn);
 }

@@ -182,8 +182,12 @@ DPUF_DEV void prep_chunk_warp_sb(float a, float b, uint8_t sa, uint8_t sb, int c
 //   q = clamp(rint(v * (127/amax)), -127, 127), xm = 8 * sum(q); amax <= 1e-4 gives zeros.
 // Every lane of the warp must call this (shuffles span the warp); `active` masks groups
 // without a chunk (they compute on zeros and store nothing).
-DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, int lane, int8_t* q8, float* xs,
-                            int32_t* xm) {
+struct PrepOut {
+  uint32_t lo, hi;  // this lane's eight codes (columns 8q .. 8q + 7 of the chunk)
+  float xs;         // the lane's 32-block scale and sum (lanes 0 and 4 of the group publish)
+  int xm;
+};
+DPUF_DEV PrepOut prep_chunk_g8_core(float (&v)[8], uint8_t sbyte, int lane) {
   const int q = lane & 7;
 #pragma unroll
   for (int r = 0; r < 8; r++)
@@ -231,18 +235,28 @@ DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, i
   }
   sum += __shfl_xor_sync(kFull, sum, 1);
   sum += __shfl_xor_sync(kFull, sum, 2);
-  if (active) {
-    uint32_t lo = 0, hi = 0;
+  PrepOut o;
+  o.lo = 0;
+  o.hi = 0;
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-      lo |= (uint32_t)(qs[r] & 0xFF) << (8 * r);
-      hi |= (uint32_t)(qs[r + 4] & 0xFF) << (8 * r);
-    }
-    *(uint2*)(q8 + c0 + 8 * q) = make_uint2(lo, hi);
+  for (int r = 0; r < 4; r++) {
+    o.lo |= (uint32_t)(qs[r] & 0xFF) << (8 * r);
+    o.hi |= (uint32_t)(qs[r + 4] & 0xFF) << (8 * r);
+  }
+  o.xs = xsv;
+  o.xm = sum * 8;
+  return o;
+}
+DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, int lane, int8_t* q8, float* xs,
+                            int32_t* xm) {
+  const int q = lane & 7;
+  const PrepOut o = prep_chunk_g8_core(v, sbyte, lane);
+  if (active) {
+    *(uint2*)(q8 + c0 + 8 * q) = make_uint2(o.lo, o.hi);
     if ((q & 3) == 0) {
       const int blk = (c0 >> 5) + (q >> 2);
-      xs[blk] = xsv;
-      xm[blk] = sum * 8;
+      xs[blk] = o.xs;
+      xm[blk] = o.xm;
     }
   }
 }

@@ -73,12 +73,31 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_cuda_prepare_expf_table.restype = ctypes.c_int64
     lib.dpuf_cuda_matmul_noalloc.restype = _I32
     lib.dpuf_cuda_matmul_noalloc.argtypes = [_I32] * 4 + [_VP] * 6
+    lib.dpuf_cuda_tp_handle.restype = _I32
+    lib.dpuf_cuda_tp_handle.argtypes = [_VP, _I32, _I32, _VP]
+    lib.dpuf_cuda_tp_attach.restype = _I32
+    lib.dpuf_cuda_tp_attach.argtypes = [_VP, _VP]
     lib.dpuf_cuda_sample_seed.restype = ctypes.c_uint64
     lib.dpuf_cuda_sample_seed.argtypes = []
     lib.dpuf_cuda_sample_token.restype = _I32
     lib.dpuf_cuda_sample_token.argtypes = [_VP, _I32, ctypes.c_float, _VP]
     lib._dpuf_typed = True
     return lib
+
+
+TP_BLOB_BYTES = 256  # DPUF_CUDA_TP_BLOB_BYTES
+
+
+def torch_all_gather(group=None):
+    """all_gather for CudaTransformerEngine.tp_attach over a torch.distributed group."""
+    import torch.distributed as dist
+
+    def gather(b: bytes) -> list[bytes]:
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, b, group=group)
+        return out
+
+    return gather
 
 
 def last_error() -> str:
@@ -156,6 +175,24 @@ class CudaTransformerEngine:
         why = ctypes.c_char_p()
         on = self.lib.dpuf_cuda_persistent_decode(self._handle, ctypes.byref(why))
         return on == 1, (why.value or b"").decode()
+
+    def tp_attach(self, rank: int, world: int, all_gather) -> None:
+        """Tensor parallelism of batch-1 decode steps over `world` processes (one GPU each):
+        publishes this rank's exchange buffer, all-gathers every rank's description with
+        `all_gather(bytes) -> list[bytes]` (in rank order; e.g. over the caller's
+        torch.distributed group) and maps the other ranks' buffers.  Every rank must then make
+        the same engine calls in the same order."""
+        blob = np.zeros(TP_BLOB_BYTES, np.uint8)
+        rc = self.lib.dpuf_cuda_tp_handle(self._handle, int(rank), int(world), blob.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"dpuf_cuda_tp_handle failed with rc={rc}: {last_error()}")
+        blobs = all_gather(blob.tobytes())
+        if len(blobs) != world or any(len(b) != TP_BLOB_BYTES for b in blobs):
+            raise ValueError("all_gather must return one blob per rank")
+        allb = np.frombuffer(b"".join(blobs), np.uint8).copy()
+        rc = self.lib.dpuf_cuda_tp_attach(self._handle, allb.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"dpuf_cuda_tp_attach failed with rc={rc}: {last_error()}")
 
     def zone_info(self):
         used, exited = np.zeros(1, np.int32), np.zeros(1, np.int32)

@@ -58,6 +58,30 @@ DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why);
 DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_t* per_cta, uint64_t* out,
                                            int64_t max_values);
 
+/* ---- tensor parallelism of batch-1 decode over processes, one GPU each ----
+ * The reference has no multi-GPU mode.  Every rank creates an engine for the same model on its
+ * own GPU (weights are replicated), then:
+ *   1. dpuf_cuda_tp_handle(h, rank, world, blob) allocates this rank's exchange buffer and
+ *      writes DPUF_CUDA_TP_BLOB_BYTES bytes describing it (its IPC handle and the model shape);
+ *   2. the caller all-gathers the blobs in rank order (any host transport: the caller's
+ *      process group, a file, a socket) - this also ensures every buffer exists before use;
+ *   3. dpuf_cuda_tp_attach(h, blobs[world * DPUF_CUDA_TP_BLOB_BYTES]) maps the other ranks'
+ *      buffers (NVLink peer access).  Every rank must be on a GPU of its own (checked by PCI bus
+ *      id): the ranks' kernels wait on each other.
+ * From then on each batch-1 step that runs as the persistent kernel splits every projection
+ * and the LM head over all ranks' CTAs; each rank stores its outputs to every rank's buffer
+ * and the ranks meet at global barriers after q/k/v, o, gate/up, down and the LM head.
+ * Attention, norms and everything else run in full on every rank, so every rank returns the
+ * same ids and logits, bit-identical to one GPU.  All ranks must make the same calls with the
+ * same arguments in the same order (steps with M > 1, or with Zone A, simply run in full on
+ * every rank).  A rank whose wait times out sets every rank's error word; the group then
+ * returns -6 for every persistent step until the engines are re-created.
+ * Returns 0; -1 bad arguments or order, or mismatching blobs; -4 CUDA error; -5 the engine
+ * cannot run the persistent kernel (dpuf_cuda_persistent_decode gives the reason). */
+#define DPUF_CUDA_TP_BLOB_BYTES 256
+DPUF_EXPORT int32_t dpuf_cuda_tp_handle(void* handle, int32_t rank, int32_t world, uint8_t* blob_out);
+DPUF_EXPORT int32_t dpuf_cuda_tp_attach(void* handle, const uint8_t* blobs);
+
 /* Zone-A decision of the last forward: {used, exited} and the top-2 values. */
 DPUF_EXPORT int32_t dpuf_cuda_zone_info(void* handle, int32_t* used, int32_t* exited, float* b1, float* b2);
 

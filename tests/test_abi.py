@@ -4,6 +4,7 @@ import ctypes
 import pathlib
 import re
 
+import numpy as np
 import pytest
 
 from dpuf_b200 import _native, model as mdl
@@ -68,3 +69,15 @@ def test_engine_rejects_non_mode12(cuda_lib):
     m = mdl.SyntheticModel(mdl.TINY, seed=0)
     m.layers[0].w_q.mode = 10  # row-major Hadamard: not served by this engine
     assert not lib.dpuf_engine_create(*m.create_args())
+
+
+def test_tp_entry_points_reject_bad_arguments(cuda_lib):
+    """Tensor-parallel setup checks its arguments before touching a GPU."""
+    from dpuf_b200 import engine
+
+    lib = engine.cuda_lib()
+    blob = np.zeros(engine.TP_BLOB_BYTES, np.uint8)
+    assert lib.dpuf_cuda_tp_handle(None, 0, 2, blob.ctypes.data) == -1
+    assert lib.dpuf_cuda_tp_attach(None, blob.ctypes.data) == -1
+    with open(pathlib.Path(__file__).resolve().parents[1] / "include" / "dpuf_cuda.h") as f:
+        assert f"#define DPUF_CUDA_TP_BLOB_BYTES {engine.TP_BLOB_BYTES}" in f.read()
