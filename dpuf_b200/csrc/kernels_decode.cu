@@ -1,39 +1,54 @@
 // kernels_decode.cu - batch-1 decode as one persistent cooperative kernel.
 //
 // One CTA per SM runs every step of a greedy decode (or one forward_token step): embedding,
-// all layers, final norm, LM head and argmax, with grid-wide barriers only where the
-// reference's step has a data dependency across rows (after each projection and after
-// attention).  The per-element arithmetic is the same as the per-step kernels' (layer_dev.cuh,
-// and the GEMV's exact block chain), so logits and ids are bit-identical to the reference's.
+// all layers, final norm, LM head and argmax.  The per-element arithmetic is the same as the
+// per-step kernels' (layer_dev.cuh, and the GEMV's exact block chain), so logits and ids are
+// bit-identical to the reference's.
 //
 // Weight stream.  The weights never depend on activations, so a producer warp per CTA walks
 // the CTA's share of every projection of every layer and step in order, moving stage s (32
 // blocks: the two 8-row groups' scales and nibbles, 4608 bytes per group) of two 16-row units
-// at a time into a shared-memory ring slot with cp.async.bulk (TMA, this CTA's own copy) completed
-// on an mbarrier.  It runs ahead across phase and grid barriers, bounded only by the ring,
-// so HBM keeps streaming while the consumers normalise, attend or wait at a barrier.
+// at a time into a shared-memory ring slot with cp.async.bulk (TMA, this CTA's own copy)
+// completed on an mbarrier.  It runs ahead across phases and barriers, bounded only by the
+// ring, so HBM keeps streaming while the consumers normalise, attend or wait.
 //
-// Consumers (warps 0..16).  Per slot, one of two teams of eight dot warps (teams take
-// alternate slots) computes the exact integer block dots
+// Consumers (warps 0..8).  Per slot, eight dot warps compute the exact integer block dots
 // sum_k u_k q_k with dp4a (lane = unit and row, four blocks each, independent chains), turn
 // them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand them to
-// the chain warp through a 4-deep ring of pair buffers (named-barrier hand-off); the chain warp runs acc = fma(p, s, acc) per row
-// over the blocks in order (dpuf_avx2.c:2601-2640), lanes 0..15 for unit A and 16..31 for
-// unit B, and writes the units' outputs (SwiGLU for a gate/up pair - gate tile in A, up tile
-// in B - and the running argmax for the LM head).
+// the chain warp through a 4-deep ring of pair buffers (named-barrier hand-off); the chain
+// warp runs acc = fma(p, s, acc) per row over the blocks in order (dpuf_avx2.c:2601-2640),
+// lanes 0..15 for unit A and 16..31 for unit B, and writes the units' outputs (SwiGLU for a
+// gate/up pair - gate tile in A, up tile in B - and the running argmax for the LM head).
 // Between projections the consumers do the row-wide steps redundantly in every CTA (the
 // residual stream h lives in each CTA's shared memory): residual add, RMSNorm, activation
-// prep; attention runs on one CTA per (KV head, query-head pair).
+// prep; attention runs on one CTA per (KV head, query-head pair) and preps its output for the
+// o projection; the gate/up output is prepped for the down projection in 64-column chunks,
+// one chunk per CTA.
+//
+// Exchange between CTAs.  The vectors a phase produces for all CTAs (q/k/v, o, gate/up, down
+// outputs, the LM head's argmax partials) are 64-bit words: the value and the generation of
+// the producing phase.  A reader stages them and re-reads any word that does not carry the
+// generation it expects yet, so no grid barrier separates a projection from its readers;
+// every phase reads the whole output of the phase before it, so no producer can overwrite a
+// word that a reader still needs.  Grid barriers remain after attention (the o projection's
+// prepped input) and, on one GPU, after the down-input prep.
+//
+// Tensor parallelism (tp_world > 1, one process per GPU).  Every projection's units are dealt
+// over all ranks' CTAs; producers store the tagged words into every rank's exchange buffer
+// (peer stores over NVLink), the down-input prep publishes tagged codes and scales, and the
+// per-GPU steps (norms, attention, the preps' inputs) run on every rank.  No cross-GPU barrier
+// is needed: the tags carry the ordering.
 //
 // Work split.  Each projection's 16-row units are dealt in contiguous ranges, and the CTA that
 // receives the remainder units rotates from one projection to the next, so every CTA streams
 // about the same bytes per layer and the ring absorbs the one-unit imbalance of a projection.
 //
-// Every wait is bounded: an mbarrier or grid-barrier wait gives up after kWaitNs, sets the
-// error word and the CTA's abort flag.  After that every wait returns at once, but the
-// consumers keep their control flow (every loop runs its full trip count and reaches every
-// named barrier, with all addresses depending on shapes only), so no warp is left waiting at
-// a barrier; the producer stops issuing and waits, bounded, for the copies it issued.
+// Every wait is bounded: an mbarrier, grid-barrier, counter or tagged-word wait gives up after
+// kWaitNs (kTpWaitNs across ranks), sets the error word (of every rank) and the CTA's abort
+// flag.  After that every wait returns at once, but the consumers keep their control flow
+// (every loop runs its full trip count and reaches every named barrier, with all addresses
+// depending on shapes only), so no warp is left waiting at a barrier; the producer stops
+// issuing and waits, bounded, for the copies it issued.
 #include <algorithm>
 
 #include "kernels.cuh"

@@ -50,11 +50,12 @@ DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why);
 
 /* Phase trace of the persistent kernel's last step, recorded when the engine was created with
  * env DPUF_CUDA_TRACE_DECODE=1 (otherwise returns -1).  Per CTA, per_cta globaltimer stamps
- * (ns): for each layer the end of norm1, q/k/v, barrier, attention, barrier, o prep, o,
- * barrier, norm2, gate/up, barrier, down prep, down, barrier (14); then step start, embedding,
- * final norm, LM head, barrier, argmax (6); then the producer's start of each projection
- * (4 per layer, then the LM head).  *n_ctas and *per_cta receive the shape; out (optional)
- * receives n_ctas * per_cta values when max_values is large enough (else -2). */
+ * (ns): for each layer the end of norm1, q/k/v, its CTA barrier, attention, the grid barrier,
+ * o prep, o, its CTA barrier, norm2, gate/up, its CTA barrier, down prep, down, its CTA
+ * barrier (14); then step start, embedding, final norm, LM head, its CTA barrier, argmax (6);
+ * then the producer's start of each projection (4 per layer, then the LM head).  *n_ctas and
+ * *per_cta receive the shape; out (optional) receives n_ctas * per_cta values when max_values
+ * is large enough (else -2). */
 DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_t* per_cta, uint64_t* out,
                                            int64_t max_values);
 
