@@ -48,7 +48,8 @@ cudaError_t configure_kernels() {
 
 namespace {
 
-constexpr int kMaxSlots = 8;
+constexpr int kMaxSlots = 8;       // the reference's slot count (DPUF_MAX_SLOTS)
+constexpr int kMaxSlotsEnv = 256;  // upper bound of env DPUF_CUDA_SLOTS (batched serving)
 constexpr int kMaxPrefixes = 8;
 
 #define CK(expr)                                                                                  \
@@ -80,10 +81,10 @@ struct Prefix {
 struct StepKey {
   int M, only_last, keep, za;
   uint32_t margin_bits;
-  int slot, greedy_loop;
+  int slot, greedy_loop, batch;
   bool operator<(const StepKey& o) const {
-    return std::tie(M, only_last, keep, za, margin_bits, slot, greedy_loop) <
-           std::tie(o.M, o.only_last, o.keep, o.za, o.margin_bits, o.slot, o.greedy_loop);
+    return std::tie(M, only_last, keep, za, margin_bits, slot, greedy_loop, batch) <
+           std::tie(o.M, o.only_last, o.keep, o.za, o.margin_bits, o.slot, o.greedy_loop, o.batch);
   }
 };
 
@@ -92,6 +93,13 @@ struct Staging {
   int32_t ids[kMaxBatch];
   int32_t pos0;
   int32_t pad[3];
+};
+// Per-row inputs of a batched decode step (rows are independent sequences): position and the
+// row's slot cache.
+struct BatchStaging {
+  int32_t pos[kMaxBatch];
+  float* k[kMaxBatch];
+  float* v[kMaxBatch];
 };
 
 struct Engine {
@@ -109,7 +117,8 @@ struct Engine {
   const float* out_norm = nullptr;
   float *cos_tab = nullptr, *sin_tab = nullptr;
 
-  Slot slots[kMaxSlots];
+  std::vector<Slot> slots;  // kMaxSlots, or env DPUF_CUDA_SLOTS for batched serving
+  int n_slots = kMaxSlots;
   int active = 0;
   Prefix prefixes[kMaxPrefixes];
 
@@ -127,6 +136,9 @@ struct Engine {
   int32_t* d_hist = nullptr;   // greedy-loop token history [max_seq] and step counter
   int32_t* d_hist_step = nullptr;
   Staging* stage = nullptr;  // pinned
+  BatchStaging* bstage = nullptr;  // pinned
+  BatchStaging* d_bstage = nullptr;
+  int32_t* d_next = nullptr;       // greedy ids of a batched step [kMaxBatch]
   float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
   uint2* d_exp_slots = nullptr;
   unsigned* d_counter = nullptr;  // last-block counters of the multi-CTA argmax
@@ -317,7 +329,8 @@ void destroy_engine(Engine* e) {
   for (void* p : e->tp_peer)
     if (p) cudaIpcCloseMemHandle(p);
   cudaFree(e->tp_buf);
-  cudaFreeHost(e->stage); cudaFreeHost(e->h_logits);
+  cudaFreeHost(e->stage); cudaFreeHost(e->h_logits); cudaFreeHost(e->bstage);
+  cudaFree(e->d_bstage); cudaFree(e->d_next);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -327,6 +340,7 @@ struct StepParams {
   int M, only_last, keep, za;
   float margin;
   bool greedy_loop;  // ids/pos live on the device and advance by greedy feedback
+  bool batch = false;  // rows are independent sequences (per-row slot and position)
 };
 
 LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
@@ -367,11 +381,15 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   const int M = P.M, H = e->H;
   if (!P.greedy_loop)
     CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
+  if (P.batch)
+    CK(cudaMemcpyAsync(e->d_bstage, e->bstage, sizeof(BatchStaging), cudaMemcpyHostToDevice, e->stream));
   CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
   const Slot& sl = e->slots[e->active];
   for (int l = 0; l < e->L; l++) {
     const LayerDev& lw = e->layers[l];
-    KvCache kv{sl.k + (size_t)l * e->nkv * e->S * e->hd, sl.v + (size_t)l * e->nkv * e->S * e->hd, e->S};
+    const size_t layer_off = (size_t)l * e->nkv * e->S * e->hd;
+    KvCache kv{sl.k + layer_off, sl.v + layer_off, e->S};
+    if (P.batch) kv = KvCache{nullptr, nullptr, e->S, e->d_bstage->pos, e->d_bstage->k, e->d_bstage->v, layer_off};
     // 1-2. [h += hn] RMSNorm + prep of q/k/v inputs
     {
       const W12* ws[3] = {&lw.q, &lw.k, &lw.v};
@@ -415,7 +433,8 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
       CK(run_linear(e, Lc, J, M, nullptr));
     }
     // 9-11. SwiGLU + prep, down (optionally pruned to the first `keep` tiles)
-    CK(launch_swiglu_prep(Lc, e->gate, e->up, M, e->I, e->deadzone, e->nt_ref, lw.down.signs, e->prep[0], e->et));
+    CK(launch_swiglu_prep(Lc, e->gate, e->up, M, e->I, e->deadzone, e->nt_ref, lw.down.signs, e->prep[0], e->et,
+                          P.batch));
     const int keep = (P.keep > 0 && P.keep < lw.down.n_tiles) ? P.keep : lw.down.n_tiles;
     CK(run_linear(e, Lc, one_job(lw.down, e->prep[0], e->hn, H, 0, keep), M, nullptr));
     if (keep < lw.down.n_tiles) CK(launch_zero_rows(Lc, e->hn, M, H, keep * kTileRows));
@@ -442,6 +461,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   if (P.greedy_loop)
     CK(launch_greedy_advance(Lc, e->logits, e->V, e->d_part, e->d_counter, e->d_ids, e->d_pos0, e->d_hist,
                              e->d_hist_step));
+  if (P.batch) CK(launch_argmax_rows(Lc, e->logits, e->V, lm_M, e->d_next));
   return cudaSuccess;
 }
 
@@ -449,7 +469,10 @@ cudaError_t run_step(Engine* e, const StepParams& P) {
   if (!e->use_graphs) return enqueue_step(e, P);
   uint32_t mb;
   memcpy(&mb, &P.margin, 4);
-  const StepKey key{P.M, P.only_last, P.keep, P.za, mb, e->active, P.greedy_loop ? 1 : 0};
+  // a batched step reads its slots' caches through device pointers, so its graph does not
+  // depend on the active slot
+  const StepKey key{P.M, P.only_last, P.keep, P.za, mb, P.batch ? -1 : e->active, P.greedy_loop ? 1 : 0,
+                    P.batch ? 1 : 0};
   auto it = e->graphs.find(key);
   if (it == e->graphs.end()) {
     cudaGraph_t g;
@@ -548,6 +571,7 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   A.tp_rank = 0;
   A.tp_world = 1;
   A.stage_cap = decode_stage_cap(A);
+  A.attn_floats = (int)(decode_uni_bytes(A) / sizeof(float));
   size_t limit = 0;
   if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");
   A.n_ring = decode_ring_slots(A, limit);
@@ -780,6 +804,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   const char* dz = getenv("DPUF_SWIGLU_DEADZONE");
   e->deadzone = dz ? (float)atof(dz) : 0.005f;
   e->nt_ref = c.n_threads <= 0 ? 8 : std::min(c.n_threads, 32);
+  e->n_slots = std::max(1, std::min(kMaxSlotsEnv, env_int("DPUF_CUDA_SLOTS", kMaxSlots)));
+  e->slots.resize(e->n_slots);
   e->use_pdl = env_int("DPUF_CUDA_PDL", 1) != 0;
   e->use_graphs = env_int("DPUF_CUDA_GRAPHS", 1) != 0;
 
@@ -859,7 +885,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
       cudaMalloc(&e->d_flag, 16) || cudaMalloc(&e->d_b12, 16) || cudaMalloc(&e->d_argmax, B * 4) ||
       cudaMalloc(&e->d_hist, (size_t)(e->S + 4) * 4) || cudaMalloc(&e->d_counter, 64) ||
       cudaMalloc(&e->d_part, kArgmaxBlocks * sizeof(float2)) ||
-      cudaMallocHost(&e->stage, sizeof(Staging)) || cudaMallocHost(&e->h_logits, (size_t)e->V * 4))
+      cudaMallocHost(&e->stage, sizeof(Staging)) || cudaMallocHost(&e->bstage, sizeof(BatchStaging)) ||
+      cudaMalloc(&e->d_bstage, sizeof(BatchStaging)) || cudaMalloc(&e->d_next, kMaxBatch * 4) || cudaMallocHost(&e->h_logits, (size_t)e->V * 4))
     return fail("activation buffers");
   if (cudaMalloc(&e->split.pairs, gemv_split_pairs_bytes(ld)) ||
       cudaMalloc(&e->split.acc, (size_t)kGemvMaxCtas * kTileRows * sizeof(float)) ||
@@ -944,7 +971,7 @@ DPUF_EXPORT void dpuf_engine_destroy(void* handle) { dpuf::destroy_engine((Engin
 
 DPUF_EXPORT int32_t dpuf_engine_set_slot(void* handle, int32_t slot_id) {
   Engine* e = (Engine*)handle;
-  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots) return -1;
+  if (!e || slot_id < 0 || slot_id >= e->n_slots) return -1;
   cudaSetDevice(e->device);
   if (dpuf::slot_alloc(e, slot_id) != cudaSuccess) return -2;
   e->active = slot_id;
@@ -953,11 +980,11 @@ DPUF_EXPORT int32_t dpuf_engine_set_slot(void* handle, int32_t slot_id) {
 
 DPUF_EXPORT int32_t dpuf_engine_get_slot(void* handle) { return handle ? ((Engine*)handle)->active : 0; }
 
-DPUF_EXPORT int32_t dpuf_engine_num_slots(void* handle) { return handle ? dpuf::kMaxSlots : 1; }
+DPUF_EXPORT int32_t dpuf_engine_num_slots(void* handle) { return handle ? ((Engine*)handle)->n_slots : 1; }
 
 DPUF_EXPORT void dpuf_engine_reset_slot(void* handle, int32_t slot_id) {
   Engine* e = (Engine*)handle;
-  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots || !e->slots[slot_id].k) return;
+  if (!e || slot_id < 0 || slot_id >= e->n_slots || !e->slots[slot_id].k) return;
   cudaSetDevice(e->device);
   const size_t n = (size_t)e->L * e->S * e->kvd * 4;
   cudaMemsetAsync(e->slots[slot_id].k, 0, n, e->stream);
@@ -1005,7 +1032,7 @@ DPUF_EXPORT int32_t dpuf_engine_freeze_prefix(void* handle, int32_t pfx_id, int3
 
 DPUF_EXPORT int32_t dpuf_engine_apply_prefix(void* handle, int32_t slot_id, int32_t pfx_id) {
   Engine* e = (Engine*)handle;
-  if (!e || slot_id < 0 || slot_id >= dpuf::kMaxSlots || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes) return 0;
+  if (!e || slot_id < 0 || slot_id >= e->n_slots || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes) return 0;
   dpuf::Prefix& p = e->prefixes[pfx_id];
   if (!p.valid || p.len <= 0) return 0;
   cudaSetDevice(e->device);
@@ -1107,6 +1134,56 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
   e->last_zone_used = 0;
   e->last_logits = persistent ? e->dec.logits : e->logits;
   return rc;
+}
+
+// One greedy step of n independent sequences (batched serving): row i is sequence slots[i] at
+// position pos[i] with input ids[i].  Every row is computed as that sequence's own batch-1 step
+// (same kernels as an M-row step, with the reference's per-step vector/scalar SwiGLU split of
+// one row), so each row's logits and id equal dpuf_engine_forward_token's on that slot.
+DPUF_EXPORT int32_t dpuf_cuda_decode_batch(void* handle, int32_t n, const int32_t* slots, const int32_t* ids,
+                                           const int32_t* pos, int32_t* next_ids, float* logits_out) {
+  Engine* e = (Engine*)handle;
+  if (!e || !slots || !ids || !pos || !next_ids) return -1;
+  if (n <= 0 || n > dpuf::kMaxBatch) return -2;
+  std::vector<char> seen(e->n_slots, 0);
+  for (int i = 0; i < n; i++) {
+    if (slots[i] < 0 || slots[i] >= e->n_slots || seen[slots[i]]) {
+      dpuf::set_error("decode_batch: slot ids must be valid and distinct");
+      return -1;
+    }
+    seen[slots[i]] = 1;
+    if (ids[i] < 0 || ids[i] >= e->tok.rows) {
+      dpuf::set_error("token id out of range");
+      return -1;
+    }
+    if (pos[i] < 0 || pos[i] >= e->S) return -3;
+  }
+  if (cudaSetDevice(e->device) != cudaSuccess) return -4;
+  for (int i = 0; i < n; i++) {
+    if (dpuf::slot_alloc(e, slots[i]) != cudaSuccess) return -2;
+    e->stage->ids[i] = ids[i];
+    e->bstage->pos[i] = pos[i];
+    e->bstage->k[i] = e->slots[slots[i]].k;
+    e->bstage->v[i] = e->slots[slots[i]].v;
+  }
+  // each row is a batch-1 step: the decode knob DPUF_GEN_KEEP_TILES, no Zone A (the reference
+  // tests lm_M == 1 per call; a batched call has lm_M == n)
+  dpuf::StepParams P = dpuf::step_params(e, 1, 1);
+  P.M = n;
+  P.only_last = 0;
+  P.za = 0;
+  P.batch = true;
+  if (dpuf::run_step(e, P) != cudaSuccess) return -4;
+  if (cudaMemcpyAsync(next_ids, e->d_next, (size_t)n * 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+    return -4;
+  if (logits_out &&
+      cudaMemcpyAsync(logits_out, e->logits, (size_t)n * e->V * 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+    return -4;
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+  e->last_rows = n;
+  e->last_zone_used = 0;
+  e->last_logits = e->logits;
+  return 0;
 }
 
 DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out) {

@@ -72,6 +72,13 @@ struct KvCache {
   float* k;  // [n_kv][max_seq][hd] for this layer
   float* v;
   int max_seq;
+  // Batched decode (rows are independent sequences): token m's position tok_pos[m] and its
+  // slot's cache tok_k[m] / tok_v[m] ([L][n_kv][max_seq][hd]) + layer_off floats; null: the
+  // single cache above at positions *pos0 + m.
+  const int32_t* tok_pos;
+  float* const* tok_k;
+  float* const* tok_v;
+  size_t layer_off;
 };
 cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
                            const float* q_norm, const float* k_norm, float eps, const float* cos_tab,
@@ -79,9 +86,11 @@ cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, 
 // Exact causal attention (gqa_attn_head_pair_f32 order) for M tokens, output [M][n_q*hd].
 cudaError_t launch_attention(const Launch& L, const float* q, int M, int n_q, int n_kv, int hd, const int* pos0_dev,
                              KvCache kv, float* out, const ExpfTable& et);
-// SwiGLU with dead-zone over [M][I] and prep of the result for w_down.
+// SwiGLU with dead-zone over [M][I] and prep of the result for w_down.  per_row: every row is
+// its own batch-1 step (the reference's vector/scalar split of one row), else the split of one
+// M-token step.
 cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* up, int M, int I, float deadzone,
-                               int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et);
+                               int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et, bool per_row = false);
 // Zero rows [r0, H) of out[M][H] (down-projection tile pruning).
 cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0);
 
@@ -96,6 +105,8 @@ cudaError_t launch_zone_mask(const Launch& L, float* logits, int from, int V, co
 // hist[(*step)++]).
 constexpr int kArgmaxBlocks = 148;
 cudaError_t launch_argmax(const Launch& L, const float* logits, int V, float2* part, unsigned* counter, int32_t* out);
+// First-index argmax of each of M rows [M][V] into out[M].
+cudaError_t launch_argmax_rows(const Launch& L, const float* logits, int V, int M, int32_t* out);
 cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, float2* part, unsigned* counter,
                                   int32_t* ids, int32_t* pos0, int32_t* hist, int32_t* step);
 
@@ -157,6 +168,7 @@ struct DecodeArgs {
   int first_id, pos0, n_steps, write_logits;
   int grid, n_ring;
   int stage_cap;      // columns per staged piece of a vector being prepped (decode_stage_cap)
+  int attn_floats;    // shared-memory floats the attention items may use (decode_uni_bytes / 4)
   // Fused o-projection prep: the attention items prep their output columns (needs
   // head_dim % 64 == 0 and q_dim % 128 == 0); every CTA then copies the prepped vector.
   int fuse_o;
@@ -173,6 +185,7 @@ struct DecodeArgs {
 // Exchange generations of one decode step (q/k/v, o, gate/up, down per layer; the LM head).
 DPUF_HD int decode_phases(int L) { return 4 * L + 1; }
 int decode_stage_cap(const DecodeArgs& A);
+size_t decode_uni_bytes(const DecodeArgs& A);
 int decode_trace_events(int L);
 size_t decode_smem_bytes(const DecodeArgs& A);
 int decode_ring_slots(const DecodeArgs& A, size_t smem_limit);

@@ -38,13 +38,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
   const int g0 = pr * 2;
   const int nh = (g0 + 1 < groups) ? 2 : 1;  // pair path or lone head
   const int qh0 = kvh * groups + g0;
-  const int kv_len = *pos0_dev + m + 1;
+  const int kv_len = (kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m) + 1;
+  const float* kbase = kv.tok_k ? kv.tok_k[m] + kv.layer_off : kv.k;
+  const float* vbase = kv.tok_v ? kv.tok_v[m] + kv.layer_off : kv.v;
   float* qs = sm;                   // [2][hd]
   float* sc = qs + 2 * hd;          // [2][max_seq]
   float* kt = sc + attn_sc_floats(kv.max_seq);  // [kAttnKeyTile][hd + 8]
   for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) qs[i] = q[((size_t)m * n_q + qh0) * hd + i];
-  attn_pair_body(qs, nh, hd, kv_len, kv.k + (size_t)kvh * kv.max_seq * hd, kv.v + (size_t)kvh * kv.max_seq * hd,
-                 kv.max_seq, sc, kt, &sh, out + ((size_t)m * n_q + qh0) * hd, et, (int)threadIdx.x, CtaSync{});
+  attn_pair_body(qs, nh, hd, kv_len, kbase + (size_t)kvh * kv.max_seq * hd, vbase + (size_t)kvh * kv.max_seq * hd,
+                 kv.max_seq, sc, kt, 1, 0, nullptr, nullptr, &sh, out + ((size_t)m * n_q + qh0) * hd, et,
+                 (int)threadIdx.x, CtaSync{});
 }
 
 }  // namespace

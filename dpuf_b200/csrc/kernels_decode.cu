@@ -835,10 +835,16 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
                               DecShared& S) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int groups = A.nq / A.nkv, n_pairs = (groups + 1) / 2, hd = A.hd;
-  float* qs = scratch;                       // [2][hd]
-  float* sc = qs + 2 * hd;                   // [2][S]
-  float* kt = sc + attn_sc_floats(A.S);      // [kAttnKeyTile][hd + 8]; inputs staged here first
-  float *kin = kt, *vin = kt + hd, *qn = kt + 2 * hd, *kn = kt + 3 * hd, *cs = kt + 4 * hd, *sn = cs + hd / 2;
+  // scratch: qs [2][hd] | inputs (key, value, gains, RoPE row) [5 hd] | scores [2][kv_len
+  // padded to 4] | n_buf key/value tiles (as many as fit, at most kAttnMaxBuf)
+  const int kv_len = pos + 1, sc_stride = (kv_len + 3) & ~3;
+  float* qs = scratch;
+  float *kin = qs + 2 * hd, *vin = kin + hd, *qn = vin + hd, *kn = qn + hd, *cs = kn + hd, *sn = cs + hd / 2;
+  float* sc = qs + 7 * hd;
+  float* kt = sc + 2 * sc_stride;
+  const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
+  const int n_buf = max(1, min(kAttnMaxBuf, (int)((A.attn_floats - 7 * hd - 2 * sc_stride) / attn_tile_floats(hd))));
+  const int pre = min(n_buf, n_t);  // history key tiles fetched while q/k/v arrive
   for (int it = blockIdx.x; it < A.nkv * n_pairs; it += gridDim.x) {
     const int kvh = it / n_pairs, pr = it % n_pairs;
     const int g0 = pr * 2, nh = (g0 + 1 < groups) ? 2 : 1, qh0 = kvh * groups + g0;
@@ -847,8 +853,10 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
     named_sync(kBarAttn, kAttnThreads);  // scratch free (previous item done)
     {
       const int q4 = hd / 4;  // 16-byte pieces per vector
-      // gains and the RoPE row asynchronously while the pair's query heads, the key and the
-      // value (tagged words of the q/k/v phase) are read, one pair of elements per thread
+      // gains and the RoPE row asynchronously (one group), then the first key tiles of the
+      // history (rows < pos: they do not depend on this step), while the pair's query heads,
+      // the key and the value (tagged words of the q/k/v phase) are read, one pair of
+      // elements per thread
       for (int i = tid; i < q4; i += kAttnThreads) {
         if (Ly.q_norm) cp_async16_cg(qn + i * 4, Ly.q_norm + i * 4);
         if (Ly.k_norm) cp_async16_cg(kn + i * 4, Ly.k_norm + i * 4);
@@ -857,6 +865,8 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
           cp_async16_cg(sn + i * 4, A.sin_tab + (size_t)pos * (hd >> 1) + i * 4);
         }
       }
+      cp_async_commit();
+      for (int t = 0; t < pre; t++) attn_issue_tile(kt + (size_t)t * attn_tile_floats(hd), kc, t, pos, hd, tid);
       for (int i = tid * 2; i < (nh + 2) * hd; i += kAttnThreads * 2) {
         const int v = i / hd, o = i % hd;
         const uint64_t* src = (v < nh ? A.q + (size_t)(qh0 + v) * hd : (v == nh ? A.k : A.v) + (size_t)kvh * hd) + o;
@@ -865,7 +875,7 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
         if (tag_of(w.x) != gen || tag_of(w.y) != gen) w = wait_tagged2(src, gen, A, S);
         *(float2*)dst = make_float2(value_of(w.x), value_of(w.y));
       }
-      cp_async_commit_wait_all();
+      cp_async_wait_pending(pre);  // the gains and the RoPE row (the tiles may stay in flight)
     }
     named_sync(kBarAttn, kAttnThreads);
     if (warp == 0) {
@@ -876,8 +886,9 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
     } else if (warp < 2 + nh) {
       qk_norm_rope_warp(qs + (warp - 2) * hd, Ly.q_norm ? qn : nullptr, A.eps, hd, cs, sn, lane);
     }
-    attn_pair_body(qs, nh, hd, pos + 1, kc, vc, A.S, sc, kt, &S.attn, A.att + (size_t)qh0 * hd, A.et, tid,
-                   AttnSync{}, A.fuse_o != 0);
+    named_sync(kBarAttn, kAttnThreads);  // rotated queries and key in place
+    attn_pair_body(qs, nh, hd, kv_len, kc, vc, sc_stride, sc, kt, n_buf, pre, kin, vin, &S.attn,
+                   A.att + (size_t)qh0 * hd, A.et, tid, AttnSync{}, A.fuse_o != 0);
     if (A.fuse_o) {
       named_sync(kBarAttn, kAttnThreads);
       const int n_ch = nh * hd / 64;
@@ -1124,7 +1135,7 @@ size_t decode_uni_bytes(const DecodeArgs& A) {
   // its signs
   const size_t uni_stage =
       xb + std::max((size_t)A.H * 12 + (size_t)A.H / 8, (size_t)A.kmax * 4 + (size_t)A.kmax / 8) + 128;
-  const size_t uni_attn = attn_scratch_floats(A.hd, A.S) * sizeof(float);
+  const size_t uni_attn = ((size_t)7 * A.hd + attn_sc_floats(A.S) + attn_tile_floats(A.hd)) * sizeof(float);
   return std::max(std::max(uni_x, uni_stage), uni_attn);
 }
 int decode_stage_cap(const DecodeArgs& A) {

@@ -90,7 +90,9 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   const int m = blockIdx.x;
   const int hidx = blockIdx.y * (blockDim.x >> 5) + warp;
   if (hidx >= n_q + n_kv) return;
-  const int pos = *pos0_dev + m;
+  const int pos = kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m;
+  float* const kbase = kv.tok_k ? kv.tok_k[m] + kv.layer_off : kv.k;
+  float* const vbase = kv.tok_v ? kv.tok_v[m] + kv.layer_off : kv.v;
   const bool is_k = hidx < n_kv;
   const int head = is_k ? hidx : hidx - n_kv;
   float* vec = is_k ? k + ((size_t)m * n_kv + head) * hd : q + ((size_t)m * n_q + head) * hd;
@@ -101,11 +103,11 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   qk_norm_rope_warp(s, nw, eps, hd, cos_tab + (size_t)pos * (hd >> 1), sin_tab + (size_t)pos * (hd >> 1), lane);
   for (int i = lane; i < hd; i += 32) {
     vec[i] = s[i];
-    if (is_k) kv.k[((size_t)head * kv.max_seq + pos) * hd + i] = s[i];
+    if (is_k) kbase[((size_t)head * kv.max_seq + pos) * hd + i] = s[i];
   }
   if (is_k) {
     const float* vr = v + ((size_t)m * n_kv + head) * hd;
-    float* vc = kv.v + ((size_t)head * kv.max_seq + pos) * hd;
+    float* vc = vbase + ((size_t)head * kv.max_seq + pos) * hd;
     for (int i = lane; i < hd; i += 32) vc[i] = vr[i];
   }
 }
@@ -113,18 +115,20 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
 // ------------------------------------------------------------------ SwiGLU + prep for w_down
 // swiglu_one per element (layer_dev.cuh), then the prep of each 64-column chunk.
 __global__ void swiglu_prep_kernel(const float* __restrict__ gate, const float* __restrict__ up, int M, int I,
-                                   float dz, int nt, const uint8_t* __restrict__ signs, Act out, ExpfTable et) {
+                                   float dz, int nt, const uint8_t* __restrict__ signs, Act out, ExpfTable et,
+                                   bool per_row) {
   cudaGridDependencySynchronize();
   const int lane = threadIdx.x & 31;
   const int chunk = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int m = blockIdx.y;
   if (chunk * 64 >= I) return;
   const int c0 = chunk * 64;
-  const long long total = (long long)M * I;
-  const bool slab = (M >= 2) && ((M + 5) / 6 >= nt);
+  const long long total = per_row ? I : (long long)M * I;
+  const bool slab = !per_row && (M >= 2) && ((M + 5) / 6 >= nt);
   const long long ia = (long long)m * I + c0 + lane, ib = ia + 32;
-  const float a = swiglu_one(gate[ia], up[ia], dz, swiglu_vector_elem(ia, total, nt, slab), et);
-  const float b = swiglu_one(gate[ib], up[ib], dz, swiglu_vector_elem(ib, total, nt, slab), et);
+  const long long ea = per_row ? c0 + lane : ia, eb = ea + 32;  // element index within the split
+  const float a = swiglu_one(gate[ia], up[ia], dz, swiglu_vector_elem(ea, total, nt, slab), et);
+  const float b = swiglu_one(gate[ib], up[ib], dz, swiglu_vector_elem(eb, total, nt, slab), et);
   prep_chunk_warp(a, b, signs, c0, lane, out.q8 + (size_t)m * out.ld, out.xs + (size_t)m * (out.ld >> 5),
                   out.xm + (size_t)m * (out.ld >> 5));
 }
@@ -162,10 +166,10 @@ cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, 
 }
 
 cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* up, int M, int I, float deadzone,
-                               int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et) {
+                               int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et, bool per_row) {
   const int chunks = I / 64, wpb = 8;
   return launch_k(L, swiglu_prep_kernel, dim3((chunks + wpb - 1) / wpb, M), dim3(wpb * 32), 0, gate, up, M, I,
-                  deadzone, nt_ref, signs, out, et);
+                  deadzone, nt_ref, signs, out, et, per_row);
 }
 
 cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0) {

@@ -144,7 +144,26 @@ __global__ void __launch_bounds__(256) argmax_blocks_kernel(const float* __restr
   }
 }
 
+// First-index argmax of each of M rows of logits (one CTA per row): the greedy id of every
+// sequence of a batched decode step.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ logits, int V,
+                                                          int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  cudaGridDependencySynchronize();
+  const float* row = logits + (size_t)blockIdx.x * V;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) better(bv, bi, row[i], i);
+  block_argmax(bv, bi, sv, si);
+  if (threadIdx.x == 0) out[blockIdx.x] = (bi == 0x7fffffff) ? 0 : bi;
+}
+
 }  // namespace
+
+cudaError_t launch_argmax_rows(const Launch& L, const float* logits, int V, int M, int32_t* out) {
+  return launch_k(L, argmax_rows_kernel, dim3(M), dim3(256), 0, logits, V, out);
+}
 
 cudaError_t launch_greedy_advance(const Launch& L, const float* logits, int V, float2* part, unsigned* counter,
                                   int32_t* ids, int32_t* pos0, int32_t* hist, int32_t* step) {

@@ -274,10 +274,15 @@ DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, i
 //   PV      per output dim: fma(p_k, v_kd, acc) over k ascending (pair path); the lone-head
 //           path takes keys two at a time, k+1 first (dpuf_engine.c:541-548).
 // qs [2][hd] holds the (normed, rotated) query heads; kc/vc are this KV head's cache rows
-// [max_seq][hd] (read through L2: other CTAs may have written them); sc [2][max_seq] and
-// kt [kAttnKeyTile][hd+8] are scratch; out receives nh * hd values.
+// [max_seq][hd] (read through L2: other CTAs may have written them); sc [2][sc_stride] and
+// n_buf key/value tiles kt [n_buf][kAttnKeyTile][hd+8] are scratch; out receives nh * hd
+// values.  Up to n_buf tiles are in flight (cp.async groups); the caller may have issued the
+// first `pre` key tiles already (attn_issue_tile, one committed group each, nothing committed
+// after them).  cur_k / cur_v (optional) are the key and value of position kv_len - 1, which
+// then replace that row of its tile instead of being read from the cache.
 constexpr int kAttnThreads = 256;
-constexpr int kAttnKeyTile = 32;  // keys staged per pass (8 threads per key)
+constexpr int kAttnKeyTile = 32;  // keys per tile (8 threads per key)
+constexpr int kAttnMaxBuf = 3;    // tiles in flight at most
 
 struct AttnShared {
   float red[2][kAttnThreads / 32];
@@ -285,11 +290,12 @@ struct AttnShared {
   float inv_s[2], max_s[2];
 };
 
-// Scratch layout: qs [2][hd] | sc [2][max_seq] padded to a multiple of 4 | kt [kAttnKeyTile][hd+8]
-// (the key tile starts 16-byte aligned for the async copies).
+DPUF_HD size_t attn_tile_floats(int hd) { return (size_t)kAttnKeyTile * (hd + 8); }
+// Scratch layout of the per-step kernel: qs [2][hd] | sc [2][max_seq] padded to a multiple of
+// 4 | one tile (16-byte aligned for the async copies).
 DPUF_HD size_t attn_sc_floats(int max_seq) { return 2 * (((size_t)max_seq + 3) & ~(size_t)3); }
 DPUF_HD size_t attn_scratch_floats(int hd, int max_seq) {
-  return (size_t)2 * hd + attn_sc_floats(max_seq) + (size_t)kAttnKeyTile * (hd + 8);
+  return (size_t)2 * hd + attn_sc_floats(max_seq) + attn_tile_floats(hd);
 }
 
 // ------------------------------------------------------------------ async copies to shared
@@ -302,41 +308,72 @@ DPUF_DEV void cp_async8_ca(void* dst, const void* src) {  // read-only tables
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
 }
+DPUF_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 DPUF_DEV void cp_async_commit_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+// Waits until at most n (0..2) of this thread's most recent groups are pending.
+DPUF_DEV void cp_async_wait_pending(int n) {
+  if (n <= 0)
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  else if (n == 1)
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+  else
+    asm volatile("cp.async.wait_group 2;" ::: "memory");
+}
 
-// Copies rows [0, nk) of a row-major [.][hd] array (read through L2; hd % 4 == 0, 16-byte
-// aligned rows) into dst with a padded row stride of hd + 8, as 16-byte async copies; each
-// thread waits for its own copies, the caller then synchronises the threads.
-DPUF_DEV void stage_rows(float* dst, const float* src, int nk, int hd, int tid) {
+// Issues (and commits, as one group of this thread) the copy of tile `t` of a cache [.][hd]
+// into buffer `buf` with a padded row stride of hd + 8: rows [32t, min(32t + 32, n_rows)) -
+// n_rows excludes a row the caller supplies itself.  Every thread commits a group, with or
+// without copies.
+DPUF_DEV void attn_issue_tile(float* buf, const float* src, int t, int n_rows, int hd, int tid) {
+  const int t0 = t * kAttnKeyTile;
+  const int nk = max(0, min(kAttnKeyTile, n_rows - t0));
   const int per_row = hd >> 2, n = nk * per_row;
   for (int i = tid; i < n; i += kAttnThreads) {
     const int r = i / per_row, c = (i - r * per_row) * 4;
-    cp_async16_cg(dst + r * (hd + 8) + c, src + (size_t)r * hd + c);
+    cp_async16_cg(buf + r * (hd + 8) + c, src + (size_t)(t0 + r) * hd + c);
   }
-  cp_async_commit_wait_all();
+  cp_async_commit();
+}
+
+// Waits for tile t (tiles t+1 .. min(t + n_buf, n_t) - 1 may stay in flight), writes row
+// `cur_row` from `cur` when the tile holds it, then sync().
+template <typename Sync>
+DPUF_DEV void attn_land_tile(float* buf, int t, int n_t, int n_buf, const float* cur, int cur_row, int hd, int tid,
+                             Sync sync) {
+  cp_async_wait_pending(min(n_buf - 1, n_t - 1 - t));
+  const int t0 = t * kAttnKeyTile;
+  if (cur && cur_row >= t0 && cur_row < t0 + kAttnKeyTile)
+    for (int i = tid; i < (hd >> 2); i += kAttnThreads)
+      *(float4*)(buf + (cur_row - t0) * (hd + 8) + 4 * i) = *(const float4*)(cur + 4 * i);
+  sync();
 }
 
 template <typename Sync>
 DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float* kc, const float* vc,
-                             int max_seq, float* sc, float* kt, AttnShared* sh, float* out, const ExpfTable& et,
-                             int tid, Sync sync, bool out_to_qs = false) {
+                             int sc_stride, float* sc, float* kt, int n_buf, int pre, const float* cur_k,
+                             const float* cur_v, AttnShared* sh, float* out, const ExpfTable& et, int tid, Sync sync,
+                             bool out_to_qs = false) {
   const int lane = tid & 31;
   const int kvs = hd + 8;  // padded smem row of a staged key
+  const size_t tile = attn_tile_floats(hd);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
+  const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
+  const int n_rows = cur_k ? kv_len - 1 : kv_len;  // rows read from the cache
   float lmax[2] = {-1e30f, -1e30f};
   // ---- scores
-  for (int t0 = 0; t0 < kv_len; t0 += kAttnKeyTile) {
+  for (int t = pre; t < min(n_buf, n_t); t++) attn_issue_tile(kt + (size_t)t * tile, kc, t, n_rows, hd, tid);
+  for (int t = 0; t < n_t; t++) {
+    const int t0 = t * kAttnKeyTile;
     const int nk = min(kAttnKeyTile, kv_len - t0);
-    sync();
-    stage_rows(kt, kc + (size_t)t0 * hd, nk, hd, tid);
-    sync();
+    float* buf = kt + (size_t)(t % n_buf) * tile;
+    attn_land_tile(buf, t, n_t, n_buf, cur_k, kv_len - 1, hd, tid, sync);
     const int key = tid >> 3, l = tid & 7;
-    const int t = t0 + key;
+    const int tk = t0 + key;
     const bool valid = key < nk;
-    const float* kp = kt + key * kvs;
+    const float* kp = buf + key * kvs;
     for (int h = 0; h < nh; h++) {
       const float* qv = qs + h * hd;
       // Shuffle trees run on all lanes (keys of one warp may sit on both sides of kv4).
@@ -360,13 +397,17 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
         }
         t_split = tree8_split(__fadd_rn(a0, a1));
       }
-      float s = __fmul_rn((t < kv4) ? t_pairs : t_split, scale);
+      float sv = __fmul_rn((tk < kv4) ? t_pairs : t_split, scale);
       if (valid && l == 0) {
-        sc[h * max_seq + t] = s;
-        lmax[h] = max_ps(lmax[h], s);
+        sc[h * sc_stride + tk] = sv;
+        lmax[h] = max_ps(lmax[h], sv);
       }
     }
+    sync();  // the buffer is free again
+    if (t + n_buf < n_t) attn_issue_tile(buf, kc, t + n_buf, n_rows, hd, tid);
   }
+  // the first value tiles load while the softmax runs
+  for (int t = 0; t < min(n_buf, n_t); t++) attn_issue_tile(kt + (size_t)t * tile, vc, t, n_rows, hd, tid);
   // ---- max
   for (int h = 0; h < nh; h++) {
     float v = warp_max(lmax[h]);
@@ -382,73 +423,75 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
   // ---- exp over the 8-aligned part
   for (int h = 0; h < nh; h++) {
     const float mx = sh->max_s[h];
-    for (int k = tid; k < kv8; k += kAttnThreads) sc[h * max_seq + k] = exp_poly(__fsub_rn(sc[h * max_seq + k], mx));
+    for (int k = tid; k < kv8; k += kAttnThreads)
+      sc[h * sc_stride + k] = exp_poly(__fsub_rn(sc[h * sc_stride + k], mx));
   }
   sync();
   // ---- lane sums (8 sequential chains per head); the <= 7 tail exponentials (glibc expf) are
   // independent, so eight more threads per head evaluate them meanwhile
   if (tid < 8 * nh) {
     const int h = tid >> 3, l = tid & 7;
-    const float* s = sc + h * max_seq;
+    const float* sp = sc + h * sc_stride;
     float acc = 0.0f;
-    for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, s[k]);
+    for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, sp[k]);
     sh->lane_sum[h][l] = acc;
   } else if (tid >= 64 && tid < 64 + 8 * nh) {
     const int h = (tid - 64) >> 3, k = kv8 + ((tid - 64) & 7);
     if (k < kv_len) {
-      float* s = sc + h * max_seq;
-      s[k] = glibc_expf(__fsub_rn(s[k], sh->max_s[h]), et);
+      float* sp = sc + h * sc_stride;
+      sp[k] = glibc_expf(__fsub_rn(sp[k], sh->max_s[h]), et);
     }
   }
   sync();
   // split tree of the lane sums, then the tail added in order
   if (tid < nh) {
-    const float* s = sc + tid * max_seq;
-    float sp = tree8_split_arr(sh->lane_sum[tid]);
-    for (int k = kv8; k < kv_len; k++) sp = __fadd_rn(sp, s[k]);
-    sh->inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(sp, 1e-12f));
+    const float* sp = sc + tid * sc_stride;
+    float su = tree8_split_arr(sh->lane_sum[tid]);
+    for (int k = kv8; k < kv_len; k++) su = __fadd_rn(su, sp[k]);
+    sh->inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(su, 1e-12f));
   }
   sync();
   for (int h = 0; h < nh; h++) {
     const float inv = sh->inv_s[h];
-    for (int k = tid; k < kv_len; k += kAttnThreads) sc[h * max_seq + k] = __fmul_rn(sc[h * max_seq + k], inv);
+    for (int k = tid; k < kv_len; k += kAttnThreads) sc[h * sc_stride + k] = __fmul_rn(sc[h * sc_stride + k], inv);
   }
-  sync();
-  // ---- PV: value rows staged a tile at a time (kt is free again); thread o owns outputs
-  // o and o + kAttnThreads, each a sequential chain over the keys in the reference's order
+  // ---- PV: thread o owns outputs o and o + kAttnThreads, each a sequential chain over the
+  // keys in the reference's order
   float acc[2] = {0.0f, 0.0f};
   const int hd8 = hd & ~7;
-  for (int t0 = 0; t0 < kv_len; t0 += kAttnKeyTile) {
+  for (int t = 0; t < n_t; t++) {
+    const int t0 = t * kAttnKeyTile;
     const int nk = min(kAttnKeyTile, kv_len - t0);
-    sync();
-    stage_rows(kt, vc + (size_t)t0 * hd, nk, hd, tid);
-    sync();
+    float* buf = kt + (size_t)(t % n_buf) * tile;
+    attn_land_tile(buf, t, n_t, n_buf, cur_v, kv_len - 1, hd, tid, sync);
 #pragma unroll
     for (int j = 0; j < 2; j++) {
       const int o = tid + j * kAttnThreads;
       if (o >= nh * hd) break;
       const int h = o / hd, d = o % hd;
-      const float* p = sc + h * max_seq + t0;
-      const float* vt = kt + d;
+      const float* pp = sc + h * sc_stride + t0;
+      const float* vt = buf + d;
       float a = acc[j];
       if (nh == 2) {
-        for (int k = 0; k < nk; k++) a = __fmaf_rn(p[k], vt[k * kvs], a);
+        for (int k = 0; k < nk; k++) a = __fmaf_rn(pp[k], vt[k * kvs], a);
       } else if ((hd & 63) == 0) {
         // keys two at a time, k+1 first (tiles hold an even number of keys but the last)
         int k = 0;
         for (; k + 1 < nk; k += 2) {
-          const float t1 = __fmaf_rn(p[k + 1], vt[(k + 1) * kvs], a);
-          a = __fmaf_rn(p[k], vt[k * kvs], t1);
+          const float t1 = __fmaf_rn(pp[k + 1], vt[(k + 1) * kvs], a);
+          a = __fmaf_rn(pp[k], vt[k * kvs], t1);
         }
-        if (k < nk) a = __fmaf_rn(p[k], vt[k * kvs], a);
+        if (k < nk) a = __fmaf_rn(pp[k], vt[k * kvs], a);
       } else {
         for (int k = 0; k < nk; k++) {
-          const float pv = p[k], vv = vt[k * kvs];
+          const float pv = pp[k], vv = vt[k * kvs];
           a = (d < hd8) ? __fmaf_rn(pv, vv, a) : __fadd_rn(a, __fmul_rn(pv, vv));
         }
       }
       acc[j] = a;
     }
+    sync();  // the buffer is free again
+    if (t + n_buf < n_t) attn_issue_tile(buf, vc, t + n_buf, n_rows, hd, tid);
   }
   // (with out_to_qs the outputs also replace the queries, which are no longer read)
 #pragma unroll

@@ -73,6 +73,8 @@ def cuda_lib() -> ctypes.CDLL:
     lib.dpuf_cuda_prepare_expf_table.restype = ctypes.c_int64
     lib.dpuf_cuda_matmul_noalloc.restype = _I32
     lib.dpuf_cuda_matmul_noalloc.argtypes = [_I32] * 4 + [_VP] * 6
+    lib.dpuf_cuda_decode_batch.restype = _I32
+    lib.dpuf_cuda_decode_batch.argtypes = [_VP, _I32, _VP, _VP, _VP, _VP, _VP]
     lib.dpuf_cuda_tp_handle.restype = _I32
     lib.dpuf_cuda_tp_handle.argtypes = [_VP, _I32, _I32, _VP]
     lib.dpuf_cuda_tp_attach.restype = _I32
@@ -169,6 +171,21 @@ class CudaTransformerEngine:
         if rc != 0:
             raise RuntimeError(f"dpuf_cuda_decode_greedy failed with rc={rc}: {last_error()}")
         return [int(i) for i in ids], float(ms.value)
+
+    def decode_batch(self, slots, ids, pos, want_logits: bool = False):
+        """One greedy step of independent sequences (row i: slot slots[i], position pos[i], input
+        ids[i]); returns the next ids (and the [n][vocab] logits when asked)."""
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        pos = np.ascontiguousarray(pos, dtype=np.int32)
+        n = slots.size
+        nxt = np.zeros(n, np.int32)
+        logits = np.empty((n, self.vocab_size), np.float32) if want_logits else None
+        rc = self.lib.dpuf_cuda_decode_batch(self._handle, n, slots.ctypes.data, ids.ctypes.data, pos.ctypes.data,
+                                             nxt.ctypes.data, logits.ctypes.data if want_logits else None)
+        if rc != 0:
+            raise RuntimeError(f"dpuf_cuda_decode_batch failed with rc={rc}: {last_error()}")
+        return (nxt, logits) if want_logits else nxt
 
     def persistent_decode(self) -> tuple[bool, str]:
         """Whether batch-1 steps run as the persistent kernel, and why not."""

@@ -31,6 +31,17 @@ DPUF_EXPORT int32_t dpuf_cuda_forward_greedy(void* handle, int32_t n_tokens, con
 DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int32_t pos0, int32_t n_steps,
                                             int32_t* ids_out, float* device_ms);
 
+/* One greedy decode step of n independent sequences (batched serving; the reference runs them
+ * one after another): row i continues the sequence in slot slots[i] (distinct, allocated on
+ * first use) at position pos[i] with input token ids[i].  Every row is computed as that
+ * sequence's own batch-1 step (the M-row kernels, with the reference's one-row SwiGLU
+ * vector/scalar split), so its logits and id equal dpuf_engine_forward_token's on that slot
+ * (DPUF_GEN_KEEP_TILES applies; Zone A does not).  next_ids[n] (host) receive the greedy ids,
+ * logits_out (optional, host) [n][vocab].  Env DPUF_CUDA_SLOTS (default 8, the reference's
+ * count; at most 256) sets the number of slots at create.  Returns the forward codes. */
+DPUF_EXPORT int32_t dpuf_cuda_decode_batch(void* handle, int32_t n, const int32_t* slots, const int32_t* ids,
+                                           const int32_t* pos, int32_t* next_ids, float* logits_out);
+
 /* Copies the last forward's logits row `row` (0-based among the rows produced) to host. */
 DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out);
 
