@@ -258,6 +258,72 @@ def run_zone_config(hbm_peak: float, peak_kind: str, n_vec: int = 4096, za: int 
                       "peak_kind": peak_kind, "us_per_vector": round(s / n_vec * 1e6, 2)}), flush=True)
 
 
+def run_serve_config(args, hbm_peak: float, peak_kind: str):
+    """Config 5 (batched serving): the 8B-shaped model, n_seq independent sequences with
+    random prompt_len-token prompts (seed 1000 + i), each prefilled into its own slot in
+    256-token forward_batch calls, then `steps` greedy decode steps of all sequences at once
+    through dpuf_cuda_decode_batch (one CUDA-graph launch per step, ids in, ids out).  The
+    timed region is the decode steps only; each call is synchronous, so the time is wall clock
+    around them (which is also the end-to-end time: it includes the per-step id copies)."""
+    from dpuf_b200 import engine, model as mdl
+
+    n_seq, plen, steps, warm = args.serve_seqs, args.serve_prompt, args.serve_steps, args.warmup
+    shape = mdl.QWEN3_8B
+    if plen + warm + steps > shape.max_seq:
+        raise SystemExit("prompt + warmup + steps exceed the 2304-position context")
+    os.environ["DPUF_CUDA_SLOTS"] = str(max(8, n_seq))
+    m = mdl.SyntheticModel(shape, seed=0)
+    eng = engine.CudaTransformerEngine(m)
+    toks, pos = [], []
+    t0 = time.perf_counter()
+    for i in range(n_seq):
+        pr = mdl.prompt_ids(plen, shape.vocab, 1000 + i)
+        if eng.set_slot(i) != 0:
+            raise RuntimeError(engine.last_error())
+        eng.reset_slot(i)
+        lg = None
+        for c0 in range(0, plen, 256):
+            lg = eng.forward_batch(pr[c0:c0 + 256], c0)
+        toks.append(int(np.argmax(lg[0])))
+        pos.append(plen)
+    prefill_s = time.perf_counter() - t0
+    slots = list(range(n_seq))
+    for _ in range(warm):
+        toks = [int(t) for t in eng.decode_batch(slots, toks, pos)]
+        pos = [p + 1 for p in pos]
+    ctx0 = pos[0]
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            toks = [int(t) for t in eng.decode_batch(slots, toks, pos)]
+            pos = [p + 1 for p in pos]
+        dt = time.perf_counter() - t0
+    eng.close()
+    # algorithmic bytes per step: the weights once, plus every sequence's K and V rows (fp32)
+    wbytes = shape.weight_bytes_per_token()
+    kvd = shape.kv_dim
+    ctx_mean = ctx0 + (steps + 1) / 2.0
+    kv_bytes = n_seq * shape.layers * 2 * ctx_mean * kvd * 4
+    step_s = dt / steps
+    value = n_seq * steps / dt
+    print(json.dumps({
+        "metric": "batched_decode_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": 1,
+        "steps": steps, "warmup": warm, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
+        "config": {"workload": f"{shape.name}-shape batched serving: {n_seq} sequences x {plen}-token prompts, "
+                               f"{steps} greedy steps at batch {n_seq}", "kv": "fp32",
+                   "context": [ctx0, ctx0 + steps]},
+        "step_roofline": {"bytes_per_step": int(wbytes + kv_bytes), "weights": wbytes, "kv": int(kv_bytes),
+                          "achieved_gbs": round((wbytes + kv_bytes) / step_s / 1e9, 1),
+                          "frac": round((wbytes + kv_bytes) / step_s / 1e9 / hbm_peak, 4), "peak": hbm_peak,
+                          "peak_kind": peak_kind},
+        "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": n_seq * 20,
+                "d2h_bytes_per_step": n_seq * 4, "what": "dpuf_cuda_decode_batch per step, synchronous"},
+        "prefill": {"tokens": n_seq * plen, "seconds": round(prefill_s, 1),
+                    "tok_per_s": round(n_seq * plen / prefill_s, 1)},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def profile_value(name: str, key: str):
     """A number recorded in a committed ncu summary under profiles/ (`key: value` line), or None."""
     prof = REPO / "profiles" / name
@@ -502,6 +568,10 @@ def main():
                     help="only the kernel-only GEMV roofline measurement (for profiling the GEMV)")
     ap.add_argument("--op", action="store_true", help="config 2: isolated mode-12 matmuls at M = 1 and 32")
     ap.add_argument("--zone", action="store_true", help="config 4: Zone-A LM head stress")
+    ap.add_argument("--serve", action="store_true", help="config 5: batched serving of independent sequences")
+    ap.add_argument("--serve-seqs", type=int, default=64)
+    ap.add_argument("--serve-prompt", type=int, default=2048)
+    ap.add_argument("--serve-steps", type=int, default=256)
     ap.add_argument("--tp", action="store_true",
                     help="with --gpus N > 1: tensor parallelism over the N GPUs (one sequence) instead of data parallel")
     ap.add_argument("--no-extras", action="store_true",
@@ -510,7 +580,7 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args.gpus)
-    if args.gemv_only or args.op or args.zone:
+    if args.gemv_only or args.op or args.zone or args.serve:
         import torch
 
         torch.cuda.set_device(local)
@@ -520,6 +590,8 @@ def main():
             run_op_configs(*peaks())
         if args.zone:
             run_zone_config(*peaks())
+        if args.serve:
+            run_serve_config(args, *peaks())
         return
     try:
         if args.impl == "reference":

@@ -1,6 +1,8 @@
-// kernels_attn.cu - exact causal GQA attention over the fp32 KV cache, one CTA per
-// (token, KV head, pair of Q heads); the arithmetic is attn_pair_body (layer_dev.cuh), a
-// restatement of gqa_attn_head_pair_f32 (dpuf_engine.c:341-577).
+// kernels_attn.cu - exact causal GQA attention over the fp32 KV cache, one CTA per (token, KV
+// head, two pairs of Q heads) - the keys and values a CTA stages serve four query heads, so a
+// KV head's cache is read once per token for groups of up to four; the arithmetic is
+// attn_pair_body (layer_dev.cuh), a restatement of gqa_attn_head_pair_f32
+// (dpuf_engine.c:341-577), pair by pair.
 #include "kernels.cuh"
 #include "layer_dev.cuh"
 
@@ -33,21 +35,24 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
   extern __shared__ __align__(16) float sm[];
   __shared__ AttnShared sh;
   cudaGridDependencySynchronize();
-  const int m = blockIdx.x, kvh = blockIdx.y, pr = blockIdx.z;
+  const int m = blockIdx.x, kvh = blockIdx.y;
+  int ppc, n_buf;
+  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf);
   const int groups = n_q / n_kv;
-  const int g0 = pr * 2;
-  const int nh = (g0 + 1 < groups) ? 2 : 1;  // pair path or lone head
+  const int g0 = blockIdx.z * 2 * ppc;
+  const int nh = min(2 * ppc, groups - g0);  // the last head of an odd group is a lone head
   const int qh0 = kvh * groups + g0;
   const int kv_len = (kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m) + 1;
   const float* kbase = kv.tok_k ? kv.tok_k[m] + kv.layer_off : kv.k;
   const float* vbase = kv.tok_v ? kv.tok_v[m] + kv.layer_off : kv.v;
-  float* qs = sm;                   // [2][hd]
-  float* sc = qs + 2 * hd;          // [2][max_seq]
-  float* kt = sc + attn_sc_floats(kv.max_seq);  // [kAttnKeyTile][hd + 8]
+  const int sc_stride = (kv.max_seq + 3) & ~3;
+  float* qs = sm;                                 // [2 ppc][hd]
+  float* sc = qs + 2 * ppc * hd;                  // [2 ppc][sc_stride]
+  float* kt = sc + (size_t)2 * ppc * sc_stride;   // [n_buf][kAttnKeyTile][hd + 8]
   for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) qs[i] = q[((size_t)m * n_q + qh0) * hd + i];
-  attn_pair_body(qs, nh, hd, kv_len, kbase + (size_t)kvh * kv.max_seq * hd, vbase + (size_t)kvh * kv.max_seq * hd,
-                 kv.max_seq, sc, kt, 1, 0, nullptr, nullptr, &sh, out + ((size_t)m * n_q + qh0) * hd, et,
-                 (int)threadIdx.x, CtaSync{});
+  attn_pair_body(qs, nh, (nh & 1) != 0, hd, kv_len, kbase + (size_t)kvh * kv.max_seq * hd,
+                 vbase + (size_t)kvh * kv.max_seq * hd, sc_stride, sc, kt, n_buf, 0, nullptr, nullptr, &sh,
+                 out + ((size_t)m * n_q + qh0) * hd, et, (int)threadIdx.x, CtaSync{});
 }
 
 }  // namespace
@@ -58,11 +63,13 @@ cudaError_t configure_attn_kernels() {
 
 cudaError_t launch_attention(const Launch& L, const float* q, int M, int n_q, int n_kv, int hd, const int* pos0_dev,
                              KvCache kv, float* out, const ExpfTable& et) {
+  int ppc, n_buf;
+  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf);
   const int groups = n_q / n_kv;
-  const size_t smem = attn_scratch_floats(hd, kv.max_seq) * sizeof(float);
+  const size_t smem = attn_step_floats(hd, kv.max_seq, ppc, n_buf) * sizeof(float);
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
-  return launch_k(L, attention_kernel, dim3(M, n_kv, (groups + 1) / 2), dim3(kAttnThreads), smem, q, n_q, n_kv, hd,
-                  pos0_dev, kv, out, et);
+  return launch_k(L, attention_kernel, dim3(M, n_kv, (groups + 2 * ppc - 1) / (2 * ppc)), dim3(kAttnThreads), smem, q,
+                  n_q, n_kv, hd, pos0_dev, kv, out, et);
 }
 
 }  // namespace dpuf

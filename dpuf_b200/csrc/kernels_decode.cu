@@ -887,7 +887,7 @@ DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, in
       qk_norm_rope_warp(qs + (warp - 2) * hd, Ly.q_norm ? qn : nullptr, A.eps, hd, cs, sn, lane);
     }
     named_sync(kBarAttn, kAttnThreads);  // rotated queries and key in place
-    attn_pair_body(qs, nh, hd, kv_len, kc, vc, sc_stride, sc, kt, n_buf, pre, kin, vin, &S.attn,
+    attn_pair_body(qs, nh, nh == 1, hd, kv_len, kc, vc, sc_stride, sc, kt, n_buf, pre, kin, vin, &S.attn,
                    A.att + (size_t)qh0 * hd, A.et, tid, AttnSync{}, A.fuse_o != 0);
     if (A.fuse_o) {
       named_sync(kBarAttn, kAttnThreads);

@@ -273,8 +273,11 @@ DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, i
 //           p_k = e_k * (1 / (sum + 1e-12)).
 //   PV      per output dim: fma(p_k, v_kd, acc) over k ascending (pair path); the lone-head
 //           path takes keys two at a time, k+1 first (dpuf_engine.c:541-548).
-// qs [2][hd] holds the (normed, rotated) query heads; kc/vc are this KV head's cache rows
-// [max_seq][hd] (read through L2: other CTAs may have written them); sc [2][sc_stride] and
+// Up to four query heads of one KV head run together (two pairs sharing the staged keys and
+// values; every head keeps its pair's arithmetic); with last_lone the last head is the lone
+// head of an odd group.  nh * hd <= 2 * kAttnThreads.
+// qs [nh][hd] holds the (normed, rotated) query heads; kc/vc are this KV head's cache rows
+// [max_seq][hd] (read through L2: other CTAs may have written them); sc [nh][sc_stride] and
 // n_buf key/value tiles kt [n_buf][kAttnKeyTile][hd+8] are scratch; out receives nh * hd
 // values.  Up to n_buf tiles are in flight (cp.async groups); the caller may have issued the
 // first `pre` key tiles already (attn_issue_tile, one committed group each, nothing committed
@@ -283,19 +286,35 @@ DPUF_DEV void prep_chunk_g8(float (&v)[8], uint8_t sbyte, bool active, int c0, i
 constexpr int kAttnThreads = 256;
 constexpr int kAttnKeyTile = 32;  // keys per tile (8 threads per key)
 constexpr int kAttnMaxBuf = 3;    // tiles in flight at most
+constexpr int kAttnMaxHeads = 4;  // query heads per call
 
 struct AttnShared {
-  float red[2][kAttnThreads / 32];
-  float lane_sum[2][8];
-  float inv_s[2], max_s[2];
+  float red[kAttnMaxHeads][kAttnThreads / 32];
+  float lane_sum[kAttnMaxHeads][8];
+  float inv_s[kAttnMaxHeads], max_s[kAttnMaxHeads];
 };
 
 DPUF_HD size_t attn_tile_floats(int hd) { return (size_t)kAttnKeyTile * (hd + 8); }
-// Scratch layout of the per-step kernel: qs [2][hd] | sc [2][max_seq] padded to a multiple of
-// 4 | one tile (16-byte aligned for the async copies).
+// Scores of two heads over max_seq keys (the persistent kernel's pair).
 DPUF_HD size_t attn_sc_floats(int max_seq) { return 2 * (((size_t)max_seq + 3) & ~(size_t)3); }
+// Scratch of the per-step kernel with ppc pairs per CTA and n_buf tiles: qs [2 ppc][hd] |
+// sc [2 ppc][max_seq padded to 4] | n_buf tiles (16-byte aligned for the async copies).
+DPUF_HD size_t attn_step_floats(int hd, int max_seq, int ppc, int n_buf) {
+  return (size_t)2 * ppc * hd + ppc * attn_sc_floats(max_seq) + n_buf * attn_tile_floats(hd);
+}
+// The per-step kernel's plan: two pairs per CTA (four query heads sharing the staged keys and
+// values) when their outputs fit two per thread, and two tiles in flight, each dropped to one
+// when the scratch would not fit the shared memory.
+DPUF_HD void attn_step_plan(int hd, int max_seq, int* ppc, int* n_buf) {
+  *ppc = 4 * hd <= 2 * kAttnThreads ? 2 : 1;
+  *n_buf = 2;
+  if (attn_step_floats(hd, max_seq, *ppc, *n_buf) * 4 > (size_t)kMaxDynSmem) *n_buf = 1;
+  if (attn_step_floats(hd, max_seq, *ppc, *n_buf) * 4 > (size_t)kMaxDynSmem) *ppc = 1;
+}
 DPUF_HD size_t attn_scratch_floats(int hd, int max_seq) {
-  return (size_t)2 * hd + attn_sc_floats(max_seq) + attn_tile_floats(hd);
+  int ppc, n_buf;
+  attn_step_plan(hd, max_seq, &ppc, &n_buf);
+  return attn_step_floats(hd, max_seq, ppc, n_buf);
 }
 
 // ------------------------------------------------------------------ async copies to shared
@@ -351,10 +370,10 @@ DPUF_DEV void attn_land_tile(float* buf, int t, int n_t, int n_buf, const float*
 }
 
 template <typename Sync>
-DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float* kc, const float* vc,
-                             int sc_stride, float* sc, float* kt, int n_buf, int pre, const float* cur_k,
-                             const float* cur_v, AttnShared* sh, float* out, const ExpfTable& et, int tid, Sync sync,
-                             bool out_to_qs = false) {
+DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_len, const float* kc,
+                             const float* vc, int sc_stride, float* sc, float* kt, int n_buf, int pre,
+                             const float* cur_k, const float* cur_v, AttnShared* sh, float* out,
+                             const ExpfTable& et, int tid, Sync sync, bool out_to_qs = false) {
   const int lane = tid & 31;
   const int kvs = hd + 8;  // padded smem row of a staged key
   const size_t tile = attn_tile_floats(hd);
@@ -362,7 +381,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
   const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
   const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
   const int n_rows = cur_k ? kv_len - 1 : kv_len;  // rows read from the cache
-  float lmax[2] = {-1e30f, -1e30f};
+  float lmax[kAttnMaxHeads] = {-1e30f, -1e30f, -1e30f, -1e30f};
   // ---- scores
   for (int t = pre; t < min(n_buf, n_t); t++) attn_issue_tile(kt + (size_t)t * tile, kc, t, n_rows, hd, tid);
   for (int t = 0; t < n_t; t++) {
@@ -374,7 +393,9 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
     const int tk = t0 + key;
     const bool valid = key < nk;
     const float* kp = buf + key * kvs;
-    for (int h = 0; h < nh; h++) {
+#pragma unroll
+    for (int h = 0; h < kAttnMaxHeads; h++) {
+      if (h >= nh) break;
       const float* qv = qs + h * hd;
       // Shuffle trees run on all lanes (keys of one warp may sit on both sides of kv4).
       float acc = 0.0f;
@@ -382,7 +403,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
         for (int i = l; i < hd; i += 8) acc = __fmaf_rn(qv[i], kp[i], acc);
       const float t_pairs = tree8_pairs(acc);
       float t_split;
-      if (nh == 2) {
+      if (!(last_lone && h == nh - 1)) {
         t_split = tree8_split(acc);
       } else {
         // lone head, tail key: dot_f32_avx2 (dpuf_engine.c:325-339)
@@ -409,7 +430,9 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
   // the first value tiles load while the softmax runs
   for (int t = 0; t < min(n_buf, n_t); t++) attn_issue_tile(kt + (size_t)t * tile, vc, t, n_rows, hd, tid);
   // ---- max
-  for (int h = 0; h < nh; h++) {
+#pragma unroll
+  for (int h = 0; h < kAttnMaxHeads; h++) {
+    if (h >= nh) break;
     float v = warp_max(lmax[h]);
     if (lane == 0) sh->red[h][tid >> 5] = v;
   }
@@ -472,7 +495,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, int hd, int kv_len, const float*
       const float* pp = sc + h * sc_stride + t0;
       const float* vt = buf + d;
       float a = acc[j];
-      if (nh == 2) {
+      if (!(last_lone && h == nh - 1)) {
         for (int k = 0; k < nk; k++) a = __fmaf_rn(pp[k], vt[k * kvs], a);
       } else if ((hd & 63) == 0) {
         // keys two at a time, k+1 first (tiles hold an even number of keys but the last)

@@ -1,9 +1,9 @@
-"""Tensor-parallel batch-1 decode (scope row e): two processes, one GPU each, split every
+"""Tensor-parallel batch-1 decode (scope row e): two or four processes, one GPU each, split every
 projection and the LM head of the persistent kernel between them and exchange outputs through
 each other's memory.  Every rank must return the ids and logits of one GPU bit for bit (one
 GPU matches the reference engine: test_gpu_parity / test_gpu_8b).
 
-Needs two GPUs; skipped otherwise."""
+Needs as many GPUs as ranks; skipped otherwise."""
 import os
 import socket
 import sys
@@ -84,8 +84,10 @@ def _rank_main(rank: int, world: int, port: int, cases, out):
 CASES = [("tiny", 3), ("tiny-mha", 5), ("qwen3-0.6b", 0)]
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-def test_tp2_decode_matches_one_gpu():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_decode_matches_one_gpu(world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     sys.path.insert(0, REPO)
@@ -96,10 +98,10 @@ def test_tp2_decode_matches_one_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, CASES, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, CASES, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = [q.get(timeout=600) for _ in range(2 * len(CASES))]
+    got = [q.get(timeout=600) for _ in range(world * len(CASES))]
     for p in procs:
         p.join(120)
         assert p.exitcode == 0
