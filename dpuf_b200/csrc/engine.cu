@@ -571,6 +571,12 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   A.tp_rank = 0;
   A.tp_world = 1;
   A.stage_cap = decode_stage_cap(A);
+  {
+    // the gate/up output is prepped by every CTA when it fits one staged piece and two prep
+    // passes; otherwise one CTA per 64-column chunk preps it and every CTA copies the result
+    const size_t stage_bytes = decode_uni_bytes(A) - (size_t)A.kmax - (size_t)(A.kmax / 32) * 8;
+    A.dprep_local = ((size_t)e->I * 8 + (size_t)e->I / 8 <= stage_bytes && e->I / 64 <= 72) ? 1 : 0;
+  }
   A.attn_floats = (int)(decode_uni_bytes(A) / sizeof(float));
   size_t limit = 0;
   if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");

@@ -150,6 +150,7 @@ struct DecodeArgs {
   // the down projection's prepped input, produced by one CTA per 64-column chunk: [I/4] words
   // of four int8 codes, then [I/32] block scales, then [I/32] block sums
   uint64_t* dprep;
+  int dprep_local;  // 1: every CTA preps the whole (small) gate/up output itself from the tagged words
   // one GPU: the same prepped input as plain codes, block scales and block sums, read after a
   // grid barrier
   int8_t* xd_q8;   float* xd_xs;  int32_t* xd_xm;   // [I], [I/32] x2

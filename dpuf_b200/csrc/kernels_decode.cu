@@ -786,6 +786,28 @@ DPUF_DEV void load_prepped_tagged(const DecodeArgs& A, int K, unsigned gen, unsi
   }
 }
 
+// Prep of a whole tagged vector (generation `gen`, complete at count `target` of completion
+// counter 0) by this CTA: staged in one piece with its sign bytes, then prepped from shared
+// memory (for vectors small enough that one hop beats the distributed prep's two).
+DPUF_DEV void prep_tagged(const DecodeArgs& A, const uint64_t* src, unsigned gen, unsigned target, int K,
+                          const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* st = (uint64_t*)stage;
+  uint8_t* sg = (uint8_t*)(st + K);
+  if (signs) stage8(sg, signs, K / 8);
+  stage_tagged(st, src, K, gen, 0, target, A, S);
+  const int nch = K / 64;
+  for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
+    const int c = cb + (lane >> 3);
+    const bool active = c < nch;
+    const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = value_of(st[col + k]);
+    prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, active ? c * 64 : 0, lane, xq, xs, xm);
+  }
+}
+
 // Copies a prepped activation (codes, block scales, block sums of K columns; K % 128 == 0)
 // written by other CTAs into x.
 DPUF_DEV void load_prepped(const int8_t* q8, const float* bxs, const int32_t* bxm, int K, int8_t* xq, float* xs,
@@ -1055,12 +1077,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
       if (tid == 0) trace_at(A, step, lb + kEvGU);
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvB4);
-      prep_slices(A, Ly.signs[3], g + kGU, S);
-      if (A.tp_world == 1) {
-        grid_sync(A, target, S);
-        load_prepped(A.xd_q8, A.xd_xs, A.xd_xm, A.I, xq, xs, xm);
+      if (A.dprep_local) {
+        prep_tagged(A, A.s_out, g + kGU, (g + kGU) * (unsigned)(gridDim.x * A.tp_world), A.I, Ly.signs[3], xq, xs,
+                    xm, stage, S);
       } else {
-        load_prepped_tagged(A, A.I, g + kGU, A.dgen0 + (unsigned)(step * A.L + l + 1), xq, xs, xm, stage, S);
+        prep_slices(A, Ly.signs[3], g + kGU, S);
+        if (A.tp_world == 1) {
+          grid_sync(A, target, S);
+          load_prepped(A.xd_q8, A.xd_xs, A.xd_xm, A.I, xq, xs, xm);
+        } else {
+          load_prepped_tagged(A, A.I, g + kGU, A.dgen0 + (unsigned)(step * A.L + l + 1), xq, xs, xm, stage, S);
+        }
       }
       cbar();
       if (tid == 0) trace_at(A, step, lb + kEvPrepD);

@@ -123,7 +123,9 @@ QWEN3_8B = ModelShape("qwen3-8b", 4096, 12288, 36, 32, 8, 128, 151936, tied=Fals
 TINY = ModelShape("tiny", 256, 512, 2, 4, 2, 64, 4096, tied=False, max_seq=512)
 TINY_ZONE = ModelShape("tiny-zone", 256, 512, 2, 4, 2, 64, 40960, tied=True, max_seq=512)
 TINY_MHA = ModelShape("tiny-mha", 256, 512, 2, 3, 3, 64, 4096, tied=False, max_seq=512)
-SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, TINY, TINY_ZONE, TINY_MHA)}
+# the 8B shape's FFN width on two small layers (the persistent kernel's distributed down-input prep)
+TINY_WIDE = ModelShape("tiny-wide", 1024, 12288, 2, 8, 4, 128, 4096, tied=False, max_seq=512)
+SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, TINY, TINY_ZONE, TINY_MHA, TINY_WIDE)}
 
 
 def _stream_id(name: str) -> int:

@@ -151,7 +151,7 @@ def test_gemv_decode_shapes_match_oracle(eng_mod, rows, cols):
         assert bitexact(eng_mod.matmul(1, bv, x), want)
 
 
-@pytest.mark.parametrize("shape", ["TINY", "TINY_MHA"])
+@pytest.mark.parametrize("shape", ["TINY", "TINY_MHA", "TINY_WIDE"])
 def test_persistent_decode_matches_step_kernels(eng_mod, shape):
     """Greedy decode as one persistent kernel gives the ids and last logits of the per-step
     kernels, which match the reference (the engine goldens above)."""

@@ -81,7 +81,7 @@ def _rank_main(rank: int, world: int, port: int, cases, out):
         dist.destroy_process_group()
 
 
-CASES = [("tiny", 3), ("tiny-mha", 5), ("qwen3-0.6b", 0)]
+CASES = [("tiny", 3), ("tiny-mha", 5), ("tiny-wide", 2), ("qwen3-0.6b", 0)]
 
 
 @pytest.mark.parametrize("world", [2, 4])
