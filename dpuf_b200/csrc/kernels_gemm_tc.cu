@@ -9,22 +9,24 @@
 // MMA per 32-column block so that every block's dot lands in its own TMEM columns; the fp32
 // chain then runs on CUDA cores in the reference's order.
 //
-// CTA = 128 weight rows (8 container tiles of one job) x N tokens (8, 16 or 32).  The raw
-// bytes of each stage (kStageBlocks blocks: nibbles and fp16 scales of 16 (tile, group)
-// pairs) arrive by TMA bulk copies into a double buffer requested one stage ahead.  Per stage
-// all 256 threads
-//   1. unpack the nibbles to u8 in shared memory, K-major without swizzle (core matrices of
-//      8 rows x 16 bytes; the two 16-byte K halves LBO = 128 bytes apart, 8-row groups
-//      SBO = 256 bytes apart) - A; copy the tokens' int8 codes the same way with cp.async - B;
-//      and the tokens' block scales and sums;
-//   2. thread 0 issues one tcgen05.mma per block (M=128, N, K=32) into TMEM columns
-//      [j*N, j*N+N) of the stage's half of TMEM and commits them to an mbarrier;
-//   3. after the (bounded) wait, warp w reads TMEM lanes 32*(w%4).. (its rows), columns of its
-//      half of the tokens (tcgen05.ld 32x32b) and runs the chains of its (row, token) pairs.
-// Steps 1 of stage s+1 run while the MMAs of stage s execute (A, B, scales and TMEM are double
-// buffered; raw weights are requested two stages ahead).  Outputs are written after the last
-// stage.  TMEM (2 x 8 x N columns) is allocated by warp 0 and freed before exit, also when a
-// wait gives up (it then sets the error word).
+// CTA = 128 weight rows (8 container tiles of one job) x N tokens (8, 16 or 32); a stage is
+// kStageBlocks blocks.  Warp-specialised pipeline, every hand-off on mbarriers (no CTA barrier
+// per stage):
+//   warp 12      TMA: the raw bytes of each stage (nibbles and fp16 scales of 16 (tile, group)
+//                pairs) by bulk copies into a 3-deep raw ring;
+//   warps 0..3   unpack: the nibbles to u8 in shared memory, K-major without swizzle (core
+//                matrices of 8 rows x 16 bytes; the two 16-byte K halves LBO = 128 bytes apart,
+//                8-row groups SBO = 256 bytes apart) - A - and the row scales, into a 3-deep
+//                stage ring; they copy the tokens' int8 codes the same way (B) and the tokens'
+//                block scales and sums one stage ahead with cp.async;
+//   warp 13      MMA: one tcgen05.mma per block (M=128, N, K=32) into TMEM columns [j*N, j*N+N)
+//                of a 2-deep TMEM ring, committed to an mbarrier;
+//   warps 4..11  chains: warp w reads TMEM lanes 32*(w%4).. (its rows), columns of its half of
+//                the tokens (tcgen05.ld 32x32b, four blocks at a time) and runs the chains of
+//                its (row, token) pairs; outputs after the last stage.
+// TMEM (2 x 8 x N columns) is allocated by warp 12 and freed before exit.  Every wait is
+// bounded: one that gives up sets the error word and the CTA's abort flag, after which every
+// role stops waiting; bulk copies still in flight are waited for (bounded) before exit.
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -33,8 +35,14 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kTcThreads = 288;   // warps 0..7 prepare stages and run the chains; warp 8 issues the MMAs
-constexpr int kWork = 256;
+constexpr int kUnpackWarps = 4;   // warps 0..3
+constexpr int kChainWarps = 8;    // warps 4..11
+constexpr int kChainWarp0 = kUnpackWarps;
+constexpr int kTmaWarp = kUnpackWarps + kChainWarps;  // 12
+constexpr int kMmaWarp = kTmaWarp + 1;                // 13
+constexpr int kTcThreads = (kMmaWarp + 1) * 32;       // 448
+constexpr int kUnpackThreads = kUnpackWarps * 32;
+constexpr int kRawRing = 3, kStageRing = 3, kTmemRing = 2;
 constexpr int kTcRows = 128;
 constexpr int kStageBlocks = 8;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
@@ -130,25 +138,28 @@ constexpr int kRawBytes = (kTcRows / 8) * kRawTG;  // 16 (tile, group) pairs
 
 template <int N>
 struct TcLayout {  // shared memory of one CTA
-  static constexpr int kA = kStageBlocks * kTcRows * 32;  // one A buffer
-  static constexpr int kB = kStageBlocks * N * 32;        // one B buffer
+  static constexpr int kA = kStageBlocks * kTcRows * 32;  // A of a stage
+  static constexpr int kB = kStageBlocks * N * 32;        // B of a stage
   static constexpr int kW = kTcRows * kStageBlocks * 2;   // row scales of a stage
   static constexpr int kX = kStageBlocks * N * 4;         // xs or xm of a stage
-  static constexpr int raw = 0;                            // [2][kRawBytes]
-  static constexpr int a = raw + 2 * kRawBytes;           // [2][kA]
-  static constexpr int b = a + 2 * kA;                     // [2][kB]
-  static constexpr int w = b + 2 * kB;                     // [2][kW]
-  static constexpr int xs = w + 2 * kW;                    // [2][kX]
-  static constexpr int xm = xs + 2 * kX;                   // [2][kX]
-  static constexpr int bytes = xm + 2 * kX;
-  static constexpr int tmem_cols = 2 * kStageBlocks * N < 32 ? 32 : 2 * kStageBlocks * N;  // D double buffer
+  static constexpr int raw = 0;                            // [kRawRing][kRawBytes]
+  static constexpr int a = raw + kRawRing * kRawBytes;    // [kStageRing][kA]
+  static constexpr int b = a + kStageRing * kA;            // [kStageRing][kB]
+  static constexpr int w = b + kStageRing * kB;            // [kStageRing][kW]
+  static constexpr int xs = w + kStageRing * kW;           // [kStageRing][kX]
+  static constexpr int xm = xs + kStageRing * kX;          // [kStageRing][kX]
+  static constexpr int bytes = xm + kStageRing * kX;
+  static constexpr int tmem_cols = kTmemRing * kStageBlocks * N < 32 ? 32 : kTmemRing * kStageBlocks * N;
 };
+static_assert(TcLayout<32>::bytes <= 200 * 1024, "shared memory of the 32-token CTA");
 
 template <int N>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   using Lay = TcLayout<N>;
   extern __shared__ __align__(128) unsigned char sm[];
-  __shared__ __align__(8) uint64_t mma_bar[2], raw_bar[2];
+  __shared__ __align__(8) uint64_t raw_full[kRawRing], raw_empty[kRawRing];
+  __shared__ __align__(8) uint64_t stg_full[kStageRing], stg_empty[kStageRing];
+  __shared__ __align__(8) uint64_t d_full[kTmemRing], d_empty[kTmemRing];
   __shared__ const uint8_t* grp_base[kTcRows / 8];  // group data of each (tile, group), or null
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
@@ -164,7 +175,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   const int cols = job.w.cols, n_blk = cols >> 5;
   const int n_stages = (n_blk + kStageBlocks - 1) / kStageBlocks;
 
-  if (warp == 0) {
+  if (warp == kTmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_sh)),
                  "r"(Lay::tmem_cols)
                  : "memory");
@@ -181,9 +192,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
     grp_base[tid] = p;
   }
   if (tid == 0) {
-    for (int i = 0; i < 2; i++) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&mma_bar[i])) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&raw_bar[i])) : "memory");
+    for (int i = 0; i < kRawRing; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&raw_full[i])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&raw_empty[i])), "r"(kUnpackWarps) : "memory");
+    }
+    for (int i = 0; i < kStageRing; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&stg_full[i])), "r"(kUnpackWarps) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&stg_empty[i])), "r"(kChainWarps) : "memory");
+    }
+    for (int i = 0; i < kTmemRing; i++) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&d_full[i])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&d_empty[i])), "r"(kChainWarps) : "memory");
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_sh = 0;
@@ -192,198 +211,233 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base_sh;
-
-  // warp 0 requests stage s's raw bytes into raw buffer s & 1 (one bulk copy per lane)
-  auto request_raw = [&](int s) {
-    const int buf = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
-    unsigned bytes = 0;
-    for (int tg = 0; tg < kTcRows / 8; tg++)
-      if (grp_base[tg]) bytes += (unsigned)kb * 144;
-    if (lane == 0)
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&raw_bar[buf])), "r"(bytes)
-                   : "memory");
-    __syncwarp();
-    const int tg = lane >> 1, part = lane & 1;
-    const uint8_t* gb = grp_base[tg];
-    if (gb) {
-      unsigned char* dst = sm + Lay::raw + buf * kRawBytes + tg * kRawTG + (part ? kStageBlocks * 128 : 0);
-      const uint8_t* src = part ? gb + (size_t)b0 * 16 : gb + (size_t)n_blk * 16 + (size_t)b0 * 128;
-      const unsigned n = (unsigned)kb * (part ? 16 : 128);
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
-          "l"(src), "r"(n), "r"(su32(&raw_bar[buf]))
-          : "memory");
-    }
+  auto arrive = [](uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+  };
+  // one lane waits for the warp, which then follows its verdict
+  auto warp_wait = [&](uint64_t* bar, unsigned par) {
+    bool ok = true;
+    if (lane == 0) ok = wait_parity(bar, par, &abort_sh, P.err);
+    return __shfl_sync(kFull, (int)ok, 0) != 0;
   };
 
-  const Act& act = job.act;
-  const int xld = act.ld >> 5;
-  // all threads: the tokens' codes, block scales and block sums of stage s into buffer s & 1
-  // (async; waited by prepare)
-  auto request_act = [&](int s) {
-    if (tid >= kWork) return;
-    const int p = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
-    unsigned char* sB = sm + Lay::b + p * Lay::kB;
-    float* sXs = (float*)(sm + Lay::xs + p * Lay::kX);
-    int* sXm = (int*)(sm + Lay::xm + p * Lay::kX);
-    for (int i = tid; i < N * kStageBlocks * 2; i += kWork) {
-      const int h = i & 1, n = (i >> 1) % N, j = (i >> 1) / N;
-      const bool ok = j < kb && tok0 + n < P.M;
-      const int8_t* src = ok ? act.q8 + (size_t)(tok0 + n) * act.ld + (size_t)(b0 + j) * 32 + h * 16 : act.q8;
-      cp16_zfill(sB + j * (N * 32) + (n >> 3) * 256 + h * 128 + (n & 7) * 16, src, ok);
-    }
-    for (int i = tid; i < N * kStageBlocks; i += kWork) {
-      const int j = i / N, n = i % N;
-      const bool ok = j < kb && tok0 + n < P.M;
-      const size_t o = ok ? (size_t)(tok0 + n) * xld + b0 + j : 0;
-      cp4_zfill(sXs + i, act.xs + o, ok);
-      cp4_zfill(sXm + i, act.xm + o, ok);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  // all threads: stage s's A (unpacked from its raw buffer) and row scales into buffer s & 1,
-  // then wait for its activation copies; the raw buffer is free again after the next barrier
-  auto prepare = [&](int s) {
-    if (tid >= kWork) return;
-    const int p = s & 1, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
-    if (lane == 0) wait_parity(&raw_bar[p], (unsigned)((s >> 1) & 1), &abort_sh, P.err);
-    __syncwarp();
-    const unsigned char* rb = sm + Lay::raw + p * kRawBytes;
-    unsigned char* sA = sm + Lay::a + p * Lay::kA;
-    // one thread: rows 4q..4q+3 of a (tile, group), one block, one chunk (a 16-byte raw load)
-    for (int i = tid; i < (kTcRows / 4) * kStageBlocks * 4; i += kWork) {
-      const int c = i & 3, q = (i >> 2) & (kTcRows / 4 - 1), j = i >> 7;  // 32 row quads per block
-      const int tg = q >> 1, ri0 = (q & 1) * 4;
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (j < kb && grp_base[tg]) w = *(const uint4*)(rb + tg * kRawTG + j * 128 + c * 32 + ri0 * 4);
-      unsigned char* dst = sA + j * (kTcRows * 32) + tg * 256 + (c >> 1) * 128 + ri0 * 16 + (c & 1) * 8;
-      *(uint2*)(dst + 0) = make_uint2(w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu);  // columns 8c..8c+7
-      *(uint2*)(dst + 16) = make_uint2(w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
-      *(uint2*)(dst + 32) = make_uint2(w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu);
-      *(uint2*)(dst + 48) = make_uint2(w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
-    }
-    uint16_t* sW = (uint16_t*)(sm + Lay::w + p * Lay::kW);
-    for (int i = tid; i < kTcRows * kStageBlocks; i += kWork) {  // [row][block]
-      const int r = i >> 3, j = i & 7;
-      sW[i] = (j < kb && grp_base[r >> 3]) ? *(const uint16_t*)(rb + (r >> 3) * kRawTG + kStageBlocks * 128 + j * 16 +
-                                                                 (r & 7) * 2)
-                                           : (uint16_t)0;
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
-  };
-
-  if (warp == 0) {  // weights do not depend on the previous kernel
-    request_raw(0);
-    if (n_stages > 1) request_raw(1);
-  }
-  cudaGridDependencySynchronize();
-  request_act(0);
-  if (n_stages > 1) request_act(1);
-  prepare(0);
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 0 && n_stages > 2) request_raw(2);  // raw buffer 0 is free again
-
-  const int row = 32 * (warp & 3) + lane;  // TMEM lane = weight row of this thread's chains
-  const int half = warp >> 2;              // which half of the N tokens
-  constexpr int NH = N / 2;
-  float acc[NH];
-#pragma unroll
-  for (int i = 0; i < NH; i++) acc[i] = 0.0f;
-  const uint32_t idesc = idesc_i8(N);
-
-  for (int s = 0; s < n_stages; s++) {
-    const int p = s & 1, kb = min(kStageBlocks, n_blk - s * kStageBlocks);
-    // ---- MMAs of stage s (buffers p) into TMEM columns p*8N + j*N
-    if (tid == kWork) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const unsigned char* sA = sm + Lay::a + p * Lay::kA;
-      const unsigned char* sB = sm + Lay::b + p * Lay::kB;
-      const uint64_t da0 = smem_desc(sA, 128, 256), db0 = smem_desc(sB, 128, 256);
-      for (int j = 0; j < kb; j++) {
-        // the start-address field (bits 0..13, 16-byte units) advances by one block's bytes
-        const uint64_t da = da0 + (uint64_t)(j * (kTcRows * 32 / 16));
-        const uint64_t db = db0 + (uint64_t)(j * (N * 32 / 16));
+  if (warp == kTmaWarp) {
+    // ================================================================ TMA: raw ring
+    int issued = 0;
+    for (int s = 0; s < n_stages; s++) {
+      const int slot = s % kRawRing, k = s / kRawRing;
+      if (!warp_wait(&raw_empty[slot], (unsigned)((k & 1) ^ 1))) break;
+      const int b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
+      unsigned bytes = 0;
+      for (int tg = 0; tg < kTcRows / 8; tg++)
+        if (grp_base[tg]) bytes += (unsigned)kb * 144;
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&raw_full[slot])), "r"(bytes)
+                     : "memory");
+      __syncwarp();
+      const int tg = lane >> 1, part = lane & 1;
+      const uint8_t* gb = grp_base[tg];
+      if (gb) {
+        unsigned char* dst = sm + Lay::raw + slot * kRawBytes + tg * kRawTG + (part ? kStageBlocks * 128 : 0);
+        const uint8_t* src = part ? gb + (size_t)b0 * 16 : gb + (size_t)n_blk * 16 + (size_t)b0 * 128;
+        const unsigned n = (unsigned)kb * (part ? 16 : 128);
         asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
-                tmem + p * (kStageBlocks * N) + j * N),
-            "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+            "l"(src), "r"(n), "r"(su32(&raw_full[slot]))
             : "memory");
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       su32(&mma_bar[p]))
-                   : "memory");
+      issued = s + 1;
     }
-    // ---- meanwhile: stage s+1 into buffers p^1
-    if (s + 1 < n_stages) prepare(s + 1);
-    // ---- chains of stage s (warps 0..7): all of the stage's TMEM columns are loaded before one
-    // wait, then the chains run
-    if (tid < kWork) {
-      if (lane == 0) wait_parity(&mma_bar[p], (unsigned)((s >> 1) & 1), &abort_sh, P.err);
+    // copies in flight must land before the CTA exits (after an abort nobody else waits)
+    if (abort_sh && lane == 0) {
+      const unsigned long long t0 = gtimer();
+      for (int q = max(0, issued - kRawRing); q < issued; q++) {
+        unsigned ok = 0;
+        while (!ok && gtimer() - t0 < kTcWaitNs)
+          asm volatile(
+              "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+              : "=r"(ok)
+              : "r"(su32(&raw_full[q % kRawRing])), "r"((unsigned)((q / kRawRing) & 1))
+              : "memory");
+      }
+    }
+  } else if (warp < kUnpackWarps) {
+    // ================================================================ unpack warps
+    const Act& act = job.act;
+    const int xld = act.ld >> 5;
+    // the tokens' codes, block scales and block sums of stage s into stage buffer s % ring (one
+    // cp.async group of this thread)
+    auto request_act = [&](int s) {
+      const int p = s % kStageRing, b0 = s * kStageBlocks, kb = min(kStageBlocks, n_blk - b0);
+      unsigned char* sB = sm + Lay::b + p * Lay::kB;
+      float* sXs = (float*)(sm + Lay::xs + p * Lay::kX);
+      int* sXm = (int*)(sm + Lay::xm + p * Lay::kX);
+      for (int i = tid; i < N * kStageBlocks * 2; i += kUnpackThreads) {
+        const int h = i & 1, n = (i >> 1) % N, j = (i >> 1) / N;
+        const bool ok = j < kb && tok0 + n < P.M;
+        const int8_t* src = ok ? act.q8 + (size_t)(tok0 + n) * act.ld + (size_t)(b0 + j) * 32 + h * 16 : act.q8;
+        cp16_zfill(sB + j * (N * 32) + (n >> 3) * 256 + h * 128 + (n & 7) * 16, src, ok);
+      }
+      for (int i = tid; i < N * kStageBlocks; i += kUnpackThreads) {
+        const int j = i / N, n = i % N;
+        const bool ok = j < kb && tok0 + n < P.M;
+        const size_t o = ok ? (size_t)(tok0 + n) * xld + b0 + j : 0;
+        cp4_zfill(sXs + i, act.xs + o, ok);
+        cp4_zfill(sXm + i, act.xm + o, ok);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    cudaGridDependencySynchronize();  // the activations come from the previous kernel
+    bool ok = warp_wait(&stg_empty[0], 1u);
+    if (ok) request_act(0);
+    for (int s = 0; ok && s < n_stages; s++) {
+      const int p = s % kStageRing, pk = s / kStageRing, rs = s % kRawRing, rk = s / kRawRing;
+      // the next stage's activations first (their buffer was freed by the chains of stage s-2)
+      bool next = s + 1 < n_stages;
+      if (next) {
+        const int q = (s + 1) % kStageRing, qk = (s + 1) / kStageRing;
+        if (!warp_wait(&stg_empty[q], (unsigned)((qk & 1) ^ 1))) break;
+        request_act(s + 1);
+      }
+      if (!warp_wait(&raw_full[rs], (unsigned)(rk & 1))) break;
+      const int kb = min(kStageBlocks, n_blk - s * kStageBlocks);
+      const unsigned char* rb = sm + Lay::raw + rs * kRawBytes;
+      unsigned char* sA = sm + Lay::a + p * Lay::kA;
+      // one thread: rows 4q..4q+3 of a (tile, group), one block, one chunk (a 16-byte raw load)
+      for (int i = tid; i < (kTcRows / 4) * kStageBlocks * 4; i += kUnpackThreads) {
+        const int c = i & 3, q = (i >> 2) & (kTcRows / 4 - 1), j = i >> 7;  // 32 row quads per block
+        const int tg = q >> 1, ri0 = (q & 1) * 4;
+        uint4 w = make_uint4(0u, 0u, 0u, 0u);
+        if (j < kb && grp_base[tg]) w = *(const uint4*)(rb + tg * kRawTG + j * 128 + c * 32 + ri0 * 4);
+        unsigned char* dst = sA + j * (kTcRows * 32) + tg * 256 + (c >> 1) * 128 + ri0 * 16 + (c & 1) * 8;
+        *(uint2*)(dst + 0) = make_uint2(w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu);  // columns 8c..8c+7
+        *(uint2*)(dst + 16) = make_uint2(w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
+        *(uint2*)(dst + 32) = make_uint2(w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu);
+        *(uint2*)(dst + 48) = make_uint2(w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+      }
+      uint16_t* sW = (uint16_t*)(sm + Lay::w + p * Lay::kW);
+      for (int i = tid; i < kTcRows * kStageBlocks; i += kUnpackThreads) {  // [row][block]
+        const int r = i >> 3, j = i & 7;
+        sW[i] = (j < kb && grp_base[r >> 3])
+                    ? *(const uint16_t*)(rb + (r >> 3) * kRawTG + kStageBlocks * 128 + j * 16 + (r & 7) * 2)
+                    : (uint16_t)0;
+      }
+      // this stage's activations landed (the next stage's may still be in flight)
+      if (next)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
       __syncwarp();
+      if (lane == 0) {
+        arrive(&raw_empty[rs]);
+        arrive(&stg_full[p]);
+      }
+      (void)pk;
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing of ours in flight at exit
+  } else if (warp == kMmaWarp) {
+    // ================================================================ MMA issuer
+    const uint32_t idesc = idesc_i8(N);
+    for (int s = 0; s < n_stages; s++) {
+      const int p = s % kStageRing, pk = s / kStageRing, ds = s % kTmemRing, dk = s / kTmemRing;
+      if (!warp_wait(&stg_full[p], (unsigned)(pk & 1))) break;
+      if (!warp_wait(&d_empty[ds], (unsigned)((dk & 1) ^ 1))) break;
+      if (lane == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int kb = min(kStageBlocks, n_blk - s * kStageBlocks);
+        const unsigned char* sA = sm + Lay::a + p * Lay::kA;
+        const unsigned char* sB = sm + Lay::b + p * Lay::kB;
+        const uint64_t da0 = smem_desc(sA, 128, 256), db0 = smem_desc(sB, 128, 256);
+        for (int j = 0; j < kb; j++) {
+          // the start-address field (bits 0..13, 16-byte units) advances by one block's bytes
+          const uint64_t da = da0 + (uint64_t)(j * (kTcRows * 32 / 16));
+          const uint64_t db = db0 + (uint64_t)(j * (N * 32 / 16));
+          asm volatile(
+              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+                  tmem + ds * (kStageBlocks * N) + j * N),
+              "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         su32(&d_full[ds]))
+                     : "memory");
+      }
+      __syncwarp();
+    }
+  } else {
+    // ================================================================ chain warps
+    const int cw = warp - kChainWarp0;
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane = weight row of this thread's chains
+    const int half = cw >> 2;                // which half of the N tokens
+    constexpr int NH = N / 2;
+    constexpr int kHB = kStageBlocks / 2;    // blocks per TMEM load
+    float acc[NH];
+#pragma unroll
+    for (int i = 0; i < NH; i++) acc[i] = 0.0f;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    for (int s = 0; s < n_stages; s++) {
+      const int p = s % kStageRing, pk = s / kStageRing, ds = s % kTmemRing, dk = s / kTmemRing;
+      // the stage's scales (written by the unpack warps; already complete when the MMAs are)
+      if (!warp_wait(&stg_full[p], (unsigned)(pk & 1))) break;
+      if (!warp_wait(&d_full[ds], (unsigned)(dk & 1))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      if (!abort_sh) {
-        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-        const uint16_t* wsp = (const uint16_t*)(sm + Lay::w + p * Lay::kW) + row * kStageBlocks;
-        const float* sXs = (const float*)(sm + Lay::xs + p * Lay::kX) + half * NH;
-        const int* sXm = (const int*)(sm + Lay::xm + p * Lay::kX) + half * NH;
-        uint32_t d[kStageBlocks][NH];
+      const int kb = min(kStageBlocks, n_blk - s * kStageBlocks);
+      const uint16_t* wsp = (const uint16_t*)(sm + Lay::w + p * Lay::kW) + row * kStageBlocks;
+      const float* sXs = (const float*)(sm + Lay::xs + p * Lay::kX) + half * NH;
+      const int* sXm = (const int*)(sm + Lay::xm + p * Lay::kX) + half * NH;
 #pragma unroll
-        for (int j = 0; j < kStageBlocks; j++)
-          if (j < kb) tmem_ld<N>(tmem + lane_base + p * (kStageBlocks * N) + j * N + half * NH, d[j]);
+      for (int hb = 0; hb < kStageBlocks / kHB; hb++) {
+        uint32_t d[kHB][NH];
+#pragma unroll
+        for (int jj = 0; jj < kHB; jj++) {
+          const int j = hb * kHB + jj;
+          if (j < kb) tmem_ld<N>(tmem + lane_base + ds * (kStageBlocks * N) + j * N + half * NH, d[jj]);
+        }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (hb == kStageBlocks / kHB - 1) {
+          // every TMEM column of this stage is read: the MMA warp may reuse them
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) arrive(&d_empty[ds]);
+        }
 #pragma unroll
-        for (int j = 0; j < kStageBlocks; j++) {
+        for (int jj = 0; jj < kHB; jj++) {
+          const int j = hb * kHB + jj;
           if (j < kb) {
             const float ws = f16bits_to_f32(wsp[j]);
             const float* xs = sXs + j * N;
             const int* xm = sXm + j * N;
 #pragma unroll
             for (int i = 0; i < NH; i++) {
-              const float pv = (float)((int)d[j][i] - xm[i]);
+              const float pv = (float)((int)d[jj][i] - xm[i]);
               acc[i] = xs[i] > 0.0f ? __fmaf_rn(pv, __fmul_rn(ws, xs[i]), acc[i]) : acc[i];
             }
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) arrive(&stg_empty[p]);  // the stage's scales are read; its A and B were read by the MMAs
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();  // buffers p and TMEM columns p are free; raw buffer (s+1)&1 is free
-    if (warp == 0 && s + 3 < n_stages) request_raw(s + 3);
-    if (s + 2 < n_stages) request_act(s + 2);
-  }
-
-  // ---- outputs
-  const int t = row >> 4;
-  if (tid < kWork && t < n_tiles_here) {
-    const int r_global = (t_first + t) * kTileRows + (row & 15);
-    if (r_global < job.w.rows)
+    // ---- outputs
+    cudaGridDependencySynchronize();  // the previous kernel is done with the output buffer
+    const int t = row >> 4;
+    if (!abort_sh && t < n_tiles_here) {
+      const int r_global = (t_first + t) * kTileRows + (row & 15);
+      if (r_global < job.w.rows)
 #pragma unroll
-      for (int i = 0; i < NH; i++) {
-        const int n = tok0 + half * NH + i;
-        if (n < P.M) job.out[(size_t)n * job.ldo + r_global] = acc[i];
-      }
+        for (int i = 0; i < NH; i++) {
+          const int n = tok0 + half * NH + i;
+          if (n < P.M) job.out[(size_t)n * job.ldo + r_global] = acc[i];
+        }
+    }
   }
   cudaTriggerProgrammaticLaunchCompletion();
-  // after an abort, raw copies still in flight must land before the CTA exits
-  if (abort_sh && warp == 0 && lane == 0) {
-    const unsigned long long t0 = gtimer();
-    for (int q = n_stages - 2; q < n_stages; q++) {
-      if (q < 0) continue;
-      unsigned ok = 0;
-      while (!ok && gtimer() - t0 < kTcWaitNs)
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(su32(&raw_bar[q & 1])), "r"((unsigned)((q >> 1) & 1))
-            : "memory");
-    }
-  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (warp == 0)
+  if (warp == kTmaWarp)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Lay::tmem_cols)
                  : "memory");
 }
