@@ -287,6 +287,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    unsigned valid_tg = 0u;  // (tile, group) pairs with rows
+    for (int tg = 0; tg < kTcRows / 8; tg++)
+      if (grp_base[tg]) valid_tg |= 1u << tg;
     cudaGridDependencySynchronize();  // the activations come from the previous kernel
     bool ok = warp_wait(&stg_empty[0], 1u);
     if (ok) request_act(0);
@@ -303,17 +306,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(TcArgs P) {
       const int kb = min(kStageBlocks, n_blk - s * kStageBlocks);
       const unsigned char* rb = sm + Lay::raw + rs * kRawBytes;
       unsigned char* sA = sm + Lay::a + p * Lay::kA;
-      // one thread: rows 4q..4q+3 of a (tile, group), one block, one chunk (a 16-byte raw load)
-      for (int i = tid; i < (kTcRows / 4) * kStageBlocks * 4; i += kUnpackThreads) {
-        const int c = i & 3, q = (i >> 2) & (kTcRows / 4 - 1), j = i >> 7;  // 32 row quads per block
-        const int tg = q >> 1, ri0 = (q & 1) * 4;
-        uint4 w = make_uint4(0u, 0u, 0u, 0u);
-        if (j < kb && grp_base[tg]) w = *(const uint4*)(rb + tg * kRawTG + j * 128 + c * 32 + ri0 * 4);
-        unsigned char* dst = sA + j * (kTcRows * 32) + tg * 256 + (c >> 1) * 128 + ri0 * 16 + (c & 1) * 8;
-        *(uint2*)(dst + 0) = make_uint2(w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu);  // columns 8c..8c+7
-        *(uint2*)(dst + 16) = make_uint2(w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
-        *(uint2*)(dst + 32) = make_uint2(w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu);
-        *(uint2*)(dst + 48) = make_uint2(w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+      // a warp unpacks one (tile group, block) at a time: lane L takes chunk c and row ri with
+      // (c >> 1, ri, c & 1) = (L >> 4, (L >> 1) & 7, L & 1), so it reads raw word c * 32 + ri * 4
+      // and writes its 8 u8 (columns 8c..8c+7 of row ri) at byte 8L of the block's 8-row core
+      // matrices: every warp load and store covers distinct banks
+      {
+        const int c = ((lane >> 4) << 1) | (lane & 1), ri = (lane >> 1) & 7;
+        const int src_off = c * 32 + ri * 4, dst_off = lane * 8;
+        constexpr int kPer = (kTcRows / 8) * kStageBlocks / kUnpackWarps;  // blocks per warp and stage
+        constexpr int kBatch = 16;                                         // loads in flight
+        static_assert(kStageBlocks == 8 && kPer % kBatch == 0, "unpack batches");
+#pragma unroll 1
+        for (int k0 = 0; k0 < kPer; k0 += kBatch) {
+          uint32_t w[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; u++) {
+            const int blk = warp + kUnpackWarps * (k0 + u), tg = blk >> 3, j = blk & 7;
+            w[u] = (j < kb && ((valid_tg >> tg) & 1u)) ? *(const uint32_t*)(rb + tg * kRawTG + j * 128 + src_off) : 0u;
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; u++) {
+            const int blk = warp + kUnpackWarps * (k0 + u), tg = blk >> 3, j = blk & 7;
+            *(uint2*)(sA + j * (kTcRows * 32) + tg * 256 + dst_off) =
+                make_uint2(w[u] & 0x0F0F0F0Fu, (w[u] >> 4) & 0x0F0F0F0Fu);
+          }
+        }
       }
       uint16_t* sW = (uint16_t*)(sm + Lay::w + p * Lay::kW);
       for (int i = tid; i < kTcRows * kStageBlocks; i += kUnpackThreads) {  // [row][block]
