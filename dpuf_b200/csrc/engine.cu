@@ -118,6 +118,7 @@ struct Engine {
   float *cos_tab = nullptr, *sin_tab = nullptr;
 
   std::vector<Slot> slots;  // kMaxSlots, or env DPUF_CUDA_SLOTS for batched serving
+  int kv_es = 4;            // bytes per KV-cache element: 4 (fp32, the reference's), 2 (fp16, env DPUF_CUDA_KV_F16=1)
   int n_slots = kMaxSlots;
   int active = 0;
   Prefix prefixes[kMaxPrefixes];
@@ -299,11 +300,11 @@ void rope_tables(const DpufModelConfig& c, std::vector<float>& cs, std::vector<f
 
 cudaError_t slot_alloc(Engine* e, int s) {
   if (e->slots[s].k) return cudaSuccess;
-  const size_t n = (size_t)e->L * e->S * e->kvd;
-  CK(cudaMalloc(&e->slots[s].k, n * 4));
-  CK(cudaMalloc(&e->slots[s].v, n * 4));
-  CK(cudaMemset(e->slots[s].k, 0, n * 4));
-  CK(cudaMemset(e->slots[s].v, 0, n * 4));
+  const size_t n = (size_t)e->L * e->S * e->kvd * e->kv_es;  // bytes
+  CK(cudaMalloc(&e->slots[s].k, n));
+  CK(cudaMalloc(&e->slots[s].v, n));
+  CK(cudaMemset(e->slots[s].k, 0, n));
+  CK(cudaMemset(e->slots[s].v, 0, n));
   return cudaSuccess;
 }
 
@@ -387,9 +388,12 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   const Slot& sl = e->slots[e->active];
   for (int l = 0; l < e->L; l++) {
     const LayerDev& lw = e->layers[l];
-    const size_t layer_off = (size_t)l * e->nkv * e->S * e->hd;
-    KvCache kv{sl.k + layer_off, sl.v + layer_off, e->S};
-    if (P.batch) kv = KvCache{nullptr, nullptr, e->S, e->d_bstage->pos, e->d_bstage->k, e->d_bstage->v, layer_off};
+    const size_t layer_off = (size_t)l * e->nkv * e->S * e->hd;  // elements
+    const int f16 = e->kv_es == 2 ? 1 : 0;
+    KvCache kv{(float*)((char*)sl.k + layer_off * e->kv_es), (float*)((char*)sl.v + layer_off * e->kv_es), e->S,
+               nullptr, nullptr, nullptr, 0, f16};
+    if (P.batch)
+      kv = KvCache{nullptr, nullptr, e->S, e->d_bstage->pos, e->d_bstage->k, e->d_bstage->v, layer_off, f16};
     // 1-2. [h += hn] RMSNorm + prep of q/k/v inputs
     {
       const W12* ws[3] = {&lw.q, &lw.k, &lw.v};
@@ -521,6 +525,7 @@ bool uniform_tiles(const DpufWeightDesc& w, long long* stride, long long* first)
 // per SM with a ring of at least four stages.
 void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* tok, const DpufWeightDesc* lm) {
   auto no = [&](const std::string& why) { e->dec_ok = false; e->dec_why = why; };
+  if (e->kv_es != 4) return no("fp16 KV cache (the persistent kernel keeps the reference's fp32 cache)");
   int coop = 0, sms = 0;
   if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device) != cudaSuccess || !coop)
     return no("device without cooperative launch");
@@ -907,6 +912,7 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
     e->prep[i] = Act{e->prep_q8 + i * B * ld, e->prep_xs + i * B * (ld / 32), e->prep_xm + i * B * (ld / 32), ld};
   cudaMemset(e->d_flag, 0, 16);
   cudaMemset(e->d_counter, 0, 64);
+  e->kv_es = env_int("DPUF_CUDA_KV_F16", 0) ? 2 : 4;
   if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
   e->use_persistent = env_int("DPUF_CUDA_PERSISTENT", 1) != 0;
   plan_decode(e, layers, tok, lm);
@@ -992,7 +998,7 @@ DPUF_EXPORT void dpuf_engine_reset_slot(void* handle, int32_t slot_id) {
   Engine* e = (Engine*)handle;
   if (!e || slot_id < 0 || slot_id >= e->n_slots || !e->slots[slot_id].k) return;
   cudaSetDevice(e->device);
-  const size_t n = (size_t)e->L * e->S * e->kvd * 4;
+  const size_t n = (size_t)e->L * e->S * e->kvd * e->kv_es;
   cudaMemsetAsync(e->slots[slot_id].k, 0, n, e->stream);
   cudaMemsetAsync(e->slots[slot_id].v, 0, n, e->stream);
   cudaStreamSynchronize(e->stream);
@@ -1005,7 +1011,7 @@ DPUF_EXPORT void dpuf_engine_reset_cache(void* handle) {
 
 DPUF_EXPORT size_t dpuf_engine_slot_memory(void* handle) {
   Engine* e = (Engine*)handle;
-  return e ? 2 * (size_t)e->L * e->S * e->kvd * sizeof(float) : 0;
+  return e ? 2 * (size_t)e->L * e->S * e->kvd * e->kv_es : 0;
 }
 
 // Freeze / apply copy [L][n_kv][len][hd] between the active slot and a prefix store with one
@@ -1020,15 +1026,15 @@ DPUF_EXPORT int32_t dpuf_engine_freeze_prefix(void* handle, int32_t pfx_id, int3
     cudaFree(p.k);
     cudaFree(p.v);
     p = dpuf::Prefix();
-    if (cudaMalloc(&p.k, rows * prefix_len * hd * 4) != cudaSuccess) { p.k = nullptr; return 0; }
-    if (cudaMalloc(&p.v, rows * prefix_len * hd * 4) != cudaSuccess) { cudaFree(p.k); p.k = nullptr; p.v = nullptr; return 0; }
+    if (cudaMalloc(&p.k, rows * prefix_len * hd * e->kv_es) != cudaSuccess) { p.k = nullptr; return 0; }
+    if (cudaMalloc(&p.v, rows * prefix_len * hd * e->kv_es) != cudaSuccess) { cudaFree(p.k); p.k = nullptr; p.v = nullptr; return 0; }
     p.cap = prefix_len;
   }
   const dpuf::Slot& s = e->slots[e->active];
   if (!s.k) return 0;
-  const size_t w = (size_t)prefix_len * hd * 4;
-  if (cudaMemcpy2DAsync(p.k, w, s.k, (size_t)e->S * hd * 4, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
-      cudaMemcpy2DAsync(p.v, w, s.v, (size_t)e->S * hd * 4, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+  const size_t w = (size_t)prefix_len * hd * e->kv_es;
+  if (cudaMemcpy2DAsync(p.k, w, s.k, (size_t)e->S * hd * e->kv_es, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(p.v, w, s.v, (size_t)e->S * hd * e->kv_es, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
       cudaStreamSynchronize(e->stream))
     return 0;
   p.len = prefix_len;
@@ -1044,9 +1050,9 @@ DPUF_EXPORT int32_t dpuf_engine_apply_prefix(void* handle, int32_t slot_id, int3
   cudaSetDevice(e->device);
   if (dpuf::slot_alloc(e, slot_id) != cudaSuccess) return 0;
   const dpuf::Slot& s = e->slots[slot_id];
-  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd, w = (size_t)p.len * hd * 4;
-  if (cudaMemcpy2DAsync(s.k, (size_t)e->S * hd * 4, p.k, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
-      cudaMemcpy2DAsync(s.v, (size_t)e->S * hd * 4, p.v, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd, w = (size_t)p.len * hd * e->kv_es;
+  if (cudaMemcpy2DAsync(s.k, (size_t)e->S * hd * e->kv_es, p.k, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(s.v, (size_t)e->S * hd * e->kv_es, p.v, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
       cudaStreamSynchronize(e->stream))
     return 0;
   return p.len;

@@ -78,7 +78,8 @@ struct KvCache {
   const int32_t* tok_pos;
   float* const* tok_k;
   float* const* tok_v;
-  size_t layer_off;
+  size_t layer_off;  // elements
+  int f16;           // 1: the caches hold fp16 elements (the pointers are then raw storage)
 };
 cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
                            const float* q_norm, const float* k_norm, float eps, const float* cos_tab,

@@ -29,6 +29,7 @@ struct CtaSync {
   DPUF_DEV void operator()() const { __syncthreads(); }
 };
 
+template <typename T>  // cache element: float, or __half for an fp16 cache
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __restrict__ q, int n_q, int n_kv, int hd,
                                                                   const int* __restrict__ pos0_dev, KvCache kv,
                                                                   float* __restrict__ out, ExpfTable et) {
@@ -37,18 +38,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
   cudaGridDependencySynchronize();
   const int m = blockIdx.x, kvh = blockIdx.y;
   int ppc, n_buf;
-  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf);
+  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf, (int)sizeof(T));
   const int groups = n_q / n_kv;
   const int g0 = blockIdx.z * 2 * ppc;
   const int nh = min(2 * ppc, groups - g0);  // the last head of an odd group is a lone head
   const int qh0 = kvh * groups + g0;
   const int kv_len = (kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m) + 1;
-  const float* kbase = kv.tok_k ? kv.tok_k[m] + kv.layer_off : kv.k;
-  const float* vbase = kv.tok_v ? kv.tok_v[m] + kv.layer_off : kv.v;
+  const T* kbase = kv.tok_k ? (const T*)kv.tok_k[m] + kv.layer_off : (const T*)kv.k;
+  const T* vbase = kv.tok_v ? (const T*)kv.tok_v[m] + kv.layer_off : (const T*)kv.v;
   const int sc_stride = (kv.max_seq + 3) & ~3;
   float* qs = sm;                                 // [2 ppc][hd]
   float* sc = qs + 2 * ppc * hd;                  // [2 ppc][sc_stride]
-  float* kt = sc + (size_t)2 * ppc * sc_stride;   // [n_buf][kAttnKeyTile][hd + 8]
+  T* kt = (T*)(sc + (size_t)2 * ppc * sc_stride);  // [n_buf][kAttnKeyTile][hd + pad]
   for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) qs[i] = q[((size_t)m * n_q + qh0) * hd + i];
   attn_pair_body(qs, nh, (nh & 1) != 0, hd, kv_len, kbase + (size_t)kvh * kv.max_seq * hd,
                  vbase + (size_t)kvh * kv.max_seq * hd, sc_stride, sc, kt, n_buf, 0, nullptr, nullptr, &sh,
@@ -58,18 +59,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const float* __
 }  // namespace
 
 cudaError_t configure_attn_kernels() {
-  return set_max_dyn_smem(attention_kernel);
+  cudaError_t e = set_max_dyn_smem(attention_kernel<float>);
+  return e != cudaSuccess ? e : set_max_dyn_smem(attention_kernel<__half>);
 }
 
 cudaError_t launch_attention(const Launch& L, const float* q, int M, int n_q, int n_kv, int hd, const int* pos0_dev,
                              KvCache kv, float* out, const ExpfTable& et) {
   int ppc, n_buf;
-  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf);
+  const int es = kv.f16 ? 2 : 4;
+  attn_step_plan(hd, kv.max_seq, &ppc, &n_buf, es);
   const int groups = n_q / n_kv;
-  const size_t smem = attn_step_floats(hd, kv.max_seq, ppc, n_buf) * sizeof(float);
+  const size_t smem = attn_step_floats(hd, kv.max_seq, ppc, n_buf, es) * sizeof(float);
   if (smem > kMaxDynSmem) return cudaErrorInvalidValue;
-  return launch_k(L, attention_kernel, dim3(M, n_kv, (groups + 2 * ppc - 1) / (2 * ppc)), dim3(kAttnThreads), smem, q,
-                  n_q, n_kv, hd, pos0_dev, kv, out, et);
+  const dim3 grid(M, n_kv, (groups + 2 * ppc - 1) / (2 * ppc));
+  if (kv.f16)
+    return launch_k(L, attention_kernel<__half>, grid, dim3(kAttnThreads), smem, q, n_q, n_kv, hd, pos0_dev, kv, out, et);
+  return launch_k(L, attention_kernel<float>, grid, dim3(kAttnThreads), smem, q, n_q, n_kv, hd, pos0_dev, kv, out, et);
 }
 
 }  // namespace dpuf

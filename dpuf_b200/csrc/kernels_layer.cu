@@ -91,8 +91,9 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   const int hidx = blockIdx.y * (blockDim.x >> 5) + warp;
   if (hidx >= n_q + n_kv) return;
   const int pos = kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m;
-  float* const kbase = kv.tok_k ? kv.tok_k[m] + kv.layer_off : kv.k;
-  float* const vbase = kv.tok_v ? kv.tok_v[m] + kv.layer_off : kv.v;
+  const int es = kv.f16 ? 2 : 4;  // bytes per cache element
+  char* const kbase = (char*)(kv.tok_k ? kv.tok_k[m] : kv.k) + (kv.tok_k ? kv.layer_off * es : 0);
+  char* const vbase = (char*)(kv.tok_v ? kv.tok_v[m] : kv.v) + (kv.tok_v ? kv.layer_off * es : 0);
   const bool is_k = hidx < n_kv;
   const int head = is_k ? hidx : hidx - n_kv;
   float* vec = is_k ? k + ((size_t)m * n_kv + head) * hd : q + ((size_t)m * n_q + head) * hd;
@@ -103,12 +104,23 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   qk_norm_rope_warp(s, nw, eps, hd, cos_tab + (size_t)pos * (hd >> 1), sin_tab + (size_t)pos * (hd >> 1), lane);
   for (int i = lane; i < hd; i += 32) {
     vec[i] = s[i];
-    if (is_k) kbase[((size_t)head * kv.max_seq + pos) * hd + i] = s[i];
+    if (is_k) {
+      const size_t e = ((size_t)head * kv.max_seq + pos) * hd + i;
+      if (kv.f16)
+        ((__half*)kbase)[e] = __float2half_rn(s[i]);
+      else
+        ((float*)kbase)[e] = s[i];
+    }
   }
   if (is_k) {
     const float* vr = v + ((size_t)m * n_kv + head) * hd;
-    float* vc = vbase + ((size_t)head * kv.max_seq + pos) * hd;
-    for (int i = lane; i < hd; i += 32) vc[i] = vr[i];
+    const size_t e0 = ((size_t)head * kv.max_seq + pos) * hd;
+    for (int i = lane; i < hd; i += 32) {
+      if (kv.f16)
+        ((__half*)vbase)[e0 + i] = __float2half_rn(vr[i]);
+      else
+        ((float*)vbase)[e0 + i] = vr[i];
+    }
   }
 }
 

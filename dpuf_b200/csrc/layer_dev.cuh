@@ -294,27 +294,40 @@ struct AttnShared {
   float inv_s[kAttnMaxHeads], max_s[kAttnMaxHeads];
 };
 
-DPUF_HD size_t attn_tile_floats(int hd) { return (size_t)kAttnKeyTile * (hd + 8); }
+// Key/value tiles hold the cache's element type T: fp32, or fp16 for an fp16 cache (values are
+// widened to fp32 as they are used).  Rows are padded (8 floats, 16 halves) so that the score
+// loop's eight threads per key and four keys per warp read distinct banks; a padded row stays a
+// multiple of 16 bytes for the async copies.
+template <typename T>
+DPUF_HD constexpr int attn_row_pad() { return sizeof(T) == 4 ? 8 : 16; }
+DPUF_DEV float kv_to_f(float x) { return x; }
+DPUF_DEV float kv_to_f(__half x) { return __half2float(x); }
+DPUF_DEV void kv_from_f(float& d, float x) { d = x; }
+DPUF_DEV void kv_from_f(__half& d, float x) { d = __float2half_rn(x); }
+// A tile's size in floats of scratch for elements of es bytes (4 or 2).
+DPUF_HD size_t attn_tile_floats(int hd, int es = 4) {
+  return es == 4 ? (size_t)kAttnKeyTile * (hd + 8) : (size_t)kAttnKeyTile * (hd + 16) / 2;
+}
 // Scores of two heads over max_seq keys (the persistent kernel's pair).
 DPUF_HD size_t attn_sc_floats(int max_seq) { return 2 * (((size_t)max_seq + 3) & ~(size_t)3); }
 // Scratch of the per-step kernel with ppc pairs per CTA and n_buf tiles: qs [2 ppc][hd] |
 // sc [2 ppc][max_seq padded to 4] | n_buf tiles (16-byte aligned for the async copies).
-DPUF_HD size_t attn_step_floats(int hd, int max_seq, int ppc, int n_buf) {
-  return (size_t)2 * ppc * hd + ppc * attn_sc_floats(max_seq) + n_buf * attn_tile_floats(hd);
+DPUF_HD size_t attn_step_floats(int hd, int max_seq, int ppc, int n_buf, int es = 4) {
+  return (size_t)2 * ppc * hd + ppc * attn_sc_floats(max_seq) + n_buf * attn_tile_floats(hd, es);
 }
 // The per-step kernel's plan: two pairs per CTA (four query heads sharing the staged keys and
 // values) when their outputs fit two per thread, and two tiles in flight, each dropped to one
 // when the scratch would not fit the shared memory.
-DPUF_HD void attn_step_plan(int hd, int max_seq, int* ppc, int* n_buf) {
+DPUF_HD void attn_step_plan(int hd, int max_seq, int* ppc, int* n_buf, int es = 4) {
   *ppc = 4 * hd <= 2 * kAttnThreads ? 2 : 1;
   *n_buf = 2;
-  if (attn_step_floats(hd, max_seq, *ppc, *n_buf) * 4 > (size_t)kMaxDynSmem) *n_buf = 1;
-  if (attn_step_floats(hd, max_seq, *ppc, *n_buf) * 4 > (size_t)kMaxDynSmem) *ppc = 1;
+  if (attn_step_floats(hd, max_seq, *ppc, *n_buf, es) * 4 > (size_t)kMaxDynSmem) *n_buf = 1;
+  if (attn_step_floats(hd, max_seq, *ppc, *n_buf, es) * 4 > (size_t)kMaxDynSmem) *ppc = 1;
 }
-DPUF_HD size_t attn_scratch_floats(int hd, int max_seq) {
+DPUF_HD size_t attn_scratch_floats(int hd, int max_seq, int es = 4) {
   int ppc, n_buf;
-  attn_step_plan(hd, max_seq, &ppc, &n_buf);
-  return attn_step_floats(hd, max_seq, ppc, n_buf);
+  attn_step_plan(hd, max_seq, &ppc, &n_buf, es);
+  return attn_step_floats(hd, max_seq, ppc, n_buf, es);
 }
 
 // ------------------------------------------------------------------ async copies to shared
@@ -345,38 +358,39 @@ DPUF_DEV void cp_async_wait_pending(int n) {
 // into buffer `buf` with a padded row stride of hd + 8: rows [32t, min(32t + 32, n_rows)) -
 // n_rows excludes a row the caller supplies itself.  Every thread commits a group, with or
 // without copies.
-DPUF_DEV void attn_issue_tile(float* buf, const float* src, int t, int n_rows, int hd, int tid) {
+template <typename T>
+DPUF_DEV void attn_issue_tile(T* buf, const T* src, int t, int n_rows, int hd, int tid) {
+  constexpr int kPer = 16 / sizeof(T);  // elements per 16-byte piece
   const int t0 = t * kAttnKeyTile;
   const int nk = max(0, min(kAttnKeyTile, n_rows - t0));
-  const int per_row = hd >> 2, n = nk * per_row;
+  const int per_row = hd / kPer, n = nk * per_row;
   for (int i = tid; i < n; i += kAttnThreads) {
-    const int r = i / per_row, c = (i - r * per_row) * 4;
-    cp_async16_cg(buf + r * (hd + 8) + c, src + (size_t)(t0 + r) * hd + c);
+    const int r = i / per_row, c = (i - r * per_row) * kPer;
+    cp_async16_cg(buf + r * (hd + attn_row_pad<T>()) + c, src + (size_t)(t0 + r) * hd + c);
   }
   cp_async_commit();
 }
 
 // Waits for tile t (tiles t+1 .. min(t + n_buf, n_t) - 1 may stay in flight), writes row
 // `cur_row` from `cur` when the tile holds it, then sync().
-template <typename Sync>
-DPUF_DEV void attn_land_tile(float* buf, int t, int n_t, int n_buf, const float* cur, int cur_row, int hd, int tid,
+template <typename T, typename Sync>
+DPUF_DEV void attn_land_tile(T* buf, int t, int n_t, int n_buf, const float* cur, int cur_row, int hd, int tid,
                              Sync sync) {
   cp_async_wait_pending(min(n_buf - 1, n_t - 1 - t));
   const int t0 = t * kAttnKeyTile;
   if (cur && cur_row >= t0 && cur_row < t0 + kAttnKeyTile)
-    for (int i = tid; i < (hd >> 2); i += kAttnThreads)
-      *(float4*)(buf + (cur_row - t0) * (hd + 8) + 4 * i) = *(const float4*)(cur + 4 * i);
+    for (int i = tid; i < hd; i += kAttnThreads) kv_from_f(buf[(cur_row - t0) * (hd + attn_row_pad<T>()) + i], cur[i]);
   sync();
 }
 
-template <typename Sync>
-DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_len, const float* kc,
-                             const float* vc, int sc_stride, float* sc, float* kt, int n_buf, int pre,
-                             const float* cur_k, const float* cur_v, AttnShared* sh, float* out,
-                             const ExpfTable& et, int tid, Sync sync, bool out_to_qs = false) {
+template <typename T, typename Sync>
+DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_len, const T* kc, const T* vc,
+                             int sc_stride, float* sc, T* kt, int n_buf, int pre, const float* cur_k,
+                             const float* cur_v, AttnShared* sh, float* out, const ExpfTable& et, int tid, Sync sync,
+                             bool out_to_qs = false) {
   const int lane = tid & 31;
-  const int kvs = hd + 8;  // padded smem row of a staged key
-  const size_t tile = attn_tile_floats(hd);
+  const int kvs = hd + attn_row_pad<T>();  // padded smem row of a staged key
+  const size_t tile = (size_t)kAttnKeyTile * kvs;  // elements
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
   const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
@@ -387,12 +401,12 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
   for (int t = 0; t < n_t; t++) {
     const int t0 = t * kAttnKeyTile;
     const int nk = min(kAttnKeyTile, kv_len - t0);
-    float* buf = kt + (size_t)(t % n_buf) * tile;
+    T* buf = kt + (size_t)(t % n_buf) * tile;
     attn_land_tile(buf, t, n_t, n_buf, cur_k, kv_len - 1, hd, tid, sync);
     const int key = tid >> 3, l = tid & 7;
     const int tk = t0 + key;
     const bool valid = key < nk;
-    const float* kp = buf + key * kvs;
+    const T* kp = buf + key * kvs;
 #pragma unroll
     for (int h = 0; h < kAttnMaxHeads; h++) {
       if (h >= nh) break;
@@ -400,7 +414,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
       // Shuffle trees run on all lanes (keys of one warp may sit on both sides of kv4).
       float acc = 0.0f;
       if (valid)
-        for (int i = l; i < hd; i += 8) acc = __fmaf_rn(qv[i], kp[i], acc);
+        for (int i = l; i < hd; i += 8) acc = __fmaf_rn(qv[i], kv_to_f(kp[i]), acc);
       const float t_pairs = tree8_pairs(acc);
       float t_split;
       if (!(last_lone && h == nh - 1)) {
@@ -411,10 +425,10 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
         if (valid) {
           int i = 0;
           for (; i + 15 < hd; i += 16) {
-            a0 = __fmaf_rn(qv[i + l], kp[i + l], a0);
-            a1 = __fmaf_rn(qv[i + 8 + l], kp[i + 8 + l], a1);
+            a0 = __fmaf_rn(qv[i + l], kv_to_f(kp[i + l]), a0);
+            a1 = __fmaf_rn(qv[i + 8 + l], kv_to_f(kp[i + 8 + l]), a1);
           }
-          for (; i + 7 < hd; i += 8) a0 = __fmaf_rn(qv[i + l], kp[i + l], a0);
+          for (; i + 7 < hd; i += 8) a0 = __fmaf_rn(qv[i + l], kv_to_f(kp[i + l]), a0);
         }
         t_split = tree8_split(__fadd_rn(a0, a1));
       }
@@ -485,7 +499,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
   for (int t = 0; t < n_t; t++) {
     const int t0 = t * kAttnKeyTile;
     const int nk = min(kAttnKeyTile, kv_len - t0);
-    float* buf = kt + (size_t)(t % n_buf) * tile;
+    T* buf = kt + (size_t)(t % n_buf) * tile;
     attn_land_tile(buf, t, n_t, n_buf, cur_v, kv_len - 1, hd, tid, sync);
 #pragma unroll
     for (int j = 0; j < 2; j++) {
@@ -493,21 +507,21 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
       if (o >= nh * hd) break;
       const int h = o / hd, d = o % hd;
       const float* pp = sc + h * sc_stride + t0;
-      const float* vt = buf + d;
+      const T* vt = buf + d;
       float a = acc[j];
       if (!(last_lone && h == nh - 1)) {
-        for (int k = 0; k < nk; k++) a = __fmaf_rn(pp[k], vt[k * kvs], a);
+        for (int k = 0; k < nk; k++) a = __fmaf_rn(pp[k], kv_to_f(vt[k * kvs]), a);
       } else if ((hd & 63) == 0) {
         // keys two at a time, k+1 first (tiles hold an even number of keys but the last)
         int k = 0;
         for (; k + 1 < nk; k += 2) {
-          const float t1 = __fmaf_rn(pp[k + 1], vt[(k + 1) * kvs], a);
-          a = __fmaf_rn(pp[k], vt[k * kvs], t1);
+          const float t1 = __fmaf_rn(pp[k + 1], kv_to_f(vt[(k + 1) * kvs]), a);
+          a = __fmaf_rn(pp[k], kv_to_f(vt[k * kvs]), t1);
         }
-        if (k < nk) a = __fmaf_rn(pp[k], vt[k * kvs], a);
+        if (k < nk) a = __fmaf_rn(pp[k], kv_to_f(vt[k * kvs]), a);
       } else {
         for (int k = 0; k < nk; k++) {
-          const float pv = pp[k], vv = vt[k * kvs];
+          const float pv = pp[k], vv = kv_to_f(vt[k * kvs]);
           a = (d < hd8) ? __fmaf_rn(pv, vv, a) : __fadd_rn(a, __fmul_rn(pv, vv));
         }
       }

@@ -38,7 +38,10 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_greedy(void* handle, int32_t first_id, int3
  * vector/scalar split), so its logits and id equal dpuf_engine_forward_token's on that slot
  * (DPUF_GEN_KEEP_TILES applies; Zone A does not).  next_ids[n] (host) receive the greedy ids,
  * logits_out (optional, host) [n][vocab].  Env DPUF_CUDA_SLOTS (default 8, the reference's
- * count; at most 256) sets the number of slots at create.  Returns the forward codes. */
+ * count; at most 256) sets the number of slots at create.  Env DPUF_CUDA_KV_F16=1 at create
+ * stores every slot's (and prefix's) K and V in fp16, halving the cache and its reads (the
+ * reference's cache is fp32: results then agree within tolerance, not bit for bit; batch-1
+ * steps use the per-step kernels).  Returns the forward codes. */
 DPUF_EXPORT int32_t dpuf_cuda_decode_batch(void* handle, int32_t n, const int32_t* slots, const int32_t* ids,
                                            const int32_t* pos, int32_t* next_ids, float* logits_out);
 
@@ -81,8 +84,9 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_
  *      buffers (NVLink peer access).  Every rank must be on a GPU of its own (checked by PCI bus
  *      id): the ranks' kernels wait on each other.
  * From then on each batch-1 step that runs as the persistent kernel splits every projection
- * and the LM head over all ranks' CTAs; each rank stores its outputs to every rank's buffer
- * and the ranks meet at global barriers after q/k/v, o, gate/up, down and the LM head.
+ * and the LM head over all ranks' CTAs; each rank stores its outputs, tagged with the phase
+ * that produced them, to every rank's buffer, and readers wait on those tags (no cross-GPU
+ * barrier).
  * Attention, norms and everything else run in full on every rank, so every rank returns the
  * same ids and logits, bit-identical to one GPU.  All ranks must make the same calls with the
  * same arguments in the same order (steps with M > 1, or with Zone A, simply run in full on
