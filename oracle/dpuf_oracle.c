@@ -453,6 +453,139 @@ static void attn_pair(int32_t hd, int32_t kv_len, float scale, const float* kc, 
     }
 }
 
+/* ------------------------------------------------------------------ Q8 KV cache (kv_type 1) */
+
+/* _mm256_cvtps_epi32 (round to nearest even) followed by the saturating packs and the
+ * max(-127) of quantize_vec_q8_blk32: a NaN or out-of-range product becomes the x86 "integer
+ * indefinite" INT32_MIN, i.e. -127 after saturation. */
+static int8_t q8_cvt(float y) {
+    if (!(y == y) || y >= 2147483648.0f || y < -2147483648.0f) return -127;
+    float r = nearbyintf(y);
+    if (r > 127.0f) return 127;
+    if (r < -127.0f) return -127;
+    return (int8_t)r;
+}
+
+/* quantize_vec_q8_blk32 (dpuf_engine.c:751-781): per 32-element block, amax by the reference's
+ * max tree (lanes j, j+8, j+16, j+24; then the 4-wide and 2-wide folds), scale = amax / 127,
+ * q = cvt(x * (127 / amax)), or 0 when amax <= 1e-12. */
+ORC_EXPORT void orc_quantize_q8_blk32(int32_t n, const float* src, int8_t* dst, float* scales) {
+    for (int32_t b = 0; b < (n >> 5); b++) {
+        const float* x = src + (b << 5);
+        float ln[8];
+        for (int l = 0; l < 8; l++)
+            ln[l] = maxf_ps(maxf_ps(fabsf(x[l]), fabsf(x[8 + l])), maxf_ps(fabsf(x[16 + l]), fabsf(x[24 + l])));
+        float m4[4];
+        for (int l = 0; l < 4; l++) m4[l] = maxf_ps(ln[l], ln[4 + l]);
+        float amax = maxf_ps(maxf_ps(m4[0], m4[2]), maxf_ps(m4[1], m4[3]));
+        scales[b] = amax / 127.0f;
+        float inv = (amax > 1e-12f) ? (127.0f / amax) : 0.0f;
+        for (int i = 0; i < 32; i++) dst[(b << 5) + i] = q8_cvt(x[i] * inv);
+    }
+}
+
+/* dot_f32_q8_blk32_avx2 (dpuf_engine.c:603-619): per block two lane accumulators (elements
+ * l, l+16 and l+8, l+24), their sum times the block scale fused into the total; split tree. */
+static float dot_q8_blk32(int32_t n, const float* q, const int8_t* kq, const float* ks) {
+    float tot[8] = {0};
+    for (int32_t b = 0; b < (n >> 5); b++) {
+        const int32_t c0 = b << 5;
+        for (int l = 0; l < 8; l++) {
+            float a0 = fmaf(q[c0 + l], (float)kq[c0 + l], 0.0f);
+            float a1 = fmaf(q[c0 + 8 + l], (float)kq[c0 + 8 + l], 0.0f);
+            a0 = fmaf(q[c0 + 16 + l], (float)kq[c0 + 16 + l], a0);
+            a1 = fmaf(q[c0 + 24 + l], (float)kq[c0 + 24 + l], a1);
+            tot[l] = fmaf(a0 + a1, ks[b], tot[l]);
+        }
+    }
+    return hsum8_split(tot);
+}
+
+/* vec_softmax_avx2 (dpuf_engine.c:579-601). */
+static void softmax_ref(int32_t n, float* s, float mx) {
+    float lane[8] = {0};
+    int32_t k = 0;
+    for (; k + 7 < n; k += 8)
+        for (int l = 0; l < 8; l++) {
+            float e = exp_poly(s[k + l] - mx);
+            s[k + l] = e;
+            lane[l] = lane[l] + e;
+        }
+    float sp = hsum8_split(lane);
+    for (; k < n; k++) { float e = expf(s[k] - mx); s[k] = e; sp += e; }
+    float inv = 1.0f / (sp + 1e-12f);
+    for (k = 0; k < n; k++) s[k] = s[k] * inv;
+}
+
+/* gqa_attn_head_pair_q8 (dpuf_engine.c:621-749) over one KV head's int8 rows kc/vc [.][hd] and
+ * block scales ksc/vsc [.][hd/32].  Pair path: keys two at a time, per block and lane
+ * t = fma(q[l], k[l], fma(q[l+8], k[l+8], t)) over the two 16-wide halves, then the block
+ * scale fused into the lane sum, pairs tree; an odd last key and the lone head use
+ * dot_q8_blk32.  PV per output d: fma(p_k * vs_k[d/32], v_kd, acc) over k ascending. */
+static void attn_pair_q8(int32_t hd, int32_t kv_len, float scale, const int8_t* kc, const float* ksc,
+                         const int8_t* vc, const float* vsc, const float* q0, const float* q1, float* sc0,
+                         float* sc1, float* o0, float* o1) {
+    const int32_t nb = hd >> 5;
+    float mx0 = -1e30f, mx1 = -1e30f;
+    int32_t t = 0;
+    if (q1) {
+        for (; t + 1 < kv_len; t += 2) {
+            float d[2][2];
+            for (int kk = 0; kk < 2; kk++) {
+                const int8_t* kp = kc + (size_t)(t + kk) * (size_t)hd;
+                const float* ks = ksc + (size_t)(t + kk) * (size_t)nb;
+                float a[8] = {0}, b[8] = {0};
+                for (int32_t bl = 0; bl < nb; bl++) {
+                    const int32_t c0 = bl << 5;
+                    for (int l = 0; l < 8; l++) {
+                        float ta = 0.0f, tb = 0.0f;
+                        for (int j = 0; j < 32; j += 16) {
+                            float fl = (float)kp[c0 + j + l], fh = (float)kp[c0 + j + 8 + l];
+                            ta = fmaf(q0[c0 + j + l], fl, fmaf(q0[c0 + j + 8 + l], fh, ta));
+                            tb = fmaf(q1[c0 + j + l], fl, fmaf(q1[c0 + j + 8 + l], fh, tb));
+                        }
+                        a[l] = fmaf(ta, ks[bl], a[l]);
+                        b[l] = fmaf(tb, ks[bl], b[l]);
+                    }
+                }
+                d[0][kk] = hsum8_pairs(a) * scale;
+                d[1][kk] = hsum8_pairs(b) * scale;
+            }
+            sc0[t] = d[0][0]; sc0[t + 1] = d[0][1];
+            sc1[t] = d[1][0]; sc1[t + 1] = d[1][1];
+            mx0 = maxf_ps(mx0, (d[0][0] > d[0][1]) ? d[0][0] : d[0][1]);
+            mx1 = maxf_ps(mx1, (d[1][0] > d[1][1]) ? d[1][0] : d[1][1]);
+        }
+        for (; t < kv_len; t++) {
+            float s0 = dot_q8_blk32(hd, q0, kc + (size_t)t * hd, ksc + (size_t)t * nb) * scale;
+            float s1 = dot_q8_blk32(hd, q1, kc + (size_t)t * hd, ksc + (size_t)t * nb) * scale;
+            sc0[t] = s0; if (s0 > mx0) mx0 = s0;
+            sc1[t] = s1; if (s1 > mx1) mx1 = s1;
+        }
+        softmax_ref(kv_len, sc0, mx0);
+        softmax_ref(kv_len, sc1, mx1);
+    } else {
+        for (; t < kv_len; t++) {
+            float s = dot_q8_blk32(hd, q0, kc + (size_t)t * hd, ksc + (size_t)t * nb) * scale;
+            sc0[t] = s;
+            if (s > mx0) mx0 = s;
+        }
+        softmax_ref(kv_len, sc0, mx0);
+    }
+    for (int32_t dd = 0; dd < hd; dd++) {
+        const int32_t bl = dd >> 5;
+        float a = 0.0f, b = 0.0f;
+        for (int32_t k = 0; k < kv_len; k++) {
+            const float vs = vsc[(size_t)k * nb + bl];
+            const float v = (float)vc[(size_t)k * hd + dd];
+            a = fmaf(sc0[k] * vs, v, a);
+            if (q1) b = fmaf(sc1[k] * vs, v, b);
+        }
+        o0[dd] = a;
+        if (q1) o1[dd] = b;
+    }
+}
+
 /* ------------------------------------------------------------------ engine */
 
 typedef struct {
@@ -462,6 +595,8 @@ typedef struct {
     const float* out_norm;
     float *cos_tab, *sin_tab;
     float *k_cache, *v_cache; /* [L][n_kv][max_seq][hd] */
+    int8_t *k_q8, *v_q8;      /* kv_type 1: [L][n_kv][max_seq][hd] and block scales */
+    float *k_sc, *v_sc;       /* [L][n_kv][max_seq][hd/32] */
     float *h, *hn, *q, *k, *v, *att, *gate, *up, *ffn;
     int8_t* pq;
     float* pxs;
@@ -495,6 +630,12 @@ ORC_EXPORT void* orc_engine_create(const DpufModelConfig* cfg, const DpufLayerWe
     size_t kv = (size_t)cfg->num_layers * (size_t)S * (size_t)kvd;
     e->k_cache = (float*)calloc(kv, sizeof(float));
     e->v_cache = (float*)calloc(kv, sizeof(float));
+    if (cfg->kv_type == DPUF_KV_Q8) {
+        e->k_q8 = (int8_t*)calloc(kv, 1);
+        e->v_q8 = (int8_t*)calloc(kv, 1);
+        e->k_sc = (float*)calloc(kv / 32, sizeof(float));
+        e->v_sc = (float*)calloc(kv / 32, sizeof(float));
+    }
     e->h = (float*)malloc(B * H * sizeof(float));
     e->hn = (float*)malloc(B * H * sizeof(float));
     e->q = (float*)malloc(B * qd * sizeof(float));
@@ -516,6 +657,7 @@ ORC_EXPORT void orc_engine_destroy(void* handle) {
     OrcEngine* e = (OrcEngine*)handle;
     if (!e) return;
     free(e->layers); free(e->cos_tab); free(e->sin_tab); free(e->k_cache); free(e->v_cache);
+    free(e->k_q8); free(e->v_q8); free(e->k_sc); free(e->v_sc);
     free(e->h); free(e->hn); free(e->q); free(e->k); free(e->v); free(e->att);
     free(e->gate); free(e->up); free(e->ffn); free(e->pq); free(e->pxs); free(e->pxm);
     free(e->sc0); free(e->sc1);
@@ -527,6 +669,12 @@ ORC_EXPORT void orc_engine_reset_cache(void* handle) {
     size_t kv = (size_t)e->cfg.num_layers * (size_t)e->cfg.max_seq_len * (size_t)(e->cfg.num_kv_heads * e->cfg.head_dim);
     memset(e->k_cache, 0, kv * sizeof(float));
     memset(e->v_cache, 0, kv * sizeof(float));
+    if (e->k_q8) {
+        memset(e->k_q8, 0, kv);
+        memset(e->v_q8, 0, kv);
+        memset(e->k_sc, 0, kv / 32 * sizeof(float));
+        memset(e->v_sc, 0, kv / 32 * sizeof(float));
+    }
 }
 
 /* y[M][rows] = W x for each token (prep with this weight's signs, then matvec). */
@@ -575,8 +723,13 @@ ORC_EXPORT int32_t orc_engine_forward(void* handle, int32_t M, const int32_t* id
                 if (c->has_qk_norm && lw->attn_k_norm) orc_add_rmsnorm(hd, ks, NULL, lw->attn_k_norm, eps, ks);
                 rope_apply(hd, ks, cs, sn);
                 size_t off = ((size_t)l * nkv + kh) * (size_t)S * hd + (size_t)pos * hd;
-                memcpy(e->k_cache + off, ks, (size_t)hd * sizeof(float));
-                memcpy(e->v_cache + off, vs, (size_t)hd * sizeof(float));
+                if (e->k_q8) {
+                    orc_quantize_q8_blk32(hd, ks, e->k_q8 + off, e->k_sc + off / 32);
+                    orc_quantize_q8_blk32(hd, vs, e->v_q8 + off, e->v_sc + off / 32);
+                } else {
+                    memcpy(e->k_cache + off, ks, (size_t)hd * sizeof(float));
+                    memcpy(e->v_cache + off, vs, (size_t)hd * sizeof(float));
+                }
             }
             for (int32_t qh = 0; qh < nq; qh++) {
                 float* qv = e->q + (size_t)m * qd + (size_t)qh * hd;
@@ -594,8 +747,15 @@ ORC_EXPORT int32_t orc_engine_forward(void* handle, int32_t M, const int32_t* id
                     const float* q0 = e->q + (size_t)m * qd + (size_t)qh * hd;
                     float* a0 = e->att + (size_t)m * qd + (size_t)qh * hd;
                     int pair = (g + 1 < groups);
-                    attn_pair(hd, kv_len, scale, kc, vc, q0, pair ? q0 + hd : NULL, e->sc0, e->sc1, a0,
-                              pair ? a0 + hd : NULL);
+                    if (e->k_q8) {
+                        const size_t ho = ((size_t)l * nkv + kh) * (size_t)S * hd;
+                        attn_pair_q8(hd, kv_len, scale, e->k_q8 + ho, e->k_sc + ho / 32, e->v_q8 + ho,
+                                     e->v_sc + ho / 32, q0, pair ? q0 + hd : NULL, e->sc0, e->sc1, a0,
+                                     pair ? a0 + hd : NULL);
+                    } else {
+                        attn_pair(hd, kv_len, scale, kc, vc, q0, pair ? q0 + hd : NULL, e->sc0, e->sc1, a0,
+                                  pair ? a0 + hd : NULL);
+                    }
                 }
             }
         }

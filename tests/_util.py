@@ -68,6 +68,7 @@ def run_scenario(engine_factory, scenario):
 
     with EnvScope(scenario.env):
         m = mdl.SyntheticModel(mdl.SHAPES[scenario.shape], seed=scenario.seed, norm_jitter=scenario.norm_jitter)
+        m.cfg.kv_type = scenario.kv_type
         eng = engine_factory(m)
         try:
             prompt = mdl.prompt_ids(scenario.prompt_len, m.shape.vocab, scenario.seed)

@@ -76,6 +76,7 @@ def main() -> None:
         os.environ.update(dict(s.env))
         try:
             m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter)
+            m.cfg.kv_type = s.kv_type
             ref = orc.RefEngine(m, n_threads=8)
             prompt = mdl.prompt_ids(s.prompt_len, m.shape.vocab, s.seed)
             rec = {"prompt": prompt.tolist()}

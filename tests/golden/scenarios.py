@@ -24,6 +24,7 @@ class EngineScenario:
     seed: int = 0
     all_logits: bool = False  # also record the prefill with only_last_logits = 0
     full_logits: bool = False  # store the full logit vectors (small vocab only)
+    kv_type: int = 0  # DpufModelConfig.kv_type: 0 fp32 cache, 1 int8 cache with per-32 scales
 
 
 ENGINE_SCENARIOS = [
@@ -35,6 +36,12 @@ ENGINE_SCENARIOS = [
                    env=(("DPUF_EARLY_TILES", "300"), ("DPUF_EARLY_MARGIN", "0.05")), norm_jitter=0.1),
     EngineScenario("tiny_long", "tiny", 200, 60, seed=3),
     EngineScenario("qwen3_0_6b_pp32_tg32", "qwen3-0.6b", 32, 32),
+    # Q8 KV cache (kv_type 1): pairs, a pair plus a lone head, lone heads only; odd and even
+    # key counts (the pair path's odd last key)
+    EngineScenario("tiny_q8", "tiny", 20, 12, norm_jitter=0.1, all_logits=True, full_logits=True, kv_type=1),
+    EngineScenario("tiny_g3_q8", "tiny-g3", 33, 9, norm_jitter=0.1, seed=4, full_logits=True, kv_type=1),
+    EngineScenario("tiny_mha_q8", "tiny-mha", 17, 8, norm_jitter=0.1, seed=2, kv_type=1),
+    EngineScenario("qwen3_0_6b_q8", "qwen3-0.6b", 16, 8, kv_type=1),
 ]
 
 # Packer cases: (rows, cols, tensor name used for the column signs, generator seed).

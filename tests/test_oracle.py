@@ -56,8 +56,8 @@ def test_oracle_engine_matches_reference(scn):
 
 
 @pytest.mark.slow
-def test_oracle_qwen3_0_6b_matches_reference():
-    scn = [s for s in sc.ENGINE_SCENARIOS if s.shape == "qwen3-0.6b"][0]
+@pytest.mark.parametrize("scn", [s for s in sc.ENGINE_SCENARIOS if s.shape == "qwen3-0.6b"], ids=lambda s: s.name)
+def test_oracle_qwen3_0_6b_matches_reference(scn):
     g = golden_engine()[scn.name]
     rec, _, _ = run_scenario(orc.OracleEngine, scn)
     assert rec["ids"] == g["ids"]
@@ -79,3 +79,28 @@ def test_zone_a_restatement():
     assert not orc.zone_a(lg, 2, 1.0)[0]
     lg[7] = 0.0
     assert not orc.zone_a(lg, 2, 0.0)[0]
+
+
+def test_q8_quantizer_restatement():
+    """quantize_vec_q8_blk32 (dpuf_engine.c:751-781): scale = amax / 127, round half to even,
+    a zero block gives scale 0 and zeros, an infinite element gives an infinite scale, zeros
+    for its finite neighbours (x * 0) and -127 for itself (inf * 0 = NaN, which the x86
+    conversion turns into INT32_MIN), and values saturate at +-127."""
+    import ctypes
+
+    lib = orc.OracleEngine.lib_()
+    lib.orc_quantize_q8_blk32.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    x = np.zeros(128, np.float32)
+    x[32:64] = np.linspace(-1.0, 1.0, 32, dtype=np.float32)
+    x[64:96] = 0.0
+    x[64] = 127.0
+    x[65:70] = [0.5, 1.5, 2.5, -0.5, -2.5]  # ties to even at inv = 1
+    x[96:128] = 1.0
+    x[100] = np.inf
+    q = np.empty(128, np.int8)
+    s = np.empty(4, np.float32)
+    lib.orc_quantize_q8_blk32(128, x.ctypes.data, q.ctypes.data, s.ctypes.data)
+    assert s[0] == 0.0 and np.all(q[:32] == 0)
+    assert s[1] == np.float32(1.0) / np.float32(127.0) and q[32] == -127 and q[63] == 127
+    assert s[2] == np.float32(1.0) and list(q[64:70]) == [127, 0, 2, 2, 0, -2]
+    assert np.isinf(s[3]) and q[100] == -127 and np.all(np.delete(q[96:128], 4) == 0)
