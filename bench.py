@@ -277,6 +277,7 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
     kv = args.serve_kv
     os.environ["DPUF_CUDA_KV_F16"] = "1" if kv == "f16" else "0"
     m = mdl.SyntheticModel(shape, seed=0)
+    m.cfg.kv_type = 1 if kv == "q8" else 0  # the reference's Q8 cache (kv_type 1)
     eng = engine.CudaTransformerEngine(m)
     toks, pos = [], []
     t0 = time.perf_counter()
@@ -307,14 +308,15 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
     wbytes = shape.weight_bytes_per_token()
     kvd = shape.kv_dim
     ctx_mean = ctx0 + (steps + 1) / 2.0
-    kv_bytes = n_seq * shape.layers * 2 * ctx_mean * kvd * (2 if kv == "f16" else 4)
+    kv_bytes = n_seq * shape.layers * 2 * ctx_mean * kvd * {"f16": 2, "f32": 4, "q8": 1.125}[kv]
     step_s = dt / steps
     value = n_seq * steps / dt
     print(json.dumps({
         "metric": "batched_decode_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": 1,
         "steps": steps, "warmup": warm, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
         "config": {"workload": f"{shape.name}-shape batched serving: {n_seq} sequences x {plen}-token prompts, "
-                               f"{steps} greedy steps at batch {n_seq}", "kv": "fp16" if kv == "f16" else "fp32",
+                               f"{steps} greedy steps at batch {n_seq}",
+                   "kv": {"f16": "fp16", "f32": "fp32", "q8": "q8 (kv_type 1)"}[kv],
                    "context": [ctx0, ctx0 + steps]},
         "step_roofline": {"bytes_per_step": int(wbytes + kv_bytes), "weights": wbytes, "kv": int(kv_bytes),
                           "achieved_gbs": round((wbytes + kv_bytes) / step_s / 1e9, 1),
@@ -576,8 +578,9 @@ def main():
     ap.add_argument("--serve-seqs", type=int, default=64)
     ap.add_argument("--serve-prompt", type=int, default=2048)
     ap.add_argument("--serve-steps", type=int, default=256)
-    ap.add_argument("--serve-kv", default="f16", choices=["f16", "f32"],
-                    help="KV cache of the serving run: fp16 (the configuration's) or fp32 (the reference's)")
+    ap.add_argument("--serve-kv", default="f16", choices=["f16", "f32", "q8"],
+                    help="KV cache of the serving run: fp16 (the configuration's), fp32 (the reference's "
+                         "kv_type 0) or q8 (the reference's kv_type 1)")
     ap.add_argument("--tp", action="store_true",
                     help="with --gpus N > 1: tensor parallelism over the N GPUs (one sequence) instead of data parallel")
     ap.add_argument("--no-extras", action="store_true",

@@ -118,7 +118,8 @@ struct Engine {
   float *cos_tab = nullptr, *sin_tab = nullptr;
 
   std::vector<Slot> slots;  // kMaxSlots, or env DPUF_CUDA_SLOTS for batched serving
-  int kv_es = 4;            // bytes per KV-cache element: 4 (fp32, the reference's), 2 (fp16, env DPUF_CUDA_KV_F16=1)
+  int kv_kind = kKvF32;     // KvKind: fp32 (kv_type 0), Q8 (kv_type 1), fp16 (env DPUF_CUDA_KV_F16=1, kv_type 0)
+  size_t kv_row = 0;        // bytes of one KV head's cache row at one position
   int n_slots = kMaxSlots;
   int active = 0;
   Prefix prefixes[kMaxPrefixes];
@@ -300,7 +301,7 @@ void rope_tables(const DpufModelConfig& c, std::vector<float>& cs, std::vector<f
 
 cudaError_t slot_alloc(Engine* e, int s) {
   if (e->slots[s].k) return cudaSuccess;
-  const size_t n = (size_t)e->L * e->S * e->kvd * e->kv_es;  // bytes
+  const size_t n = (size_t)e->L * e->S * e->nkv * e->kv_row;  // bytes
   CK(cudaMalloc(&e->slots[s].k, n));
   CK(cudaMalloc(&e->slots[s].v, n));
   CK(cudaMemset(e->slots[s].k, 0, n));
@@ -388,12 +389,11 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
   const Slot& sl = e->slots[e->active];
   for (int l = 0; l < e->L; l++) {
     const LayerDev& lw = e->layers[l];
-    const size_t layer_off = (size_t)l * e->nkv * e->S * e->hd;  // elements
-    const int f16 = e->kv_es == 2 ? 1 : 0;
-    KvCache kv{(float*)((char*)sl.k + layer_off * e->kv_es), (float*)((char*)sl.v + layer_off * e->kv_es), e->S,
-               nullptr, nullptr, nullptr, 0, f16};
+    const size_t layer_off = (size_t)l * e->nkv * e->S * e->kv_row;  // bytes
+    KvCache kv{(float*)((char*)sl.k + layer_off), (float*)((char*)sl.v + layer_off), e->S, nullptr, nullptr, nullptr, 0,
+               e->kv_kind};
     if (P.batch)
-      kv = KvCache{nullptr, nullptr, e->S, e->d_bstage->pos, e->d_bstage->k, e->d_bstage->v, layer_off, f16};
+      kv = KvCache{nullptr, nullptr, e->S, e->d_bstage->pos, e->d_bstage->k, e->d_bstage->v, layer_off, e->kv_kind};
     // 1-2. [h += hn] RMSNorm + prep of q/k/v inputs
     {
       const W12* ws[3] = {&lw.q, &lw.k, &lw.v};
@@ -525,7 +525,8 @@ bool uniform_tiles(const DpufWeightDesc& w, long long* stride, long long* first)
 // per SM with a ring of at least four stages.
 void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* tok, const DpufWeightDesc* lm) {
   auto no = [&](const std::string& why) { e->dec_ok = false; e->dec_why = why; };
-  if (e->kv_es != 4) return no("fp16 KV cache (the persistent kernel keeps the reference's fp32 cache)");
+  if (e->kv_kind == kKvF16) return no("fp16 KV cache (the persistent kernel keeps the reference's fp32 cache)");
+  if (e->kv_kind == kKvQ8) return no("Q8 KV cache (kv_type 1 runs on the per-step kernels)");
   int coop = 0, sms = 0;
   if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device) != cudaSuccess || !coop)
     return no("device without cooperative launch");
@@ -782,7 +783,7 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   const DpufModelConfig& c = *cfg;
   if (c.hidden_size <= 0 || c.num_layers < 0 || c.num_q_heads <= 0 || c.num_kv_heads <= 0 ||
       c.num_q_heads % c.num_kv_heads != 0 || c.head_dim <= 0 || c.head_dim % 32 != 0 || c.head_dim > 256 ||
-      c.max_seq_len <= 0 || c.kv_type != DPUF_KV_F32 || c.hidden_size % 64 != 0 || c.intermediate_size % 64 != 0 ||
+      c.max_seq_len <= 0 || (c.kv_type != DPUF_KV_F32 && c.kv_type != DPUF_KV_Q8) || c.hidden_size % 64 != 0 || c.intermediate_size % 64 != 0 ||
       (c.num_q_heads * c.head_dim) % 64 != 0) {
     set_error("unsupported model configuration");
     return nullptr;
@@ -912,7 +913,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
     e->prep[i] = Act{e->prep_q8 + i * B * ld, e->prep_xs + i * B * (ld / 32), e->prep_xm + i * B * (ld / 32), ld};
   cudaMemset(e->d_flag, 0, 16);
   cudaMemset(e->d_counter, 0, 64);
-  e->kv_es = env_int("DPUF_CUDA_KV_F16", 0) ? 2 : 4;
+  e->kv_kind = c.kv_type == DPUF_KV_Q8 ? kKvQ8 : env_int("DPUF_CUDA_KV_F16", 0) ? kKvF16 : kKvF32;
+  e->kv_row = kv_row_bytes(e->kv_kind, e->hd);
   if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
   e->use_persistent = env_int("DPUF_CUDA_PERSISTENT", 1) != 0;
   plan_decode(e, layers, tok, lm);
@@ -998,7 +1000,7 @@ DPUF_EXPORT void dpuf_engine_reset_slot(void* handle, int32_t slot_id) {
   Engine* e = (Engine*)handle;
   if (!e || slot_id < 0 || slot_id >= e->n_slots || !e->slots[slot_id].k) return;
   cudaSetDevice(e->device);
-  const size_t n = (size_t)e->L * e->S * e->kvd * e->kv_es;
+  const size_t n = (size_t)e->L * e->S * e->nkv * e->kv_row;
   cudaMemsetAsync(e->slots[slot_id].k, 0, n, e->stream);
   cudaMemsetAsync(e->slots[slot_id].v, 0, n, e->stream);
   cudaStreamSynchronize(e->stream);
@@ -1011,7 +1013,7 @@ DPUF_EXPORT void dpuf_engine_reset_cache(void* handle) {
 
 DPUF_EXPORT size_t dpuf_engine_slot_memory(void* handle) {
   Engine* e = (Engine*)handle;
-  return e ? 2 * (size_t)e->L * e->S * e->kvd * e->kv_es : 0;
+  return e ? 2 * (size_t)e->L * e->S * e->nkv * e->kv_row : 0;
 }
 
 // Freeze / apply copy [L][n_kv][len][hd] between the active slot and a prefix store with one
@@ -1021,20 +1023,20 @@ DPUF_EXPORT int32_t dpuf_engine_freeze_prefix(void* handle, int32_t pfx_id, int3
   if (!e || pfx_id < 0 || pfx_id >= dpuf::kMaxPrefixes || prefix_len <= 0 || prefix_len > e->S) return 0;
   cudaSetDevice(e->device);
   dpuf::Prefix& p = e->prefixes[pfx_id];
-  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd;
+  const size_t rows = (size_t)e->L * e->nkv;
   if (p.cap < prefix_len || !p.k) {
     cudaFree(p.k);
     cudaFree(p.v);
     p = dpuf::Prefix();
-    if (cudaMalloc(&p.k, rows * prefix_len * hd * e->kv_es) != cudaSuccess) { p.k = nullptr; return 0; }
-    if (cudaMalloc(&p.v, rows * prefix_len * hd * e->kv_es) != cudaSuccess) { cudaFree(p.k); p.k = nullptr; p.v = nullptr; return 0; }
+    if (cudaMalloc(&p.k, rows * prefix_len * e->kv_row) != cudaSuccess) { p.k = nullptr; return 0; }
+    if (cudaMalloc(&p.v, rows * prefix_len * e->kv_row) != cudaSuccess) { cudaFree(p.k); p.k = nullptr; p.v = nullptr; return 0; }
     p.cap = prefix_len;
   }
   const dpuf::Slot& s = e->slots[e->active];
   if (!s.k) return 0;
-  const size_t w = (size_t)prefix_len * hd * e->kv_es;
-  if (cudaMemcpy2DAsync(p.k, w, s.k, (size_t)e->S * hd * e->kv_es, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
-      cudaMemcpy2DAsync(p.v, w, s.v, (size_t)e->S * hd * e->kv_es, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+  const size_t w = (size_t)prefix_len * e->kv_row;
+  if (cudaMemcpy2DAsync(p.k, w, s.k, (size_t)e->S * e->kv_row, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(p.v, w, s.v, (size_t)e->S * e->kv_row, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
       cudaStreamSynchronize(e->stream))
     return 0;
   p.len = prefix_len;
@@ -1050,9 +1052,9 @@ DPUF_EXPORT int32_t dpuf_engine_apply_prefix(void* handle, int32_t slot_id, int3
   cudaSetDevice(e->device);
   if (dpuf::slot_alloc(e, slot_id) != cudaSuccess) return 0;
   const dpuf::Slot& s = e->slots[slot_id];
-  const size_t rows = (size_t)e->L * e->nkv, hd = e->hd, w = (size_t)p.len * hd * e->kv_es;
-  if (cudaMemcpy2DAsync(s.k, (size_t)e->S * hd * e->kv_es, p.k, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
-      cudaMemcpy2DAsync(s.v, (size_t)e->S * hd * e->kv_es, p.v, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+  const size_t rows = (size_t)e->L * e->nkv, w = (size_t)p.len * e->kv_row;
+  if (cudaMemcpy2DAsync(s.k, (size_t)e->S * e->kv_row, p.k, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
+      cudaMemcpy2DAsync(s.v, (size_t)e->S * e->kv_row, p.v, w, w, rows, cudaMemcpyDeviceToDevice, e->stream) ||
       cudaStreamSynchronize(e->stream))
     return 0;
   return p.len;

@@ -68,23 +68,34 @@ struct PrepTarget {
 cudaError_t launch_norm_prep(const Launch& L, float* h, const float* res, const float* w, float eps, int M, int H,
                              const PrepTarget* targets, int n_targets, float* norm_out);
 // Per (token, head): QK RMSNorm + NeoX RoPE; K/V of the new tokens stored to the cache.
+// KV-cache kinds.  A cache holds, per layer and KV head, max_seq rows, one per position:
+//   kKvF32  hd fp32 values (the reference's kv_type 0);
+//   kKvF16  hd fp16 values (env DPUF_CUDA_KV_F16, not a reference format);
+//   kKvQ8   the reference's kv_type 1 (quantize_vec_q8_blk32, dpuf_engine.c:751-781): hd int8
+//           values followed by hd/32 fp32 block scales in the same row, so that one
+//           contiguous read fetches a key or value with its scales.
+enum KvKind { kKvF32 = 0, kKvF16 = 1, kKvQ8 = 2 };
+DPUF_HD size_t kv_row_bytes(int kind, int hd) {
+  return kind == kKvF32 ? (size_t)hd * 4 : kind == kKvF16 ? (size_t)hd * 2 : (size_t)hd + hd / 8;
+}
 struct KvCache {
-  float* k;  // [n_kv][max_seq][hd] for this layer
+  float* k;  // rows [n_kv][max_seq] of this layer (raw storage of the cache's kind)
   float* v;
   int max_seq;
   // Batched decode (rows are independent sequences): token m's position tok_pos[m] and its
-  // slot's cache tok_k[m] / tok_v[m] ([L][n_kv][max_seq][hd]) + layer_off floats; null: the
+  // slot's cache tok_k[m] / tok_v[m] ([L][n_kv][max_seq] rows) + layer_off bytes; null: the
   // single cache above at positions *pos0 + m.
   const int32_t* tok_pos;
   float* const* tok_k;
   float* const* tok_v;
-  size_t layer_off;  // elements
-  int f16;           // 1: the caches hold fp16 elements (the pointers are then raw storage)
+  size_t layer_off;  // bytes
+  int kind;          // KvKind
 };
 cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
                            const float* q_norm, const float* k_norm, float eps, const float* cos_tab,
                            const float* sin_tab, const int* pos0_dev, KvCache kv);
-// Exact causal attention (gqa_attn_head_pair_f32 order) for M tokens, output [M][n_q*hd].
+// Exact causal attention for M tokens, output [M][n_q*hd]: gqa_attn_head_pair_f32's order
+// (fp32 and fp16 caches) or gqa_attn_head_pair_q8's (Q8 cache).
 cudaError_t launch_attention(const Launch& L, const float* q, int M, int n_q, int n_kv, int hd, const int* pos0_dev,
                              KvCache kv, float* out, const ExpfTable& et);
 // SwiGLU with dead-zone over [M][I] and prep of the result for w_down.  per_row: every row is

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(1024) norm_prep_kernel(float* __restrict__ h, 
 // head's norm gain (same lane/tree order as above), NeoX rotation with host cos/sin tables
 // (apply_rope_neox_f32, dpuf_engine.c:274-295: x1*c - x2*s and x2*c + x1*s as fused
 // multiply-subtract/add of the rounded cross product), then K and V rows are written to the
-// cache at position pos0 + m.  One warp per head vector.
+// cache at position pos0 + m: as fp32, fp16, or quantized Q8 rows.  One warp per head vector.
 __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_q,
                                int n_kv, int hd, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                float eps, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
@@ -91,9 +91,8 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   const int hidx = blockIdx.y * (blockDim.x >> 5) + warp;
   if (hidx >= n_q + n_kv) return;
   const int pos = kv.tok_pos ? kv.tok_pos[m] : *pos0_dev + m;
-  const int es = kv.f16 ? 2 : 4;  // bytes per cache element
-  char* const kbase = (char*)(kv.tok_k ? kv.tok_k[m] : kv.k) + (kv.tok_k ? kv.layer_off * es : 0);
-  char* const vbase = (char*)(kv.tok_v ? kv.tok_v[m] : kv.v) + (kv.tok_v ? kv.layer_off * es : 0);
+  char* const kbase = (char*)(kv.tok_k ? kv.tok_k[m] : kv.k) + (kv.tok_k ? kv.layer_off : 0);
+  char* const vbase = (char*)(kv.tok_v ? kv.tok_v[m] : kv.v) + (kv.tok_v ? kv.layer_off : 0);
   const bool is_k = hidx < n_kv;
   const int head = is_k ? hidx : hidx - n_kv;
   float* vec = is_k ? k + ((size_t)m * n_kv + head) * hd : q + ((size_t)m * n_q + head) * hd;
@@ -102,24 +101,23 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   for (int i = lane; i < hd; i += 32) s[i] = vec[i];
   __syncwarp();
   qk_norm_rope_warp(s, nw, eps, hd, cos_tab + (size_t)pos * (hd >> 1), sin_tab + (size_t)pos * (hd >> 1), lane);
-  for (int i = lane; i < hd; i += 32) {
-    vec[i] = s[i];
-    if (is_k) {
-      const size_t e = ((size_t)head * kv.max_seq + pos) * hd + i;
-      if (kv.f16)
-        ((__half*)kbase)[e] = __float2half_rn(s[i]);
-      else
-        ((float*)kbase)[e] = s[i];
-    }
+  for (int i = lane; i < hd; i += 32) vec[i] = s[i];
+  if (!is_k) return;
+  // this head's cache row at pos (kv_row_bytes per row)
+  const size_t row = ((size_t)head * kv.max_seq + pos) * kv_row_bytes(kv.kind, hd);
+  const float* vr = v + ((size_t)m * n_kv + head) * hd;
+  if (kv.kind == kKvQ8) {  // quantize_vec_q8_blk32 of K and V (dpuf_engine.c:1801-1802)
+    q8_row_warp(s, kbase + row, hd, lane);
+    q8_row_warp(vr, vbase + row, hd, lane);
+    return;
   }
-  if (is_k) {
-    const float* vr = v + ((size_t)m * n_kv + head) * hd;
-    const size_t e0 = ((size_t)head * kv.max_seq + pos) * hd;
-    for (int i = lane; i < hd; i += 32) {
-      if (kv.f16)
-        ((__half*)vbase)[e0 + i] = __float2half_rn(vr[i]);
-      else
-        ((float*)vbase)[e0 + i] = vr[i];
+  for (int i = lane; i < hd; i += 32) {
+    if (kv.kind == kKvF16) {
+      ((__half*)(kbase + row))[i] = __float2half_rn(s[i]);
+      ((__half*)(vbase + row))[i] = __float2half_rn(vr[i]);
+    } else {
+      ((float*)(kbase + row))[i] = s[i];
+      ((float*)(vbase + row))[i] = vr[i];
     }
   }
 }

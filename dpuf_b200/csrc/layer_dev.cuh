@@ -304,9 +304,12 @@ DPUF_DEV float kv_to_f(float x) { return x; }
 DPUF_DEV float kv_to_f(__half x) { return __half2float(x); }
 DPUF_DEV void kv_from_f(float& d, float x) { d = x; }
 DPUF_DEV void kv_from_f(__half& d, float x) { d = __float2half_rn(x); }
-// A tile's size in floats of scratch for elements of es bytes (4 or 2).
+// A tile's size in floats of scratch for elements of es bytes: 4 (fp32), 2 (fp16), or 1 for
+// Q8 rows (hd int8 values + hd/32 fp32 scales, unpadded).
 DPUF_HD size_t attn_tile_floats(int hd, int es = 4) {
-  return es == 4 ? (size_t)kAttnKeyTile * (hd + 8) : (size_t)kAttnKeyTile * (hd + 16) / 2;
+  return es == 4   ? (size_t)kAttnKeyTile * (hd + 8)
+         : es == 2 ? (size_t)kAttnKeyTile * (hd + 16) / 2
+                   : (size_t)kAttnKeyTile * (hd + hd / 8) / 4;
 }
 // Scores of two heads over max_seq keys (the persistent kernel's pair).
 DPUF_HD size_t attn_sc_floats(int max_seq) { return 2 * (((size_t)max_seq + 3) & ~(size_t)3); }
@@ -383,16 +386,73 @@ DPUF_DEV void attn_land_tile(T* buf, int t, int n_t, int n_buf, const float* cur
   sync();
 }
 
+// vec_softmax_avx2 (dpuf_engine.c:579-601) of the nh score rows sc[h][0, kv_len) in place;
+// lmax holds each thread's running maximum per head.  The scores must be complete (the
+// caller's last sync() came after them); no sync() follows the final normalisation.
+template <typename Sync>
+DPUF_DEV void attn_softmax(float* sc, int sc_stride, int nh, int kv_len, const float (&lmax)[kAttnMaxHeads],
+                           AttnShared* sh, const ExpfTable& et, int tid, Sync sync) {
+  const int lane = tid & 31, kv8 = kv_len & ~7;
+  // ---- max
+#pragma unroll
+  for (int h = 0; h < kAttnMaxHeads; h++) {
+    if (h >= nh) break;
+    float v = warp_max(lmax[h]);
+    if (lane == 0) sh->red[h][tid >> 5] = v;
+  }
+  sync();
+  if (tid < nh) {
+    float v = -1e30f;
+    for (int w = 0; w < kAttnThreads / 32; w++) v = max_ps(v, sh->red[tid][w]);
+    sh->max_s[tid] = v;
+  }
+  sync();
+  // ---- exp over the 8-aligned part
+  for (int h = 0; h < nh; h++) {
+    const float mx = sh->max_s[h];
+    for (int k = tid; k < kv8; k += kAttnThreads)
+      sc[h * sc_stride + k] = exp_poly(__fsub_rn(sc[h * sc_stride + k], mx));
+  }
+  sync();
+  // ---- lane sums (8 sequential chains per head); the <= 7 tail exponentials (glibc expf) are
+  // independent, so eight more threads per head evaluate them meanwhile
+  if (tid < 8 * nh) {
+    const int h = tid >> 3, l = tid & 7;
+    const float* sp = sc + h * sc_stride;
+    float acc = 0.0f;
+    for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, sp[k]);
+    sh->lane_sum[h][l] = acc;
+  } else if (tid >= 64 && tid < 64 + 8 * nh) {
+    const int h = (tid - 64) >> 3, k = kv8 + ((tid - 64) & 7);
+    if (k < kv_len) {
+      float* sp = sc + h * sc_stride;
+      sp[k] = glibc_expf(__fsub_rn(sp[k], sh->max_s[h]), et);
+    }
+  }
+  sync();
+  // split tree of the lane sums, then the tail added in order
+  if (tid < nh) {
+    const float* sp = sc + tid * sc_stride;
+    float su = tree8_split_arr(sh->lane_sum[tid]);
+    for (int k = kv8; k < kv_len; k++) su = __fadd_rn(su, sp[k]);
+    sh->inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(su, 1e-12f));
+  }
+  sync();
+  for (int h = 0; h < nh; h++) {
+    const float inv = sh->inv_s[h];
+    for (int k = tid; k < kv_len; k += kAttnThreads) sc[h * sc_stride + k] = __fmul_rn(sc[h * sc_stride + k], inv);
+  }
+}
+
 template <typename T, typename Sync>
 DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_len, const T* kc, const T* vc,
                              int sc_stride, float* sc, T* kt, int n_buf, int pre, const float* cur_k,
                              const float* cur_v, AttnShared* sh, float* out, const ExpfTable& et, int tid, Sync sync,
                              bool out_to_qs = false) {
-  const int lane = tid & 31;
   const int kvs = hd + attn_row_pad<T>();  // padded smem row of a staged key
   const size_t tile = (size_t)kAttnKeyTile * kvs;  // elements
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
+  const int kv4 = kv_len & ~3;
   const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
   const int n_rows = cur_k ? kv_len - 1 : kv_len;  // rows read from the cache
   float lmax[kAttnMaxHeads] = {-1e30f, -1e30f, -1e30f, -1e30f};
@@ -443,55 +503,7 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
   }
   // the first value tiles load while the softmax runs
   for (int t = 0; t < min(n_buf, n_t); t++) attn_issue_tile(kt + (size_t)t * tile, vc, t, n_rows, hd, tid);
-  // ---- max
-#pragma unroll
-  for (int h = 0; h < kAttnMaxHeads; h++) {
-    if (h >= nh) break;
-    float v = warp_max(lmax[h]);
-    if (lane == 0) sh->red[h][tid >> 5] = v;
-  }
-  sync();
-  if (tid < nh) {
-    float v = -1e30f;
-    for (int w = 0; w < kAttnThreads / 32; w++) v = max_ps(v, sh->red[tid][w]);
-    sh->max_s[tid] = v;
-  }
-  sync();
-  // ---- exp over the 8-aligned part
-  for (int h = 0; h < nh; h++) {
-    const float mx = sh->max_s[h];
-    for (int k = tid; k < kv8; k += kAttnThreads)
-      sc[h * sc_stride + k] = exp_poly(__fsub_rn(sc[h * sc_stride + k], mx));
-  }
-  sync();
-  // ---- lane sums (8 sequential chains per head); the <= 7 tail exponentials (glibc expf) are
-  // independent, so eight more threads per head evaluate them meanwhile
-  if (tid < 8 * nh) {
-    const int h = tid >> 3, l = tid & 7;
-    const float* sp = sc + h * sc_stride;
-    float acc = 0.0f;
-    for (int k = l; k < kv8; k += 8) acc = __fadd_rn(acc, sp[k]);
-    sh->lane_sum[h][l] = acc;
-  } else if (tid >= 64 && tid < 64 + 8 * nh) {
-    const int h = (tid - 64) >> 3, k = kv8 + ((tid - 64) & 7);
-    if (k < kv_len) {
-      float* sp = sc + h * sc_stride;
-      sp[k] = glibc_expf(__fsub_rn(sp[k], sh->max_s[h]), et);
-    }
-  }
-  sync();
-  // split tree of the lane sums, then the tail added in order
-  if (tid < nh) {
-    const float* sp = sc + tid * sc_stride;
-    float su = tree8_split_arr(sh->lane_sum[tid]);
-    for (int k = kv8; k < kv_len; k++) su = __fadd_rn(su, sp[k]);
-    sh->inv_s[tid] = __fdiv_rn(1.0f, __fadd_rn(su, 1e-12f));
-  }
-  sync();
-  for (int h = 0; h < nh; h++) {
-    const float inv = sh->inv_s[h];
-    for (int k = tid; k < kv_len; k += kAttnThreads) sc[h * sc_stride + k] = __fmul_rn(sc[h * sc_stride + k], inv);
-  }
+  attn_softmax(sc, sc_stride, nh, kv_len, lmax, sh, et, tid, sync);
   // ---- PV: thread o owns outputs o and o + kAttnThreads, each a sequential chain over the
   // keys in the reference's order
   float acc[2] = {0.0f, 0.0f};
@@ -538,6 +550,155 @@ DPUF_DEV void attn_pair_body(float* qs, int nh, bool last_lone, int hd, int kv_l
       out[o] = acc[j];
       if (out_to_qs) qs[o] = acc[j];
     }
+  }
+}
+
+// ------------------------------------------------------------------ Q8 KV cache (kv_type 1)
+// _mm256_cvtps_epi32 (round to nearest even), the saturating packs and max(-127) of
+// quantize_vec_q8_blk32: a NaN or out-of-range product converts to INT32_MIN, i.e. -127.
+DPUF_DEV int q8_cvt(float y) {
+  if (!(y == y) || y >= 2147483648.0f || y < -2147483648.0f) return -127;
+  return max(-127, min(127, __float2int_rn(y)));
+}
+
+// One warp quantizes the hd values x (lane-strided: element i is read by lane i % 32) into a
+// Q8 cache row: hd int8 values, then hd/32 fp32 scales (quantize_vec_q8_blk32,
+// dpuf_engine.c:751-781).  Per 32-block: amax by the reference's max tree (lanes j, j+8 and
+// j+16, j+24 first, then the 4-wide and 2-wide folds), scale = amax / 127,
+// q = cvt(x * (127 / amax)), or 0 when amax <= 1e-12.  hd % 32 == 0.
+DPUF_DEV void q8_row_warp(const float* x, char* row, int hd, int lane) {
+  float* scales = (float*)(row + hd);
+  for (int c0 = 0; c0 < hd; c0 += 32) {
+    const float v = x[c0 + lane];
+    float m = fabsf(v);
+    m = max_ps(m, __shfl_down_sync(kFull, m, 8));   // lanes 0-7, 16-23: max(|x_l|, |x_l+8|)
+    m = max_ps(m, __shfl_down_sync(kFull, m, 16));  // lanes 0-7: the 8-lane vector
+    m = max_ps(m, __shfl_down_sync(kFull, m, 4));   // lanes 0-3: 128-bit halves folded
+    m = max_ps(m, __shfl_down_sync(kFull, m, 2));   // movehl fold
+    m = max_ps(m, __shfl_down_sync(kFull, m, 1));   // max_ss
+    const float amax = __shfl_sync(kFull, m, 0);
+    const float inv = (amax > 1e-12f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    row[c0 + lane] = (char)q8_cvt(__fmul_rn(v, inv));
+    if (lane == 0) scales[c0 >> 5] = __fdiv_rn(amax, 127.0f);
+  }
+}
+
+// Issues (and commits, as one group of this thread) the copy of Q8 tile `t` - rows
+// [32t, min(32t + 32, n_rows)) of rb bytes, contiguous in the cache - into buf (unpadded).
+// Rows of a multiple of 16 bytes go by async copies through L2; other row sizes (hd = 32 or
+// 64) by plain L2 loads, complete when this returns.
+DPUF_DEV void attn_q8_issue(char* buf, const char* src, int t, int n_rows, int rb, int tid) {
+  const int t0 = t * kAttnKeyTile;
+  const int nbytes = max(0, min(kAttnKeyTile, n_rows - t0)) * rb;
+  const char* s = src + (size_t)t0 * rb;
+  if ((rb & 15) == 0) {
+    for (int i = tid * 16; i < nbytes; i += kAttnThreads * 16) cp_async16_cg(buf + i, s + i);
+  } else {
+    for (int i = tid * 4; i < nbytes; i += kAttnThreads * 4) *(int*)(buf + i) = __ldcg((const int*)(s + i));
+  }
+  cp_async_commit();
+}
+
+// gqa_attn_head_pair_q8 (dpuf_engine.c:621-749) for nh <= 4 query heads of one KV head over
+// its Q8 rows kc / vc (n_buf tiles kt of kAttnKeyTile rows in flight), in the layout of
+// attn_pair_body.  Scores: pair heads take keys two at a time - per block and lane l,
+// t = fma(q[l], k[l], fma(q[l+8], k[l+8], t)) over the two 16-wide halves, then
+// fma(t, k_scale, acc), pairs tree; the odd last key and the lone head use
+// dot_f32_q8_blk32_avx2 (dpuf_engine.c:603-619): lane accumulators over (l, l+16) and
+// (l+8, l+24), fma(a0 + a1, k_scale, acc), split tree.  Softmax as attn_softmax.  PV for
+// output d of every head: fma(p_k * vs_k[d/32], v_kd, acc) over k ascending.
+template <typename Sync>
+DPUF_DEV void attn_q8_body(float* qs, int nh, bool last_lone, int hd, int kv_len, const char* kc, const char* vc,
+                           int sc_stride, float* sc, char* kt, int n_buf, AttnShared* sh, float* out,
+                           const ExpfTable& et, int tid, Sync sync) {
+  const int rb = hd + hd / 8, nb = hd >> 5;
+  const size_t tile = (size_t)kAttnKeyTile * rb;  // bytes
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const int kv2 = kv_len & ~1;
+  const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
+  float lmax[kAttnMaxHeads] = {-1e30f, -1e30f, -1e30f, -1e30f};
+  // ---- scores
+  for (int t = 0; t < min(n_buf, n_t); t++) attn_q8_issue(kt + (size_t)t * tile, kc, t, kv_len, rb, tid);
+  for (int t = 0; t < n_t; t++) {
+    const int t0 = t * kAttnKeyTile;
+    const int nk = min(kAttnKeyTile, kv_len - t0);
+    char* buf = kt + (size_t)(t % n_buf) * tile;
+    cp_async_wait_pending(min(n_buf - 1, n_t - 1 - t));
+    sync();
+    const int key = tid >> 3, l = tid & 7;
+    const int tk = t0 + key;
+    const bool valid = key < nk;
+    const int8_t* kp = (const int8_t*)(buf + key * rb);
+    const float* ks = (const float*)(buf + key * rb + hd);
+#pragma unroll
+    for (int h = 0; h < kAttnMaxHeads; h++) {
+      if (h >= nh) break;
+      const float* qv = qs + h * hd;
+      const bool tail = (last_lone && h == nh - 1) || tk >= kv2;
+      float acc = 0.0f;
+      if (valid) {
+        if (!tail) {
+          for (int b = 0; b < nb; b++) {
+            const int c0 = b << 5;
+            float u = __fmaf_rn(qv[c0 + 8 + l], (float)kp[c0 + 8 + l], 0.0f);
+            u = __fmaf_rn(qv[c0 + l], (float)kp[c0 + l], u);
+            u = __fmaf_rn(qv[c0 + 24 + l], (float)kp[c0 + 24 + l], u);
+            u = __fmaf_rn(qv[c0 + 16 + l], (float)kp[c0 + 16 + l], u);
+            acc = __fmaf_rn(u, ks[b], acc);
+          }
+        } else {
+          for (int b = 0; b < nb; b++) {
+            const int c0 = b << 5;
+            float a0 = __fmaf_rn(qv[c0 + l], (float)kp[c0 + l], 0.0f);
+            float a1 = __fmaf_rn(qv[c0 + 8 + l], (float)kp[c0 + 8 + l], 0.0f);
+            a0 = __fmaf_rn(qv[c0 + 16 + l], (float)kp[c0 + 16 + l], a0);
+            a1 = __fmaf_rn(qv[c0 + 24 + l], (float)kp[c0 + 24 + l], a1);
+            acc = __fmaf_rn(__fadd_rn(a0, a1), ks[b], acc);
+          }
+        }
+      }
+      // both trees run on all lanes (a warp's four keys may take different forms)
+      const float tp = tree8_pairs(acc), ts = tree8_split(acc);
+      const float sv = __fmul_rn(tail ? ts : tp, scale);
+      if (valid && l == 0) {
+        sc[h * sc_stride + tk] = sv;
+        lmax[h] = max_ps(lmax[h], sv);
+      }
+    }
+    sync();  // the buffer is free again
+    if (t + n_buf < n_t) attn_q8_issue(buf, kc, t + n_buf, kv_len, rb, tid);
+  }
+  // the first value tiles load while the softmax runs
+  for (int t = 0; t < min(n_buf, n_t); t++) attn_q8_issue(kt + (size_t)t * tile, vc, t, kv_len, rb, tid);
+  attn_softmax(sc, sc_stride, nh, kv_len, lmax, sh, et, tid, sync);
+  // ---- PV: thread o owns outputs o and o + kAttnThreads
+  float acc[2] = {0.0f, 0.0f};
+  for (int t = 0; t < n_t; t++) {
+    const int t0 = t * kAttnKeyTile;
+    const int nk = min(kAttnKeyTile, kv_len - t0);
+    char* buf = kt + (size_t)(t % n_buf) * tile;
+    cp_async_wait_pending(min(n_buf - 1, n_t - 1 - t));
+    sync();
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int o = tid + j * kAttnThreads;
+      if (o >= nh * hd) break;
+      const int h = o / hd, d = o % hd;
+      const float* pp = sc + h * sc_stride + t0;
+      const int8_t* vt = (const int8_t*)buf + d;
+      const char* vs = buf + hd + 4 * (d >> 5);
+      float a = acc[j];
+      for (int k = 0; k < nk; k++)
+        a = __fmaf_rn(__fmul_rn(pp[k], *(const float*)(vs + k * rb)), (float)vt[k * rb], a);
+      acc[j] = a;
+    }
+    sync();  // the buffer is free again
+    if (t + n_buf < n_t) attn_q8_issue(buf, vc, t + n_buf, kv_len, rb, tid);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int o = tid + j * kAttnThreads;
+    if (o < nh * hd) out[o] = acc[j];
   }
 }
 

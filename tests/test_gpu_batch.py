@@ -18,11 +18,14 @@ def eng_mod():
     return engine
 
 
-@pytest.mark.parametrize("shape,n_seq", [("TINY", 5), ("TINY_MHA", 3), ("QWEN3_0_6B", 4)])
-def test_decode_batch_matches_sequence_at_a_time(eng_mod, shape, n_seq):
+@pytest.mark.parametrize("shape,n_seq,kv_type", [("TINY", 5, 0), ("TINY_MHA", 3, 0), ("QWEN3_0_6B", 4, 0),
+                                                 ("TINY_G3", 3, 1), ("QWEN3_0_6B", 3, 1)])
+def test_decode_batch_matches_sequence_at_a_time(eng_mod, shape, n_seq, kv_type):
+    """kv_type 1: the Q8 cache (its batch-1 steps match the reference: the *_q8 engine goldens)."""
     from dpuf_b200 import model as mdl
 
     m = mdl.SyntheticModel(getattr(mdl, shape), seed=6, norm_jitter=0.1)
+    m.cfg.kv_type = kv_type
     slots = [2 * i + 1 for i in range(n_seq)]  # not 0..n-1, and beyond the reference's 8
     prompts = [mdl.prompt_ids(5 + 7 * i, m.shape.vocab, 40 + i) for i in range(n_seq)]
     steps = 5

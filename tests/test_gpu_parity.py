@@ -83,13 +83,15 @@ def test_greedy_api_matches_logits(eng_mod):
     e.close()
 
 
-def test_slots_and_prefixes_match_oracle(eng_mod):
+@pytest.mark.parametrize("kv_type", [0, 1])
+def test_slots_and_prefixes_match_oracle(eng_mod, kv_type):
     """Prefix freeze/apply and slot switching (dpuf_engine.c:1404-1600) give the same logits as
-    recomputing the prefix."""
+    recomputing the prefix, with the fp32 and the Q8 cache."""
     from dpuf_b200 import model as mdl
     from oracle import oracle as orc
 
     m = mdl.SyntheticModel(mdl.TINY, seed=2, norm_jitter=0.1)
+    m.cfg.kv_type = kv_type
     e = eng_mod.CudaTransformerEngine(m)
     o = orc.OracleEngine(m)
     prefix = mdl.prompt_ids(12, m.shape.vocab, 2)
@@ -233,3 +235,24 @@ def test_config2_ops_match_oracle(eng_mod, rows, cols, name, M):
     if "down" in name:
         x[np.abs(x) < 0.3] = 0.0
     assert bitexact(eng_mod.matmul(M, bv, x), orc.oracle_matmul(M, bv, x))
+
+
+def test_q8_cache_layout_and_fallback(eng_mod):
+    """kv_type 1 stores hd int8 values + hd/32 fp32 scales per row: a slot takes the bytes the
+    reference's dpuf_engine_slot_memory reports (dpuf_engine.c:1476-1488), and decode runs on
+    the per-step kernels (the persistent kernel keeps the fp32 cache)."""
+    from dpuf_b200 import model as mdl
+
+    m = mdl.SyntheticModel(mdl.QWEN3_0_6B, seed=1)
+    m.cfg.kv_type = 1
+    e = eng_mod.CudaTransformerEngine(m)
+    try:
+        s = m.shape
+        elems = s.layers * s.max_seq * s.n_kv * s.head_dim
+        assert e.slot_memory() == 2 * elems + 2 * (elems // 32) * 4
+        on, why = e.persistent_decode()
+        assert not on and "Q8" in why
+        ids, _ = e.decode_greedy(5, 0, 4)
+        assert len(ids) == 4
+    finally:
+        e.close()
