@@ -79,7 +79,7 @@ typedef struct {
     float rope_low_freq;
     float rope_high_freq;
     int32_t rope_orig_max_pos;
-    int32_t kv_type;
+    int32_t kv_type;            /* DPUF_KV_F32, or DPUF_KV_Q8: int8 rows with per-32 fp32 scales */
     int32_t has_mrope;
     int32_t mrope_section[3];
     int32_t mrope_interleaved;
