@@ -304,6 +304,12 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
             pos = [p + 1 for p in pos]
         dt = time.perf_counter() - t0
     eng.close()
+    if args.no_extras:
+        cpu = None
+    else:
+        from oracle import oracle as orc
+
+        cpu = serve_cpu_baseline(m, plen, n_seq, 4, min(32, orc.host_threads()))
     # algorithmic bytes per step: the weights once, plus every sequence's K and V rows
     wbytes = shape.weight_bytes_per_token()
     kvd = shape.kv_dim
@@ -326,7 +332,104 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
                 "d2h_bytes_per_step": n_seq * 4, "what": "dpuf_cuda_decode_batch per step, synchronous"},
         "prefill": {"tokens": n_seq * plen, "seconds": round(prefill_s, 1),
                     "tok_per_s": round(n_seq * plen / prefill_s, 1)},
+        "cpu_baseline": cpu,
         "clocks": clk.summary(),
+    }), flush=True)
+
+
+def serve_cpu_baseline(m, plen: int, n_seq: int, n_steps: int, threads: int):
+    """The reference engine serves sequences one at a time, so its throughput at any batch is its
+    batch-1 rate at that context: 2 sequences, each prefilled with a plen-token prompt (untimed)
+    and then n_steps greedy steps (timed), extrapolated linearly to the batch."""
+    from oracle import oracle as orc
+
+    if not orc.RefEngine.available():
+        return None
+    ref = orc.RefEngine(m, n_threads=threads)
+    steps_done, dt = 0, 0.0
+    for i in range(2):
+        pr = mdl_prompt(plen, m.shape.vocab, 1000 + i)
+        ref.reset()
+        lg = None
+        for c0 in range(0, plen, 256):
+            lg = ref.forward(pr[c0:c0 + 256], c0, 1)
+        nxt, pos = int(np.argmax(lg[0])), plen
+        t0 = time.perf_counter()
+        for _ in range(n_steps):
+            nxt = int(np.argmax(ref.forward(np.array([nxt], np.int32), pos, 1)[0]))
+            pos += 1
+        dt += time.perf_counter() - t0
+        steps_done += n_steps
+    ref.close()
+    kv = "q8 (kv_type 1)" if m.cfg.kv_type == 1 else "fp32 (kv_type 0)"
+    return {"value": round(steps_done / dt, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"2 sequences x ({plen}-token prompt untimed + {n_steps} timed greedy steps), one at a time "
+                      f"as the reference serves them, {kv} KV; extrapolated linearly to {n_seq} sequences "
+                      f"(same tok/s); reference AVX2/OpenMP engine, {orc.cpu_model_string()}"}
+
+
+def mdl_prompt(n: int, vocab: int, seed: int):
+    from dpuf_b200 import model as mdl
+
+    return mdl.prompt_ids(n, vocab, seed)
+
+
+TRACE_EVENTS = ["norm1", "qkv", "bar_qkv", "attn", "grid_bar", "prep_o", "o", "bar_o", "norm2", "gate_up",
+                "bar_gu", "prep_down", "down", "bar_down"]
+
+
+def run_trace(args):
+    """Phase trace of the persistent decode kernel (env DPUF_CUDA_TRACE_DECODE=1): per layer, the
+    critical-path time of each consumer phase - the increase of the latest CTA's end time over
+    the previous phase's, averaged over layers 1..L-2 of the last of 8 greedy steps - and the
+    mean per-CTA time in it.  Not a benchmark value: the trace stores a timestamp per phase."""
+    import ctypes
+
+    from dpuf_b200 import engine, model as mdl
+
+    os.environ["DPUF_CUDA_TRACE_DECODE"] = "1"
+    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    m = mdl.SyntheticModel(shape, seed=0)
+    e = engine.CudaTransformerEngine(m)
+    prompt = mdl.prompt_ids(32, shape.vocab, 1)
+    e.reset_cache()
+    tok = int(np.argmax(e.forward_batch(prompt, 0)[0]))
+    for _ in range(max(3, args.warmup)):
+        _, ms = e.decode_greedy(tok, len(prompt), 8)
+    lib = e.lib
+    n_ctas, per = ctypes.c_int32(), ctypes.c_int32()
+    lib.dpuf_cuda_decode_trace.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64]
+    lib.dpuf_cuda_decode_trace(e._handle, ctypes.byref(n_ctas), ctypes.byref(per), None, 0)
+    C, P = n_ctas.value, per.value
+    out = np.zeros(C * P, np.uint64)
+    if lib.dpuf_cuda_decode_trace(e._handle, ctypes.byref(n_ctas), ctypes.byref(per), out.ctypes.data, out.size):
+        raise RuntimeError("no decode trace (persistent kernel not used?)")
+    e.close()
+    L = shape.layers
+    t = out.reshape(C, P).astype(np.int64)
+    sb = 14 * L
+    tt = (t - t[:, sb].min()) / 1000.0
+    crit, mean = np.zeros(14), np.zeros(14)
+    for l in range(1, L - 1):
+        prev = tt[:, 14 * (l - 1) + 13]
+        for j in range(14):
+            cur = tt[:, 14 * l + j]
+            crit[j] += cur.max() - prev.max()
+            mean[j] += float(np.mean(cur - prev))
+            prev = cur
+    crit /= L - 2
+    mean /= L - 2
+    lm = L // 2
+    d_attn = tt[:, 14 * lm + 3] - tt[:, 14 * lm + 2]
+    n_attn = int(np.sum(d_attn > 2 * np.median(d_attn) + 1.0))
+    print(json.dumps({
+        "trace": "decode_kernel phases", "model": shape.name, "ctas": C, "step_us": round(float(tt[:, sb + 5].max()), 1),
+        "device_ms_per_step_untraced_run": round(ms / 8, 4),
+        "layer_us": round(float(crit.sum()), 2),
+        "critical_us": {k: round(float(v), 2) for k, v in zip(TRACE_EVENTS, crit)},
+        "mean_cta_us": {k: round(float(v), 2) for k, v in zip(TRACE_EVENTS, mean)},
+        "attention_ctas": n_attn, "attention_us_layer_mid": round(float(d_attn.max()), 2),
+        "lm_head_us": round(float(tt[:, sb + 3].max() - tt[:, sb + 2].max()), 1),
     }), flush=True)
 
 
@@ -583,12 +686,20 @@ def main():
                          "kv_type 0) or q8 (the reference's kv_type 1)")
     ap.add_argument("--tp", action="store_true",
                     help="with --gpus N > 1: tensor parallelism over the N GPUs (one sequence) instead of data parallel")
+    ap.add_argument("--trace", action="store_true",
+                    help="phase trace of the persistent decode kernel (per-layer critical path), not a benchmark")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args.gpus)
+    if args.trace:
+        import torch
+
+        torch.cuda.set_device(local)
+        run_trace(args)
+        return
     if args.gemv_only or args.op or args.zone or args.serve:
         import torch
 
