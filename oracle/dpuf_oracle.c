@@ -194,6 +194,71 @@ ORC_EXPORT void orc_matmul_mode12_f32(int32_t M, int32_t rows, int32_t cols, int
     free(q); free(xs); free(xm);
 }
 
+/* Modes 13 (QR_HAD4_ASYM) and 14 (QR_HAD6): dpuf_matmul_qr_had4_asym_f32 / _had6_f32
+ * (dpuf_avx2.c:3084-3144, had_asym_tile_range_impl :2947-3066).  Same activation prep as mode 12
+ * (dpuf_prep_had4_packed_slab).  A tile is a 16-byte header and, per 8-row group, n64 x
+ * [8 fp16 d | 8 fp16 m] (per 64-block), then per 32-block 128 bytes of nibbles ordered
+ * [chunk c][row r][e] (low nibble: weight of x[8c+e], high: x[8c+4+e]), then (mode 14) per
+ * 32-block 64 bytes of high bit pairs (byte c*16 + half*8 + (r%2)*4 + e, bits 2*(r/2)).  The
+ * block dots are exact integers (no int16 saturation or wrap at these ranges).  Per row and
+ * 64-block g, in order: fdot = fma(d0, xs0, d1 * xs1), acc = fma(fdot, d, acc),
+ * acc = fma(m, xm_s, acc) with xm_s = fma(xsum0, xs0, xsum1 * xs1) * 0.125: the reference's
+ * scalar "(xsum0 * xs0 + xsum1 * xs1) * 0.125f" as its build (gcc, gnu11, -mfma: contraction
+ * on by default) computes it - checked against the built reference, which the other two
+ * orders do not match. */
+ORC_EXPORT void orc_matmul_had_asym_f32(int32_t is_had6, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                        const float* x_in, const uint8_t* tensor_base,
+                                        const uint64_t* tile_offsets, const uint8_t* sign_bits, float* out) {
+    const int32_t n_blk = cols >> 5, n_64 = cols >> 6;
+    const size_t grp_bytes = is_had6 ? 416u : 288u;
+    int8_t* q = (int8_t*)malloc((size_t)cols);
+    float* xs = (float*)malloc((size_t)n_blk * sizeof(float));
+    int32_t* xm = (int32_t*)malloc((size_t)n_blk * sizeof(int32_t));
+    for (int32_t m = 0; m < M; m++) {
+        orc_prep_mode12(cols, x_in + (size_t)m * (size_t)cols, sign_bits, q, xs, xm);
+        for (int32_t t = 0; t < n_tiles; t++) {
+            const uint8_t* tp = tensor_base + tile_offsets[t];
+            const int32_t n_r = tp[4] | (tp[5] << 8);
+            for (int32_t rg = 0; rg * 8 < n_r; rg++) {
+                const uint8_t* grp = tp + 16 + (size_t)rg * (size_t)n_64 * grp_bytes;
+                const uint16_t* dm = (const uint16_t*)grp;
+                const uint8_t* q4 = grp + (size_t)n_64 * 32u;
+                const uint8_t* q2 = q4 + (size_t)n_64 * 256u;
+                for (int32_t r = 0; r < 8 && rg * 8 + r < n_r; r++) {
+                    float acc = 0.0f;
+                    for (int32_t g = 0; g < n_64; g++) {
+                        int32_t d[2];
+                        for (int k = 0; k < 2; k++) {
+                            const int32_t b = 2 * g + k;
+                            int32_t dot = 0;
+                            for (int c = 0; c < 4; c++)
+                                for (int e = 0; e < 4; e++) {
+                                    const uint8_t byte = q4[(size_t)b * 128u + c * 32 + r * 4 + e];
+                                    int32_t ulo = byte & 15, uhi = byte >> 4;
+                                    if (is_had6) {
+                                        const int sh = 2 * (r >> 1);
+                                        const uint8_t* hp = q2 + (size_t)b * 64u + c * 16 + (r & 1) * 4 + e;
+                                        ulo |= ((hp[0] >> sh) & 3) << 4;
+                                        uhi |= ((hp[8] >> sh) & 3) << 4;
+                                    }
+                                    dot += ulo * q[b * 32 + c * 8 + e] + uhi * q[b * 32 + c * 8 + 4 + e];
+                                }
+                            d[k] = dot;
+                        }
+                        const int32_t b0 = 2 * g, b1 = b0 + 1;
+                        const float fdot = fmaf((float)d[0], xs[b0], (float)d[1] * xs[b1]);
+                        const float xms = fmaf((float)xm[b0], xs[b0], (float)xm[b1] * xs[b1]) * 0.125f;
+                        acc = fmaf(fdot, f16_to_f32(dm[g * 16 + r]), acc);
+                        acc = fmaf(f16_to_f32(dm[g * 16 + 8 + r]), xms, acc);
+                    }
+                    out[(size_t)m * rows + (size_t)t * 16 + rg * 8 + r] = acc;
+                }
+            }
+        }
+    }
+    free(q); free(xs); free(xm);
+}
+
 /* Row lookup: nibbles -> (u-8)*ws -> FWHT-64 -> sign (dpuf_avx2.c:2738-2783). */
 ORC_EXPORT void orc_embed_mode12_f32(int32_t n_tokens, int32_t cols, const int32_t* ids,
                                      const uint8_t* tensor_base, const uint64_t* tile_offsets,

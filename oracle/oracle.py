@@ -179,6 +179,18 @@ def oracle_matmul(M, blob, x):
     return out
 
 
+def oracle_matmul_had(mode: int, M, blob, x):
+    """Mode 13 (QR_HAD4_ASYM) or 14 (QR_HAD6) matmul restated (dpuf_avx2.c:3084-3144)."""
+    lib = OracleEngine.lib_()
+    lib.orc_matmul_had_asym_f32.argtypes = [ctypes.c_int32] * 5 + [ctypes.c_void_p] * 5
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty((M, blob.rows), dtype=np.float32)
+    lib.orc_matmul_had_asym_f32(int(mode == 14), M, blob.rows, blob.cols, blob.n_tiles, x.ctypes.data,
+                                blob.tiles.ctypes.data, blob.tile_offsets.ctypes.data, blob.sign_bits.ctypes.data,
+                                out.ctypes.data)
+    return out
+
+
 def ref_matmul(M, blob, x):
     lib = RefEngine.lib_()
     x = np.ascontiguousarray(x, dtype=np.float32)

@@ -15,6 +15,7 @@ the reference packer by pack.json.
 """
 from __future__ import annotations
 
+import ctypes
 import json
 import os
 import pathlib
@@ -67,6 +68,26 @@ def main() -> None:
         arrays[f"embed_{ci}_ids"] = ids
         arrays[f"embed_{ci}"] = out
     np.savez_compressed(HERE / "matmul.npz", **arrays)
+
+    # ---- modes 13 / 14 (blobs from the reference packer, outputs from the reference library)
+    had = {}
+    for ci, (rows, cols, mode, seed) in enumerate(sc.HAD_CASES):
+        w = packer.gen_normal_bf16(seed, 100 + ci, (rows, cols), 0.02)
+        enc = ref_format.encode_tensor_qr_had4_asym if mode == 13 else ref_format.encode_tensor_qr_had6
+        had[f"blob_{ci}"] = np.frombuffer(enc(w, tensor_name=f"had.{ci}"), np.uint8).copy()
+    fn = {13: lib.dpuf_matmul_qr_had4_asym_f32, 14: lib.dpuf_matmul_qr_had6_f32}
+    for f in fn.values():
+        f.argtypes = [ctypes.c_int32] * 4 + [ctypes.c_void_p] * 5
+    for ci, M, kind in sc.HAD_MATMUL:
+        rows, cols, mode, _ = sc.HAD_CASES[ci]
+        bv = packer.BlobView(had[f"blob_{ci}"])
+        assert bv.mode == mode
+        x = sc.matmul_input(50 + ci, M, kind, cols)
+        out = np.empty((M, rows), np.float32)
+        fn[mode](M, rows, cols, bv.n_tiles, x.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data,
+                 bv.sign_bits.ctypes.data, out.ctypes.data)
+        had[f"out_{ci}_{M}_{kind}"] = out
+    np.savez_compressed(HERE / "had_asym.npz", **had)
 
     # ---- engine scenarios
     eng_out = {}

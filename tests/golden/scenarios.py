@@ -64,6 +64,15 @@ MATMUL_CASES = [
 ]
 
 
+# Modes 13 (QR_HAD4_ASYM) and 14 (QR_HAD6) standalone matmul: (rows, cols, mode, seed).  The
+# blobs come from the reference packer (encode_tensor_qr_had4_asym / _had6) and are stored in
+# had_asym.npz with the reference library's outputs; rows that are not a multiple of 16 give a
+# ragged last tile (and a half-empty 8-row group).
+HAD_CASES = [(72, 256, 13, 1), (100, 512, 14, 2), (256, 512, 13, 3), (264, 512, 14, 4)]
+HAD_MATMUL = [(0, 1, "normal"), (0, 5, "normal"), (1, 1, "normal"), (1, 7, "normal"), (2, 1, "sparse"),
+              (2, 13, "normal"), (3, 1, "normal"), (3, 6, "sparse")]
+
+
 def matmul_input(case_idx: int, M: int, kind: str, cols: int) -> np.ndarray:
     rng = np.random.default_rng(1000 + 17 * case_idx + M)
     x = rng.standard_normal((M, cols)).astype(np.float32)

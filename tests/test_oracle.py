@@ -29,6 +29,20 @@ def test_oracle_embed_matches_reference(ci):
     assert bitexact(out, g[f"embed_{ci}"])
 
 
+@pytest.mark.parametrize("ci,M,kind", sc.HAD_MATMUL)
+def test_oracle_had_asym_matches_reference(ci, M, kind):
+    """Modes 13 / 14: the restatement reproduces the reference library's outputs on blobs made
+    by the reference packer (tests/golden/had_asym.npz)."""
+    from dpuf_b200 import packer
+
+    g = golden_arrays("had_asym.npz")
+    rows, cols, mode, _ = sc.HAD_CASES[ci]
+    bv = packer.BlobView(g[f"blob_{ci}"])
+    assert (bv.mode, bv.rows, bv.cols) == (mode, rows, cols)
+    x = sc.matmul_input(50 + ci, M, kind, cols)
+    assert bitexact(orc.oracle_matmul_had(mode, M, bv, x), g[f"out_{ci}_{M}_{kind}"])
+
+
 def test_swiglu_range_split_matches_reference_threads():
     lib = orc.OracleEngine.lib_()
     # I = 3072, M = 1 over 8 threads: every range is a multiple of 8 -> all vector
