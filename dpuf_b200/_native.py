@@ -37,6 +37,7 @@ CUDA_SOURCES = [
     "kernels_lmhead.cu",
     "kernels_decode.cu",
     "ops_abi.cu",
+    "ops_had_asym.cu",
     "noalloc.cu",
     "sampling.cu",
 ]

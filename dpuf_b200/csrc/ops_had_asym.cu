@@ -1,0 +1,265 @@
+// ops_had_asym.cu - standalone matmul of the reference's modes 13 (QR_HAD4_ASYM, 4-bit) and 14
+// (QR_HAD6, 6-bit) behind its exported signatures (dpuf_kernels.h:279-313,
+// dpuf_avx2.c:2785-3144): the mode-12 activation prep (launch_prep: sign flip, FWHT-64, int8
+// per 32 with block scale and block sum x 8), then had_asym_kernel.
+//
+// Tile layout (16-byte header, then per 8-row group): n64 x [8 fp16 d | 8 fp16 m] per 64-block,
+// then per 32-block 128 bytes of nibbles ordered [chunk c][row r][e] - the low nibble weighs
+// x[8c+e], the high nibble x[8c+4+e] - and, for mode 14, per 32-block 64 bytes of high bit pairs
+// (byte c*16 + half*8 + (r%2)*4 + e holds, at bits 2*(r/2), the pair of the low (half 0) or high
+// (half 1) nibble).  Weights are asymmetric: w = d * u + m with u unsigned.
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "dpuf_cuda.h"
+#include "dpuf_kernels.h"
+#include "engine_internal.h"
+#include "kernels.cuh"
+
+namespace dpuf {
+namespace {
+
+constexpr int kHadWarps = 8;     // 8-row groups per CTA
+constexpr int kHadChunk = 256;   // tokens per prep + matmul launch pair
+
+// One warp computes one 8-row group (rg) of tile t for token blockIdx.y; lane = 4 r + c: row r,
+// chunk c (8 of the 32 columns) of every 32-block.  The block dot d_b = sum u * q is exact
+// (dp4a over the lane's 4 + 4 weights, a two-step shuffle sum over the row's four lanes), as the
+// reference's maddubs/madd sums are (no saturation or wrap at these ranges).  Then, per row and
+// 64-block g in order (had_asym_tile_range_impl):
+//   fdot = fma(d_{2g}, xs_{2g}, d_{2g+1} * xs_{2g+1})
+//   acc  = fma(fdot, d_row, acc);  acc = fma(m_row, xm_s, acc)
+// with xm_s = fma(xsum_{2g}, xs_{2g}, xsum_{2g+1} * xs_{2g+1}) * 0.125: the reference's scalar
+// "(xsum0 * xs0 + xsum1 * xs1) * 0.125f", which its build (gcc, gnu11, -mfma) contracts.
+template <bool kHad6>
+__global__ void __launch_bounds__(kHadWarps * 32) had_asym_kernel(const uint8_t* __restrict__ tiles,
+                                                                  const uint64_t* __restrict__ toff, int rows,
+                                                                  int cols, int n_tiles, Act a,
+                                                                  float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kHadWarps + (threadIdx.x >> 5);
+  const int t = gw >> 1, rg = gw & 1;
+  if (t >= n_tiles) return;
+  const uint8_t* tp = tiles + toff[t];
+  const int n_r = tp[4] | (tp[5] << 8);
+  if (rg * 8 >= n_r) return;
+  const int m = blockIdx.y;
+  const int n_64 = cols >> 6;
+  const size_t grp_bytes = kHad6 ? 416 : 288;
+  const uint8_t* grp = tp + 16 + (size_t)rg * n_64 * grp_bytes;
+  const uint16_t* dm = (const uint16_t*)grp;
+  const uint8_t* q4 = grp + (size_t)n_64 * 32;
+  const uint8_t* q2 = q4 + (size_t)n_64 * 256;
+  const int r = lane >> 2, c = lane & 3, sh = 2 * (r >> 1);
+  const int8_t* xq = a.q8 + (size_t)m * a.ld;
+  const float* xs = a.xs + (size_t)m * (a.ld >> 5);
+  const int* xm = a.xm + (size_t)m * (a.ld >> 5);
+  float acc = 0.0f;
+#pragma unroll 2
+  for (int g = 0; g < n_64; g++) {
+    int d[2];
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const int b = 2 * g + k;
+      const uint32_t w = __ldg((const uint32_t*)(q4 + (size_t)b * 128 + c * 32 + r * 4));
+      uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+      if (kHad6) {
+        const uint8_t* hp = q2 + (size_t)b * 64 + c * 16 + (r & 1) * 4;
+        lo |= ((__ldg((const uint32_t*)hp) >> sh) & 0x03030303u) << 4;
+        hi |= ((__ldg((const uint32_t*)(hp + 8)) >> sh) & 0x03030303u) << 4;
+      }
+      const int* xw = (const int*)(xq + b * 32 + c * 8);
+      int p = __dp4a((int)lo, xw[0], 0);
+      p = __dp4a((int)hi, xw[1], p);
+      p += __shfl_xor_sync(kFull, p, 1);
+      p += __shfl_xor_sync(kFull, p, 2);
+      d[k] = p;
+    }
+    const int b0 = 2 * g, b1 = b0 + 1;
+    const float xs0 = xs[b0], xs1 = xs[b1];
+    const float fdot = __fmaf_rn(__int2float_rn(d[0]), xs0, __fmul_rn(__int2float_rn(d[1]), xs1));
+    const float xms = __fmul_rn(__fmaf_rn(__int2float_rn(xm[b0]), xs0, __fmul_rn(__int2float_rn(xm[b1]), xs1)), 0.125f);
+    acc = __fmaf_rn(fdot, f16bits_to_f32(__ldg(dm + g * 16 + r)), acc);
+    acc = __fmaf_rn(f16bits_to_f32(__ldg(dm + g * 16 + 8 + r)), xms, acc);
+  }
+  if (c == 0 && rg * 8 + r < n_r) out[(size_t)m * rows + t * 16 + rg * 8 + r] = acc;
+}
+
+// A mode-13/14 matrix in device memory: its tile span, tile offsets relative to it, signs.
+struct HadMat {
+  unsigned char* mem = nullptr;
+  const uint64_t* toff = nullptr;
+  const uint8_t* signs = nullptr;
+  int rows = 0, cols = 0, n_tiles = 0, had6 = 0;
+};
+
+bool had_fail(const char* where, cudaError_t e) {
+  set_error(std::string(where) + ": " + cudaGetErrorString(e));
+  return false;
+}
+
+// Checks the descriptor (every tile's rows inside [0, rows), 16-byte aligned offsets) and
+// uploads tiles [0, n_tiles); the span end comes from the last bytes each tile's groups use.
+bool had_upload(HadMat& h, int had6, int rows, int cols, int n_tiles, const uint8_t* base, const uint64_t* toff,
+                const uint8_t* signs) {
+  if (rows <= 0 || cols <= 0 || cols % 64 != 0 || n_tiles <= 0 || !base || !toff) {
+    set_error("bad mode-13/14 descriptor");
+    return false;
+  }
+  const uint64_t grp = (uint64_t)(cols / 64) * (had6 ? 416 : 288);
+  uint64_t lo = toff[0], hi = 0;
+  for (int t = 0; t < n_tiles; t++) {
+    const uint8_t* tp = base + toff[t];
+    const int n_r = tp[4] | (tp[5] << 8);
+    if (toff[t] % 16 != 0 || n_r < 1 || n_r > kTileRows || (int64_t)t * kTileRows + n_r > rows) {
+      set_error("mode-13/14 tile outside the matrix (row count or alignment)");
+      return false;
+    }
+    lo = std::min<uint64_t>(lo, toff[t]);
+    hi = std::max<uint64_t>(hi, toff[t] + 16 + (uint64_t)((n_r + 7) / 8) * grp);
+  }
+  const size_t span = (size_t)(hi - lo);
+  const size_t off_toff = (span + 255) & ~(size_t)255;
+  const size_t off_sign = (off_toff + (size_t)n_tiles * 8 + 255) & ~(size_t)255;
+  const size_t total = off_sign + (size_t)cols / 8;
+  cudaError_t e;
+  if ((e = cudaMalloc(&h.mem, total)) != cudaSuccess) return had_fail("cudaMalloc", e);
+  if ((e = cudaMemcpy(h.mem, base + lo, span, cudaMemcpyHostToDevice)) != cudaSuccess) return had_fail("upload", e);
+  std::string rel((size_t)n_tiles * 8, '\0');
+  uint64_t* rp = (uint64_t*)&rel[0];
+  for (int t = 0; t < n_tiles; t++) rp[t] = toff[t] - lo;
+  if ((e = cudaMemcpy(h.mem + off_toff, rp, (size_t)n_tiles * 8, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return had_fail("upload", e);
+  if (signs && (e = cudaMemcpy(h.mem + off_sign, signs, (size_t)cols / 8, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return had_fail("upload", e);
+  h.toff = (const uint64_t*)(h.mem + off_toff);
+  h.signs = signs ? h.mem + off_sign : nullptr;
+  h.rows = rows;
+  h.cols = cols;
+  h.n_tiles = n_tiles;
+  h.had6 = had6;
+  return true;
+}
+
+cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+  const dim3 grid((2 * h.n_tiles + kHadWarps - 1) / kHadWarps, M);
+  if (h.had6)
+    had_asym_kernel<true><<<grid, kHadWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+  else
+    had_asym_kernel<false><<<grid, kHadWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+  return cudaGetLastError();
+}
+
+// Activation buffers for kHadChunk tokens.
+struct HadAct {
+  Act a{};
+  bool alloc(int cols) {
+    cudaError_t e;
+    if ((e = cudaMalloc(&a.q8, (size_t)kHadChunk * cols)) != cudaSuccess) return had_fail("cudaMalloc", e);
+    if ((e = cudaMalloc(&a.xs, (size_t)kHadChunk * (cols / 32) * 4)) != cudaSuccess) return had_fail("cudaMalloc", e);
+    if ((e = cudaMalloc(&a.xm, (size_t)kHadChunk * (cols / 32) * 4)) != cudaSuccess) return had_fail("cudaMalloc", e);
+    a.ld = cols;
+    return true;
+  }
+  ~HadAct() {
+    cudaFree(a.q8);
+    cudaFree(a.xs);
+    cudaFree(a.xm);
+  }
+};
+
+// y = W x for M tokens (device pointers), kHadChunk tokens per prep + matmul pair.
+bool had_matmul_dev(const HadMat& h, HadAct& act, int M, const float* x, float* y, cudaStream_t s) {
+  const Launch L{s, false};
+  for (int m0 = 0; m0 < M; m0 += kHadChunk) {
+    const int mc = std::min(kHadChunk, M - m0);
+    cudaError_t e = launch_prep(L, x + (size_t)m0 * h.cols, h.cols, mc, h.cols, h.signs, act.a);
+    if (e != cudaSuccess) return had_fail("prep", e);
+    if ((e = launch_had(s, h, act.a, mc, y + (size_t)m0 * h.rows)) != cudaSuccess) return had_fail("matmul", e);
+  }
+  return true;
+}
+
+// Reference signature, host in / host out, synchronous.
+void had_matmul_host(int had6, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles, const float* x_in,
+                     const uint8_t* base, const uint64_t* toff, const uint8_t* signs, float* out) {
+  set_error("");
+  if (M <= 0 || !x_in || !out) return;
+  HadMat h;
+  HadAct act;
+  float *dx = nullptr, *dy = nullptr;
+  if (had_upload(h, had6, rows, cols, n_tiles, base, toff, signs) && act.alloc(cols) &&
+      cudaMalloc(&dx, (size_t)M * cols * 4) == cudaSuccess && cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
+      cudaMemcpy(dx, x_in, (size_t)M * cols * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+      had_matmul_dev(h, act, M, dx, dy, nullptr)) {
+    const cudaError_t e = cudaMemcpy(out, dy, (size_t)M * rows * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) set_error(cudaGetErrorString(e));
+  }
+  cudaFree(dx);
+  cudaFree(dy);
+  cudaFree(h.mem);
+}
+
+}  // namespace
+}  // namespace dpuf
+
+extern "C" {
+
+DPUF_EXPORT void dpuf_matmul_qr_had4_asym_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                              const float* x_in, const uint8_t* tensor_base,
+                                              const uint64_t* tile_offsets, const uint8_t* sign_bits, float* out) {
+  dpuf::had_matmul_host(0, M, rows, cols, n_tiles, x_in, tensor_base, tile_offsets, sign_bits, out);
+}
+
+DPUF_EXPORT void dpuf_matmul_qr_had6_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles, const float* x_in,
+                                         const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                                         const uint8_t* sign_bits, float* out) {
+  dpuf::had_matmul_host(1, M, rows, cols, n_tiles, x_in, tensor_base, tile_offsets, sign_bits, out);
+}
+
+DPUF_EXPORT int32_t dpuf_cuda_had_asym_timed(int32_t mode, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                             const float* x_in, const uint8_t* tensor_base,
+                                             const uint64_t* tile_offsets, const uint8_t* sign_bits,
+                                             int32_t n_copies, int32_t reps, float* ms_per_matmul) {
+  using namespace dpuf;
+  set_error("");
+  if ((mode != 13 && mode != 14) || M <= 0 || M > kHadChunk || !x_in || n_copies <= 0 || n_copies > 64 ||
+      reps <= 0 || !ms_per_matmul) {
+    set_error("bad arguments");
+    return -1;
+  }
+  std::vector<HadMat> hs((size_t)n_copies);
+  HadAct act;
+  float *dx = nullptr, *dy = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int32_t rc = -4;
+  bool ok = act.alloc(cols) && cudaMalloc(&dx, (size_t)M * cols * 4) == cudaSuccess &&
+            cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
+            cudaMemcpy(dx, x_in, (size_t)M * cols * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+            cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+  for (int i = 0; ok && i < n_copies; i++)
+    ok = had_upload(hs[i], mode == 14, rows, cols, n_tiles, tensor_base, tile_offsets, sign_bits);
+  if (ok) ok = launch_prep(Launch{nullptr, false}, dx, cols, M, cols, hs[0].signs, act.a) == cudaSuccess;
+  for (int i = 0; ok && i < n_copies; i++) ok = launch_had(nullptr, hs[i], act.a, M, dy) == cudaSuccess;  // warm-up
+  if (ok) {
+    cudaEventRecord(e0);
+    for (int k = 0; k < reps; k++) launch_had(nullptr, hs[k % n_copies], act.a, M, dy);
+    cudaEventRecord(e1);
+    float ms = 0.0f;
+    if (cudaEventSynchronize(e1) == cudaSuccess && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess &&
+        cudaGetLastError() == cudaSuccess) {
+      *ms_per_matmul = ms / reps;
+      rc = 0;
+    }
+  }
+  if (ok && rc != 0) set_error("CUDA error in the timed mode-13/14 matmul");
+  for (auto& h : hs) cudaFree(h.mem);
+  cudaFree(dx);
+  cudaFree(dy);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  return rc;
+}
+
+}  // extern "C"

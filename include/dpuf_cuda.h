@@ -143,6 +143,16 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t co
                                              const uint64_t* tile_offsets_dev, const uint8_t* sign_bits_dev,
                                              float* y_dev, void* stream);
 
+/* Measurement of the mode-13/14 matmul kernel (no reference counterpart): uploads n_copies
+ * copies of the matrix (so that a rotation over them exceeds the L2 cache), preps the M <= 256
+ * tokens of x_in once, then times `reps` launches of the matmul kernel over the copies in
+ * turn; *ms_per_matmul receives the mean device time of one launch.  mode is 13 or 14.
+ * Returns 0, -1 for bad arguments, -4 for a CUDA error. */
+DPUF_EXPORT int32_t dpuf_cuda_had_asym_timed(int32_t mode, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                             const float* x_in, const uint8_t* tensor_base,
+                                             const uint64_t* tile_offsets, const uint8_t* sign_bits,
+                                             int32_t n_copies, int32_t reps, float* ms_per_matmul);
+
 /* Builds or loads the glibc expf exception table; returns its entry count (host only). */
 DPUF_EXPORT int64_t dpuf_cuda_prepare_expf_table(void);
 

@@ -117,6 +117,21 @@ DPUF_EXPORT void dpuf_embed_qr_hadamard4_packed_f32(
     const uint8_t* tensor_base, const uint64_t* tile_offsets,
     const uint8_t* sign_bits, float* out);
 
+/* ---- standalone mode-13 / mode-14 matmul (reference dpuf_kernels.h:286-309) -------------
+ * QR_HAD4_ASYM (4-bit) and QR_HAD6 (6-bit): asymmetric blk64 tiles (8 fp16 d, 8 fp16 m per
+ * 64-block and 8-row group) over the same FWHT-64 activation prep; same calling convention as
+ * the mode-12 matmul.  A bad descriptor (cols % 64, a tile whose rows fall outside [0, rows))
+ * leaves out untouched and is reported by dpuf_cuda_last_error(). */
+DPUF_EXPORT void dpuf_matmul_qr_had4_asym_f32(
+    int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+    const float* x_in, const uint8_t* tensor_base, const uint64_t* tile_offsets,
+    const uint8_t* sign_bits, float* out);
+
+DPUF_EXPORT void dpuf_matmul_qr_had6_f32(
+    int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+    const float* x_in, const uint8_t* tensor_base, const uint64_t* tile_offsets,
+    const uint8_t* sign_bits, float* out);
+
 /* ---- persistent engine (reference dpuf_kernels.h:316-360) -------------------------------
  * create: copies every weight, norm and sign table to device memory (the caller's buffers
  *         need not outlive the call); returns NULL on bad arguments, unsupported weight
