@@ -20,7 +20,6 @@
 namespace dpuf {
 namespace {
 
-constexpr int kHadWarps = 8;     // 8-row groups per CTA
 constexpr int kHadChunk = 256;   // tokens per prep + matmul launch pair
 
 // One warp computes one 8-row group (rg) of tile t for token blockIdx.y; lane = 4 r + c: row r,
@@ -32,13 +31,17 @@ constexpr int kHadChunk = 256;   // tokens per prep + matmul launch pair
 //   acc  = fma(fdot, d_row, acc);  acc = fma(m_row, xm_s, acc)
 // with xm_s = fma(xsum_{2g}, xs_{2g}, xsum_{2g+1} * xs_{2g+1}) * 0.125: the reference's scalar
 // "(xsum0 * xs0 + xsum1 * xs1) * 0.125f", which its build (gcc, gnu11, -mfma) contracts.
-template <bool kHad6>
-__global__ void __launch_bounds__(kHadWarps * 32) had_asym_kernel(const uint8_t* __restrict__ tiles,
+// kG 64-blocks per batch (all their loads issued before their dots and chain steps) and kWarps
+// 8-row groups per CTA: deep batches in small CTAs for one token (a GEMV streaming from HBM),
+// shallow batches in larger CTAs for several tokens (the tiles are re-read from L2, and more
+// resident warps hide that better).
+template <bool kHad6, int kG, int kWarps>
+__global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __restrict__ tiles,
                                                                   const uint64_t* __restrict__ toff, int rows,
                                                                   int cols, int n_tiles, Act a,
                                                                   float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * kHadWarps + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
   const int t = gw >> 1, rg = gw & 1;
   if (t >= n_tiles) return;
   const uint8_t* tp = tiles + toff[t];
@@ -56,32 +59,52 @@ __global__ void __launch_bounds__(kHadWarps * 32) had_asym_kernel(const uint8_t*
   const float* xs = a.xs + (size_t)m * (a.ld >> 5);
   const int* xm = a.xm + (size_t)m * (a.ld >> 5);
   float acc = 0.0f;
-#pragma unroll 2
-  for (int g = 0; g < n_64; g++) {
-    int d[2];
+  for (int g0 = 0; g0 < n_64; g0 += kG) {
+    const int ng = min(kG, n_64 - g0);
+    uint32_t lo[kG][2], hi[kG][2];
+    int xa[kG][2], xb[kG][2];
+    uint16_t dv[kG], mv[kG];
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-      const int b = 2 * g + k;
-      const uint32_t w = __ldg((const uint32_t*)(q4 + (size_t)b * 128 + c * 32 + r * 4));
-      uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-      if (kHad6) {
-        const uint8_t* hp = q2 + (size_t)b * 64 + c * 16 + (r & 1) * 4;
-        lo |= ((__ldg((const uint32_t*)hp) >> sh) & 0x03030303u) << 4;
-        hi |= ((__ldg((const uint32_t*)(hp + 8)) >> sh) & 0x03030303u) << 4;
+    for (int i = 0; i < kG; i++) {
+      if (i >= ng) break;
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int b = 2 * (g0 + i) + k;
+        const uint32_t w = __ldg((const uint32_t*)(q4 + (size_t)b * 128 + c * 32 + r * 4));
+        lo[i][k] = w & 0x0F0F0F0Fu;
+        hi[i][k] = (w >> 4) & 0x0F0F0F0Fu;
+        if (kHad6) {
+          const uint8_t* hp = q2 + (size_t)b * 64 + c * 16 + (r & 1) * 4;
+          lo[i][k] |= ((__ldg((const uint32_t*)hp) >> sh) & 0x03030303u) << 4;
+          hi[i][k] |= ((__ldg((const uint32_t*)(hp + 8)) >> sh) & 0x03030303u) << 4;
+        }
+        const int* xw = (const int*)(xq + b * 32 + c * 8);
+        xa[i][k] = xw[0];
+        xb[i][k] = xw[1];
       }
-      const int* xw = (const int*)(xq + b * 32 + c * 8);
-      int p = __dp4a((int)lo, xw[0], 0);
-      p = __dp4a((int)hi, xw[1], p);
-      p += __shfl_xor_sync(kFull, p, 1);
-      p += __shfl_xor_sync(kFull, p, 2);
-      d[k] = p;
+      dv[i] = __ldg(dm + (g0 + i) * 16 + r);
+      mv[i] = __ldg(dm + (g0 + i) * 16 + 8 + r);
     }
-    const int b0 = 2 * g, b1 = b0 + 1;
-    const float xs0 = xs[b0], xs1 = xs[b1];
-    const float fdot = __fmaf_rn(__int2float_rn(d[0]), xs0, __fmul_rn(__int2float_rn(d[1]), xs1));
-    const float xms = __fmul_rn(__fmaf_rn(__int2float_rn(xm[b0]), xs0, __fmul_rn(__int2float_rn(xm[b1]), xs1)), 0.125f);
-    acc = __fmaf_rn(fdot, f16bits_to_f32(__ldg(dm + g * 16 + r)), acc);
-    acc = __fmaf_rn(f16bits_to_f32(__ldg(dm + g * 16 + 8 + r)), xms, acc);
+#pragma unroll
+    for (int i = 0; i < kG; i++) {
+      if (i >= ng) break;
+      int d[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        int p = __dp4a((int)lo[i][k], xa[i][k], 0);
+        p = __dp4a((int)hi[i][k], xb[i][k], p);
+        p += __shfl_xor_sync(kFull, p, 1);
+        p += __shfl_xor_sync(kFull, p, 2);
+        d[k] = p;
+      }
+      const int b0 = 2 * (g0 + i), b1 = b0 + 1;
+      const float xs0 = xs[b0], xs1 = xs[b1];
+      const float fdot = __fmaf_rn(__int2float_rn(d[0]), xs0, __fmul_rn(__int2float_rn(d[1]), xs1));
+      const float xms =
+          __fmul_rn(__fmaf_rn(__int2float_rn(xm[b0]), xs0, __fmul_rn(__int2float_rn(xm[b1]), xs1)), 0.125f);
+      acc = __fmaf_rn(fdot, f16bits_to_f32(dv[i]), acc);
+      acc = __fmaf_rn(f16bits_to_f32(mv[i]), xms, acc);
+    }
   }
   if (c == 0 && rg * 8 + r < n_r) out[(size_t)m * rows + t * 16 + rg * 8 + r] = acc;
 }
@@ -142,12 +165,20 @@ bool had_upload(HadMat& h, int had6, int rows, int cols, int n_tiles, const uint
   return true;
 }
 
-cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
-  const dim3 grid((2 * h.n_tiles + kHadWarps - 1) / kHadWarps, M);
+template <int kG, int kWarps>
+void launch_had_t(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+  const dim3 grid((2 * h.n_tiles + kWarps - 1) / kWarps, M);
   if (h.had6)
-    had_asym_kernel<true><<<grid, kHadWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+    had_asym_kernel<true, kG, kWarps><<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
   else
-    had_asym_kernel<false><<<grid, kHadWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+    had_asym_kernel<false, kG, kWarps><<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+}
+
+cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+  if (M == 1)
+    launch_had_t<8, 2>(s, h, a, M, y);
+  else
+    launch_had_t<2, 8>(s, h, a, M, y);
   return cudaGetLastError();
 }
 
