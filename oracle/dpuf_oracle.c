@@ -287,6 +287,48 @@ ORC_EXPORT void orc_embed_mode12_f32(int32_t n_tokens, int32_t cols, const int32
     }
 }
 
+/* Mode 13 / 14 row lookup (embed_qr_had_asym_impl, dpuf_avx2.c:3146-3221): per 64-block the
+ * row's d and m, per element v = q * d + m, then FWHT-64 and the column signs.  q * d is exact
+ * (q < 64, d an fp16: at most 17 significant bits), so a fused multiply-add gives the same
+ * bits. */
+ORC_EXPORT void orc_embed_had_asym_f32(int32_t is_had6, int32_t n_tokens, int32_t cols, const int32_t* ids,
+                                       const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                                       const uint8_t* sign_bits, float* out) {
+    const int32_t n_64 = cols >> 6;
+    const size_t grp_bytes = is_had6 ? 416u : 288u;
+    for (int32_t tok = 0; tok < n_tokens; tok++) {
+        const int32_t r = ids[tok], t = r / 16, lr = r % 16, rg = lr >> 3, ri = lr & 7;
+        const uint8_t* grp = tensor_base + tile_offsets[t] + 16 + (size_t)rg * (size_t)n_64 * grp_bytes;
+        const uint16_t* dm = (const uint16_t*)grp;
+        const uint8_t* q4 = grp + (size_t)n_64 * 32u;
+        const uint8_t* q2 = q4 + (size_t)n_64 * 256u;
+        float* dst = out + (size_t)tok * (size_t)cols;
+        for (int32_t g = 0; g < n_64; g++) {
+            const float wd = f16_to_f32(dm[g * 16 + ri]), wm = f16_to_f32(dm[g * 16 + 8 + ri]);
+            for (int k2 = 0; k2 < 2; k2++) {
+                const int32_t b = 2 * g + k2;
+                for (int c = 0; c < 4; c++)
+                    for (int e = 0; e < 4; e++) {
+                        const uint8_t byte = q4[(size_t)b * 128u + c * 32 + ri * 4 + e];
+                        int32_t ulo = byte & 15, uhi = byte >> 4;
+                        if (is_had6) {
+                            const uint8_t* hp = q2 + (size_t)b * 64u + c * 16 + (ri & 1) * 4 + e;
+                            ulo |= ((hp[0] >> (2 * (ri >> 1))) & 3) << 4;
+                            uhi |= ((hp[8] >> (2 * (ri >> 1))) & 3) << 4;
+                        }
+                        float* d0 = dst + b * 32 + c * 8 + e;
+                        d0[0] = (float)ulo * wd + wm;
+                        d0[4] = (float)uhi * wd + wm;
+                    }
+            }
+        }
+        for (int32_t c = 0; c < cols; c += 64) fwht64(dst + c);
+        if (sign_bits)
+            for (int32_t c = 0; c < cols; c++)
+                if ((sign_bits[c >> 3] >> (c & 7)) & 1) dst[c] = -dst[c];
+    }
+}
+
 /* ------------------------------------------------------------------ pointwise ops */
 
 /* x += res (if res); out = (x * inv) * w, inv = 1/sqrt(ss/n + eps) with ss the 8-lane fma

@@ -191,6 +191,17 @@ def oracle_matmul_had(mode: int, M, blob, x):
     return out
 
 
+def oracle_embed_had(mode: int, blob, ids):
+    """Mode 13 / 14 row lookup restated (dpuf_avx2.c:3146-3221): out[len(ids)][cols]."""
+    lib = OracleEngine.lib_()
+    lib.orc_embed_had_asym_f32.argtypes = [ctypes.c_int32] * 3 + [ctypes.c_void_p] * 5
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    out = np.empty((ids.size, blob.cols), dtype=np.float32)
+    lib.orc_embed_had_asym_f32(int(mode == 14), ids.size, blob.cols, ids.ctypes.data, blob.tiles.ctypes.data,
+                               blob.tile_offsets.ctypes.data, blob.sign_bits.ctypes.data, out.ctypes.data)
+    return out
+
+
 def ref_matmul(M, blob, x):
     lib = RefEngine.lib_()
     x = np.ascontiguousarray(x, dtype=np.float32)

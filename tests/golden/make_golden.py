@@ -87,6 +87,16 @@ def main() -> None:
         fn[mode](M, rows, cols, bv.n_tiles, x.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data,
                  bv.sign_bits.ctypes.data, out.ctypes.data)
         had[f"out_{ci}_{M}_{kind}"] = out
+    emb = {13: lib.dpuf_embed_qr_had4_asym_f32, 14: lib.dpuf_embed_qr_had6_f32}
+    for f in emb.values():
+        f.argtypes = [ctypes.c_int32] * 2 + [ctypes.c_void_p] * 5
+    for ci, (rows, cols, mode, _) in enumerate(sc.HAD_CASES):
+        bv = packer.BlobView(had[f"blob_{ci}"])
+        ids = sc.had_embed_ids(ci, rows)
+        out = np.empty((ids.size, cols), np.float32)
+        emb[mode](ids.size, cols, ids.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data,
+                  bv.sign_bits.ctypes.data, out.ctypes.data)
+        had[f"embed_{ci}"] = out
     np.savez_compressed(HERE / "had_asym.npz", **had)
 
     # ---- engine scenarios

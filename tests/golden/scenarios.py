@@ -73,6 +73,13 @@ HAD_MATMUL = [(0, 1, "normal"), (0, 5, "normal"), (1, 1, "normal"), (1, 7, "norm
               (2, 13, "normal"), (3, 1, "normal"), (3, 6, "sparse")]
 
 
+def had_embed_ids(case_idx: int, rows: int) -> np.ndarray:
+    """Row ids for the mode-13/14 embedding fixtures: the first and last rows (the last tile may
+    be ragged) and seeded random rows."""
+    rng = np.random.default_rng(900 + case_idx)
+    return np.concatenate([[0, rows - 1], rng.integers(0, rows, 7)]).astype(np.int32)
+
+
 def matmul_input(case_idx: int, M: int, kind: str, cols: int) -> np.ndarray:
     rng = np.random.default_rng(1000 + 17 * case_idx + M)
     x = rng.standard_normal((M, cols)).astype(np.float32)

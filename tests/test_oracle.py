@@ -43,6 +43,16 @@ def test_oracle_had_asym_matches_reference(ci, M, kind):
     assert bitexact(orc.oracle_matmul_had(mode, M, bv, x), g[f"out_{ci}_{M}_{kind}"])
 
 
+@pytest.mark.parametrize("ci", range(len(sc.HAD_CASES)))
+def test_oracle_had_embed_matches_reference(ci):
+    from dpuf_b200 import packer
+
+    g = golden_arrays("had_asym.npz")
+    rows, cols, mode, _ = sc.HAD_CASES[ci]
+    bv = packer.BlobView(g[f"blob_{ci}"])
+    assert bitexact(orc.oracle_embed_had(mode, bv, sc.had_embed_ids(ci, rows)), g[f"embed_{ci}"])
+
+
 def test_swiglu_range_split_matches_reference_threads():
     lib = orc.OracleEngine.lib_()
     # I = 3072, M = 1 over 8 threads: every range is a multiple of 8 -> all vector
