@@ -1,7 +1,7 @@
-// ops_had_asym.cu - standalone matmul of the reference's modes 13 (QR_HAD4_ASYM, 4-bit) and 14
-// (QR_HAD6, 6-bit) behind its exported signatures (dpuf_kernels.h:279-313,
-// dpuf_avx2.c:2785-3144): the mode-12 activation prep (launch_prep: sign flip, FWHT-64, int8
-// per 32 with block scale and block sum x 8), then had_asym_kernel.
+// ops_had_asym.cu - standalone matmul and row lookup of the reference's modes 13 (QR_HAD4_ASYM,
+// 4-bit) and 14 (QR_HAD6, 6-bit) behind its exported signatures (dpuf_kernels.h:279-313,
+// dpuf_avx2.c:2785-3221): the mode-12 activation prep (launch_prep: sign flip, FWHT-64, int8
+// per 32 with block scale and block sum x 8), then had_asym_kernel; had_embed_kernel.
 //
 // Tile layout (16-byte header, then per 8-row group): n64 x [8 fp16 d | 8 fp16 m] per 64-block,
 // then per 32-block 128 bytes of nibbles ordered [chunk c][row r][e] - the low nibble weighs
@@ -107,6 +107,45 @@ __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __
     }
   }
   if (c == 0 && rg * 8 + r < n_r) out[(size_t)m * rows + t * 16 + rg * 8 + r] = acc;
+}
+
+// Row lookup (embed_qr_had_asym_impl, dpuf_avx2.c:3146-3221): one warp per 64-column chunk of
+// one token's row.  Lane l dequantises columns c0+l and c0+32+l, v = u * d + m (u * d is exact:
+// u < 64, d an fp16), then the chunk's FWHT-64 (fwht64_warp, the mode-12 lookup's) and the
+// column signs.  Row ids were checked against the tiles on the host.
+template <bool kHad6>
+__global__ void __launch_bounds__(256) had_embed_kernel(const uint8_t* __restrict__ tiles,
+                                                        const uint64_t* __restrict__ toff, int cols,
+                                                        const int32_t* __restrict__ ids,
+                                                        const uint8_t* __restrict__ signs, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int ch = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (ch * 64 >= cols) return;
+  const int tok = blockIdx.y;
+  const int row = ids[tok], t = row >> 4, lr = row & 15, rg = lr >> 3, ri = lr & 7;
+  const int n_64 = cols >> 6;
+  const uint8_t* grp = tiles + toff[t] + 16 + (size_t)rg * n_64 * (kHad6 ? 416 : 288);
+  const uint16_t* dm = (const uint16_t*)grp;
+  const uint8_t* q4 = grp + (size_t)n_64 * 32;
+  const uint8_t* q2 = q4 + (size_t)n_64 * 256;
+  const float wd = f16bits_to_f32(dm[ch * 16 + ri]), wm = f16bits_to_f32(dm[ch * 16 + 8 + ri]);
+  float v[2];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int b = 2 * ch + h, p = lane, c = p >> 3, e = p & 3, high = (p >> 2) & 1;
+    const uint8_t byte = q4[(size_t)b * 128 + c * 32 + ri * 4 + e];
+    int u = high ? (byte >> 4) : (byte & 15);
+    if (kHad6) u |= ((q2[(size_t)b * 64 + c * 16 + high * 8 + (ri & 1) * 4 + e] >> (2 * (ri >> 1))) & 3) << 4;
+    v[h] = __fadd_rn(__fmul_rn((float)u, wd), wm);
+  }
+  fwht64_warp(v[0], v[1], lane);
+  const int ca = ch * 64 + lane, cb = ca + 32;
+  if (signs) {
+    if ((signs[ca >> 3] >> (ca & 7)) & 1) v[0] = -v[0];
+    if ((signs[cb >> 3] >> (cb & 7)) & 1) v[1] = -v[1];
+  }
+  out[(size_t)tok * cols + ca] = v[0];
+  out[(size_t)tok * cols + cb] = v[1];
 }
 
 // A mode-13/14 matrix in device memory: its tile span, tile offsets relative to it, signs.
@@ -232,10 +271,66 @@ void had_matmul_host(int had6, int32_t M, int32_t rows, int32_t cols, int32_t n_
   cudaFree(h.mem);
 }
 
+// Reference signature: rows are looked up by id; the tiles up to the largest id are uploaded,
+// and an id whose row is not in its tile is rejected (the reference would read past it).
+void had_embed_host(int had6, int32_t n_tokens, int32_t cols, const int32_t* ids, const uint8_t* base,
+                    const uint64_t* toff, const uint8_t* signs, float* out) {
+  set_error("");
+  if (n_tokens <= 0 || !ids || !out || !base || !toff) return;
+  int32_t max_id = 0;
+  for (int i = 0; i < n_tokens; i++) {
+    const int32_t r = ids[i];
+    if (r < 0) {
+      set_error("negative token id");
+      return;
+    }
+    const uint8_t* tp = base + toff[r >> 4];
+    if ((r & 15) >= (tp[4] | (tp[5] << 8))) {
+      set_error("token id beyond its tile's rows");
+      return;
+    }
+    max_id = std::max(max_id, r);
+  }
+  const int n_tiles = max_id / kTileRows + 1;
+  HadMat h;
+  int32_t* dids = nullptr;
+  float* dy = nullptr;
+  if (had_upload(h, had6, n_tiles * kTileRows, cols, n_tiles, base, toff, signs) &&
+      cudaMalloc(&dids, (size_t)n_tokens * 4) == cudaSuccess &&
+      cudaMalloc(&dy, (size_t)n_tokens * cols * 4) == cudaSuccess &&
+      cudaMemcpy(dids, ids, (size_t)n_tokens * 4, cudaMemcpyHostToDevice) == cudaSuccess) {
+    for (int m0 = 0; m0 < n_tokens; m0 += 65535) {
+      const int mc = std::min(65535, n_tokens - m0);
+      const dim3 grid((cols / 64 + 7) / 8, mc);
+      if (had6)
+        had_embed_kernel<true><<<grid, 256>>>(h.mem, h.toff, cols, dids + m0, h.signs, dy + (size_t)m0 * cols);
+      else
+        had_embed_kernel<false><<<grid, 256>>>(h.mem, h.toff, cols, dids + m0, h.signs, dy + (size_t)m0 * cols);
+    }
+    const cudaError_t e = cudaMemcpy(out, dy, (size_t)n_tokens * cols * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) set_error(cudaGetErrorString(e));
+  }
+  cudaFree(dids);
+  cudaFree(dy);
+  cudaFree(h.mem);
+}
+
 }  // namespace
 }  // namespace dpuf
 
 extern "C" {
+
+DPUF_EXPORT void dpuf_embed_qr_had4_asym_f32(int32_t n_tokens, int32_t cols, const int32_t* token_ids,
+                                             const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                                             const uint8_t* sign_bits, float* out) {
+  dpuf::had_embed_host(0, n_tokens, cols, token_ids, tensor_base, tile_offsets, sign_bits, out);
+}
+
+DPUF_EXPORT void dpuf_embed_qr_had6_f32(int32_t n_tokens, int32_t cols, const int32_t* token_ids,
+                                        const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                                        const uint8_t* sign_bits, float* out) {
+  dpuf::had_embed_host(1, n_tokens, cols, token_ids, tensor_base, tile_offsets, sign_bits, out);
+}
 
 DPUF_EXPORT void dpuf_matmul_qr_had4_asym_f32(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
                                               const float* x_in, const uint8_t* tensor_base,

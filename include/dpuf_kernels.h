@@ -117,7 +117,7 @@ DPUF_EXPORT void dpuf_embed_qr_hadamard4_packed_f32(
     const uint8_t* tensor_base, const uint64_t* tile_offsets,
     const uint8_t* sign_bits, float* out);
 
-/* ---- standalone mode-13 / mode-14 matmul (reference dpuf_kernels.h:286-309) -------------
+/* ---- standalone mode-13 / mode-14 ops (reference dpuf_kernels.h:279-314) -----------------
  * QR_HAD4_ASYM (4-bit) and QR_HAD6 (6-bit): asymmetric blk64 tiles (8 fp16 d, 8 fp16 m per
  * 64-block and 8-row group) over the same FWHT-64 activation prep; same calling convention as
  * the mode-12 matmul.  A bad descriptor (cols % 64, a tile whose rows fall outside [0, rows))
@@ -130,6 +130,18 @@ DPUF_EXPORT void dpuf_matmul_qr_had4_asym_f32(
 DPUF_EXPORT void dpuf_matmul_qr_had6_f32(
     int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
     const float* x_in, const uint8_t* tensor_base, const uint64_t* tile_offsets,
+    const uint8_t* sign_bits, float* out);
+
+/* Row lookup of modes 13 / 14 (reference dpuf_kernels.h:293-297 and 310-314): out is
+ * [n_tokens][cols]; an id whose row is not in its tile is rejected (dpuf_cuda_last_error). */
+DPUF_EXPORT void dpuf_embed_qr_had4_asym_f32(
+    int32_t n_tokens, int32_t cols, const int32_t* token_ids,
+    const uint8_t* tensor_base, const uint64_t* tile_offsets,
+    const uint8_t* sign_bits, float* out);
+
+DPUF_EXPORT void dpuf_embed_qr_had6_f32(
+    int32_t n_tokens, int32_t cols, const int32_t* token_ids,
+    const uint8_t* tensor_base, const uint64_t* tile_offsets,
     const uint8_t* sign_bits, float* out);
 
 /* ---- persistent engine (reference dpuf_kernels.h:316-360) -------------------------------

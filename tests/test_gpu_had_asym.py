@@ -89,3 +89,28 @@ def test_had_asym_timed_entry_point(lib):
     assert lib.dpuf_cuda_had_asym_timed(12, 4, rows, cols, bv.n_tiles, x.ctypes.data, bv.tiles.ctypes.data,
                                         bv.tile_offsets.ctypes.data, bv.sign_bits.ctypes.data, 2, 5,
                                         ctypes.byref(ms)) == -1
+
+
+@pytest.mark.parametrize("ci", range(len(sc.HAD_CASES)))
+def test_had_embed_matches_reference(lib, ci):
+    g, bv, (rows, cols, mode, _) = _case(ci)
+    ids = sc.had_embed_ids(ci, rows)
+    fn = lib.dpuf_embed_qr_had4_asym_f32 if mode == 13 else lib.dpuf_embed_qr_had6_f32
+    fn.argtypes = [ctypes.c_int32] * 2 + [ctypes.c_void_p] * 5
+    out = np.empty((ids.size, cols), np.float32)
+    fn(ids.size, cols, ids.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data, bv.sign_bits.ctypes.data,
+       out.ctypes.data)
+    assert bitexact(out, g[f"embed_{ci}"])
+
+
+def test_had_embed_rejects_rows_outside_tiles(lib):
+    from dpuf_b200 import engine
+
+    _, bv, (rows, cols, mode, _) = _case(1)  # 100 rows: the last tile holds rows 96..99
+    lib.dpuf_embed_qr_had6_f32.argtypes = [ctypes.c_int32] * 2 + [ctypes.c_void_p] * 5
+    for bad in (rows, -1):
+        ids = np.array([3, bad], np.int32)
+        out = np.full((2, cols), 7.0, np.float32)
+        lib.dpuf_embed_qr_had6_f32(2, cols, ids.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data,
+                                   bv.sign_bits.ctypes.data, out.ctypes.data)
+        assert np.all(out == 7.0) and engine.last_error(), bad
