@@ -109,6 +109,86 @@ __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __
   if (c == 0 && rg * 8 + r < n_r) out[(size_t)m * rows + t * 16 + rg * 8 + r] = acc;
 }
 
+// One token (a GEMV): one CTA per 8-row group, its 64-blocks split over kSplit warps.  Each
+// warp computes, for its blocks, the same per-row terms as had_asym_kernel (exact integer dots,
+// fdot, xm_s, the row's d and m) into shared memory, loads of kG blocks in flight; then warp 0
+// runs each row's chain over all blocks in order.  Same bits as the one-warp form, kSplit times
+// the loads in flight.  Shared memory: n64 * 8 float4.
+template <bool kHad6, int kSplit, int kG>
+__global__ void __launch_bounds__(kSplit * 32) had_gemv_split_kernel(const uint8_t* __restrict__ tiles,
+                                                                     const uint64_t* __restrict__ toff, int rows,
+                                                                     int cols, Act a, float* __restrict__ out) {
+  extern __shared__ float4 terms[];  // [n64][8]: fdot, xm_s, d, m
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x >> 1, rg = blockIdx.x & 1;
+  const uint8_t* tp = tiles + toff[t];
+  const int n_r = tp[4] | (tp[5] << 8);
+  if (rg * 8 >= n_r) return;  // the whole CTA
+  const int n_64 = cols >> 6;
+  const uint8_t* grp = tp + 16 + (size_t)rg * n_64 * (kHad6 ? 416 : 288);
+  const uint16_t* dm = (const uint16_t*)grp;
+  const uint8_t* q4 = grp + (size_t)n_64 * 32;
+  const uint8_t* q2 = q4 + (size_t)n_64 * 256;
+  const int r = lane >> 2, c = lane & 3, sh = 2 * (r >> 1);
+  const int g_lo = warp * n_64 / kSplit, g_hi = (warp + 1) * n_64 / kSplit;
+  for (int g0 = g_lo; g0 < g_hi; g0 += kG) {
+    const int ng = min(kG, g_hi - g0);
+    uint32_t lo[kG][2], hi[kG][2];
+    int xa[kG][2], xb[kG][2];
+    uint16_t dv[kG], mv[kG];
+#pragma unroll
+    for (int i = 0; i < kG; i++) {
+      if (i >= ng) break;
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int b = 2 * (g0 + i) + k;
+        const uint32_t w = __ldg((const uint32_t*)(q4 + (size_t)b * 128 + c * 32 + r * 4));
+        lo[i][k] = w & 0x0F0F0F0Fu;
+        hi[i][k] = (w >> 4) & 0x0F0F0F0Fu;
+        if (kHad6) {
+          const uint8_t* hp = q2 + (size_t)b * 64 + c * 16 + (r & 1) * 4;
+          lo[i][k] |= ((__ldg((const uint32_t*)hp) >> sh) & 0x03030303u) << 4;
+          hi[i][k] |= ((__ldg((const uint32_t*)(hp + 8)) >> sh) & 0x03030303u) << 4;
+        }
+        const int* xw = (const int*)(a.q8 + b * 32 + c * 8);
+        xa[i][k] = xw[0];
+        xb[i][k] = xw[1];
+      }
+      dv[i] = __ldg(dm + (g0 + i) * 16 + r);
+      mv[i] = __ldg(dm + (g0 + i) * 16 + 8 + r);
+    }
+#pragma unroll
+    for (int i = 0; i < kG; i++) {
+      if (i >= ng) break;
+      int d[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        int p = __dp4a((int)lo[i][k], xa[i][k], 0);
+        p = __dp4a((int)hi[i][k], xb[i][k], p);
+        p += __shfl_xor_sync(kFull, p, 1);
+        p += __shfl_xor_sync(kFull, p, 2);
+        d[k] = p;
+      }
+      const int b0 = 2 * (g0 + i), b1 = b0 + 1;
+      const float xs0 = a.xs[b0], xs1 = a.xs[b1];
+      const float fdot = __fmaf_rn(__int2float_rn(d[0]), xs0, __fmul_rn(__int2float_rn(d[1]), xs1));
+      const float xms =
+          __fmul_rn(__fmaf_rn(__int2float_rn(a.xm[b0]), xs0, __fmul_rn(__int2float_rn(a.xm[b1]), xs1)), 0.125f);
+      if (c == 0) terms[(g0 + i) * 8 + r] = make_float4(fdot, xms, f16bits_to_f32(dv[i]), f16bits_to_f32(mv[i]));
+    }
+  }
+  __syncthreads();
+  if (warp == 0 && lane < 8 && rg * 8 + lane < n_r) {
+    float acc = 0.0f;
+    for (int g = 0; g < n_64; g++) {
+      const float4 v = terms[g * 8 + lane];
+      acc = __fmaf_rn(v.x, v.z, acc);
+      acc = __fmaf_rn(v.w, v.y, acc);
+    }
+    out[t * 16 + rg * 8 + lane] = acc;
+  }
+}
+
 // Row lookup (embed_qr_had_asym_impl, dpuf_avx2.c:3146-3221): one warp per 64-column chunk of
 // one token's row.  Lane l dequantises columns c0+l and c0+32+l, v = u * d + m (u * d is exact:
 // u < 64, d an fp16), then the chunk's FWHT-64 (fwht64_warp, the mode-12 lookup's) and the
@@ -213,11 +293,37 @@ void launch_had_t(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y
     had_asym_kernel<false, kG, kWarps><<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
 }
 
+constexpr int kHadSplit = 4;  // warps per 8-row group in the one-token kernel
+
+cudaError_t configure_had_kernels() {
+  cudaError_t e = cudaFuncSetAttribute(had_gemv_split_kernel<false, kHadSplit, 4>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(had_gemv_split_kernel<true, kHadSplit, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxDynSmem);
+  return e;
+}
+
 cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
-  if (M == 1)
+  const size_t smem = (size_t)(h.cols / 64) * 8 * sizeof(float4);
+  if (M == 1 && smem <= (size_t)kMaxDynSmem) {
+    static thread_local int configured = -1;  // per host thread: the device it was done for
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured != dev) {
+      if (cudaError_t e = configure_had_kernels()) return e;
+      configured = dev;
+    }
+    const dim3 grid(2 * h.n_tiles);
+    if (h.had6)
+      had_gemv_split_kernel<true, kHadSplit, 4><<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, a, y);
+    else
+      had_gemv_split_kernel<false, kHadSplit, 4><<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, a, y);
+  } else if (M == 1) {
     launch_had_t<8, 2>(s, h, a, M, y);
-  else
+  } else {
     launch_had_t<2, 8>(s, h, a, M, y);
+  }
   return cudaGetLastError();
 }
 
