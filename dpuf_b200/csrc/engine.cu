@@ -118,6 +118,7 @@ struct Engine {
   float *cos_tab = nullptr, *sin_tab = nullptr;
 
   std::vector<Slot> slots;  // kMaxSlots, or env DPUF_CUDA_SLOTS for batched serving
+  bool stage_neg[kMaxBatch] = {};  // rows of the current step taken from embeds_in
   int kv_kind = kKvF32;     // KvKind: fp32 (kv_type 0), Q8 (kv_type 1), fp16 (env DPUF_CUDA_KV_F16=1, kv_type 0)
   size_t kv_row = 0;        // bytes of one KV head's cache row at one position
   int n_slots = kMaxSlots;
@@ -343,6 +344,8 @@ struct StepParams {
   float margin;
   bool greedy_loop;  // ids/pos live on the device and advance by greedy feedback
   bool batch = false;  // rows are independent sequences (per-row slot and position)
+  const float* embeds = nullptr;  // host [M][H] rows for ids < 0 (or all rows without ids)
+  bool all_embeds = false;        // every row comes from `embeds`
 };
 
 LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
@@ -385,7 +388,12 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
     CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
   if (P.batch)
     CK(cudaMemcpyAsync(e->d_bstage, e->bstage, sizeof(BatchStaging), cudaMemcpyHostToDevice, e->stream));
-  CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
+  if (!P.all_embeds) CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
+  if (P.embeds)  // rows given by the caller (dpuf_engine.c:1658-1672); ids < 0 were staged as 0
+    for (int m = 0; m < M; m++)
+      if (P.all_embeds || e->stage_neg[m])
+        CK(cudaMemcpyAsync(e->h + (size_t)m * H, P.embeds + (size_t)m * H, (size_t)H * 4, cudaMemcpyHostToDevice,
+                           e->stream));
   const Slot& sl = e->slots[e->active];
   for (int l = 0; l < e->L; l++) {
     const LayerDev& lw = e->layers[l];
@@ -470,7 +478,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
 }
 
 cudaError_t run_step(Engine* e, const StepParams& P) {
-  if (!e->use_graphs) return enqueue_step(e, P);
+  if (!e->use_graphs || P.embeds) return enqueue_step(e, P);  // caller rows: no graph
   uint32_t mb;
   memcpy(&mb, &P.margin, 4);
   // a batched step reads its slots' caches through device pointers, so its graph does not
@@ -651,7 +659,7 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
 }
 
 bool persistent_step(const Engine* e, const StepParams& P) {
-  return P.M == 1 && P.za == 0 && e->dec_ok && e->use_persistent;
+  return P.M == 1 && P.za == 0 && !P.embeds && e->dec_ok && e->use_persistent;
 }
 
 // Launches the persistent kernel for n_steps batch-1 steps from (first_id, pos0) and queues the
@@ -723,26 +731,40 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   if (!e || (!ids && !embeds) || (want_logits && !logits_out && only_last != 2)) return -1;
   if (n <= 0 || n > kMaxBatch) return -2;
   if (pos0 < 0 || pos0 + n > e->S) return -3;
-  if (embeds || ds) {
-    set_error("embeds_in / deepstack_in are not supported by this engine");
+  if (ds) {
+    set_error("deepstack_in is not supported by this engine");
     return -5;
   }
   if (e->cfg.has_mrope && (pt || ph || pw)) {
     set_error("M-RoPE positions are not supported by this engine");
     return -5;
   }
+  // without M-RoPE the reference rotates token m by pos_t[m] (dpuf_engine.c:1681-1686); only
+  // pos_t[m] == pos0 + m, the cache position, is supported here
+  if (pt)
+    for (int i = 0; i < n; i++)
+      if (pt[i] != pos0 + i) {
+        set_error("pos_t different from pos0 + m is not supported by this engine");
+        return -5;
+      }
   for (int i = 0; i < n; i++)
-    if (ids[i] < 0 || ids[i] >= e->tok.rows) {
+    if (ids && (ids[i] >= e->tok.rows || (ids[i] < 0 && !embeds))) {
       set_error("token id out of range");
       return -1;
     }
   if (cudaSetDevice(e->device) != cudaSuccess) return -4;
-  const StepParams P = step_params(e, n, only_last);
+  StepParams P = step_params(e, n, only_last);
+  P.embeds = embeds;
+  P.all_embeds = embeds && !ids;
   const int lm_M = P.only_last == 1 ? 1 : n;
-  memcpy(e->stage->ids, ids, (size_t)n * 4);
+  for (int i = 0; i < n; i++) {  // ids < 0 mark rows taken from embeds_in
+    e->stage_neg[i] = ids && ids[i] < 0;
+    e->stage->ids[i] = (!ids || ids[i] < 0) ? 0 : ids[i];
+  }
   e->stage->pos0 = pos0;
   const bool persistent = persistent_step(e, P);
   cudaError_t err = persistent ? run_decode(e, ids[0], pos0, 1, P.only_last != 2, P.keep) : run_step(e, P);
+  if (embeds && err == cudaSuccess && cudaStreamSynchronize(e->stream) != cudaSuccess) err = cudaErrorUnknown;
   if (err != cudaSuccess) return -4;
   e->last_zone_used = P.za > 0;
   e->last_rows = P.only_last == 2 ? 0 : lm_M;

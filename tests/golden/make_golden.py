@@ -135,8 +135,44 @@ def main() -> None:
                     os.environ.pop(k, None)
                 else:
                     os.environ[k] = v
+    eng_out["embeds_in"] = embeds_golden(lib)
     (HERE / "engine.json").write_text(json.dumps(eng_out, indent=1))
     np.savez_compressed(HERE / "engine_logits.npz", **eng_logits)
+
+
+def embeds_golden(lib) -> dict:
+    """forward_batch_ex with embeds_in on the reference engine (8 threads): all rows from
+    embeddings (every row's logits), then 4 greedy steps from ids; and a mixed call whose ids
+    -1 take their rows from embeds_in (last row's logits)."""
+    shape, seed, rows = sc.EMBEDS_CASE
+    m = mdl.SyntheticModel(mdl.SHAPES[shape], seed=seed, norm_jitter=0.1)
+    ref = orc.RefEngine(m, n_threads=8)
+    f = lib.dpuf_engine_forward_batch_ex
+    f.restype = ctypes.c_int32
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p] + \
+        [ctypes.c_void_p] * 4 + [ctypes.c_int32, ctypes.c_void_p]
+    emb = sc.embeds_input(rows, m.shape.hidden)
+    V = m.shape.vocab
+    ref.reset()
+    allp = np.empty((rows, V), np.float32)
+    assert f(ref.h, rows, None, 0, emb.ctypes.data, None, None, None, None, 0, allp.ctypes.data) == 0
+    rec = {"all_digest": sc.logits_digest(allp)}
+    tok, pos, digs, ids = int(np.argmax(allp[-1])), rows, [], []
+    for _ in range(4):
+        lg = ref.forward(np.array([tok], np.int32), pos, 1)[0]
+        digs.append(sc.logits_digest(lg))
+        tok = int(np.argmax(lg))
+        ids.append(tok)
+        pos += 1
+    rec["steps_digests"], rec["steps_ids"] = digs, ids
+    ref.reset()
+    mixed = mdl.prompt_ids(rows, V, seed).astype(np.int32)
+    mixed[list(sc.EMBEDS_MIXED_NEG)] = -1
+    last = np.empty((1, V), np.float32)
+    assert f(ref.h, rows, mixed.ctypes.data, 0, emb.ctypes.data, None, None, None, None, 1, last.ctypes.data) == 0
+    rec["mixed_last_digest"] = sc.logits_digest(last)
+    ref.close()
+    return rec
 
 
 if __name__ == "__main__":

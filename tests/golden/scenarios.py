@@ -73,6 +73,16 @@ HAD_MATMUL = [(0, 1, "normal"), (0, 5, "normal"), (1, 1, "normal"), (1, 7, "norm
               (2, 13, "normal"), (3, 1, "normal"), (3, 6, "sparse")]
 
 
+# forward_batch_ex with embeds_in (dpuf_engine.c:1658-1672): model shape, seed, rows, and the
+# ids of the mixed call (-1: the row comes from embeds_in).
+EMBEDS_CASE = ("tiny", 5, 12)
+EMBEDS_MIXED_NEG = (2, 5, 11)
+
+
+def embeds_input(rows: int, hidden: int) -> np.ndarray:
+    return (np.random.default_rng(4242).standard_normal((rows, hidden)) * 0.05).astype(np.float32)
+
+
 def had_embed_ids(case_idx: int, rows: int) -> np.ndarray:
     """Row ids for the mode-13/14 embedding fixtures: the first and last rows (the last tile may
     be ragged) and seeded random rows."""

@@ -256,3 +256,52 @@ def test_q8_cache_layout_and_fallback(eng_mod):
         assert len(ids) == 4
     finally:
         e.close()
+
+
+def test_embeds_in_matches_reference(eng_mod):
+    """forward_batch_ex with embeds_in (dpuf_engine.c:1658-1672): every row from the caller's
+    embeddings, then greedy steps from ids; and a mixed call whose ids -1 take their rows from
+    embeds_in.  Logits equal the reference engine's (digests in engine.json).  DeepStack
+    injection and rotary positions other than pos0 + m stay rejected (-5)."""
+    import ctypes
+
+    from dpuf_b200 import model as mdl
+
+    g = golden_engine()["embeds_in"]
+    shape, seed, rows = sc.EMBEDS_CASE
+    m = mdl.SyntheticModel(mdl.SHAPES[shape], seed=seed, norm_jitter=0.1)
+    e = eng_mod.CudaTransformerEngine(m)
+    try:
+        f = e.lib.dpuf_engine_forward_batch_ex
+        f.restype = ctypes.c_int32
+        f.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p] + \
+            [ctypes.c_void_p] * 4 + [ctypes.c_int32, ctypes.c_void_p]
+        emb = sc.embeds_input(rows, m.shape.hidden)
+        V = m.shape.vocab
+        e.reset_cache()
+        allp = np.empty((rows, V), np.float32)
+        assert f(e._handle, rows, None, 0, emb.ctypes.data, None, None, None, None, 0, allp.ctypes.data) == 0
+        assert sc.logits_digest(allp) == g["all_digest"]
+        tok, pos = int(np.argmax(allp[-1])), rows
+        for dig, want in zip(g["steps_digests"], g["steps_ids"]):
+            lg = e.forward_token(tok, pos)
+            assert sc.logits_digest(lg) == dig
+            tok = int(np.argmax(lg))
+            assert tok == want
+            pos += 1
+        e.reset_cache()
+        mixed = mdl.prompt_ids(rows, V, seed).astype(np.int32)
+        mixed[list(sc.EMBEDS_MIXED_NEG)] = -1
+        last = np.empty((1, V), np.float32)
+        assert f(e._handle, rows, mixed.ctypes.data, 0, emb.ctypes.data, None, None, None, None, 1,
+                 last.ctypes.data) == 0
+        assert sc.logits_digest(last) == g["mixed_last_digest"]
+        # a negative id without embeddings, a shifted rotary position, DeepStack rows
+        assert f(e._handle, rows, mixed.ctypes.data, 0, None, None, None, None, None, 1, last.ctypes.data) == -1
+        shifted = (np.arange(rows) + 3).astype(np.int32)
+        assert f(e._handle, rows, None, 0, emb.ctypes.data, shifted.ctypes.data, None, None, None, 1,
+                 last.ctypes.data) == -5
+        ds = (ctypes.c_void_p * 3)(emb.ctypes.data, None, None)
+        assert f(e._handle, rows, None, 0, emb.ctypes.data, None, None, None, ds, 1, last.ctypes.data) == -5
+    finally:
+        e.close()
