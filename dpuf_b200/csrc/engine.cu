@@ -142,6 +142,7 @@ struct Engine {
   BatchStaging* bstage = nullptr;  // pinned
   BatchStaging* d_bstage = nullptr;
   int32_t* d_next = nullptr;       // greedy ids of a batched step [kMaxBatch]
+  float* d_ds = nullptr;           // DeepStack rows of the current step [3][kMaxBatch][H], on first use
   float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
   uint2* d_exp_slots = nullptr;
   unsigned* d_counter = nullptr;  // last-block counters of the multi-CTA argmax
@@ -333,7 +334,7 @@ void destroy_engine(Engine* e) {
     if (p) cudaIpcCloseMemHandle(p);
   cudaFree(e->tp_buf);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits); cudaFreeHost(e->bstage);
-  cudaFree(e->d_bstage); cudaFree(e->d_next);
+  cudaFree(e->d_bstage); cudaFree(e->d_next); cudaFree(e->d_ds);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -346,6 +347,7 @@ struct StepParams {
   bool batch = false;  // rows are independent sequences (per-row slot and position)
   const float* embeds = nullptr;  // host [M][H] rows for ids < 0 (or all rows without ids)
   bool all_embeds = false;        // every row comes from `embeds`
+  int ds_mask = 0;                // layers (bit l, l < 3) whose down output gets d_ds[l] added
 };
 
 LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
@@ -450,6 +452,8 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
     const int keep = (P.keep > 0 && P.keep < lw.down.n_tiles) ? P.keep : lw.down.n_tiles;
     CK(run_linear(e, Lc, one_job(lw.down, e->prep[0], e->hn, H, 0, keep), M, nullptr));
     if (keep < lw.down.n_tiles) CK(launch_zero_rows(Lc, e->hn, M, H, keep * kTileRows));
+    if (l < 3 && ((P.ds_mask >> l) & 1))  // DeepStack injection (dpuf_engine.c:2046-2054)
+      CK(launch_add_rows(Lc, e->hn, e->d_ds + (size_t)l * kMaxBatch * H, M * H));
   }
   if (P.only_last == 2) return cudaSuccess;
   const int lm_start = P.only_last ? M - 1 : 0, lm_M = M - lm_start;
@@ -478,7 +482,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
 }
 
 cudaError_t run_step(Engine* e, const StepParams& P) {
-  if (!e->use_graphs || P.embeds) return enqueue_step(e, P);  // caller rows: no graph
+  if (!e->use_graphs || P.embeds || P.ds_mask) return enqueue_step(e, P);  // caller rows: no graph
   uint32_t mb;
   memcpy(&mb, &P.margin, 4);
   // a batched step reads its slots' caches through device pointers, so its graph does not
@@ -659,7 +663,7 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
 }
 
 bool persistent_step(const Engine* e, const StepParams& P) {
-  return P.M == 1 && P.za == 0 && !P.embeds && e->dec_ok && e->use_persistent;
+  return P.M == 1 && P.za == 0 && !P.embeds && !P.ds_mask && e->dec_ok && e->use_persistent;
 }
 
 // Launches the persistent kernel for n_steps batch-1 steps from (first_id, pos0) and queues the
@@ -731,10 +735,6 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   if (!e || (!ids && !embeds) || (want_logits && !logits_out && only_last != 2)) return -1;
   if (n <= 0 || n > kMaxBatch) return -2;
   if (pos0 < 0 || pos0 + n > e->S) return -3;
-  if (ds) {
-    set_error("deepstack_in is not supported by this engine");
-    return -5;
-  }
   if (e->cfg.has_mrope && (pt || ph || pw)) {
     set_error("M-RoPE positions are not supported by this engine");
     return -5;
@@ -756,6 +756,20 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   StepParams P = step_params(e, n, only_last);
   P.embeds = embeds;
   P.all_embeds = embeds && !ids;
+  if (ds) {  // DeepStack rows of layers 0..2, [n][H] each (null: none for that layer)
+    if (!e->d_ds && cudaMalloc(&e->d_ds, (size_t)3 * kMaxBatch * e->H * 4) != cudaSuccess) {
+      e->d_ds = nullptr;
+      set_error("cudaMalloc (DeepStack rows)");
+      return -4;
+    }
+    for (int l = 0; l < 3 && l < e->L; l++)
+      if (ds[l]) {
+        if (cudaMemcpyAsync(e->d_ds + (size_t)l * kMaxBatch * e->H, ds[l], (size_t)n * e->H * 4,
+                            cudaMemcpyHostToDevice, e->stream) != cudaSuccess)
+          return -4;
+        P.ds_mask |= 1 << l;
+      }
+  }
   const int lm_M = P.only_last == 1 ? 1 : n;
   for (int i = 0; i < n; i++) {  // ids < 0 mark rows taken from embeds_in
     e->stage_neg[i] = ids && ids[i] < 0;
@@ -764,7 +778,7 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   e->stage->pos0 = pos0;
   const bool persistent = persistent_step(e, P);
   cudaError_t err = persistent ? run_decode(e, ids[0], pos0, 1, P.only_last != 2, P.keep) : run_step(e, P);
-  if (embeds && err == cudaSuccess && cudaStreamSynchronize(e->stream) != cudaSuccess) err = cudaErrorUnknown;
+  if ((embeds || ds) && err == cudaSuccess && cudaStreamSynchronize(e->stream) != cudaSuccess) err = cudaErrorUnknown;
   if (err != cudaSuccess) return -4;
   e->last_zone_used = P.za > 0;
   e->last_rows = P.only_last == 2 ? 0 : lm_M;

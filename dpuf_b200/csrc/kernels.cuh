@@ -105,6 +105,8 @@ cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* 
                                int nt_ref, const uint8_t* signs, Act out, const ExpfTable& et, bool per_row = false);
 // Zero rows [r0, H) of out[M][H] (down-projection tile pruning).
 cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0);
+// out[i] += add[i] for i < n (DeepStack injection into the down projection's output).
+cudaError_t launch_add_rows(const Launch& L, float* out, const float* add, int n);
 
 // ---- kernels_lmhead.cu
 // Zone-A test over logits[0, n): top-2 (b1, b2); flag = margin > 0 && b1 - b2 >= margin.

@@ -1,6 +1,8 @@
 // kernels_layer.cu - per-layer pointwise and row-reduction kernels with the reference's
 // exact fp32 operation order: residual add + RMSNorm + mode-12 prep, QK RMSNorm + NeoX RoPE
 // + KV-cache store, SwiGLU with dead-zone + prep of the down-projection input.
+#include <algorithm>
+
 #include "kernels.cuh"
 #include "layer_dev.cuh"
 
@@ -180,6 +182,16 @@ cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* 
   const int chunks = I / 64, wpb = 8;
   return launch_k(L, swiglu_prep_kernel, dim3((chunks + wpb - 1) / wpb, M), dim3(wpb * 32), 0, gate, up, M, I,
                   deadzone, nt_ref, signs, out, et, per_row);
+}
+
+__global__ void add_rows_kernel(float* __restrict__ out, const float* __restrict__ add, int n) {
+  cudaGridDependencySynchronize();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = __fadd_rn(out[i], add[i]);
+}
+
+cudaError_t launch_add_rows(const Launch& L, float* out, const float* add, int n) {
+  return launch_k(L, add_rows_kernel, dim3(std::min((n + 255) / 256, 1184)), dim3(256), 0, out, add, n);
 }
 
 cudaError_t launch_zero_rows(const Launch& L, float* out, int M, int H, int r0) {

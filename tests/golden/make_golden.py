@@ -171,6 +171,24 @@ def embeds_golden(lib) -> dict:
     last = np.empty((1, V), np.float32)
     assert f(ref.h, rows, mixed.ctypes.data, 0, emb.ctypes.data, None, None, None, None, 1, last.ctypes.data) == 0
     rec["mixed_last_digest"] = sc.logits_digest(last)
+    # DeepStack rows for layers 0 and 2 (layer 1: none) with embeddings, all rows' logits; then
+    # one token from an id with DeepStack rows.  The reference adds the DeepStack rows right
+    # after each thread's own part of the down projection, without a barrier
+    # (dpuf_engine.c:2018-2054), so with several threads a row may be added to before another
+    # thread has written it and the result depends on timing (repeated 8-thread runs differ).
+    # One thread cannot race; for this model its SwiGLU split and down-projection path give the
+    # same bits as eight threads (the digests above match either way).
+    ref.close()
+    ref = orc.RefEngine(m, n_threads=1)
+    ds = sc.deepstack_input(rows, m.shape.hidden)
+    ref.reset()
+    arr = (ctypes.c_void_p * 3)(ds[0].ctypes.data, None, ds[2].ctypes.data)
+    assert f(ref.h, rows, None, 0, emb.ctypes.data, None, None, None, arr, 0, allp.ctypes.data) == 0
+    rec["deepstack_all_digest"] = sc.logits_digest(allp)
+    one = np.array([int(np.argmax(allp[-1]))], np.int32)
+    arr1 = (ctypes.c_void_p * 3)(ds[1].ctypes.data, ds[0].ctypes.data, None)
+    assert f(ref.h, 1, one.ctypes.data, rows, None, None, None, None, arr1, 1, last.ctypes.data) == 0
+    rec["deepstack_token_digest"] = sc.logits_digest(last)
     ref.close()
     return rec
 

@@ -83,6 +83,12 @@ def embeds_input(rows: int, hidden: int) -> np.ndarray:
     return (np.random.default_rng(4242).standard_normal((rows, hidden)) * 0.05).astype(np.float32)
 
 
+def deepstack_input(rows: int, hidden: int) -> list:
+    """Three DeepStack row sets [rows][hidden] (the one-token call uses the first row of each)."""
+    rng = np.random.default_rng(4343)
+    return [(rng.standard_normal((rows, hidden)) * 0.02).astype(np.float32) for _ in range(3)]
+
+
 def had_embed_ids(case_idx: int, rows: int) -> np.ndarray:
     """Row ids for the mode-13/14 embedding fixtures: the first and last rows (the last tile may
     be ragged) and seeded random rows."""

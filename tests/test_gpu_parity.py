@@ -261,8 +261,9 @@ def test_q8_cache_layout_and_fallback(eng_mod):
 def test_embeds_in_matches_reference(eng_mod):
     """forward_batch_ex with embeds_in (dpuf_engine.c:1658-1672): every row from the caller's
     embeddings, then greedy steps from ids; and a mixed call whose ids -1 take their rows from
-    embeds_in.  Logits equal the reference engine's (digests in engine.json).  DeepStack
-    injection and rotary positions other than pos0 + m stay rejected (-5)."""
+    embeds_in; DeepStack rows added after layers 0 and 2 (dpuf_engine.c:2046-2054), for 12 rows
+    and for one token.  Logits equal the reference engine's (digests in engine.json).  Rotary
+    positions other than pos0 + m stay rejected (-5)."""
     import ctypes
 
     from dpuf_b200 import model as mdl
@@ -296,12 +297,19 @@ def test_embeds_in_matches_reference(eng_mod):
         assert f(e._handle, rows, mixed.ctypes.data, 0, emb.ctypes.data, None, None, None, None, 1,
                  last.ctypes.data) == 0
         assert sc.logits_digest(last) == g["mixed_last_digest"]
-        # a negative id without embeddings, a shifted rotary position, DeepStack rows
+        ds = sc.deepstack_input(rows, m.shape.hidden)
+        e.reset_cache()
+        arr = (ctypes.c_void_p * 3)(ds[0].ctypes.data, None, ds[2].ctypes.data)
+        assert f(e._handle, rows, None, 0, emb.ctypes.data, None, None, None, arr, 0, allp.ctypes.data) == 0
+        assert sc.logits_digest(allp) == g["deepstack_all_digest"]
+        one = np.array([int(np.argmax(allp[-1]))], np.int32)
+        arr1 = (ctypes.c_void_p * 3)(ds[1].ctypes.data, ds[0].ctypes.data, None)
+        assert f(e._handle, 1, one.ctypes.data, rows, None, None, None, None, arr1, 1, last.ctypes.data) == 0
+        assert sc.logits_digest(last) == g["deepstack_token_digest"]
+        # a negative id without embeddings; a shifted rotary position
         assert f(e._handle, rows, mixed.ctypes.data, 0, None, None, None, None, None, 1, last.ctypes.data) == -1
         shifted = (np.arange(rows) + 3).astype(np.int32)
         assert f(e._handle, rows, None, 0, emb.ctypes.data, shifted.ctypes.data, None, None, None, 1,
                  last.ctypes.data) == -5
-        ds = (ctypes.c_void_p * 3)(emb.ctypes.data, None, None)
-        assert f(e._handle, rows, None, 0, emb.ctypes.data, None, None, None, ds, 1, last.ctypes.data) == -5
     finally:
         e.close()
