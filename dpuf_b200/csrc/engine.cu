@@ -143,6 +143,9 @@ struct Engine {
   BatchStaging* d_bstage = nullptr;
   int32_t* d_next = nullptr;       // greedy ids of a batched step [kMaxBatch]
   float* d_ds = nullptr;           // DeepStack rows of the current step [3][kMaxBatch][H], on first use
+  float* d_tok_rope = nullptr;     // per-token cos | sin rows [2][kMaxBatch][hd/2], on first use
+  std::vector<float> h_cos, h_sin; // host copies of the RoPE tables [max_seq][hd/2]
+  std::vector<float> h_tok_rope;   // staging of d_tok_rope
   float* h_logits = nullptr; // pinned [256][V] staging is too large; [V] for the last row
   uint2* d_exp_slots = nullptr;
   unsigned* d_counter = nullptr;  // last-block counters of the multi-CTA argmax
@@ -334,7 +337,7 @@ void destroy_engine(Engine* e) {
     if (p) cudaIpcCloseMemHandle(p);
   cudaFree(e->tp_buf);
   cudaFreeHost(e->stage); cudaFreeHost(e->h_logits); cudaFreeHost(e->bstage);
-  cudaFree(e->d_bstage); cudaFree(e->d_next); cudaFree(e->d_ds);
+  cudaFree(e->d_bstage); cudaFree(e->d_next); cudaFree(e->d_ds); cudaFree(e->d_tok_rope);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -348,6 +351,7 @@ struct StepParams {
   const float* embeds = nullptr;  // host [M][H] rows for ids < 0 (or all rows without ids)
   bool all_embeds = false;        // every row comes from `embeds`
   int ds_mask = 0;                // layers (bit l, l < 3) whose down output gets d_ds[l] added
+  bool tok_rope = false;          // tokens rotate by d_tok_rope rows (forward_batch_ex positions)
 };
 
 LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1) {
@@ -425,7 +429,8 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
     // 3-4. QK norm, RoPE, KV store; attention
     CK(launch_qk_post(Lc, e->q, e->k, e->v, M, e->nq, e->nkv, e->hd, e->cfg.has_qk_norm ? lw.q_norm : nullptr,
                       e->cfg.has_qk_norm ? lw.k_norm : nullptr, e->cfg.rms_eps, e->cos_tab, e->sin_tab, e->d_pos0,
-                      kv));
+                      kv, P.tok_rope ? e->d_tok_rope : nullptr,
+                      P.tok_rope ? e->d_tok_rope + (size_t)kMaxBatch * (e->hd / 2) : nullptr));
     CK(launch_attention(Lc, e->q, M, e->nq, e->nkv, e->hd, e->d_pos0, kv, e->att, e->et));
     // 5. o_proj
     CK(launch_prep(Lc, e->att, e->qd, M, e->qd, lw.o.signs, e->prep[0]));
@@ -482,7 +487,7 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
 }
 
 cudaError_t run_step(Engine* e, const StepParams& P) {
-  if (!e->use_graphs || P.embeds || P.ds_mask) return enqueue_step(e, P);  // caller rows: no graph
+  if (!e->use_graphs || P.embeds || P.ds_mask || P.tok_rope) return enqueue_step(e, P);  // caller rows: no graph
   uint32_t mb;
   memcpy(&mb, &P.margin, 4);
   // a batched step reads its slots' caches through device pointers, so its graph does not
@@ -663,7 +668,7 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
 }
 
 bool persistent_step(const Engine* e, const StepParams& P) {
-  return P.M == 1 && P.za == 0 && !P.embeds && !P.ds_mask && e->dec_ok && e->use_persistent;
+  return P.M == 1 && P.za == 0 && !P.embeds && !P.ds_mask && !P.tok_rope && e->dec_ok && e->use_persistent;
 }
 
 // Launches the persistent kernel for n_steps batch-1 steps from (first_id, pos0) and queues the
@@ -735,18 +740,6 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   if (!e || (!ids && !embeds) || (want_logits && !logits_out && only_last != 2)) return -1;
   if (n <= 0 || n > kMaxBatch) return -2;
   if (pos0 < 0 || pos0 + n > e->S) return -3;
-  if (e->cfg.has_mrope && (pt || ph || pw)) {
-    set_error("M-RoPE positions are not supported by this engine");
-    return -5;
-  }
-  // without M-RoPE the reference rotates token m by pos_t[m] (dpuf_engine.c:1681-1686); only
-  // pos_t[m] == pos0 + m, the cache position, is supported here
-  if (pt)
-    for (int i = 0; i < n; i++)
-      if (pt[i] != pos0 + i) {
-        set_error("pos_t different from pos0 + m is not supported by this engine");
-        return -5;
-      }
   for (int i = 0; i < n; i++)
     if (ids && (ids[i] >= e->tok.rows || (ids[i] < 0 && !embeds))) {
       set_error("token id out of range");
@@ -756,6 +749,42 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   StepParams P = step_params(e, n, only_last);
   P.embeds = embeds;
   P.all_embeds = embeds && !ids;
+  if (pt || ph || pw) {  // per-token rotation rows (dpuf_engine.c:1679-1696)
+    const int half = e->hd / 2;
+    e->h_tok_rope.assign((size_t)2 * kMaxBatch * half, 0.0f);
+    for (int i = 0; i < n; i++) {
+      const int t = pt ? pt[i] : pos0 + i, hh = ph ? ph[i] : pos0 + i, w = pw ? pw[i] : pos0 + i;
+      float* cr = &e->h_tok_rope[(size_t)i * half];
+      float* sr = &e->h_tok_rope[(size_t)(kMaxBatch + i) * half];
+      if (!e->cfg.has_mrope || (t == hh && t == w)) {  // the tables' row at t
+        if (t < 0 || t >= e->S) {
+          set_error("rotary position outside [0, max_seq_len)");
+          return -3;
+        }
+        memcpy(cr, &e->h_cos[(size_t)t * half], (size_t)half * 4);
+        memcpy(sr, &e->h_sin[(size_t)t * half], (size_t)half * 4);
+      } else {  // eng_compute_mrope_cos_sin (dpuf_engine.c:1602-1623), the same libm
+        const int sec_h = e->cfg.mrope_section[1], len_hw = 3 * sec_h;
+        for (int j = 0; j < half; j++) {
+          const float freq = 1.0f / powf(e->cfg.rope_theta, (2.0f * (float)j) / (float)e->hd);
+          float pv = (float)t;
+          if (j < len_hw) pv = (j % 3 == 1) ? (float)hh : ((j % 3 == 2) ? (float)w : (float)t);
+          const float ang = pv * freq;
+          cr[j] = cosf(ang);
+          sr[j] = sinf(ang);
+        }
+      }
+    }
+    if (!e->d_tok_rope && cudaMalloc(&e->d_tok_rope, e->h_tok_rope.size() * 4) != cudaSuccess) {
+      e->d_tok_rope = nullptr;
+      set_error("cudaMalloc (rotary rows)");
+      return -4;
+    }
+    if (cudaMemcpyAsync(e->d_tok_rope, e->h_tok_rope.data(), e->h_tok_rope.size() * 4, cudaMemcpyHostToDevice,
+                        e->stream) != cudaSuccess)
+      return -4;
+    P.tok_rope = true;
+  }
   if (ds) {  // DeepStack rows of layers 0..2, [n][H] each (null: none for that layer)
     if (!e->d_ds && cudaMalloc(&e->d_ds, (size_t)3 * kMaxBatch * e->H * 4) != cudaSuccess) {
       e->d_ds = nullptr;
@@ -778,7 +807,7 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
   e->stage->pos0 = pos0;
   const bool persistent = persistent_step(e, P);
   cudaError_t err = persistent ? run_decode(e, ids[0], pos0, 1, P.only_last != 2, P.keep) : run_step(e, P);
-  if ((embeds || ds) && err == cudaSuccess && cudaStreamSynchronize(e->stream) != cudaSuccess) err = cudaErrorUnknown;
+  if ((embeds || ds || P.tok_rope) && err == cudaSuccess && cudaStreamSynchronize(e->stream) != cudaSuccess) err = cudaErrorUnknown;
   if (err != cudaSuccess) return -4;
   e->last_zone_used = P.za > 0;
   e->last_rows = P.only_last == 2 ? 0 : lm_M;
@@ -905,6 +934,8 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   {
     std::vector<float> cs, sn;
     rope_tables(c, cs, sn);
+    e->h_cos = cs;
+    e->h_sin = sn;
     if (cudaMalloc(&e->cos_tab, cs.size() * 4) || cudaMalloc(&e->sin_tab, sn.size() * 4) ||
         cudaMemcpy(e->cos_tab, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) ||
         cudaMemcpy(e->sin_tab, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice))

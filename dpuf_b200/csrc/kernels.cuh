@@ -91,9 +91,12 @@ struct KvCache {
   size_t layer_off;  // bytes
   int kind;          // KvKind
 };
+// tok_cos / tok_sin (optional, [M][hd/2]): each token's rotation rows instead of the tables'
+// rows at its cache position (forward_batch_ex rotary positions, M-RoPE).
 cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
                            const float* q_norm, const float* k_norm, float eps, const float* cos_tab,
-                           const float* sin_tab, const int* pos0_dev, KvCache kv);
+                           const float* sin_tab, const int* pos0_dev, KvCache kv, const float* tok_cos = nullptr,
+                           const float* tok_sin = nullptr);
 // Exact causal attention for M tokens, output [M][n_q*hd]: gqa_attn_head_pair_f32's order
 // (fp32 and fp16 caches) or gqa_attn_head_pair_q8's (Q8 cache).
 cudaError_t launch_attention(const Launch& L, const float* q, int M, int n_q, int n_kv, int hd, const int* pos0_dev,

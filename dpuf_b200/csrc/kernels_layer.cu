@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(1024) norm_prep_kernel(float* __restrict__ h, 
 __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_q,
                                int n_kv, int hd, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
                                float eps, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab,
-                               const int* __restrict__ pos0_dev, KvCache kv) {
+                               const int* __restrict__ pos0_dev, KvCache kv, const float* __restrict__ tok_cos,
+                               const float* __restrict__ tok_sin) {
   extern __shared__ __align__(16) float sv[];  // [warps][hd]
   cudaGridDependencySynchronize();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -102,7 +103,8 @@ __global__ void qk_post_kernel(float* __restrict__ q, float* __restrict__ k, con
   float* s = sv + warp * hd;
   for (int i = lane; i < hd; i += 32) s[i] = vec[i];
   __syncwarp();
-  qk_norm_rope_warp(s, nw, eps, hd, cos_tab + (size_t)pos * (hd >> 1), sin_tab + (size_t)pos * (hd >> 1), lane);
+  const size_t rrow = tok_cos ? (size_t)m * (hd >> 1) : (size_t)pos * (hd >> 1);
+  qk_norm_rope_warp(s, nw, eps, hd, (tok_cos ? tok_cos : cos_tab) + rrow, (tok_sin ? tok_sin : sin_tab) + rrow, lane);
   for (int i = lane; i < hd; i += 32) vec[i] = s[i];
   if (!is_k) return;
   // this head's cache row at pos (kv_row_bytes per row)
@@ -170,11 +172,12 @@ cudaError_t launch_norm_prep(const Launch& L, float* h, const float* res, const 
 
 cudaError_t launch_qk_post(const Launch& L, float* q, float* k, const float* v, int M, int n_q, int n_kv, int hd,
                            const float* q_norm, const float* k_norm, float eps, const float* cos_tab,
-                           const float* sin_tab, const int* pos0_dev, KvCache kv) {
+                           const float* sin_tab, const int* pos0_dev, KvCache kv, const float* tok_cos,
+                           const float* tok_sin) {
   const int wpb = 4;
   const int heads = n_q + n_kv;
   return launch_k(L, qk_post_kernel, dim3(M, (heads + wpb - 1) / wpb), dim3(wpb * 32), (size_t)wpb * hd * 4, q, k, v,
-                  n_q, n_kv, hd, q_norm, k_norm, eps, cos_tab, sin_tab, pos0_dev, kv);
+                  n_q, n_kv, hd, q_norm, k_norm, eps, cos_tab, sin_tab, pos0_dev, kv, tok_cos, tok_sin);
 }
 
 cudaError_t launch_swiglu_prep(const Launch& L, const float* gate, const float* up, int M, int I, float deadzone,

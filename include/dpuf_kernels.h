@@ -150,8 +150,9 @@ DPUF_EXPORT void dpuf_embed_qr_had6_f32(
  *         modes, or device errors (reference dpuf_engine.c:1208-1354).
  * forward_*: 0 on success; -1 null argument, -2 n_tokens outside [1, 256], -3 position
  *         outside [0, max_seq_len) (reference dpuf_engine.c:1639-1641); this engine adds
- *         -4 for a CUDA error and -5 for an argument it does not support (M-RoPE,
- *         pos_t other than pos0 + m; embeds_in and deepstack_in are supported).  logits_out is host memory: [vocab] floats when
+ *         -4 for a CUDA error and -5 for an argument it does not support (embeds_in,
+ *         deepstack_in, pos_t/h/w and M-RoPE are all supported); -3 also for a rotary
+ *         position outside the RoPE table.  logits_out is host memory: [vocab] floats when
  *         only_last_logits == 1, [n_tokens][vocab] when 0, unused when 2. */
 DPUF_EXPORT void* dpuf_engine_create(
     const DpufModelConfig* cfg,

@@ -136,6 +136,7 @@ def main() -> None:
                 else:
                     os.environ[k] = v
     eng_out["embeds_in"] = embeds_golden(lib)
+    eng_out["rope_positions"] = rope_golden(lib)
     (HERE / "engine.json").write_text(json.dumps(eng_out, indent=1))
     np.savez_compressed(HERE / "engine_logits.npz", **eng_logits)
 
@@ -190,6 +191,50 @@ def embeds_golden(lib) -> dict:
     assert f(ref.h, 1, one.ctypes.data, rows, None, None, None, None, arr1, 1, last.ctypes.data) == 0
     rec["deepstack_token_digest"] = sc.logits_digest(last)
     ref.close()
+    return rec
+
+
+def rope_golden(lib) -> dict:
+    """forward_batch_ex rotary positions (dpuf_engine.c:1679-1696): pos_t = pos0 + m + 5 on a
+    model without M-RoPE; on an M-RoPE model (sections MROPE_SECTION) distinct t/h/w rows, then a
+    one-token call with distinct and one with equal t/h/w.  Reference engine, 8 threads."""
+    shape, seed, rows = sc.EMBEDS_CASE
+    f = lib.dpuf_engine_forward_batch_ex
+    f.restype = ctypes.c_int32
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p] + \
+        [ctypes.c_void_p] * 4 + [ctypes.c_int32, ctypes.c_void_p]
+    rec = {}
+    for mrope in (0, 1):
+        m = mdl.SyntheticModel(mdl.SHAPES[shape], seed=seed, norm_jitter=0.1)
+        if mrope:
+            m.cfg.has_mrope = 1
+            for i, v in enumerate(sc.MROPE_SECTION):
+                m.cfg.mrope_section[i] = v
+        ref = orc.RefEngine(m, n_threads=8)
+        V = m.shape.vocab
+        ids = mdl.prompt_ids(rows, V, seed).astype(np.int32)
+        allp = np.empty((rows, V), np.float32)
+        last = np.empty((1, V), np.float32)
+        ref.reset()
+        if not mrope:
+            pt = (np.arange(rows) + 5).astype(np.int32)
+            assert f(ref.h, rows, ids.ctypes.data, 0, None, pt.ctypes.data, None, None, None, 0, allp.ctypes.data) == 0
+            rec["shifted_all_digest"] = sc.logits_digest(allp)
+        else:
+            t, h, w = sc.rope_positions(rows)
+            assert f(ref.h, rows, ids.ctypes.data, 0, None, t.ctypes.data, h.ctypes.data, w.ctypes.data, None, 0,
+                     allp.ctypes.data) == 0
+            rec["mrope_all_digest"] = sc.logits_digest(allp)
+            one = np.array([int(np.argmax(allp[-1]))], np.int32)
+            t1, h1, w1 = (np.array([v], np.int32) for v in (rows, 2, 7))
+            assert f(ref.h, 1, one.ctypes.data, rows, None, t1.ctypes.data, h1.ctypes.data, w1.ctypes.data, None, 1,
+                     last.ctypes.data) == 0
+            rec["mrope_token_digest"] = sc.logits_digest(last)
+            e1 = np.array([rows + 1], np.int32)
+            assert f(ref.h, 1, one.ctypes.data, rows + 1, None, e1.ctypes.data, e1.ctypes.data, e1.ctypes.data, None,
+                     1, last.ctypes.data) == 0
+            rec["mrope_equal_digest"] = sc.logits_digest(last)
+        ref.close()
     return rec
 
 

@@ -89,6 +89,15 @@ def deepstack_input(rows: int, hidden: int) -> list:
     return [(rng.standard_normal((rows, hidden)) * 0.02).astype(np.float32) for _ in range(3)]
 
 
+MROPE_SECTION = (4, 6, 6)
+
+
+def rope_positions(rows: int):
+    """pos_t / pos_h / pos_w of the M-RoPE prefill: distinct for most rows, equal for row 0."""
+    m = np.arange(rows, dtype=np.int32)
+    return m.copy(), (m // 3).astype(np.int32), (m % 4).astype(np.int32)
+
+
 def had_embed_ids(case_idx: int, rows: int) -> np.ndarray:
     """Row ids for the mode-13/14 embedding fixtures: the first and last rows (the last tile may
     be ragged) and seeded random rows."""

@@ -262,8 +262,7 @@ def test_embeds_in_matches_reference(eng_mod):
     """forward_batch_ex with embeds_in (dpuf_engine.c:1658-1672): every row from the caller's
     embeddings, then greedy steps from ids; and a mixed call whose ids -1 take their rows from
     embeds_in; DeepStack rows added after layers 0 and 2 (dpuf_engine.c:2046-2054), for 12 rows
-    and for one token.  Logits equal the reference engine's (digests in engine.json).  Rotary
-    positions other than pos0 + m stay rejected (-5)."""
+    and for one token.  Logits equal the reference engine's (digests in engine.json)."""
     import ctypes
 
     from dpuf_b200 import model as mdl
@@ -306,10 +305,61 @@ def test_embeds_in_matches_reference(eng_mod):
         arr1 = (ctypes.c_void_p * 3)(ds[1].ctypes.data, ds[0].ctypes.data, None)
         assert f(e._handle, 1, one.ctypes.data, rows, None, None, None, None, arr1, 1, last.ctypes.data) == 0
         assert sc.logits_digest(last) == g["deepstack_token_digest"]
-        # a negative id without embeddings; a shifted rotary position
+        # a negative id without embeddings
         assert f(e._handle, rows, mixed.ctypes.data, 0, None, None, None, None, None, 1, last.ctypes.data) == -1
-        shifted = (np.arange(rows) + 3).astype(np.int32)
-        assert f(e._handle, rows, None, 0, emb.ctypes.data, shifted.ctypes.data, None, None, None, 1,
-                 last.ctypes.data) == -5
     finally:
         e.close()
+
+
+def test_rope_positions_match_reference(eng_mod):
+    """forward_batch_ex rotary positions (dpuf_engine.c:1679-1696): pos_t shifted from the cache
+    position on a model without M-RoPE; M-RoPE t/h/w rows (the reference's own cos/sin
+    formula, eng_compute_mrope_cos_sin) for 12 tokens and for one token, and equal t/h/w (the
+    tables' row).  Logits equal the reference engine's."""
+    import ctypes
+
+    from dpuf_b200 import model as mdl
+
+    g = golden_engine()["rope_positions"]
+    shape, seed, rows = sc.EMBEDS_CASE
+    for mrope in (0, 1):
+        m = mdl.SyntheticModel(mdl.SHAPES[shape], seed=seed, norm_jitter=0.1)
+        if mrope:
+            m.cfg.has_mrope = 1
+            for i, v in enumerate(sc.MROPE_SECTION):
+                m.cfg.mrope_section[i] = v
+        e = eng_mod.CudaTransformerEngine(m)
+        try:
+            f = e.lib.dpuf_engine_forward_batch_ex
+            f.restype = ctypes.c_int32
+            f.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p] + \
+                [ctypes.c_void_p] * 4 + [ctypes.c_int32, ctypes.c_void_p]
+            V = m.shape.vocab
+            ids = mdl.prompt_ids(rows, V, seed).astype(np.int32)
+            allp = np.empty((rows, V), np.float32)
+            last = np.empty((1, V), np.float32)
+            e.reset_cache()
+            if not mrope:
+                pt = (np.arange(rows) + 5).astype(np.int32)
+                assert f(e._handle, rows, ids.ctypes.data, 0, None, pt.ctypes.data, None, None, None, 0,
+                         allp.ctypes.data) == 0
+                assert sc.logits_digest(allp) == g["shifted_all_digest"]
+                far = np.full(rows, m.shape.max_seq, np.int32)
+                assert f(e._handle, rows, ids.ctypes.data, 0, None, far.ctypes.data, None, None, None, 1,
+                         last.ctypes.data) == -3
+                continue
+            t, h, w = sc.rope_positions(rows)
+            assert f(e._handle, rows, ids.ctypes.data, 0, None, t.ctypes.data, h.ctypes.data, w.ctypes.data, None, 0,
+                     allp.ctypes.data) == 0
+            assert sc.logits_digest(allp) == g["mrope_all_digest"]
+            one = np.array([int(np.argmax(allp[-1]))], np.int32)
+            t1, h1, w1 = (np.array([v], np.int32) for v in (rows, 2, 7))
+            assert f(e._handle, 1, one.ctypes.data, rows, None, t1.ctypes.data, h1.ctypes.data, w1.ctypes.data, None,
+                     1, last.ctypes.data) == 0
+            assert sc.logits_digest(last) == g["mrope_token_digest"]
+            e1 = np.array([rows + 1], np.int32)
+            assert f(e._handle, 1, one.ctypes.data, rows + 1, None, e1.ctypes.data, e1.ctypes.data, e1.ctypes.data,
+                     None, 1, last.ctypes.data) == 0
+            assert sc.logits_digest(last) == g["mrope_equal_digest"]
+        finally:
+            e.close()
