@@ -13,10 +13,14 @@ A step is one greedy decode token at batch 1 (the reference CLI's decode loop, d
           with CUDA events over 8 weight copies (> L2), bytes = tile bytes per launch
   cpu_baseline  the reference's own AVX2/OpenMP engine (built from its sources) on this host's
           cores, same model and prompt, a bounded number of decode steps
-Multi-GPU (torchrun, --gpus N): data parallel, one independent sequence per GPU (weak scaling);
-the time is the max over ranks.  With --tp the N ranks decode ONE sequence with tensor
-parallelism (every projection and the LM head split over all GPUs' CTAs, outputs exchanged
-through peer memory inside the persistent kernel; strong scaling).
+Model: the random-init model is written once as a DPUF0001 container by a separate process
+(`python -m dpuf_b200.container write`) and both arms map that same file.
+Multi-GPU (torchrun, --gpus N): the N ranks decode ONE sequence with tensor parallelism (every
+projection and the LM head split over all GPUs' CTAs, outputs exchanged through peer memory
+inside the persistent kernel; strong scaling); every rank first records the same sequence on its
+GPU alone and the line's tp_parity says whether ids and logits were bit-identical (rank 0 exits
+non-zero if not).  With --dp each GPU decodes its own sequence instead (weak scaling).  Times
+are the max over ranks.
 """
 from __future__ import annotations
 
@@ -49,60 +53,79 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of one GPU, sampled through NVML every 5 ms
+    from a background thread while the timed region runs (plus one sample at its start).  The
+    GPU is found by the PCI bus id of the CUDA device, so the sampler follows torchrun's and
+    CUDA_VISIBLE_DEVICES' device numbering."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
-        self.thread = None
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []  # (sm MHz, reasons bitmask)
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        self._h = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        try:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except pynvml.NVMLError:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _sample(self):
+        nv = self._nvml
+        self.samples.append((float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)),
+                             int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))))
+
+    def _run(self):
+        while not self._stop.wait(0.005):
+            try:
+                self._sample()
+            except Exception as e:  # noqa: BLE001 - a sampling failure must not end the run
+                self.error = str(e)
+                return
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            self._h = self._handle()
+            self.max_mhz = float(self._nvml.nvmlDeviceGetMaxClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # noqa: BLE001
+            self.error = str(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread:
-                self.thread.join(timeout=2)
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=2)
+        try:
+            if self._h is not None:
+                self._sample()
+        except Exception:  # noqa: BLE001
+            pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "NVML, 5 ms"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def dist_setup(n_gpus: int):
@@ -518,6 +541,63 @@ def decode_roofline(wbytes: int, step_s: float, hbm_peak: float, peak_kind: str)
             "traffic_note": "dram bytes per algorithmic byte from the 0.6B-shape ncu capture, times the 8B step bytes"}
 
 
+MODEL_FORMAT = "v1"  # bump when the synthetic model or the container layout changes
+
+
+def cache_dir() -> pathlib.Path:
+    """Where the benchmark's .dpuf model files live: env DPUF_BENCH_CACHE, else /dev/shm when it
+    has room for two 8B models, else .bench_cache/ in the repository."""
+    env = os.environ.get("DPUF_BENCH_CACHE")
+    if env:
+        return pathlib.Path(env)
+    try:
+        st = os.statvfs("/dev/shm")
+        if st.f_bavail * st.f_frsize > 12 * 2**30:
+            return pathlib.Path("/dev/shm/dpuf_bench")
+    except OSError:
+        pass
+    return REPO / ".bench_cache"
+
+
+def model_file(shape_name: str, seed: int = 0) -> pathlib.Path:
+    """The random-init model `shape_name` as a DPUF0001 container, written once by a separate
+    process (python -m dpuf_b200.container write), so that the process that reads it - the CPU
+    reference arm in particular - maps no library of this package."""
+    path = cache_dir() / f"{shape_name}-seed{seed}-{MODEL_FORMAT}.dpuf"
+    if not path.exists():
+        env = dict(os.environ)
+        env.pop("OMP_NUM_THREADS", None)
+        subprocess.run([sys.executable, "-m", "dpuf_b200.container", "write", str(path), "--shape", shape_name,
+                        "--seed", str(seed)], cwd=str(REPO), env=env, check=True, stdout=subprocess.DEVNULL)
+    return path
+
+
+def shared_model_file(shape_name: str, world: int, rank: int) -> pathlib.Path:
+    """model_file() made by rank 0 while the other ranks wait at a barrier."""
+    if rank == 0:
+        path = model_file(shape_name)
+    barrier(world)
+    if rank != 0:
+        path = model_file(shape_name)
+    return path
+
+
+def bench_config(shape, world: int, parallelism: str) -> dict:
+    """The `config` object of both arms' lines (same workload, same keys)."""
+    return {"workload": f"{shape.name}-shape random-init mode-12 .dpuf, pp32 then batch-1 greedy decode",
+            "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab, "prompt": 32,
+            "batch": 1, "kv": "fp32", "parallelism": parallelism, "n_gpus": world,
+            "l2": f"weights {shape.weight_bytes_per_token() / 1e9:.2f} GB > 126 MB L2: every step streams them from HBM"}
+
+
+def cpu_threads() -> int:
+    """Threads for the reference CPU engine: every core this process may use (the engine caps
+    its team at 32, dpuf_engine.c:1220)."""
+    from oracle import oracle as orc
+
+    return min(32, orc.host_threads())
+
+
 def cpu_baseline(m, prompt, n_steps: int, threads: int):
     from oracle import oracle as orc
 
@@ -534,29 +614,36 @@ def cpu_baseline(m, prompt, n_steps: int, threads: int):
         nxt = int(np.argmax(lg))
         pos += 1
     dt = time.perf_counter() - t0
+    used = ref.threads
     ref.close()
-    return {"value": round(n_steps / dt, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-            "sample": f"{n_steps} greedy decode steps after pp32 on the same 8B-shaped model, "
-                      f"reference AVX2/OpenMP engine, {orc.cpu_model_string()}"}
+    return {"value": round(n_steps / dt, 3), "unit": "tok/s", "cores": used, "kind": "reference",
+            "sample": f"{n_steps} greedy decode steps after pp32 on the same .dpuf model, reference "
+                      f"AVX2/OpenMP engine with {used} OpenMP threads, {orc.cpu_model_string()}"}
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU engine on this host, same workload and metric."""
-    from dpuf_b200 import model as mdl
+    """--impl reference: the reference's CPU engine (oracle/_ref/libdpuf_avx2.so, built from its
+    unmodified sources) on this host, through its own C ABI, over the same .dpuf file as the
+    GPU arm: same workload, metric and config.  This process maps no library of this package:
+    the model file is written by a separate process and read here with numpy."""
+    from dpuf_b200 import container, model as mdl
     from oracle import oracle as orc
 
+    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    parallelism = ("single" if world == 1 else (f"dp{world}" if args.dp else f"tp{world}"))
     if rank != 0:
         return
-    cfg = {"workload": "qwen3-8b-shape random-init mode-12, pp32 then batch-1 greedy decode", "prompt": 32,
-           "batch": 1, "kv": "fp32"}
     if not orc.RefEngine.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdpuf_avx2.so not built "
                                                               "(needs the reference sources at build time)"}))
         return
-    threads = min(32, orc.host_threads())
-    m = mdl.SyntheticModel(mdl.QWEN3_8B, seed=0)
-    prompt = mdl.prompt_ids(32, m.shape.vocab, 0)
+    m = container.DpufFile(model_file(shape.name))
+    threads = cpu_threads()
+    prompt = mdl.prompt_ids(32, shape.vocab, 0)
     ref = orc.RefEngine(m, n_threads=threads)
+    used = ref.threads
+    ref.reset()
+    ref.forward(prompt, 0, 1)  # first touch of the mapped weights
     ref.reset()
     t0 = time.perf_counter()
     lg = ref.forward(prompt, 0, 1)[0]
@@ -576,37 +663,69 @@ def run_reference(args, world, rank):
     print(json.dumps({
         "impl": "reference", "metric": "decode_tok_per_s", "value": round(v, 3), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4->f32",
-        "data": "synthetic random-init weights ~N(0,0.02), seed-0 prompt", "config": cfg,
+        "higher_is_better": True, "scaling": "weak" if args.dp else "strong", "vs_baseline": None,
+        "dtype": "int8xint4->f32", "data": "synthetic random-init weights ~N(0,0.02), seed-0 prompt",
+        "config": bench_config(shape, world, parallelism),
         "prefill": {"tok_per_s": round(32 / pp_s, 3)},
-        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                         "sample": f"{args.steps} decode steps after pp32, {orc.cpu_model_string()}"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": used, "kind": "reference",
+                         "sample": f"{args.steps} decode steps after pp32, {used} OpenMP threads, "
+                                   f"{orc.cpu_model_string()}"},
         "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def greedy_record(eng, prompt, n_logit_steps: int, n_greedy: int):
+    """pp(prompt) plus n_logit_steps forward_token steps with host logits (all kept), then
+    n_greedy device-fed greedy steps (ids kept): the sequence the parity check compares."""
+    eng.reset_cache()
+    lg = eng.forward_batch(prompt, 0)[0]
+    logits = [lg.copy()]
+    nxt, pos = int(np.argmax(lg)), len(prompt)
+    ids = [nxt]
+    for _ in range(n_logit_steps):
+        lg = eng.forward_token(nxt, pos)
+        logits.append(lg.copy())
+        nxt = int(np.argmax(lg))
+        ids.append(nxt)
+        pos += 1
+    g, _ = eng.decode_greedy(nxt, pos, n_greedy)
+    return ids + [int(x) for x in g], np.stack(logits)
 
 
 def run_dpuf(args, world, rank, local):
     import torch
 
-    from dpuf_b200 import engine, model as mdl
+    from dpuf_b200 import container, engine, model as mdl
 
     torch.cuda.set_device(local)
     hbm_peak, peak_kind = peaks()
     shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    tp = world > 1 and not args.dp
+    parallelism = "single" if world == 1 else (f"tp{world}" if tp else f"dp{world}")
     t_build = time.perf_counter()
-    m = mdl.SyntheticModel(shape, seed=0)
+    m = container.DpufFile(shared_model_file(shape.name, world, rank))
     t_build = time.perf_counter() - t_build
-    eng = engine.CudaTransformerEngine(m)
-    lib = eng.lib
-    tp = args.tp and world > 1
-    if tp:
-        eng.tp_attach(rank, world, engine.torch_all_gather())
     # data parallel: each rank decodes its own sequence (rank 0 uses the seed-0 prompt); tensor
     # parallel: all ranks decode the seed-0 sequence together
     prompt = mdl.prompt_ids(32, shape.vocab, 0 if tp else rank)
     n_total = args.warmup + args.steps
     if 32 + 2 * n_total + 8 > shape.max_seq:
         raise SystemExit("steps + warmup exceed the 2304-position context")
+
+    # ---- tensor parallel: every rank first records the sequence on its GPU alone (the 1-GPU
+    # reference of the parity check), then joins the split engine and records it again
+    parity = None
+    ids_1 = None
+    if tp:
+        solo = engine.CudaTransformerEngine(m)
+        ids_1, lg_1 = greedy_record(solo, prompt, 4, n_total)
+        solo.close()
+    eng = engine.CudaTransformerEngine(m)
+    lib = eng.lib
+    if tp:
+        eng.tp_attach(rank, world, engine.torch_all_gather())
+        ids_n, lg_n = greedy_record(eng, prompt, 4, n_total)
+        parity = ids_n == ids_1 and np.array_equal(lg_n.view(np.uint32), lg_1.view(np.uint32))
 
     # ---- pp32 (prefill) through the C ABI
     eng.reset_cache()
@@ -618,7 +737,7 @@ def run_dpuf(args, world, rank, local):
     pp_s = time.perf_counter() - t0
     first = int(np.argmax(lg))
 
-    # ---- device-timed decode (value)
+    # ---- device-timed decode (value): W warm-up steps, then K steps in one call
     ids = np.zeros(n_total, np.int32)
     ms = ctypes.c_float()
     rc = lib.dpuf_cuda_decode_greedy(eng._handle, first, 32, args.warmup, ids.ctypes.data, ctypes.byref(ms))
@@ -627,18 +746,20 @@ def run_dpuf(args, world, rank, local):
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("decode")
-        rc = lib.dpuf_cuda_decode_greedy(eng._handle, int(ids[args.warmup - 1]) if args.warmup else first,
-                                         32 + args.warmup, args.steps, ids[args.warmup:].ctypes.data,
-                                         ctypes.byref(ms))
+        rc = lib.dpuf_cuda_decode_greedy(eng._handle, int(ids[args.warmup - 1]), 32 + args.warmup, args.steps,
+                                         ids[args.warmup:].ctypes.data, ctypes.byref(ms))
         torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
     if rc != 0:
         raise RuntimeError(engine.last_error())
     barrier(world)
     value, dev_ms = dp_value(float(ms.value), args.steps, world)
-    if tp:  # one sequence: the job's tokens are the steps
-        value /= world
+    if tp:
+        value /= world  # one sequence: the job's tokens are the steps
+        # the timed run (pp32 id, then device-fed steps from position 32) is the same greedy
+        # sequence as the recording (pp32 id, 4 host-logit steps, device-fed steps)
+        timed = [first] + [int(x) for x in ids]
+        parity = parity and timed == ids_1[:len(timed)]
+        parity = allreduce_max(0.0 if parity else 1.0, world) == 0.0
 
     if args.no_extras:
         persistent = eng.persistent_decode()[0]
@@ -646,9 +767,9 @@ def run_dpuf(args, world, rank, local):
         if rank == 0:
             print(json.dumps({"metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s",
                               "model": shape.name, "ms_per_step": round(dev_ms / args.steps, 4),
-                              "persistent": persistent}), flush=True)
-        return
-    # ---- e2e through the drop-in C ABI with host buffers
+                              "persistent": persistent, "tp_parity": parity}), flush=True)
+        return 0 if parity is not False else 1
+    # ---- e2e through the drop-in C ABI with host buffers (token id in, logits out)
     eng.reset_cache()
     lg = eng.forward_batch(prompt, 0)[0]
     nxt = int(np.argmax(lg))
@@ -674,30 +795,25 @@ def run_dpuf(args, world, rank, local):
     if tp:  # each GPU streams its share of the weights
         wbytes //= world
     step_s = dev_ms * 1e-3 / args.steps
+    eng.close()
     if rank == 0:
         roof = decode_roofline(wbytes, step_s, hbm_peak, peak_kind) if persistent else None
         gemv = gemv_roofline(hbm_peak, peak_kind)
         if roof is None:
             roof = gemv
-        from oracle import oracle as orc
-
-        cpu = cpu_baseline(m, prompt, n_steps=24, threads=min(32, orc.host_threads()))
-    eng.close()
+        cpu = cpu_baseline(m, prompt, n_steps=24, threads=cpu_threads())
     if rank != 0:
-        return
+        return 0 if parity is not False else 1
     clocks = clk.summary()
     line = {
         "metric": "decode_tok_per_s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak" if (world > 1 and not tp) else "strong", "vs_baseline": None,
         "dtype": "int8xint4->f32",
-        "data": "synthetic random-init weights ~N(0,0.02) (bf16-rounded, mode-12 packed), seed-0 prompt",
-        "config": {"workload": f"{shape.name}-shape random-init mode-12, pp32 then batch-1 greedy decode",
-                   "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab, "prompt": 32,
-                   "batch_per_gpu": 1,
-                   "kv": "fp32", "parallelism": (f"tp{world}" if tp else f"dp{world}") if world > 1 else "single",
-                   "l2": "weights 4.26 GB > 126 MB L2: every step streams them from HBM"},
-        "step_roofline": {"bytes_per_step": wbytes, "achieved_gbs": round(wbytes / step_s / 1e9, 1),
+        "data": "synthetic random-init weights ~N(0,0.02) (bf16-rounded, mode-12 packed .dpuf), seed-0 prompt",
+        "config": bench_config(shape, world, parallelism),
+        "tp_parity": parity,
+        "step_roofline": {"bytes_per_step_per_gpu": wbytes, "achieved_gbs": round(wbytes / step_s / 1e9, 1),
                           "frac": round(wbytes / step_s / 1e9 / hbm_peak, 4), "peak": hbm_peak,
                           "peak_kind": peak_kind},
         "roofline": roof,
@@ -710,12 +826,17 @@ def run_dpuf(args, world, rank, local):
         "cpu_baseline": cpu,
         "clocks": clocks,
         "gpu_launches": None,
-        "model_build_s": round(t_build, 1),
+        "model_load_s": round(t_build, 1),
     }
+    if tp:
+        line["tp_parity_check"] = ("every rank's greedy ids (pp32, 4 host-logit steps, then the device-fed steps "
+                                   "incl. the timed ones) and its logits (pp32 and the 4 steps) bit-identical to "
+                                   "the same sequence on its GPU alone")
     # the timed decode_greedy call is one launch of the persistent kernel (all steps), or the
     # per-step kernels of every step
     line["gpu_launches"] = 1 if persistent else steps_launch_count(shape) * args.steps
     print(json.dumps(line), flush=True)
+    return 0 if parity is not False else 1
 
 
 def steps_launch_count(shape) -> int:
@@ -743,8 +864,10 @@ def main():
     ap.add_argument("--serve-kv", default="f16", choices=["f16", "f32", "q8"],
                     help="KV cache of the serving run: fp16 (the configuration's), fp32 (the reference's "
                          "kv_type 0) or q8 (the reference's kv_type 1)")
-    ap.add_argument("--tp", action="store_true",
-                    help="with --gpus N > 1: tensor parallelism over the N GPUs (one sequence) instead of data parallel")
+    ap.add_argument("--dp", action="store_true",
+                    help="with --gpus N > 1: N independent data-parallel replicas (one sequence each) instead of "
+                         "the default tensor parallelism over the N GPUs (one sequence)")
+    ap.add_argument("--tp", action="store_true", help="(the default for --gpus N > 1) tensor parallelism")
     ap.add_argument("--trace", action="store_true",
                     help="phase trace of the persistent decode kernel (per-layer critical path), not a benchmark")
     ap.add_argument("--no-extras", action="store_true",
@@ -773,16 +896,19 @@ def main():
         if args.serve:
             run_serve_config(args, *peaks())
         return
+    rc = 0
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
         else:
-            run_dpuf(args, world, rank, local)
+            rc = run_dpuf(args, world, rank, local) or 0
     finally:
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
+    if rc:
+        sys.exit(rc)
 
 
 if __name__ == "__main__":

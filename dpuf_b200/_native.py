@@ -31,6 +31,7 @@ CUDA_SOURCES = [
     "expf_table.cu",
     "kernels_mode12.cu",
     "kernels_gemv.cu",
+    "kernels_gemv_wg.cu",
     "kernels_gemm_tc.cu",
     "kernels_layer.cu",
     "kernels_attn.cu",

@@ -51,6 +51,12 @@ constexpr int kGemvMaxCtas = 600;
 constexpr int kMaxTp = 8;  // tensor-parallel ranks of the persistent decode kernel
 size_t gemv_split_pairs_bytes(int max_cols);
 cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split);
+// M == 1 with every consumer warp owning whole 8-row groups (kernels_gemv_wg.cu): one CTA per SM,
+// per-warp cp.async.bulk rings.  launch_gemv uses it unless env DPUF_CUDA_GEMV=mma.  *err
+// (optional, device) becomes 1 if a wait gives up.
+cudaError_t configure_gemv_wg_kernel();
+size_t gemv_wg_smem_bytes(int cols, int n_x);
+cudaError_t launch_gemv_wg(const Launch& L, const LinJobs& jobs, const int* skip_flag, int* err);
 // M > 1: exact integer-dot GEMM on CUDA cores (reference order per (token,row)).
 cudaError_t launch_gemm_exact(const Launch& L, const LinJobs& jobs, int M);
 // M > 1 on the tensor cores (kernels_gemm_tc.cu): per-block int8 MMA into TMEM, then the same

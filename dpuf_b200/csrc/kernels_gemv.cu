@@ -31,6 +31,8 @@
 // Bank layout.  Within a stage the nibbles of group g start at g * (KB*128 + 32) bytes; the B
 // load of one MMA (lane (g, t) reads word 8t + g of a block) covers 32 consecutive words.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "kernels.cuh"
 
@@ -372,6 +374,7 @@ cudaError_t configure_gemv_kernels() {
   if (e == cudaSuccess && dev >= 0 && dev < 64)
     e = cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess) e = set_max_dyn_smem(gemv_stream_kernel);
+  if (e == cudaSuccess) e = configure_gemv_wg_kernel();
   return e;
 }
 
@@ -380,6 +383,21 @@ size_t gemv_split_pairs_bytes(int max_cols) {
 }
 
 cudaError_t launch_gemv(const Launch& L, const LinJobs& jobs, const int* skip_flag, const GemvSplit* split) {
+  static const bool use_mma = [] {
+    const char* v = getenv("DPUF_CUDA_GEMV");
+    return v && strcmp(v, "mma") == 0;
+  }();
+  if (!use_mma) {
+    int n_x = 0;
+    const void* seen[kMaxJobs];
+    for (int i = 0; i < jobs.n; i++) {
+      bool dup = false;
+      for (int k = 0; k < n_x; k++) dup = dup || seen[k] == jobs.j[i].act.q8;
+      if (!dup) seen[n_x++] = jobs.j[i].act.q8;
+    }
+    if (gemv_wg_smem_bytes(jobs.j[0].w.cols, n_x) <= (size_t)kMaxDynSmem)
+      return launch_gemv_wg(L, jobs, skip_flag, nullptr);
+  }
   GemvArgs A;
   A.J = jobs;
   A.unit_prefix[0] = 0;

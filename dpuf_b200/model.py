@@ -134,7 +134,70 @@ def _stream_id(name: str) -> int:
     return zlib.crc32(name.encode("utf-8"))
 
 
-class SyntheticModel:
+class ModelData:
+    """A mode-12 model in host memory: `blobs` (tensor name -> packer.BlobView), `norms` (name ->
+    fp32 gains) and `shape`, with the C-ABI descriptors built over them (`create_args`).  The
+    arrays must stay alive while an engine created from them is (the reference engine borrows
+    them; this library's engine copies them at create)."""
+
+    shape: ModelShape
+    blobs: dict
+    norms: dict
+    has_qk_norm: bool = True
+
+    def desc(self, name: str) -> DpufWeightDesc:
+        bv = self.blobs[name]
+        d = DpufWeightDesc()
+        d.mode = bv.mode
+        d.rows = bv.rows
+        d.cols = bv.cols
+        d.n_tiles = bv.n_tiles
+        d.tensor_base = bv.tiles.ctypes.data
+        d.tile_offsets = bv.tile_offsets.ctypes.data
+        d.col_scale = None
+        d.sign_bits = bv.sign_bits.ctypes.data
+        return d
+
+    def _build_descs(self) -> None:
+        s = self.shape
+        cfg = DpufModelConfig()
+        cfg.hidden_size = s.hidden
+        cfg.intermediate_size = s.inter
+        cfg.num_layers = s.layers
+        cfg.num_q_heads = s.n_q
+        cfg.num_kv_heads = s.n_kv
+        cfg.head_dim = s.head_dim
+        cfg.vocab_size = s.vocab
+        cfg.max_seq_len = s.max_seq
+        cfg.has_qk_norm = 1 if self.has_qk_norm else 0
+        cfg.rms_eps = s.rms_eps
+        cfg.rope_theta = s.rope_theta
+        cfg.n_threads = 8
+        cfg.kv_type = 0
+        self.cfg = cfg
+        arr = (DpufLayerWeights * s.layers)()
+        keys = ["w_q", "w_k", "w_v", "w_o", "w_gate", "w_up", "w_down"]
+        for l in range(s.layers):
+            lw = arr[l]
+            lw.attn_norm = self.norms[f"blk.{l}.attn_norm.weight"].ctypes.data
+            if self.has_qk_norm:
+                lw.attn_q_norm = self.norms[f"blk.{l}.attn_q_norm.weight"].ctypes.data
+                lw.attn_k_norm = self.norms[f"blk.{l}.attn_k_norm.weight"].ctypes.data
+            lw.ffn_norm = self.norms[f"blk.{l}.ffn_norm.weight"].ctypes.data
+            for key, (suffix, _, _) in zip(keys, s.linear_shapes()):
+                setattr(lw, key, self.desc(f"blk.{l}.{suffix}"))
+        self.layers = arr
+        self.tok = self.desc("token_embd.weight")
+        self.lm = self.desc("output.weight" if "output.weight" in self.blobs else "token_embd.weight")
+        self.out_norm = self.norms["output_norm.weight"]
+
+    def create_args(self):
+        """Arguments of dpuf_engine_create (reference dpuf_kernels.h:316-322)."""
+        return (ctypes.byref(self.cfg), self.layers, ctypes.byref(self.tok), ctypes.byref(self.lm),
+                self.out_norm.ctypes.data)
+
+
+class SyntheticModel(ModelData):
     """Random-init model in mode-12 layout held in host memory, with C-ABI descriptors."""
 
     def __init__(self, shape: ModelShape, seed: int = 0, norm_jitter: float = 0.0, n_threads: int | None = None):
@@ -170,56 +233,6 @@ class SyntheticModel:
             norm(f"blk.{l}.attn_q_norm.weight", s.head_dim)
             norm(f"blk.{l}.attn_k_norm.weight", s.head_dim)
         self._build_descs()
-
-    def desc(self, name: str) -> DpufWeightDesc:
-        bv = self.blobs[name]
-        d = DpufWeightDesc()
-        d.mode = bv.mode
-        d.rows = bv.rows
-        d.cols = bv.cols
-        d.n_tiles = bv.n_tiles
-        d.tensor_base = bv.tiles.ctypes.data
-        d.tile_offsets = bv.tile_offsets.ctypes.data
-        d.col_scale = None
-        d.sign_bits = bv.sign_bits.ctypes.data
-        return d
-
-    def _build_descs(self) -> None:
-        s = self.shape
-        cfg = DpufModelConfig()
-        cfg.hidden_size = s.hidden
-        cfg.intermediate_size = s.inter
-        cfg.num_layers = s.layers
-        cfg.num_q_heads = s.n_q
-        cfg.num_kv_heads = s.n_kv
-        cfg.head_dim = s.head_dim
-        cfg.vocab_size = s.vocab
-        cfg.max_seq_len = s.max_seq
-        cfg.has_qk_norm = 1
-        cfg.rms_eps = s.rms_eps
-        cfg.rope_theta = s.rope_theta
-        cfg.n_threads = 8
-        cfg.kv_type = 0
-        self.cfg = cfg
-        arr = (DpufLayerWeights * s.layers)()
-        keys = ["w_q", "w_k", "w_v", "w_o", "w_gate", "w_up", "w_down"]
-        for l in range(s.layers):
-            lw = arr[l]
-            lw.attn_norm = self.norms[f"blk.{l}.attn_norm.weight"].ctypes.data
-            lw.attn_q_norm = self.norms[f"blk.{l}.attn_q_norm.weight"].ctypes.data
-            lw.attn_k_norm = self.norms[f"blk.{l}.attn_k_norm.weight"].ctypes.data
-            lw.ffn_norm = self.norms[f"blk.{l}.ffn_norm.weight"].ctypes.data
-            for key, (suffix, _, _) in zip(keys, s.linear_shapes()):
-                setattr(lw, key, self.desc(f"blk.{l}.{suffix}"))
-        self.layers = arr
-        self.tok = self.desc("token_embd.weight")
-        self.lm = self.desc("token_embd.weight" if s.tied else "output.weight")
-        self.out_norm = self.norms["output_norm.weight"]
-
-    def create_args(self):
-        """Arguments of dpuf_engine_create (reference dpuf_kernels.h:316-322)."""
-        return (ctypes.byref(self.cfg), self.layers, ctypes.byref(self.tok), ctypes.byref(self.lm),
-                self.out_norm.ctypes.data)
 
 
 def prompt_ids(n: int, vocab: int, seed: int = 0) -> np.ndarray:

@@ -3,7 +3,7 @@
 # parity checker and the timed CPU baseline.  Test infrastructure only: nothing in the
 # product links or loads this library.
 #
-#   usage: oracle/build_ref.sh [REF_DIR]        (REF_DIR defaults to /root/reference)
+#   usage: oracle/build_ref.sh REF_DIR     (or env DPUF_REFERENCE_DIR; there is no default)
 #
 # Outputs go only to oracle/_ref/ (git-ignored; it still travels with the repository
 # snapshot to the GPU box).  The reference sources are read where they lie; the only
@@ -20,7 +20,11 @@
 #     pre-include maps calloc to a 64-byte aligned allocation (freeable with free()).
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${1:-/root/reference}"
+REF="${1:-${DPUF_REFERENCE_DIR:-}}"
+if [ -z "$REF" ]; then
+  echo "build_ref: give the reference source directory (argument or DPUF_REFERENCE_DIR)" >&2
+  exit 2
+fi
 OUT="$HERE/_ref"
 if [ ! -f "$REF/dpuf_engine.c" ]; then
   echo "build_ref: reference sources not found at $REF" >&2

@@ -21,7 +21,9 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libdpuf_avx2.so"
-REF_SRC_DEFAULT = pathlib.Path("/root/reference")
+# Where the reference sources are, for rebuilding oracle/_ref: env DPUF_REFERENCE_DIR (no default;
+# without it an existing oracle/_ref build is kept as it is).
+REF_SRC_ENV = "DPUF_REFERENCE_DIR"
 
 
 def build(force: bool = False) -> pathlib.Path:
@@ -33,9 +35,12 @@ def build(force: bool = False) -> pathlib.Path:
     return ORACLE_LIB
 
 
-def build_ref(ref_dir: pathlib.Path = REF_SRC_DEFAULT) -> pathlib.Path | None:
-    """Builds oracle/_ref/libdpuf_avx2.so when the reference sources are present."""
-    if not (ref_dir / "dpuf_engine.c").exists():
+def build_ref(ref_dir: pathlib.Path | None = None) -> pathlib.Path | None:
+    """Builds oracle/_ref/libdpuf_avx2.so from the reference sources at `ref_dir` (default: env
+    DPUF_REFERENCE_DIR).  Without sources, an existing build is returned as it is (or None)."""
+    if ref_dir is None and os.environ.get(REF_SRC_ENV):
+        ref_dir = pathlib.Path(os.environ[REF_SRC_ENV])
+    if ref_dir is None or not (ref_dir / "dpuf_engine.c").exists():
         return REF_LIB if REF_LIB.exists() else None
     subprocess.run(["bash", str(HERE / "build_ref.sh"), str(ref_dir)], check=True, capture_output=True)
     return REF_LIB
@@ -140,6 +145,8 @@ class RefEngine(_EngineBase):
     def __init__(self, model, n_threads: int = 8):
         self.lib = self.lib_()
         self.model = model
+        # the engine runs min(n_threads, 32, omp_get_max_threads()) threads (dpuf_engine.c:1219-1223)
+        self.threads = min(int(n_threads), 32, set_omp_threads(n_threads))
         model.cfg.n_threads = n_threads
         self.h = self.lib.dpuf_engine_create(*model.create_args())
         model.cfg.n_threads = 8
@@ -238,7 +245,21 @@ def cpu_model_string() -> str:
 
 
 def host_threads() -> int:
+    """Host cores this process may run on (its CPU affinity)."""
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def set_omp_threads(n: int) -> int:
+    """Sets the OpenMP thread count of the calling thread in the process's GNU OpenMP runtime
+    (the libgomp.so.1 the reference library links) and returns omp_get_max_threads() as read
+    back.  The reference engine clamps its team to omp_get_max_threads()
+    (dpuf_engine.c:1219-1223), which launchers such as torchrun pin to 1 through
+    OMP_NUM_THREADS; this call overrides that for the CPU baseline."""
+    gomp = ctypes.CDLL("libgomp.so.1")
+    gomp.omp_set_num_threads.argtypes = [ctypes.c_int]
+    gomp.omp_get_max_threads.restype = ctypes.c_int
+    gomp.omp_set_num_threads(int(n))
+    return int(gomp.omp_get_max_threads())
 
 
 def zone_a(logits: np.ndarray, za_tiles: int, margin: float):

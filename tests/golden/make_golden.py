@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this directory from the REFERENCE itself.
 
-Run in a container that has the reference sources (default /root/reference):
-    python tests/golden/make_golden.py [REF_DIR]
+Run in a container that has the reference sources:
+    python tests/golden/make_golden.py REF_DIR      (or env DPUF_REFERENCE_DIR)
 It builds oracle/_ref/libdpuf_avx2.so from the unmodified reference sources
 (oracle/build_ref.sh), imports the reference packer module, and records:
   * pack.json     sha256 of the reference packer's blob for each PACK_CASES input;
@@ -34,7 +34,10 @@ import scenarios as sc  # noqa: E402
 
 
 def main() -> None:
-    ref_dir = pathlib.Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(orc.REF_SRC_ENV, "")
+    if not src:
+        raise SystemExit("give the reference source directory (argument or DPUF_REFERENCE_DIR)")
+    ref_dir = pathlib.Path(src)
     _native.build_pack()
     orc.build_ref(ref_dir)
     sys.path.insert(0, str(ref_dir))
