@@ -188,3 +188,38 @@ void expf_exception_hash(std::vector<uint2>& slots, uint32_t* mask, int* max_pro
 extern "C" __attribute__((visibility("default"))) int64_t dpuf_cuda_prepare_expf_table(void) {
   return (int64_t)dpuf::expf_exception_keys().size();
 }
+
+namespace dpuf {
+namespace {
+
+__global__ void expf_eval_kernel(uint32_t bits0, long long n, float* out, ExpfTable t) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = glibc_expf(__uint_as_float(bits0 + (uint32_t)i), t);
+}
+
+}  // namespace
+}  // namespace dpuf
+
+// The device's glibc-compatible expf (the function the softmax and SwiGLU tails use), evaluated
+// for the `count` consecutive float bit patterns starting at bits_begin into out_dev (device,
+// `count` floats), so that a test can compare it with the host libm over whole input ranges.
+// Uploads the exception table for the call (allocates and frees it); synchronous.  Returns 0,
+// -1 for bad arguments (the range must not pass 0xFFFFFFFF), -4 for a CUDA error.
+extern "C" __attribute__((visibility("default"))) int32_t dpuf_cuda_expf_eval(uint32_t bits_begin, int64_t count,
+                                                                           float* out_dev) {
+  if (!out_dev || count <= 0 || (uint64_t)bits_begin + (uint64_t)count > (1ull << 32)) return -1;
+  std::vector<uint2> slots;
+  dpuf::ExpfTable t{};
+  dpuf::expf_exception_hash(slots, &t.mask, &t.max_probe);
+  uint2* d = nullptr;
+  if (cudaMalloc(&d, slots.size() * sizeof(uint2)) != cudaSuccess) return -4;
+  cudaError_t e = cudaMemcpy(d, slots.data(), slots.size() * sizeof(uint2), cudaMemcpyHostToDevice);
+  t.slots = d;
+  if (e == cudaSuccess) {
+    dpuf::expf_eval_kernel<<<1184, 256>>>(bits_begin, (long long)count, out_dev, t);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(d);
+  return e == cudaSuccess ? 0 : -4;
+}

@@ -13,11 +13,12 @@
 // scales, then 4096 bytes of nibbles: exactly the container's bytes, in two cp.async.bulk
 // copies).
 //
-// Ring.  Every consumer warp has its own kSlots-deep ring of stages with full/empty mbarriers;
-// one producer thread walks the warps round-robin and refills whichever slot has been
-// released, so the CTA keeps kWarps * kSlots * 4.6 KB of weights in flight and a slow warp
-// never stalls the others.  The weights do not depend on the previous kernel, so the stream
-// starts before griddepcontrol.wait (programmatic dependent launch).
+// Ring.  Every warp has its own kSlots-deep ring of stages, one mbarrier each, and issues its own
+// copies: lane 0 requests the first kSlots stages at start and refills a slot with the stage
+// kSlots ahead as soon as the warp has finished with it, so the CTA keeps kWarps * kSlots *
+// 4.6 KB of weights in flight, no thread polls other warps' slots and a slow warp never stalls
+// the others.  The weights do not depend on the previous kernel, so the stream starts before
+// griddepcontrol.wait (programmatic dependent launch).
 //
 // Lanes.  Lane (ri = lane % 8, q = lane / 8) computes row ri's dots of blocks 8q .. 8q+7 of a
 // stage; its four nibble words per block are read starting at chunk q (rotated), so the four
@@ -32,12 +33,12 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kWarps = 12;                    // consumer warps
+constexpr int kWarps = 12;                    // warps, each its own ring
 constexpr int kSlots = 3;                     // ring slots per consumer warp
 constexpr int kKB = 32;                       // blocks per stage
 constexpr int kScBytes = kKB * 16;            // 512: fp16 scales [32][8]
 constexpr int kSlotBytes = kScBytes + kKB * 128;  // 4608
-constexpr int kThreads = (kWarps + 1) * 32;   // 416
+constexpr int kThreads = kWarps * 32;         // 384
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 struct WgArgs {
@@ -155,113 +156,61 @@ DPUF_DEV void stage_chain(const unsigned char* slot, const int8_t* xq, const flo
   (void)lane;
 }
 
+// The copies of one stage (scales, then nibbles) of group `gr` into `dst`, completing on `bar`.
+DPUF_DEV void issue_stage(const GroupRef& gr, int s, int n_blk, unsigned char* dst, uint64_t* bar, uint64_t pol) {
+  const int kb = min(kKB, n_blk - s * kKB);
+  if (gr.n_r == 0) {
+    wg_mbar_arrive(bar);  // empty group: nothing to copy
+    return;
+  }
+  wg_mbar_expect_tx(bar, (unsigned)kb * 144);
+  wg_bulk(dst, gr.base + (size_t)s * kScBytes, (unsigned)kb * 16, bar, pol);
+  wg_bulk(dst + kScBytes, gr.base + (size_t)n_blk * 16 + (size_t)s * (kKB * 128), (unsigned)kb * 128, bar, pol);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) gemv_wg_kernel(WgArgs A, const int* skip_flag) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full[kWarps * kSlots], empty[kWarps * kSlots];
+  __shared__ uint64_t full[kWarps * kSlots];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g0 = (int)((long long)A.n_groups * blockIdx.x / gridDim.x);
   const int g1 = (int)((long long)A.n_groups * (blockIdx.x + 1) / gridDim.x);
   const int n_local = g1 - g0;
-  unsigned char* ring = smem;
+  unsigned char* ring = smem + (size_t)warp * kSlots * kSlotBytes;
+  uint64_t* bars = full + warp * kSlots;
   int8_t* xall = (int8_t*)(smem + (size_t)kWarps * kSlots * kSlotBytes);
-  if (tid == 0) {
-    for (int i = 0; i < kWarps * kSlots; i++) {
-      wg_mbar_init(&full[i], 1);
-      wg_mbar_init(&empty[i], 1);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
   const int n_st = A.n_st, n_blk = A.n_blk;
-
-  if (warp == kWarps) {
-    // ---------------------------------------------------------------- producer
-    if (lane != 0) return;
-    if (skip_flag) {
-      cudaGridDependencySynchronize();
-      if (*(volatile const int*)skip_flag) return;
+  // this warp's stages: groups k = warp, warp + kWarps, ... of the CTA's range, n_st each
+  const int my_groups = warp < n_local ? (n_local - warp + kWarps - 1) / kWarps : 0;
+  const int my_stages = my_groups * n_st;
+  const uint64_t pol = wg_evict_first();
+  if (lane == 0)
+    for (int i = 0; i < kSlots; i++) wg_mbar_init(&bars[i], 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncwarp();
+  const bool skip_mode = skip_flag != nullptr;
+  // issue cursor (lane 0): stage `is` of this warp's group `ik`
+  int ik = 0, is = 0, issued = 0;
+  GroupRef icur{};
+  auto issue_next = [&](int slot) {
+    if (is == 0) icur = group_ref(A, g0 + warp + ik * kWarps);
+    issue_stage(icur, is, n_blk, ring + (size_t)slot * kSlotBytes, &bars[slot], pol);
+    if (++is == n_st) {
+      is = 0;
+      ik++;
     }
-    const uint64_t pol = wg_evict_first();
-    int k[kWarps], s[kWarps], slot[kWarps];
-    unsigned ph[kWarps];
-    GroupRef cur[kWarps];
-    int left = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; w++) {
-      k[w] = w;
-      s[w] = 0;
-      slot[w] = 0;
-      ph[w] = 0;
-      if (w < n_local) {
-        cur[w] = group_ref(A, g0 + w);
-        if (cur[w].n_r == 0) cur[w].base = nullptr;
-      }
-      const int ng = w < n_local ? (n_local - w + kWarps - 1) / kWarps : 0;
-      left += ng * n_st;
-    }
-    unsigned long long t0 = 0;
-    while (left > 0) {
-      bool progressed = false;
-#pragma unroll
-      for (int w = 0; w < kWarps; w++) {
-        if (k[w] >= n_local) continue;
-        const int si = w * kSlots + slot[w];
-        if (!wg_mbar_try(&empty[si], ph[w] ^ 1u)) continue;
-        const int kb = min(kKB, n_blk - s[w] * kKB);
-        unsigned char* dst = ring + (size_t)si * kSlotBytes;
-        if (cur[w].base) {
-          wg_mbar_expect_tx(&full[si], (unsigned)kb * 144);
-          wg_bulk(dst, cur[w].base + (size_t)s[w] * kScBytes, (unsigned)kb * 16, &full[si], pol);
-          wg_bulk(dst + kScBytes, cur[w].base + (size_t)n_blk * 16 + (size_t)s[w] * (kKB * 128), (unsigned)kb * 128,
-                  &full[si], pol);
-        } else {
-          wg_mbar_arrive(&full[si]);  // empty group: nothing to copy, the consumer skips it
-        }
-        if (++slot[w] == kSlots) {
-          slot[w] = 0;
-          ph[w] ^= 1u;
-        }
-        if (++s[w] == n_st) {
-          s[w] = 0;
-          k[w] += kWarps;
-          if (k[w] < n_local) {
-            cur[w] = group_ref(A, g0 + k[w]);
-            if (cur[w].n_r == 0) cur[w].base = nullptr;
-          }
-        }
-        left--;
-        progressed = true;
-      }
-      if (!progressed) {
-        const unsigned long long now = wg_timer();
-        if (t0 == 0) {
-          t0 = now;
-        } else if (now - t0 > kWaitNs) {
-          if (A.err) atomicExch(A.err, 1);
-          break;  // consumers give up on their own limit
-        }
-      } else {
-        t0 = 0;
-      }
-    }
-    // copies still in flight must land before the CTA exits: wait (bounded) on every slot's
-    // last fill
-    const unsigned long long tw = wg_timer();
-    for (int w = 0; w < kWarps; w++)
-      for (int i = 0; i < kSlots; i++) {
-        const int si = w * kSlots + i;
-        // slot i of warp w was last filled in phase ph (if i < slot) or ph ^ 1
-        const unsigned par = i < slot[w] ? ph[w] : (ph[w] ^ 1u);
-        while (!wg_mbar_try(&full[si], par) && wg_timer() - tw < kWaitNs) {
-        }
-      }
-    return;
-  }
-
-  // ------------------------------------------------------------------ consumers
+    issued++;
+  };
+  // the weights do not depend on the previous kernel: the first stages are requested before
+  // waiting for it (programmatic dependent launch), unless a skip flag decides whether to run
+  if (!skip_mode && lane == 0)
+    for (int i = 0; i < kSlots && issued < my_stages; i++) issue_next(i);
   cudaGridDependencySynchronize();
   cudaTriggerProgrammaticLaunchCompletion();
-  if (skip_flag && *(volatile const int*)skip_flag) return;
+  if (skip_mode) {
+    if (*(volatile const int*)skip_flag) return;
+    if (lane == 0)
+      for (int i = 0; i < kSlots && issued < my_stages; i++) issue_next(i);
+  }
   // stage each distinct activation: codes, block scales, block sums
   for (int jx = 0; jx < A.J.n; jx++) {
     bool first = true;
@@ -271,29 +220,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_wg_kernel(WgArgs A, const in
     int8_t* xq = xall + A.x_slot[jx] * A.x_stride;
     float* xs = (float*)(xq + A.cols);
     int* xm = (int*)(xs + n_blk);
-    for (int i = tid; i < A.cols / 16; i += kWarps * 32) ((int4*)xq)[i] = ((const int4*)a.q8)[i];
-    for (int i = tid; i < n_blk; i += kWarps * 32) {
+    for (int i = tid; i < A.cols / 16; i += kThreads) ((int4*)xq)[i] = ((const int4*)a.q8)[i];
+    for (int i = tid; i < n_blk; i += kThreads) {
       xs[i] = a.xs[i];
       xm[i] = a.xm[i];
     }
   }
-  asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
+  __syncthreads();
 
   const int ri = lane & 7, q = lane >> 3;
-  int slot = 0;
+  int slot = 0, consumed = 0;
   unsigned ph = 0;
   bool ok = true;
-  for (int k = warp; k < n_local; k += kWarps) {
-    const GroupRef gr = group_ref(A, g0 + k);
+  for (int k = 0; k < my_groups; k++) {
+    const GroupRef gr = group_ref(A, g0 + warp + k * kWarps);
     const int8_t* xq = xall + gr.xoff;
     const float* xs = (const float*)(xq + A.cols);
     const int* xm = (const int*)(xs + n_blk);
     float acc = 0.0f;
     for (int s = 0; s < n_st; s++) {
-      const int si = warp * kSlots + slot;
-      if (ok && !wg_mbar_try(&full[si], ph)) {
+      if (ok && !wg_mbar_try(&bars[slot], ph)) {
         const unsigned long long t0 = wg_timer();
-        while (!wg_mbar_try(&full[si], ph)) {
+        while (!wg_mbar_try(&bars[slot], ph)) {
           if (wg_timer() - t0 > kWaitNs) {
             if (A.err) atomicExch(A.err, 1);
             ok = false;
@@ -301,22 +249,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_wg_kernel(WgArgs A, const in
           }
         }
       }
+      ok = __all_sync(kFull, ok);
       if (ok && gr.n_r > 0) {
         const int b0 = s * kKB, kb = min(kKB, n_blk - b0);
-        const unsigned char* st = ring + (size_t)si * kSlotBytes;
+        const unsigned char* st = ring + (size_t)slot * kSlotBytes;
         if (kb == kKB)
           stage_chain<true>(st, xq, xs, xm, b0, kb, ri, q, lane, acc);
         else
           stage_chain<false>(st, xq, xs, xm, b0, kb, ri, q, lane, acc);
       }
-      __syncwarp();
-      if (lane == 0) wg_mbar_arrive(&empty[si]);
+      __syncwarp();  // every lane is done with the slot: refill it
+      if (ok) consumed++;
+      if (lane == 0 && ok && issued < my_stages) issue_next(slot);
       if (++slot == kSlots) {
         slot = 0;
         ph ^= 1u;
       }
     }
     if (ok && q == 0 && ri < gr.n_r) gr.out[ri] = acc;
+  }
+  // copies still in flight (only after a wait gave up) must land before the CTA exits: stages
+  // consumed .. issued-1, stage i in slot i % kSlots with parity (i / kSlots) & 1
+  if (!ok && lane == 0) {
+    const unsigned long long t0 = wg_timer();
+    for (int i = consumed; i < issued; i++)
+      while (!wg_mbar_try(&bars[i % kSlots], (unsigned)(i / kSlots) & 1u) && wg_timer() - t0 < kWaitNs) {
+      }
   }
 }
 

@@ -17,9 +17,14 @@
 //     to start at zero: every call rewrites the codes, scales and sums it reads.  Calls whose
 //     kernels overlap on the GPU (different streams, or different host threads on one device)
 //     race on the array and give wrong results; serialise them.
-//   * The first call on each device resolves the array's device address (cudaGetSymbolAddress,
-//     with that device current) and sets the kernels' shared-memory limits; make that first call
-//     before any stream capture.
+//   * Every call resolves the array's device address on the current device
+//     (cudaGetSymbolAddress, which allocates nothing), so a module reloaded after
+//     cudaDeviceReset is picked up; the first call on each device also sets the kernels'
+//     shared-memory limits - make that first call before any stream capture.
+//   * Tile offsets must be multiples of 16 bytes (as the container writes them); the offsets
+//     live in device memory and are not read back, so a misaligned offset gives undefined
+//     results instead of an error code.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -41,21 +46,21 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-unsigned char* g_scratch_addr[kMaxDevices] = {};
+bool g_configured[kMaxDevices] = {};
 
-// Once per device, with that device current: resolve the scratch address and raise the kernels'
-// shared-memory limits.  Neither allocates.
+// With device `dev` current: the scratch array's device address (looked up on every call), and
+// once per device the kernels' shared-memory limits.  Neither allocates.
 cudaError_t setup_device(int dev, unsigned char** out) {
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  if (!g_configured[dev]) {
     e = configure_kernels();
     if (e != cudaSuccess) return e;
-    g_scratch_addr[dev] = (unsigned char*)p;
+    g_configured[dev] = true;
   }
-  *out = g_scratch_addr[dev];
+  *out = (unsigned char*)p;
   return cudaSuccess;
 }
 
@@ -96,17 +101,27 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t co
     dpuf::set_error(std::string("dpuf_cuda_matmul_noalloc: setup: ") + cudaGetErrorString(e));
     return -4;
   }
-  const dpuf::Act a{(int8_t*)base, (float*)(base + dpuf::kNoAllocMaxValues),
-                    (int32_t*)(base + dpuf::kNoAllocMaxValues + dpuf::kNoAllocBlocks * sizeof(float)), cols};
+  int8_t* q8 = (int8_t*)base;
+  float* xs = (float*)(base + dpuf::kNoAllocMaxValues);
+  int32_t* xm = (int32_t*)(base + dpuf::kNoAllocMaxValues + dpuf::kNoAllocBlocks * sizeof(float));
   const dpuf::W12 w{tiles_dev, tile_offsets_dev, sign_bits_dev, rows, cols, n_tiles};
   const dpuf::Launch L{(cudaStream_t)stream, false};
-  e = dpuf::launch_prep(L, x_dev, cols, M, cols, sign_bits_dev, a);
-  if (e == cudaSuccess) {
+  // the whole input is prepped into the array once, then the tokens go through the matmul in
+  // chunks of at most kMaxBatch (256), as the allocating entry point splits them
+  e = dpuf::launch_prep(L, x_dev, cols, M, cols, sign_bits_dev, dpuf::Act{q8, xs, xm, cols});
+  for (int c0 = 0; e == cudaSuccess && c0 < M; c0 += dpuf::kMaxBatch) {
+    const int mc = std::min(dpuf::kMaxBatch, M - c0);
+    const size_t o = (size_t)c0 * cols;
+    const dpuf::Act a{q8 + o, xs + o / 32, xm + o / 32, cols};
     dpuf::LinJobs J = {};
     J.n = 1;
-    J.j[0] = {w, a, y_dev, rows, 0, n_tiles};
+    J.j[0] = {w, a, y_dev + (size_t)c0 * rows, rows, 0, n_tiles};
     J.tile_prefix[1] = n_tiles;
-    e = M == 1 ? dpuf::launch_gemv(L, J, nullptr, nullptr) : dpuf::launch_gemm_exact(L, J, M);
+    e = mc == 1 ? dpuf::launch_gemv(L, J, nullptr, nullptr) : dpuf::launch_gemm_exact(L, J, mc);
+  }
+  if (e == cudaErrorInvalidValue) {
+    dpuf::set_error("dpuf_cuda_matmul_noalloc: shape not supported by the matmul kernels (cols too large)");
+    return -1;
   }
   if (e != cudaSuccess) {
     dpuf::set_error(std::string("dpuf_cuda_matmul_noalloc: launch: ") + cudaGetErrorString(e));

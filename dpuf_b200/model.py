@@ -127,7 +127,9 @@ TINY_MHA = ModelShape("tiny-mha", 256, 512, 2, 3, 3, 64, 4096, tied=False, max_s
 TINY_WIDE = ModelShape("tiny-wide", 1024, 12288, 2, 8, 4, 128, 4096, tied=False, max_seq=512)
 # three query heads per KV head: one pair and one lone head in every group
 TINY_G3 = ModelShape("tiny-g3", 256, 512, 2, 6, 2, 64, 4096, tied=False, max_seq=512)
-SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, TINY, TINY_ZONE, TINY_MHA, TINY_WIDE, TINY_G3)}
+# a small model with the configurations' longest context (fp32 KV cache beyond 2048 positions)
+TINY_LONG = ModelShape("tiny-long", 256, 512, 2, 4, 2, 64, 4096, tied=False, max_seq=2304)
+SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, TINY, TINY_ZONE, TINY_MHA, TINY_WIDE, TINY_G3, TINY_LONG)}
 
 
 def _stream_id(name: str) -> int:

@@ -134,10 +134,13 @@ DPUF_EXPORT int32_t dpuf_cuda_matmul_dev_timed(void** whs, int32_t n_handles, in
  * sign bits (tiles_dev 16-byte aligned, tile offsets multiples of 16 as every packed container
  * has them).  Allocates nothing: the quantised activation lives in a fixed device array of
  * 2^20 values (1.25 MiB, held by every GPU that loads the library until exit).
- * Returns 0; -1 bad arguments; -2 M * cols > 2^20 (rejected, see dpuf_cuda_last_error);
- * -4 CUDA error.  Enqueues on `stream` without synchronising.  The first call on a device sets
- * the device up (resolves the array's address); make it before any stream capture.  All calls
- * share the array: calls that overlap on the GPU race and must be serialised. */
+ * Returns 0; -1 bad arguments (also a shape the matmul kernels do not take); -2 M * cols > 2^20
+ * (rejected, see dpuf_cuda_last_error); -4 CUDA error.  A tile offset that is not a multiple of
+ * 16 is not detected (the offsets stay on the device) and gives undefined results.  Enqueues on
+ * `stream` without synchronising.  Every call looks the array's address up on the current
+ * device (no allocation); the first call on a device also sets the kernels up - make it before
+ * any stream capture.  All calls share the array: calls that overlap on the GPU race and must be
+ * serialised. */
 DPUF_EXPORT int32_t dpuf_cuda_matmul_noalloc(int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
                                              const float* x_dev, const uint8_t* tiles_dev,
                                              const uint64_t* tile_offsets_dev, const uint8_t* sign_bits_dev,

@@ -949,3 +949,26 @@ ORC_EXPORT int32_t orc_argmax(const float* x, int32_t n) {
         if (x[i] > bv) { bv = x[i]; best = i; }
     return best;
 }
+
+/* ---- host libm expf over a range of inputs (test infrastructure) ----
+ * Counts the inputs bits0 .. bits0 + n - 1 (as float bit patterns) where got[i] differs bit
+ * for bit from this host's expf; *first (optional) receives the first differing index or -1. */
+int64_t orc_expf_mismatch(uint32_t bits0, int64_t n, const float* got, int64_t* first) {
+    int64_t bad = 0, lo = -1;
+    #pragma omp parallel for reduction(+:bad) schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        uint32_t b = bits0 + (uint32_t)i, gb, wb;
+        float x, w;
+        memcpy(&x, &b, 4);
+        w = expf(x);
+        memcpy(&wb, &w, 4);
+        memcpy(&gb, &got[i], 4);
+        if (gb != wb) {
+            bad++;
+            #pragma omp critical
+            { if (lo < 0 || i < lo) lo = i; }
+        }
+    }
+    if (first) *first = lo;
+    return bad;
+}

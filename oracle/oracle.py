@@ -223,7 +223,12 @@ def greedy_run(engine, prompt, n_decode: int):
     """pp(prompt) + n_decode greedy steps at batch 1 (run_turn_ex, dpuf-cli.c:2344-2420).
     Returns (generated ids, list of per-step logits [prefill last + each decode step])."""
     engine.reset()
-    logits = [engine.forward(prompt, 0, 1)[0].copy()]
+    # prompts longer than the 256-token batch limit go in chunks, only the last one returning
+    # logits (run_turn_ex, dpuf-cli.c:2380-2395)
+    for c0 in range(0, len(prompt) - 256, 256):
+        engine.forward(prompt[c0:c0 + 256], c0, 2)
+    c0 = (len(prompt) - 1) // 256 * 256
+    logits = [engine.forward(prompt[c0:], c0, 1)[0].copy()]
     ids = []
     pos = len(prompt)
     for _ in range(n_decode):
@@ -337,3 +342,15 @@ def ref_sample_token(logits: np.ndarray, temp: float, state: int) -> tuple[int, 
     st = ctypes.c_uint64(state)
     r = lib.ref_sample_token(lg.ctypes.data, lg.size, float(temp), ctypes.byref(st))
     return int(r), int(st.value)
+
+
+def expf_mismatch(bits0: int, got: np.ndarray) -> tuple[int, int]:
+    """(count, first index) of the inputs bits0 .. bits0 + len(got) - 1 (float bit patterns) where
+    `got` differs bit for bit from this host's libm expf (orc_expf_mismatch)."""
+    lib = OracleEngine.lib_()
+    lib.orc_expf_mismatch.restype = ctypes.c_int64
+    lib.orc_expf_mismatch.argtypes = [ctypes.c_uint32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+    got = np.ascontiguousarray(got, dtype=np.float32)
+    first = ctypes.c_int64(-1)
+    n = lib.orc_expf_mismatch(bits0, got.size, got.ctypes.data, ctypes.byref(first))
+    return int(n), int(first.value)

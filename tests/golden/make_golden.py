@@ -2,6 +2,8 @@
 
 Run in a container that has the reference sources:
     python tests/golden/make_golden.py REF_DIR      (or env DPUF_REFERENCE_DIR)
+    python tests/golden/make_golden.py REF_DIR --scenario NAME[,NAME]   (only those engine
+                                                                         scenarios, merged)
 It builds oracle/_ref/libdpuf_avx2.so from the unmodified reference sources
 (oracle/build_ref.sh), imports the reference packer module, and records:
   * pack.json     sha256 of the reference packer's blob for each PACK_CASES input;
@@ -34,12 +36,21 @@ import scenarios as sc  # noqa: E402
 
 
 def main() -> None:
-    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(orc.REF_SRC_ENV, "")
+    args = sys.argv[1:]
+    only = None
+    if "--scenario" in args:  # --scenario NAME[,NAME...]: only those engine scenarios
+        i = args.index("--scenario")
+        only = args[i + 1].split(",")
+        del args[i:i + 2]
+    src = args[0] if args else os.environ.get(orc.REF_SRC_ENV, "")
     if not src:
         raise SystemExit("give the reference source directory (argument or DPUF_REFERENCE_DIR)")
     ref_dir = pathlib.Path(src)
     _native.build_pack()
     orc.build_ref(ref_dir)
+    if only:
+        update_scenarios(only)
+        return
     sys.path.insert(0, str(ref_dir))
     import dpuf_format as ref_format  # the reference packer module
 
@@ -106,42 +117,62 @@ def main() -> None:
     eng_out = {}
     eng_logits = {}
     for s in sc.ENGINE_SCENARIOS:
-        saved = {k: os.environ.get(k) for k, _ in s.env}
-        os.environ.update(dict(s.env))
-        try:
-            m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter)
-            m.cfg.kv_type = s.kv_type
-            ref = orc.RefEngine(m, n_threads=8)
-            prompt = mdl.prompt_ids(s.prompt_len, m.shape.vocab, s.seed)
-            rec = {"prompt": prompt.tolist()}
-            if s.all_logits:
-                ref.reset()
-                allp = ref.forward(prompt, 0, 0)
-                rec["prefill_all_digest"] = sc.logits_digest(allp)
-            ids, logits = orc.greedy_run(ref, prompt, s.n_decode)
-            rec["ids"] = ids
-            rec["digests"] = [sc.logits_digest(l) for l in logits]
-            rec["head"] = [l[:4].tolist() for l in logits]
-            rms = float(np.sqrt(np.mean(np.stack(logits) ** 2)))
-            rec["logit_rms"] = rms
-            if dict(s.env).get("DPUF_EARLY_TILES"):
-                za = max(256, int(dict(s.env)["DPUF_EARLY_TILES"]))
-                rec["zone_exit"] = [bool(np.all(l[16 * za:] == np.float32(-1e9))) for l in logits]
-            if s.full_logits:
-                eng_logits[s.name] = np.stack(logits)
-            eng_out[s.name] = rec
-            ref.close()
-            print(s.name, "ids", ids[:8], "rms", rms, flush=True)
-        finally:
-            for k, v in saved.items():
-                if v is None:
-                    os.environ.pop(k, None)
-                else:
-                    os.environ[k] = v
+        rec, full = scenario_golden(s)
+        eng_out[s.name] = rec
+        if full is not None:
+            eng_logits[s.name] = full
     eng_out["embeds_in"] = embeds_golden(lib)
     eng_out["rope_positions"] = rope_golden(lib)
     (HERE / "engine.json").write_text(json.dumps(eng_out, indent=1))
     np.savez_compressed(HERE / "engine_logits.npz", **eng_logits)
+
+
+def scenario_golden(s):
+    """Greedy ids and logit digests of one engine scenario on the reference engine (8 threads);
+    returns (record, full logits or None)."""
+    saved = {k: os.environ.get(k) for k, _ in s.env}
+    os.environ.update(dict(s.env))
+    try:
+        m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter)
+        m.cfg.kv_type = s.kv_type
+        ref = orc.RefEngine(m, n_threads=8)
+        prompt = mdl.prompt_ids(s.prompt_len, m.shape.vocab, s.seed)
+        rec = {"prompt": prompt.tolist()}
+        if s.all_logits:
+            ref.reset()
+            allp = ref.forward(prompt, 0, 0)
+            rec["prefill_all_digest"] = sc.logits_digest(allp)
+        ids, logits = orc.greedy_run(ref, prompt, s.n_decode)
+        rec["ids"] = ids
+        rec["digests"] = [sc.logits_digest(l) for l in logits]
+        rec["head"] = [l[:4].tolist() for l in logits]
+        rms = float(np.sqrt(np.mean(np.stack(logits) ** 2)))
+        rec["logit_rms"] = rms
+        if dict(s.env).get("DPUF_EARLY_TILES"):
+            za = max(256, int(dict(s.env)["DPUF_EARLY_TILES"]))
+            rec["zone_exit"] = [bool(np.all(l[16 * za:] == np.float32(-1e9))) for l in logits]
+        ref.close()
+        print(s.name, "ids", ids[:8], "rms", rms, flush=True)
+        return rec, (np.stack(logits) if s.full_logits else None)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+def update_scenarios(names) -> None:
+    """(Re)computes only the named engine scenarios and merges them into engine.json."""
+    path = HERE / "engine.json"
+    eng_out = json.loads(path.read_text())
+    for s in sc.ENGINE_SCENARIOS:
+        if s.name in names:
+            rec, full = scenario_golden(s)
+            if full is not None:
+                raise SystemExit("full-logit scenarios need the full run")
+            eng_out[s.name] = rec
+    path.write_text(json.dumps(eng_out, indent=1))
 
 
 def embeds_golden(lib) -> dict:

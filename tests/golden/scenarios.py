@@ -42,6 +42,9 @@ ENGINE_SCENARIOS = [
     EngineScenario("tiny_g3_q8", "tiny-g3", 33, 9, norm_jitter=0.1, seed=4, full_logits=True, kv_type=1),
     EngineScenario("tiny_mha_q8", "tiny-mha", 17, 8, norm_jitter=0.1, seed=2, kv_type=1),
     EngineScenario("qwen3_0_6b_q8", "qwen3-0.6b", 16, 8, kv_type=1),
+    # fp32 KV cache past 2048 positions: a 2040-token prompt in 256-token chunks, then decode
+    # steps whose attention reads up to 2052 keys
+    EngineScenario("tiny_long_2k", "tiny-long", 2040, 12, norm_jitter=0.1, seed=5),
 ]
 
 # Packer cases: (rows, cols, tensor name used for the column signs, generator seed).

@@ -1,7 +1,8 @@
-"""The headline configuration: Qwen3-8B-shaped random-init model, pp32 then greedy decode at
-batch 1, against the reference engine (oracle/_ref, built from the reference sources) on the
-same host.  Ids and every step's logits must be bit-identical; both batch-1 paths (persistent
-kernel through forward_token, and the device greedy loop) are checked."""
+"""The headline configuration: Qwen3-8B-shaped random-init model, pp32 then 32 greedy decode
+steps at batch 1 (tg32), against the reference engine (oracle/_ref, built from the reference
+sources) on the same host.  Ids and every step's logits must be bit-identical over the whole
+generated sequence; both batch-1 paths (persistent kernel through forward_token, and the device
+greedy loop) are checked."""
 import numpy as np
 import pytest
 
@@ -21,7 +22,7 @@ def test_8b_greedy_decode_matches_reference_engine():
         pytest.skip("oracle/_ref/libdpuf_avx2.so not built")
     m = mdl.SyntheticModel(mdl.QWEN3_8B, seed=0)
     prompt = mdl.prompt_ids(32, m.shape.vocab, 0)
-    n = 8
+    n = 32
     ref = orc.RefEngine(m, n_threads=8)
     want_ids, want_logits = orc.greedy_run(ref, prompt, n)
     ref.close()

@@ -24,7 +24,8 @@ def test_noalloc_matmul_matches_allocating_entry_point():
     tiles = torch.from_numpy(bv.tiles.copy()).cuda()
     toff = torch.from_numpy(bv.tile_offsets.astype(np.uint64).view(np.int64).copy()).cuda()
     signs = torch.from_numpy(bv.sign_bits.copy()).cuda()
-    for call, M in enumerate((7, 1)):
+    # M = 300 crosses the 256-token chunk of the matmul; M = 1024 fills the 2^20-value array
+    for call, M in enumerate((7, 1, 300, (1 << 20) // bv.cols)):
         x = np.random.default_rng(100 + call).standard_normal((M, bv.cols)).astype(np.float32)
         x[:, 128:160] = 0.0  # a zero block exercises the skipped-block path
         want = engine.matmul(M, bv, x)
