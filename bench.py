@@ -164,6 +164,18 @@ def dp_value(local_ms: float, steps: int, world: int, device: str = "cuda"):
     return world * steps / (dev_ms * 1e-3), dev_ms
 
 
+def tp_value(local_ms: float, steps: int, world: int, device: str = "cuda"):
+    """Tensor-parallel decode throughput: all ranks decode ONE sequence, so the job's tokens are
+    the steps and its time is the slowest rank's.  Returns (tok/s, the max time in ms)."""
+    dev_ms = allreduce_max(float(local_ms), world, device)
+    return steps / (dev_ms * 1e-3), dev_ms
+
+
+def parity_agreed(local_ok: bool, world: int, device: str = "cuda") -> bool:
+    """True only if every rank's own parity check passed (one failing rank fails them all)."""
+    return allreduce_max(0.0 if local_ok else 1.0, world, device) == 0.0
+
+
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
@@ -456,8 +468,9 @@ def mdl_prompt(n: int, vocab: int, seed: int):
     return mdl.prompt_ids(n, vocab, seed)
 
 
-TRACE_EVENTS = ["norm1", "qkv", "bar_qkv", "attn", "grid_bar", "prep_o", "o", "bar_o", "norm2", "gate_up",
-                "bar_gu", "prep_down", "down", "bar_down"]
+TRACE_EVENTS = ["norm1_res", "norm1_chain", "norm1", "qkv", "attn_in", "attn_wait", "attn_rope", "attn_scores",
+                "attn_softmax", "attn_pv", "attn", "load_o", "o", "norm2_res", "norm2_chain", "norm2", "gate_up_stages",
+                "gate_up", "load_down", "down"]
 
 
 def run_trace(args):
@@ -487,25 +500,29 @@ def run_trace(args):
     if lib.dpuf_cuda_decode_trace(e._handle, ctypes.byref(n_ctas), ctypes.byref(per), out.ctypes.data, out.size):
         raise RuntimeError("no decode trace (persistent kernel not used?)")
     e.close()
+    if args.trace_out:
+        np.save(args.trace_out, out.reshape(C, P))
     L = shape.layers
+    E = len(TRACE_EVENTS)
     t = out.reshape(C, P).astype(np.int64)
-    sb = 14 * L
+    sb = E * L  # per-step events: start, embedding, final norm, LM head, argmax
     tt = (t - t[:, sb].min()) / 1000.0
-    crit, mean = np.zeros(14), np.zeros(14)
+    crit, mean = np.zeros(E), np.zeros(E)
     for l in range(1, L - 1):
-        prev = tt[:, 14 * (l - 1) + 13]
-        for j in range(14):
-            cur = tt[:, 14 * l + j]
+        prev = tt[:, E * (l - 1) + E - 1]
+        for j in range(E):
+            cur = tt[:, E * l + j]
             crit[j] += cur.max() - prev.max()
             mean[j] += float(np.mean(cur - prev))
             prev = cur
     crit /= L - 2
     mean /= L - 2
     lm = L // 2
-    d_attn = tt[:, 14 * lm + 3] - tt[:, 14 * lm + 2]
+    i_attn, i_qkv = TRACE_EVENTS.index("attn"), TRACE_EVENTS.index("qkv")
+    d_attn = tt[:, E * lm + i_attn] - tt[:, E * lm + i_qkv]
     n_attn = int(np.sum(d_attn > 2 * np.median(d_attn) + 1.0))
     print(json.dumps({
-        "trace": "decode_kernel phases", "model": shape.name, "ctas": C, "step_us": round(float(tt[:, sb + 5].max()), 1),
+        "trace": "decode_kernel phases", "model": shape.name, "ctas": C, "step_us": round(float(tt[:, sb + 4].max()), 1),
         "device_ms_per_step_untraced_run": round(ms / 8, 4),
         "layer_us": round(float(crit.sum()), 2),
         "critical_us": {k: round(float(v), 2) for k, v in zip(TRACE_EVENTS, crit)},
@@ -752,14 +769,14 @@ def run_dpuf(args, world, rank, local):
     if rc != 0:
         raise RuntimeError(engine.last_error())
     barrier(world)
-    value, dev_ms = dp_value(float(ms.value), args.steps, world)
     if tp:
-        value /= world  # one sequence: the job's tokens are the steps
+        value, dev_ms = tp_value(float(ms.value), args.steps, world)
         # the timed run (pp32 id, then device-fed steps from position 32) is the same greedy
         # sequence as the recording (pp32 id, 4 host-logit steps, device-fed steps)
         timed = [first] + [int(x) for x in ids]
-        parity = parity and timed == ids_1[:len(timed)]
-        parity = allreduce_max(0.0 if parity else 1.0, world) == 0.0
+        parity = parity_agreed(parity and timed == ids_1[:len(timed)], world)
+    else:
+        value, dev_ms = dp_value(float(ms.value), args.steps, world)
 
     if args.no_extras:
         persistent = eng.persistent_decode()[0]
@@ -870,6 +887,7 @@ def main():
     ap.add_argument("--tp", action="store_true", help="(the default for --gpus N > 1) tensor parallelism")
     ap.add_argument("--trace", action="store_true",
                     help="phase trace of the persistent decode kernel (per-layer critical path), not a benchmark")
+    ap.add_argument("--trace-out", default="", help="with --trace: also save the raw [CTA][stamp] array (.npy)")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode timing only (no e2e, roofline or CPU baseline), for profiling runs")
     args = ap.parse_args()

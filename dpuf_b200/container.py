@@ -67,6 +67,30 @@ def model_config_json(shape: mdl.ModelShape, has_qk_norm: bool = True) -> dict:
             "model_type": "qwen3"}
 
 
+def byte_symbols() -> list[str]:
+    """The byte-level BPE alphabet (GPT-2's byte-to-unicode map, which the reference CLI's
+    tokenizer inverts, dpuf-cli.c:553-568): printable bytes stand for themselves, the others for
+    code points 256 + n in byte order."""
+    keep = set(range(33, 127)) | set(range(161, 173)) | set(range(174, 256))
+    out, n = [], 0
+    for b in range(256):
+        if b in keep:
+            out.append(chr(b))
+        else:
+            out.append(chr(256 + n))
+            n += 1
+    return out
+
+
+def synthetic_tokenizer(vocab: int) -> dict:
+    """A tokenizer object for the container's metadata (the keys dpuf-cli.c:1309-1400 reads) for
+    random-init models: ids 0..255 are the 256 byte symbols, so any text encodes byte by byte (no
+    merges), and every other id decodes to "[id]".  No end-of-sequence id, raw chat format."""
+    syms = byte_symbols()
+    return {"vocab": syms + [f"[{i}]" for i in range(256, vocab)], "merges": [], "eos_token_ids": [],
+            "bos_token_id": None, "add_bos": False, "chat_format": "raw"}
+
+
 def tensor_order(shape: mdl.ModelShape) -> list[str]:
     names = ["token_embd.weight"]
     if not shape.tied:
@@ -106,7 +130,8 @@ def write(path: str | os.PathLike, m: mdl.ModelData, tokenizer: dict | None = No
         meta["tokenizer"] = tokenizer
     if extra_meta:
         meta.update(extra_meta)
-    hdr = json.dumps({"__metadata__": meta, "__tensors__": index}, separators=(",", ":")).encode("utf-8")
+    hdr = json.dumps({"__metadata__": meta, "__tensors__": index}, separators=(",", ":"),
+                     ensure_ascii=False).encode("utf-8")
     hdr += b" " * _pad64(24 + len(hdr))
     top = struct.pack("<8sIIII", MAGIC, len(names), zlib.crc32(hdr) & 0xFFFFFFFF, pay_crc & 0xFFFFFFFF, len(hdr))
     tmp = path.with_name(path.name + ".part")
@@ -194,7 +219,7 @@ class DpufFile(mdl.ModelData):
 def write_synthetic(path: str | os.PathLike, shape_name: str, seed: int = 0) -> int:
     """Builds the random-init model `shape_name` (model.SHAPES) and writes it as a container."""
     m = mdl.SyntheticModel(mdl.SHAPES[shape_name], seed=seed)
-    return write(path, m, extra_meta={"synthetic_seed": seed})
+    return write(path, m, tokenizer=synthetic_tokenizer(m.shape.vocab), extra_meta={"synthetic_seed": seed})
 
 
 def main(argv=None) -> int:

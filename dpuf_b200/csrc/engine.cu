@@ -165,16 +165,14 @@ struct Engine {
   std::string dec_why;     // why the persistent kernel is not used
   DecodeArgs dec{};        // everything but the per-call fields
   DecLayer* d_dec_layers = nullptr;
-  // tagged exchange vectors of the persistent kernel (q, k, v, o, gate/up, down; partials)
-  uint64_t *dec_q = nullptr, *dec_k = nullptr, *dec_v = nullptr, *dec_o = nullptr, *dec_s = nullptr,
-           *dec_d = nullptr, *dec_part = nullptr, *dec_dprep = nullptr;
-  unsigned dec_gen = 1;  // exchange generation of the next persistent launch's first phase
-  unsigned dec_dgen = 0; // down-input preps completed by earlier persistent launches
-  unsigned* dec_ctr = nullptr;  // completion counters [2]
-  unsigned* dec_bar = nullptr;  // [0] grid barrier counter, [1] error word
-  unsigned char* dec_prep = nullptr;  // prepped o-projection input (fused prep)
-  unsigned char* dec_dprep_plain = nullptr;  // prepped down-projection input (one GPU)
-  size_t dec_bar_bytes = 0;
+  // the persistent kernel's exchange area on one GPU (tagged vectors, down-input counters and
+  // prep, argmax partials, error word; layout dec_layout) and this GPU's prepped o input
+  unsigned char* dec_xbuf = nullptr;
+  size_t dec_xbytes = 0;
+  uint64_t* dec_oprep = nullptr;
+  unsigned dec_gen = 1;  // exchange generation of the next persistent launch's first layer
+  int dec_failed = 0;    // the last persistent launch gave up a wait (reset the exchange first)
+  int dec_stall_next = -1;  // test hook: q/k/v unit whose rows are withheld in the next launch
   float* last_logits = nullptr;  // where the last step's logits are (per-step or persistent)
 
   // tensor parallelism of the persistent decode (dpuf_cuda_tp_handle / dpuf_cuda_tp_attach)
@@ -329,10 +327,7 @@ void destroy_engine(Engine* e) {
   cudaFree(e->d_ids); cudaFree(e->d_hist); cudaFree(e->d_flag); cudaFree(e->d_b12); cudaFree(e->d_argmax);
   cudaFree(e->d_exp_slots); cudaFree(e->d_counter); cudaFree(e->d_part); cudaFree(e->d_tc_err);
   cudaFree(e->split.pairs); cudaFree(e->split.acc); cudaFree(e->split.count);
-  cudaFree(e->d_dec_layers); cudaFree(e->dec_o); cudaFree(e->dec_s); cudaFree(e->dec_d);
-  cudaFree(e->dec_q); cudaFree(e->dec_k); cudaFree(e->dec_v); cudaFree(e->dec_dprep); cudaFree(e->dec_ctr);
-  cudaFree(e->dec_part); cudaFree(e->dec_bar); cudaFree(e->dec.trace); cudaFree(e->dec_prep);
-  cudaFree(e->dec_dprep_plain);
+  cudaFree(e->d_dec_layers); cudaFree(e->dec_xbuf); cudaFree(e->dec_oprep); cudaFree(e->dec.trace);
   for (void* p : e->tp_peer)
     if (p) cudaIpcCloseMemHandle(p);
   cudaFree(e->tp_buf);
@@ -536,6 +531,47 @@ bool uniform_tiles(const DpufWeightDesc& w, long long* stride, long long* first)
   return true;
 }
 
+// Exchange area of the persistent kernel on one GPU: the tagged vectors, the down input's raw
+// values, chunk counters and prep, the argmax partials, the logits and the error word.  Under
+// tensor parallelism every rank holds one (the IPC-shared buffer) and producers store into every
+// rank's copy.  Zeroed at allocation: every tag is 0 and the first launch's generation is 1.
+struct DecLayout {
+  size_t err, q, k, v, o, d, dprep, s_raw, logits, part, total;
+};
+DecLayout dec_layout(const Engine* e, int world, int grid) {
+  DecLayout t{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  t.err = take(4);
+  t.q = take((size_t)e->qd * 8);
+  t.k = take((size_t)e->kvd * 8);
+  t.v = take((size_t)e->kvd * 8);
+  t.o = take((size_t)e->H * 8);
+  t.d = take((size_t)e->H * 8);
+  t.dprep = take((size_t)(e->I / 64) * 20 * 8);
+  t.s_raw = take((size_t)e->I * 8);
+  t.logits = take((size_t)e->V * 4);
+  t.part = take((size_t)2 * world * grid * 16);
+  t.total = off;
+  return t;
+}
+void dec_bind(DecodeArgs& A, unsigned char* base, const DecLayout& t) {
+  A.err = (int*)(base + t.err);
+  A.q = (uint64_t*)(base + t.q);
+  A.k = (uint64_t*)(base + t.k);
+  A.v = (uint64_t*)(base + t.v);
+  A.o_out = (uint64_t*)(base + t.o);
+  A.d_out = (uint64_t*)(base + t.d);
+  A.dprep = (uint64_t*)(base + t.dprep);
+  A.s_raw = (uint64_t*)(base + t.s_raw);
+  A.logits = (float*)(base + t.logits);
+  A.part = (uint64_t*)(base + t.part);
+}
+
 // Decides whether batch-1 steps run as the persistent kernel and prepares its arguments.
 // Falls back (dec_ok = false, reason in dec_why) when a matrix's tiles are not equally
 // spaced, when co-inputs use different sign tables, or when the device cannot hold one CTA
@@ -589,74 +625,40 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   A.cos_tab = e->cos_tab;
   A.sin_tab = e->sin_tab;
   A.et = e->et;
-  A.att = e->att; A.logits = e->logits; A.hist = e->d_hist;
+  A.hist = e->d_hist;
   A.grid = sms;
   A.tp_rank = 0;
   A.tp_world = 1;
-  A.stage_cap = decode_stage_cap(A);
-  {
-    // the gate/up output is prepped by every CTA when it fits one staged piece and two prep
-    // passes; otherwise one CTA per 64-column chunk preps it and every CTA copies the result
-    const size_t stage_bytes = decode_uni_bytes(A) - (size_t)A.kmax - (size_t)(A.kmax / 32) * 8;
-    A.dprep_local = ((size_t)e->I * 8 + (size_t)e->I / 8 <= stage_bytes && e->I / 64 <= 72) ? 1 : 0;
-  }
-  A.attn_floats = (int)(decode_uni_bytes(A) / sizeof(float));
+  if (e->hd % 64 || e->hd > 128) return no("head_dim not a multiple of 64 up to 128");
+  if (e->I % 64 || e->H % 64 || e->qd % 64) return no("widths not multiples of 64");
   size_t limit = 0;
   if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");
-  A.n_ring = decode_ring_slots(A, limit);
-  if (A.n_ring < 4) return no("shared memory: ring shorter than four stages");
+  // ring slots: as many as shared memory holds (env DPUF_CUDA_RING_SLOTS caps them)
+  A.n_slots = std::min(decode_ring_slots(A, limit), std::max(1, env_int("DPUF_CUDA_RING_SLOTS", 1 << 20)));
+  if (A.n_slots < 2 * kDecodeConsWarps + 2) return no("shared memory: ring shorter than 24 stages");
   int per_sm = 0;
   if (decode_blocks_per_sm(A, &per_sm) != cudaSuccess || per_sm < 1) return no("occupancy");
   if (cudaMalloc(&e->d_dec_layers, std::max<size_t>(1, tab.size()) * sizeof(DecLayer)) ||
       (!tab.empty() &&
-       cudaMemcpy(e->d_dec_layers, tab.data(), tab.size() * sizeof(DecLayer), cudaMemcpyHostToDevice)) ||
-      cudaMalloc(&e->dec_q, (size_t)e->qd * 8) || cudaMalloc(&e->dec_k, (size_t)e->kvd * 8) ||
-      cudaMalloc(&e->dec_v, (size_t)e->kvd * 8) || cudaMalloc(&e->dec_o, (size_t)e->H * 8) ||
-      cudaMalloc(&e->dec_s, (size_t)e->I * 8) || cudaMalloc(&e->dec_d, (size_t)e->H * 8) ||
-      cudaMalloc(&e->dec_part, (size_t)2 * sms * 16) ||
-      cudaMalloc(&e->dec_dprep, ((size_t)e->I / 4 + (size_t)e->I / 16) * 8) ||
-      cudaMalloc(&e->dec_ctr, 256))
+       cudaMemcpy(e->d_dec_layers, tab.data(), tab.size() * sizeof(DecLayer), cudaMemcpyHostToDevice)))
     return no("allocation");
-  // tags start at 0; the first launch's generation is 1
-  if (cudaMemset(e->dec_q, 0, (size_t)e->qd * 8) || cudaMemset(e->dec_k, 0, (size_t)e->kvd * 8) ||
-      cudaMemset(e->dec_v, 0, (size_t)e->kvd * 8) || cudaMemset(e->dec_o, 0, (size_t)e->H * 8) ||
-      cudaMemset(e->dec_s, 0, (size_t)e->I * 8) || cudaMemset(e->dec_d, 0, (size_t)e->H * 8) ||
-      cudaMemset(e->dec_part, 0, (size_t)2 * sms * 16) ||
-      cudaMemset(e->dec_dprep, 0, ((size_t)e->I / 4 + (size_t)e->I / 16) * 8) ||
-      cudaMemset(e->dec_ctr, 0, 256))
+  const DecLayout t = dec_layout(e, 1, sms);
+  e->dec_xbytes = t.total;
+  const size_t oprep_bytes = (size_t)(e->qd / 64) * 20 * 8;
+  if (cudaMalloc(&e->dec_xbuf, t.total) || cudaMemset(e->dec_xbuf, 0, t.total) ||
+      cudaMalloc(&e->dec_oprep, oprep_bytes) || cudaMemset(e->dec_oprep, 0, oprep_bytes))
     return no("allocation");
   e->dec_gen = 1;
-  e->dec_dgen = 0;
-  // barrier counter and error word, zeroed before every launch
-  e->dec_bar_bytes = 16;
-  if (cudaMalloc(&e->dec_bar, e->dec_bar_bytes)) return no("allocation");
-  // the down projection's input is prepped in 64-column chunks and copied in 128-column pieces
-  if (e->I % 128) return no("intermediate size not a multiple of 128");
-  A.fuse_o = (e->hd % 64 == 0 && e->qd % 128 == 0 && A.kmax % 128 == 0) ? 1 : 0;
-  {
-    const size_t qo = align256((size_t)e->qd), so = align256((size_t)e->qd / 8);
-    if (cudaMalloc(&e->dec_prep, qo + 2 * so)) return no("allocation");
-    A.xo_q8 = (int8_t*)e->dec_prep;
-    A.xo_xs = (float*)(e->dec_prep + qo);
-    A.xo_xm = (int32_t*)(e->dec_prep + qo + so);
-    const size_t dq = align256((size_t)e->I), ds = align256((size_t)e->I / 8);
-    if (cudaMalloc(&e->dec_dprep_plain, dq + 2 * ds)) return no("allocation");
-    A.xd_q8 = (int8_t*)e->dec_dprep_plain;
-    A.xd_xs = (float*)(e->dec_dprep_plain + dq);
-    A.xd_xm = (int32_t*)(e->dec_dprep_plain + dq + ds);
-  }
+  dec_bind(A, e->dec_xbuf, t);
+  A.oprep = e->dec_oprep;
   A.layers = e->d_dec_layers;
-  A.q = e->dec_q;
-  A.k = e->dec_k;
-  A.v = e->dec_v;
-  A.o_out = e->dec_o;
-  A.s_out = e->dec_s;
-  A.d_out = e->dec_d;
-  A.part = e->dec_part;
-  A.dprep = e->dec_dprep;
-  A.ctr = e->dec_ctr;
-  A.bar = e->dec_bar;
-  A.err = (int*)(e->dec_bar + 1);
+  // every device wait gives up after this long (env DPUF_CUDA_WAIT_MS, default 2000 ms)
+  A.wait_ns = (unsigned long long)std::max(1, env_int("DPUF_CUDA_WAIT_MS", 2000)) * 1000000ull;
+  A.stall_unit = -1;
+  // stages in flight per CTA (env DPUF_CUDA_INFLIGHT): enough to keep HBM busy, few enough that
+  // the exchange words between CTAs do not queue behind megabytes of weight requests.  At least
+  // one producer round (one stage per consumer warp); the ring must hold a round more.
+  A.max_inflight = std::max(kDecodeConsWarps, std::min(A.n_slots - kDecodeConsWarps - 1, env_int("DPUF_CUDA_INFLIGHT", 30)));
   if (env_int("DPUF_CUDA_TRACE_DECODE", 0)) {
     A.trace_per_cta = decode_trace_events(e->L);
     if (cudaMalloc(&A.trace, (size_t)sms * A.trace_per_cta * 8) ||
@@ -671,9 +673,22 @@ bool persistent_step(const Engine* e, const StepParams& P) {
   return P.M == 1 && P.za == 0 && !P.embeds && !P.ds_mask && !P.tok_rope && e->dec_ok && e->use_persistent;
 }
 
+// After a launch that gave up a wait, the exchange area holds a partial layer's tags and counts:
+// one GPU zeroes it and starts again from generation 1 (under tensor parallelism the ranks
+// cannot agree on that here, so their engines stay failed).
+cudaError_t dec_recover(Engine* e) {
+  if (!e->dec_failed || e->tp_world > 1) return cudaSuccess;
+  CK(cudaMemsetAsync(e->dec_xbuf, 0, e->dec_xbytes, e->stream));
+  CK(cudaMemsetAsync(e->dec_oprep, 0, (size_t)(e->qd / 64) * 20 * 8, e->stream));
+  e->dec_gen = 1;
+  e->dec_failed = 0;
+  return cudaSuccess;
+}
+
 // Launches the persistent kernel for n_steps batch-1 steps from (first_id, pos0) and queues the
 // read of its error word into the pinned staging (checked by the caller after synchronising).
 cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool write_logits, int keep) {
+  CK(dec_recover(e));
   DecodeArgs A = e->dec;
   A.first_id = first_id;
   A.pos0 = pos0;
@@ -684,14 +699,13 @@ cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool writ
   A.kv_k = e->slots[e->active].k;
   A.kv_v = e->slots[e->active].v;
   A.gen0 = e->dec_gen;
-  A.dgen0 = e->dec_dgen;
+  A.stall_unit = e->dec_stall_next;
+  e->dec_stall_next = -1;
   e->stage->pad[0] = 0;
-  // the barrier counter and this GPU's error word (under tensor parallelism the error word is
-  // in the exchange buffer and stays set once a rank has failed)
-  CK(cudaMemsetAsync(e->dec_bar, 0, e->dec_bar_bytes, e->stream));
+  // this GPU's error word (under tensor parallelism it stays set once a rank has failed)
+  if (e->tp_world == 1) CK(cudaMemsetAsync(A.err, 0, 4, e->stream));
   CK(launch_decode(e->stream, A));
   e->dec_gen += (unsigned)n_steps * (unsigned)decode_phases(e->L);
-  e->dec_dgen += (unsigned)n_steps * (unsigned)e->L;
   CK(cudaMemcpyAsync(&e->stage->pad[0], A.err, 4, cudaMemcpyDeviceToHost, e->stream));
   return cudaSuccess;
 }
@@ -700,8 +714,9 @@ cudaError_t run_decode(Engine* e, int first_id, int pos0, int n_steps, bool writ
 int32_t decode_status(Engine* e) {
   const int code = e->stage->pad[0];
   if (code == 0) return 0;
-  set_error(code == 1 ? "persistent decode: a pipeline wait timed out"
-                      : "persistent decode: a grid barrier wait timed out");
+  e->dec_failed = 1;
+  set_error(code == 1 ? "persistent decode: a weight-stream wait timed out"
+                      : "persistent decode: a wait for another CTA's (or rank's) outputs timed out");
   return -6;
 }
 
@@ -990,34 +1005,6 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
 
 }  // namespace
 // ------------------------------------------------------------------ tensor parallelism
-// Exchange buffer of one rank: the persistent kernel's tagged vectors, the logits and the
-// error word, which every rank stores into every rank's copy (zeroed: all tags 0).
-struct TpLayout {
-  size_t err, ctr, q, k, v, o, s, d, dprep, logits, part, total;
-};
-TpLayout tp_layout(const Engine* e, int world) {
-  TpLayout t{};
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    const size_t o = off;
-    off += align256(bytes);
-    return o;
-  };
-  t.err = take(4);
-  t.ctr = take(8);
-  t.q = take((size_t)e->qd * 8);
-  t.k = take((size_t)e->kvd * 8);
-  t.v = take((size_t)e->kvd * 8);
-  t.o = take((size_t)e->H * 8);
-  t.s = take((size_t)e->I * 8);
-  t.d = take((size_t)e->H * 8);
-  t.dprep = take(((size_t)e->I / 4 + (size_t)e->I / 16) * 8);
-  t.logits = take((size_t)e->V * 4);
-  t.part = take((size_t)2 * world * e->dec.grid * 16);
-  t.total = off;
-  return t;
-}
-
 // What one rank publishes (DPUF_CUDA_TP_BLOB_BYTES): its IPC handle and what the other ranks
 // check before mapping it - same rank order, world, grid and model shape, and a GPU of its own
 // (ranks whose kernels wait on each other must never share a GPU: nothing guarantees that two
@@ -1283,6 +1270,19 @@ DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t
   if (!strcmp(name, "graphs")) { e->use_graphs = value != 0; dpuf::drop_graphs(e); return 0; }
   if (!strcmp(name, "persistent")) { e->use_persistent = value != 0; return 0; }
   if (!strcmp(name, "tc_gemm")) { e->use_tc_gemm = value != 0; dpuf::drop_graphs(e); return 0; }
+  if (!strcmp(name, "wait_ms")) {
+    if (value <= 0) return -1;
+    e->dec.wait_ns = (unsigned long long)value * 1000000ull;
+    return 0;
+  }
+  if (!strcmp(name, "test_stall_unit")) {
+    // failure-detection test hook: in the next persistent launch, the CTA that computes q/k/v
+    // unit `value` (8 rows of layer 0, q rows first) withholds its outputs of the first step,
+    // so every wait on them runs into the wait limit
+    if (value < 0 || value >= (int64_t)(e->dec.qd + 2 * e->dec.kvd) / 8) return -1;
+    e->dec_stall_next = (int)value;
+    return 0;
+  }
   return -1;
 }
 
@@ -1323,7 +1323,7 @@ DPUF_EXPORT int32_t dpuf_cuda_tp_handle(void* handle, int32_t rank, int32_t worl
     return -1;
   }
   if (cudaSetDevice(e->device) != cudaSuccess) return -4;
-  const dpuf::TpLayout t = dpuf::tp_layout(e, world);
+  const dpuf::DecLayout t = dpuf::dec_layout(e, world, e->dec.grid);
   dpuf::TpBlob b{};
   if (cudaDeviceGetPCIBusId(b.pci, (int)sizeof(b.pci) - 1, e->device) != cudaSuccess) return -4;
   if (cudaMalloc(&e->tp_buf, t.total) != cudaSuccess || cudaMemset(e->tp_buf, 0, t.total) != cudaSuccess ||
@@ -1386,7 +1386,7 @@ DPUF_EXPORT int32_t dpuf_cuda_tp_attach(void* handle, const uint8_t* blobs) {
       return -4;
     }
   }
-  const dpuf::TpLayout t = dpuf::tp_layout(e, world);
+  const dpuf::DecLayout t = dpuf::dec_layout(e, world, e->dec.grid);
   dpuf::DecodeArgs& A = e->dec;
   unsigned char* base = e->tp_buf;
   for (int r = 0; r < world; r++) {
@@ -1395,20 +1395,9 @@ DPUF_EXPORT int32_t dpuf_cuda_tp_attach(void* handle, const uint8_t* blobs) {
   }
   A.tp_rank = e->tp_rank;
   A.tp_world = world;
-  A.err = (int*)(base + t.err);
-  A.ctr = (unsigned*)(base + t.ctr);
-  A.q = (uint64_t*)(base + t.q);
-  A.k = (uint64_t*)(base + t.k);
-  A.v = (uint64_t*)(base + t.v);
-  A.o_out = (uint64_t*)(base + t.o);
-  A.s_out = (uint64_t*)(base + t.s);
-  A.d_out = (uint64_t*)(base + t.d);
-  A.dprep = (uint64_t*)(base + t.dprep);
-  A.logits = (float*)(base + t.logits);
-  A.part = (uint64_t*)(base + t.part);
+  dpuf::dec_bind(A, base, t);
   e->tp_world = world;
   e->dec_gen = 1;  // every rank starts at the same generation over zeroed buffers and counters
-  e->dec_dgen = 0;
   return 0;
 }
 

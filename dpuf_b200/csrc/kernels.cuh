@@ -165,54 +165,41 @@ struct DecodeArgs {
   float* kv_v;
   ExpfTable et;
   // Vectors other CTAs (and ranks) produce are exchanged as tagged words: value bits in the low
-  // half, the producing phase's generation in the high half (one 64-bit store, so a reader sees
-  // the value and its tag together).  Readers wait on the tags of the elements they need, so
-  // no grid barrier is needed after a projection.
-  uint64_t *q, *k, *v, *o_out, *s_out, *d_out;  // [qd], [kvd] x2, [H], [I], [H]
+  // half, the generation of the producing layer in the high half (one 64-bit store, so a reader
+  // sees the value and its tag together).  Readers wait on the tags of the words they need; no
+  // grid barrier separates the phases.
+  uint64_t *q, *k, *v, *o_out, *d_out;  // [qd], [kvd] x2, [H], [H]
+  // prepped projection inputs, 20 tagged words per 64-column chunk (16 words of four int8 codes,
+  // 2 block scales, 2 block sums): the o projection's (written by the attention CTAs of this
+  // GPU) and the down projection's (written by the warp holding each chunk's last gate/up pair)
+  uint64_t *oprep, *dprep;            // [qd/64 * 20], [I/64 * 20]
+  uint64_t* s_raw;                    // [I] SwiGLU outputs (tagged), read by the chunk's prep
   uint64_t* part;  // argmax partials [2 (LM generation parity)][ctas of all ranks][value, index]
-  // the down projection's prepped input, produced by one CTA per 64-column chunk: [I/4] words
-  // of four int8 codes, then [I/32] block scales, then [I/32] block sums
-  uint64_t* dprep;
-  int dprep_local;  // 1: every CTA preps the whole (small) gate/up output itself from the tagged words
-  // one GPU: the same prepped input as plain codes, block scales and block sums, read after a
-  // grid barrier
-  int8_t* xd_q8;   float* xd_xs;  int32_t* xd_xm;   // [I], [I/32] x2
-  float* att;      // attention output (this CTA set only; read after a local grid barrier)
   float* logits;   // [V] plain values, read by the host after the launch
-  unsigned gen0;   // generation of this launch's first phase (4 per layer + 1 per step)
-  unsigned dgen0;  // down-input preps (one per layer) completed before this launch
-  // Completion counters (never reset; wrap-safe): [0] += 1 per CTA of every rank and phase once
-  // its chain warp has stored the phase's outputs (so generation g is complete at (ctas of all
-  // ranks) * g), [1] the same per down-input prep.  Relaxed adds: a reader that finds a stale
-  // tag waits for the count, then re-copies what is still stale.
-  unsigned* ctr;
-  unsigned* bar;  // grid barrier counter (the barrier after attention), zero at launch
-  int* err;       // 0 at launch; 1 = mbarrier wait, 2 = grid barrier, 3 = exchange wait timed out
-  int32_t* hist;  // [n_steps] greedy ids
+  unsigned gen0;   // generation of this launch's first layer (L + 1 per step: layers, LM head)
+  int* err;        // 0 at launch; 1 = a ring wait, 3 = a wait for another CTA's outputs timed out
+  int32_t* hist;   // [n_steps] greedy ids
   int first_id, pos0, n_steps, write_logits;
-  int grid, n_ring;
-  int stage_cap;      // columns per staged piece of a vector being prepped (decode_stage_cap)
-  int attn_floats;    // shared-memory floats the attention items may use (decode_uni_bytes / 4)
-  // Fused o-projection prep: the attention items prep their output columns (needs
-  // head_dim % 64 == 0 and q_dim % 128 == 0); every CTA then copies the prepped vector.
-  int fuse_o;
-  int8_t* xo_q8;   float* xo_xs;  int32_t* xo_xm;   // [q_dim], [q_dim/32] x2
+  int grid, n_slots;                  // CTAs (one per SM); ring slots of a CTA
+  int max_inflight;                   // ring stages a CTA may have requested but not received
+  unsigned long long wait_ns;         // limit of every device wait
+  int stall_unit;  // test hook: the CTA owning this q/k/v unit withholds its first outputs (-1: none)
   unsigned long long* trace;  // optional per-CTA phase timestamps of the last step (null: off)
   int trace_per_cta;
   // Tensor parallelism over tp_world processes (one GPU each; 1 = off).  Every projection's
-  // units are dealt over all ranks' CTAs (virtual CTA tp_rank * gridDim.x + blockIdx.x); the
-  // tagged vectors, the logits and the error word live in an exchange buffer that every rank
-  // maps, and producers store to every rank's copy (peer address = local + tp_delta[r]).
+  // units are dealt over all ranks' CTAs (virtual CTA blockIdx.x * tp_world + tp_rank); the
+  // tagged vectors, the down input's raw values, counters and prep, the logits and the error
+  // word live in an exchange buffer that every rank maps, and producers store to every rank's
+  // copy (peer address = local + tp_delta[r]).
   int tp_rank, tp_world;
   long long tp_delta[kMaxTp];
 };
-// Exchange generations of one decode step (q/k/v, o, gate/up, down per layer; the LM head).
-DPUF_HD int decode_phases(int L) { return 4 * L + 1; }
-int decode_stage_cap(const DecodeArgs& A);
-size_t decode_uni_bytes(const DecodeArgs& A);
-int decode_trace_events(int L);
+// Exchange generations of one decode step (one per layer, one for the LM head).
+DPUF_HD int decode_phases(int L) { return L + 1; }
+constexpr int kDecodeConsWarps = 11;  // consumer warps of a decode CTA (plus one producer warp)
 size_t decode_smem_bytes(const DecodeArgs& A);
 int decode_ring_slots(const DecodeArgs& A, size_t smem_limit);
+int decode_trace_events(int L);
 cudaError_t configure_decode_kernel();
 cudaError_t decode_max_dyn_smem(size_t* bytes);
 cudaError_t decode_blocks_per_sm(const DecodeArgs& A, int* blocks);

@@ -1,54 +1,49 @@
 // kernels_decode.cu - batch-1 decode as one persistent cooperative kernel.
 //
-// One CTA per SM runs every step of a greedy decode (or one forward_token step): embedding,
-// all layers, final norm, LM head and argmax.  The per-element arithmetic is the same as the
-// per-step kernels' (layer_dev.cuh, and the GEMV's exact block chain), so logits and ids are
-// bit-identical to the reference's.
+// One CTA per SM runs every step of a greedy decode (or one forward_token step): embedding, all
+// layers, final norm, LM head and argmax.  The per-element arithmetic is the reference's
+// (layer_dev.cuh and the exact block chain below), so logits and ids are bit-identical to the
+// reference engine's.
 //
-// Weight stream.  The weights never depend on activations, so a producer warp per CTA walks
-// the CTA's share of every projection of every layer and step in order, moving stage s (32
-// blocks: the two 8-row groups' scales and nibbles, 4608 bytes per group) of two 16-row units
-// at a time into a shared-memory ring slot with cp.async.bulk (TMA, this CTA's own copy)
-// completed on an mbarrier.  It runs ahead across phases and barriers, bounded only by the
-// ring, so HBM keeps streaming while the consumers normalise, attend or wait.
+// Weight stream.  The weights never depend on activations.  A producer warp (one thread) walks
+// the CTA's sequence of stages - every projection of every layer and step - and moves each stage
+// (32 blocks of one 8-row group: 512 bytes of fp16 row scales and 4096 bytes of nibbles, two
+// cp.async.bulk copies on one mbarrier) into the next slot of a ring shared by the CTA's consumer
+// warps, as soon as the slot's previous stage has been released.  So while the consumers
+// normalise, attend or wait for another CTA, the ring fills with the next projection's weights.
 //
-// Consumers (warps 0..8).  Per slot, eight dot warps compute the exact integer block dots
-// sum_k u_k q_k with dp4a (lane = unit and row, four blocks each, independent chains), turn
-// them into pairs p = float(dot - xm), s = ws * xs (0, 0 for a skipped block) and hand them to
-// the chain warp through a 4-deep ring of pair buffers (named-barrier hand-off); the chain
-// warp runs acc = fma(p, s, acc) per row over the blocks in order (dpuf_avx2.c:2601-2640),
-// lanes 0..15 for unit A and 16..31 for unit B, and writes the units' outputs (SwiGLU for a
-// gate/up pair - gate tile in A, up tile in B - and the running argmax for the LM head).
-// Between projections the consumers do the row-wide steps redundantly in every CTA (the
-// residual stream h lives in each CTA's shared memory): residual add, RMSNorm, activation
-// prep; attention runs on one CTA per (KV head, query-head pair) and preps its output for the
-// o projection; the gate/up output is prepped for the down projection in 64-column chunks,
-// one chunk per CTA.
+// Projections.  Every consumer warp owns whole units - 8-row groups, or gate/up pairs - of every
+// projection (the CTA's contiguous range of units, dealt to its warps in turn); the warps'
+// stages are interleaved round by round in the ring, so a phase in which only a few warps have
+// units still has the whole ring in flight for them.  Lane (ri = lane % 8, q = lane / 8) of the
+// owning warp computes row ri's exact integer block dots of blocks 8q .. 8q+7 of a stage (dp4a on
+// the nibbles, chunk reads rotated by q so the four octets use different banks) and the pairs
+// (p, s) = (dot - xm, ws * xs); the in-order chain acc = fma(p, s, acc) then runs octet by octet,
+// handed on by shuffles (dpuf_avx2.c:2601-2640).  Outputs other CTAs read are stored as tagged
+// 64-bit words (value, generation of the layer), so readers wait on exactly the words they need.
 //
-// Exchange between CTAs.  The vectors a phase produces for all CTAs (q/k/v, o, gate/up, down
-// outputs, the LM head's argmax partials) are 64-bit words: the value and the generation of
-// the producing phase.  A reader stages them and re-reads any word that does not carry the
-// generation it expects yet, so no grid barrier separates a projection from its readers;
-// every phase reads the whole output of the phase before it, so no producer can overwrite a
-// word that a reader still needs.  Grid barriers remain after attention (the o projection's
-// prepped input) and, on one GPU, after the down-input prep.
+// Per layer:
+//   norm1   every CTA: residual += the previous down output (tagged), RMSNorm, prep -> x
+//   q/k/v   projection; outputs tagged
+//   attn    one CTA per query head (all its warps): QK-norm, RoPE, K/V store, scores, softmax,
+//           PV, and the prep of the head's output columns for the o projection (tagged)
+//   o       every CTA loads the prepped o input, projection; outputs tagged
+//   norm2   residual += o output, RMSNorm, prep -> x
+//   gate/up pairs (gate group and up group of the same rows in one warp), SwiGLU (tagged); the
+//           warp holding the last pair of a 64-column chunk preps the chunk for the down
+//           projection (tagged)
+//   down    every CTA loads the prepped down input, projection; outputs tagged
+// then the final norm, the LM head (logits and per-CTA argmax partials, tagged) and the argmax.
 //
-// Tensor parallelism (tp_world > 1, one process per GPU).  Every projection's units are dealt
-// over all ranks' CTAs; producers store the tagged words into every rank's exchange buffer
-// (peer stores over NVLink), the down-input prep publishes tagged codes and scales, and the
-// per-GPU steps (norms, attention, the preps' inputs) run on every rank.  No cross-GPU barrier
-// is needed: the tags carry the ordering.
+// Tensor parallelism (tp_world > 1, one process per GPU): every projection's units are dealt over
+// all ranks' CTAs; producers store their tagged words into every rank's exchange buffer (peer
+// stores over NVLink); every rank normalises and attends over all heads itself, so its KV cache
+// stays complete.
 //
-// Work split.  Each projection's 16-row units are dealt in contiguous ranges, and the CTA that
-// receives the remainder units rotates from one projection to the next, so every CTA streams
-// about the same bytes per layer and the ring absorbs the one-unit imbalance of a projection.
-//
-// Every wait is bounded: an mbarrier, grid-barrier, counter or tagged-word wait gives up after
-// kWaitNs (kTpWaitNs across ranks), sets the error word (of every rank) and the CTA's abort
-// flag.  After that every wait returns at once, but the consumers keep their control flow
-// (every loop runs its full trip count and reaches every named barrier, with all addresses
-// depending on shapes only), so no warp is left waiting at a barrier; the producer stops
-// issuing and waits, bounded, for the copies it issued.
+// Every wait is bounded (wait_ns): a wait that gives up sets the error word (of every rank) and
+// the CTA's abort flag, after which waits return at once and the control flow stays uniform (so
+// every barrier completes); the producer stops issuing and waits, bounded, for the copies it
+// issued before the CTA exits.
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -58,30 +53,17 @@ namespace dpuf {
 
 namespace {
 
-constexpr int kTeamWarps = 8;                   // dot warps per team (one slot per team at a time)
-constexpr int kTeams = 1;                       // teams take alternate slots
-constexpr int kMmaWarps = kTeamWarps * kTeams;  // dot warps
-constexpr int kChainWarp = kMmaWarps;
-constexpr int kProdWarp = kMmaWarps + 1;
-constexpr int kThreads = (kMmaWarps + 2) * 32;  // 576
-constexpr int kConsumers = (kMmaWarps + 1) * 32;
-// A ring slot holds stage s (32 blocks) of two 16-row units A and B; per unit: nibbles of
-// group 0 | group 1 (+32 pad) | scales of group 0 | group 1, and unit B starts 64 bytes past
-// a unit's size so that A's and B's lanes read different banks.
-constexpr int kNib1 = 4128, kSc0 = 8256, kSc1 = 8800;
-constexpr int kHalf = 9408;
-constexpr int kSlotBytes = 2 * kHalf;
-constexpr int kMaxRing = 24;
-constexpr int kNPs = 4;             // pair buffers between the dot warps and the chain warp
-constexpr int kPsRow = 34;          // float2 per row of a pair buffer: 32 blocks + pad (banks)
-constexpr int kPsBuf = 2 * 16 * kPsRow;  // float2 per pair buffer: [unit][row][block]
-// Named barriers: 1 consumers, 2 attention, then per pair buffer "filled" and "emptied".
-constexpr int kBarFilled = 3, kBarEmptied = kBarFilled + kNPs;
-static_assert(kBarEmptied + kNPs <= 16, "named barrier ids");
-constexpr int kHandoff = (kTeamWarps + 1) * 32;  // threads of a pair-buffer hand-off
-constexpr int kBarConsumers = 1, kBarAttn = 2;
-constexpr unsigned long long kWaitNs = 2000000000ull;    // 2 s
-constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s: other ranks' hosts may launch later
+constexpr int kConsWarps = kDecodeConsWarps;   // consumer warps
+constexpr int kProdWarp = kConsWarps;           // the producer warp
+constexpr int kThreads = (kConsWarps + 1) * 32;  // 384
+constexpr int kConsThreads = kConsWarps * 32;    // 352
+constexpr int kKB = 32;                // blocks per stage
+constexpr int kScBytes = kKB * 16;     // 512: fp16 scales [32][8]
+constexpr int kSlotBytes = kScBytes + kKB * 128;  // 4608
+constexpr int kMaxSlots = 48;          // ring slots (shared by the CTA's consumer warps)
+constexpr int kChunkWords = 20;        // tagged words of one prepped 64-column chunk
+constexpr int kVTile = 8;              // keys per staged value tile (attention)
+constexpr int kKeyGroups = kConsThreads / 8;
 enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
 
 // ------------------------------------------------------------------ PTX helpers
@@ -104,19 +86,8 @@ DPUF_DEV bool mbar_try(uint64_t* b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// try_wait that lets the hardware park the thread until the phase completes or `ns` pass, so
-// a waiting thread takes no issue slots from the warps doing the work.
-DPUF_DEV bool mbar_try_for(uint64_t* b, unsigned parity, unsigned ns) {
-  unsigned ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
 // Weight bytes are read once per step, so their L2 lines are marked evict-first: the stream
-// then does not push the KV cache, the activations and the barrier words out of L2.
+// then does not push the KV cache, the activations and the exchange words out of L2.
 DPUF_DEV uint64_t l2_evict_first_policy() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -129,336 +100,364 @@ DPUF_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
+DPUF_DEV void prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 DPUF_DEV unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-DPUF_DEV unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// u8 (weight nibbles, 0..15 or 16 * 0..15) x s8 (activation codes) dot of four byte pairs
+DPUF_DEV int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
-DPUF_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-DPUF_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-// Shared state of a CTA that is not in the dynamic buffer.
-struct DecShared {
-  uint64_t full[kMaxRing], empty[kMaxRing];
-  AttnShared attn;
-  float lanes[8];
-  float inv;
-  float arg_v[kConsumers / 32];  // per-warp argmax of the LM partials
-  int arg_i[kConsumers / 32];
-  int next_id;
-  volatile int abort;
+// One phase as seen by this CTA: units u0 .. u0+n-1; consumer warp w takes units u0 + w + k*W.
+// Its stages are interleaved round-robin in the CTA's ring: round r holds stage r of every warp
+// that has one.
+struct Phase {
+  int u0, n;       // the CTA's units
+  int a, extra;    // every warp has a units, warps w < extra one more
+  int n_st, n_sub; // stages per group, groups per unit
+  int spu;         // stages per unit
+  long long total; // stages of the phase in this CTA
 };
 
-// ------------------------------------------------------------------ exchange of vectors
-// A value other CTAs read is one 64-bit word: the value's bits, and the generation of the
-// phase that produced it in the high half.  It is stored to this rank's buffer and to every
-// other rank's copy (stores to the peer's memory over NVLink); a reader waits until the word
-// carries the generation it expects.  Every phase reads the whole output of the phase before,
-// so no producer can overwrite a word (with a later generation) that a reader still needs.
+// Shared state of a CTA outside the dynamic buffer.
+struct DecShared {
+  uint64_t full[kMaxSlots], empty[kMaxSlots];
+  float red[kConsWarps];
+  float lanes[8];
+  float arg_v[kConsWarps];
+  int arg_i[kConsWarps];
+  int next_id;
+  volatile int abort;
+  const uint8_t* pg[kConsWarps];  // producer: the current round's group of each consumer warp
+  Phase ph[5];                     // this CTA's share of each phase kind (fixed for the launch)
+};
+
+// ------------------------------------------------------------------ exchange
 DPUF_DEV uint64_t tagged(float v, unsigned gen) { return ((uint64_t)gen << 32) | __float_as_uint(v); }
-DPUF_DEV void st_tagged_sys(uint64_t* p, uint64_t w) {
-  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+DPUF_DEV unsigned tag_of(uint64_t w) { return (unsigned)(w >> 32); }
+DPUF_DEV float value_of(uint64_t w) { return __uint_as_float((unsigned)w); }
+DPUF_DEV void st_relaxed(uint64_t* p, uint64_t w, bool sys) {
+  if (sys)
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+  else
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-DPUF_DEV void st_tagged_gpu(uint64_t* p, uint64_t w) {
-  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+DPUF_DEV uint64_t ld_relaxed(const uint64_t* p, bool sys) {
+  uint64_t w;
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
-// (one GPU: device scope; several ranks: system scope, every rank's copy)
+template <typename T>
+DPUF_DEV T* peer_ptr(const DecodeArgs& A, T* p, int r) {
+  return (T*)((char*)p + A.tp_delta[r]);
+}
+// A tagged word into this rank's buffer and every other rank's copy.
 DPUF_DEV void put_tagged(const DecodeArgs& A, uint64_t* p, uint64_t w) {
-  if (A.tp_world == 1) {
-    st_tagged_gpu(p, w);
-    return;
-  }
-  st_tagged_sys(p, w);
+  const bool sys = A.tp_world > 1;
+  st_relaxed(p, w, sys);
   for (int r = 0; r < A.tp_world; r++)
-    if (r != A.tp_rank) st_tagged_sys((uint64_t*)((char*)p + A.tp_delta[r]), w);
+    if (r != A.tp_rank) st_relaxed(peer_ptr(A, p, r), w, true);
 }
 DPUF_DEV void put_float(const DecodeArgs& A, float* p, float v) {
   *p = v;
   for (int r = 0; r < A.tp_world; r++)
-    if (r != A.tp_rank) *(float*)((char*)p + A.tp_delta[r]) = v;
+    if (r != A.tp_rank) *peer_ptr(A, p, r) = v;
 }
-// Adds 1 to completion counter i of this rank and of every other rank (relaxed: no fence; the
-// tags, not the count, say whether a value has arrived).
-DPUF_DEV void count_done(const DecodeArgs& A, int i) {
-  asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(A.ctr + i) : "memory");
-  for (int r = 0; r < A.tp_world; r++)
-    if (r != A.tp_rank)
-      asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"((char*)(A.ctr + i) + A.tp_delta[r]) : "memory");
-}
-DPUF_DEV ulonglong2 ld_tagged2(const uint64_t* p, bool sys) {
-  ulonglong2 v;
-  if (sys)
-    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
-  else
-    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
-  return v;
-}
-DPUF_DEV unsigned tag_of(uint64_t w) { return (unsigned)(w >> 32); }
-DPUF_DEV float value_of(uint64_t w) { return __uint_as_float((unsigned)w); }
-// Records a failure in the error word of this rank and of every other rank, whose waits then
-// stop at once instead of running into their own limits.
+// Records a failure in this rank's error word and every other rank's, whose waits then stop.
 DPUF_DEV void raise_err(const DecodeArgs& A, int code) {
   atomicCAS(A.err, 0, code);
   for (int r = 0; r < A.tp_world; r++)
-    if (r != A.tp_rank) atomicCAS((int*)((char*)A.err + A.tp_delta[r]), 0, code);
+    if (r != A.tp_rank) atomicCAS(peer_ptr(A, A.err, r), 0, code);
 }
-
-// Bounded mbarrier wait by one thread: false (and the CTA abort flag and the error word set)
-// once kWaitNs pass, or when the CTA or another CTA has aborted.  Each try parks the thread
-// for up to 20 us unless the phase completes first.
-DPUF_DEV bool wait_bar(uint64_t* b, unsigned parity, DecShared& S, const DecodeArgs& A) {
-  int* err = A.err;
-  if (mbar_try(b, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (;;) {
-    if (mbar_try_for(b, parity, 20000u)) return true;
-    if (S.abort) return false;
-    if (*(volatile int*)err) {
-      S.abort = 1;
-      return false;
-    }
-    if (globaltimer() - t0 > kWaitNs) {
-      S.abort = 1;
-      raise_err(A, 1);
-      return false;
-    }
+DPUF_DEV bool check_abort(const DecodeArgs& A, DecShared& S) {
+  if (S.abort) return true;
+  if (*(volatile int*)A.err) {
+    S.abort = 1;
+    return true;
   }
+  return false;
 }
 
-// Bounded wait of one thread for a pair of tagged words to carry generation `gen`: re-reads
-// until they do; gives up (returning what it read) once the CTA or another CTA or rank has
-// aborted, or the wait limit has passed (error word 3).  Under tensor parallelism the limit
-// allows for other ranks' hosts launching later.
-DPUF_DEV ulonglong2 wait_tagged2(const uint64_t* p, unsigned gen, const DecodeArgs& A, DecShared& S) {
-  unsigned long long t0 = 0;
-  const unsigned long long limit = A.tp_world > 1 ? kTpWaitNs : kWaitNs;
-  for (int it = 0;; it++) {
-    const ulonglong2 w = ld_tagged2(p, A.tp_world > 1);
-    if ((tag_of(w.x) == gen && tag_of(w.y) == gen) || S.abort) return w;
-    if (it >= 4) __nanosleep(64);  // polls of many threads share L2 with the weight stream
-    if ((it & 31) == 31) {
-      if (*(volatile int*)A.err) {
-        S.abort = 1;
-        return w;
-      }
-      const unsigned long long now = globaltimer();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > limit) {
+// Waits (bounded) until every word j of wv whose bit is set in `stale` carries generation `gen`
+// (wv[j] holds a first read of *addr(j)); on abort, wv holds whatever was read last.  Each round
+// re-reads all the still-stale words at once, so a thread waiting for n words pays one memory
+// round trip per round, not one per word.  Rounds back off from 32 to 256 ns: thousands of
+// threads may poll at once, and every poll is an L2 request beside the weight stream.
+template <int N, class Addr>
+DPUF_DEV void wait_words(const DecodeArgs& A, uint64_t (&wv)[N], unsigned stale, Addr addr, unsigned gen,
+                         DecShared& S) {
+  if (!stale || S.abort) return;
+  const bool sys = A.tp_world > 1;
+  const unsigned long long t0 = globaltimer();
+  unsigned ns = 32;
+  for (int it = 1; stale; it++) {
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if ((stale >> j) & 1u) wv[j] = ld_relaxed(addr(j), sys);
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if (((stale >> j) & 1u) && tag_of(wv[j]) == gen) stale &= ~(1u << j);
+    if (stale && (it & 7) == 0) {
+      if (check_abort(A, S)) return;
+      if (globaltimer() - t0 > A.wait_ns) {
         raise_err(A, 3);
         S.abort = 1;
-        return w;
+        return;
       }
     }
   }
+}
+// The stale mask of N first reads.
+template <int N>
+DPUF_DEV unsigned stale_mask(const uint64_t (&wv)[N], unsigned valid, unsigned gen) {
+  unsigned m = 0;
+#pragma unroll
+  for (int j = 0; j < N; j++)
+    if (((valid >> j) & 1u) && tag_of(wv[j]) != gen) m |= 1u << j;
+  return m;
 }
 
 // ------------------------------------------------------------------ work plan
-struct Unit {
-  const uint8_t* tile;
-  int n_r;         // rows in the tile
-  int row;         // first row of the tile in its matrix
-  uint64_t* tout;  // tagged output of row `row` (chain epilogue), or null
-  float* out;      // plain output of row `row` (the LM head's logits), or null
-};
-
-DPUF_DEV int kind_cols(const DecodeArgs& A, int kind) {
+// A projection phase is a list of units: 8-row groups (q/k/v, o, down, LM head) or gate/up pairs
+// (the gate group and the up group of the same 8 rows).  The units are dealt in contiguous
+// ranges to the CTAs of all ranks (virtual CTA v = blockIdx.x * tp_world + tp_rank, so every
+// rank holds units of every phase), and a CTA's units to its consumer warps in turn.
+DPUF_DEV int phase_units(const DecodeArgs& A, int kind) {
+  switch (kind) {
+    case kQKV: return (A.qd + 2 * A.kvd) / 8;
+    case kO: return A.H / 8;
+    case kGU: return A.I / 8;
+    case kDown: return 2 * A.keep_down;
+    default: return 2 * ((A.V + 15) / 16);
+  }
+}
+DPUF_DEV int phase_cols(const DecodeArgs& A, int kind) {
   return kind == kO ? A.qd : (kind == kDown ? A.I : A.H);
 }
-DPUF_DEV int kind_units(const DecodeArgs& A, int kind) {
-  const int tq = (A.qd + 15) >> 4, tkv = (A.kvd + 15) >> 4, th = (A.H + 15) >> 4, ti = (A.I + 15) >> 4;
-  switch (kind) {
-    case kQKV: return tq + 2 * tkv;
-    case kO: return th;
-    case kGU: return ti;
-    case kDown: return A.keep_down;
-    default: return (A.V + 15) >> 4;
-  }
-}
+DPUF_DEV int vcta(const DecodeArgs& A) { return blockIdx.x * A.tp_world + A.tp_rank; }
 
-DPUF_DEV Unit make_unit(const uint8_t* tiles, long long stride, int rows, int t, uint64_t* tout,
-                       float* out = nullptr) {
-  Unit u;
-  u.tile = tiles + (size_t)t * stride;
-  u.row = t * kTileRows;
-  u.n_r = min(kTileRows, rows - u.row);
-  u.tout = tout ? tout + u.row : nullptr;
-  u.out = out ? out + u.row : nullptr;
-  return u;
+// (Computed once per launch into DecShared: the 64-bit divisions cost ~1 us of one thread.)
+DPUF_DEV Phase compute_phase(const DecodeArgs& A, int kind) {
+  Phase P;
+  const int U = phase_units(A, kind), G = gridDim.x * A.tp_world, c = vcta(A);
+  P.u0 = (int)((long long)U * c / G);
+  P.n = (int)((long long)U * (c + 1) / G) - P.u0;
+  P.a = P.n / kConsWarps;
+  P.extra = P.n % kConsWarps;
+  P.n_st = ((phase_cols(A, kind) >> 5) + kKB - 1) / kKB;
+  P.n_sub = kind == kGU ? 2 : 1;
+  P.spu = P.n_st * P.n_sub;
+  P.total = (long long)P.n * P.spu;
+  return P;
 }
+DPUF_DEV int warp_units(const Phase& P, int w) { return P.a + (w < P.extra ? 1 : 0); }
+// Ring position of warp w's stage r, relative to the phase's base:
+//   r < a*spu: r*kConsWarps + w;  else: a*spu*kConsWarps + (r - a*spu)*extra + w.
+// Producer and consumers walk it incrementally (produce_phase, consume_phase).
 
-DPUF_DEV Unit unit_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, int sub) {
+// One 8-row group: where its scales start (the group's data: [n_blk][8] fp16 scales, then
+// [n_blk][4][8][4] nibbles), its rows and its first output row.
+struct Group {
+  const uint8_t* base;
+  int n_r;   // rows (0: an empty second group of a short last tile)
+  int row;   // first output row
+  int mat;   // q/k/v: 0, 1, 2; gate/up pair: 0 gate, 1 up
+};
+DPUF_DEV Group rows_of(int rows, int gi, int mat) {
+  Group g;
+  g.row = (gi >> 1) * kTileRows + (gi & 1) * 8;
+  g.n_r = max(0, min(8, rows - g.row));
+  g.base = nullptr;
+  g.mat = mat;
+  return g;
+}
+DPUF_DEV Group make_group(const uint8_t* tiles, long long stride, int rows, int n_blk, int gi, int mat) {
+  Group g = rows_of(rows, gi, mat);
+  g.base = tiles + (size_t)(gi >> 1) * stride + 16 + (size_t)(gi & 1) * n_blk * 144;
+  return g;
+}
+DPUF_DEV const uint8_t* ldg_ptr(const uint8_t* const* p) { return (const uint8_t*)__ldg((const unsigned long long*)p); }
+// Group `sub` (gate/up: 0 gate, 1 up; else 0) of unit u of phase `kind` in layer l.
+DPUF_DEV Group group_of(const DecodeArgs& A, int l, int kind, int u, int sub) {
+  const int n_blk = phase_cols(A, kind) >> 5;
+  if (kind == kLM) return make_group(A.lm_tiles, A.lm_stride, A.V, n_blk, u, 0);
+  const DecLayer* Ly = A.layers + l;
   switch (kind) {
     case kQKV: {
-      const int tq = (A.qd + 15) >> 4, tkv = (A.kvd + 15) >> 4;
-      if (u < tq) return make_unit(Ly.tiles[0], Ly.stride[0], A.qd, u, A.q);
-      if (u < tq + tkv) return make_unit(Ly.tiles[1], Ly.stride[1], A.kvd, u - tq, A.k);
-      return make_unit(Ly.tiles[2], Ly.stride[2], A.kvd, u - tq - tkv, A.v);
+      const int gq = A.qd / 8, gk = A.kvd / 8;
+      if (u < gq) return make_group(ldg_ptr(&Ly->tiles[0]), __ldg(&Ly->stride[0]), A.qd, n_blk, u, 0);
+      if (u < gq + gk) return make_group(ldg_ptr(&Ly->tiles[1]), __ldg(&Ly->stride[1]), A.kvd, n_blk, u - gq, 1);
+      return make_group(ldg_ptr(&Ly->tiles[2]), __ldg(&Ly->stride[2]), A.kvd, n_blk, u - gq - gk, 2);
     }
-    case kO: return make_unit(Ly.tiles[3], Ly.stride[3], A.H, u, A.o_out);
-    case kGU: return sub == 0 ? make_unit(Ly.tiles[4], Ly.stride[4], A.I, u, nullptr)
-                              : make_unit(Ly.tiles[5], Ly.stride[5], A.I, u, A.s_out);
-    case kDown: return make_unit(Ly.tiles[6], Ly.stride[6], A.H, u, A.d_out);
-    default: return make_unit(A.lm_tiles, A.lm_stride, A.V, u, nullptr, A.logits);
+    case kO: return make_group(ldg_ptr(&Ly->tiles[3]), __ldg(&Ly->stride[3]), A.H, n_blk, u, 0);
+    case kGU: return make_group(ldg_ptr(&Ly->tiles[4 + sub]), __ldg(&Ly->stride[4 + sub]), A.I, n_blk, u, sub);
+    default: return make_group(ldg_ptr(&Ly->tiles[6]), __ldg(&Ly->stride[6]), A.H, n_blk, u, 0);
   }
 }
 
-// Contiguous unit range of CTA c in a projection of U units; the remainder units go to the
-// `U % G` CTAs starting at `rot`, which then advances by U % G.  With tensor parallelism the
-// G CTAs are all ranks' CTAs, interleaved (c = blockIdx.x * ranks + rank), so that every rank
-// gets units of every projection with at least `ranks` units: each rank then takes part in
-// every phase, which is what keeps a fast rank from overwriting an exchanged vector (with a
-// later generation) before a slow rank has read it.
-DPUF_DEV void take_range(const DecodeArgs& A, int U, int& rot, int& u0, int& n) {
-  const int G = gridDim.x * A.tp_world, c = blockIdx.x * A.tp_world + A.tp_rank;
-  const int v = (c - rot + G) % G;
-  const int base = U / G, ext = U % G;
-  n = base + (v < ext ? 1 : 0);
-  u0 = v * base + min(v, ext);
-  rot = (rot + ext) % G;
+// The rows of that group without its address (no memory access: the consumers' view).
+DPUF_DEV Group group_rows(const DecodeArgs& A, int kind, int u, int sub) {
+  switch (kind) {
+    case kQKV: {
+      const int gq = A.qd / 8, gk = A.kvd / 8;
+      if (u < gq) return rows_of(A.qd, u, 0);
+      if (u < gq + gk) return rows_of(A.kvd, u - gq, 1);
+      return rows_of(A.kvd, u - gq - gk, 2);
+    }
+    case kO: return rows_of(A.H, u, 0);
+    case kGU: return rows_of(A.I, u, sub);
+    case kDown: return rows_of(A.H, u, 0);
+    default: return rows_of(A.V, u, 0);
+  }
 }
 
 // ------------------------------------------------------------------ producer
+// The producer warp walks the CTA's stage sequence (every step, layer and phase) round by round:
+// lane w moves consumer warp w's stage of the round into ring slot (cursor + w) once that slot's
+// previous use is released.  One round (up to kConsWarps stages) then costs one pass of the
+// warp, not kConsWarps passes of one thread: the issue rate keeps up with the stream (a 4.6 KB
+// stage arrives every ~100 ns at the full rate, about one thread-iteration's worth of latency).
 struct Producer {
-  int slot = 0;
-  unsigned phase = 0;     // parity of the slot's current use
   long long issued = 0;
-  uint64_t policy = 0;    // L2 policy of the weight copies
+  int slot = 0;      // ring slot of the round's first stage
+  unsigned par = 0;  // parity of that slot's current use
+  uint64_t pol = 0;
 };
 
-// Copies of stage s of unit un into the half-slot dst; returns the bytes.
-DPUF_DEV unsigned copy_stage(const Unit& un, int n_blk, int s, unsigned char* dst, uint64_t* bar, uint64_t pol) {
-  const int groups = un.n_r > 8 ? 2 : 1;
-  const int kb = min(32, n_blk - s * 32);
-  for (int g = 0; g < groups; g++) {
-    const uint8_t* gp = un.tile + 16 + (size_t)g * n_blk * 144;
-    bulk_g2s(dst + (g ? kNib1 : 0), gp + (size_t)n_blk * 16 + (size_t)s * 4096, (unsigned)kb * 128, bar, pol);
-    bulk_g2s(dst + (g ? kSc1 : kSc0), gp + (size_t)s * 512, (unsigned)kb * 16, bar, pol);
-  }
-  return (unsigned)(groups * kb * 144);
-}
-
-DPUF_DEV bool produce_pair(const Unit& ua, const Unit& ub, bool has_b, int n_blk, int n_st, unsigned char* ring,
-                           int n_ring, Producer& P, DecShared& S, const DecodeArgs& A) {
-  for (int s = 0; s < n_st; s++) {
-    if (!wait_bar(&S.empty[P.slot], P.phase ^ 1u, S, A)) return false;
-    const int kb = min(32, n_blk - s * 32);
-    const unsigned bytes = (unsigned)(((ua.n_r > 8 ? 2 : 1) + (has_b ? (ub.n_r > 8 ? 2 : 1) : 0)) * kb * 144);
-    uint64_t* bar = &S.full[P.slot];
-    unsigned char* dst = ring + (size_t)P.slot * kSlotBytes;
-    mbar_expect_tx(bar, bytes);
-    copy_stage(ua, n_blk, s, dst, bar, P.policy);
-    if (has_b) copy_stage(ub, n_blk, s, dst + kHalf, bar, P.policy);
-    P.issued++;
-    if (++P.slot == n_ring) {
-      P.slot = 0;
-      P.phase ^= 1u;
+// A bounded wait for the completion of the phase of parity `par` of barrier `bar` (a slot's
+// release, or a stage's arrival); polls the abort flag.
+DPUF_DEV bool wait_bar(const DecodeArgs& A, uint64_t* bar, unsigned par, DecShared& S) {
+  if (mbar_try(bar, par)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (int it = 1; !mbar_try(bar, par); it++) {
+    if ((it & 63) == 0) {
+      if (check_abort(A, S)) return false;
+      if (globaltimer() - t0 > A.wait_ns) {
+        raise_err(A, 1);
+        S.abort = 1;
+        return false;
+      }
     }
   }
   return true;
 }
 
-// Units of a projection are consumed in pairs: for gate/up, (gate tile u, up tile u); for the
-// others, consecutive units of the CTA's range (the last one alone when the count is odd).
-DPUF_DEV void pair_of(const DecodeArgs& A, const DecLayer& Ly, int kind, int u, int u_end, Unit& ua, Unit& ub,
-                      bool& has_b, int& step) {
-  if (kind == kGU) {
-    ua = unit_of(A, Ly, kind, u, 0);
-    ub = unit_of(A, Ly, kind, u, 1);
-    has_b = true;
-    step = 1;
-  } else {
-    ua = unit_of(A, Ly, kind, u, 0);
-    has_b = u + 1 < u_end;
-    ub = has_b ? unit_of(A, Ly, kind, u + 1, 0) : ua;
-    step = 2;
-  }
-}
-
-DPUF_DEV bool produce_phase(const DecodeArgs& A, const DecLayer* layers, int l, int kind, int& rot,
-                            unsigned char* ring, int n_ring, Producer& P, DecShared& S) {
-  int u0, n;
-  take_range(A, kind_units(A, kind), rot, u0, n);
-  const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
-  const DecLayer& Ly = layers[kind == kLM ? 0 : l];
-  for (int u = u0, step = 1; u < u0 + n; u += step) {
-    Unit ua, ub;
-    bool has_b;
-    pair_of(A, Ly, kind, u, u0 + n, ua, ub, has_b, step);
-    if (!produce_pair(ua, ub, has_b, n_blk, n_st, ring, n_ring, P, S, A)) return false;
+DPUF_DEV bool produce_phase(const DecodeArgs& A, int l, int kind, unsigned char* ring, Producer& P, DecShared& S) {
+  const int lane = threadIdx.x & 31;
+  const Phase ph = S.ph[kind];
+  const int n_blk = phase_cols(A, kind) >> 5;
+  const size_t nib0 = (size_t)n_blk * 16;
+  const int n_k = ph.a + (ph.extra ? 1 : 0);
+  for (int k = 0; k < n_k; k++) {
+    const int W = k < ph.a ? kConsWarps : ph.extra;
+    const bool mine = lane < W;
+    for (int sub = 0; sub < ph.n_sub; sub++) {
+      const uint8_t* gb = nullptr;
+      if (mine) {
+        const Group g = group_of(A, l, kind, ph.u0 + lane + k * kConsWarps, sub);
+        if (g.n_r > 0) gb = g.base;
+      }
+      for (int s = 0; s < ph.n_st; s++) {
+        const int kb = min(kKB, n_blk - s * kKB);
+        int slot = P.slot + lane;
+        unsigned par = P.par;
+        if (slot >= A.n_slots) {  // W <= n_slots: one wrap at most
+          slot -= A.n_slots;
+          par ^= 1u;
+        }
+        // at most max_inflight stages requested and not yet landed: the round's last stage
+        // waits for the one max_inflight positions before it (copies land about in order).
+        // max_inflight >= W puts that position before this round; n_slots > max_inflight + W
+        // keeps its slot from being reissued before it.
+        bool ok = true;
+        const int back = W - 1 - A.max_inflight;
+        if (lane == 0 && P.issued + back >= 0) {
+          int qs = P.slot + back;
+          unsigned qp = P.par;
+          if (qs < 0) {
+            qs += A.n_slots;
+            qp ^= 1u;
+          }
+          ok = wait_bar(A, &S.full[qs], qp, S);
+        }
+        // the slot's previous use must be released (the first use passes at once)
+        if (ok && mine) ok = wait_bar(A, &S.empty[slot], par ^ 1u, S);
+        if (!__all_sync(kFull, ok)) return false;
+        if (mine) {
+          uint64_t* bar = &S.full[slot];
+          if (gb == nullptr) {
+            mbar_arrive(bar);  // empty group: nothing to copy, the consumer skips it
+          } else {
+            unsigned char* dst = ring + (size_t)slot * kSlotBytes;
+            mbar_expect_tx(bar, (unsigned)kb * 144);
+            bulk_g2s(dst, gb + (size_t)s * kScBytes, (unsigned)kb * 16, bar, P.pol);
+            bulk_g2s(dst + kScBytes, gb + nib0 + (size_t)s * (kKB * 128), (unsigned)kb * 128, bar, P.pol);
+          }
+        }
+        P.slot += W;
+        if (P.slot >= A.n_slots) {
+          P.slot -= A.n_slots;
+          P.par ^= 1u;
+        }
+        P.issued += W;
+      }
+      if (S.abort) return false;
+    }
   }
   return true;
 }
 
-// ------------------------------------------------------------------ consumers
-struct Consumer {
-  int slot = 0;
-  unsigned phase = 0;  // ring parity
-  int pb = 0;
-  int rot = 0;
-  unsigned item = 0;   // slots consumed so far (team of a slot = item % kTeams)
-};
-
-DPUF_DEV void cbar() { named_sync(kBarConsumers, kConsumers); }
-// Barrier of the consumer threads that also returns whether any of them passed true.
-DPUF_DEV bool cbar_or(bool v) {
-  unsigned r;
-  asm volatile(
-      "{ .reg .pred p, q; setp.ne.u32 q, %1, 0; bar.red.or.pred p, %2, %3, q; selp.u32 %0, 1, 0, p; }"
-      : "=r"(r)
-      : "r"((unsigned)v), "r"(kBarConsumers), "r"(kConsumers)
-      : "memory");
-  return r != 0;
-}
-
-// Dot warp w: blocks 4w..4w+3 of both units of the slot; lane = (unit lane/16, row lane%16)
-// computes dot = sum_k u_k q_k with dp4a on the row's nibbles (low nibbles against x bytes
-// 8c..8c+3, high against 8c+4..8c+7) and stores p = float(dot - xm), s = ws * xs (0, 0 for
-// a skipped block) at buf[unit][row][block].  kAll: all four blocks exist (a full stage), so
-// the four independent computations are scheduled together without guards.
-DPUF_DEV float2 dot_pair(const unsigned char* wb, const unsigned char* sb, const int8_t* xq, const float* xs,
-                         const int* xm, int b0, int bb) {
-  const int4 xa = *(const int4*)(xq + (b0 + bb) * 32), xc = *(const int4*)(xq + (b0 + bb) * 32 + 16);
-  const uint32_t w0 = *(const uint32_t*)(wb + bb * 128), w1 = *(const uint32_t*)(wb + bb * 128 + 32);
-  const uint32_t w2 = *(const uint32_t*)(wb + bb * 128 + 64), w3 = *(const uint32_t*)(wb + bb * 128 + 96);
-  int d0 = __dp4a((int)(w0 & 0x0F0F0F0Fu), xa.x, 0);
-  int d1 = __dp4a((int)((w0 >> 4) & 0x0F0F0F0Fu), xa.y, 0);
-  d0 = __dp4a((int)(w1 & 0x0F0F0F0Fu), xa.z, d0);
-  d1 = __dp4a((int)((w1 >> 4) & 0x0F0F0F0Fu), xa.w, d1);
-  d0 = __dp4a((int)(w2 & 0x0F0F0F0Fu), xc.x, d0);
-  d1 = __dp4a((int)((w2 >> 4) & 0x0F0F0F0Fu), xc.y, d1);
-  d0 = __dp4a((int)(w3 & 0x0F0F0F0Fu), xc.z, d0);
-  d1 = __dp4a((int)((w3 >> 4) & 0x0F0F0F0Fu), xc.w, d1);
-  const int b = b0 + bb;
-  const float bsc = xs[b];
-  const float ws = f16bits_to_f32(*(const uint16_t*)(sb + bb * 16));
-  const float2 pr = make_float2((float)(d0 + d1 - xm[b]), __fmul_rn(ws, bsc));
-  return bsc > 0.0f ? pr : make_float2(0.0f, 0.0f);
-}
-
-template <bool kAll>
-DPUF_DEV void dot_stage(const unsigned char* st, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
-                        bool has_b, int warp, int lane, float2* buf) {
-  const int unit = lane >> 4, r = lane & 15, g = r >> 3, ri = r & 7;
-  if (unit == 1 && !has_b) return;
-  const unsigned char* ut = st + unit * kHalf;
-  const unsigned char* wb = ut + (g ? kNib1 : 0) + ri * 4;
-  const unsigned char* sb = ut + (g ? kSc1 : kSc0) + ri * 2;
-  float2* o = buf + (unit * 16 + r) * kPsRow + warp * 4;
-  if (kAll) {
-    float2 pr[4];
+// ------------------------------------------------------------------ one stage of one group
+// Lane (ri, q): row ri's blocks 8q .. 8q+7 of the stage; then the in-order chain over the
+// stage's blocks, octet by octet (octet q continues the accumulator of octet q-1).
+template <bool kFull>
+DPUF_DEV void stage_chain(const unsigned char* slot, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
+                          int ri, int q, float& acc) {
+  const unsigned char* nib = slot + kScBytes;
+  float pp[8], ss[8];
 #pragma unroll
-    for (int j = 0; j < 4; j++) pr[j] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
-    *(float4*)o = make_float4(pr[0].x, pr[0].y, pr[1].x, pr[1].y);
-    *(float4*)(o + 2) = make_float4(pr[2].x, pr[2].y, pr[3].x, pr[3].y);
-  } else {
-    for (int j = 0; j < 4; j++)
-      if (warp * 4 + j < kb) o[j] = dot_pair(wb, sb, xq, xs, xm, b0, warp * 4 + j);
+  for (int j = 0; j < 8; j++) {
+    const int bl = q * 8 + j;
+    pp[j] = 0.0f;
+    ss[j] = 0.0f;
+    if (kFull || bl < kb) {
+      const int b = b0 + bl;
+      int dlo = 0, dhi = 0;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; c4++) {
+        const int cc = (c4 + q) & 3;
+        const uint32_t w = *(const uint32_t*)(nib + bl * 128 + cc * 32 + ri * 4);
+        const int2 xv = *(const int2*)(xq + b * 32 + cc * 8);
+        dlo = dp4a_us(w & 0x0F0F0F0Fu, xv.x, dlo);
+        dhi = dp4a_us(w & 0xF0F0F0F0u, xv.y, dhi);
+      }
+      const float bsc = xs[b];
+      const float ws = f16bits_to_f32(*(const uint16_t*)(slot + bl * 16 + ri * 2));
+      pp[j] = (float)(dlo + (dhi >> 4) - xm[b]);
+      // a block with xs == 0 is skipped by the reference: (0, 0) leaves the chain unchanged
+      ss[j] = bsc > 0.0f ? __fmul_rn(ws, bsc) : 0.0f;
+      if (!(bsc > 0.0f)) pp[j] = 0.0f;
+    }
+  }
+#pragma unroll
+  for (int qq = 0; qq < 4; qq++) {
+    if (q == qq) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc = __fmaf_rn(pp[j], ss[j], acc);
+    }
+    acc = __shfl_sync(kFull, acc, ri + 8 * qq);
   }
 }
 
@@ -469,232 +468,214 @@ DPUF_DEV void better(float& bv, int& bi, float v, int i) {
   }
 }
 
-// One projection on the consumer side.
-DPUF_DEV void consume_phase(const DecodeArgs& A, const DecLayer& Ly, int kind, unsigned gen, Consumer& C,
-                            unsigned char* ring, int n_ring, const int8_t* xq, const float* xs, const int* xm,
-                            float2* ps, DecShared& S) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = lane >> 4, r = lane & 15;
-  int u0, n;
-  take_range(A, kind_units(A, kind), C.rot, u0, n);
-  const int n_blk = kind_cols(A, kind) >> 5, n_st = (n_blk + 31) >> 5;
-  float bv = -INFINITY;
+// Per-warp consuming state.
+struct Consumer {
+  int slot = 0;          // ring slot of the current phase's first stage
+  unsigned par = 0;      // parity of that slot's use
+  float bv = -INFINITY;  // running argmax of the LM head (lanes of octet 0)
   int bi = 0x7fffffff;
-  for (int u = u0, step = 1; u < u0 + n; u += step) {
-    Unit ua, ub;
-    bool has_b;
-    pair_of(A, Ly, kind, u, u0 + n, ua, ub, has_b, step);
-    float acc = 0.0f;
-    for (int s = 0; s < n_st; s++) {
-      const int kb = min(32, n_blk - s * 32);
-      float2* buf = ps + C.pb * kPsBuf;
-      if (warp < kMmaWarps) {
-        if ((int)(C.item % kTeams) == warp / kTeamWarps) {
-          const int wt = warp % kTeamWarps;
-          bool ok = true;
-          if (lane == 0) ok = wait_bar(&S.full[C.slot], C.phase, S, A);
-          named_sync(kBarEmptied + C.pb, kHandoff);  // the chain is done with this pair buffer
-          if (__shfl_sync(kFull, (int)ok, 0)) {
-            if (kb == 32)
-              dot_stage<true>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, wt, lane, buf);
-            else
-              dot_stage<false>(ring + (size_t)C.slot * kSlotBytes, xq, xs, xm, s * 32, kb, has_b, wt, lane, buf);
-          }
-          __syncwarp();
-          named_arrive(kBarFilled + C.pb, kHandoff);
-          if (lane == 0) mbar_arrive(&S.empty[C.slot]);
-        }
-      } else {
-        named_sync(kBarFilled + C.pb, kHandoff);  // the dot warps filled this pair buffer
-        if (!S.abort && (half == 0 || has_b)) {
-          const float2* row = buf + (half * 16 + r) * kPsRow;
-          if (kb == 32) {
-            // all 32 pairs are loaded (two per 16-byte load) before the chain starts
-            float4 v[16];
-#pragma unroll
-            for (int q = 0; q < 16; q++) v[q] = *(const float4*)(row + 2 * q);
-#pragma unroll
-            for (int q = 0; q < 16; q++) {
-              acc = __fmaf_rn(v[q].x, v[q].y, acc);
-              acc = __fmaf_rn(v[q].z, v[q].w, acc);
-            }
-          } else {
-            for (int b = 0; b < kb; b++) {
-              const float2 v = row[b];
-              acc = __fmaf_rn(v.x, v.y, acc);
-            }
-          }
-        }
-        named_arrive(kBarEmptied + C.pb, kHandoff);
-      }
-      C.item++;
-      if (++C.slot == n_ring) {
-        C.slot = 0;
-        C.phase ^= 1u;
-      }
-      if (++C.pb == kNPs) C.pb = 0;
-    }
-    // ---- epilogue of the pair (chain warp: lanes 0..15 unit A's rows, 16..31 unit B's)
-    if (warp == kChainWarp) {
-      if (kind == kGU) {
-        const float up = __shfl_down_sync(kFull, acc, 16);
-        if (half == 0 && r < ua.n_r) {
-          const int row = ua.row + r;
-          put_tagged(A, A.s_out + row,
-                     tagged(swiglu_one(acc, up, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et),
-                            gen));
-        }
-      } else if (half == 0 || has_b) {
-        const Unit& un = half ? ub : ua;
-        if (r < un.n_r) {
-          if (kind == kLM) {
-            if (A.write_logits) put_float(A, un.out + r, acc);
-            better(bv, bi, acc, un.row + r);
-          } else {
-            put_tagged(A, un.tout + r, tagged(acc, gen));
-          }
-        }
-      }
-    }
-  }
-  if (kind == kLM && warp == kChainWarp) {
-    for (int m = 16; m; m >>= 1) {
-      const float ov = __shfl_xor_sync(kFull, bv, m);
-      const int oi = __shfl_xor_sync(kFull, bi, m);
-      better(bv, bi, ov, oi);
-    }
-    // other ranks' hosts read this CTA's logits once they have seen its partial
-    if (A.tp_world > 1 && A.write_logits) __threadfence_system();
-    if (lane == 0) {
-      const int g_all = gridDim.x * A.tp_world;
-      uint64_t* pw = A.part + ((size_t)(gen & 1) * g_all + A.tp_rank * gridDim.x + blockIdx.x) * 2;
-      put_tagged(A, pw, tagged(bv, gen));
-      put_tagged(A, pw + 1, ((uint64_t)gen << 32) | (unsigned)bi);
-    }
-  }
-  if (warp == kChainWarp) {
-    __syncwarp();
-    if (lane == 0) count_done(A, 0);
-  }
-}
+};
 
-// Bounded poll by one thread until a counter has reached `target` (wrap-safe), the CTA or
-// another CTA (or rank) has aborted, or the wait limit has passed (error word 2).
-DPUF_DEV void wait_count(const DecodeArgs& A, const unsigned* ctr, unsigned target, DecShared& S) {
-  unsigned long long t0 = 0;
-  const unsigned long long limit = A.tp_world > 1 ? kTpWaitNs : kWaitNs;
-  for (int it = 0; !S.abort; it++) {
-    if ((int)(ld_acquire(ctr) - target) >= 0) break;
-    if (*(volatile int*)A.err) {
-      S.abort = 1;
-      break;
-    }
-    if ((it & 15) == 15) {
-      const unsigned long long now = globaltimer();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > limit) {
-        raise_err(A, 2);
+// Waits (bounded, every lane) for a stage to land; false once the CTA aborted.
+DPUF_DEV bool ring_wait(const DecodeArgs& A, uint64_t* bar, unsigned ph, DecShared& S) {
+  if (S.abort) return false;
+  if (mbar_try(bar, ph)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (int it = 1;; it++) {
+    if (mbar_try(bar, ph)) return true;
+    if ((it & 63) == 0) {
+      if (check_abort(A, S)) return false;
+      if (globaltimer() - t0 > A.wait_ns) {
+        raise_err(A, 1);
         S.abort = 1;
-        break;
+        return false;
       }
     }
-    __nanosleep(20);
   }
 }
 
-// Grid-wide barrier of the consumer threads of this GPU (the producer never joins): arrive on
-// a global counter (release) and wait, bounded, until every CTA has arrived `target /
-// gridDim.x` times (acquire).
-DPUF_DEV void grid_sync(const DecodeArgs& A, unsigned& target, DecShared& S) {
-  cbar();
-  target += gridDim.x;
-  if (threadIdx.x == 0) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.bar) : "memory");
-    wait_count(A, A.bar, target, S);
-  }
-  cbar();
-}
-
-// Async copies by the consumer threads into shared memory: 16-byte pieces through L2 (data
-// other CTAs wrote; bytes % 16 == 0) and 8-byte pieces of read-only tables (bytes % 8 == 0).
-DPUF_DEV void stage16(void* dst, const void* src, int bytes) {
-  for (int i = threadIdx.x * 16; i < bytes; i += kConsumers * 16)
-    cp_async16_cg((unsigned char*)dst + i, (const unsigned char*)src + i);
-}
-DPUF_DEV void stage8(void* dst, const void* src, int bytes) {
-  for (int i = threadIdx.x * 8; i < bytes; i += kConsumers * 8)
-    cp_async8_ca((unsigned char*)dst + i, (const unsigned char*)src + i);
-}
-
-// Stages words [0, n) (n even) of a tagged vector that other CTAs (or ranks) produce in
-// generation `gen`, together with whatever async copies the caller has issued (all consumer
-// threads call this).  Each thread copies its 16-byte pieces and waits; if any thread finds a
-// piece that predates `gen`, thread 0 alone waits (bounded) until completion counter ctr_i
-// reaches `target`, then every thread re-copies its stale pieces, and repeats (waiting on its
-// first stale piece itself) until no thread has one.  On return every staged word carries
-// `gen` (or the CTA has aborted) and the consumer threads have passed a CTA barrier.
-DPUF_DEV void stage_tagged(uint64_t* dst, const uint64_t* src, int n, unsigned gen, int ctr_i, unsigned target,
-                           const DecodeArgs& A, DecShared& S) {
-  for (int i = threadIdx.x * 2; i < n; i += kConsumers * 2) cp_async16_cg(dst + i, src + i);
-  cp_async_commit_wait_all();
-  auto first_stale = [&]() {
-    for (int i = threadIdx.x * 2; i < n; i += kConsumers * 2) {
-      const ulonglong2 w = *(const ulonglong2*)(dst + i);
-      if (tag_of(w.x) != gen || tag_of(w.y) != gen) return i;
+// The prep of one 64-column chunk of the down projection's input from its 64 tagged SwiGLU
+// outputs (generation gen), by one warp (lanes 0..7 hold columns 8i .. 8i+7; the other lanes
+// compute the same and store nothing), into every rank's dprep as tagged words.  sb: the lane's
+// column-sign byte of the chunk (0 without signs).
+DPUF_DEV void prep_down_chunk(const DecodeArgs& A, int ch, unsigned gen, uint8_t sb, DecShared& S) {
+  const int lane = threadIdx.x & 31, qi = lane & 7;
+  const uint64_t* src = A.s_raw + ch * 64 + qi * 8;
+  uint64_t wv[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) wv[j] = ld_relaxed(src + j, A.tp_world > 1);
+  wait_words(A, wv, stale_mask(wv, 0xFFu, gen), [&](int j) { return src + j; }, gen, S);
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] = value_of(wv[j]);
+  const PrepOut o = prep_chunk_g8_core(v, sb, lane);
+  if (lane < 8) {
+    uint64_t* dst = A.dprep + (size_t)ch * kChunkWords;
+    const uint64_t tg = (uint64_t)gen << 32;
+    put_tagged(A, dst + 2 * qi, tg | o.lo);
+    put_tagged(A, dst + 2 * qi + 1, tg | o.hi);
+    if ((qi & 3) == 0) {
+      put_tagged(A, dst + 16 + (qi >> 2), tagged(o.xs, gen));
+      put_tagged(A, dst + 18 + (qi >> 2), tg | (unsigned)o.xm);
     }
-    return -1;
-  };
-  int first = first_stale();
-  if (!cbar_or(first >= 0)) return;
-  if (threadIdx.x == 0) wait_count(A, A.ctr + ctr_i, target, S);
-  cbar();
-  for (int round = 0;; round++) {
-    if (first >= 0 && !S.abort) {
-      if (round > 0) *(ulonglong2*)(dst + first) = wait_tagged2(src + first, gen, A, S);
-      for (int i = first; i < n; i += kConsumers * 2) {
-        const ulonglong2 w = *(const ulonglong2*)(dst + i);
-        if (tag_of(w.x) != gen || tag_of(w.y) != gen) cp_async16_cg(dst + i, src + i);
+  }
+}
+
+// Optional trace of the last step: per CTA, the time (globaltimer, ns) at which each phase ended.
+enum {
+  kEvNorm1Res, kEvNorm1Chain, kEvNorm1, kEvQKV, kEvAttnIn, kEvAttnWait, kEvAttnRope, kEvAttnScores, kEvAttnSoftmax,
+  kEvAttnPV, kEvAttn, kEvLoadO, kEvO, kEvNorm2Res, kEvNorm2Chain, kEvNorm2, kEvGUStages, kEvGU, kEvLoadD, kEvDown,
+  kEvPerLayer
+};
+enum { kEvStart, kEvEmbed, kEvNormF, kEvLM, kEvArg, kEvPerStep };
+DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
+  if (A.trace && step == A.n_steps - 1 && threadIdx.x == 0)
+    A.trace[(size_t)blockIdx.x * A.trace_per_cta + ev] = globaltimer();
+}
+
+// One projection phase on the consumer side of warp `warp`: every unit of the warp, every group,
+// every stage; the epilogue stores the rows.
+DPUF_DEV void consume_phase(const DecodeArgs& A, int step, int l, int kind, unsigned gen, unsigned char* ring,
+                            Consumer& C, const int8_t* xq, const float* xs, const int* xm, DecShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ri = lane & 7, q = lane >> 3;
+  const Phase ph = S.ph[kind];
+  const int n_w = warp_units(ph, warp);
+  const int n_blk = phase_cols(A, kind) >> 5;
+  const bool stall = step == 0 && l == 0 && kind == kQKV && A.stall_unit >= ph.u0 && A.stall_unit < ph.u0 + ph.n;
+  // gate/up: the down projection's sign table, read now so that its latency hides behind the
+  // stages (the sign byte itself is read after the gate half of the unit)
+  const uint8_t* dsigns = kind == kGU ? ldg_ptr(&A.layers[l].signs[3]) : nullptr;
+  // ring cursor of this warp's stages: positions (phase start) + w, then +kConsWarps per stage
+  // through the full rounds, then +extra through the last (partial) round
+  const long long full = (long long)ph.a * ph.spu;
+  int slot = C.slot + warp;
+  unsigned par = C.par;
+  if (slot >= A.n_slots) {
+    slot -= A.n_slots;
+    par ^= 1u;
+  }
+  int r = 0;
+  if (kind == kGU && n_w == 0) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+  for (int k = 0; k < n_w; k++) {
+    const int u = ph.u0 + warp + k * kConsWarps;
+    float accs[2] = {0.0f, 0.0f};
+    Group g{};
+    uint8_t dsb = 0;
+    for (int sub = 0; sub < ph.n_sub; sub++) {
+      g = group_rows(A, kind, u, sub);
+      if (sub == 1 && dsigns && (u & 7) == 7) dsb = __ldg(dsigns + (u >> 3) * 8 + (lane & 7));
+      float acc = 0.0f;
+      for (int s = 0; s < ph.n_st; s++, r++) {
+        if (r > 0) {
+          slot += r <= full ? kConsWarps : ph.extra;
+          while (slot >= A.n_slots) {
+            slot -= A.n_slots;
+            par ^= 1u;
+          }
+        }
+        const bool ok = __all_sync(kFull, ring_wait(A, &S.full[slot], par, S));
+        if (ok && g.n_r > 0) {
+          const int b0 = s * kKB, kb = min(kKB, n_blk - b0);
+          const unsigned char* st = ring + (size_t)slot * kSlotBytes;
+          if (kb == kKB)
+            stage_chain<true>(st, xq, xs, xm, b0, kb, ri, q, acc);
+          else
+            stage_chain<false>(st, xq, xs, xm, b0, kb, ri, q, acc);
+        }
+        __syncwarp();  // every lane is done with the slot: release it
+        if (lane == 0) mbar_arrive(&S.empty[slot]);
       }
-      cp_async_commit_wait_all();
-      first = first_stale();
+      accs[sub] = acc;
     }
-    if (!cbar_or(first >= 0 && !S.abort)) return;
+    if (kind == kGU && k == n_w - 1) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+    // ---- epilogue: lanes of octet 0 hold rows g.row + ri
+    const bool mine = q == 0 && ri < g.n_r;
+    const int row = g.row + ri;
+    if (kind == kQKV) {
+      uint64_t* dst = g.mat == 0 ? A.q : (g.mat == 1 ? A.k : A.v);
+      if (mine && !stall) put_tagged(A, dst + row, tagged(accs[0], gen));
+    } else if (kind == kO) {
+      if (mine) put_tagged(A, A.o_out + row, tagged(accs[0], gen));
+    } else if (kind == kDown) {
+      if (mine) put_tagged(A, A.d_out + row, tagged(accs[0], gen));
+    } else if (kind == kLM) {
+      if (mine) {
+        if (A.write_logits) put_float(A, A.logits + row, accs[0]);
+        better(C.bv, C.bi, accs[0], row);
+      }
+    } else {
+      // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every
+      // rank; the warp holding the last pair of a 64-column chunk preps that chunk
+      if (mine)
+        put_tagged(A, A.s_raw + row,
+                   tagged(swiglu_one(accs[0], accs[1], A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et),
+                          gen));
+      if ((u & 7) == 7) {
+        __syncwarp();
+        prep_down_chunk(A, u >> 3, gen, dsb, S);
+      }
+    }
+  }
+  {  // the next phase starts ph.total positions later
+    const int tot = (int)ph.total, q = tot / A.n_slots;
+    C.slot += tot - q * A.n_slots;
+    C.par ^= (unsigned)q & 1u;
+    if (C.slot >= A.n_slots) {
+      C.slot -= A.n_slots;
+      C.par ^= 1u;
+    }
   }
 }
 
-// Residual add, RMSNorm and activation prep of the result (add_and_rms_norm_f32 /
-// rms_norm_f32, dpuf_engine.c:225-272, then the prep).  The residual (optional; tagged words of
-// generation `gen` from other CTAs; rows >= n_valid add 0, as the pruned down projection's
-// zero rows do), the gains and the sign bytes are staged in one async round (plus re-copies
-// of residual words staged before they were produced); all threads add the residual, then
-// threads 0..7 run the eight "AVX lane" chains over h after the residual add, 32 elements at
-// a time.
+// ------------------------------------------------------------------ row-wide steps
+DPUF_DEV void cta_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kConsThreads) : "memory"); }
+
+
+// Residual add (tagged words of generation `gen`; rows >= n_valid add 0, as the pruned down
+// projection's zero rows do), RMSNorm (add_and_rms_norm_f32 / rms_norm_f32,
+// dpuf_engine.c:225-272) and the activation prep of the result into x.  The gains and the sign
+// bytes go to shared memory (stage) asynchronously before the residual is waited for.
 DPUF_DEV void norm_prep(const DecodeArgs& A, float* h, const uint64_t* res, unsigned gen, int n_valid, const float* w,
-                        int H, float eps, const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage,
-                        DecShared& S) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint64_t* sr = (uint64_t*)stage;  // [H] tagged residual
-  float* sw = stage + 2 * H;         // [H] gains
-  uint8_t* sg = (uint8_t*)(stage + 3 * H);
-  stage16(sw, w, H * 4);
-  if (signs) stage8(sg, signs, H / 8);
-  if (res)
-    stage_tagged(sr, res, min(H, n_valid), gen, 0, gen * (unsigned)(gridDim.x * A.tp_world), A, S);
-  else
-    cp_async_commit_wait_all();
-  cbar();
+                        const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S, int step,
+                        int ev) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = A.H;
+  float* sw = stage;
+  uint8_t* sg = (uint8_t*)(stage + H);
+  for (int i = tid * 4; i < H; i += kConsThreads * 4) cp_async16_cg(sw + i, w + i);
+  if (signs)
+    for (int i = tid * 8; i < H / 8; i += kConsThreads * 8) cp_async8_ca(sg + i, signs + i);
+  cp_async_commit();
   if (res) {
-    for (int i = tid; i < H; i += kConsumers) h[i] = __fadd_rn(h[i], i < n_valid ? value_of(sr[i]) : 0.0f);
-    cbar();
+    // every word is loaded first (all in flight), then the stale ones are waited for
+    constexpr int kPer = 12;
+    const bool sys = A.tp_world > 1;
+    for (int i0 = tid; i0 < H; i0 += kConsThreads * kPer) {
+      uint64_t wv[kPer];
+      unsigned valid = 0;
+#pragma unroll
+      for (int j = 0; j < kPer; j++) {
+        const int i = i0 + j * kConsThreads;
+        const bool ok = i < H && i < n_valid;
+        wv[j] = ok ? ld_relaxed(res + i, sys) : 0;
+        if (ok) valid |= 1u << j;
+      }
+      wait_words(A, wv, stale_mask(wv, valid, gen), [&](int j) { return res + i0 + j * kConsThreads; }, gen, S);
+#pragma unroll
+      for (int j = 0; j < kPer; j++) {
+        const int i = i0 + j * kConsThreads;
+        if (i < H) h[i] = __fadd_rn(h[i], ((valid >> j) & 1u) ? value_of(wv[j]) : 0.0f);
+      }
+    }
+    cta_sync();
   }
+  if (ev >= 0) trace_at(A, step, ev);
   if (tid < 8) S.lanes[tid] = sumsq_lane32(h, H & ~7, tid);
-  cbar();
-  if (tid == 0) S.inv = rms_inv(S.lanes, h, H, eps);
-  cbar();
-  const float inv = S.inv;
+  cp_async_wait_pending(0);
+  cta_sync();
+  if (ev >= 0) trace_at(A, step, ev + 1);
+  const float inv = rms_inv(S.lanes, h, H, A.eps);  // every thread, same bits
   const int nch = H / 64;
-  for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
+  for (int cb = warp * 4; cb < nch; cb += kConsThreads / 8) {
     const int c = cb + (lane >> 3);
     const bool active = c < nch;
     const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
@@ -711,416 +692,454 @@ DPUF_DEV void norm_prep(const DecodeArgs& A, float* h, const uint64_t* res, unsi
     v[7] = __fmul_rn(__fmul_rn(h1.w, inv), w1.w);
     prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, active ? c * 64 : 0, lane, xq, xs, xm);
   }
+  cta_sync();
 }
 
-// Distributed prep of the gate/up output (tagged words of generation `gen`) for the down
-// projection: 64-column chunk ch is prepped by one CTA of all ranks (virtual CTA ch mod the
-// CTA count; eight lanes per chunk, so a warp preps four).  One GPU: the CTA stores the codes,
-// block scales and block sums as plain values, read by every CTA after a grid barrier.
-// Several ranks: it publishes them to every rank as tagged words of the same generation (four
-// codes per word) and counts its prep on completion counter 1.
-DPUF_DEV void prep_slices(const DecodeArgs& A, const uint8_t* signs, unsigned gen, DecShared& S) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = gridDim.x * A.tp_world, vc = blockIdx.x * A.tp_world + A.tp_rank;
-  const int nch = A.I / 64;
-  uint64_t* dq = A.dprep;
-  uint64_t* ds = dq + A.I / 4;
-  uint64_t* dm = ds + A.I / 32;
-  for (int k0 = warp * 4; vc + k0 * G < nch; k0 += kConsumers / 8) {
-    const int ch = vc + (k0 + (lane >> 3)) * G;
-    const bool active = ch < nch;
-    const int col = (active ? ch : 0) * 64 + (lane & 7) * 8;
-    const uint8_t sbyte = (active && signs) ? __ldg(signs + (col >> 3)) : 0;  // issued before the waits
-    float v[8];
+// A prepped projection input (n_ch chunks of kChunkWords tagged words, generation `gen`) into x:
+// codes, block scales, block sums.
+DPUF_DEV void load_prepped(const DecodeArgs& A, const uint64_t* src, int n_ch, unsigned gen, int8_t* xq, float* xs,
+                           int* xm, DecShared& S) {
+  const int n = n_ch * kChunkWords;
+  const bool sys = A.tp_world > 1;
+  constexpr int kPer = 12;
+  for (int i0 = threadIdx.x; i0 < n; i0 += kConsThreads * kPer) {
+    uint64_t wv[kPer];
+    unsigned valid = 0;
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      ulonglong2 w = make_ulonglong2(0, 0);
-      if (active) {
-        w = ld_tagged2(A.s_out + col + j, A.tp_world > 1);
-        if (tag_of(w.x) != gen || tag_of(w.y) != gen) w = wait_tagged2(A.s_out + col + j, gen, A, S);
-      }
-      v[j] = value_of(w.x);
-      v[j + 1] = value_of(w.y);
+    for (int j = 0; j < kPer; j++) {
+      const int i = i0 + j * kConsThreads;
+      wv[j] = i < n ? ld_relaxed(src + i, sys) : 0;
+      if (i < n) valid |= 1u << j;
     }
-    const PrepOut o = prep_chunk_g8_core(v, sbyte, lane);
-    if (active && A.tp_world == 1) {
-      *(uint2*)(A.xd_q8 + col) = make_uint2(o.lo, o.hi);
-      if ((lane & 3) == 0) {
-        A.xd_xs[col >> 5] = o.xs;
-        A.xd_xm[col >> 5] = o.xm;
-      }
-    } else if (active) {
-      const uint64_t tg = (uint64_t)gen << 32;
-      put_tagged(A, dq + col / 4, tg | o.lo);
-      put_tagged(A, dq + col / 4 + 1, tg | o.hi);
-      if ((lane & 3) == 0) {
-        put_tagged(A, ds + (col >> 5), tagged(o.xs, gen));
-        put_tagged(A, dm + (col >> 5), tg | (unsigned)o.xm);
-      }
-    }
-  }
-  if (A.tp_world > 1) {
-    cbar();
-    if (threadIdx.x == 0) count_done(A, 1);
-  }
-}
-
-// The down projection's prepped input (prep_slices, generation `gen`, the `dgen`-th prep) into
-// x: the tagged words are staged, then unpacked to codes, block scales and block sums.
-// K % 64 == 0.
-DPUF_DEV void load_prepped_tagged(const DecodeArgs& A, int K, unsigned gen, unsigned dgen, int8_t* xq, float* xs,
-                                  int* xm, float* stage, DecShared& S) {
-  uint64_t* st = (uint64_t*)stage;
-  const int nq = K / 4, nb = K / 32;
-  // the chunks are published by all CTAs at about the same time, shortly after this CTA's own:
-  // wait for the count first, so that the one staging round finds them
-  const unsigned target = dgen * (unsigned)(gridDim.x * A.tp_world);
-  if (threadIdx.x == 0) wait_count(A, A.ctr + 1, target, S);
-  cbar();
-  stage_tagged(st, A.dprep, nq + 2 * nb, gen, 1, target, A, S);
-  cbar();
-  for (int i = threadIdx.x; i < nq; i += kConsumers) *(uint32_t*)(xq + 4 * i) = (uint32_t)st[i];
-  for (int b = threadIdx.x; b < nb; b += kConsumers) {
-    xs[b] = value_of(st[nq + b]);
-    xm[b] = (int)(unsigned)st[nq + nb + b];
-  }
-}
-
-// Prep of a whole tagged vector (generation `gen`, complete at count `target` of completion
-// counter 0) by this CTA: staged in one piece with its sign bytes, then prepped from shared
-// memory (for vectors small enough that one hop beats the distributed prep's two).
-DPUF_DEV void prep_tagged(const DecodeArgs& A, const uint64_t* src, unsigned gen, unsigned target, int K,
-                          const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t* st = (uint64_t*)stage;
-  uint8_t* sg = (uint8_t*)(st + K);
-  if (signs) stage8(sg, signs, K / 8);
-  stage_tagged(st, src, K, gen, 0, target, A, S);
-  const int nch = K / 64;
-  for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
-    const int c = cb + (lane >> 3);
-    const bool active = c < nch;
-    const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
-    float v[8];
+    wait_words(A, wv, stale_mask(wv, valid, gen), [&](int j) { return src + i0 + j * kConsThreads; }, gen, S);
 #pragma unroll
-    for (int k = 0; k < 8; k++) v[k] = value_of(st[col + k]);
-    prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, active ? c * 64 : 0, lane, xq, xs, xm);
-  }
-}
-
-// Copies a prepped activation (codes, block scales, block sums of K columns; K % 128 == 0)
-// written by other CTAs into x.
-DPUF_DEV void load_prepped(const int8_t* q8, const float* bxs, const int32_t* bxm, int K, int8_t* xq, float* xs,
-                           int* xm) {
-  stage16(xq, q8, K);
-  stage16(xs, bxs, K / 8);
-  stage16(xm, bxm, K / 8);
-  cp_async_commit_wait_all();
-}
-
-// Activation prep of a vector written by other CTAs before a grid barrier: pieces of `cap`
-// columns (a multiple of 128) are staged into shared memory with their sign bytes, then
-// prepped from there.
-DPUF_DEV void prep_global(const float* src, int K, const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage,
-                          int cap) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* sg = (uint8_t*)(stage + cap);
-  for (int p0 = 0; p0 < K; p0 += cap) {
-    const int n = min(cap, K - p0);
-    stage16(stage, src + p0, n * 4);
-    if (signs) stage8(sg, signs + p0 / 8, n / 8);
-    cp_async_commit_wait_all();
-    cbar();
-    const int nch = n / 64;
-    for (int cb = warp * 4; cb < nch; cb += kConsumers / 8) {
-      const int c = cb + (lane >> 3);
-      const bool active = c < nch;
-      const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
-      const float4 a0 = *(const float4*)(stage + col), a1 = *(const float4*)(stage + col + 4);
-      float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      prep_chunk_g8(v, signs ? sg[col >> 3] : 0, active, p0 + (active ? c * 64 : 0), lane, xq, xs, xm);
+    for (int j = 0; j < kPer; j++) {
+      const int i = i0 + j * kConsThreads;
+      if (i >= n) continue;
+      const uint64_t x = wv[j];
+      const int ch = i / kChunkWords, o = i - ch * kChunkWords;
+      if (o < 16) *(uint32_t*)(xq + ch * 64 + o * 4) = (uint32_t)x;
+      else if (o < 18) xs[ch * 2 + (o - 16)] = value_of(x);
+      else xm[ch * 2 + (o - 18)] = (int)(unsigned)x;
     }
-    cbar();
   }
+  cta_sync();
 }
 
-struct AttnSync {
-  DPUF_DEV void operator()() const { named_sync(kBarAttn, kAttnThreads); }
+// ------------------------------------------------------------------ attention of one head
+// gqa_attn_head_pair_f32 (dpuf_engine.c:341-577) for query head h at position pos by the CTA's
+// consumer threads, with the pair path's arithmetic (the lone path's for the last head of an odd
+// group): QK-norm and RoPE of the query and the key, the K/V store (by the group's first head),
+// scores (eight threads per key, the reference's 8-lane accumulation and trees), softmax, PV (one
+// thread per output dimension, keys in order), then the prep of the head's output columns for
+// the o projection, stored as tagged words of this GPU.  Everything that does not depend on this
+// step - the QK-norm gains, the RoPE row, the o projection's sign bytes, the first value tiles
+// and each thread's first history key - is requested before the query, key and value are
+// waited for.
+// The attention scratch of one head in the union (all float offsets from U).
+struct AttnScratch {
+  float *qs, *kin, *vin, *outv, *qn, *kn, *cs, *sn, *sc, *vt;
+  uint8_t* osg;
 };
+DPUF_DEV AttnScratch attn_scratch(const DecodeArgs& A, float* U) {
+  const int hd = A.hd;
+  AttnScratch X;
+  X.qs = U;
+  X.kin = X.qs + hd;
+  X.vin = X.kin + hd;
+  X.outv = X.vin + hd;
+  X.qn = X.outv + hd;
+  X.kn = X.qn + hd;
+  X.cs = X.kn + hd;
+  X.sn = X.cs + hd / 2;
+  X.osg = (uint8_t*)(X.sn + hd / 2);  // hd / 8 sign bytes (16-byte padded)
+  X.sc = (float*)(X.osg + 16 * ((hd / 8 + 15) / 16));
+  X.vt = X.sc + ((A.S + 3) & ~3);  // two value tiles [kVTile][hd]
+  return X;
+}
+DPUF_DEV float* kv_rows(const DecodeArgs& A, float* base, int l, int kvh) {
+  return base + ((size_t)l * A.nkv + kvh) * A.S * A.hd;
+}
+// Value tile t (keys t*kVTile .., history rows only) into buffer t & 1, one commit group.
+DPUF_DEV void issue_vtile(const DecodeArgs& A, const AttnScratch& X, const float* vc, int n_rows, int t) {
+  const int hd = A.hd, t0 = t * kVTile, nk = max(0, min(kVTile, n_rows - t0)), per_row = hd / 4;
+  float* buf = X.vt + (size_t)(t & 1) * kVTile * hd;
+  for (int i = threadIdx.x; i < nk * per_row; i += kConsThreads) {
+    const int r = i / per_row, c = (i - r * per_row) * 4;
+    cp_async16_cg(buf + r * hd + c, vc + (size_t)(t0 + r) * hd + c);
+  }
+  cp_async_commit();
+}
 
-// Attention items (KV head, query-head pair) of this CTA: the pair's query heads, the KV
-// head's key and value, the QK-norm gains and the RoPE row are staged in one async round;
-// QK-norm + RoPE of the queries and the key, K/V rows stored at `pos` (both pairs of a KV head
-// store the same bits), then attn_pair_body.  With fuse_o the item also preps its output
-// columns (whole 64-column chunks) for the o projection.  Threads 0..255 only.
-DPUF_DEV void attention_items(const DecodeArgs& A, const DecLayer& Ly, int l, int pos, unsigned gen, float* scratch,
-                              DecShared& S) {
+// Everything the attention of head h at position pos needs that does not depend on this step's
+// q/k/v: the QK-norm gains, the RoPE row and the o projection's sign bytes (one commit group),
+// the first two value tiles (a group each), and the key and value history rows into L2.  Issued
+// by the hosting CTA before its q/k/v stages, so that it lands while they run.
+DPUF_DEV void attention_prefetch(const DecodeArgs& A, const DecLayer* Ly, int l, int pos, int h, float* U) {
+  const int tid = threadIdx.x, hd = A.hd, kvh = h / (A.nq / A.nkv), n_rows = pos;
+  const AttnScratch X = attn_scratch(A, U);
+  // the history rows were stored by other CTAs in earlier steps, before tagged outputs this CTA
+  // has since read: order this CTA's reads of the cache after them
+  __threadfence();
+  for (int i = tid * 4; i < hd; i += kConsThreads * 4) {
+    if (Ly->q_norm) cp_async16_cg(X.qn + i, Ly->q_norm + i);
+    if (Ly->k_norm) cp_async16_cg(X.kn + i, Ly->k_norm + i);
+    if (i < hd / 2) {
+      cp_async16_cg(X.cs + i, A.cos_tab + (size_t)pos * (hd >> 1) + i);
+      cp_async16_cg(X.sn + i, A.sin_tab + (size_t)pos * (hd >> 1) + i);
+    }
+  }
+  const uint8_t* so = Ly->signs[1];
+  if (so && tid == 0)
+    for (int i = 0; i < hd / 8; i += 8) cp_async8_ca(X.osg + i, so + (size_t)h * hd / 8 + i);
+  cp_async_commit();
+  const float* kc = kv_rows(A, A.kv_k, l, kvh);
+  const float* vc = kv_rows(A, A.kv_v, l, kvh);
+  const int n_vt = (n_rows + 1 + kVTile - 1) / kVTile;
+  issue_vtile(A, X, vc, n_rows, 0);
+  if (n_vt > 1) issue_vtile(A, X, vc, n_rows, 1);
+  else cp_async_commit();
+  // the key rows, and the value rows past the first two tiles, into L2 (32 KB pieces)
+  const size_t row_b = (size_t)hd * 4, kb = (size_t)n_rows * row_b;
+  const size_t v0 = min(kb, (size_t)2 * kVTile * row_b);
+  constexpr size_t kPiece = 32768;
+  const size_t nk = (kb + kPiece - 1) / kPiece, nv = (kb - v0 + kPiece - 1) / kPiece;
+  for (size_t i = tid; i < nk + nv; i += kConsThreads) {
+    const char* src = i < nk ? (const char*)kc + i * kPiece : (const char*)vc + v0 + (i - nk) * kPiece;
+    const size_t end = i < nk ? kb : kb - v0;
+    const size_t off = i < nk ? i * kPiece : (i - nk) * kPiece;
+    prefetch_l2(src, (unsigned)min(kPiece, end - off));
+  }
+}
+
+// gqa_attn_head_pair_f32 (dpuf_engine.c:341-577) for query head h at position pos by the CTA's
+// consumer threads, with the pair path's arithmetic (the lone path's for the last head of an odd
+// group): QK-norm and RoPE of the query and the key, the K/V store (by the group's first head),
+// scores (eight threads per key, the reference's 8-lane accumulation and trees), softmax, PV (one
+// thread per output dimension, keys in order), then the prep of the head's output columns for
+// the o projection, stored as tagged words of this GPU.  attention_prefetch (by this call when
+// `prefetched` is false) has requested the step-independent inputs.
+DPUF_DEV void attention_head(const DecodeArgs& A, const DecLayer* Ly, int l, int pos, int h, unsigned gen, float* U,
+                             bool prefetched, DecShared& S, int step, int ev) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int groups = A.nq / A.nkv, n_pairs = (groups + 1) / 2, hd = A.hd;
-  // scratch: qs [2][hd] | inputs (key, value, gains, RoPE row) [5 hd] | scores [2][kv_len
-  // padded to 4] | n_buf key/value tiles (as many as fit, at most kAttnMaxBuf)
-  const int kv_len = pos + 1, sc_stride = (kv_len + 3) & ~3;
-  float* qs = scratch;
-  float *kin = qs + 2 * hd, *vin = kin + hd, *qn = vin + hd, *kn = qn + hd, *cs = kn + hd, *sn = cs + hd / 2;
-  float* sc = qs + 7 * hd;
-  float* kt = sc + 2 * sc_stride;
-  const int n_t = (kv_len + kAttnKeyTile - 1) / kAttnKeyTile;
-  const int n_buf = max(1, min(kAttnMaxBuf, (int)((A.attn_floats - 7 * hd - 2 * sc_stride) / attn_tile_floats(hd))));
-  const int pre = min(n_buf, n_t);  // history key tiles fetched while q/k/v arrive
-  for (int it = blockIdx.x; it < A.nkv * n_pairs; it += gridDim.x) {
-    const int kvh = it / n_pairs, pr = it % n_pairs;
-    const int g0 = pr * 2, nh = (g0 + 1 < groups) ? 2 : 1, qh0 = kvh * groups + g0;
-    float* kc = A.kv_k + ((size_t)l * A.nkv + kvh) * A.S * hd;
-    float* vc = A.kv_v + ((size_t)l * A.nkv + kvh) * A.S * hd;
-    named_sync(kBarAttn, kAttnThreads);  // scratch free (previous item done)
-    {
-      const int q4 = hd / 4;  // 16-byte pieces per vector
-      // gains and the RoPE row asynchronously (one group), then the first key tiles of the
-      // history (rows < pos: they do not depend on this step), while the pair's query heads,
-      // the key and the value (tagged words of the q/k/v phase) are read, one pair of
-      // elements per thread
-      for (int i = tid; i < q4; i += kAttnThreads) {
-        if (Ly.q_norm) cp_async16_cg(qn + i * 4, Ly.q_norm + i * 4);
-        if (Ly.k_norm) cp_async16_cg(kn + i * 4, Ly.k_norm + i * 4);
-        if (i < q4 / 2) {
-          cp_async16_cg(cs + i * 4, A.cos_tab + (size_t)pos * (hd >> 1) + i * 4);
-          cp_async16_cg(sn + i * 4, A.sin_tab + (size_t)pos * (hd >> 1) + i * 4);
+  const int hd = A.hd, groups = A.nq / A.nkv, kvh = h / groups, kv_len = pos + 1;
+  const bool lone = (groups & 1) && (h % groups == groups - 1);
+  const int kv4 = kv_len & ~3, kv8 = kv_len & ~7;
+  if (!prefetched) attention_prefetch(A, Ly, l, pos, h, U);
+  const AttnScratch X = attn_scratch(A, U);
+  float* qs = X.qs;
+  float* kin = X.kin;
+  float* vin = X.vin;
+  float* outv = X.outv;
+  float* qn = X.qn;
+  float* kn = X.kn;
+  float* cs = X.cs;
+  float* sn = X.sn;
+  uint8_t* osg = X.osg;
+  float* sc = X.sc;
+  float* vt = X.vt;
+  float* kc = kv_rows(A, A.kv_k, l, kvh);
+  float* vc = kv_rows(A, A.kv_v, l, kvh);
+  const int n_rows = kv_len - 1;  // history rows read from the cache (the current one comes from vin)
+  const int n_vt = (kv_len + kVTile - 1) / kVTile;
+  const uint8_t* so = Ly->signs[1];
+  // each key group's first key (history rows only) into registers
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const int j = tid & 7, kg = tid >> 3;
+  const int warp_kg0 = warp * 4;  // key groups of this warp: warp_kg0 .. +3
+  float kv[16];
+  {
+    const int t = kg;
+    const bool pre = t < n_rows;
+#pragma unroll
+    for (int m = 0; m < 16; m++) kv[m] = (pre && j + 8 * m < hd) ? __ldcg(kc + (size_t)t * hd + j + 8 * m) : 0.0f;
+  }
+  // this step's query head, key and value (tagged words of the q/k/v phase; 3 * hd <= 2 threads'
+  // worth, hd <= 128)
+  {
+    auto src = [&](int j) {
+      const int i = tid + j * kConsThreads;
+      return i < hd ? A.q + (size_t)h * hd + i
+                    : (i < 2 * hd ? A.k + (size_t)kvh * hd + (i - hd) : A.v + (size_t)kvh * hd + (i - 2 * hd));
+    };
+    uint64_t wv[2];
+    unsigned valid = 0;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const bool ok = tid + j * kConsThreads < 3 * hd;
+      wv[j] = ok ? ld_relaxed(src(j), A.tp_world > 1) : 0;
+      if (ok) valid |= 1u << j;
+    }
+    wait_words(A, wv, stale_mask(wv, valid, gen), src, gen, S);
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+      if ((valid >> j) & 1u) qs[tid + j * kConsThreads] = value_of(wv[j]);  // qs, kin, vin are contiguous
+  }
+  trace_at(A, step, ev);  // thread 0's q/k/v words are in
+  cp_async_wait_pending(n_vt > 1 ? 2 : 1);  // the constants (the value tiles may stay in flight)
+  cta_sync();
+  trace_at(A, step, ev + 1);
+  if (warp == 0) qk_norm_rope_warp(qs, Ly->q_norm ? qn : nullptr, A.eps, hd, cs, sn, lane);
+  if (warp == 1) qk_norm_rope_warp(kin, Ly->k_norm ? kn : nullptr, A.eps, hd, cs, sn, lane);
+  cta_sync();
+  trace_at(A, step, ev + 2);
+  if (h % groups == 0) {  // the group's first head stores the key and value at pos
+    if (warp == 2)
+      for (int i = lane; i < hd; i += 32) kc[(size_t)pos * hd + i] = kin[i];
+    if (warp == 3)
+      for (int i = lane; i < hd; i += 32) vc[(size_t)pos * hd + i] = vin[i];
+  }
+  // ---- scores: key group kg takes keys kg, kg + kKeyGroups, ...; lane j of the group
+  // accumulates elements j, j+8, ... of the dot
+  float qv[16];
+#pragma unroll
+  for (int m = 0; m < 16; m++) qv[m] = (j + 8 * m < hd) ? qs[j + 8 * m] : 0.0f;
+  float lmax = -1e30f;
+  for (int t0 = warp_kg0; t0 < kv_len; t0 += kKeyGroups) {
+    const int t = t0 + (kg - warp_kg0);
+    const bool valid = t < kv_len;
+    if (t0 != warp_kg0) {  // keys past the first round come from the cache now
+#pragma unroll
+      for (int m = 0; m < 16; m++)
+        kv[m] = (t < n_rows && j + 8 * m < hd) ? __ldcg(kc + (size_t)t * hd + j + 8 * m) : 0.0f;
+    }
+    if (t == pos) {
+#pragma unroll
+      for (int m = 0; m < 16; m++) kv[m] = (j + 8 * m < hd) ? kin[j + 8 * m] : 0.0f;
+    }
+    float acc = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    if (valid) {
+#pragma unroll
+      for (int m = 0; m < 16; m++)
+        if (j + 8 * m < hd) acc = __fmaf_rn(qv[m], kv[m], acc);
+      if (lone && t >= kv4) {
+        // lone head, tail key: dot_f32_avx2 (dpuf_engine.c:325-339), two accumulators over
+        // 16-wide steps (hd % 64 == 0: no 8-wide remainder), summed lane-wise before the split tree
+#pragma unroll
+        for (int p2 = 0; p2 < 8; p2++)
+          if (16 * p2 < hd) {
+            a0 = __fmaf_rn(qv[2 * p2], kv[2 * p2], a0);
+            a1 = __fmaf_rn(qv[2 * p2 + 1], kv[2 * p2 + 1], a1);
+          }
+      }
+    }
+    const float t_pairs = tree8_pairs(acc);
+    const float t_split = tree8_split(acc);
+    const float t_lone = tree8_split(__fadd_rn(a0, a1));
+    const float sv = __fmul_rn(t < kv4 ? t_pairs : (lone ? t_lone : t_split), scale);
+    if (valid && j == 0) {
+      sc[t] = sv;
+      lmax = max_ps(lmax, sv);
+    }
+  }
+  {
+    const float v = warp_max(lmax);
+    if (lane == 0) S.red[warp] = v;
+  }
+  cta_sync();
+  trace_at(A, step, ev + 3);
+  float mx = -1e30f;
+  for (int w = 0; w < kConsWarps; w++) mx = max_ps(mx, S.red[w]);
+  // ---- softmax (vec_softmax_avx2, dpuf_engine.c:579-601)
+  for (int t = tid; t < kv8; t += kConsThreads) sc[t] = exp_poly(__fsub_rn(sc[t], mx));
+  if (tid >= kConsThreads - 8) {
+    const int t = kv8 + (tid - (kConsThreads - 8));
+    if (t < kv_len) sc[t] = glibc_expf(__fsub_rn(sc[t], mx), A.et);
+  }
+  cta_sync();
+  if (tid < 8) {
+    float acc = 0.0f;
+    for (int t = tid; t < kv8; t += 8) acc = __fadd_rn(acc, sc[t]);
+    S.lanes[tid] = acc;
+  }
+  cta_sync();
+  float su = tree8_split_arr(S.lanes);
+  for (int t = kv8; t < kv_len; t++) su = __fadd_rn(su, sc[t]);
+  const float inv = __fdiv_rn(1.0f, __fadd_rn(su, 1e-12f));
+  cta_sync();  // every thread has read the lane sums and the tail
+  for (int t = tid; t < kv_len; t += kConsThreads) sc[t] = __fmul_rn(sc[t], inv);
+  trace_at(A, step, ev + 4);
+  // ---- PV: thread d < hd, keys in order (pair path: fma(p_k, v_kd, acc); lone path: keys two at
+  // a time, k+1 first, dpuf_engine.c:541-548)
+  float acc = 0.0f;
+  const int hd8 = hd & ~7;
+  for (int t = 0; t < n_vt; t++) {
+    cp_async_wait_pending(t + 1 < n_vt ? 1 : 0);
+    cta_sync();
+    const float* buf = vt + (size_t)(t & 1) * kVTile * hd;
+    const int t0 = t * kVTile, nk = min(kVTile, kv_len - t0);
+    if (tid < hd) {
+      const int d = tid;
+      auto vat = [&](int k) { return (t0 + k == pos) ? vin[d] : buf[k * hd + d]; };
+      if (!lone) {
+        for (int k = 0; k < nk; k++) acc = __fmaf_rn(sc[t0 + k], vat(k), acc);
+      } else if ((hd & 63) == 0) {
+        int k = 0;
+        for (; k + 1 < nk; k += 2) {
+          const float t1 = __fmaf_rn(sc[t0 + k + 1], vat(k + 1), acc);
+          acc = __fmaf_rn(sc[t0 + k], vat(k), t1);
+        }
+        if (k < nk) acc = __fmaf_rn(sc[t0 + k], vat(k), acc);
+      } else {
+        for (int k = 0; k < nk; k++) {
+          const float pv = sc[t0 + k], vv = vat(k);
+          acc = (d < hd8) ? __fmaf_rn(pv, vv, acc) : __fadd_rn(acc, __fmul_rn(pv, vv));
         }
       }
-      cp_async_commit();
-      for (int t = 0; t < pre; t++) attn_issue_tile(kt + (size_t)t * attn_tile_floats(hd), kc, t, pos, hd, tid);
-      for (int i = tid * 2; i < (nh + 2) * hd; i += kAttnThreads * 2) {
-        const int v = i / hd, o = i % hd;
-        const uint64_t* src = (v < nh ? A.q + (size_t)(qh0 + v) * hd : (v == nh ? A.k : A.v) + (size_t)kvh * hd) + o;
-        float* dst = (v < nh ? qs + v * hd : (v == nh ? kin : vin)) + o;
-        ulonglong2 w = ld_tagged2(src, A.tp_world > 1);
-        if (tag_of(w.x) != gen || tag_of(w.y) != gen) w = wait_tagged2(src, gen, A, S);
-        *(float2*)dst = make_float2(value_of(w.x), value_of(w.y));
-      }
-      cp_async_wait_pending(pre);  // the gains and the RoPE row (the tiles may stay in flight)
     }
-    named_sync(kBarAttn, kAttnThreads);
-    if (warp == 0) {
-      qk_norm_rope_warp(kin, Ly.k_norm ? kn : nullptr, A.eps, hd, cs, sn, lane);
-      for (int i = lane; i < hd; i += 32) kc[(size_t)pos * hd + i] = kin[i];
-    } else if (warp == 1) {
-      for (int i = lane; i < hd; i += 32) vc[(size_t)pos * hd + i] = vin[i];
-    } else if (warp < 2 + nh) {
-      qk_norm_rope_warp(qs + (warp - 2) * hd, Ly.q_norm ? qn : nullptr, A.eps, hd, cs, sn, lane);
-    }
-    named_sync(kBarAttn, kAttnThreads);  // rotated queries and key in place
-    attn_pair_body(qs, nh, nh == 1, hd, kv_len, kc, vc, sc_stride, sc, kt, n_buf, pre, kin, vin, &S.attn,
-                   A.att + (size_t)qh0 * hd, A.et, tid, AttnSync{}, A.fuse_o != 0);
-    if (A.fuse_o) {
-      named_sync(kBarAttn, kAttnThreads);
-      const int n_ch = nh * hd / 64;
-      if (warp * 4 < n_ch) {
-        const int c = warp * 4 + (lane >> 3);
-        const bool active = c < n_ch;
-        const int col = (active ? c * 64 : 0) + (lane & 7) * 8;
-        float v[8];
+    cta_sync();  // the tile buffer is free again
+    if (t + 2 < n_vt) issue_vtile(A, X, vc, n_rows, t + 2);
+    else cp_async_commit();
+  }
+  trace_at(A, step, ev + 5);
+  if (tid < hd) outv[tid] = acc;
+  if (h % groups == 0) __threadfence();  // the K/V rows stored above, before the tagged outputs
+  cta_sync();
+  // ---- prep of the head's output columns (hd / 64 chunks) for the o projection
+  const int n_ch = hd / 64;
+  if (warp * 4 < n_ch) {
+    const int c = warp * 4 + (lane >> 3), qi = lane & 7;
+    const bool active = c < n_ch;
+    float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) v[k] = qs[col + k];
-        const int gcol = qh0 * hd + col;  // column of the o-projection input
-        prep_chunk_g8(v, Ly.signs[1] ? Ly.signs[1][gcol >> 3] : 0, active, qh0 * hd + (active ? c * 64 : 0), lane,
-                      A.xo_q8, A.xo_xs, A.xo_xm);
+    for (int k = 0; k < 8; k++) v[k] = outv[(active ? c * 64 : 0) + qi * 8 + k];
+    const int gch = (h * hd) / 64 + (active ? c : 0);  // chunk of the o-projection input
+    const PrepOut o = prep_chunk_g8_core(v, so ? osg[(active ? c : 0) * 8 + qi] : 0, lane);
+    if (active) {
+      uint64_t* dst = A.oprep + (size_t)gch * kChunkWords;
+      const uint64_t tg = (uint64_t)gen << 32;
+      st_relaxed(dst + 2 * qi, tg | o.lo, false);
+      st_relaxed(dst + 2 * qi + 1, tg | o.hi, false);
+      if ((qi & 3) == 0) {
+        st_relaxed(dst + 16 + (qi >> 2), tagged(o.xs, gen), false);
+        st_relaxed(dst + 18 + (qi >> 2), tg | (unsigned)o.xm, false);
       }
     }
   }
-}
-
-// Optional trace of the last step: per CTA, the time (globaltimer, ns) at which each phase of
-// the consumer side ended (14 per layer, then 6 per step) and at which the producer began each
-// projection (4 per layer + the LM head).
-enum {
-  kEvNorm1, kEvQKV, kEvB1, kEvAttn, kEvB2, kEvPrepO, kEvO, kEvB3, kEvNorm2, kEvGU, kEvB4, kEvPrepD, kEvDown, kEvB5,
-  kEvPerLayer
-};
-enum { kEvStart, kEvEmbed, kEvNormF, kEvLM, kEvBLM, kEvArg, kEvPerStep };
-DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
-  if (A.trace && step == A.n_steps - 1) A.trace[(size_t)blockIdx.x * A.trace_per_cta + ev] = globaltimer();
+  cta_sync();
 }
 
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
-  static_assert(kAttnThreads <= kTeamWarps * 32, "attention runs on the first team");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ DecShared S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_ring = A.n_ring;
+  const int H = A.H;
   unsigned char* ring = smem;
-  DecLayer* layers = (DecLayer*)(smem + (size_t)n_ring * kSlotBytes);
-  float* h = (float*)(layers + max(A.L, 1));
-  unsigned char* uni = (unsigned char*)(h + A.H);
-  int8_t* xq = (int8_t*)uni;
-  float* xs = (float*)(uni + A.kmax);
+  float* h = (float*)(smem + (size_t)A.n_slots * kSlotBytes);
+  int8_t* xq = (int8_t*)(h + H);
+  float* xs = (float*)(xq + A.kmax);
   int* xm = (int*)(xs + A.kmax / 32);
-  float2* ps = (float2*)(xm + A.kmax / 32);
-  float* stage = (float*)(xm + A.kmax / 32);  // staging area (overlaps the pair buffers)
-  float* attn_scratch = (float*)uni;
+  float* U = (float*)(((uintptr_t)(xm + A.kmax / 32) + 15) & ~(uintptr_t)15);  // union (16-byte aligned)
 
   if (tid == 0) {
-    for (int i = 0; i < n_ring; i++) {
+    for (int i = 0; i < A.n_slots; i++) {
       mbar_init(&S.full[i], 1);
-      mbar_init(&S.empty[i], kTeamWarps);
+      mbar_init(&S.empty[i], 1);
     }
     S.abort = 0;
+    for (int k = kQKV; k <= kLM; k++) S.ph[k] = compute_phase(A, k);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  {
-    const int4* src = (const int4*)A.layers;
-    int4* dst = (int4*)layers;
-    for (int i = tid; i < A.L * (int)(sizeof(DecLayer) / 16); i += kThreads) dst[i] = src[i];
   }
   __syncthreads();
 
   // ---------------------------------------------------------------- producer warp
   if (warp == kProdWarp) {
-    if (lane != 0) return;
     Producer P;
-    P.policy = l2_evict_first_policy();
-    int rot = 0;
+    P.pol = l2_evict_first_policy();
     bool ok = true;
-    const int ev0 = kEvPerLayer * A.L + kEvPerStep;
     for (int step = 0; ok && step < A.n_steps; step++) {
       for (int l = 0; ok && l < A.L; l++)
-        for (int kind = kQKV; ok && kind <= kDown; kind++) {
-          trace_at(A, step, ev0 + 4 * l + kind);
-          ok = produce_phase(A, layers, l, kind, rot, ring, n_ring, P, S);
-        }
-      trace_at(A, step, ev0 + 4 * A.L);
-      if (ok) ok = produce_phase(A, layers, 0, kLM, rot, ring, n_ring, P, S);
+        for (int kind = kQKV; ok && kind <= kDown; kind++) ok = produce_phase(A, l, kind, ring, P, S);
+      if (ok) ok = produce_phase(A, A.L, kLM, ring, P, S);
     }
-    if (!ok) {
-      // copies still in flight must land before the CTA exits: wait (bounded) for the last
-      // use of every slot
+    // copies still in flight must land before the CTA exits: every slot's last fill
+    if (lane == 0) {
       const unsigned long long t0 = globaltimer();
-      for (int sl = 0; sl < n_ring; sl++) {
-        const long long uses = P.issued / n_ring + (sl < P.issued % n_ring ? 1 : 0);
-        if (uses == 0) continue;
-        const unsigned par = (unsigned)((uses - 1) & 1);
-        while (!mbar_try(&S.full[sl], par) && globaltimer() - t0 < kWaitNs) {
+      for (long long p = max(0LL, P.issued - A.n_slots); p < P.issued; p++)
+        while (!mbar_try(&S.full[p % A.n_slots], (unsigned)((p / A.n_slots) & 1)) && globaltimer() - t0 < A.wait_ns) {
         }
-      }
     }
     return;
   }
 
   // ---------------------------------------------------------------- consumer warps
-  // Pair-buffer hand-off on named barriers: the dot warps bar.sync "emptied" before filling a
-  // buffer and bar.arrive "filled"; the chain warp bar.syncs "filled" and bar.arrives
-  // "emptied".  The chain's first arrivals here free every buffer; the dot warps' syncs at the
-  // end take its last ones, so every barrier generation completes.
-  if (warp == kChainWarp)
-    for (int i = 0; i < kNPs; i++) named_arrive(kBarEmptied + i, kHandoff);
   Consumer C;
-  unsigned target = 0;
-  const int H = A.H;
-  const int n_chunks = A.H / 64;
+  // query heads of this CTA: hh with floor(hh * grid / nq) == blockIdx.x, i.e. [head_lo, head_hi)
+  const int head_lo = (int)((blockIdx.x * A.nq + gridDim.x - 1) / gridDim.x);
+  const int head_hi = (int)(((blockIdx.x + 1) * A.nq + gridDim.x - 1) / gridDim.x);
+  const int n_chunks = H / 64;
   for (int step = 0; step < A.n_steps; step++) {
     const int pos = A.pos0 + step;
     const int id = step == 0 ? A.first_id : S.next_id;
-    const int sb = kEvPerLayer * A.L;
-    if (tid == 0) trace_at(A, step, sb + kEvStart);
-    // embedding row -> h: the row's 8-row group of its tile and the sign table are staged in
-    // shared memory, then every warp expands its chunks from there
+    const unsigned g_step = A.gen0 + (unsigned)step * (unsigned)decode_phases(A.L);
+    trace_at(A, step, kEvPerLayer * A.L + kEvStart);
+    // ---- embedding row -> h: the row's 8-row group of its tile and the sign bytes are staged,
+    // then every warp expands its chunks from there
     {
       const int n_blk = H >> 5, lr = id % kTileRows;
       const uint8_t* grp = A.tok_tiles + (size_t)(id / kTileRows) * A.tok_stride + 16 + (size_t)(lr >> 3) * n_blk * 144;
-      uint8_t* sgrp = (uint8_t*)stage;
+      uint8_t* sgrp = (uint8_t*)U;
       uint8_t* sg = sgrp + n_blk * 144;
-      stage16(sgrp, grp, n_blk * 144);
-      if (A.tok_signs) stage8(sg, A.tok_signs, H / 8);
+      for (int i = tid * 16; i < n_blk * 144; i += kConsThreads * 16) cp_async16_cg(sgrp + i, grp + i);
+      if (A.tok_signs)
+        for (int i = tid * 8; i < H / 8; i += kConsThreads * 8) cp_async8_ca(sg + i, A.tok_signs + i);
       cp_async_commit_wait_all();
-      cbar();
-      for (int c = warp; c < n_chunks; c += kConsumers / 32) {
+      cta_sync();
+      for (int c = warp; c < n_chunks; c += kConsWarps) {
         float a, b;
         embed_chunk_warp(sgrp - 16, n_blk, lr & 7, A.tok_signs ? sg : nullptr, c * 64, lane, a, b);
         h[c * 64 + lane] = a;
         h[c * 64 + 32 + lane] = b;
       }
+      cta_sync();
     }
-    cbar();
-    if (tid == 0) trace_at(A, step, sb + kEvEmbed);
-    // exchange generations: 4 per layer (q/k/v, o, gate/up, down) and the LM head's
-    const unsigned g_step = A.gen0 + (unsigned)step * (unsigned)decode_phases(A.L);
+    trace_at(A, step, kEvPerLayer * A.L + kEvEmbed);
     for (int l = 0; l < A.L; l++) {
-      const DecLayer& Ly = layers[l];
+      const DecLayer* Ly = A.layers + l;
       const int lb = kEvPerLayer * l;
-      const unsigned g = g_step + 4u * l;
-      // the previous layer's down output (generation g - 1) is the residual
-      norm_prep(A, h, l > 0 ? A.d_out : nullptr, g - 1, A.keep_down * kTileRows, Ly.attn_norm, H, A.eps, Ly.signs[0],
-                xq, xs, xm, stage, S);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvNorm1);
-      consume_phase(A, Ly, kQKV, g + kQKV, C, ring, n_ring, xq, xs, xm, ps, S);
-      if (tid == 0) trace_at(A, step, lb + kEvQKV);
-      cbar();  // the attention scratch overlaps the pair buffers
-      if (tid == 0) trace_at(A, step, lb + kEvB1);
-      if (tid < kAttnThreads) attention_items(A, Ly, l, pos, g + kQKV, attn_scratch, S);
-      if (tid == 0) trace_at(A, step, lb + kEvAttn);
-      grid_sync(A, target, S);
-      if (tid == 0) trace_at(A, step, lb + kEvB2);
-      if (A.fuse_o)
-        load_prepped(A.xo_q8, A.xo_xs, A.xo_xm, A.qd, xq, xs, xm);
-      else
-        prep_global(A.att, A.qd, Ly.signs[1], xq, xs, xm, stage, A.stage_cap);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvPrepO);
-      consume_phase(A, Ly, kO, g + kO, C, ring, n_ring, xq, xs, xm, ps, S);
-      if (tid == 0) trace_at(A, step, lb + kEvO);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvB3);
-      norm_prep(A, h, A.o_out, g + kO, H, Ly.ffn_norm, H, A.eps, Ly.signs[2], xq, xs, xm, stage, S);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvNorm2);
-      consume_phase(A, Ly, kGU, g + kGU, C, ring, n_ring, xq, xs, xm, ps, S);
-      if (tid == 0) trace_at(A, step, lb + kEvGU);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvB4);
-      if (A.dprep_local) {
-        prep_tagged(A, A.s_out, g + kGU, (g + kGU) * (unsigned)(gridDim.x * A.tp_world), A.I, Ly.signs[3], xq, xs,
-                    xm, stage, S);
-      } else {
-        prep_slices(A, Ly.signs[3], g + kGU, S);
-        if (A.tp_world == 1) {
-          grid_sync(A, target, S);
-          load_prepped(A.xd_q8, A.xd_xs, A.xd_xm, A.I, xq, xs, xm);
-        } else {
-          load_prepped_tagged(A, A.I, g + kGU, A.dgen0 + (unsigned)(step * A.L + l + 1), xq, xs, xm, stage, S);
-        }
-      }
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvPrepD);
-      consume_phase(A, Ly, kDown, g + kDown, C, ring, n_ring, xq, xs, xm, ps, S);
-      if (tid == 0) trace_at(A, step, lb + kEvDown);
-      cbar();
-      if (tid == 0) trace_at(A, step, lb + kEvB5);
+      const unsigned g = g_step + (unsigned)l;
+      norm_prep(A, h, l > 0 ? A.d_out : nullptr, g - 1, A.keep_down * kTileRows, Ly->attn_norm, Ly->signs[0], xq,
+                xs, xm, U, S, step, lb + kEvNorm1Res);
+      trace_at(A, step, lb + kEvNorm1);
+      // the first head this CTA hosts: its step-independent inputs are requested now
+      if (head_lo < head_hi) attention_prefetch(A, Ly, l, pos, head_lo, U);
+      consume_phase(A, step, l, kQKV, g, ring, C, xq, xs, xm, S);
+      cta_sync();
+      trace_at(A, step, lb + kEvQKV);
+      for (int hh = head_lo; hh < head_hi; hh++)
+        attention_head(A, Ly, l, pos, hh, g, U, hh == head_lo, S, step, lb + kEvAttnIn);
+      if (head_lo == head_hi)
+        for (int ev = kEvAttnIn; ev <= kEvAttnPV; ev++) trace_at(A, step, lb + ev);
+      trace_at(A, step, lb + kEvAttn);
+      load_prepped(A, A.oprep, A.qd / 64, g, xq, xs, xm, S);
+      trace_at(A, step, lb + kEvLoadO);
+      consume_phase(A, step, l, kO, g, ring, C, xq, xs, xm, S);
+      cta_sync();
+      trace_at(A, step, lb + kEvO);
+      norm_prep(A, h, A.o_out, g, H, Ly->ffn_norm, Ly->signs[2], xq, xs, xm, U, S, step, lb + kEvNorm2Res);
+      trace_at(A, step, lb + kEvNorm2);
+      consume_phase(A, step, l, kGU, g, ring, C, xq, xs, xm, S);
+      cta_sync();
+      trace_at(A, step, lb + kEvGU);
+      load_prepped(A, A.dprep, A.I / 64, g, xq, xs, xm, S);
+      trace_at(A, step, lb + kEvLoadD);
+      consume_phase(A, step, l, kDown, g, ring, C, xq, xs, xm, S);
+      cta_sync();
+      trace_at(A, step, lb + kEvDown);
     }
-    const unsigned g_lm = g_step + 4u * A.L;
-    norm_prep(A, h, A.L > 0 ? A.d_out : nullptr, g_lm - 1, A.keep_down * kTileRows, A.out_norm, H, A.eps, A.lm_signs,
-              xq, xs, xm, stage, S);
-    cbar();
-    if (tid == 0) trace_at(A, step, sb + kEvNormF);
-    consume_phase(A, layers[0], kLM, g_lm, C, ring, n_ring, xq, xs, xm, ps, S);
-    if (tid == 0) trace_at(A, step, sb + kEvLM);
-    cbar();
-    if (tid == 0) trace_at(A, step, sb + kEvBLM);
+    const unsigned g_lm = g_step + (unsigned)A.L;
+    const int sb = kEvPerLayer * A.L;
+    norm_prep(A, h, A.L > 0 ? A.d_out : nullptr, g_lm - 1, A.keep_down * kTileRows, A.out_norm, A.lm_signs, xq, xs,
+              xm, U, S, step, -1);
+    trace_at(A, step, sb + kEvNormF);
+    C.bv = -INFINITY;
+    C.bi = 0x7fffffff;
+    consume_phase(A, step, A.L, kLM, g_lm, ring, C, xq, xs, xm, S);
+    trace_at(A, step, sb + kEvLM);
     {
-      // every CTA's partial (of every rank), tagged with the LM generation, read by all
-      // consumer threads; the two partial buffers alternate with the generation's parity, so
-      // a CTA already at the next step's LM head never overwrites a partial another CTA has
-      // yet to read
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      const int g_all = gridDim.x * A.tp_world;
-      const uint64_t* part = A.part + (size_t)(g_lm & 1) * g_all * 2;
-      for (int c = tid; c < g_all; c += kConsumers) {
-        ulonglong2 w = ld_tagged2(part + 2 * c, A.tp_world > 1);
-        if (tag_of(w.x) != g_lm || tag_of(w.y) != g_lm) w = wait_tagged2(part + 2 * c, g_lm, A, S);
-        better(bv, bi, value_of(w.x), (int)(unsigned)w.y);
-      }
-      // the logits other ranks stored before their partials are visible to this rank's host
-      if (A.tp_world > 1 && A.write_logits) __threadfence_system();
+      // this CTA's argmax partial (lanes of octet 0 of every warp hold running maxima)
+      float bv = C.bv;
+      int bi = C.bi;
       for (int m = 16; m; m >>= 1) {
         const float ov = __shfl_xor_sync(kFull, bv, m);
         const int oi = __shfl_xor_sync(kFull, bi, m);
@@ -1130,59 +1149,92 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
         S.arg_v[warp] = bv;
         S.arg_i[warp] = bi;
       }
-      cbar();
+      cta_sync();
+      const int G_all = gridDim.x * A.tp_world;
+      uint64_t* part = A.part + (size_t)(g_lm & 1) * G_all * 2;
       if (tid == 0) {
-        for (int w = 1; w < kConsumers / 32; w++) better(bv, bi, S.arg_v[w], S.arg_i[w]);
+        for (int w = 1; w < kConsWarps; w++) better(bv, bi, S.arg_v[w], S.arg_i[w]);
+        // other ranks' hosts read this CTA's logits once they have seen its partial
+        if (A.write_logits) {
+          if (A.tp_world > 1) __threadfence_system();
+          else __threadfence();
+        }
+        put_tagged(A, part + 2 * vcta(A), tagged(bv, g_lm));
+        put_tagged(A, part + 2 * vcta(A) + 1, ((uint64_t)g_lm << 32) | (unsigned)bi);
+      }
+      // every CTA reduces every CTA's partial (the partial buffers alternate with the
+      // generation's parity, so a CTA already at the next step never overwrites one still read)
+      bv = -INFINITY;
+      bi = 0x7fffffff;
+      for (int c0 = tid; c0 < G_all; c0 += 4 * kConsThreads) {
+        // four CTAs' partials per round (value and index words)
+        auto src = [&](int j) { return part + 2 * (c0 + (j >> 1) * kConsThreads) + (j & 1); };
+        uint64_t wv[8];
+        unsigned valid = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const bool ok = c0 + (j >> 1) * kConsThreads < G_all;
+          wv[j] = ok ? ld_relaxed(src(j), A.tp_world > 1) : 0;
+          if (ok) valid |= 1u << j;
+        }
+        wait_words(A, wv, stale_mask(wv, valid, g_lm), src, g_lm, S);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2)
+          if ((valid >> j) & 1u) better(bv, bi, value_of(wv[j]), (int)(unsigned)wv[j + 1]);
+      }
+      if (A.tp_world > 1 && A.write_logits) __threadfence_system();
+      for (int m = 16; m; m >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, m);
+        const int oi = __shfl_xor_sync(kFull, bi, m);
+        better(bv, bi, ov, oi);
+      }
+      cta_sync();
+      if (lane == 0) {
+        S.arg_v[warp] = bv;
+        S.arg_i[warp] = bi;
+      }
+      cta_sync();
+      if (tid == 0) {
+        for (int w = 1; w < kConsWarps; w++) better(bv, bi, S.arg_v[w], S.arg_i[w]);
         // the winner is a row of the head; anything else (all logits NaN, or an aborted run)
         // feeds row 0 so that the embedding lookup stays in bounds
         const int id_next = (bi >= 0 && bi < A.V && bi < A.tok_rows) ? bi : 0;
         S.next_id = id_next;
         if (blockIdx.x == 0) A.hist[step] = id_next;
       }
+      cta_sync();
     }
-    if (tid == 0) trace_at(A, step, sb + kEvArg);
-    cbar();
+    trace_at(A, step, sb + kEvArg);
   }
-  if (warp < kMmaWarps)
-    for (int i = 0; i < kNPs; i++) named_sync(kBarEmptied + i, kHandoff);
 }
 
 }  // namespace
 
-// Shared memory of one CTA: ring | layer table | h | a union of {activation x + pair buffers
-// or staging area} and the attention scratch.  The staging area (after x) holds an embedding
-// group with its sign table (4.625 H bytes), a tagged residual with the norm gains and signs
-// (12.125 H), the down projection's tagged prepped input (2.5 I) or a piece of a vector being
-// prepped (4.125 bytes per column).
-size_t decode_x_bytes(const DecodeArgs& A) { return (size_t)A.kmax + (size_t)(A.kmax / 32) * 8; }
-size_t decode_uni_bytes(const DecodeArgs& A) {
-  const size_t xb = decode_x_bytes(A);
-  const size_t uni_x = xb + (size_t)kNPs * kPsBuf * sizeof(float2);
-  // tagged residual + gains + signs of a norm, or a whole plain vector of kmax columns with
-  // its signs
-  const size_t uni_stage =
-      xb + std::max((size_t)A.H * 12 + (size_t)A.H / 8, (size_t)A.kmax * 4 + (size_t)A.kmax / 8) + 128;
-  const size_t uni_attn = ((size_t)7 * A.hd + attn_sc_floats(A.S) + attn_tile_floats(A.hd)) * sizeof(float);
-  return std::max(std::max(uni_x, uni_stage), uni_attn);
-}
-int decode_stage_cap(const DecodeArgs& A) {
-  const size_t bytes = decode_uni_bytes(A) - decode_x_bytes(A);
-  return (int)(bytes * 8 / 33 / 128 * 128);  // 4 + 1/8 bytes per column
+// Shared memory of one CTA: the ring | h | x (codes, block scales, block sums) | a union of the
+// attention scratch (q, k, v, output, QK-norm gains, RoPE row, sign bytes, scores over max_seq
+// keys, two value tiles), the norm staging (gains, sign bytes) and the embedding staging (the
+// row's group and the sign bytes).
+size_t decode_union_bytes(const DecodeArgs& A) {
+  const size_t attn = ((size_t)7 * A.hd + (((size_t)A.S + 3) & ~(size_t)3) + (size_t)2 * kVTile * A.hd) * sizeof(float) +
+                      16 * (((size_t)A.hd / 8 + 15) / 16);
+  const size_t norm = (size_t)A.H * 4 + (size_t)A.H / 8 + 16;
+  const size_t embed = (size_t)(A.H / 32) * 144 + (size_t)A.H / 8 + 16;
+  return std::max(attn, std::max(norm, embed));
 }
 size_t decode_smem_bytes(const DecodeArgs& A) {
-  return (size_t)A.n_ring * kSlotBytes + (size_t)std::max(A.L, 1) * sizeof(DecLayer) + (size_t)A.H * 4 +
-         decode_uni_bytes(A);
+  const size_t head = (size_t)A.n_slots * kSlotBytes + (size_t)A.H * 4 + (size_t)A.kmax + (size_t)(A.kmax / 32) * 8;
+  return ((head + 15) & ~(size_t)15) + decode_union_bytes(A);
 }
 
 int decode_ring_slots(const DecodeArgs& A, size_t smem_limit) {
   DecodeArgs B = A;
-  B.n_ring = 0;
+  B.n_slots = 0;
   const size_t fixed = decode_smem_bytes(B);
   if (fixed >= smem_limit) return 0;
-  return (int)std::min<size_t>(kMaxRing, (smem_limit - fixed) / kSlotBytes);
+  return (int)std::min<size_t>(kMaxSlots, (smem_limit - fixed) / kSlotBytes);
 }
 
-int decode_trace_events(int L) { return kEvPerLayer * L + kEvPerStep + 4 * L + 1; }
+int decode_trace_events(int L) { return kEvPerLayer * L + kEvPerStep; }
 
 cudaError_t configure_decode_kernel() { return set_max_dyn_smem(decode_kernel); }
 
@@ -1198,7 +1250,8 @@ cudaError_t decode_blocks_per_sm(const DecodeArgs& A, int* blocks) {
 }
 
 cudaError_t launch_decode(cudaStream_t stream, const DecodeArgs& A) {
-  if (A.n_ring < 2 || A.n_ring > kMaxRing) return cudaErrorInvalidValue;
+  if (A.n_slots < 2 * kConsWarps + 2 || A.n_slots > kMaxSlots || A.max_inflight < kConsWarps || A.max_inflight + kConsWarps >= A.n_slots)
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)A.grid);
   cfg.blockDim = dim3(kThreads);

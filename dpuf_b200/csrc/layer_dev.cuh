@@ -23,16 +23,25 @@ DPUF_DEV float sumsq_lane(const float* S, int n8, int j) {
   return acc;
 }
 
-// The same chain with 32 loads in flight per step (identical operation order).
+// The same chain (identical operation order), software-pipelined: the next 32 values are loaded
+// while the current 32 go through the fma chain, whose latency then bounds the loop.
 DPUF_DEV float sumsq_lane32(const float* S, int n8, int j) {
   float acc = 0.0f;
   int i = j;
-  for (; i + 248 < n8; i += 256) {
+  if (i + 248 < n8) {
     float v[32];
 #pragma unroll
     for (int u = 0; u < 32; u++) v[u] = S[i + 8 * u];
+    for (; i + 248 < n8; i += 256) {
+      const bool more = i + 256 + 248 < n8;
+      float nv[32];
 #pragma unroll
-    for (int u = 0; u < 32; u++) acc = __fmaf_rn(v[u], v[u], acc);
+      for (int u = 0; u < 32; u++) nv[u] = more ? S[i + 256 + 8 * u] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 32; u++) acc = __fmaf_rn(v[u], v[u], acc);
+#pragma unroll
+      for (int u = 0; u < 32; u++) v[u] = nv[u];
+    }
   }
   for (; i < n8; i += 8) acc = __fmaf_rn(S[i], S[i], acc);
   return acc;
@@ -92,6 +101,14 @@ DPUF_DEV void qk_norm_rope_warp(float* s, const float* nw, float eps, int hd, co
 // its slab-fused path (M >= 2 and ceil(M/6) >= nt, dpuf_engine.c:1983-2005).
 DPUF_DEV bool swiglu_vector_elem(long long idx, long long total, int nt, bool slab) {
   if (slab) return true;
+  if (total * nt < (1LL << 31)) {  // the same in 32-bit arithmetic (64-bit division is a long routine)
+    const unsigned T = (unsigned)total, i = (unsigned)idx, n = (unsigned)nt;
+    unsigned t = (i * n) / T;
+    while (t > 0 && (T * t) / n > i) t--;
+    while (t + 1 < n && (T * (t + 1)) / n <= i) t++;
+    const unsigned s0 = (T * t) / n, s1 = (T * (t + 1)) / n;
+    return (i - s0) < ((s1 - s0) & ~7u);
+  }
   long long tid = (idx * nt) / total;
   while (tid > 0 && (total * tid) / nt > idx) tid--;
   while (tid + 1 < nt && (total * (tid + 1)) / nt <= idx) tid++;

@@ -120,6 +120,11 @@ class CudaTransformerEngine:
             if self.lib.dpuf_cuda_set_option(self._handle, k.encode(), int(v)) != 0:
                 raise ValueError(f"unknown engine option {k}")
 
+    def set_option(self, name: str, value: int) -> None:
+        """dpuf_cuda_set_option (include/dpuf_cuda.h): engine options and test hooks."""
+        if self.lib.dpuf_cuda_set_option(self._handle, name.encode(), int(value)) != 0:
+            raise ValueError(f"engine option {name}={value} rejected")
+
     # --- reference driver surface (dpuf_format.py:2250-2287)
     def reset_cache(self):
         if self._handle:

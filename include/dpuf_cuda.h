@@ -53,7 +53,14 @@ DPUF_EXPORT int32_t dpuf_cuda_read_logits(void* handle, int32_t row, float* out)
  *   "graphs" (0/1)     capture each step shape in a CUDA graph (default 1)
  *   "persistent" (0/1) run batch-1 steps (forward_token, forward_batch with one token,
  *                      decode_greedy) as one persistent cooperative kernel when the engine
- *                      supports it (default 1; env DPUF_CUDA_PERSISTENT=0 turns it off) */
+ *                      supports it (default 1; env DPUF_CUDA_PERSISTENT=0 turns it off)
+ *   "wait_ms" (> 0)    how long any wait inside the persistent kernel may last before the call
+ *                      gives up with -6 (default: env DPUF_CUDA_WAIT_MS at create, else 2000)
+ *   "test_stall_unit"  failure-detection test hook: in the next persistent launch only, the CTA
+ *                      computing q/k/v unit `value` (8 rows of layer 0, q rows first) withholds
+ *                      its outputs of the first step, so the waits on them run out and the call
+ *                      returns -6; the next call on the same engine starts from a reset
+ *                      exchange area (one GPU) and is exact again */
 DPUF_EXPORT int32_t dpuf_cuda_set_option(void* handle, const char* name, int64_t value);
 
 /* 1 if batch-1 steps run as the persistent kernel, 0 if they run as per-step kernels, -1 for a
@@ -64,12 +71,13 @@ DPUF_EXPORT int32_t dpuf_cuda_persistent_decode(void* handle, const char** why);
 
 /* Phase trace of the persistent kernel's last step, recorded when the engine was created with
  * env DPUF_CUDA_TRACE_DECODE=1 (otherwise returns -1).  Per CTA, per_cta globaltimer stamps
- * (ns): for each layer the end of norm1, q/k/v, its CTA barrier, attention, the grid barrier,
- * o prep, o, its CTA barrier, norm2, gate/up, its CTA barrier, down prep, down, its CTA
- * barrier (14); then step start, embedding, final norm, LM head, its CTA barrier, argmax (6);
- * then the producer's start of each projection (4 per layer, then the LM head).  *n_ctas and
- * *per_cta receive the shape; out (optional) receives n_ctas * per_cta values when max_values
- * is large enough (else -2). */
+ * (ns), as recorded by the CTA's thread 0: for each layer (20) the end of the norm1 residual,
+ * sum of squares and prep; q/k/v; the attention steps (q/k/v words in, inputs ready, QK-norm
+ * and RoPE, scores, softmax, PV, output prep; CTAs hosting no head stamp them all at once);
+ * the o input's load; o; the norm2 residual, sum of squares and prep; the end of warp 0's
+ * gate/up stages; gate/up; the down input's load; down.  Then per step (5): start, embedding,
+ * final norm, LM head, argmax.  *n_ctas and *per_cta receive the shape; out (optional) receives
+ * n_ctas * per_cta values when max_values is large enough (else -2). */
 DPUF_EXPORT int32_t dpuf_cuda_decode_trace(void* handle, int32_t* n_ctas, int32_t* per_cta, uint64_t* out,
                                            int64_t max_values);
 

@@ -79,8 +79,22 @@ gcc "${CFLAGS[@]}" -c "$OUT/src/dpuf_engine.c" -o "$OUT/dpuf_engine.o"
 gcc "${CFLAGS[@]}" -c "$REF/dpuf_vision.c"    -o "$OUT/dpuf_vision.o"
 gcc -shared -fopenmp -o "$OUT/libdpuf_avx2.so" \
     "$OUT/dpuf_avx2.o" "$OUT/dpuf_engine.o" "$OUT/dpuf_vision.o" -lm
-rm -f "$OUT"/*.o
 echo "build_ref: built $OUT/libdpuf_avx2.so"
+
+# The reference's own C host (dpuf-cli.c, unmodified): once over the reference engine, and once
+# linked as its Makefile would be with this repository's libdpuf_cuda.so providing every
+# dpuf_engine_* symbol (the CLI's load-time helpers - tile CRC checks, vision - stay the
+# reference's objects).  The second binary is the drop-in demonstration the GPU tests run.
+gcc "${CFLAGS[@]}" -c "$REF/dpuf-cli.c" -o "$OUT/dpuf-cli.o"
+gcc -fopenmp -o "$OUT/dpuf-cli" "$OUT/dpuf-cli.o" -L"$OUT" -ldpuf_avx2 -Wl,-rpath,'$ORIGIN' -lm
+echo "build_ref: built $OUT/dpuf-cli"
+CUDA_LIB_DIR="$HERE/../dpuf_b200"
+if [ -f "$CUDA_LIB_DIR/libdpuf_cuda.so" ]; then
+  gcc -fopenmp -o "$OUT/dpuf-cli-cuda" "$OUT/dpuf-cli.o" "$OUT/dpuf_avx2.o" "$OUT/dpuf_vision.o" \
+      -L"$CUDA_LIB_DIR" -ldpuf_cuda -Wl,-rpath,'$ORIGIN/../../dpuf_b200' -lm
+  echo "build_ref: built $OUT/dpuf-cli-cuda"
+fi
+rm -f "$OUT"/*.o
 
 # The CLI's token sampler (file-static in dpuf-cli.c), exported by oracle/ref_sample_harness.c.
 gcc "${CFLAGS[@]}" -shared "$HERE/ref_sample_harness.c" -o "$OUT/libdpuf_ref_sample.so" \
