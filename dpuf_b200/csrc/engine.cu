@@ -183,6 +183,14 @@ struct Engine {
   void* tp_peer[kMaxTp] = {};        // other ranks' exchange buffers, opened
 };
 
+// Synchronises the engine's stream; on failure records the CUDA error (a kernel fault surfaces here).
+bool sync_ok(const Engine* e) {
+  const cudaError_t err = cudaStreamSynchronize(e->stream);
+  if (err == cudaSuccess) return true;
+  set_error(std::string("stream synchronisation: ") + cudaGetErrorString(err));
+  return false;
+}
+
 // ------------------------------------------------------------------ helpers
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -832,14 +840,14 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
     if (lm_M == 1) {
       if (cudaMemcpyAsync(e->h_logits, e->last_logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
         return -4;
-      if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+      if (!sync_ok(e)) return -4;
       memcpy(logits_out, e->h_logits, bytes);
     } else {
       if (cudaMemcpyAsync(logits_out, e->logits, bytes, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess) return -4;
-      if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+      if (!sync_ok(e)) return -4;
     }
   } else {
-    if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+    if (!sync_ok(e)) return -4;
   }
   cudaError_t le = cudaGetLastError();
   if (le != cudaSuccess) {
@@ -1247,7 +1255,7 @@ DPUF_EXPORT int32_t dpuf_cuda_decode_batch(void* handle, int32_t n, const int32_
   if (logits_out &&
       cudaMemcpyAsync(logits_out, e->logits, (size_t)n * e->V * 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
     return -4;
-  if (cudaStreamSynchronize(e->stream) != cudaSuccess) return -4;
+  if (!sync_ok(e)) return -4;
   e->last_rows = n;
   e->last_zone_used = 0;
   e->last_logits = e->logits;

@@ -53,6 +53,7 @@ namespace dpuf {
 
 namespace {
 
+
 constexpr int kConsWarps = kDecodeConsWarps;   // consumer warps
 constexpr int kProdWarp = kConsWarps;           // the producer warp
 constexpr int kThreads = (kConsWarps + 1) * 32;  // 384
@@ -61,10 +62,18 @@ constexpr int kKB = 32;                // blocks per stage
 constexpr int kScBytes = kKB * 16;     // 512: fp16 scales [32][8]
 constexpr int kSlotBytes = kScBytes + kKB * 128;  // 4608
 constexpr int kMaxSlots = 48;          // ring slots (shared by the CTA's consumer warps)
+constexpr int kMailbox = 64;           // accumulator hand-over entries (a power of two)
+constexpr int kHandMax = 6;            // at most this many units per CTA: stages spread over all warps
+// Bytes of the norm staging at the start of the union (gains, sign bytes), 16-byte rounded.
+DPUF_HD size_t decode_norm_stage_bytes(const DecodeArgs& A) {
+  return ((size_t)A.H * 4 + (size_t)A.H / 8 + 15) & ~(size_t)15;
+}
+static_assert(kMailbox >= 2 * kHandMax + kMaxSlots + 1, "hand-over entries must outlive their readers");
 constexpr int kChunkWords = 20;        // tagged words of one prepped 64-column chunk
 constexpr int kVTile = 8;              // keys per staged value tile (attention)
 constexpr int kKeyGroups = kConsThreads / 8;
 enum { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
+constexpr int kPhasesPerLayer = 4;  // q/k/v, o, gate/up, down
 
 // ------------------------------------------------------------------ PTX helpers
 DPUF_DEV unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -115,15 +124,13 @@ DPUF_DEV int dp4a_us(unsigned a, int b, int c) {
   return d;
 }
 
-// One phase as seen by this CTA: units u0 .. u0+n-1; consumer warp w takes units u0 + w + k*W.
-// Its stages are interleaved round-robin in the CTA's ring: round r holds stage r of every warp
-// that has one.
+// One phase as seen by this CTA: units u0 .. u0+n-1, in the stage order of Item.
 struct Phase {
   int u0, n;       // the CTA's units
-  int a, extra;    // every warp has a units, warps w < extra one more
   int n_st, n_sub; // stages per group, groups per unit
   int spu;         // stages per unit
-  long long total; // stages of the phase in this CTA
+  int B;           // units per batch: kConsWarps (a warp per unit), or n (hand-over, n <= kHandMax)
+  long long total; // ring positions of the phase in this CTA (batches of B units, padded)
 };
 
 // Shared state of a CTA outside the dynamic buffer.
@@ -137,6 +144,12 @@ struct DecShared {
   volatile int abort;
   const uint8_t* pg[kConsWarps];  // producer: the current round's group of each consumer warp
   Phase ph[5];                     // this CTA's share of each phase kind (fixed for the launch)
+  // the layer table of the current and the next layer (by running layer index step * L + l, mod
+  // 2): the next one is copied during the current one's norm2, so that no consumer step waits
+  // on a global read of a pointer
+  alignas(16) DecLayer lay[2];     // 16-byte aligned: filled by 16-byte cp.async / int4 stores
+  uint64_t mb_bar[kMailbox];       // accumulator hand-over between consumer warps (mb_put / mb_get)
+  float mb_val[kMailbox][8];
 };
 
 // ------------------------------------------------------------------ exchange
@@ -254,18 +267,65 @@ DPUF_DEV Phase compute_phase(const DecodeArgs& A, int kind) {
   const int U = phase_units(A, kind), G = gridDim.x * A.tp_world, c = vcta(A);
   P.u0 = (int)((long long)U * c / G);
   P.n = (int)((long long)U * (c + 1) / G) - P.u0;
-  P.a = P.n / kConsWarps;
-  P.extra = P.n % kConsWarps;
   P.n_st = ((phase_cols(A, kind) >> 5) + kKB - 1) / kKB;
   P.n_sub = kind == kGU ? 2 : 1;
   P.spu = P.n_st * P.n_sub;
-  P.total = (long long)P.n * P.spu;
+  if (P.n <= kHandMax) {
+    P.B = max(P.n, 1);
+    P.total = (long long)P.n * P.spu;
+  } else {
+    P.B = kConsWarps;
+    P.total = (long long)((P.n + kConsWarps - 1) / kConsWarps) * kConsWarps * P.spu;
+  }
   return P;
 }
-DPUF_DEV int warp_units(const Phase& P, int w) { return P.a + (w < P.extra ? 1 : 0); }
-// Ring position of warp w's stage r, relative to the phase's base:
-//   r < a*spu: r*kConsWarps + w;  else: a*spu*kConsWarps + (r - a*spu)*extra + w.
-// Producer and consumers walk it incrementally (produce_phase, consume_phase).
+
+// The stages of a phase in production (ring) order, position p going to consumer warp
+// p % kConsWarps.  The CTA's units go in batches of B; a batch's stages are ordered (stage, group
+// of the unit, unit).
+//  - Many units (B = kConsWarps): warp w takes every stage of unit w of each batch, in order, its
+//    running accumulators in registers.  The last batch is padded with empty units (no rows:
+//    nothing copied, nothing computed), so that this holds for it too.
+//  - Few units (n <= kHandMax, one batch of B = n): stage s+1 of a group is n_sub * B positions
+//    after stage s, on another warp; the running accumulator is handed over through shared
+//    memory (consume_phase).  Every warp then has stages to compute although only n units exist
+//    (q/k/v, o and down have 3 to 6 units per CTA on the 8B shape).
+struct Item {
+  int b;       // batch
+  int t;       // position within the batch
+  int j;       // unit within the batch
+  int sub, s;  // group of the unit (gate/up: 0, 1) and stage
+};
+DPUF_DEV void item_at(const Phase& ph, int p, Item& it) {
+  const int per_batch = ph.spu * ph.B;
+  it.b = p / per_batch;
+  it.t = p - it.b * per_batch;
+  const int r = it.t / ph.B;
+  it.j = it.t - r * ph.B;
+  it.s = r / ph.n_sub;
+  it.sub = r - it.s * ph.n_sub;
+}
+// The item kConsWarps positions later (valid while that position is < ph.total).
+DPUF_DEV void item_next(const Phase& ph, Item& it) {
+  it.t += kConsWarps;
+  it.j += kConsWarps;
+  while (it.j >= ph.B) {
+    it.j -= ph.B;
+    if (++it.sub == ph.n_sub) {
+      it.sub = 0;
+      if (++it.s == ph.n_st) {  // (a warp per unit) the same unit of the next batch
+        it.s = 0;
+        it.b++;
+        it.t -= ph.spu * ph.B;
+      }
+    }
+  }
+}
+// The item's unit, or -1 for a padding unit.
+DPUF_DEV int item_unit(const Phase& ph, const Item& it) {
+  const int v = it.b * ph.B + it.j;
+  return v < ph.n ? ph.u0 + v : -1;
+}
 
 // One 8-row group: where its scales start (the group's data: [n_blk][8] fp16 scales, then
 // [n_blk][4][8][4] nibbles), its rows and its first output row.
@@ -359,62 +419,67 @@ DPUF_DEV bool produce_phase(const DecodeArgs& A, int l, int kind, unsigned char*
   const Phase ph = S.ph[kind];
   const int n_blk = phase_cols(A, kind) >> 5;
   const size_t nib0 = (size_t)n_blk * 16;
-  const int n_k = ph.a + (ph.extra ? 1 : 0);
-  for (int k = 0; k < n_k; k++) {
-    const int W = k < ph.a ? kConsWarps : ph.extra;
+  const int total = (int)ph.total;
+  for (int p0 = 0; p0 < total; p0 += kConsWarps) {
+    const int W = min(kConsWarps, total - p0);
     const bool mine = lane < W;
-    for (int sub = 0; sub < ph.n_sub; sub++) {
-      const uint8_t* gb = nullptr;
-      if (mine) {
-        const Group g = group_of(A, l, kind, ph.u0 + lane + k * kConsWarps, sub);
+    const uint8_t* gb = nullptr;  // the lane's group (null: padding or no rows, nothing to copy)
+    int st = 0, kb = 0;           // its stage and that stage's blocks
+    if (mine) {
+      Item it;
+      item_at(ph, p0 + lane, it);
+      const int u = item_unit(ph, it);
+      if (u >= 0) {
+        const Group g = group_of(A, l, kind, u, it.sub);
+        st = it.s;
+        kb = min(kKB, n_blk - st * kKB);
         if (g.n_r > 0) gb = g.base;
       }
-      for (int s = 0; s < ph.n_st; s++) {
-        const int kb = min(kKB, n_blk - s * kKB);
-        int slot = P.slot + lane;
-        unsigned par = P.par;
-        if (slot >= A.n_slots) {  // W <= n_slots: one wrap at most
-          slot -= A.n_slots;
-          par ^= 1u;
-        }
-        // at most max_inflight stages requested and not yet landed: the round's last stage
-        // waits for the one max_inflight positions before it (copies land about in order).
-        // max_inflight >= W puts that position before this round; n_slots > max_inflight + W
-        // keeps its slot from being reissued before it.
-        bool ok = true;
-        const int back = W - 1 - A.max_inflight;
-        if (lane == 0 && P.issued + back >= 0) {
-          int qs = P.slot + back;
-          unsigned qp = P.par;
-          if (qs < 0) {
-            qs += A.n_slots;
-            qp ^= 1u;
-          }
-          ok = wait_bar(A, &S.full[qs], qp, S);
-        }
-        // the slot's previous use must be released (the first use passes at once)
-        if (ok && mine) ok = wait_bar(A, &S.empty[slot], par ^ 1u, S);
-        if (!__all_sync(kFull, ok)) return false;
-        if (mine) {
-          uint64_t* bar = &S.full[slot];
-          if (gb == nullptr) {
-            mbar_arrive(bar);  // empty group: nothing to copy, the consumer skips it
-          } else {
-            unsigned char* dst = ring + (size_t)slot * kSlotBytes;
-            mbar_expect_tx(bar, (unsigned)kb * 144);
-            bulk_g2s(dst, gb + (size_t)s * kScBytes, (unsigned)kb * 16, bar, P.pol);
-            bulk_g2s(dst + kScBytes, gb + nib0 + (size_t)s * (kKB * 128), (unsigned)kb * 128, bar, P.pol);
-          }
-        }
-        P.slot += W;
-        if (P.slot >= A.n_slots) {
-          P.slot -= A.n_slots;
-          P.par ^= 1u;
-        }
-        P.issued += W;
-      }
-      if (S.abort) return false;
     }
+    int slot = P.slot + lane;
+    unsigned par = P.par;
+    if (slot >= A.n_slots) {  // W <= n_slots: one wrap at most
+      slot -= A.n_slots;
+      par ^= 1u;
+    }
+    // at most max_inflight stages requested and not yet landed: the round's last stage waits
+    // for the one max_inflight positions before it (copies land about in order).
+    // max_inflight >= W puts that position before this round; n_slots > max_inflight + W keeps
+    // its slot from being reissued before it.
+    bool ok = true;
+    const int back = W - 1 - A.max_inflight;
+    if (lane == 0 && P.issued + back >= 0) {
+      int qs = P.slot + back;
+      unsigned qp = P.par;
+      if (qs < 0) {
+        qs += A.n_slots;
+        qp ^= 1u;
+      }
+      ok = wait_bar(A, &S.full[qs], qp, S);
+    }
+    // the slot's previous use must be released (the first use passes at once)
+    if (ok && mine) ok = wait_bar(A, &S.empty[slot], par ^ 1u, S);
+    if (!__all_sync(kFull, ok)) return false;
+    if (mine) {
+      uint64_t* bar = &S.full[slot];
+      if (gb == nullptr) {
+        mbar_arrive(bar);  // empty group: nothing to copy, the consumer skips it
+      } else {
+        // the stage's scales (16 B per block) and nibbles (128 B per block, after the group's
+        // n_blk scales)
+        unsigned char* dst = ring + (size_t)slot * kSlotBytes;
+        mbar_expect_tx(bar, (unsigned)kb * 144);
+        bulk_g2s(dst, gb + (size_t)st * kScBytes, (unsigned)kb * 16, bar, P.pol);
+        bulk_g2s(dst + kScBytes, gb + nib0 + (size_t)st * (kKB * 128), (unsigned)kb * 128, bar, P.pol);
+      }
+    }
+    P.slot += W;
+    if (P.slot >= A.n_slots) {
+      P.slot -= A.n_slots;
+      P.par ^= 1u;
+    }
+    P.issued += W;
+    if (S.abort) return false;
   }
   return true;
 }
@@ -423,10 +488,9 @@ DPUF_DEV bool produce_phase(const DecodeArgs& A, int l, int kind, unsigned char*
 // Lane (ri, q): row ri's blocks 8q .. 8q+7 of the stage; then the in-order chain over the
 // stage's blocks, octet by octet (octet q continues the accumulator of octet q-1).
 template <bool kFull>
-DPUF_DEV void stage_chain(const unsigned char* slot, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
-                          int ri, int q, float& acc) {
+DPUF_DEV void stage_terms(const unsigned char* slot, const int8_t* xq, const float* xs, const int* xm, int b0, int kb,
+                          int ri, int q, float (&pp)[8], float (&ss)[8]) {
   const unsigned char* nib = slot + kScBytes;
-  float pp[8], ss[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int bl = q * 8 + j;
@@ -451,6 +515,10 @@ DPUF_DEV void stage_chain(const unsigned char* slot, const int8_t* xq, const flo
       if (!(bsc > 0.0f)) pp[j] = 0.0f;
     }
   }
+}
+// The stage's chain: octet q continues the accumulator of octet q-1 (every lane ends with its
+// row's running accumulator).
+DPUF_DEV void octet_chain(const float (&pp)[8], const float (&ss)[8], int ri, int q, float& acc) {
 #pragma unroll
   for (int qq = 0; qq < 4; qq++) {
     if (q == qq) {
@@ -472,6 +540,7 @@ DPUF_DEV void better(float& bv, int& bi, float v, int i) {
 struct Consumer {
   int slot = 0;          // ring slot of the current phase's first stage
   unsigned par = 0;      // parity of that slot's use
+  unsigned hpos = 0;     // positions of the hand-over phases so far (the hand-over tags)
   float bv = -INFINITY;  // running argmax of the LM head (lanes of octet 0)
   int bi = 0x7fffffff;
 };
@@ -533,97 +602,147 @@ DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
     A.trace[(size_t)blockIdx.x * A.trace_per_cta + ev] = globaltimer();
 }
 
-// One projection phase on the consumer side of warp `warp`: every unit of the warp, every group,
-// every stage; the epilogue stores the rows.
+// Hand-over of running accumulators between consumer warps: entry (tag mod kMailbox) holds the
+// eight rows' accumulators after the stage with tag `tag` - its position counted over the
+// hand-over phases only, from 0 in each launch.  Its mbarrier completes one phase per tag: the
+// warp of every position of a hand-over phase arrives once (mb_done, after writing the values if
+// anyone reads them), so tag `tag` is phase tag / kMailbox of its entry (parity
+// (tag / kMailbox) & 1).  Phases with a warp per unit do not use it.
+// An entry is rewritten kMailbox positions later; its reader is at most 2 * kHandMax positions
+// after the writer and releases its own stage only after reading, and a stage is only produced
+// once every position n_slots or more before it has been released - so with kMailbox >=
+// 2 * kHandMax + kMaxSlots + 1 an entry is never rewritten (nor its barrier advanced twice)
+// before it is read.
+DPUF_DEV void mb_put(DecShared& S, unsigned tag, int lane, float acc) {
+  if (lane < 8) S.mb_val[tag & (kMailbox - 1)][lane] = acc;  // lane ri of octet 0: row ri
+}
+DPUF_DEV void mb_done(DecShared& S, unsigned tag, int lane) {
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_block();
+    mbar_arrive(&S.mb_bar[tag & (kMailbox - 1)]);  // release: the values before the phase completes
+  }
+}
+DPUF_DEV float mb_get(const DecodeArgs& A, DecShared& S, unsigned tag, int ri) {
+  const int e = (int)(tag & (kMailbox - 1));
+  const unsigned par = (tag / kMailbox) & 1u;
+  if (!mbar_try(&S.mb_bar[e], par)) {
+    const unsigned long long t0 = globaltimer();
+    for (int it = 1; !mbar_try(&S.mb_bar[e], par); it++) {
+      if ((it & 63) == 0) {
+        if (check_abort(A, S)) break;
+        if (globaltimer() - t0 > A.wait_ns) {
+          raise_err(A, 4);
+          S.abort = 1;
+          break;
+        }
+      }
+    }
+  }
+  return S.mb_val[e][ri];
+}
+
+// One projection phase on the consumer side of warp `warp`: its positions warp, warp +
+// kConsWarps, ... of the phase (Item), each stage's terms, the accumulator chain (continued from
+// this warp's registers or from the hand-over), and at a unit's last stage the epilogue, which
+// stores the rows.  dsg: the down projection's column-sign bytes in shared memory (gate/up only).
 DPUF_DEV void consume_phase(const DecodeArgs& A, int step, int l, int kind, unsigned gen, unsigned char* ring,
-                            Consumer& C, const int8_t* xq, const float* xs, const int* xm, DecShared& S) {
+                            Consumer& C, const int8_t* xq, const float* xs, const int* xm, const uint8_t* dsg,
+                            DecShared& S) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ri = lane & 7, q = lane >> 3;
   const Phase ph = S.ph[kind];
-  const int n_w = warp_units(ph, warp);
+  const int total = (int)ph.total;
   const int n_blk = phase_cols(A, kind) >> 5;
   const bool stall = step == 0 && l == 0 && kind == kQKV && A.stall_unit >= ph.u0 && A.stall_unit < ph.u0 + ph.n;
-  // gate/up: the down projection's sign table, read now so that its latency hides behind the
-  // stages (the sign byte itself is read after the gate half of the unit)
-  const uint8_t* dsigns = kind == kGU ? ldg_ptr(&A.layers[l].signs[3]) : nullptr;
-  // ring cursor of this warp's stages: positions (phase start) + w, then +kConsWarps per stage
-  // through the full rounds, then +extra through the last (partial) round
-  const long long full = (long long)ph.a * ph.spu;
   int slot = C.slot + warp;
   unsigned par = C.par;
-  if (slot >= A.n_slots) {
+  while (slot >= A.n_slots) {
     slot -= A.n_slots;
     par ^= 1u;
   }
-  int r = 0;
-  if (kind == kGU && n_w == 0) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
-  for (int k = 0; k < n_w; k++) {
-    const int u = ph.u0 + warp + k * kConsWarps;
-    float accs[2] = {0.0f, 0.0f};
-    Group g{};
-    uint8_t dsb = 0;
-    for (int sub = 0; sub < ph.n_sub; sub++) {
-      g = group_rows(A, kind, u, sub);
-      if (sub == 1 && dsigns && (u & 7) == 7) dsb = __ldg(dsigns + (u >> 3) * 8 + (lane & 7));
-      float acc = 0.0f;
-      for (int s = 0; s < ph.n_st; s++, r++) {
-        if (r > 0) {
-          slot += r <= full ? kConsWarps : ph.extra;
-          while (slot >= A.n_slots) {
-            slot -= A.n_slots;
-            par ^= 1u;
-          }
-        }
-        const bool ok = __all_sync(kFull, ring_wait(A, &S.full[slot], par, S));
-        if (ok && g.n_r > 0) {
-          const int b0 = s * kKB, kb = min(kKB, n_blk - b0);
-          const unsigned char* st = ring + (size_t)slot * kSlotBytes;
-          if (kb == kKB)
-            stage_chain<true>(st, xq, xs, xm, b0, kb, ri, q, acc);
-          else
-            stage_chain<false>(st, xq, xs, xm, b0, kb, ri, q, acc);
-        }
-        __syncwarp();  // every lane is done with the slot: release it
-        if (lane == 0) mbar_arrive(&S.empty[slot]);
-      }
-      accs[sub] = acc;
+  Item it;
+  if (warp < total) item_at(ph, warp, it);
+  if (kind == kGU && warp >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+  const bool own = ph.B == kConsWarps;  // every stage of a unit is one warp's
+  float acc0 = 0.0f, acc1 = 0.0f;        // (own) the running accumulators of the warp's unit
+  for (int p = warp; p < total; p += kConsWarps) {
+    const int u = item_unit(ph, it);
+    const Group g = u >= 0 ? group_rows(A, kind, u, it.sub) : rows_of(0, 0, 0);  // padding: no rows
+    const bool ok = __all_sync(kFull, ring_wait(A, &S.full[slot], par, S));
+    float pp[8], ss[8];
+    const bool live = ok && g.n_r > 0;
+    if (live) {
+      const int b0 = it.s * kKB, kb = min(kKB, n_blk - b0);
+      const unsigned char* st = ring + (size_t)slot * kSlotBytes;
+      if (kb == kKB)
+        stage_terms<true>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
+      else
+        stage_terms<false>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
     }
-    if (kind == kGU && k == n_w - 1) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
-    // ---- epilogue: lanes of octet 0 hold rows g.row + ri
-    const bool mine = q == 0 && ri < g.n_r;
-    const int row = g.row + ri;
-    if (kind == kQKV) {
-      uint64_t* dst = g.mat == 0 ? A.q : (g.mat == 1 ? A.k : A.v);
-      if (mine && !stall) put_tagged(A, dst + row, tagged(accs[0], gen));
-    } else if (kind == kO) {
-      if (mine) put_tagged(A, A.o_out + row, tagged(accs[0], gen));
-    } else if (kind == kDown) {
-      if (mine) put_tagged(A, A.d_out + row, tagged(accs[0], gen));
-    } else if (kind == kLM) {
-      if (mine) {
-        if (A.write_logits) put_float(A, A.logits + row, accs[0]);
-        better(C.bv, C.bi, accs[0], row);
+    float acc = 0.0f;
+    if (it.s > 0) acc = own ? (it.sub ? acc1 : acc0) : mb_get(A, S, C.hpos + (unsigned)(p - ph.n_sub * ph.B), ri);
+    if (live) octet_chain(pp, ss, ri, q, acc);
+    if (own) {
+      if (it.sub) acc1 = acc;
+      else acc0 = acc;
+    }
+    __syncwarp();  // every lane is done with the slot (and the hand-over): release it
+    if (lane == 0) mbar_arrive(&S.empty[slot]);
+    if (kind == kGU && p + kConsWarps >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+    const bool last = it.s == ph.n_st - 1 && it.sub == ph.n_sub - 1;  // the unit's last stage
+    if (!own) {
+      if (!last) mb_put(S, C.hpos + (unsigned)p, lane, acc);
+      mb_done(S, C.hpos + (unsigned)p, lane);
+    }
+    if (last && u >= 0) {
+      // ---- the unit's last stage: epilogue (lanes of octet 0 hold rows g.row + ri)
+      float a0 = acc, a1 = 0.0f;
+      if (ph.n_sub == 2) {
+        a1 = acc;
+        a0 = own ? acc0 : mb_get(A, S, C.hpos + (unsigned)(p - ph.B), ri);
       }
-    } else {
-      // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every
-      // rank; the warp holding the last pair of a 64-column chunk preps that chunk
-      if (mine)
-        put_tagged(A, A.s_raw + row,
-                   tagged(swiglu_one(accs[0], accs[1], A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et),
-                          gen));
-      if ((u & 7) == 7) {
-        __syncwarp();
-        prep_down_chunk(A, u >> 3, gen, dsb, S);
+      const bool mine = q == 0 && ri < g.n_r;
+      const int row = g.row + ri;
+      if (kind == kQKV) {
+        uint64_t* dst = g.mat == 0 ? A.q : (g.mat == 1 ? A.k : A.v);
+        if (mine && !stall) put_tagged(A, dst + row, tagged(a0, gen));
+      } else if (kind == kO) {
+        if (mine) put_tagged(A, A.o_out + row, tagged(a0, gen));
+      } else if (kind == kDown) {
+        if (mine) put_tagged(A, A.d_out + row, tagged(a0, gen));
+      } else if (kind == kLM) {
+        if (mine) {
+          if (A.write_logits) put_float(A, A.logits + row, a0);
+          better(C.bv, C.bi, a0, row);
+        }
+      } else {
+        // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every
+        // rank; the warp holding the last pair of a 64-column chunk preps that chunk
+        if (mine)
+          put_tagged(A, A.s_raw + row,
+                     tagged(swiglu_one(a0, a1, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et), gen));
+        if ((u & 7) == 7) {
+          __syncwarp();
+          prep_down_chunk(A, u >> 3, gen, dsg ? dsg[(u >> 3) * 8 + (lane & 7)] : (uint8_t)0, S);
+        }
       }
     }
+    slot += kConsWarps;
+    while (slot >= A.n_slots) {
+      slot -= A.n_slots;
+      par ^= 1u;
+    }
+    if (p + kConsWarps < total) item_next(ph, it);
   }
   {  // the next phase starts ph.total positions later
-    const int tot = (int)ph.total, q = tot / A.n_slots;
-    C.slot += tot - q * A.n_slots;
-    C.par ^= (unsigned)q & 1u;
+    const int q2 = total / A.n_slots;
+    C.slot += total - q2 * A.n_slots;
+    C.par ^= (unsigned)q2 & 1u;
     if (C.slot >= A.n_slots) {
       C.slot -= A.n_slots;
       C.par ^= 1u;
     }
+    if (!own) C.hpos += (unsigned)total;
   }
 }
 
@@ -637,13 +756,20 @@ DPUF_DEV void cta_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kConsThreads) : 
 // bytes go to shared memory (stage) asynchronously before the residual is waited for.
 DPUF_DEV void norm_prep(const DecodeArgs& A, float* h, const uint64_t* res, unsigned gen, int n_valid, const float* w,
                         const uint8_t* signs, int8_t* xq, float* xs, int* xm, float* stage, DecShared& S, int step,
-                        int ev) {
+                        int ev, const DecLayer* next_src = nullptr, DecLayer* next_dst = nullptr,
+                        const uint8_t* xsrc = nullptr, uint8_t* xdst = nullptr, int xbytes = 0) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = A.H;
   float* sw = stage;
   uint8_t* sg = (uint8_t*)(stage + H);
   for (int i = tid * 4; i < H; i += kConsThreads * 4) cp_async16_cg(sw + i, w + i);
   if (signs)
     for (int i = tid * 8; i < H / 8; i += kConsThreads * 8) cp_async8_ca(sg + i, signs + i);
+  // the next layer's table and extra bytes (the down projection's sign bytes) ride along, waited
+  // for with the gains
+  if (next_src && tid < (int)(sizeof(DecLayer) / 16))
+    cp_async16_cg((unsigned char*)next_dst + tid * 16, (const unsigned char*)next_src + tid * 16);
+  if (xsrc)
+    for (int i = tid * 8; i < xbytes; i += kConsThreads * 8) cp_async8_ca(xdst + i, xsrc + i);
   cp_async_commit();
   if (res) {
     // every word is loaded first (all in flight), then the stale ones are waited for
@@ -1030,12 +1156,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
   float* xs = (float*)(xq + A.kmax);
   int* xm = (int*)(xs + A.kmax / 32);
   float* U = (float*)(((uintptr_t)(xm + A.kmax / 32) + 15) & ~(uintptr_t)15);  // union (16-byte aligned)
+  // the down projection's sign bytes (staged by norm2, read by the gate/up epilogues), after the
+  // norm staging in the union
+  uint8_t* dsg = (uint8_t*)U + decode_norm_stage_bytes(A);
 
   if (tid == 0) {
     for (int i = 0; i < A.n_slots; i++) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.empty[i], 1);
     }
+    for (int i = 0; i < kMailbox; i++) mbar_init(&S.mb_bar[i], 1);
     S.abort = 0;
     for (int k = kQKV; k <= kLM; k++) S.ph[k] = compute_phase(A, k);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1047,10 +1177,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
     Producer P;
     P.pol = l2_evict_first_policy();
     bool ok = true;
-    for (int step = 0; ok && step < A.n_steps; step++) {
-      for (int l = 0; ok && l < A.L; l++)
-        for (int kind = kQKV; ok && kind <= kDown; kind++) ok = produce_phase(A, l, kind, ring, P, S);
-      if (ok) ok = produce_phase(A, A.L, kLM, ring, P, S);
+    // one call site for every phase (the body is inlined once: see the consumer loop)
+    const int n_ph = kPhasesPerLayer * A.L + 1;
+    for (int i = 0; ok && i < A.n_steps * n_ph; i++) {
+      const int k = i % n_ph, l = k / kPhasesPerLayer;
+      ok = produce_phase(A, l, l < A.L ? k % kPhasesPerLayer : kLM, ring, P, S);
     }
     // copies still in flight must land before the CTA exits: every slot's last fill
     if (lane == 0) {
@@ -1067,6 +1198,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
   // query heads of this CTA: hh with floor(hh * grid / nq) == blockIdx.x, i.e. [head_lo, head_hi)
   const int head_lo = (int)((blockIdx.x * A.nq + gridDim.x - 1) / gridDim.x);
   const int head_hi = (int)(((blockIdx.x + 1) * A.nq + gridDim.x - 1) / gridDim.x);
+  // the first layer's table (later ones are staged one layer ahead)
+  if (A.L > 0 && tid < (int)(sizeof(DecLayer) / 16))
+    ((int4*)&S.lay[0])[tid] = __ldg((const int4*)A.layers + tid);
+  cta_sync();
   const int n_chunks = H / 64;
   for (int step = 0; step < A.n_steps; step++) {
     const int pos = A.pos0 + step;
@@ -1094,47 +1229,56 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
       cta_sync();
     }
     trace_at(A, step, kEvPerLayer * A.L + kEvEmbed);
-    for (int l = 0; l < A.L; l++) {
-      const DecLayer* Ly = A.layers + l;
-      const int lb = kEvPerLayer * l;
-      const unsigned g = g_step + (unsigned)l;
-      norm_prep(A, h, l > 0 ? A.d_out : nullptr, g - 1, A.keep_down * kTileRows, Ly->attn_norm, Ly->signs[0], xq,
-                xs, xm, U, S, step, lb + kEvNorm1Res);
-      trace_at(A, step, lb + kEvNorm1);
-      // the first head this CTA hosts: its step-independent inputs are requested now
-      if (head_lo < head_hi) attention_prefetch(A, Ly, l, pos, head_lo, U);
-      consume_phase(A, step, l, kQKV, g, ring, C, xq, xs, xm, S);
-      cta_sync();
-      trace_at(A, step, lb + kEvQKV);
-      for (int hh = head_lo; hh < head_hi; hh++)
-        attention_head(A, Ly, l, pos, hh, g, U, hh == head_lo, S, step, lb + kEvAttnIn);
-      if (head_lo == head_hi)
-        for (int ev = kEvAttnIn; ev <= kEvAttnPV; ev++) trace_at(A, step, lb + ev);
-      trace_at(A, step, lb + kEvAttn);
-      load_prepped(A, A.oprep, A.qd / 64, g, xq, xs, xm, S);
-      trace_at(A, step, lb + kEvLoadO);
-      consume_phase(A, step, l, kO, g, ring, C, xq, xs, xm, S);
-      cta_sync();
-      trace_at(A, step, lb + kEvO);
-      norm_prep(A, h, A.o_out, g, H, Ly->ffn_norm, Ly->signs[2], xq, xs, xm, U, S, step, lb + kEvNorm2Res);
-      trace_at(A, step, lb + kEvNorm2);
-      consume_phase(A, step, l, kGU, g, ring, C, xq, xs, xm, S);
-      cta_sync();
-      trace_at(A, step, lb + kEvGU);
-      load_prepped(A, A.dprep, A.I / 64, g, xq, xs, xm, S);
-      trace_at(A, step, lb + kEvLoadD);
-      consume_phase(A, step, l, kDown, g, ring, C, xq, xs, xm, S);
-      cta_sync();
-      trace_at(A, step, lb + kEvDown);
-    }
+    // The layers' phases and the LM head as one sequence, so that every phase body (norm, prep
+    // loads, attention, the projection) is inlined once: the kernel re-executes all of it every
+    // layer, and a footprint that the instruction cache holds keeps instruction fetches off L2,
+    // which is busy with the weight stream.
+    const int n_ph = kPhasesPerLayer * A.L + 1;
     const unsigned g_lm = g_step + (unsigned)A.L;
     const int sb = kEvPerLayer * A.L;
-    norm_prep(A, h, A.L > 0 ? A.d_out : nullptr, g_lm - 1, A.keep_down * kTileRows, A.out_norm, A.lm_signs, xq, xs,
-              xm, U, S, step, -1);
-    trace_at(A, step, sb + kEvNormF);
     C.bv = -INFINITY;
     C.bi = 0x7fffffff;
-    consume_phase(A, step, A.L, kLM, g_lm, ring, C, xq, xs, xm, S);
+    for (int k = 0; k < n_ph; k++) {
+      const int l = k / kPhasesPerLayer, kind = l < A.L ? k % kPhasesPerLayer : kLM;
+      const int gl = step * A.L + l;  // running layer index: table buffer gl & 1
+      const DecLayer* Ly = &S.lay[gl & 1];
+      const int lb = kEvPerLayer * l;
+      const unsigned g = g_step + (unsigned)l;
+      // ---- before the projection: its input
+      if (kind == kQKV || kind == kGU || kind == kLM) {
+        // residual add + RMSNorm + prep: attention norm (the previous layer's down output, none
+        // before layer 0), FFN norm (the o output; the next layer's table and the down
+        // projection's sign bytes ride along), final norm
+        const bool ffn = kind == kGU, more = l + 1 < A.L || step + 1 < A.n_steps;
+        const uint64_t* res = ffn ? A.o_out : (l > 0 ? A.d_out : nullptr);
+        norm_prep(A, h, res, ffn ? g : g - 1, ffn ? H : A.keep_down * kTileRows,
+                  kind == kLM ? A.out_norm : (ffn ? Ly->ffn_norm : Ly->attn_norm),
+                  kind == kLM ? A.lm_signs : (ffn ? Ly->signs[2] : Ly->signs[0]), xq, xs, xm, U, S, step,
+                  kind == kLM ? -1 : lb + (ffn ? kEvNorm2Res : kEvNorm1Res),
+                  ffn && more ? A.layers + (l + 1 < A.L ? l + 1 : 0) : nullptr, &S.lay[(gl + 1) & 1],
+                  ffn ? Ly->signs[3] : nullptr, dsg, A.I / 8);
+        trace_at(A, step, kind == kLM ? sb + kEvNormF : lb + (ffn ? kEvNorm2 : kEvNorm1));
+        // the first head this CTA hosts: its step-independent inputs are requested now
+        if (kind == kQKV && head_lo < head_hi) attention_prefetch(A, Ly, l, pos, head_lo, U);
+      } else {
+        if (kind == kO) {
+          for (int hh = head_lo; hh < head_hi; hh++)
+            attention_head(A, Ly, l, pos, hh, g, U, hh == head_lo, S, step, lb + kEvAttnIn);
+          if (head_lo == head_hi)
+            for (int ev = kEvAttnIn; ev <= kEvAttnPV; ev++) trace_at(A, step, lb + ev);
+          trace_at(A, step, lb + kEvAttn);
+        }
+        // the prepped input of o (from the attention CTAs) or of down (from the gate/up epilogues)
+        load_prepped(A, kind == kO ? A.oprep : A.dprep, (kind == kO ? A.qd : A.I) / 64, g, xq, xs, xm, S);
+        trace_at(A, step, lb + (kind == kO ? kEvLoadO : kEvLoadD));
+      }
+      consume_phase(A, step, l, kind, kind == kLM ? g_lm : g, ring, C, xq, xs, xm,
+                    kind == kGU && Ly->signs[3] ? dsg : nullptr, S);
+      if (kind != kLM) {
+        cta_sync();
+        trace_at(A, step, lb + (kind == kQKV ? kEvQKV : (kind == kO ? kEvO : (kind == kGU ? kEvGU : kEvDown))));
+      }
+    }
     trace_at(A, step, sb + kEvLM);
     {
       // this CTA's argmax partial (lanes of octet 0 of every warp hold running maxima)
@@ -1212,12 +1356,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
 
 // Shared memory of one CTA: the ring | h | x (codes, block scales, block sums) | a union of the
 // attention scratch (q, k, v, output, QK-norm gains, RoPE row, sign bytes, scores over max_seq
-// keys, two value tiles), the norm staging (gains, sign bytes) and the embedding staging (the
-// row's group and the sign bytes).
+// keys, two value tiles), the norm staging (gains, sign bytes; and after norm2 the down
+// projection's sign bytes, read by the gate/up epilogues) and the embedding staging (the row's
+// group and the sign bytes).
 size_t decode_union_bytes(const DecodeArgs& A) {
   const size_t attn = ((size_t)7 * A.hd + (((size_t)A.S + 3) & ~(size_t)3) + (size_t)2 * kVTile * A.hd) * sizeof(float) +
                       16 * (((size_t)A.hd / 8 + 15) / 16);
-  const size_t norm = (size_t)A.H * 4 + (size_t)A.H / 8 + 16;
+  const size_t norm = decode_norm_stage_bytes(A) + (size_t)A.I / 8;  // + the down projection's sign bytes
   const size_t embed = (size_t)(A.H / 32) * 144 + (size_t)A.H / 8 + 16;
   return std::max(attn, std::max(norm, embed));
 }
