@@ -642,10 +642,65 @@ DPUF_DEV float mb_get(const DecodeArgs& A, DecShared& S, unsigned tag, int ri) {
   return S.mb_val[e][ri];
 }
 
+// The terms of one stage (in ring slot `slot`, stage s of a group with rows): false without rows
+// or after an abort.
+DPUF_DEV bool stage_at(const DecodeArgs& A, DecShared& S, const unsigned char* ring, int slot, unsigned par, int s,
+                       int n_r, int n_blk, const int8_t* xq, const float* xs, const int* xm, int ri, int q,
+                       float (&pp)[8], float (&ss)[8]) {
+  const bool ok = __all_sync(kFull, ring_wait(A, &S.full[slot], par, S));
+  if (!ok || n_r <= 0) return false;
+  const int b0 = s * kKB, kb = min(kKB, n_blk - b0);
+  const unsigned char* st = ring + (size_t)slot * kSlotBytes;
+  if (kb == kKB)
+    stage_terms<true>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
+  else
+    stage_terms<false>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
+  return true;
+}
+// Releases a ring slot once every lane is done with it.
+DPUF_DEV void release_slot(DecShared& S, int slot, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&S.empty[slot]);
+}
+
+// The epilogue of unit u (final accumulators a0, and a1 for the up half of a gate/up pair;
+// lanes of octet 0 hold rows g.row + ri): stores the rows, as the phase's consumers read them.
+DPUF_DEV void unit_epilogue(const DecodeArgs& A, DecShared& S, int kind, int u, const Group& g, float a0, float a1,
+                            unsigned gen, bool stall, const uint8_t* dsg, Consumer& C, int lane) {
+  const int ri = lane & 7, q = lane >> 3;
+  const bool mine = q == 0 && ri < g.n_r;
+  const int row = g.row + ri;
+  if (kind == kQKV) {
+    uint64_t* dst = g.mat == 0 ? A.q : (g.mat == 1 ? A.k : A.v);
+    if (mine && !stall) put_tagged(A, dst + row, tagged(a0, gen));
+  } else if (kind == kO) {
+    if (mine) put_tagged(A, A.o_out + row, tagged(a0, gen));
+  } else if (kind == kDown) {
+    if (mine) put_tagged(A, A.d_out + row, tagged(a0, gen));
+  } else if (kind == kLM) {
+    if (mine) {
+      if (A.write_logits) put_float(A, A.logits + row, a0);
+      better(C.bv, C.bi, a0, row);
+    }
+  } else {
+    // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every rank;
+    // the warp holding the last pair of a 64-column chunk preps that chunk
+    if (mine)
+      put_tagged(A, A.s_raw + row,
+                 tagged(swiglu_one(a0, a1, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et), gen));
+    if ((u & 7) == 7) {
+      __syncwarp();
+      prep_down_chunk(A, u >> 3, gen, dsg ? dsg[(u >> 3) * 8 + (lane & 7)] : (uint8_t)0, S);
+    }
+  }
+}
+
 // One projection phase on the consumer side of warp `warp`: its positions warp, warp +
-// kConsWarps, ... of the phase (Item), each stage's terms, the accumulator chain (continued from
-// this warp's registers or from the hand-over), and at a unit's last stage the epilogue, which
-// stores the rows.  dsg: the down projection's column-sign bytes in shared memory (gate/up only).
+// kConsWarps, ... of the phase (Item).  A warp per unit: for each batch, the stages of the
+// warp's unit in a tight loop (accumulators in registers), then its epilogue, so that the loop
+// body stays small.  Hand-over: each position's stage terms, the accumulator chain continued from
+// the hand-over, and at a unit's last stage the epilogue.  dsg: the down projection's
+// column-sign bytes in shared memory (gate/up only).
 DPUF_DEV void consume_phase(const DecodeArgs& A, int step, int l, int kind, unsigned gen, unsigned char* ring,
                             Consumer& C, const int8_t* xq, const float* xs, const int* xm, const uint8_t* dsg,
                             DecShared& S) {
@@ -660,79 +715,63 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, int step, int l, int kind, unsi
     slot -= A.n_slots;
     par ^= 1u;
   }
-  Item it;
-  if (warp < total) item_at(ph, warp, it);
-  if (kind == kGU && warp >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
-  const bool own = ph.B == kConsWarps;  // every stage of a unit is one warp's
-  float acc0 = 0.0f, acc1 = 0.0f;        // (own) the running accumulators of the warp's unit
-  for (int p = warp; p < total; p += kConsWarps) {
-    const int u = item_unit(ph, it);
-    const Group g = u >= 0 ? group_rows(A, kind, u, it.sub) : rows_of(0, 0, 0);  // padding: no rows
-    const bool ok = __all_sync(kFull, ring_wait(A, &S.full[slot], par, S));
-    float pp[8], ss[8];
-    const bool live = ok && g.n_r > 0;
-    if (live) {
-      const int b0 = it.s * kKB, kb = min(kKB, n_blk - b0);
-      const unsigned char* st = ring + (size_t)slot * kSlotBytes;
-      if (kb == kKB)
-        stage_terms<true>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
-      else
-        stage_terms<false>(st, xq, xs, xm, b0, kb, ri, q, pp, ss);
-    }
-    float acc = 0.0f;
-    if (it.s > 0) acc = own ? (it.sub ? acc1 : acc0) : mb_get(A, S, C.hpos + (unsigned)(p - ph.n_sub * ph.B), ri);
-    if (live) octet_chain(pp, ss, ri, q, acc);
-    if (own) {
-      if (it.sub) acc1 = acc;
-      else acc0 = acc;
-    }
-    __syncwarp();  // every lane is done with the slot (and the hand-over): release it
-    if (lane == 0) mbar_arrive(&S.empty[slot]);
-    if (kind == kGU && p + kConsWarps >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
-    const bool last = it.s == ph.n_st - 1 && it.sub == ph.n_sub - 1;  // the unit's last stage
-    if (!own) {
-      if (!last) mb_put(S, C.hpos + (unsigned)p, lane, acc);
-      mb_done(S, C.hpos + (unsigned)p, lane);
-    }
-    if (last && u >= 0) {
-      // ---- the unit's last stage: epilogue (lanes of octet 0 hold rows g.row + ri)
-      float a0 = acc, a1 = 0.0f;
-      if (ph.n_sub == 2) {
-        a1 = acc;
-        a0 = own ? acc0 : mb_get(A, S, C.hpos + (unsigned)(p - ph.B), ri);
-      }
-      const bool mine = q == 0 && ri < g.n_r;
-      const int row = g.row + ri;
-      if (kind == kQKV) {
-        uint64_t* dst = g.mat == 0 ? A.q : (g.mat == 1 ? A.k : A.v);
-        if (mine && !stall) put_tagged(A, dst + row, tagged(a0, gen));
-      } else if (kind == kO) {
-        if (mine) put_tagged(A, A.o_out + row, tagged(a0, gen));
-      } else if (kind == kDown) {
-        if (mine) put_tagged(A, A.d_out + row, tagged(a0, gen));
-      } else if (kind == kLM) {
-        if (mine) {
-          if (A.write_logits) put_float(A, A.logits + row, a0);
-          better(C.bv, C.bi, a0, row);
-        }
-      } else {
-        // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every
-        // rank; the warp holding the last pair of a 64-column chunk preps that chunk
-        if (mine)
-          put_tagged(A, A.s_raw + row,
-                     tagged(swiglu_one(a0, a1, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et), gen));
-        if ((u & 7) == 7) {
-          __syncwarp();
-          prep_down_chunk(A, u >> 3, gen, dsg ? dsg[(u >> 3) * 8 + (lane & 7)] : (uint8_t)0, S);
-        }
-      }
-    }
+  auto advance = [&]() {
     slot += kConsWarps;
     while (slot >= A.n_slots) {
       slot -= A.n_slots;
       par ^= 1u;
     }
-    if (p + kConsWarps < total) item_next(ph, it);
+  };
+  const bool own = ph.B == kConsWarps;
+  if (own) {
+    // unit b * kConsWarps + warp of batch b: its stage r (r = s * n_sub + sub) is at position
+    // b * kConsWarps * spu + r * kConsWarps + warp
+    const int nb = total / (kConsWarps * ph.spu);
+    for (int b = 0; b < nb; b++) {
+      const int v = b * kConsWarps + warp;
+      const int u = v < ph.n ? ph.u0 + v : -1;  // -1: padding (nothing copied, nothing computed)
+      const Group g0 = u >= 0 ? group_rows(A, kind, u, 0) : rows_of(0, 0, 0);
+      const Group g1 = u >= 0 && ph.n_sub == 2 ? group_rows(A, kind, u, 1) : g0;
+      float acc0 = 0.0f, acc1 = 0.0f;
+      for (int r = 0; r < ph.spu; r++) {
+        const int sub = ph.n_sub == 2 ? (r & 1) : 0, s = ph.n_sub == 2 ? (r >> 1) : r;
+        float pp[8], ss[8];
+        const bool live = stage_at(A, S, ring, slot, par, s, sub ? g1.n_r : g0.n_r, n_blk, xq, xs, xm, ri, q, pp, ss);
+        if (live) {
+          if (sub) octet_chain(pp, ss, ri, q, acc1);
+          else octet_chain(pp, ss, ri, q, acc0);
+        }
+        release_slot(S, slot, lane);
+        advance();
+      }
+      if (kind == kGU && b == nb - 1) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+      if (u >= 0) unit_epilogue(A, S, kind, u, ph.n_sub == 2 ? g1 : g0, acc0, acc1, gen, stall, dsg, C, lane);
+    }
+    if (kind == kGU && nb == 0) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+  } else {
+    Item it;
+    if (warp < total) item_at(ph, warp, it);
+    if (kind == kGU && warp >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+    for (int p = warp; p < total; p += kConsWarps) {
+      const int u = item_unit(ph, it);  // (no padding in this mode)
+      const Group g = group_rows(A, kind, u, it.sub);
+      float pp[8], ss[8];
+      const bool live = stage_at(A, S, ring, slot, par, it.s, g.n_r, n_blk, xq, xs, xm, ri, q, pp, ss);
+      float acc = 0.0f;
+      if (it.s > 0) acc = mb_get(A, S, C.hpos + (unsigned)(p - ph.n_sub * ph.B), ri);
+      if (live) octet_chain(pp, ss, ri, q, acc);
+      release_slot(S, slot, lane);  // (after the hand-over read: see mb_put)
+      if (kind == kGU && p + kConsWarps >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+      const bool last = it.s == ph.n_st - 1 && it.sub == ph.n_sub - 1;  // the unit's last stage
+      if (!last) mb_put(S, C.hpos + (unsigned)p, lane, acc);
+      mb_done(S, C.hpos + (unsigned)p, lane);
+      if (last) {
+        const float a0 = ph.n_sub == 2 ? mb_get(A, S, C.hpos + (unsigned)(p - ph.B), ri) : acc;
+        unit_epilogue(A, S, kind, u, g, a0, acc, gen, stall, dsg, C, lane);
+      }
+      advance();
+      if (p + kConsWarps < total) item_next(ph, it);
+    }
   }
   {  // the next phase starts ph.total positions later
     const int q2 = total / A.n_slots;
