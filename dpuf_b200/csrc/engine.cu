@@ -639,6 +639,7 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
   A.tp_world = 1;
   if (e->hd % 64 || e->hd > 128) return no("head_dim not a multiple of 64 up to 128");
   if (e->I % 64 || e->H % 64 || e->qd % 64) return no("widths not multiples of 64");
+  if ((e->I / 8 + sms - 1) / sms > kDecodeSvUnits) return no("gate/up units per CTA above the shared-memory SwiGLU buffer");
   size_t limit = 0;
   if (decode_max_dyn_smem(&limit) != cudaSuccess) return no("kernel attributes");
   // ring slots: as many as shared memory holds (env DPUF_CUDA_RING_SLOTS caps them)

@@ -197,6 +197,7 @@ struct DecodeArgs {
 // Exchange generations of one decode step (one per layer, one for the LM head).
 DPUF_HD int decode_phases(int L) { return L + 1; }
 constexpr int kDecodeConsWarps = 11;  // consumer warps of a decode CTA (plus one producer warp)
+constexpr int kDecodeSvUnits = 24;    // gate/up units per decode CTA (SwiGLU outputs kept in shared memory)
 size_t decode_smem_bytes(const DecodeArgs& A);
 int decode_ring_slots(const DecodeArgs& A, size_t smem_limit);
 int decode_trace_events(int L);

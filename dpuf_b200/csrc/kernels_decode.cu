@@ -64,6 +64,7 @@ constexpr int kSlotBytes = kScBytes + kKB * 128;  // 4608
 constexpr int kMaxSlots = 48;          // ring slots (shared by the CTA's consumer warps)
 constexpr int kMailbox = 64;           // accumulator hand-over entries (a power of two)
 constexpr int kHandMax = 6;            // at most this many units per CTA: stages spread over all warps
+constexpr int kSvUnits = kDecodeSvUnits;  // gate/up units per CTA (their SwiGLU outputs stay in shared memory)
 // Bytes of the norm staging at the start of the union (gains, sign bytes), 16-byte rounded.
 DPUF_HD size_t decode_norm_stage_bytes(const DecodeArgs& A) {
   return ((size_t)A.H * 4 + (size_t)A.H / 8 + 15) & ~(size_t)15;
@@ -148,6 +149,7 @@ struct DecShared {
   // 2): the next one is copied during the current one's norm2, so that no consumer step waits
   // on a global read of a pointer
   alignas(16) DecLayer lay[2];     // 16-byte aligned: filled by 16-byte cp.async / int4 stores
+  float sv[kSvUnits][8];           // this CTA's SwiGLU outputs (gate/up unit - u0, row), for the down prep
   uint64_t mb_bar[kMailbox];       // accumulator hand-over between consumer warps (mb_put / mb_get)
   float mb_val[kMailbox][8];
 };
@@ -563,29 +565,41 @@ DPUF_DEV bool ring_wait(const DecodeArgs& A, uint64_t* bar, unsigned ph, DecShar
   }
 }
 
-// The prep of one 64-column chunk of the down projection's input from its 64 tagged SwiGLU
-// outputs (generation gen), by one warp (lanes 0..7 hold columns 8i .. 8i+7; the other lanes
-// compute the same and store nothing), into every rank's dprep as tagged words.  sb: the lane's
-// column-sign byte of the chunk (0 without signs).
-DPUF_DEV void prep_down_chunk(const DecodeArgs& A, int ch, unsigned gen, uint8_t sb, DecShared& S) {
-  const int lane = threadIdx.x & 31, qi = lane & 7;
-  const uint64_t* src = A.s_raw + ch * 64 + qi * 8;
-  uint64_t wv[8];
+// The prep of the down projection's input chunks this CTA owns - chunk ch belongs to the CTA
+// holding gate/up unit 8ch + 7 - after the gate/up phase: lane group 8 lanes per chunk (lane qi:
+// unit 8ch + qi, its eight SwiGLU outputs from shared memory if this CTA computed them, else the
+// tagged words of the previous CTA (or rank)), then the reference's activation prep, stored as
+// tagged words (generation gen) into every rank's dprep.  One warp per owned chunk.
+DPUF_DEV void prep_down_owned(const DecodeArgs& A, const Phase& ph, unsigned gen, const uint8_t* dsg, DecShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qi = lane & 7;
+  if (ph.n <= 0) return;
+  const int u0 = ph.u0, u_end = ph.u0 + ph.n;
+  const int ch_lo = u0 / 8, ch_hi = u_end >= 8 ? (u_end - 8) / 8 : -1;  // chunks with 8ch + 7 in [u0, u_end)
+  for (int ch = ch_lo + warp; ch <= ch_hi; ch += kConsWarps) {
+    const int u = ch * 8 + qi;
+    float v[8];
+    if (u >= u0) {
 #pragma unroll
-  for (int j = 0; j < 8; j++) wv[j] = ld_relaxed(src + j, A.tp_world > 1);
-  wait_words(A, wv, stale_mask(wv, 0xFFu, gen), [&](int j) { return src + j; }, gen, S);
-  float v[8];
+      for (int j = 0; j < 8; j++) v[j] = S.sv[u - u0][j];
+    } else {
+      const uint64_t* src = A.s_raw + (size_t)u * 8;
+      uint64_t wv[8];
 #pragma unroll
-  for (int j = 0; j < 8; j++) v[j] = value_of(wv[j]);
-  const PrepOut o = prep_chunk_g8_core(v, sb, lane);
-  if (lane < 8) {
-    uint64_t* dst = A.dprep + (size_t)ch * kChunkWords;
-    const uint64_t tg = (uint64_t)gen << 32;
-    put_tagged(A, dst + 2 * qi, tg | o.lo);
-    put_tagged(A, dst + 2 * qi + 1, tg | o.hi);
-    if ((qi & 3) == 0) {
-      put_tagged(A, dst + 16 + (qi >> 2), tagged(o.xs, gen));
-      put_tagged(A, dst + 18 + (qi >> 2), tg | (unsigned)o.xm);
+      for (int j = 0; j < 8; j++) wv[j] = ld_relaxed(src + j, A.tp_world > 1);
+      wait_words(A, wv, stale_mask(wv, 0xFFu, gen), [&](int j) { return src + j; }, gen, S);
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[j] = value_of(wv[j]);
+    }
+    const PrepOut o = prep_chunk_g8_core(v, dsg ? dsg[ch * 8 + qi] : (uint8_t)0, lane);
+    if (lane < 8) {
+      uint64_t* dst = A.dprep + (size_t)ch * kChunkWords;
+      const uint64_t tg = (uint64_t)gen << 32;
+      put_tagged(A, dst + 2 * qi, tg | o.lo);
+      put_tagged(A, dst + 2 * qi + 1, tg | o.hi);
+      if ((qi & 3) == 0) {
+        put_tagged(A, dst + 16 + (qi >> 2), tagged(o.xs, gen));
+        put_tagged(A, dst + 18 + (qi >> 2), tg | (unsigned)o.xm);
+      }
     }
   }
 }
@@ -683,14 +697,14 @@ DPUF_DEV void unit_epilogue(const DecodeArgs& A, DecShared& S, int kind, int u, 
       better(C.bv, C.bi, a0, row);
     }
   } else {
-    // gate/up: SwiGLU with the reference's vector/scalar split, as tagged words to every rank;
-    // the warp holding the last pair of a 64-column chunk preps that chunk
-    if (mine)
-      put_tagged(A, A.s_raw + row,
-                 tagged(swiglu_one(a0, a1, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et), gen));
-    if ((u & 7) == 7) {
-      __syncwarp();
-      prep_down_chunk(A, u >> 3, gen, dsg ? dsg[(u >> 3) * 8 + (lane & 7)] : (uint8_t)0, S);
+    // gate/up: SwiGLU with the reference's vector/scalar split: kept in shared memory for this
+    // CTA's down-input preps (prep_down_owned) and stored as tagged words to every rank for
+    // the next CTA's
+    (void)dsg;
+    if (mine) {
+      const float sw = swiglu_one(a0, a1, A.deadzone, swiglu_vector_elem(row, A.I, A.nt_ref, false), A.et);
+      S.sv[u - S.ph[kGU].u0][ri] = sw;
+      put_tagged(A, A.s_raw + row, tagged(sw, gen));
     }
   }
 }
@@ -1315,6 +1329,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(DecodeArgs A) {
                     kind == kGU && Ly->signs[3] ? dsg : nullptr, S);
       if (kind != kLM) {
         cta_sync();
+        if (kind == kGU) prep_down_owned(A, S.ph[kGU], g, Ly->signs[3] ? dsg : nullptr, S);
         trace_at(A, step, lb + (kind == kQKV ? kEvQKV : (kind == kO ? kEvO : (kind == kGU ? kEvGU : kEvDown))));
       }
     }
