@@ -622,11 +622,12 @@ DPUF_DEV void trace_at(const DecodeArgs& A, int step, int ev) {
 // warp of every position of a hand-over phase arrives once (mb_done, after writing the values if
 // anyone reads them), so tag `tag` is phase tag / kMailbox of its entry (parity
 // (tag / kMailbox) & 1).  Phases with a warp per unit do not use it.
-// An entry is rewritten kMailbox positions later; its reader is at most 2 * kHandMax positions
-// after the writer and releases its own stage only after reading, and a stage is only produced
-// once every position n_slots or more before it has been released - so with kMailbox >=
-// 2 * kHandMax + kMaxSlots + 1 an entry is never rewritten (nor its barrier advanced twice)
-// before it is read.
+// An entry is rewritten kMailbox positions later.  Its reader is at most 2 * kHandMax positions
+// after the writer, and every position releases its ring stage only after its hand-over reads
+// and its own arrival; a stage is only produced once every position n_slots or more before it
+// has been released.  So with kMailbox >= 2 * kHandMax + kMaxSlots + 1, when a reader waits on
+// an entry, the entry's previous use has completed its phase (the parity test cannot pass on a
+// stale phase) and its next use has not been written.
 DPUF_DEV void mb_put(DecShared& S, unsigned tag, int lane, float acc) {
   if (lane < 8) S.mb_val[tag & (kMailbox - 1)][lane] = acc;  // lane ri of octet 0: row ri
 }
@@ -774,15 +775,14 @@ DPUF_DEV void consume_phase(const DecodeArgs& A, int step, int l, int kind, unsi
       float acc = 0.0f;
       if (it.s > 0) acc = mb_get(A, S, C.hpos + (unsigned)(p - ph.n_sub * ph.B), ri);
       if (live) octet_chain(pp, ss, ri, q, acc);
-      release_slot(S, slot, lane);  // (after the hand-over read: see mb_put)
-      if (kind == kGU && p + kConsWarps >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
       const bool last = it.s == ph.n_st - 1 && it.sub == ph.n_sub - 1;  // the unit's last stage
+      const float a0 = last && ph.n_sub == 2 ? mb_get(A, S, C.hpos + (unsigned)(p - ph.B), ri) : acc;
       if (!last) mb_put(S, C.hpos + (unsigned)p, lane, acc);
       mb_done(S, C.hpos + (unsigned)p, lane);
-      if (last) {
-        const float a0 = ph.n_sub == 2 ? mb_get(A, S, C.hpos + (unsigned)(p - ph.B), ri) : acc;
-        unit_epilogue(A, S, kind, u, g, a0, acc, gen, stall, dsg, C, lane);
-      }
+      // the slot goes back only now: after this position's hand-over reads and its own arrival
+      release_slot(S, slot, lane);
+      if (kind == kGU && p + kConsWarps >= total) trace_at(A, step, kEvPerLayer * l + kEvGUStages);
+      if (last) unit_epilogue(A, S, kind, u, g, a0, acc, gen, stall, dsg, C, lane);
       advance();
       if (p + kConsWarps < total) item_next(ph, it);
     }
