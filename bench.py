@@ -483,7 +483,7 @@ def run_trace(args):
     from dpuf_b200 import engine, model as mdl
 
     os.environ["DPUF_CUDA_TRACE_DECODE"] = "1"
-    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    shape = model_shape(args.model)
     m = mdl.SyntheticModel(shape, seed=0)
     e = engine.CudaTransformerEngine(m)
     prompt = mdl.prompt_ids(32, shape.vocab, 1)
@@ -549,13 +549,14 @@ def profile_value(name: str, key: str):
 def decode_roofline(wbytes: int, step_s: float, hbm_peak: float, peak_kind: str):
     """Roofline of the persistent decode kernel: one launch runs all timed steps, each step
     streams the layer + LM-head weights once (the algorithmic bytes)."""
-    ratio = profile_value("decode_kernel_qwen3-0.6b_step.md", "traffic_per_algorithmic_byte")
+    ratio = profile_value("decode_kernel_qwen3-8b-l4_step.md", "traffic_per_algorithmic_byte")
     achieved = wbytes / step_s / 1e9
     return {"kernel": "decode_kernel (persistent, one step)", "bound": "hbm", "achieved": round(achieved, 1),
             "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "traffic": int(wbytes * ratio) if ratio else None, "algorithmic_bytes_per_step": wbytes,
             "us_per_step": round(step_s * 1e6, 2),
-            "traffic_note": "dram bytes per algorithmic byte from the 0.6B-shape ncu capture, times the 8B step bytes"}
+            "traffic_note": "dram bytes per algorithmic byte from the ncu capture of the 8B shape cut to 4 layers, "
+                            "times the 8B step bytes"}
 
 
 MODEL_FORMAT = "v1"  # bump when the synthetic model or the container layout changes
@@ -574,6 +575,14 @@ def cache_dir() -> pathlib.Path:
     except OSError:
         pass
     return REPO / ".bench_cache"
+
+
+def model_shape(name: str):
+    """--model: "8b" (the benchmark), "0.6b" (configuration 1), "8b-l4" (the 8B shape cut to four
+    layers, for profiler captures only)."""
+    from dpuf_b200 import model as mdl
+
+    return {"8b": mdl.QWEN3_8B, "0.6b": mdl.QWEN3_0_6B, "8b-l4": mdl.QWEN3_8B_L4}[name]
 
 
 def model_file(shape_name: str, seed: int = 0) -> pathlib.Path:
@@ -646,7 +655,7 @@ def run_reference(args, world, rank):
     from dpuf_b200 import container, model as mdl
     from oracle import oracle as orc
 
-    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    shape = model_shape(args.model)
     parallelism = ("single" if world == 1 else (f"dp{world}" if args.dp else f"tp{world}"))
     if rank != 0:
         return
@@ -716,7 +725,7 @@ def run_dpuf(args, world, rank, local):
 
     torch.cuda.set_device(local)
     hbm_peak, peak_kind = peaks()
-    shape = mdl.QWEN3_8B if args.model == "8b" else mdl.QWEN3_0_6B
+    shape = model_shape(args.model)
     tp = world > 1 and not args.dp
     parallelism = "single" if world == 1 else (f"tp{world}" if tp else f"dp{world}")
     t_build = time.perf_counter()
@@ -868,8 +877,9 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="dpuf", choices=["dpuf", "reference"])
-    ap.add_argument("--model", default="8b", choices=["8b", "0.6b"],
-                    help="8b = the benchmark workload; 0.6b = a small case for profiling")
+    ap.add_argument("--model", default="8b", choices=["8b", "0.6b", "8b-l4"],
+                    help="8b = the benchmark workload; 0.6b = configuration 1; 8b-l4 = the 8B shape cut to "
+                         "four layers, for profiler captures")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the kernel-only GEMV roofline measurement (for profiling the GEMV)")
     ap.add_argument("--op", action="store_true", help="config 2: isolated mode-12 matmuls at M = 1 and 32")

@@ -129,7 +129,11 @@ TINY_WIDE = ModelShape("tiny-wide", 1024, 12288, 2, 8, 4, 128, 4096, tied=False,
 TINY_G3 = ModelShape("tiny-g3", 256, 512, 2, 6, 2, 64, 4096, tied=False, max_seq=512)
 # a small model with the configurations' longest context (fp32 KV cache beyond 2048 positions)
 TINY_LONG = ModelShape("tiny-long", 256, 512, 2, 4, 2, 64, 4096, tied=False, max_seq=2304)
-SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, TINY, TINY_ZONE, TINY_MHA, TINY_WIDE, TINY_G3, TINY_LONG)}
+# the 8B shape cut to four layers (same per-layer work and LM head): profiler captures of the
+# decode kernel that fit a few GB on the device
+QWEN3_8B_L4 = dataclasses.replace(QWEN3_8B, name="qwen3-8b-l4", layers=4)
+SHAPES = {s.name: s for s in (QWEN3_0_6B, QWEN3_8B, QWEN3_8B_L4, TINY, TINY_ZONE, TINY_MHA, TINY_WIDE, TINY_G3,
+                              TINY_LONG)}
 
 
 def _stream_id(name: str) -> int:
