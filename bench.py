@@ -267,44 +267,18 @@ def run_op_configs(hbm_peak: float, peak_kind: str):
             engine.w12_free(h)
 
 
-def synth_had_tiles(rows: int, cols: int, mode: int, seed: int):
-    """A mode-13/14 tile set in the reference packer's layout (16-byte header with the row
-    count, per 8-row group n64 x [8 fp16 d | 8 fp16 m], nibbles, mode-14 bit pairs; tiles padded
-    to 64 bytes) with random codes and small finite scales: the kernel's time does not depend on
-    the values.  Returns (tiles, tile_offsets, sign_bits)."""
-    rng = np.random.default_rng(seed)
-    n64 = cols // 64
-    grp = n64 * (416 if mode == 14 else 288)
-    parts, offs, off = [], [], 0
-    for t in range((rows + 15) // 16):
-        n_r = min(16, rows - 16 * t)
-        n_g = (n_r + 7) // 8
-        body = rng.integers(0, 256, n_g * grp, dtype=np.uint8)
-        for g in range(n_g):
-            dm = (rng.standard_normal(n64 * 16) * 0.01).astype(np.float16).view(np.uint8)
-            body[g * grp:g * grp + n64 * 32] = dm
-        hdr = np.zeros(16, np.uint8)
-        hdr[4:6] = np.frombuffer(np.uint16(n_r).tobytes(), np.uint8)
-        tile = np.concatenate([hdr, body, np.zeros((-(16 + body.size)) % 64, np.uint8)])
-        offs.append(off)
-        parts.append(tile)
-        off += tile.size
-    return (np.concatenate(parts), np.array(offs, np.uint64),
-            rng.integers(0, 256, cols // 8, dtype=np.uint8))
-
-
 def run_had_op_configs(hbm_peak: float, peak_kind: str):
     """Modes 13 / 14 (standalone matmul, dpuf_cuda_had_asym_timed): the gate-shaped 12288x4096
     matrix at M = 1 (GB/s of tile bytes against the copy bandwidth) and M = 32, kernel-only
     timing over copies that together exceed L2."""
-    from dpuf_b200 import engine
+    from dpuf_b200 import engine, packer
 
     lib = engine.cuda_lib()
     lib.dpuf_cuda_had_asym_timed.argtypes = [ctypes.c_int32] * 5 + [ctypes.c_void_p] * 4 + [ctypes.c_int32] * 2 + \
         [ctypes.c_void_p]
     rows, cols = 12288, 4096
     for mode in (13, 14):
-        tiles, offs, signs = synth_had_tiles(rows, cols, mode, 7 + mode)
+        tiles, offs, signs = packer.synth_had_tiles(rows, cols, mode, 7 + mode)
         n_copies = 6  # 6 x 28.3 MB (mode 13) or 6 x 40.9 MB (mode 14) > 126 MB L2
         x = np.random.default_rng(mode).standard_normal((32, cols)).astype(np.float32)
         for M in (1, 32):

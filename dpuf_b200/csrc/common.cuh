@@ -33,6 +33,7 @@ struct W12 {
   const uint64_t* toff;
   const uint8_t* signs;  // cols/8 bytes, bit k of byte j = column 8j+k negated
   int rows, cols, n_tiles;
+  int mode = 12;         // 12 (QR_HAD4_PACKED); 13 / 14 (QR_HAD4_ASYM / QR_HAD6) on the per-step path
 };
 
 // Activation after prep (dpuf_prep_had4_packed_slab plain layout, dpuf_avx2.c:2364-2449):

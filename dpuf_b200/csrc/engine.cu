@@ -40,6 +40,7 @@ cudaError_t configure_attn_kernels();
 cudaError_t configure_kernels() {
   cudaError_t e;
   if ((e = configure_mode12_kernels()) != cudaSuccess) return e;
+  if ((e = configure_had_engine_kernels()) != cudaSuccess) return e;
   if ((e = configure_layer_kernels()) != cudaSuccess) return e;
   if ((e = configure_decode_kernel()) != cudaSuccess) return e;
   if ((e = configure_gemm_tc_kernels()) != cudaSuccess) return e;
@@ -198,11 +199,15 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 // from the last tile's row count, since the tile offset array has n_tiles entries in the ABI).
 size_t tile_span(const DpufWeightDesc& w, uint64_t* base_off) {
   uint64_t lo = w.tile_offsets[0], hi = 0;
-  const int n_blk = w.cols / 32;
+  // bytes of one 8-row group: mode 12 per 32 columns 144 (scales + nibbles), modes 13 / 14
+  // per 64 columns 288 / 416 (d, m, nibbles, mode 14's high bit pairs)
+  const uint64_t grp = w.mode == DPUF_MODE_QR_HAD6 ? (uint64_t)(w.cols / 64) * 416
+                       : w.mode == DPUF_MODE_QR_HAD4_ASYM ? (uint64_t)(w.cols / 64) * 288
+                                                          : (uint64_t)(w.cols / 32) * 144;
   for (int t = 0; t < w.n_tiles; t++) {
     const uint8_t* tp = w.tensor_base + w.tile_offsets[t];
     const int n_r = tp[4] | (tp[5] << 8);
-    const uint64_t end = w.tile_offsets[t] + 16 + (uint64_t)((n_r + 7) / 8) * n_blk * 144;
+    const uint64_t end = w.tile_offsets[t] + 16 + (uint64_t)((n_r + 7) / 8) * grp;
     lo = std::min<uint64_t>(lo, w.tile_offsets[t]);
     hi = std::max<uint64_t>(hi, end);
   }
@@ -210,8 +215,11 @@ size_t tile_span(const DpufWeightDesc& w, uint64_t* base_off) {
   return (size_t)(hi - lo);
 }
 
+// Modes 12 (QR_HAD4_PACKED) and, on the per-step path, 13 / 14 (QR_HAD4_ASYM / QR_HAD6: the
+// reference's had4p-hybrid packing, dpuf_engine.c:1079-1088).
 bool desc_ok(const DpufWeightDesc& w, int rows, int cols) {
-  if (w.mode != DPUF_MODE_QR_HAD4_PACKED || !w.tensor_base || !w.tile_offsets || !w.sign_bits) return false;
+  if (w.mode != DPUF_MODE_QR_HAD4_PACKED && w.mode != DPUF_MODE_QR_HAD4_ASYM && w.mode != DPUF_MODE_QR_HAD6) return false;
+  if (!w.tensor_base || !w.tile_offsets || !w.sign_bits) return false;
   if (w.rows != rows || w.cols != cols || (cols % 64) != 0) return false;
   if (w.n_tiles != (rows + kTileRows - 1) / kTileRows) return false;
   for (int t = 0; t < w.n_tiles; t++)  // the GEMV streams tiles with 16-byte async copies
@@ -259,6 +267,7 @@ cudaError_t upload_w(Engine* e, const ArenaPlan& P, const DpufWeightDesc& w, W12
   out->rows = w.rows;
   out->cols = w.cols;
   out->n_tiles = w.n_tiles;
+  out->mode = w.mode;
   if (!done.insert(t_at).second) return cudaSuccess;
   uint64_t base;
   const size_t span = tile_span(w, &base);
@@ -366,10 +375,31 @@ LinJobs one_job(const W12& w, const Act& a, float* out, int ldo, int t0, int t1)
   return J;
 }
 
-cudaError_t run_linear(const Engine* e, const Launch& Lc, const LinJobs& J, int M, const int* skip) {
+cudaError_t run_linear_m12(const Engine* e, const Launch& Lc, const LinJobs& J, int M, const int* skip) {
   if (J.tile_prefix[J.n] == 0) return cudaSuccess;
   if (M == 1) return launch_gemv(Lc, J, skip, &e->split);
   return e->use_tc_gemm ? launch_gemm_tc(Lc, J, M, e->d_tc_err) : launch_gemm_exact(Lc, J, M);
+}
+
+// The jobs' matmuls: mode-12 jobs together (one launch), mode-13/14 jobs one launch each.  A set
+// `skip` flag (the Zone-A exit) turns every launch into no work.
+cudaError_t run_linear(const Engine* e, const Launch& Lc, const LinJobs& J, int M, const int* skip) {
+  bool any_had = false;
+  for (int i = 0; i < J.n; i++) any_had |= J.j[i].w.mode != 12;
+  if (!any_had) return run_linear_m12(e, Lc, J, M, skip);
+  LinJobs J12 = {};
+  J12.tile_prefix[0] = 0;
+  for (int i = 0; i < J.n; i++) {
+    const LinJob& jb = J.j[i];
+    if (jb.w.mode == 12) {
+      J12.j[J12.n] = jb;
+      J12.tile_prefix[J12.n + 1] = J12.tile_prefix[J12.n] + (jb.t_end - jb.t_begin);
+      J12.n++;
+    } else {
+      CK(launch_had_w(Lc.stream, jb.w, jb.act, M, jb.out, jb.ldo, jb.t_begin, jb.t_end, skip));
+    }
+  }
+  return J12.n ? run_linear_m12(e, Lc, J12, M, skip) : cudaSuccess;
 }
 
 // Prep targets for weights sharing one input: identical sign tables share a prep slot
@@ -397,7 +427,9 @@ cudaError_t enqueue_step(Engine* e, const StepParams& P) {
     CK(cudaMemcpyAsync(e->d_ids, e->stage, sizeof(Staging), cudaMemcpyHostToDevice, e->stream));
   if (P.batch)
     CK(cudaMemcpyAsync(e->d_bstage, e->bstage, sizeof(BatchStaging), cudaMemcpyHostToDevice, e->stream));
-  if (!P.all_embeds) CK(launch_embed(Lc, e->tok, e->d_ids, M, e->h));
+  if (!P.all_embeds)
+    CK(e->tok.mode == 12 ? launch_embed(Lc, e->tok, e->d_ids, M, e->h)
+                         : launch_had_embed_w(Lc.stream, e->tok, e->d_ids, M, e->h));
   if (P.embeds)  // rows given by the caller (dpuf_engine.c:1658-1672); ids < 0 were staged as 0
     for (int m = 0; m < M; m++)
       if (P.all_embeds || e->stage_neg[m])
@@ -593,6 +625,13 @@ void plan_decode(Engine* e, const DpufLayerWeights* lw, const DpufWeightDesc* to
     return no("device without cooperative launch");
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device) != cudaSuccess || sms <= 0)
     return no("SM count");
+  if (tok->mode != DPUF_MODE_QR_HAD4_PACKED || lm->mode != DPUF_MODE_QR_HAD4_PACKED)
+    return no("a mode-13/14 embedding or LM head (the per-step kernels serve it)");
+  for (int l = 0; l < e->L; l++) {
+    const DpufLayerWeights& w = lw[l];
+    for (const DpufWeightDesc* d : {&w.w_q, &w.w_k, &w.w_v, &w.w_o, &w.w_gate, &w.w_up, &w.w_down})
+      if (d->mode != DPUF_MODE_QR_HAD4_PACKED) return no("mode-13/14 layers (the per-step kernels serve them)");
+  }
   std::vector<DecLayer> tab(e->L);
   for (int l = 0; l < e->L; l++) {
     const DpufLayerWeights& w = lw[l];
@@ -884,12 +923,12 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
     if (!desc_ok(w.w_q, qd, H) || !desc_ok(w.w_k, kvd, H) || !desc_ok(w.w_v, kvd, H) || !desc_ok(w.w_o, H, qd) ||
         !desc_ok(w.w_gate, I, H) || !desc_ok(w.w_up, I, H) || !desc_ok(w.w_down, H, I) || !w.attn_norm ||
         !w.ffn_norm) {
-      set_error("layer " + std::to_string(l) + ": weights must be mode 12 with matching shapes");
+      set_error("layer " + std::to_string(l) + ": weights must be mode 12, 13 or 14 with matching shapes");
       return nullptr;
     }
   }
   if (!desc_ok(*tok, tok->rows, H) || !desc_ok(*lm, c.vocab_size, H)) {
-    set_error("embedding / LM head must be mode 12 with cols == hidden_size");
+    set_error("embedding / LM head must be mode 12, 13 or 14 with cols == hidden_size");
     return nullptr;
   }
   Engine* e = new Engine();

@@ -38,12 +38,12 @@ constexpr int kHadChunk = 256;   // tokens per prep + matmul launch pair
 template <bool kHad6, int kG, int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __restrict__ tiles,
                                                                   const uint64_t* __restrict__ toff, int rows,
-                                                                  int cols, int n_tiles, Act a,
-                                                                  float* __restrict__ out) {
+                                                                  int cols, int t0, int n_tiles, Act a,
+                                                                  float* __restrict__ out, const int* skip) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  const int t = gw >> 1, rg = gw & 1;
-  if (t >= n_tiles) return;
+  const int t = t0 + (gw >> 1), rg = gw & 1;
+  if (t >= n_tiles || (skip && *skip)) return;
   const uint8_t* tp = tiles + toff[t];
   const int n_r = tp[4] | (tp[5] << 8);
   if (rg * 8 >= n_r) return;
@@ -117,10 +117,12 @@ __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __
 template <bool kHad6, int kSplit, int kG>
 __global__ void __launch_bounds__(kSplit * 32) had_gemv_split_kernel(const uint8_t* __restrict__ tiles,
                                                                      const uint64_t* __restrict__ toff, int rows,
-                                                                     int cols, Act a, float* __restrict__ out) {
+                                                                     int cols, int t0, Act a, float* __restrict__ out,
+                                                                     const int* skip) {
   extern __shared__ float4 terms[];  // [n64][8]: fdot, xm_s, d, m
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x >> 1, rg = blockIdx.x & 1;
+  const int t = t0 + (blockIdx.x >> 1), rg = blockIdx.x & 1;
+  if (skip && *skip) return;  // the whole CTA
   const uint8_t* tp = tiles + toff[t];
   const int n_r = tp[4] | (tp[5] << 8);
   if (rg * 8 >= n_r) return;  // the whole CTA
@@ -234,6 +236,8 @@ struct HadMat {
   const uint64_t* toff = nullptr;
   const uint8_t* signs = nullptr;
   int rows = 0, cols = 0, n_tiles = 0, had6 = 0;
+  int t0 = 0;                 // the launches cover tiles [t0, n_tiles)
+  const int* skip = nullptr;  // device flag: when set at launch time, the launch does nothing
 };
 
 bool had_fail(const char* where, cudaError_t e) {
@@ -286,11 +290,13 @@ bool had_upload(HadMat& h, int had6, int rows, int cols, int n_tiles, const uint
 
 template <int kG, int kWarps>
 void launch_had_t(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
-  const dim3 grid((2 * h.n_tiles + kWarps - 1) / kWarps, M);
+  const dim3 grid((2 * (h.n_tiles - h.t0) + kWarps - 1) / kWarps, M);
   if (h.had6)
-    had_asym_kernel<true, kG, kWarps><<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+    had_asym_kernel<true, kG, kWarps>
+        <<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, h.n_tiles, a, y, h.skip);
   else
-    had_asym_kernel<false, kG, kWarps><<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.n_tiles, a, y);
+    had_asym_kernel<false, kG, kWarps>
+        <<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, h.n_tiles, a, y, h.skip);
 }
 
 constexpr int kHadSplit = 4;  // warps per 8-row group in the one-token kernel
@@ -304,27 +310,36 @@ cudaError_t configure_had_kernels() {
   return e;
 }
 
-cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+// The launches of the matmul; the one-token kernel's shared-memory attribute must be set
+// (configure_had_kernels) on the current device first.
+cudaError_t launch_had_configured(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+  if (h.n_tiles <= h.t0) return cudaSuccess;
   const size_t smem = (size_t)(h.cols / 64) * 8 * sizeof(float4);
   if (M == 1 && smem <= (size_t)kMaxDynSmem) {
-    static thread_local int configured = -1;  // per host thread: the device it was done for
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-      if (cudaError_t e = configure_had_kernels()) return e;
-      configured = dev;
-    }
-    const dim3 grid(2 * h.n_tiles);
+    const dim3 grid(2 * (h.n_tiles - h.t0));
     if (h.had6)
-      had_gemv_split_kernel<true, kHadSplit, 4><<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, a, y);
+      had_gemv_split_kernel<true, kHadSplit, 4>
+          <<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, a, y, h.skip);
     else
-      had_gemv_split_kernel<false, kHadSplit, 4><<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, a, y);
+      had_gemv_split_kernel<false, kHadSplit, 4>
+          <<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, a, y, h.skip);
   } else if (M == 1) {
     launch_had_t<8, 2>(s, h, a, M, y);
   } else {
     launch_had_t<2, 8>(s, h, a, M, y);
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
+  static thread_local int configured = -1;  // per host thread: the device it was done for
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    if (cudaError_t e = configure_had_kernels()) return e;
+    configured = dev;
+  }
+  return launch_had_configured(s, h, a, M, y);
 }
 
 // Activation buffers for kHadChunk tokens.
@@ -422,6 +437,35 @@ void had_embed_host(int had6, int32_t n_tokens, int32_t cols, const int32_t* ids
 }
 
 }  // namespace
+
+// ---- engine layers in modes 13 / 14 (the per-step path; the engine configures the kernels at
+// create, so these launch without touching function attributes, e.g. during a graph capture)
+cudaError_t configure_had_engine_kernels() { return configure_had_kernels(); }
+
+cudaError_t launch_had_w(cudaStream_t s, const W12& w, const Act& a, int M, float* y, int ldo, int t_begin,
+                         int t_end, const int* skip) {
+  HadMat h;
+  h.t0 = t_begin;
+  h.skip = skip;
+  h.mem = const_cast<unsigned char*>(w.tiles);
+  h.toff = w.toff;
+  h.signs = w.signs;
+  h.rows = ldo;  // the kernels use it as the output row stride
+  h.cols = w.cols;
+  h.n_tiles = t_end;
+  h.had6 = w.mode == 14 ? 1 : 0;
+  return launch_had_configured(s, h, a, M, y);
+}
+
+cudaError_t launch_had_embed_w(cudaStream_t s, const W12& w, const int32_t* ids, int M, float* out) {
+  const dim3 grid((w.cols / 64 + 7) / 8, M);
+  if (w.mode == 14)
+    had_embed_kernel<true><<<grid, 256, 0, s>>>(w.tiles, w.toff, w.cols, ids, w.signs, out);
+  else
+    had_embed_kernel<false><<<grid, 256, 0, s>>>(w.tiles, w.toff, w.cols, ids, w.signs, out);
+  return cudaGetLastError();
+}
+
 }  // namespace dpuf
 
 extern "C" {

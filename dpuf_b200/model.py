@@ -203,10 +203,24 @@ class ModelData:
                 self.out_norm.ctypes.data)
 
 
-class SyntheticModel(ModelData):
-    """Random-init model in mode-12 layout held in host memory, with C-ABI descriptors."""
+def hybrid_mode(name: str) -> int:
+    """The mode the reference packer's "had4p-hybrid" setting gives a matrix (pack_dpuf.py:249-266):
+    14 (QR_HAD6) for the down projection, k and v, the o projection of even layers and the
+    untied LM head; 13 (QR_HAD4_ASYM) for the rest."""
+    l_idx = int(name.split(".")[1]) if name.startswith("blk.") else -1
+    if (name.endswith(".ffn_down.weight") or name.endswith(".attn_v.weight") or name.endswith(".attn_k.weight")
+            or (name.endswith(".attn_output.weight") and l_idx >= 0 and l_idx % 2 == 0) or name == "output.weight"):
+        return 14
+    return 13
 
-    def __init__(self, shape: ModelShape, seed: int = 0, norm_jitter: float = 0.0, n_threads: int | None = None):
+
+class SyntheticModel(ModelData):
+    """Random-init model held in host memory, with C-ABI descriptors: mode-12 matrices encoded by
+    the packer, or (hybrid) every matrix in mode 13 or 14 as the reference's had4p-hybrid setting
+    assigns them, with synthetic codes (packer.HadTiles)."""
+
+    def __init__(self, shape: ModelShape, seed: int = 0, norm_jitter: float = 0.0, n_threads: int | None = None,
+                 hybrid: bool = False):
         self.shape = shape
         self.seed = seed
         self.blobs: dict[str, packer.BlobView] = {}
@@ -224,6 +238,9 @@ class SyntheticModel(ModelData):
             return self.norms[name]
 
         def mat(name: str, rows: int, cols: int):
+            if hybrid:
+                self.blobs[name] = packer.HadTiles(hybrid_mode(name), rows, cols, seed * 1000003 + _stream_id(name))
+                return
             w = packer.gen_normal_bf16(seed, _stream_id(name), (rows, cols), 0.02, n_threads)
             self.blobs[name] = packer.BlobView(packer.encode_mode12(w, packer.hadamard_seed_name(name), n_threads))
 

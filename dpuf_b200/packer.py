@@ -101,6 +101,46 @@ def gen_normal_bf16(seed: int, stream: int, shape, sigma: float = 0.02, n_thread
     return out.reshape(shape)
 
 
+def synth_had_tiles(rows: int, cols: int, mode: int, seed: int, scale: float = 0.01):
+    """A mode-13/14 tile set in the reference's layout (dpuf_avx2.c:2785-2830: a 16-byte header
+    with the row count, then per 8-row group n64 x [8 fp16 d | 8 fp16 m], the nibbles and, for
+    mode 14, the high bit pairs; tiles padded to 64 bytes) with random codes and small finite
+    scales (d, m ~ N(0, scale)).  Returns (tiles, tile_offsets, sign_bits)."""
+    rng = np.random.default_rng(seed)
+    n64 = cols // 64
+    grp = n64 * (416 if mode == 14 else 288)
+    parts, offs, off = [], [], 0
+    for t in range((rows + TILE_ROWS - 1) // TILE_ROWS):
+        n_r = min(TILE_ROWS, rows - TILE_ROWS * t)
+        n_g = (n_r + 7) // 8
+        body = rng.integers(0, 256, n_g * grp, dtype=np.uint8)
+        for g in range(n_g):
+            dm = (rng.standard_normal(n64 * 16) * scale).astype(np.float16).view(np.uint8)
+            body[g * grp:g * grp + n64 * 32] = dm
+        hdr = np.zeros(16, np.uint8)
+        hdr[4:6] = np.frombuffer(np.uint16(n_r).tobytes(), np.uint8)
+        tile = np.concatenate([hdr, body, np.zeros((-(16 + body.size)) % 64, np.uint8)])
+        offs.append(off)
+        parts.append(tile)
+        off += tile.size
+    return (np.concatenate(parts), np.array(offs, np.uint64),
+            rng.integers(0, 256, cols // 8, dtype=np.uint8))
+
+
+class HadTiles:
+    """A mode-13 (QR_HAD4_ASYM) or mode-14 (QR_HAD6) matrix with synthetic codes
+    (synth_had_tiles), exposing the fields an engine descriptor takes, as BlobView does."""
+
+    def __init__(self, mode: int, rows: int, cols: int, seed: int, scale: float = 0.002):
+        if mode not in (13, 14) or cols % 64:
+            raise ValueError("modes 13 / 14 with cols % 64 == 0")
+        self.mode, self.rows, self.cols = mode, rows, cols
+        self.tiles, offs, self.sign_bits = synth_had_tiles(rows, cols, mode, seed, scale)
+        self.n_tiles = offs.size
+        self.tile_offsets = np.append(offs, np.uint64(self.tiles.size)).astype(np.uint64)
+        self.blob = self.tiles
+
+
 class BlobView:
     """Parsed view of a mode-12 blob: finder header fields and the arrays the engine binds
     (the same fields `bind_qr_weight` fills, dpuf-cli.c:1646-1756)."""

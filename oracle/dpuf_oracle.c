@@ -206,17 +206,12 @@ ORC_EXPORT void orc_matmul_mode12_f32(int32_t M, int32_t rows, int32_t cols, int
  * scalar "(xsum0 * xs0 + xsum1 * xs1) * 0.125f" as its build (gcc, gnu11, -mfma: contraction
  * on by default) computes it - checked against the built reference, which the other two
  * orders do not match. */
-ORC_EXPORT void orc_matmul_had_asym_f32(int32_t is_had6, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
-                                        const float* x_in, const uint8_t* tensor_base,
-                                        const uint64_t* tile_offsets, const uint8_t* sign_bits, float* out) {
-    const int32_t n_blk = cols >> 5, n_64 = cols >> 6;
+static void had_tiles(int32_t is_had6, int32_t cols, const uint8_t* tensor_base, const uint64_t* tile_offsets,
+                      int32_t t0, int32_t t1, const int8_t* q, const float* xs, const int32_t* xm, float* out) {
+    const int32_t n_64 = cols >> 6;
     const size_t grp_bytes = is_had6 ? 416u : 288u;
-    int8_t* q = (int8_t*)malloc((size_t)cols);
-    float* xs = (float*)malloc((size_t)n_blk * sizeof(float));
-    int32_t* xm = (int32_t*)malloc((size_t)n_blk * sizeof(int32_t));
-    for (int32_t m = 0; m < M; m++) {
-        orc_prep_mode12(cols, x_in + (size_t)m * (size_t)cols, sign_bits, q, xs, xm);
-        for (int32_t t = 0; t < n_tiles; t++) {
+    {
+        for (int32_t t = t0; t < t1; t++) {
             const uint8_t* tp = tensor_base + tile_offsets[t];
             const int32_t n_r = tp[4] | (tp[5] << 8);
             for (int32_t rg = 0; rg * 8 < n_r; rg++) {
@@ -251,10 +246,23 @@ ORC_EXPORT void orc_matmul_had_asym_f32(int32_t is_had6, int32_t M, int32_t rows
                         acc = fmaf(fdot, f16_to_f32(dm[g * 16 + r]), acc);
                         acc = fmaf(f16_to_f32(dm[g * 16 + 8 + r]), xms, acc);
                     }
-                    out[(size_t)m * rows + (size_t)t * 16 + rg * 8 + r] = acc;
+                    out[(size_t)t * 16 + rg * 8 + r] = acc;
                 }
             }
         }
+    }
+}
+
+ORC_EXPORT void orc_matmul_had_asym_f32(int32_t is_had6, int32_t M, int32_t rows, int32_t cols, int32_t n_tiles,
+                                        const float* x_in, const uint8_t* tensor_base,
+                                        const uint64_t* tile_offsets, const uint8_t* sign_bits, float* out) {
+    const int32_t n_blk = cols >> 5;
+    int8_t* q = (int8_t*)malloc((size_t)cols);
+    float* xs = (float*)malloc((size_t)n_blk * sizeof(float));
+    int32_t* xm = (int32_t*)malloc((size_t)n_blk * sizeof(int32_t));
+    for (int32_t m = 0; m < M; m++) {
+        orc_prep_mode12(cols, x_in + (size_t)m * (size_t)cols, sign_bits, q, xs, xm);
+        had_tiles(is_had6, cols, tensor_base, tile_offsets, 0, n_tiles, q, xs, xm, out + (size_t)m * (size_t)rows);
     }
     free(q); free(xs); free(xm);
 }
@@ -784,12 +792,21 @@ ORC_EXPORT void orc_engine_reset_cache(void* handle) {
     }
 }
 
+/* Tiles [t0, t1) of weight w on a prepped activation, by the weight's mode (12, 13 or 14; the
+ * reference engine's run_weight_tile_range, dpuf_engine.c:1046-1089). */
+static void tiles_range(const DpufWeightDesc* w, int32_t t0, int32_t t1, const int8_t* q, const float* xs,
+                        const int32_t* xm, float* out) {
+    if (w->mode == 13 || w->mode == 14)
+        had_tiles(w->mode == 14, w->cols, w->tensor_base, w->tile_offsets, t0, t1, q, xs, xm, out);
+    else
+        matvec_tiles(w->cols, w->tensor_base, w->tile_offsets, t0, t1, q, xs, xm, out);
+}
+
 /* y[M][rows] = W x for each token (prep with this weight's signs, then matvec). */
 static void linear(OrcEngine* e, const DpufWeightDesc* w, int32_t M, const float* x, float* y, int32_t t_end) {
     for (int32_t m = 0; m < M; m++) {
         orc_prep_mode12(w->cols, x + (size_t)m * (size_t)w->cols, w->sign_bits, e->pq, e->pxs, e->pxm);
-        matvec_tiles(w->cols, w->tensor_base, w->tile_offsets, 0, t_end, e->pq, e->pxs, e->pxm,
-                     y + (size_t)m * (size_t)w->rows);
+        tiles_range(w, 0, t_end, e->pq, e->pxs, e->pxm, y + (size_t)m * (size_t)w->rows);
     }
 }
 
@@ -810,7 +827,11 @@ ORC_EXPORT int32_t orc_engine_forward(void* handle, int32_t M, const int32_t* id
     const float eps = c->rms_eps, scale = 1.0f / sqrtf((float)hd);
     if (zone_out) memset(zone_out, 0, 4 * sizeof(int32_t));
 
-    orc_embed_mode12_f32(M, H, ids, e->tok.tensor_base, e->tok.tile_offsets, e->tok.sign_bits, e->h);
+    if (e->tok.mode == 13 || e->tok.mode == 14)
+        orc_embed_had_asym_f32(e->tok.mode == 14, M, H, ids, e->tok.tensor_base, e->tok.tile_offsets,
+                               e->tok.sign_bits, e->h);
+    else
+        orc_embed_mode12_f32(M, H, ids, e->tok.tensor_base, e->tok.tile_offsets, e->tok.sign_bits, e->h);
 
     for (int32_t l = 0; l < c->num_layers; l++) {
         const DpufLayerWeights* lw = &e->layers[l];
@@ -907,7 +928,7 @@ ORC_EXPORT int32_t orc_engine_forward(void* handle, int32_t M, const int32_t* id
         if (za < 256) za = 256;
         if (za > w->n_tiles) za = w->n_tiles;
         orc_prep_mode12(w->cols, e->att, w->sign_bits, e->pq, e->pxs, e->pxm);
-        matvec_tiles(w->cols, w->tensor_base, w->tile_offsets, 0, za, e->pq, e->pxs, e->pxm, logits);
+        tiles_range(w, 0, za, e->pq, e->pxs, e->pxm, logits);
         int32_t n_za = za * 16;
         if (n_za > c->vocab_size) n_za = c->vocab_size;
         float b1 = -1e30f, b2 = -1e30f;
@@ -928,7 +949,7 @@ ORC_EXPORT int32_t orc_engine_forward(void* handle, int32_t M, const int32_t* id
         if (exited) {
             for (int32_t i = za * 16; i < c->vocab_size; i++) logits[i] = -1e9f;
         } else {
-            matvec_tiles(w->cols, w->tensor_base, w->tile_offsets, za, w->n_tiles, e->pq, e->pxs, e->pxm, logits);
+            tiles_range(w, za, w->n_tiles, e->pq, e->pxs, e->pxm, logits);
         }
     } else {
         linear(e, w, lm_M, e->att, logits, w->n_tiles);

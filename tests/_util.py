@@ -67,7 +67,8 @@ def run_scenario(engine_factory, scenario):
     from oracle import oracle as orc
 
     with EnvScope(scenario.env):
-        m = mdl.SyntheticModel(mdl.SHAPES[scenario.shape], seed=scenario.seed, norm_jitter=scenario.norm_jitter)
+        m = mdl.SyntheticModel(mdl.SHAPES[scenario.shape], seed=scenario.seed, norm_jitter=scenario.norm_jitter,
+                               hybrid=scenario.hybrid)
         m.cfg.kv_type = scenario.kv_type
         eng = engine_factory(m)
         try:

@@ -133,7 +133,7 @@ def scenario_golden(s):
     saved = {k: os.environ.get(k) for k, _ in s.env}
     os.environ.update(dict(s.env))
     try:
-        m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter)
+        m = mdl.SyntheticModel(mdl.SHAPES[s.shape], seed=s.seed, norm_jitter=s.norm_jitter, hybrid=s.hybrid)
         m.cfg.kv_type = s.kv_type
         ref = orc.RefEngine(m, n_threads=8)
         prompt = mdl.prompt_ids(s.prompt_len, m.shape.vocab, s.seed)
@@ -166,13 +166,16 @@ def update_scenarios(names) -> None:
     """(Re)computes only the named engine scenarios and merges them into engine.json."""
     path = HERE / "engine.json"
     eng_out = json.loads(path.read_text())
+    logits_path = HERE / "engine_logits.npz"
+    eng_logits = dict(np.load(logits_path)) if logits_path.exists() else {}
     for s in sc.ENGINE_SCENARIOS:
         if s.name in names:
             rec, full = scenario_golden(s)
             if full is not None:
-                raise SystemExit("full-logit scenarios need the full run")
+                eng_logits[s.name] = full
             eng_out[s.name] = rec
     path.write_text(json.dumps(eng_out, indent=1))
+    np.savez_compressed(logits_path, **eng_logits)
 
 
 def embeds_golden(lib) -> dict:

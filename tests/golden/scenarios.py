@@ -25,6 +25,7 @@ class EngineScenario:
     all_logits: bool = False  # also record the prefill with only_last_logits = 0
     full_logits: bool = False  # store the full logit vectors (small vocab only)
     kv_type: int = 0  # DpufModelConfig.kv_type: 0 fp32 cache, 1 int8 cache with per-32 scales
+    hybrid: bool = False  # every matrix in mode 13 or 14, as the reference's had4p-hybrid packing assigns
 
 
 ENGINE_SCENARIOS = [
@@ -45,6 +46,16 @@ ENGINE_SCENARIOS = [
     # fp32 KV cache past 2048 positions: a 2040-token prompt in 256-token chunks, then decode
     # steps whose attention reads up to 2052 keys
     EngineScenario("tiny_long_2k", "tiny-long", 2040, 12, norm_jitter=0.1, seed=5),
+    # modes 13 / 14 as engine layers (had4p-hybrid: q, gate, up, odd-layer o and the embedding in
+    # mode 13; k, v, down, even-layer o and the LM head in mode 14), also with pruned down tiles
+    EngineScenario("tiny_hybrid", "tiny", 20, 12, norm_jitter=0.1, all_logits=True, full_logits=True, hybrid=True),
+    EngineScenario("tiny_hybrid_keep", "tiny-mha", 37, 9, env=(("DPUF_PREFILL_KEEP_TILES", "12"),
+                                                                ("DPUF_GEN_KEEP_TILES", "14")),
+                   norm_jitter=0.1, seed=7, hybrid=True),
+    # Zone A on a tied hybrid model: the LM head is the mode-13 embedding
+    EngineScenario("tiny_zone_a_hybrid", "tiny-zone", 20, 16,
+                   env=(("DPUF_EARLY_TILES", "300"), ("DPUF_EARLY_MARGIN", "0.05")), norm_jitter=0.1, seed=4,
+                   hybrid=True),
 ]
 
 # Packer cases: (rows, cols, tensor name used for the column signs, generator seed).

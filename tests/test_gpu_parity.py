@@ -363,3 +363,28 @@ def test_rope_positions_match_reference(eng_mod):
             assert sc.logits_digest(last) == g["mrope_equal_digest"]
         finally:
             e.close()
+
+
+def test_hybrid_model_runs_on_step_kernels(eng_mod):
+    """A model with mode-13/14 layers (the reference's had4p-hybrid packing) is served by the
+    per-step kernels - batch-1 steps included, bit-identical to the oracle engine - and the
+    engine says why it does not use the persistent kernel."""
+    from dpuf_b200 import model as mdl
+    from oracle import oracle as orc
+
+    m = mdl.SyntheticModel(mdl.TINY_G3, seed=9, norm_jitter=0.1, hybrid=True)
+    prompt = mdl.prompt_ids(23, m.shape.vocab, 9)
+    ref = orc.OracleEngine(m)
+    want_ids, want_logits = orc.greedy_run(ref, prompt, 6)
+    ref.close()
+    e = eng_mod.CudaTransformerEngine(m)
+    on, why = e.persistent_decode()
+    assert not on and "mode-13/14" in why
+    got_ids, got_logits = orc.greedy_run(e, prompt, 6)
+    assert got_ids == want_ids
+    assert all(bitexact(g, w) for g, w in zip(got_logits, want_logits))
+    e.reset_cache()
+    e.forward_batch(prompt, 0)
+    ids, _ = e.decode_greedy(want_ids[0], len(prompt), 5)
+    assert ids == want_ids[1:6]
+    e.close()
