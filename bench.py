@@ -227,8 +227,9 @@ def gemv_roofline(hbm_peak: float, peak_kind: str):
 
 def run_op_configs(hbm_peak: float, peak_kind: str):
     """Config 2 (isolated op): gate-shaped 12288x4096 and down-shaped 4096x12288 mode-12
-    matrices at M = 1 (GB/s of tile bytes) and M = 32 (dense-4-bit-equivalent TOP/s, 2*M*N*K),
-    kernel-only timing over copies that together exceed L2."""
+    matrices at M = 1 (GB/s of tile bytes) and M = 8 / 32 / 64 / 256 (dense-4-bit-equivalent TOP/s,
+    2*M*N*K, and the GB/s of the expanded copy the tensor-core GEMM streams), kernel-only timing
+    over copies that together exceed L2."""
     import torch
 
     from dpuf_b200 import engine, packer
@@ -240,11 +241,11 @@ def run_op_configs(hbm_peak: float, peak_kind: str):
         n_copies = 8  # 8 x 28.4 MB > 126 MB L2
         hs = [engine.upload(bv) for _ in range(n_copies)]
         arr = (ctypes.c_void_p * n_copies)(*hs)
-        x = torch.randn(32, cols, device="cuda")
+        x = torch.randn(256, cols, device="cuda")
         if "down" in name:
             x[x.abs() < 0.3] = 0.0
-        y = torch.empty(32, rows, device="cuda")
-        for M in (1, 32):
+        y = torch.empty(256, rows, device="cuda")
+        for M in (1, 8, 32, 64, 256):
             ms = ctypes.c_float()
             rc = lib.dpuf_cuda_matmul_dev_timed(arr, n_copies, M, ctypes.c_void_p(x.data_ptr()),
                                                 ctypes.c_void_p(y.data_ptr()), 40,
@@ -259,9 +260,19 @@ def run_op_configs(hbm_peak: float, peak_kind: str):
                 gbs = bv.tiles.nbytes / s / 1e9
                 line.update({"GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4), "peak_kind": peak_kind})
             else:
+                tc = os.environ.get("DPUF_CUDA_TC_GEMM", "1") != "0"
+                x8 = tc and os.environ.get("DPUF_CUDA_TC_EXPAND", "1") != "0"
+                # the expanded copy: per 128-row group and 32-column block, 4096 B of s8 weights
+                # and 256 B of row scales
+                x8_bytes = (bv.n_tiles + 7) // 8 * (cols // 32) * 4352
                 line.update({"TOP/s_4bit_equiv": round(2 * M * rows * cols / s / 1e12, 2),
                              "GB/s": round(bv.tiles.nbytes / s / 1e9, 1),
-                             "kernel": "gemm_tc_kernel (tcgen05 kind::i8, TMEM)" if os.environ.get("DPUF_CUDA_TC_GEMM", "1") != "0" else "gemm_exact_kernel (dp4a)"})
+                             "kernel": ("gemm_x8_kernel (tcgen05 kind::i8 over the expanded s8 copy, TMEM)" if x8
+                                        else "gemm_tc_kernel (tcgen05 kind::i8, in-kernel unpack, TMEM)" if tc
+                                        else "gemm_exact_kernel (dp4a)")})
+                if x8:
+                    line.update({"expanded_bytes": x8_bytes, "GB/s_expanded": round(x8_bytes / s / 1e9, 1),
+                                 "frac_hbm_expanded": round(x8_bytes / s / 1e9 / hbm_peak, 4)})
             print(json.dumps(line), flush=True)
         for h in hs:
             engine.w12_free(h)

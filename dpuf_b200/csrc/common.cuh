@@ -34,6 +34,7 @@ struct W12 {
   const uint8_t* signs;  // cols/8 bytes, bit k of byte j = column 8j+k negated
   int rows, cols, n_tiles;
   int mode = 12;         // 12 (QR_HAD4_PACKED); 13 / 14 (QR_HAD4_ASYM / QR_HAD6) on the per-step path
+  const uint8_t* x8 = nullptr;  // expanded copy for the tensor-core GEMM (kernels_gemm_tc.cu), or null
 };
 
 // Activation after prep (dpuf_prep_had4_packed_slab plain layout, dpuf_avx2.c:2364-2449):

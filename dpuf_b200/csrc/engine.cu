@@ -160,6 +160,7 @@ struct Engine {
 
   bool use_tc_gemm = true;  // M > 1 projections on the tensor cores (else the dp4a GEMM)
   int* d_tc_err = nullptr;  // error word of the tensor-core GEMM
+  unsigned char* x8_arena = nullptr;  // expanded copies of the mode-12 matrices (W12::x8)
 
   // persistent batch-1 decode (kernels_decode.cu)
   bool dec_ok = false, use_persistent = true;
@@ -329,6 +330,52 @@ cudaError_t slot_alloc(Engine* e, int s) {
   return cudaSuccess;
 }
 
+int env_int(const char* name, int def);
+
+// Expanded copies of the mode-12 matrices the tensor-core GEMM streams at M > 1 (W12::x8), one
+// per distinct matrix, unless env DPUF_CUDA_TC_EXPAND=0 at create.  When the allocation fails,
+// or a matrix holds a scale that is not finite, the GEMM unpacks that matrix's tiles itself.
+cudaError_t build_expanded(Engine* e) {
+  if (env_int("DPUF_CUDA_TC_EXPAND", 1) == 0) return cudaSuccess;
+  std::vector<W12*> ws;
+  for (LayerDev& d : e->layers)
+    for (W12* w : {&d.q, &d.k, &d.v, &d.o, &d.gate, &d.up, &d.down}) ws.push_back(w);
+  ws.push_back(&e->lm);
+  std::map<const uint8_t*, size_t> at;  // by tile data: shared matrices are expanded once
+  std::map<const uint8_t*, int> idx;
+  size_t bytes = 0;
+  for (W12* w : ws)
+    if (w->mode == 12 && !at.count(w->tiles)) {
+      idx[w->tiles] = (int)at.size();
+      at[w->tiles] = bytes;
+      bytes = align256(bytes + x8_bytes(*w));
+    }
+  if (!bytes) return cudaSuccess;
+  if (cudaMalloc(&e->x8_arena, bytes) != cudaSuccess) {
+    cudaGetLastError();  // not fatal
+    e->x8_arena = nullptr;
+    return cudaSuccess;
+  }
+  int* bad = nullptr;
+  CK(cudaMalloc(&bad, at.size() * sizeof(int)));
+  std::vector<int> h_bad(at.size(), 0);
+  cudaError_t err = cudaMemsetAsync(bad, 0, at.size() * sizeof(int), e->stream);
+  for (auto it = idx.begin(); err == cudaSuccess && it != idx.end(); ++it) {
+    const W12* w = nullptr;
+    for (W12* c : ws)
+      if (c->tiles == it->first) w = c;
+    err = launch_x8_expand(e->stream, *w, e->x8_arena + at[it->first], bad + it->second);
+  }
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(h_bad.data(), bad, h_bad.size() * sizeof(int), cudaMemcpyDeviceToHost, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  cudaFree(bad);
+  if (err != cudaSuccess) return err;
+  for (W12* w : ws)
+    if (w->mode == 12 && !h_bad[idx[w->tiles]]) w->x8 = e->x8_arena + at[w->tiles];
+  return cudaSuccess;
+}
+
 void destroy_engine(Engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
@@ -337,6 +384,7 @@ void destroy_engine(Engine* e) {
   for (auto& s : e->slots) { cudaFree(s.k); cudaFree(s.v); }
   for (auto& p : e->prefixes) { cudaFree(p.k); cudaFree(p.v); }
   cudaFree(e->arena);
+  cudaFree(e->x8_arena);
   cudaFree(e->cos_tab); cudaFree(e->sin_tab);
   cudaFree(e->h); cudaFree(e->hn); cudaFree(e->q); cudaFree(e->k); cudaFree(e->v); cudaFree(e->att);
   cudaFree(e->gate); cudaFree(e->up); cudaFree(e->logits);
@@ -1047,6 +1095,7 @@ Engine* create_engine(const DpufModelConfig* cfg, const DpufLayerWeights* layers
   e->kv_row = kv_row_bytes(e->kv_kind, e->hd);
   if (slot_alloc(e, 0) != cudaSuccess) return fail("KV slot 0");
   e->use_persistent = env_int("DPUF_CUDA_PERSISTENT", 1) != 0;
+  if (build_expanded(e) != cudaSuccess) return fail("expanded weights");
   plan_decode(e, layers, tok, lm);
   return e;
 }

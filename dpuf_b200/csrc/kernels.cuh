@@ -70,6 +70,11 @@ cudaError_t launch_gemm_exact(const Launch& L, const LinJobs& jobs, int M);
 // fp32 chain; *err (device) becomes nonzero if an MMA wait gives up.
 cudaError_t configure_gemm_tc_kernels();
 cudaError_t launch_gemm_tc(const Launch& L, const LinJobs& jobs, int M, int* err);
+// The expanded copy of a mode-12 matrix that lets launch_gemm_tc skip the in-kernel unpack:
+// x8_bytes(w) device bytes, filled by launch_x8_expand (*bad set when a stored scale is not finite,
+// in which case the copy must not be used).
+size_t x8_bytes(const W12& w);
+cudaError_t launch_x8_expand(cudaStream_t s, const W12& w, uint8_t* x8, int* bad);
 
 // ---- kernels_layer.cu
 struct PrepTarget {

@@ -22,7 +22,8 @@ struct W12Handle {
   float* xs = nullptr;
   int32_t* xm = nullptr;
   GemvSplit split{};  // GEMV scratch (units shared by CTAs)
-  int* tc_err = nullptr;  // error word of the tensor-core GEMM
+  int* tc_err = nullptr;  // error word of the tensor-core GEMM (and [1]: the expansion's flag)
+  uint8_t* x8 = nullptr;  // expanded copy for the tensor-core GEMM (w.x8), or null
 };
 
 constexpr int kOpChunk = kMaxBatch;  // tokens per launch of the standalone matmul
@@ -93,8 +94,32 @@ bool tc_gemm_enabled() {
   return !v || atoi(v) != 0;
 }
 
+// The expanded copy of the matrix for the tensor-core GEMM, unless env DPUF_CUDA_TC_EXPAND=0.
+// When the allocation fails, or a stored scale is not finite, the GEMM unpacks the tiles itself.
+bool expand(W12Handle* h) {
+  const char* v = getenv("DPUF_CUDA_TC_EXPAND");
+  if (v && atoi(v) == 0) return true;
+  if (cudaMalloc(&h->x8, x8_bytes(h->w)) != cudaSuccess) {
+    cudaGetLastError();  // not fatal
+    h->x8 = nullptr;
+    return true;
+  }
+  int bad = 0;
+  cudaError_t e;
+  if ((e = cudaMemset(h->tc_err + 1, 0, 4)) != cudaSuccess || (e = launch_x8_expand(0, h->w, h->x8, h->tc_err + 1)) ||
+      (e = cudaMemcpy(&bad, h->tc_err + 1, 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return fail("expanded weights", e);
+  if (bad) {
+    cudaFree(h->x8);
+    h->x8 = nullptr;
+  }
+  h->w.x8 = h->x8;
+  return true;
+}
+
 void free_handle(W12Handle* h) {
   if (!h) return;
+  cudaFree(h->x8);
   cudaFree(h->mem);
   cudaFree(h->q8);
   cudaFree(h->xs);
@@ -150,7 +175,7 @@ DPUF_EXPORT void* dpuf_cuda_w12_upload(const DpufWeightDesc* w) {
   }
   W12Handle* h = new W12Handle();
   if (!dpuf::upload(h, w->rows, w->cols, w->n_tiles, w->tensor_base, w->tile_offsets, w->sign_bits) ||
-      !dpuf::alloc_act(h)) {
+      !dpuf::alloc_act(h) || !dpuf::expand(h)) {
     dpuf::free_handle(h);
     return nullptr;
   }
@@ -276,7 +301,7 @@ DPUF_EXPORT void dpuf_matmul_qr_hadamard4_packed_f32(int32_t M, int32_t rows, in
   W12Handle* h = new W12Handle();
   float *dx = nullptr, *dy = nullptr;
   if (dpuf::upload(h, rows, cols, n_tiles, tensor_base, tile_offsets, sign_bits) && dpuf::alloc_act(h) &&
-      cudaMalloc(&dx, (size_t)M * cols * 4) == cudaSuccess && cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
+      (M == 1 || dpuf::expand(h)) && cudaMalloc(&dx, (size_t)M * cols * 4) == cudaSuccess && cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
       cudaMemcpy(dx, x_in, (size_t)M * cols * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
       dpuf::matmul_dev(h, M, dx, dy, nullptr) == 0) {
     cudaError_t e = cudaMemcpy(out, dy, (size_t)M * rows * 4, cudaMemcpyDeviceToHost);

@@ -37,14 +37,18 @@ def test_embed_matches_reference(eng_mod, ci):
     assert bitexact(eng_mod.embed(bv, g[f"embed_{ci}_ids"]), g[f"embed_{ci}"])
 
 
-@pytest.mark.parametrize("M", [1, 2, 5, 16, 17, 33, 256])
-def test_matmul_token_counts_match_oracle(eng_mod, M):
+@pytest.mark.parametrize("expand", ["1", "0"])
+@pytest.mark.parametrize("M", [1, 2, 5, 16, 17, 33, 64, 100, 256])
+def test_matmul_token_counts_match_oracle(eng_mod, M, expand):
+    """M > 1 runs on the tensor cores: over the expanded s8 copy of the matrix, or (env
+    DPUF_CUDA_TC_EXPAND=0) unpacking the tiles in the kernel."""
     from oracle import oracle as orc
 
     bv = pack_case_blob(3)
     x = np.random.default_rng(M).standard_normal((M, bv.cols)).astype(np.float32)
     x[:, 64:96] = 0.0
-    assert bitexact(eng_mod.matmul(M, bv, x), orc.oracle_matmul(M, bv, x))
+    with EnvScope([("DPUF_CUDA_TC_EXPAND", expand)]):
+        assert bitexact(eng_mod.matmul(M, bv, x), orc.oracle_matmul(M, bv, x))
 
 
 @pytest.mark.parametrize("scn", sc.ENGINE_SCENARIOS, ids=lambda s: s.name)
@@ -68,6 +72,9 @@ def test_engine_without_graphs_or_pdl_matches(eng_mod):
     for opts in ({"graphs": 0}, {"pdl": 0}, {"persistent": 0}):
         rec, _, _ = run_scenario(lambda m: eng_mod.CudaTransformerEngine(m, opts), scn)
         assert rec["digests"] == g["digests"], opts
+    with EnvScope([("DPUF_CUDA_TC_EXPAND", "0")]):  # the tensor-core GEMM unpacking in the kernel
+        rec, _, _ = run_scenario(eng_mod.CudaTransformerEngine, scn)
+    assert rec["digests"] == g["digests"]
 
 
 def test_greedy_api_matches_logits(eng_mod):
