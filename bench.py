@@ -302,7 +302,7 @@ def run_had_op_configs(hbm_peak: float, peak_kind: str):
             gbs = tiles.nbytes / sec / 1e9
             line = {"config": "op", "mode": mode, "shape": f"{rows}x{cols}", "M": M,
                     "us_per_call": round(sec * 1e6, 2), "tile_bytes": int(tiles.nbytes), "GB/s": round(gbs, 1),
-                    "kernel": "had_gemv_split_kernel (dp4a, 4 warps per 8-row group)" if M == 1
+                    "kernel": "had_gemv_stream_kernel (dp4a, a warp per 8-row group, bulk-copy ring)" if M == 1
                     else "had_asym_kernel (dp4a)", "data": "synthetic codes and scales in the reference layout"}
             if M == 1:
                 line.update({"frac_hbm": round(gbs / hbm_peak, 4), "peak_kind": peak_kind})

@@ -161,6 +161,7 @@ struct Engine {
   bool use_tc_gemm = true;  // M > 1 projections on the tensor cores (else the dp4a GEMM)
   int* d_tc_err = nullptr;  // error word of the tensor-core GEMM
   unsigned char* x8_arena = nullptr;  // expanded copies of the mode-12 matrices (W12::x8)
+  bool has_had = false;               // some matrix is in mode 13 or 14
 
   // persistent batch-1 decode (kernels_decode.cu)
   bool dec_ok = false, use_persistent = true;
@@ -269,6 +270,7 @@ cudaError_t upload_w(Engine* e, const ArenaPlan& P, const DpufWeightDesc& w, W12
   out->cols = w.cols;
   out->n_tiles = w.n_tiles;
   out->mode = w.mode;
+  if (w.mode != DPUF_MODE_QR_HAD4_PACKED) e->has_had = true;
   if (!done.insert(t_at).second) return cudaSuccess;
   uint64_t base;
   const size_t span = tile_span(w, &base);
@@ -444,7 +446,7 @@ cudaError_t run_linear(const Engine* e, const Launch& Lc, const LinJobs& J, int 
       J12.tile_prefix[J12.n + 1] = J12.tile_prefix[J12.n] + (jb.t_end - jb.t_begin);
       J12.n++;
     } else {
-      CK(launch_had_w(Lc.stream, jb.w, jb.act, M, jb.out, jb.ldo, jb.t_begin, jb.t_end, skip));
+      CK(launch_had_w(Lc.stream, jb.w, jb.act, M, jb.out, jb.ldo, jb.t_begin, jb.t_end, skip, e->d_tc_err));
     }
   }
   return J12.n ? run_linear_m12(e, Lc, J12, M, skip) : cudaSuccess;
@@ -942,11 +944,11 @@ int32_t forward_common(Engine* e, int32_t n, const int32_t* ids, int32_t pos0, c
     set_error(cudaGetErrorString(le));
     return -4;
   }
-  if (!persistent && n > 1 && e->use_tc_gemm) {
+  if (!persistent && ((n > 1 && e->use_tc_gemm) || e->has_had)) {
     int tc_err = 0;
     if (cudaMemcpy(&tc_err, e->d_tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -4;
     if (tc_err) {
-      set_error("tensor-core GEMM: an MMA wait timed out");
+      set_error("a matmul kernel's bounded wait gave up (tensor-core GEMM or mode-13/14 GEMV)");
       return -6;
     }
   }

@@ -38,11 +38,12 @@ cudaError_t configure_kernels();
 cudaError_t launch_prep(const Launch& L, const float* x, int ldx, int M, int cols, const uint8_t* signs, Act out);
 cudaError_t launch_embed(const Launch& L, const W12& w, const int32_t* ids, int M, float* out);
 // Modes 13 / 14 (ops_had_asym.cu): y[m * ldo + r] for the rows of tiles [t_begin, t_end) of w
-// on a prepped activation (nothing when *skip is set at launch time); the row lookup of a
-// mode-13/14 embedding.  Kernels configured at engine create (configure_had_engine_kernels).
+// on a prepped activation (nothing when *skip is set at launch time; *err set when a bounded
+// wait of the one-token kernel gives up); the row lookup of a mode-13/14 embedding.  Kernels
+// configured at engine create (configure_had_engine_kernels).
 cudaError_t configure_had_engine_kernels();
 cudaError_t launch_had_w(cudaStream_t s, const W12& w, const Act& a, int M, float* y, int ldo, int t_begin,
-                         int t_end, const int* skip);
+                         int t_end, const int* skip, int* err);
 cudaError_t launch_had_embed_w(cudaStream_t s, const W12& w, const int32_t* ids, int M, float* out);
 // M == 1: HBM-streaming GEMV over a persistent grid (kernels_gemv.cu).  All jobs of one launch
 // share K.  skip_flag: when non-null and nonzero at run time, CTAs exit.  split: scratch that

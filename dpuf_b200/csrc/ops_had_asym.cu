@@ -109,86 +109,173 @@ __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __
   if (c == 0 && rg * 8 + r < n_r) out[(size_t)m * rows + t * 16 + rg * 8 + r] = acc;
 }
 
-// One token (a GEMV): one CTA per 8-row group, its 64-blocks split over kSplit warps.  Each
-// warp computes, for its blocks, the same per-row terms as had_asym_kernel (exact integer dots,
-// fdot, xm_s, the row's d and m) into shared memory, loads of kG blocks in flight; then warp 0
-// runs each row's chain over all blocks in order.  Same bits as the one-warp form, kSplit times
-// the loads in flight.  Shared memory: n64 * 8 float4.
-template <bool kHad6, int kSplit, int kG>
-__global__ void __launch_bounds__(kSplit * 32) had_gemv_split_kernel(const uint8_t* __restrict__ tiles,
-                                                                     const uint64_t* __restrict__ toff, int rows,
-                                                                     int cols, int t0, Act a, float* __restrict__ out,
-                                                                     const int* skip) {
-  extern __shared__ float4 terms[];  // [n64][8]: fdot, xm_s, d, m
+// One token (a GEMV), streamed: one warp per 8-row group.  The group's bytes move by bulk
+// copies (scales, nibbles and, for mode 14, high pairs: three contiguous parts per stage of
+// kHS 64-blocks) into a kHRing-deep ring of the warp's own, so that each warp keeps kHRing
+// stages of weight bytes in flight; the lanes then compute exactly as had_asym_kernel does,
+// reading the stage from shared memory (same bits).  A wait that gives up sets *err.
+constexpr int kHWarps = 4, kHRing = 3, kHS = 16;
+constexpr unsigned long long kHWaitNs = 2000000000ull;
+template <bool kHad6>
+DPUF_HD constexpr int had_stage_bytes() {
+  return kHS * (32 + 256 + (kHad6 ? 128 : 0));
+}
+
+DPUF_DEV unsigned hsu32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+DPUF_DEV bool had_try(uint64_t* bar, unsigned par) {
+  unsigned ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok)
+               : "r"(hsu32(bar)), "r"(par)
+               : "memory");
+  return ok != 0;
+}
+DPUF_DEV unsigned long long had_timer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+DPUF_DEV bool had_wait(uint64_t* bar, unsigned par) {  // bounded; the timer only after a failed try
+  if (had_try(bar, par)) return true;
+  const unsigned long long t0 = had_timer();
+  for (int it = 1;; it++) {
+    if (had_try(bar, par)) return true;
+    if ((it & 15) == 0 && had_timer() - t0 > kHWaitNs) return false;
+  }
+}
+DPUF_DEV void had_bulk(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   hsu32(dst)),
+               "l"(src), "r"(bytes), "r"(hsu32(bar))
+               : "memory");
+}
+
+template <bool kHad6>
+__global__ void __launch_bounds__(kHWarps * 32, 4) had_gemv_stream_kernel(const uint8_t* __restrict__ tiles,
+                                                                        const uint64_t* __restrict__ toff, int cols,
+                                                                        int t0, int n_tiles, Act a,
+                                                                        float* __restrict__ out, const int* skip,
+                                                                        int* err) {
+  constexpr int kSt = had_stage_bytes<kHad6>();
+  constexpr int kB = kHad6 ? 4 : 8;  // 64-blocks whose loads are in flight together
+  static_assert(kHS % kB == 0, "batches");
+  extern __shared__ __align__(128) unsigned char hsm[];
+  __shared__ __align__(8) uint64_t full[kHWarps][kHRing];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = t0 + (blockIdx.x >> 1), rg = blockIdx.x & 1;
-  if (skip && *skip) return;  // the whole CTA
+  if (skip && *skip) return;
+  const int gw = blockIdx.x * kHWarps + warp;
+  const int t = t0 + (gw >> 1), rg = gw & 1;
+  if (t >= n_tiles) return;  // warp-uniform from here on
   const uint8_t* tp = tiles + toff[t];
   const int n_r = tp[4] | (tp[5] << 8);
-  if (rg * 8 >= n_r) return;  // the whole CTA
+  if (rg * 8 >= n_r) return;
   const int n_64 = cols >> 6;
   const uint8_t* grp = tp + 16 + (size_t)rg * n_64 * (kHad6 ? 416 : 288);
-  const uint16_t* dm = (const uint16_t*)grp;
-  const uint8_t* q4 = grp + (size_t)n_64 * 32;
-  const uint8_t* q2 = q4 + (size_t)n_64 * 256;
+  const uint8_t* gdm = grp;
+  const uint8_t* gq4 = grp + (size_t)n_64 * 32;
+  const uint8_t* gq2 = gq4 + (size_t)n_64 * 256;
+  unsigned char* ring = hsm + (size_t)warp * kHRing * kSt;
+  uint64_t* bar = full[warp];
+  const int n_st = (n_64 + kHS - 1) / kHS;
+  auto issue = [&](int st) {  // lane 0: stage st into its slot
+    const int slot = st % kHRing, g0 = st * kHS, kb = min(kHS, n_64 - g0);
+    unsigned char* d = ring + slot * kSt;
+    const unsigned bytes = (unsigned)kb * (32u + 256u + (kHad6 ? 128u : 0u));
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(hsu32(&bar[slot])), "r"(bytes)
+                 : "memory");
+    had_bulk(d, gdm + (size_t)g0 * 32, (unsigned)kb * 32u, &bar[slot]);
+    had_bulk(d + kHS * 32, gq4 + (size_t)g0 * 256, (unsigned)kb * 256u, &bar[slot]);
+    if (kHad6) had_bulk(d + kHS * 288, gq2 + (size_t)g0 * 128, (unsigned)kb * 128u, &bar[slot]);
+  };
+  int issued = min(kHRing, n_st);
+  if (lane == 0) {
+    for (int i = 0; i < kHRing; i++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(hsu32(&bar[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int st = 0; st < issued; st++) issue(st);
+  }
+  __syncwarp();
   const int r = lane >> 2, c = lane & 3, sh = 2 * (r >> 1);
-  const int g_lo = warp * n_64 / kSplit, g_hi = (warp + 1) * n_64 / kSplit;
-  for (int g0 = g_lo; g0 < g_hi; g0 += kG) {
-    const int ng = min(kG, g_hi - g0);
-    uint32_t lo[kG][2], hi[kG][2];
-    int xa[kG][2], xb[kG][2];
-    uint16_t dv[kG], mv[kG];
+  float acc = 0.0f;
+  int st = 0;
+  for (; st < n_st; st++) {
+    const int slot = st % kHRing;
+    const bool ok = had_wait(&bar[slot], (unsigned)((st / kHRing) & 1));
+    if (__any_sync(kFull, !ok)) break;
+    const unsigned char* d = ring + slot * kSt;
+    const uint16_t* sdm = (const uint16_t*)d;
+    const uint8_t* sq4 = d + kHS * 32;
+    const uint8_t* sq2 = d + kHS * 288;
+    const int g0 = st * kHS, kb = min(kHS, n_64 - g0);
+    // kB 64-blocks at a time: every load first, then the exact dots and per-block terms, then
+    // the row chain in block order (the only serial part)
+    for (int i0 = 0; i0 < kb; i0 += kB) {
+      uint32_t lo[kB][2], hi[kB][2];
+      int xa[kB][2], xb[kB][2];
+      float2 xs[kB];
+      int2 xm[kB];
+      uint16_t dv[kB], mv[kB];
 #pragma unroll
-    for (int i = 0; i < kG; i++) {
-      if (i >= ng) break;
+      for (int j = 0; j < kB; j++) {
+        const int i = min(i0 + j, kb - 1), g = g0 + i;  // a batch past kb repeats the last block, unused
 #pragma unroll
-      for (int k = 0; k < 2; k++) {
-        const int b = 2 * (g0 + i) + k;
-        const uint32_t w = __ldg((const uint32_t*)(q4 + (size_t)b * 128 + c * 32 + r * 4));
-        lo[i][k] = w & 0x0F0F0F0Fu;
-        hi[i][k] = (w >> 4) & 0x0F0F0F0Fu;
-        if (kHad6) {
-          const uint8_t* hp = q2 + (size_t)b * 64 + c * 16 + (r & 1) * 4;
-          lo[i][k] |= ((__ldg((const uint32_t*)hp) >> sh) & 0x03030303u) << 4;
-          hi[i][k] |= ((__ldg((const uint32_t*)(hp + 8)) >> sh) & 0x03030303u) << 4;
+        for (int k = 0; k < 2; k++) {
+          const uint32_t w = *(const uint32_t*)(sq4 + (2 * i + k) * 128 + c * 32 + r * 4);
+          lo[j][k] = w & 0x0F0F0F0Fu;
+          hi[j][k] = (w >> 4) & 0x0F0F0F0Fu;
+          if (kHad6) {
+            const uint8_t* hp = sq2 + (2 * i + k) * 64 + c * 16 + (r & 1) * 4;
+            lo[j][k] |= ((*(const uint32_t*)hp >> sh) & 0x03030303u) << 4;
+            hi[j][k] |= ((*(const uint32_t*)(hp + 8) >> sh) & 0x03030303u) << 4;
+          }
+          const int2 xw = *(const int2*)(a.q8 + (2 * g + k) * 32 + c * 8);
+          xa[j][k] = xw.x;
+          xb[j][k] = xw.y;
         }
-        const int* xw = (const int*)(a.q8 + b * 32 + c * 8);
-        xa[i][k] = xw[0];
-        xb[i][k] = xw[1];
+        xs[j] = *(const float2*)(a.xs + 2 * g);
+        xm[j] = *(const int2*)(a.xm + 2 * g);
+        dv[j] = sdm[i * 16 + r];
+        mv[j] = sdm[i * 16 + 8 + r];
       }
-      dv[i] = __ldg(dm + (g0 + i) * 16 + r);
-      mv[i] = __ldg(dm + (g0 + i) * 16 + 8 + r);
+      float fdot[kB], xms[kB];
+#pragma unroll
+      for (int j = 0; j < kB; j++) {
+        int dd[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          int p = __dp4a((int)lo[j][k], xa[j][k], 0);
+          p = __dp4a((int)hi[j][k], xb[j][k], p);
+          p += __shfl_xor_sync(kFull, p, 1);
+          p += __shfl_xor_sync(kFull, p, 2);
+          dd[k] = p;
+        }
+        fdot[j] = __fmaf_rn(__int2float_rn(dd[0]), xs[j].x, __fmul_rn(__int2float_rn(dd[1]), xs[j].y));
+        xms[j] = __fmul_rn(__fmaf_rn(__int2float_rn(xm[j].x), xs[j].x, __fmul_rn(__int2float_rn(xm[j].y), xs[j].y)),
+                           0.125f);
+      }
+#pragma unroll
+      for (int j = 0; j < kB; j++)
+        if (i0 + j < kb) {
+          acc = __fmaf_rn(fdot[j], f16bits_to_f32(dv[j]), acc);
+          acc = __fmaf_rn(f16bits_to_f32(mv[j]), xms[j], acc);
+        }
     }
-#pragma unroll
-    for (int i = 0; i < kG; i++) {
-      if (i >= ng) break;
-      int d[2];
-#pragma unroll
-      for (int k = 0; k < 2; k++) {
-        int p = __dp4a((int)lo[i][k], xa[i][k], 0);
-        p = __dp4a((int)hi[i][k], xb[i][k], p);
-        p += __shfl_xor_sync(kFull, p, 1);
-        p += __shfl_xor_sync(kFull, p, 2);
-        d[k] = p;
-      }
-      const int b0 = 2 * (g0 + i), b1 = b0 + 1;
-      const float xs0 = a.xs[b0], xs1 = a.xs[b1];
-      const float fdot = __fmaf_rn(__int2float_rn(d[0]), xs0, __fmul_rn(__int2float_rn(d[1]), xs1));
-      const float xms =
-          __fmul_rn(__fmaf_rn(__int2float_rn(a.xm[b0]), xs0, __fmul_rn(__int2float_rn(a.xm[b1]), xs1)), 0.125f);
-      if (c == 0) terms[(g0 + i) * 8 + r] = make_float4(fdot, xms, f16bits_to_f32(dv[i]), f16bits_to_f32(mv[i]));
+    __syncwarp();  // every lane is done with the slot
+    if (lane == 0 && st + kHRing < n_st) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads before the copy's writes
+      issue(st + kHRing);
+      issued = st + kHRing + 1;
     }
   }
-  __syncthreads();
-  if (warp == 0 && lane < 8 && rg * 8 + lane < n_r) {
-    float acc = 0.0f;
-    for (int g = 0; g < n_64; g++) {
-      const float4 v = terms[g * 8 + lane];
-      acc = __fmaf_rn(v.x, v.z, acc);
-      acc = __fmaf_rn(v.w, v.y, acc);
+  if (st < n_st) {  // a wait gave up: report it, and let the copies in flight land before exiting
+    if (lane == 0) {
+      atomicOr(err, 1);
+      issued = min(n_st, st + kHRing);
+      for (int q = st; q < issued; q++) had_wait(&bar[q % kHRing], (unsigned)((q / kHRing) & 1));
     }
-    out[t * 16 + rg * 8 + lane] = acc;
+    return;
   }
+  if (c == 0 && rg * 8 + r < n_r) out[t * 16 + rg * 8 + r] = acc;
 }
 
 // Row lookup (embed_qr_had_asym_impl, dpuf_avx2.c:3146-3221): one warp per 64-column chunk of
@@ -238,6 +325,7 @@ struct HadMat {
   int rows = 0, cols = 0, n_tiles = 0, had6 = 0;
   int t0 = 0;                 // the launches cover tiles [t0, n_tiles)
   const int* skip = nullptr;  // device flag: when set at launch time, the launch does nothing
+  int* err = nullptr;         // device word set when a bounded wait of the one-token kernel gives up
 };
 
 bool had_fail(const char* where, cudaError_t e) {
@@ -299,14 +387,12 @@ void launch_had_t(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y
         <<<grid, kWarps * 32, 0, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, h.n_tiles, a, y, h.skip);
 }
 
-constexpr int kHadSplit = 4;  // warps per 8-row group in the one-token kernel
-
 cudaError_t configure_had_kernels() {
-  cudaError_t e = cudaFuncSetAttribute(had_gemv_split_kernel<false, kHadSplit, 4>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  cudaError_t e = cudaFuncSetAttribute(had_gemv_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kHWarps * kHRing * had_stage_bytes<false>());
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(had_gemv_split_kernel<true, kHadSplit, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kMaxDynSmem);
+    e = cudaFuncSetAttribute(had_gemv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kHWarps * kHRing * had_stage_bytes<true>());
   return e;
 }
 
@@ -314,17 +400,15 @@ cudaError_t configure_had_kernels() {
 // (configure_had_kernels) on the current device first.
 cudaError_t launch_had_configured(cudaStream_t s, const HadMat& h, const Act& a, int M, float* y) {
   if (h.n_tiles <= h.t0) return cudaSuccess;
-  const size_t smem = (size_t)(h.cols / 64) * 8 * sizeof(float4);
-  if (M == 1 && smem <= (size_t)kMaxDynSmem) {
-    const dim3 grid(2 * (h.n_tiles - h.t0));
+  if (M == 1) {
+    if (!h.err) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((2 * (h.n_tiles - h.t0) + kHWarps - 1) / kHWarps));
     if (h.had6)
-      had_gemv_split_kernel<true, kHadSplit, 4>
-          <<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, a, y, h.skip);
+      had_gemv_stream_kernel<true><<<grid, kHWarps * 32, kHWarps * kHRing * had_stage_bytes<true>(), s>>>(
+          h.mem, h.toff, h.cols, h.t0, h.n_tiles, a, y, h.skip, h.err);
     else
-      had_gemv_split_kernel<false, kHadSplit, 4>
-          <<<grid, kHadSplit * 32, smem, s>>>(h.mem, h.toff, h.rows, h.cols, h.t0, a, y, h.skip);
-  } else if (M == 1) {
-    launch_had_t<8, 2>(s, h, a, M, y);
+      had_gemv_stream_kernel<false><<<grid, kHWarps * 32, kHWarps * kHRing * had_stage_bytes<false>(), s>>>(
+          h.mem, h.toff, h.cols, h.t0, h.n_tiles, a, y, h.skip, h.err);
   } else {
     launch_had_t<2, 8>(s, h, a, M, y);
   }
@@ -345,15 +429,24 @@ cudaError_t launch_had(cudaStream_t s, const HadMat& h, const Act& a, int M, flo
 // Activation buffers for kHadChunk tokens.
 struct HadAct {
   Act a{};
+  int* err = nullptr;  // the one-token kernel's error word
   bool alloc(int cols) {
     cudaError_t e;
+    if ((e = cudaMalloc(&err, 4)) != cudaSuccess || (e = cudaMemset(err, 0, 4)) != cudaSuccess)
+      return had_fail("cudaMalloc", e);
     if ((e = cudaMalloc(&a.q8, (size_t)kHadChunk * cols)) != cudaSuccess) return had_fail("cudaMalloc", e);
     if ((e = cudaMalloc(&a.xs, (size_t)kHadChunk * (cols / 32) * 4)) != cudaSuccess) return had_fail("cudaMalloc", e);
     if ((e = cudaMalloc(&a.xm, (size_t)kHadChunk * (cols / 32) * 4)) != cudaSuccess) return had_fail("cudaMalloc", e);
     a.ld = cols;
     return true;
   }
+  // after the stream is synchronised: did a bounded wait give up?
+  bool timed_out() {
+    int v = 0;
+    return cudaMemcpy(&v, err, 4, cudaMemcpyDeviceToHost) == cudaSuccess && v != 0;
+  }
   ~HadAct() {
+    cudaFree(err);
     cudaFree(a.q8);
     cudaFree(a.xs);
     cudaFree(a.xm);
@@ -361,8 +454,9 @@ struct HadAct {
 };
 
 // y = W x for M tokens (device pointers), kHadChunk tokens per prep + matmul pair.
-bool had_matmul_dev(const HadMat& h, HadAct& act, int M, const float* x, float* y, cudaStream_t s) {
+bool had_matmul_dev(HadMat h, HadAct& act, int M, const float* x, float* y, cudaStream_t s) {
   const Launch L{s, false};
+  h.err = act.err;
   for (int m0 = 0; m0 < M; m0 += kHadChunk) {
     const int mc = std::min(kHadChunk, M - m0);
     cudaError_t e = launch_prep(L, x + (size_t)m0 * h.cols, h.cols, mc, h.cols, h.signs, act.a);
@@ -386,6 +480,7 @@ void had_matmul_host(int had6, int32_t M, int32_t rows, int32_t cols, int32_t n_
       had_matmul_dev(h, act, M, dx, dy, nullptr)) {
     const cudaError_t e = cudaMemcpy(out, dy, (size_t)M * rows * 4, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) set_error(cudaGetErrorString(e));
+    else if (act.timed_out()) set_error("mode-13/14 GEMV: a bounded wait for weight bytes gave up");
   }
   cudaFree(dx);
   cudaFree(dy);
@@ -443,10 +538,11 @@ void had_embed_host(int had6, int32_t n_tokens, int32_t cols, const int32_t* ids
 cudaError_t configure_had_engine_kernels() { return configure_had_kernels(); }
 
 cudaError_t launch_had_w(cudaStream_t s, const W12& w, const Act& a, int M, float* y, int ldo, int t_begin,
-                         int t_end, const int* skip) {
+                         int t_end, const int* skip, int* err) {
   HadMat h;
   h.t0 = t_begin;
   h.skip = skip;
+  h.err = err;
   h.mem = const_cast<unsigned char*>(w.tiles);
   h.toff = w.toff;
   h.signs = w.signs;
@@ -514,8 +610,10 @@ DPUF_EXPORT int32_t dpuf_cuda_had_asym_timed(int32_t mode, int32_t M, int32_t ro
             cudaMalloc(&dy, (size_t)M * rows * 4) == cudaSuccess &&
             cudaMemcpy(dx, x_in, (size_t)M * cols * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
             cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
-  for (int i = 0; ok && i < n_copies; i++)
+  for (int i = 0; ok && i < n_copies; i++) {
     ok = had_upload(hs[i], mode == 14, rows, cols, n_tiles, tensor_base, tile_offsets, sign_bits);
+    hs[i].err = act.err;
+  }
   if (ok) ok = launch_prep(Launch{nullptr, false}, dx, cols, M, cols, hs[0].signs, act.a) == cudaSuccess;
   for (int i = 0; ok && i < n_copies; i++) ok = launch_had(nullptr, hs[i], act.a, M, dy) == cudaSuccess;  // warm-up
   if (ok) {
@@ -527,9 +625,13 @@ DPUF_EXPORT int32_t dpuf_cuda_had_asym_timed(int32_t mode, int32_t M, int32_t ro
         cudaGetLastError() == cudaSuccess) {
       *ms_per_matmul = ms / reps;
       rc = 0;
+      if (act.timed_out()) {
+        set_error("mode-13/14 GEMV: a bounded wait for weight bytes gave up");
+        rc = -6;
+      }
     }
   }
-  if (ok && rc != 0) set_error("CUDA error in the timed mode-13/14 matmul");
+  if (ok && rc == -4) set_error("CUDA error in the timed mode-13/14 matmul");
   for (auto& h : hs) cudaFree(h.mem);
   cudaFree(dx);
   cudaFree(dy);
