@@ -117,6 +117,12 @@ class ModelShape:
         per_layer = sum(mat(r, c) for _, r, c in self.linear_shapes())
         return self.layers * per_layer + mat(self.vocab, self.hidden)
 
+    def expanded_bytes_per_layer(self) -> int:
+        """Bytes of one layer's expanded copies, which the tensor-core GEMM streams for M > 1:
+        per 128-row group (8 tiles) and 32-column block, 4,096 B of s8 weights and 256 B of
+        fp16 row scales."""
+        return sum(((r + 15) // 16 + 7) // 8 * (c // 32) * 4352 for _, r, c in self.linear_shapes())
+
 
 QWEN3_0_6B = ModelShape("qwen3-0.6b", 1024, 3072, 28, 16, 8, 128, 151936, tied=True)
 QWEN3_8B = ModelShape("qwen3-8b", 4096, 12288, 36, 32, 8, 128, 151936, tied=False)
