@@ -573,6 +573,7 @@ __global__ void __launch_bounds__(kXThreads, MINB) gemm_x8_kernel(TcArgs P) {
   using Lay = XLayout<N, SB, R, TR>;
   extern __shared__ __align__(128) unsigned char sm[];
   __shared__ __align__(8) uint64_t full[R], s_empty[R];
+  __shared__ __align__(16) float xfix[kXChainWarps * (N / 2) * SB];  // see the chain warps
   __shared__ __align__(8) uint64_t d_full[TR], d_empty[TR];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
@@ -721,24 +722,38 @@ __global__ void __launch_bounds__(kXThreads, MINB) gemm_x8_kernel(TcArgs P) {
     }
   } else {
     // ================================================================ chain warps
+    // From 16 tokens on, two tokens per packed fp32x2 multiply and fma (each element rounds as
+    // the scalar op).  A block scale that is not > 0 is then taken as 0 once per stage: with the
+    // row scale finite (the expanded copy is only made then) the fma returns acc exactly (acc is
+    // never -0), as the reference's skip does.  At 8 tokens the chain is cheap next to the MMA
+    // issue, and the scalar form with the skip per step is faster.
+    constexpr bool kPacked = N >= 16;
     const int row = 32 * (warp & 3) + lane;  // TMEM lane = weight row of this thread's chains
     const int half = warp >> 2;
     constexpr int NH = N / 2;
     constexpr int kRegs = MINB > 1 ? 32 : 64;  // TMEM values held per batch
     constexpr int HB = kRegs / NH < 1 ? 1 : (kRegs / NH > SB ? SB : kRegs / NH);
-    static_assert(SB % HB == 0, "TMEM batches");
-    float acc[NH];
+    static_assert(SB % HB == 0 && NH % 2 == 0, "TMEM batches, token pairs");
+    float* xf = xfix + warp * (NH * SB);  // this warp's block scales of the stage, [block][token]
+    uint64_t acc2[NH / 2];
 #pragma unroll
-    for (int i = 0; i < NH; i++) acc[i] = 0.0f;
+    for (int i = 0; i < NH / 2; i++) acc2[i] = 0ull;  // +0.0f twice
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     for (int s = 0; s < n_stages; s++) {
       const int p = s % R, pk = s / R, ds = s % TR, dk = s / TR;
       if (!warp_wait(&full[p], (unsigned)(pk & 1))) break;  // the row and block scales
+      const int kb = min(SB, n_blk - s * SB);
+      const float* sXs = (const float*)(sm + Lay::xs + p * Lay::kX) + half * NH;  // block j: [j * N]
+      if (kPacked) {
+        for (int e = lane; e < NH * SB; e += 32) {
+          const float v = sXs[(e / NH) * N + e % NH];
+          xf[e] = v > 0.0f ? v : 0.0f;
+        }
+        __syncwarp();
+      }
       if (!warp_wait(&d_full[ds], (unsigned)(dk & 1))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int kb = min(SB, n_blk - s * SB);
-      const uint16_t* wsp = (const uint16_t*)(sm + Lay::w + p * Lay::kW) + row;       // block j: [j * 128]
-      const float* sXs = (const float*)(sm + Lay::xs + p * Lay::kX) + half * NH;     // block j: [j * N]
+      const uint16_t* wsp = (const uint16_t*)(sm + Lay::w + p * Lay::kW) + row;  // block j: [j * 128]
 #pragma unroll
       for (int hb = 0; hb < SB / HB; hb++) {
         uint32_t d[HB][NH];
@@ -757,18 +772,41 @@ __global__ void __launch_bounds__(kXThreads, MINB) gemm_x8_kernel(TcArgs P) {
 #pragma unroll
         for (int jj = 0; jj < HB; jj++) {
           const int j = hb * HB + jj;
-          if (j < kb) {
+          if (j < kb && !kPacked) {
             const float ws = f16bits_to_f32(wsp[j * kTcRows]);
             const float* xs = sXs + j * N;
 #pragma unroll
-            for (int i = 0; i < NH; i++)  // a block whose scale is not > 0 is skipped, as in the reference
-              acc[i] = xs[i] > 0.0f ? __fmaf_rn(__int2float_rn((int)d[jj][i]), __fmul_rn(ws, xs[i]), acc[i]) : acc[i];
+            for (int q = 0; q < NH / 2; q++) {  // acc2[q] holds tokens 2q, 2q + 1
+              float a0, a1;
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc2[q]));
+              const float x0 = xs[2 * q], x1 = xs[2 * q + 1];
+              a0 = x0 > 0.0f ? __fmaf_rn(__int2float_rn((int)d[jj][2 * q]), __fmul_rn(ws, x0), a0) : a0;
+              a1 = x1 > 0.0f ? __fmaf_rn(__int2float_rn((int)d[jj][2 * q + 1]), __fmul_rn(ws, x1), a1) : a1;
+              asm("mov.b64 %0, {%1, %2};" : "=l"(acc2[q]) : "f"(a0), "f"(a1));
+            }
+          } else if (j < kb) {
+            const float ws = f16bits_to_f32(wsp[j * kTcRows]);
+            uint64_t ws2;
+            asm("mov.b64 %0, {%1, %1};" : "=l"(ws2) : "f"(ws));
+            const uint64_t* xs2 = (const uint64_t*)(xf + j * NH);
+#pragma unroll
+            for (int q = 0; q < NH / 2; q++) {
+              uint64_t w2, pv2;
+              asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(w2) : "l"(ws2), "l"(xs2[q]));
+              asm("mov.b64 %0, {%1, %2};"
+                  : "=l"(pv2)
+                  : "f"(__int2float_rn((int)d[jj][2 * q])), "f"(__int2float_rn((int)d[jj][2 * q + 1])));
+              asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc2[q]) : "l"(pv2), "l"(w2));
+            }
           }
         }
       }
       __syncwarp();
       if (lane == 0) arrive(&s_empty[p]);  // scales read; A and B were read by the MMAs
     }
+    float acc[NH];
+#pragma unroll
+    for (int q = 0; q < NH / 2; q++) asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * q]), "=f"(acc[2 * q + 1]) : "l"(acc2[q]));
     // ---- outputs
     cudaGridDependencySynchronize();  // the previous kernel is done with the output buffer
     const int t = row >> 4;
@@ -847,10 +885,10 @@ cudaError_t x8_configure() {
 }
 #define DPUF_X8(N, SB, R, TR, MINB, C) {N, MINB, C, x8_launch<N, SB, R, TR, MINB>, x8_configure<N, SB, R, TR, MINB>}
 const X8Variant kX8Variants[] = {
-    DPUF_X8(8, 8, 4, 4, 1, 0.117f),
-    DPUF_X8(16, 8, 4, 4, 1, 0.148f),
-    DPUF_X8(32, 8, 4, 2, 1, 0.21f),
-    DPUF_X8(64, 4, 6, 2, 1, 0.33f),
+    DPUF_X8(8, 8, 4, 4, 1, 0.105f),
+    DPUF_X8(16, 8, 4, 4, 1, 0.126f),
+    DPUF_X8(32, 8, 4, 2, 1, 0.174f),
+    DPUF_X8(64, 4, 6, 2, 1, 0.30f),
 };
 #undef DPUF_X8
 constexpr int kX8NumVariants = (int)(sizeof(kX8Variants) / sizeof(kX8Variants[0]));
