@@ -335,10 +335,11 @@ cudaError_t slot_alloc(Engine* e, int s) {
 int env_int(const char* name, int def);
 
 // Expanded copies of the mode-12 matrices the tensor-core GEMM streams at M > 1 (W12::x8), one
-// per distinct matrix, unless env DPUF_CUDA_TC_EXPAND=0 at create.  When the allocation fails,
+// per distinct matrix, unless env DPUF_CUDA_TC_EXPAND=0 or DPUF_CUDA_TC_GEMM=0 at create (the
+// "tc_gemm" option switched on later then runs the unpacking kernel).  When the allocation fails,
 // or a matrix holds a scale that is not finite, the GEMM unpacks that matrix's tiles itself.
 cudaError_t build_expanded(Engine* e) {
-  if (env_int("DPUF_CUDA_TC_EXPAND", 1) == 0) return cudaSuccess;
+  if (!e->use_tc_gemm || env_int("DPUF_CUDA_TC_EXPAND", 1) == 0) return cudaSuccess;
   std::vector<W12*> ws;
   for (LayerDev& d : e->layers)
     for (W12* w : {&d.q, &d.k, &d.v, &d.o, &d.gate, &d.up, &d.down}) ws.push_back(w);

@@ -32,9 +32,9 @@ constexpr int kHadChunk = 256;   // tokens per prep + matmul launch pair
 // with xm_s = fma(xsum_{2g}, xs_{2g}, xsum_{2g+1} * xs_{2g+1}) * 0.125: the reference's scalar
 // "(xsum0 * xs0 + xsum1 * xs1) * 0.125f", which its build (gcc, gnu11, -mfma) contracts.
 // kG 64-blocks per batch (all their loads issued before their dots and chain steps) and kWarps
-// 8-row groups per CTA: deep batches in small CTAs for one token (a GEMV streaming from HBM),
-// shallow batches in larger CTAs for several tokens (the tiles are re-read from L2, and more
-// resident warps hide that better).
+// 8-row groups per CTA; used for several tokens (shallow batches in larger CTAs: the tiles are
+// re-read from L2, and more resident warps hide that better); one token runs on
+// had_gemv_stream_kernel below.
 template <bool kHad6, int kG, int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) had_asym_kernel(const uint8_t* __restrict__ tiles,
                                                                   const uint64_t* __restrict__ toff, int rows,
