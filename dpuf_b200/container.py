@@ -14,7 +14,8 @@ readers open_dpuf_qr_mmap, dpuf_format.py:2290-2356, and dpuf_cli_open, dpuf-cli
     ..  payload: every tensor blob at a 64-byte aligned offset (zero padding in between)
 
 Tensor blobs are the reference encoders' bytes: mode 12 (QR finder header, tile offsets, ECC
-table, sign bits, tiles; `packer.encode_mode12`) for the matrices, mode 0 ("raw tiny":
+table, sign bits, tiles; `packer.encode_mode12`) for the matrices, or modes 13 / 14 for a
+hybrid model (synthetic codes in the same blob layout, `packer.assemble_qr_blob`), mode 0 ("raw tiny":
 `<BBII` mode, ndim, d0, d1, then bf16 values) for the norm gains.  The JSON keys of
 `model_config` are the ones dpuf-cli.c:1191-1249 and DPUFCTransformerEngine
 (dpuf_format.py:2150-2200) read.
@@ -24,7 +25,7 @@ table, sign bits, tiles; `packer.encode_mode12`) for the matrices, mode 0 ("raw 
 can be created over it.  This module loads no native library: a process that only reads a
 container (the CPU reference arm of bench.py) maps no library of this package.
 
-    python -m dpuf_b200.container write PATH --shape qwen3-8b --seed 0
+    python -m dpuf_b200.container write PATH --shape qwen3-8b --seed 0 [--hybrid]
 """
 from __future__ import annotations
 
@@ -44,6 +45,7 @@ from . import packer
 MAGIC = b"DPUF0001"
 MODE_RAW_TINY = 0
 MODE_QR_HAD4_PACKED = 12
+MODES_QR_HAD_ASYM = (13, 14)  # QR_HAD4_ASYM, QR_HAD6 (the reference packer's "had4p-hybrid")
 
 
 def _pad64(n: int) -> int:
@@ -123,8 +125,11 @@ def write(path: str | os.PathLike, m: mdl.ModelData, tokenizer: dict | None = No
         pay_crc = zlib.crc32(memoryview(b), pay_crc)
         offset += int(b.size)
         blobs.append(b)
+    hybrid = any(getattr(b, "mode", MODE_QR_HAD4_PACKED) != MODE_QR_HAD4_PACKED for b in m.blobs.values())
     meta = {"format": "DPUF / LR-FLAC", "min_reader_version": "1.2.0", "model_name": m.shape.name,
-            "architecture": "qwen3", "compression_mode": "had4p (mode 12)", "num_tensors": len(names),
+            "architecture": "qwen3",
+            "compression_mode": "had4p-hybrid (modes 13/14)" if hybrid else "had4p (mode 12)",
+            "num_tensors": len(names),
             "payload_bytes": offset, "model_config": model_config_json(m.shape, m.has_qk_norm)}
     if tokenizer is not None:
         meta["tokenizer"] = tokenizer
@@ -177,7 +182,7 @@ class DpufFile(mdl.ModelData):
         for name, (off, length) in index.items():
             view = u8[base + int(off): base + int(off) + int(length)]
             mode = int(view[0])
-            if mode == MODE_QR_HAD4_PACKED:
+            if mode == MODE_QR_HAD4_PACKED or mode in MODES_QR_HAD_ASYM:
                 self.blobs[name] = packer.BlobView(view)
             elif mode == MODE_RAW_TINY:
                 _, ndim, d0, d1 = struct.unpack("<BBII", bytes(view[:10]))
@@ -216,9 +221,11 @@ class DpufFile(mdl.ModelData):
             self._f.close()
 
 
-def write_synthetic(path: str | os.PathLike, shape_name: str, seed: int = 0) -> int:
-    """Builds the random-init model `shape_name` (model.SHAPES) and writes it as a container."""
-    m = mdl.SyntheticModel(mdl.SHAPES[shape_name], seed=seed)
+def write_synthetic(path: str | os.PathLike, shape_name: str, seed: int = 0, hybrid: bool = False) -> int:
+    """Builds the random-init model `shape_name` (model.SHAPES) and writes it as a container;
+    `hybrid`: every matrix in mode 13 or 14 as the reference's had4p-hybrid packing assigns them
+    (model.hybrid_mode), with synthetic codes."""
+    m = mdl.SyntheticModel(mdl.SHAPES[shape_name], seed=seed, hybrid=hybrid)
     return write(path, m, tokenizer=synthetic_tokenizer(m.shape.vocab), extra_meta={"synthetic_seed": seed})
 
 
@@ -229,9 +236,10 @@ def main(argv=None) -> int:
     w.add_argument("path")
     w.add_argument("--shape", default="qwen3-8b", choices=sorted(mdl.SHAPES))
     w.add_argument("--seed", type=int, default=0)
+    w.add_argument("--hybrid", action="store_true", help="modes 13/14 as the had4p-hybrid packing assigns them")
     args = ap.parse_args(argv)
     if args.cmd == "write":
-        n = write_synthetic(args.path, args.shape, args.seed)
+        n = write_synthetic(args.path, args.shape, args.seed, args.hybrid)
         print(json.dumps({"path": args.path, "bytes": n}))
     return 0
 

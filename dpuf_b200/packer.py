@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import struct
 import zlib
 
 import numpy as np
@@ -20,7 +21,10 @@ import numpy as np
 from . import _native
 
 MODE_QR_HAD4_PACKED = 12
+MODE_QR_HAD4_ASYM = 13
+MODE_QR_HAD6 = 14
 TILE_ROWS = 16
+QR_FINDER = struct.Struct("<B4sBHIIIIQQQ16x")  # the 64-byte finder header (dpuf_format.py:936-938)
 ECC_GROUP = 64
 FINDER_BYTES = 64
 
@@ -101,11 +105,55 @@ def gen_normal_bf16(seed: int, stream: int, shape, sigma: float = 0.02, n_thread
     return out.reshape(shape)
 
 
+def assemble_qr_blob(mode: int, rows: int, cols: int, sign_bits: np.ndarray, tiles: np.ndarray,
+                     tile_offsets: np.ndarray, tile_rows: int = TILE_ROWS, ecc_group: int = 64) -> np.ndarray:
+    """A QR-tiled tensor blob around tiles that are already encoded, laid out as the reference's
+    assembler does for every tiled mode (_assemble_qr_blob, dpuf_format.py:1182-1251): the
+    64-byte finder header, the n_tiles + 1 tile offsets, the n_ecc + 1 parity offsets, the sign
+    bits at the next 64-byte boundary, the tiles at the next one, then per group of `ecc_group`
+    tiles their XOR as 64-bit words (each tile zero-extended to the group's longest).
+    `tile_offsets` has n_tiles + 1 entries, relative to `tiles`."""
+    offs = np.asarray(tile_offsets, dtype=np.uint64)
+    n_tiles = offs.size - 1
+    t = np.ascontiguousarray(tiles, dtype=np.uint8)
+    n_ecc = (n_tiles + ecc_group - 1) // ecc_group if ecc_group > 0 else 0
+    ecc_offs = np.zeros(n_ecc + 1, np.uint64)
+    parity, cur = [], 0
+    for g in range(n_ecc):
+        ecc_offs[g] = cur
+        lo, hi = g * ecc_group, min(n_tiles, (g + 1) * ecc_group)
+        lens = [int(offs[i + 1] - offs[i]) for i in range(lo, hi)]
+        acc = np.zeros(max(lens) // 8, np.uint64)
+        for i, n in zip(range(lo, hi), lens):
+            acc[:n // 8] ^= t[int(offs[i]):int(offs[i]) + n // 8 * 8].view(np.uint64)
+        parity.append(acc.view(np.uint8))
+        cur += acc.nbytes
+    ecc_offs[n_ecc] = cur
+    after_tables = QR_FINDER.size + offs.nbytes + ecc_offs.nbytes
+    aux_off = after_tables + (-after_tables) % 64
+    tiles_base = aux_off + sign_bits.size + (-(aux_off + sign_bits.size)) % 64
+    ecc_base = tiles_base + int(offs[-1])
+    hdr = QR_FINDER.pack(mode, b"QRDP", tile_rows, ecc_group, rows, cols, n_tiles, n_ecc, aux_off, tiles_base,
+                         ecc_base)
+    out = np.zeros(ecc_base + cur, np.uint8)
+    out[:QR_FINDER.size] = np.frombuffer(hdr, np.uint8)
+    out[QR_FINDER.size:QR_FINDER.size + offs.nbytes] = offs.view(np.uint8)
+    out[QR_FINDER.size + offs.nbytes:after_tables] = ecc_offs.view(np.uint8)
+    out[aux_off:aux_off + sign_bits.size] = sign_bits
+    out[tiles_base:ecc_base] = t[:int(offs[-1])]
+    pos = ecc_base
+    for p in parity:
+        out[pos:pos + p.size] = p
+        pos += p.size
+    return out
+
+
 def synth_had_tiles(rows: int, cols: int, mode: int, seed: int, scale: float = 0.01):
     """A mode-13/14 tile set in the reference's layout (dpuf_avx2.c:2785-2830: a 16-byte header
-    with the row count, then per 8-row group n64 x [8 fp16 d | 8 fp16 m], the nibbles and, for
-    mode 14, the high bit pairs; tiles padded to 64 bytes) with random codes and small finite
-    scales (d, m ~ N(0, scale)).  Returns (tiles, tile_offsets, sign_bits)."""
+    with the CRC32 of the tile body and the row count, as dpuf_format.py:1704-1709 writes it,
+    then per 8-row group n64 x [8 fp16 d | 8 fp16 m], the nibbles and, for mode 14, the high bit
+    pairs; tiles padded to 64 bytes) with random codes and small finite scales
+    (d, m ~ N(0, scale)).  Returns (tiles, tile_offsets, sign_bits)."""
     rng = np.random.default_rng(seed)
     n64 = cols // 64
     grp = n64 * (416 if mode == 14 else 288)
@@ -118,6 +166,7 @@ def synth_had_tiles(rows: int, cols: int, mode: int, seed: int, scale: float = 0
             dm = (rng.standard_normal(n64 * 16) * scale).astype(np.float16).view(np.uint8)
             body[g * grp:g * grp + n64 * 32] = dm
         hdr = np.zeros(16, np.uint8)
+        hdr[0:4] = np.frombuffer(np.uint32(zlib.crc32(body.tobytes()) & 0xFFFFFFFF).tobytes(), np.uint8)
         hdr[4:6] = np.frombuffer(np.uint16(n_r).tobytes(), np.uint8)
         tile = np.concatenate([hdr, body, np.zeros((-(16 + body.size)) % 64, np.uint8)])
         offs.append(off)
@@ -129,7 +178,8 @@ def synth_had_tiles(rows: int, cols: int, mode: int, seed: int, scale: float = 0
 
 class HadTiles:
     """A mode-13 (QR_HAD4_ASYM) or mode-14 (QR_HAD6) matrix with synthetic codes
-    (synth_had_tiles), exposing the fields an engine descriptor takes, as BlobView does."""
+    (synth_had_tiles), exposing the fields an engine descriptor takes, as BlobView does, and
+    `blob`, the tensor blob a container holds (assemble_qr_blob)."""
 
     def __init__(self, mode: int, rows: int, cols: int, seed: int, scale: float = 0.002):
         if mode not in (13, 14) or cols % 64:
@@ -138,7 +188,7 @@ class HadTiles:
         self.tiles, offs, self.sign_bits = synth_had_tiles(rows, cols, mode, seed, scale)
         self.n_tiles = offs.size
         self.tile_offsets = np.append(offs, np.uint64(self.tiles.size)).astype(np.uint64)
-        self.blob = self.tiles
+        self.blob = assemble_qr_blob(mode, rows, cols, self.sign_bits, self.tiles, self.tile_offsets)
 
 
 class BlobView:

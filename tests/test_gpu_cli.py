@@ -7,7 +7,8 @@ relink the CLI (the engine ABI of dpuf_kernels.h:316-360).  A greedy raw-mode tu
 (run_turn_ex, dpuf-cli.c:2344-2420: `[tokens: ...]`, then the decoded continuation) must print
 the same bytes from both.  The CPU case checks that the reference CLI reads the DPUF0001
 container this repository writes (header, tensor index, model_config, tokenizer) and that its
-greedy continuation is the oracle engine's.
+greedy continuation is the oracle engine's.  Both run on a mode-12 model and on a hybrid one
+(every matrix in mode 13 or 14, as the reference's had4p-hybrid packing assigns them).
 """
 from __future__ import annotations
 
@@ -51,10 +52,10 @@ def _turn(cli: pathlib.Path, model: pathlib.Path, n: int, threads: int = 4):
     return tok_line, gen
 
 
-@pytest.fixture(scope="module")
-def tiny_file(tmp_path_factory):
+@pytest.fixture(scope="module", params=[False, True], ids=["mode12", "hybrid"])
+def tiny_file(tmp_path_factory, request):
     p = tmp_path_factory.mktemp("cli") / "tiny.dpuf"
-    container.write_synthetic(p, "tiny", seed=11)
+    container.write_synthetic(p, "tiny", seed=11, hybrid=request.param)
     return p
 
 
@@ -81,14 +82,15 @@ def test_reference_cli_reads_container(tiny_file):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape,seed,n", [("tiny", 11, 40), ("tiny-long", 5, 64)])
-def test_cli_relinked_on_cuda_engine(tmp_path, shape, seed, n):
+@pytest.mark.parametrize("shape,seed,n,hybrid", [("tiny", 11, 40, False), ("tiny-long", 5, 64, False),
+                                                 ("tiny", 11, 40, True)])
+def test_cli_relinked_on_cuda_engine(tmp_path, shape, seed, n, hybrid):
     """The reference CLI relinked on libdpuf_cuda.so prints what it prints on the reference
     engine (prompt ids and the greedy continuation, byte for byte)."""
     if not (CLI_REF.exists() and CLI_CUDA.exists()):
         pytest.skip("oracle/_ref/dpuf-cli{,-cuda} are not built (needs the reference sources)")
     p = tmp_path / f"{shape}.dpuf"
-    container.write_synthetic(p, shape, seed=seed)
+    container.write_synthetic(p, shape, seed=seed, hybrid=hybrid)
     ref = _turn(CLI_REF, p, n, threads=8)
     got = _turn(CLI_CUDA, p, n, threads=8)
     assert got[0] == ref[0]

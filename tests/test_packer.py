@@ -71,3 +71,40 @@ def test_rejects_bad_shapes():
         packer.encode_mode12(np.zeros((64, 96), np.uint16), "x")
     with pytest.raises(ValueError):
         packer.encode_mode12(np.zeros((32, 128), np.uint16), "x")
+
+
+@pytest.mark.parametrize("i", range(len(sc.PACK_CASES)))
+def test_blob_assembler_rebuilds_mode12_blobs(i):
+    """assemble_qr_blob (the reference's shared blob layout) around a mode-12 blob's own tiles,
+    offsets and sign bits gives the blob back byte for byte (those blobs are pinned to the
+    reference packer by their sha256)."""
+    bv = pack_case_blob(i)
+    b = packer.assemble_qr_blob(bv.mode, bv.rows, bv.cols, bv.sign_bits, bv.tiles, bv.tile_offsets, bv.tile_rows,
+                                bv.ecc_group)
+    assert np.array_equal(b, bv.blob)
+
+
+@pytest.mark.parametrize("mode", [13, 14])
+def test_hybrid_blob_round_trip(mode):
+    """A synthetic mode-13/14 matrix as a blob: the finder header, tile offsets and sign bits read
+    back, every tile header carries the CRC32 of its body, the parity groups XOR to zero with
+    their tiles."""
+    h = packer.HadTiles(mode, 1000, 256, seed=5)
+    v = packer.BlobView(h.blob)
+    assert (v.mode, v.rows, v.cols, v.n_tiles) == (mode, 1000, 256, h.n_tiles)
+    assert np.array_equal(v.tiles, h.tiles) and np.array_equal(v.tile_offsets, h.tile_offsets)
+    assert np.array_equal(v.sign_bits, h.sign_bits)
+    grp = 256 // 64 * (416 if mode == 14 else 288)
+    for t in range(h.n_tiles):
+        tile = h.tiles[int(h.tile_offsets[t]):int(h.tile_offsets[t + 1])]
+        n_r = int(tile[4:6].view(np.uint16)[0])
+        body = tile[16:16 + (n_r + 7) // 8 * grp]
+        assert int(tile[:4].view(np.uint32)[0]) == zlib.crc32(body.tobytes())
+    ecc = v.blob[v.ecc_base_off:]
+    eoffs = v.blob[64 + (v.n_tiles + 1) * 8:64 + (v.n_tiles + 1) * 8 + (v.n_ecc + 1) * 8].view(np.uint64)
+    for g in range(v.n_ecc):
+        par = ecc[int(eoffs[g]):int(eoffs[g + 1])].view(np.uint64).copy()
+        for t in range(g * v.ecc_group, min(v.n_tiles, (g + 1) * v.ecc_group)):
+            tile = h.tiles[int(h.tile_offsets[t]):int(h.tile_offsets[t + 1])].view(np.uint64)
+            par[:tile.size] ^= tile
+        assert not par.any()
