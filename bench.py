@@ -632,7 +632,9 @@ def cpu_baseline(m, prompt, n_steps: int, threads: int):
         return None
     ref = orc.RefEngine(m, n_threads=threads)
     ref.reset()
+    t0 = time.perf_counter()
     lg = ref.forward(prompt, 0, 1)[0]
+    pp_s = time.perf_counter() - t0
     nxt = int(np.argmax(lg))
     pos = len(prompt)
     t0 = time.perf_counter()
@@ -644,8 +646,10 @@ def cpu_baseline(m, prompt, n_steps: int, threads: int):
     used = ref.threads
     ref.close()
     return {"value": round(n_steps / dt, 3), "unit": "tok/s", "cores": used, "kind": "reference",
-            "sample": f"{n_steps} greedy decode steps after pp32 on the same .dpuf model, reference "
-                      f"AVX2/OpenMP engine with {used} OpenMP threads, {orc.cpu_model_string()}"}
+            "prefill_tok_per_s": round(len(prompt) / pp_s, 2),
+            "sample": f"{n_steps} greedy decode steps after pp{len(prompt)} (prefill_tok_per_s: that one "
+                      f"forward_batch call) on the same .dpuf model, reference AVX2/OpenMP engine with {used} "
+                      f"OpenMP threads, {orc.cpu_model_string()}"}
 
 
 def run_reference(args, world, rank):
