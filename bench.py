@@ -337,14 +337,17 @@ def run_zone_config(hbm_peak: float, peak_kind: str, n_vec: int = 4096, za: int 
                       "peak_kind": peak_kind, "us_per_vector": round(s / n_vec * 1e6, 2)}), flush=True)
 
 
-def run_serve_config(args, hbm_peak: float, peak_kind: str):
+def run_serve_config(args, hbm_peak: float, peak_kind: str, world: int = 1, rank: int = 0, local: int = 0):
     """Config 5 (batched serving): the 8B-shaped model, n_seq independent sequences with
     random prompt_len-token prompts (seed 1000 + i), each prefilled into its own slot in
     256-token forward_batch calls, then `steps` greedy decode steps of all sequences at once
     (the first `warmup` of them untimed)
     through dpuf_cuda_decode_batch (one CUDA-graph launch per step, ids in, ids out).  The
     timed region is the decode steps only; each call is synchronous, so the time is wall clock
-    around them (which is also the end-to-end time: it includes the per-step id copies)."""
+    around them (which is also the end-to-end time: it includes the per-step id copies).  Under
+    torchrun every rank serves its own n_seq sequences (prompt seeds 1000 + rank * n_seq + i) on
+    its GPU, data parallel: the job's tokens are world * n_seq * steps and its time the slowest
+    rank's (`scaling` "weak")."""
     from dpuf_b200 import engine, model as mdl
 
     n_seq, plen, steps, warm = args.serve_seqs, args.serve_prompt, args.serve_steps, args.warmup
@@ -361,7 +364,7 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
     toks, pos = [], []
     t0 = time.perf_counter()
     for i in range(n_seq):
-        pr = mdl.prompt_ids(plen, shape.vocab, 1000 + i)
+        pr = mdl.prompt_ids(plen, shape.vocab, 1000 + rank * n_seq + i)
         if eng.set_slot(i) != 0:
             raise RuntimeError(engine.last_error())
         eng.reset_slot(i)
@@ -376,13 +379,21 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
         toks = [int(t) for t in eng.decode_batch(slots, toks, pos)]
         pos = [p + 1 for p in pos]
     ctx0 = pos[0]
-    with ClockSampler(0) as clk:
+    barrier(world)
+    with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for _ in range(steps):
             toks = [int(t) for t in eng.decode_batch(slots, toks, pos)]
             pos = [p + 1 for p in pos]
         dt = time.perf_counter() - t0
     eng.close()
+    if world > 1:  # the slowest rank's time for every rank's tokens
+        value, max_ms = dp_value(dt * 1e3, n_seq * steps, world)
+        dt = max_ms * 1e-3
+    else:
+        value = n_seq * steps / dt
+    if rank != 0:
+        return
     if args.no_extras:
         cpu = None
     else:
@@ -395,12 +406,13 @@ def run_serve_config(args, hbm_peak: float, peak_kind: str):
     ctx_mean = ctx0 + (steps + 1) / 2.0
     kv_bytes = n_seq * shape.layers * 2 * ctx_mean * kvd * {"f16": 2, "f32": 4, "q8": 1.125}[kv]
     step_s = dt / steps
-    value = n_seq * steps / dt
     print(json.dumps({
-        "metric": "batched_decode_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": 1,
+        "metric": "batched_decode_tok_per_s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak",
         "config": {"workload": f"{shape.name}-shape batched serving: {n_seq} sequences x {plen}-token prompts, "
-                               f"{steps} greedy steps at batch {n_seq}",
+                               f"{steps} greedy steps at batch {n_seq}" + (" per GPU" if world > 1 else ""),
+                   "parallelism": f"dp{world}" if world > 1 else "single",
                    "kv": {"f16": "fp16", "f32": "fp32", "q8": "q8 (kv_type 1)"}[kv],
                    "context": [ctx0, ctx0 + steps]},
         "step_roofline": {"bytes_per_step": int(wbytes + kv_bytes), "weights": wbytes, "kv": int(kv_bytes),
@@ -928,7 +940,13 @@ def main():
         if args.zone:
             run_zone_config(*peaks())
         if args.serve:
-            run_serve_config(args, *peaks())
+            try:
+                run_serve_config(args, *peaks(), world=world, rank=rank, local=local)
+            finally:
+                if world > 1:
+                    import torch.distributed as dist
+
+                    dist.destroy_process_group()
         return
     rc = 0
     try:
