@@ -52,6 +52,8 @@ ENGINE_SCENARIOS = [
     EngineScenario("tiny_hybrid_keep", "tiny-mha", 37, 9, env=(("DPUF_PREFILL_KEEP_TILES", "12"),
                                                                 ("DPUF_GEN_KEEP_TILES", "14")),
                    norm_jitter=0.1, seed=7, hybrid=True),
+    # the Qwen3-0.6B shape as a hybrid model (tied mode-13 embedding as the LM head)
+    EngineScenario("qwen3_0_6b_hybrid", "qwen3-0.6b", 32, 8, hybrid=True),
     # Zone A on a tied hybrid model: the LM head is the mode-13 embedding
     EngineScenario("tiny_zone_a_hybrid", "tiny-zone", 20, 16,
                    env=(("DPUF_EARLY_TILES", "300"), ("DPUF_EARLY_MARGIN", "0.05")), norm_jitter=0.1, seed=4,
