@@ -114,3 +114,19 @@ def test_had_embed_rejects_rows_outside_tiles(lib):
         lib.dpuf_embed_qr_had6_f32(2, cols, ids.ctypes.data, bv.tiles.ctypes.data, bv.tile_offsets.ctypes.data,
                                    bv.sign_bits.ctypes.data, out.ctypes.data)
         assert np.all(out == 7.0) and engine.last_error(), bad
+
+
+@pytest.mark.parametrize("mode", [13, 14])
+@pytest.mark.parametrize("cols", [4096, 12288])
+def test_had_rows_of_many_stages_match_oracle(lib, mode, cols):
+    """Rows of 4,096 and 12,288 columns: the one-token kernel streams each 8-row group through
+    its shared-memory ring in several stages (slots reused), the several-token kernel in many
+    batches; both against the oracle (pinned to the reference's fixtures above)."""
+    from dpuf_b200 import packer
+    from oracle import oracle as orc
+
+    h = packer.HadTiles(mode, 72, cols, seed=cols + mode)
+    x = np.random.default_rng(cols + mode).standard_normal((3, cols)).astype(np.float32)
+    x[:, 64:128] = 0.0  # a zero block (block scale 0)
+    for M in (1, 3):
+        assert bitexact(_run(lib, mode, M, h, x[:M]), orc.oracle_matmul_had(mode, M, h, x[:M])), M
