@@ -37,6 +37,23 @@ def test_embed_matches_reference(eng_mod, ci):
     assert bitexact(eng_mod.embed(bv, g[f"embed_{ci}_ids"]), g[f"embed_{ci}"])
 
 
+@pytest.mark.parametrize("variant", ["0", "1", "2", "3"])
+def test_expanded_gemm_shapes_match_oracle(eng_mod, variant):
+    """Every shape of the expanded-weight GEMM (8 / 16 / 32 / 64 tokens per CTA, forced through
+    env DPUF_CUDA_X8_VARIANT) on a 512x4096 matrix at M = 64: several stages per CTA with the
+    ring reused, the scalar and the packed chains, against the oracle."""
+    from dpuf_b200 import packer
+    from oracle import oracle as orc
+
+    w = packer.gen_normal_bf16(77, 5, (512, 4096), 0.02)
+    bv = packer.BlobView(packer.encode_mode12(w, "blk.0.ffn_up.weight"))
+    x = np.random.default_rng(77).standard_normal((64, 4096)).astype(np.float32)
+    x[:, 64:96] = 0.0
+    x[5, :] = 0.0
+    with EnvScope([("DPUF_CUDA_X8_VARIANT", variant)]):
+        assert bitexact(eng_mod.matmul(64, bv, x), orc.oracle_matmul(64, bv, x))
+
+
 @pytest.mark.parametrize("expand", ["1", "0"])
 @pytest.mark.parametrize("M", [1, 2, 5, 16, 17, 33, 64, 100, 256])
 def test_matmul_token_counts_match_oracle(eng_mod, M, expand):
